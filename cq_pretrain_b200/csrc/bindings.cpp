@@ -1,0 +1,41 @@
+// Python bindings of the cq_pretrain_b200 sm_100a kernel library.
+#include <torch/extension.h>
+
+#include <atomic>
+#include <vector>
+
+namespace cqb {
+std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> counter{0};
+  return counter;
+}
+long long launch_count() { return launch_counter().load(); }
+
+// rowops.cu
+std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps);
+std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd);
+std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w, double eps);
+std::vector<at::Tensor> gated_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor z, at::Tensor w, at::Tensor rstd);
+std::vector<at::Tensor> ln_modulate_fwd(at::Tensor x, at::Tensor scale, at::Tensor shift, at::Tensor idx, double eps);
+std::vector<at::Tensor> ln_modulate_bwd(at::Tensor dy, at::Tensor x, at::Tensor scale, at::Tensor idx, at::Tensor mean,
+                                        at::Tensor rstd);
+at::Tensor gated_add_fwd(at::Tensor x, at::Tensor branch, at::Tensor gate, at::Tensor idx);
+std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tensor gate, at::Tensor idx);
+at::Tensor swiglu_fwd(at::Tensor x);
+at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x);
+}  // namespace cqb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "cq_pretrain_b200 sm_100a kernels";
+  m.def("launch_count", &cqb::launch_count);
+  m.def("rms_norm_fwd", &cqb::rms_norm_fwd);
+  m.def("rms_norm_bwd", &cqb::rms_norm_bwd);
+  m.def("gated_norm_fwd", &cqb::gated_norm_fwd);
+  m.def("gated_norm_bwd", &cqb::gated_norm_bwd);
+  m.def("ln_modulate_fwd", &cqb::ln_modulate_fwd);
+  m.def("ln_modulate_bwd", &cqb::ln_modulate_bwd);
+  m.def("gated_add_fwd", &cqb::gated_add_fwd);
+  m.def("gated_add_bwd", &cqb::gated_add_bwd);
+  m.def("swiglu_fwd", &cqb::swiglu_fwd);
+  m.def("swiglu_bwd", &cqb::swiglu_bwd);
+}

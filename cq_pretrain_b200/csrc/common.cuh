@@ -1,0 +1,88 @@
+// Shared helpers for the sm_100a kernels of cq_pretrain_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include <atomic>
+#include <cstdint>
+
+namespace cqb {
+
+// Number of kernels this library has launched (read by benchmarks to count native launches).
+std::atomic<long long>& launch_counter();
+inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_order_relaxed); }
+
+#define CQB_CHECK_CUDA(expr)                                                                        \
+  do {                                                                                              \
+    cudaError_t err__ = (expr);                                                                     \
+    TORCH_CHECK(err__ == cudaSuccess, "CUDA error ", cudaGetErrorString(err__), " at ", __FILE__, \
+                ":", __LINE__);                                                                     \
+  } while (0)
+
+#define CQB_LAUNCH_CHECK() CQB_CHECK_CUDA(cudaGetLastError())
+
+inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+inline int sm_count() {
+  static int count = [] {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+  }();
+  return count;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 8 x bf16 <-> 8 x float through one 16-byte vector.
+struct alignas(16) Bf16x8 {
+  __nv_bfloat162 v[4];
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* out) {
+  Bf16x8 x = *reinterpret_cast<const Bf16x8*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(x.v[i]);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void load8(const float* p, float* out) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* in) {
+  Bf16x8 x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x.v[i] = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
+  *reinterpret_cast<Bf16x8*>(p) = x;
+}
+
+__device__ __forceinline__ void store8(float* p, const float* in) {
+  *reinterpret_cast<float4*>(p) = make_float4(in[0], in[1], in[2], in[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(in[4], in[5], in[6], in[7]);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+}  // namespace cqb

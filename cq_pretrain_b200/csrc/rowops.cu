@@ -1,0 +1,736 @@
+// Row-wise normalisation / activation kernels (memory-bound; one warp per row, fp32 statistics).
+//
+//  rms_norm      y = x * rsqrt(mean x^2 + eps) * (1 + w)                  (Qwen3.5 offset RMSNorm)
+//  gated_norm    y = bf16(x * rsqrt(mean x^2 + eps)) * w * silu(z)          (GDN output norm)
+//  ln_modulate   y = LN(x) * (1 + scale[idx[r]]) + shift[idx[r]]            (Wan adaLN, fp32 math)
+//  gated_add     y = x + gate[idx[r]] * branch                              (Wan fp32 gated residual)
+//  swiglu        y = silu(x[:, :F]) * x[:, F:]
+//
+// Backward kernels reduce weight / modulation gradients per warp over contiguous rows in
+// registers, then per block in shared memory, then with one fp32 atomicAdd per block and column.
+#include "common.cuh"
+
+namespace cqb {
+
+namespace {
+
+constexpr int kWarps = 8;  // rows per 256-thread block in forward kernels
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* p, float* out) { load8(p, out); }
+
+template <int NV, typename T, typename WT>
+__global__ void __launch_bounds__(256) rms_fwd_kernel(const T* __restrict__ x, const WT* __restrict__ w,
+                                                     T* __restrict__ y, float* __restrict__ rstd, int rows, int width,
+                                                     float eps) {
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + (size_t)row * width;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width) {
+      load_vec(xr + c, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / width + eps);
+  T* yr = y + (size_t)row * width;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width) {
+      float wv[8], o[8];
+      load_vec(w + c, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * r * (1.f + wv[j]);
+      store8(yr + c, o);
+    }
+  }
+  if (lane == 0) rstd[row] = r;
+}
+
+// dx = r * (g - xhat * mean(g * xhat)), g = dy * (1 + w);  dw += dy * xhat
+template <int NV, typename T, typename WT>
+__global__ void __launch_bounds__(512) rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                     const WT* __restrict__ w, const float* __restrict__ rstd,
+                                                     T* __restrict__ dx, float* __restrict__ dw, int rows, int width) {
+  extern __shared__ float smem[];  // [width]
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) smem[c] = 0.f;
+  __syncthreads();
+  float acc[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int total = gridDim.x * warps;
+  const int per = (rows + total - 1) / total;
+  const int gw = blockIdx.x * warps + warp;
+  const int r0 = gw * per, r1 = min(rows, r0 + per);
+  for (int row = r0; row < r1; ++row) {
+    const float r = rstd[row];
+    const T* xr = x + (size_t)row * width;
+    const T* gr = dy + (size_t)row * width;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float xv[8], gv[8], wv[8];
+        load_vec(xr + c, xv);
+        load_vec(gr + c, gv);
+        load_vec(w + c, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = xv[j] * r;
+          acc[i][j] += gv[j] * xh;
+          dot += gv[j] * (1.f + wv[j]) * xh;
+        }
+      }
+    }
+    dot = warp_sum(dot) / width;
+    T* dr = dx + (size_t)row * width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float xv[8], gv[8], wv[8], o[8];
+        load_vec(xr + c, xv);
+        load_vec(gr + c, gv);
+        load_vec(w + c, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * (1.f + wv[j]) - xv[j] * r * dot);
+        store8(dr + c, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&smem[c + j], acc[i][j]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) atomicAdd(&dw[c], smem[c]);
+}
+
+template <int NV, typename T, typename WT>
+__global__ void __launch_bounds__(256) gated_fwd_kernel(const T* __restrict__ x, const T* __restrict__ z,
+                                                       const WT* __restrict__ w, T* __restrict__ y,
+                                                       float* __restrict__ rstd, int rows, int width, float eps) {
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + (size_t)row * width;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width) {
+      load_vec(xr + c, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / width + eps);
+  const T* zr = z + (size_t)row * width;
+  T* yr = y + (size_t)row * width;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width) {
+      float wv[8], zv[8], o[8];
+      load_vec(w + c, wv);
+      load_vec(zr + c, zv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float n = __bfloat162float(__float2bfloat16(v[i][j] * r));
+        o[j] = n * wv[j] * silu(zv[j]);
+      }
+      store8(yr + c, o);
+    }
+  }
+  if (lane == 0) rstd[row] = r;
+}
+
+// n = x r; dn = dy w silu(z); dx = r (dn - n mean(dn n)); dz = dy n w silu'(z); dw += dy n silu(z)
+template <int NV, typename T, typename WT>
+__global__ void __launch_bounds__(512) gated_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                       const T* __restrict__ z, const WT* __restrict__ w,
+                                                       const float* __restrict__ rstd, T* __restrict__ dx,
+                                                       T* __restrict__ dz, float* __restrict__ dw, int rows, int width) {
+  extern __shared__ float smem[];
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) smem[c] = 0.f;
+  __syncthreads();
+  float acc[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int total = gridDim.x * warps;
+  const int per = (rows + total - 1) / total;
+  const int gw = blockIdx.x * warps + warp;
+  const int r0 = gw * per, r1 = min(rows, r0 + per);
+  for (int row = r0; row < r1; ++row) {
+    const float r = rstd[row];
+    const size_t off = (size_t)row * width;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float xv[8], gv[8], wv[8], zv[8], dzo[8];
+        load_vec(x + off + c, xv);
+        load_vec(dy + off + c, gv);
+        load_vec(w + c, wv);
+        load_vec(z + off + c, zv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float n = xv[j] * r;
+          const float sg = 1.f / (1.f + __expf(-zv[j]));
+          const float s = zv[j] * sg;
+          acc[i][j] += gv[j] * n * s;
+          dot += gv[j] * wv[j] * s * n;
+          dzo[j] = gv[j] * n * wv[j] * sg * (1.f + zv[j] * (1.f - sg));
+        }
+        store8(dz + off + c, dzo);
+      }
+    }
+    dot = warp_sum(dot) / width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float xv[8], gv[8], wv[8], zv[8], o[8];
+        load_vec(x + off + c, xv);
+        load_vec(dy + off + c, gv);
+        load_vec(w + c, wv);
+        load_vec(z + off + c, zv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * wv[j] * silu(zv[j]) - xv[j] * r * dot);
+        store8(dx + off + c, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&smem[c + j], acc[i][j]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) atomicAdd(&dw[c], smem[c]);
+}
+
+template <int NV, typename T>
+__global__ void __launch_bounds__(256) lnmod_fwd_kernel(const T* __restrict__ x, const float* __restrict__ scale,
+                                                       const float* __restrict__ shift, const int* __restrict__ idx,
+                                                       __nv_bfloat16* __restrict__ y, float* __restrict__ mean_out,
+                                                       float* __restrict__ rstd_out, int rows, int width, float eps) {
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + (size_t)row * width;
+  float v[NV][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width) {
+      load_vec(xr + c, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[i][j];
+    }
+  }
+  const float mu = warp_sum(s) / width;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[i][j] - mu;
+        ss += d * d;
+      }
+  }
+  const float r = rsqrtf(warp_sum(ss) / width + eps);
+  const size_t m = (size_t)idx[row] * width;
+  __nv_bfloat16* yr = y + (size_t)row * width;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width) {
+      float sc[8], sh[8], o[8];
+      load8(scale + m + c, sc);
+      load8(shift + m + c, sh);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mu) * r * (1.f + sc[j]) + sh[j];
+      store8(yr + c, o);
+    }
+  }
+  if (lane == 0) {
+    mean_out[row] = mu;
+    rstd_out[row] = r;
+  }
+}
+
+// Flush per-warp accumulators of modulation-row `m` into global fp32 gradients.
+template <int NV>
+__device__ __forceinline__ void flush(float (&a)[NV][8], float* dst, int lane, int width) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < width)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (a[i][j] != 0.f) atomicAdd(dst + c + j, a[i][j]);
+        a[i][j] = 0.f;
+      }
+  }
+}
+
+template <int NV, typename T>
+__global__ void __launch_bounds__(256) lnmod_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const T* __restrict__ x,
+                                                       const float* __restrict__ scale, const int* __restrict__ idx,
+                                                       const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                       T* __restrict__ dx, float* __restrict__ dscale,
+                                                       float* __restrict__ dshift, int rows, int width, int per) {
+  const int warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int r0 = warp * per, r1 = min(rows, r0 + per);
+  if (r0 >= rows) return;
+  float as[NV][8], ah[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) as[i][j] = ah[i][j] = 0.f;
+  int cur = idx[r0];
+  for (int row = r0; row < r1; ++row) {
+    const int m = idx[row];
+    if (m != cur) {
+      flush<NV>(as, dscale + (size_t)cur * width, lane, width);
+      flush<NV>(ah, dshift + (size_t)cur * width, lane, width);
+      cur = m;
+    }
+    const float mu = mean[row], r = rstd[row];
+    const size_t off = (size_t)row * width, mo = (size_t)m * width;
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float xv[8], gv[8], sc[8];
+        load_vec(x + off + c, xv);
+        load8(dy + off + c, gv);
+        load8(scale + mo + c, sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = (xv[j] - mu) * r;
+          const float dn = gv[j] * (1.f + sc[j]);
+          as[i][j] += gv[j] * xh;
+          ah[i][j] += gv[j];
+          s1 += dn;
+          s2 += dn * xh;
+        }
+      }
+    }
+    s1 = warp_sum(s1) / width;
+    s2 = warp_sum(s2) / width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float xv[8], gv[8], sc[8], o[8];
+        load_vec(x + off + c, xv);
+        load8(dy + off + c, gv);
+        load8(scale + mo + c, sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = (xv[j] - mu) * r;
+          o[j] = r * (gv[j] * (1.f + sc[j]) - s1 - xh * s2);
+        }
+        store8(dx + off + c, o);
+      }
+    }
+  }
+  flush<NV>(as, dscale + (size_t)cur * width, lane, width);
+  flush<NV>(ah, dshift + (size_t)cur * width, lane, width);
+}
+
+template <typename BT>
+__global__ void gated_add_fwd_kernel(const float* __restrict__ x, const BT* __restrict__ branch,
+                                     const float* __restrict__ gate, const int* __restrict__ idx,
+                                     float* __restrict__ y, int rows, int width) {
+  const size_t vecs = (size_t)rows * width / 8;
+  for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < vecs; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;
+    const int row = (int)(e / width), c = (int)(e % width);
+    float xv[8], bv[8], gv[8], o[8];
+    load8(x + e, xv);
+    load_vec(branch + e, bv);
+    load8(gate + (size_t)idx[row] * width + c, gv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = xv[j] + gv[j] * bv[j];
+    store8(y + e, o);
+  }
+}
+
+template <int NV, typename BT>
+__global__ void __launch_bounds__(256) gated_add_bwd_kernel(const float* __restrict__ dy, const BT* __restrict__ branch,
+                                                           const float* __restrict__ gate, const int* __restrict__ idx,
+                                                           BT* __restrict__ dbranch, float* __restrict__ dgate, int rows,
+                                                           int width, int per) {
+  const int warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int r0 = warp * per, r1 = min(rows, r0 + per);
+  if (r0 >= rows) return;
+  float ag[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ag[i][j] = 0.f;
+  int cur = idx[r0];
+  for (int row = r0; row < r1; ++row) {
+    const int m = idx[row];
+    if (m != cur) {
+      flush<NV>(ag, dgate + (size_t)cur * width, lane, width);
+      cur = m;
+    }
+    const size_t off = (size_t)row * width, mo = (size_t)m * width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float gv[8], bv[8], gt[8], o[8];
+        load8(dy + off + c, gv);
+        load_vec(branch + off + c, bv);
+        load8(gate + mo + c, gt);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ag[i][j] += gv[j] * bv[j];
+          o[j] = gv[j] * gt[j];
+        }
+        store8(dbranch + off + c, o);
+      }
+    }
+  }
+  flush<NV>(ag, dgate + (size_t)cur * width, lane, width);
+}
+
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int rows,
+                                  int half) {
+  const size_t vecs = (size_t)rows * half / 8;
+  for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < vecs; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;
+    const size_t row = e / half, c = e % half;
+    float g[8], u[8], o[8];
+    load8(x + row * 2 * half + c, g);
+    load8(x + row * 2 * half + half + c, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = silu(g[j]) * u[j];
+    store8(y + e, o);
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                  __nv_bfloat16* __restrict__ dx, int rows, int half) {
+  const size_t vecs = (size_t)rows * half / 8;
+  for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < vecs; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;
+    const size_t row = e / half, c = e % half;
+    float g[8], u[8], d[8], dg[8], du[8];
+    load8(x + row * 2 * half + c, g);
+    load8(x + row * 2 * half + half + c, u);
+    load8(dy + e, d);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float sg = 1.f / (1.f + __expf(-g[j]));
+      du[j] = d[j] * g[j] * sg;
+      dg[j] = d[j] * u[j] * sg * (1.f + g[j] * (1.f - sg));
+    }
+    store8(dx + row * 2 * half + c, dg);
+    store8(dx + row * 2 * half + half + c, du);
+  }
+}
+
+int grid_for(size_t vecs) {
+  const size_t blocks = (vecs + 255) / 256;
+  return (int)std::min<size_t>(blocks, (size_t)sm_count() * 16);
+}
+
+#define NV_DISPATCH(width, ...)                                          \
+  [&] {                                                                  \
+    const int nv__ = ((width) + 255) / 256;                              \
+    if (nv__ <= 1) { constexpr int NV = 1; __VA_ARGS__(); }              \
+    else if (nv__ <= 2) { constexpr int NV = 2; __VA_ARGS__(); }         \
+    else if (nv__ <= 4) { constexpr int NV = 4; __VA_ARGS__(); }         \
+    else if (nv__ <= 6) { constexpr int NV = 6; __VA_ARGS__(); }         \
+    else if (nv__ <= 8) { constexpr int NV = 8; __VA_ARGS__(); }         \
+    else TORCH_CHECK(false, "row width above 2048 is not supported"); \
+  }()
+
+void check_rows(const at::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "expected a contiguous 2-D CUDA tensor");
+  TORCH_CHECK(x.size(1) % 8 == 0, "row width must be a multiple of 8");
+}
+
+}  // namespace
+
+std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps) {
+  check_rows(x);
+  const int rows = x.size(0), width = x.size(1);
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (!rows) return {y, rstd};
+  auto wc = w.contiguous();
+  const int blocks = (rows + kWarps - 1) / kWarps;
+  AT_DISPATCH_SWITCH(x.scalar_type(), "rms_norm_fwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
+                       using T = __nv_bfloat16;
+                       NV_DISPATCH(width, [&] {
+                         if (wc.scalar_type() == at::kFloat)
+                           rms_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>(
+                               (const T*)x.data_ptr(), wc.data_ptr<float>(), (T*)y.data_ptr(), rstd.data_ptr<float>(),
+                               rows, width, (float)eps);
+                         else
+                           rms_fwd_kernel<NV, T, T><<<blocks, 256, 0, stream()>>>(
+                               (const T*)x.data_ptr(), (const T*)wc.data_ptr(), (T*)y.data_ptr(), rstd.data_ptr<float>(),
+                               rows, width, (float)eps);
+                       });
+                     }) AT_DISPATCH_CASE(at::kFloat, [&] {
+                       using T = float;
+                       NV_DISPATCH(width, [&] {
+                         auto wf = wc.to(at::kFloat);
+                         rms_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>(
+                             x.data_ptr<float>(), wf.data_ptr<float>(), y.data_ptr<float>(), rstd.data_ptr<float>(), rows,
+                             width, (float)eps);
+                       });
+                     }));
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {y, rstd};
+}
+
+static int bwd_grid(int rows) { return std::max(1, std::min(sm_count(), (rows + 15) / 16)); }
+
+std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd) {
+  check_rows(x);
+  const int rows = x.size(0), width = x.size(1);
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({width}, x.options().dtype(at::kFloat));
+  if (!rows) return {dx, dw};
+  auto wc = w.contiguous();
+  const int grid = bwd_grid(rows);
+  const size_t sm = width * sizeof(float);
+  AT_DISPATCH_SWITCH(x.scalar_type(), "rms_norm_bwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
+                       using T = __nv_bfloat16;
+                       NV_DISPATCH(width, [&] {
+                         if (wc.scalar_type() == at::kFloat)
+                           rms_bwd_kernel<NV, T, float><<<grid, 512, sm, stream()>>>(
+                               (const T*)dy.data_ptr(), (const T*)x.data_ptr(), wc.data_ptr<float>(),
+                               rstd.data_ptr<float>(), (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
+                         else
+                           rms_bwd_kernel<NV, T, T><<<grid, 512, sm, stream()>>>(
+                               (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)wc.data_ptr(),
+                               rstd.data_ptr<float>(), (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
+                       });
+                     }) AT_DISPATCH_CASE(at::kFloat, [&] {
+                       NV_DISPATCH(width, [&] {
+                         auto wf = wc.to(at::kFloat);
+                         rms_bwd_kernel<NV, float, float><<<grid, 512, sm, stream()>>>(
+                             dy.data_ptr<float>(), x.data_ptr<float>(), wf.data_ptr<float>(), rstd.data_ptr<float>(),
+                             dx.data_ptr<float>(), dw.data_ptr<float>(), rows, width);
+                       });
+                     }));
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {dx, dw};
+}
+
+std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w, double eps) {
+  check_rows(x);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && z.scalar_type() == at::kBFloat16, "gated norm expects bf16");
+  const int rows = x.size(0), width = x.size(1);
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (!rows) return {y, rstd};
+  auto wf = w.to(at::kFloat).contiguous();
+  const int blocks = (rows + kWarps - 1) / kWarps;
+  using T = __nv_bfloat16;
+  NV_DISPATCH(width, [&] {
+    gated_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>((const T*)x.data_ptr(), (const T*)z.data_ptr(),
+                                                                 wf.data_ptr<float>(), (T*)y.data_ptr(),
+                                                                 rstd.data_ptr<float>(), rows, width, (float)eps);
+  });
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> gated_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor z, at::Tensor w, at::Tensor rstd) {
+  const int rows = x.size(0), width = x.size(1);
+  auto dx = at::empty_like(x);
+  auto dz = at::empty_like(z);
+  auto dw = at::zeros({width}, x.options().dtype(at::kFloat));
+  if (!rows) return {dx, dz, dw};
+  auto wf = w.to(at::kFloat).contiguous();
+  using T = __nv_bfloat16;
+  const int grid = bwd_grid(rows);
+  NV_DISPATCH(width, [&] {
+    gated_bwd_kernel<NV, T, float><<<grid, 512, width * sizeof(float), stream()>>>(
+        (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)z.data_ptr(), wf.data_ptr<float>(),
+        rstd.data_ptr<float>(), (T*)dx.data_ptr(), (T*)dz.data_ptr(), dw.data_ptr<float>(), rows, width);
+  });
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {dx, dz, dw};
+}
+
+std::vector<at::Tensor> ln_modulate_fwd(at::Tensor x, at::Tensor scale, at::Tensor shift, at::Tensor idx, double eps) {
+  check_rows(x);
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && shift.scalar_type() == at::kFloat, "modulation must be fp32");
+  const int rows = x.size(0), width = x.size(1);
+  auto y = at::empty({rows, width}, x.options().dtype(at::kBFloat16));
+  auto mean = at::empty({rows}, x.options().dtype(at::kFloat));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (!rows) return {y, mean, rstd};
+  const int blocks = (rows + kWarps - 1) / kWarps;
+  AT_DISPATCH_SWITCH(x.scalar_type(), "ln_modulate_fwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
+                       using T = __nv_bfloat16;
+                       NV_DISPATCH(width, [&] {
+                         lnmod_fwd_kernel<NV, T><<<blocks, 256, 0, stream()>>>(
+                             (const T*)x.data_ptr(), scale.data_ptr<float>(), shift.data_ptr<float>(),
+                             idx.data_ptr<int>(), (__nv_bfloat16*)y.data_ptr(), mean.data_ptr<float>(),
+                             rstd.data_ptr<float>(), rows, width, (float)eps);
+                       });
+                     }) AT_DISPATCH_CASE(at::kFloat, [&] {
+                       NV_DISPATCH(width, [&] {
+                         lnmod_fwd_kernel<NV, float><<<blocks, 256, 0, stream()>>>(
+                             x.data_ptr<float>(), scale.data_ptr<float>(), shift.data_ptr<float>(), idx.data_ptr<int>(),
+                             (__nv_bfloat16*)y.data_ptr(), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, width,
+                             (float)eps);
+                       });
+                     }));
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {y, mean, rstd};
+}
+
+std::vector<at::Tensor> ln_modulate_bwd(at::Tensor dy, at::Tensor x, at::Tensor scale, at::Tensor idx, at::Tensor mean,
+                                        at::Tensor rstd) {
+  const int rows = x.size(0), width = x.size(1);
+  auto dx = at::empty_like(x);
+  auto dscale = at::zeros_like(scale);
+  auto dshift = at::zeros_like(scale);
+  if (!rows) return {dx, dscale, dshift};
+  auto dyc = dy.to(at::kBFloat16).contiguous();
+  const int warps_total = std::min(rows, sm_count() * 64);
+  const int per = (rows + warps_total - 1) / warps_total;
+  const int warps_needed = (rows + per - 1) / per;
+  const int blocks = (warps_needed + kWarps - 1) / kWarps;
+  AT_DISPATCH_SWITCH(x.scalar_type(), "ln_modulate_bwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
+                       using T = __nv_bfloat16;
+                       NV_DISPATCH(width, [&] {
+                         lnmod_bwd_kernel<NV, T><<<blocks, 256, 0, stream()>>>(
+                             (const __nv_bfloat16*)dyc.data_ptr(), (const T*)x.data_ptr(), scale.data_ptr<float>(),
+                             idx.data_ptr<int>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), (T*)dx.data_ptr(),
+                             dscale.data_ptr<float>(), dshift.data_ptr<float>(), rows, width, per);
+                       });
+                     }) AT_DISPATCH_CASE(at::kFloat, [&] {
+                       NV_DISPATCH(width, [&] {
+                         lnmod_bwd_kernel<NV, float><<<blocks, 256, 0, stream()>>>(
+                             (const __nv_bfloat16*)dyc.data_ptr(), x.data_ptr<float>(), scale.data_ptr<float>(),
+                             idx.data_ptr<int>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(),
+                             dscale.data_ptr<float>(), dshift.data_ptr<float>(), rows, width, per);
+                       });
+                     }));
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {dx, dscale, dshift};
+}
+
+at::Tensor gated_add_fwd(at::Tensor x, at::Tensor branch, at::Tensor gate, at::Tensor idx) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && gate.scalar_type() == at::kFloat, "gated add expects fp32 x and gate");
+  const int rows = x.size(0), width = x.size(1);
+  auto y = at::empty_like(x);
+  if (!rows) return y;
+  auto b = branch.contiguous();
+  const int grid = grid_for((size_t)rows * width / 8);
+  if (b.scalar_type() == at::kBFloat16)
+    gated_add_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(
+        x.data_ptr<float>(), (const __nv_bfloat16*)b.data_ptr(), gate.data_ptr<float>(), idx.data_ptr<int>(),
+        y.data_ptr<float>(), rows, width);
+  else
+    gated_add_fwd_kernel<float><<<grid, 256, 0, stream()>>>(x.data_ptr<float>(), b.to(at::kFloat).data_ptr<float>(),
+                                                            gate.data_ptr<float>(), idx.data_ptr<int>(),
+                                                            y.data_ptr<float>(), rows, width);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return y;
+}
+
+std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tensor gate, at::Tensor idx) {
+  const int rows = dy.size(0), width = dy.size(1);
+  auto dgate = at::zeros_like(gate);
+  auto dbranch = at::empty_like(branch);
+  if (!rows) return {dbranch, dgate};
+  const int warps_total = std::min(rows, sm_count() * 64);
+  const int per = (rows + warps_total - 1) / warps_total;
+  const int warps_needed = (rows + per - 1) / per;
+  const int blocks = (warps_needed + kWarps - 1) / kWarps;
+  auto dyc = dy.to(at::kFloat).contiguous();
+  NV_DISPATCH(width, [&] {
+    if (branch.scalar_type() == at::kBFloat16)
+      gated_add_bwd_kernel<NV, __nv_bfloat16><<<blocks, 256, 0, stream()>>>(
+          dyc.data_ptr<float>(), (const __nv_bfloat16*)branch.data_ptr(), gate.data_ptr<float>(), idx.data_ptr<int>(),
+          (__nv_bfloat16*)dbranch.data_ptr(), dgate.data_ptr<float>(), rows, width, per);
+    else
+      gated_add_bwd_kernel<NV, float><<<blocks, 256, 0, stream()>>>(
+          dyc.data_ptr<float>(), branch.data_ptr<float>(), gate.data_ptr<float>(), idx.data_ptr<int>(),
+          dbranch.data_ptr<float>(), dgate.data_ptr<float>(), rows, width, per);
+  });
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {dbranch, dgate};
+}
+
+at::Tensor swiglu_fwd(at::Tensor x) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(), "swiglu expects bf16 2-D");
+  const int rows = x.size(0), half = x.size(1) / 2;
+  TORCH_CHECK(half % 8 == 0, "swiglu half width must be a multiple of 8");
+  auto y = at::empty({rows, half}, x.options());
+  if (!rows) return y;
+  swiglu_fwd_kernel<<<grid_for((size_t)rows * half / 8), 256, 0, stream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), (__nv_bfloat16*)y.data_ptr(), rows, half);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return y;
+}
+
+at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x) {
+  const int rows = x.size(0), half = x.size(1) / 2;
+  auto dx = at::empty_like(x);
+  if (!rows) return dx;
+  auto d = dy.contiguous();
+  swiglu_bwd_kernel<<<grid_for((size_t)rows * half / 8), 256, 0, stream()>>>(
+      (const __nv_bfloat16*)d.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (__nv_bfloat16*)dx.data_ptr(), rows,
+      half);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return dx;
+}
+
+}  // namespace cqb

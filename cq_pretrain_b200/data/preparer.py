@@ -1,0 +1,63 @@
+"""Per-consumption flow randomness and host->device preparation of packed batches.
+
+Flow noise, flow times and time features come from a private CPU generator seeded by
+``sha256(snapshot, seed, epoch, rank, serial)`` (reference ``data/codec.py:69-71,128-134``), so
+the draw depends only on which pack is consumed, never on prefetch depth or model RNG.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import torch
+
+from .generation import time_features
+
+
+def consumption_seed(signature, serial) -> int:
+    key = f"{signature['snapshot']}:{signature['seed']}:{signature['epoch']}:{signature['rank']}:{serial}"
+    return int.from_bytes(hashlib.sha256(key.encode()).digest()[:8], "little") & ((1 << 63) - 1)
+
+
+class FakeLatentEncoder:
+    """Deterministic stand-in VAE for pipeline tests: average-pool + fixed channel projection."""
+
+    def __init__(self, channels=16, stride=8):
+        weight = torch.arange(channels * 3, dtype=torch.float32).reshape(-1, 3, 1, 1)
+        self.projection = (weight.remainder(11) - 5) / 15
+        self.stride = stride
+
+    def encode(self, pixels):
+        from torch.nn import functional as F
+        x = F.avg_pool2d(pixels.float(), self.stride)
+        return F.conv2d(x, self.projection.to(x.device))
+
+
+class DevicePreparer:
+    """Attach flow noise/times/time features to a host batch and return a device copy."""
+
+    def __init__(self, cfg, device="cpu", dtype=torch.float32):
+        self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+
+    def randomness(self, batch, receipt):
+        layout = batch.generation
+        if layout is None:
+            return None
+        signature = receipt["next_state"]["documents"].get("signature") or dict(snapshot="synthetic", seed=0, epoch=0, rank=0)
+        gen = torch.Generator().manual_seed(consumption_seed(signature, receipt["serial"]))
+        noise = torch.randn(sum(layout.lengths), self.cfg.latent_channels * 4, generator=gen)
+        times = torch.randn(len(layout.lengths), generator=gen).sigmoid().clamp(1e-5, 1 - 1e-5)
+        return noise, times, time_features(times, self.cfg.wan_freq_dim)
+
+    def __call__(self, batch, receipt, non_blocking=False):
+        extra = self.randomness(batch, receipt)
+        if extra is not None:
+            noise, times, feats = extra
+            batch.noise, batch.times = noise, times
+            batch.generation.time_features = feats
+            if batch.latents is None:
+                raise ValueError("generation targets need latents (cached or encoded)")
+        out = batch.to(self.device, non_blocking=non_blocking)
+        if out.vision is not None and out.vision.features is not None:
+            out.vision.features = out.vision.features.to(self.dtype)
+        return out

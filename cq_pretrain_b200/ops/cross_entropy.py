@@ -1,0 +1,105 @@
+"""Chunked, recomputed linear cross-entropy over a vocabulary-parallel weight.
+
+For each chunk of rows: ``logits = h W_local^T`` (fp32), the row max, target logit and sum of
+exponentials are combined across the TP group, and ``loss = log(sum) + max - target``. No
+``[rows, vocab]`` tensor survives the forward; backward recomputes each chunk, forms
+``dlogits = softmax - onehot``, and accumulates ``dW`` in fp32 (straight into ``main_grad`` when
+present) and ``dh = dlogits W_local`` (summed over TP by the caller's row collective).
+Reference: ``ops/cross_entropy.py:17-116``.
+
+On CUDA the per-chunk work is an LM-head GEMM whose epilogue computes the row statistics
+online (``csrc/ce.cu``), so logits are never written to memory in the forward; the TP combine
+of the three ``[rows]`` statistics uses one all-reduce of a packed ``[3, rows]`` buffer.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _ext
+from . import gemm
+from ..parallel import state as ps
+
+
+def _stats_combine(mx, tgt, sexp, group):
+    """Merge per-rank (max, target logit, sum exp relative to the local max) into global values."""
+    if group is None:
+        return mx, tgt, sexp
+    gmax = mx.clone()
+    dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
+    packed = torch.stack((tgt, sexp * torch.exp(mx - gmax)))
+    dist.all_reduce(packed, group=group)
+    return gmax, packed[0], packed[1]
+
+
+def _chunk_stats(h, w, targets, lo):
+    """Local (max, target logit (0 if not owned), sum exp relative to local max) for one chunk."""
+    if h.is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "ce_stats") and h.dtype == torch.bfloat16 \
+            and w.shape[1] % 16 == 0:
+        return _ext.ops().ce_stats(h.contiguous(), w, targets, lo)
+    logits = gemm.linear(h, w).float()
+    mx = logits.max(-1).values
+    local = targets - lo
+    owned = (local >= 0) & (local < w.shape[0])
+    tgt = logits.gather(1, local.clamp(0, w.shape[0] - 1)[:, None])[:, 0] * owned
+    sexp = torch.exp(logits - mx[:, None]).sum(-1)
+    return mx, tgt, sexp
+
+
+class _LinearCE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, chunk, group, rank):
+        lo = rank * weight.shape[0]
+        total = torch.zeros((), dtype=torch.float32, device=hidden.device)
+        lse_all = torch.empty(hidden.shape[0], dtype=torch.float32, device=hidden.device)
+        for start in range(0, hidden.shape[0], chunk):
+            h, t = hidden[start:start + chunk], targets[start:start + chunk]
+            mx, tgt, sexp = _stats_combine(*_chunk_stats(h, weight, t, lo), group)
+            lse = mx + torch.log(sexp)
+            lse_all[start:start + chunk] = lse
+            total += (lse - tgt).sum()
+        ctx.save_for_backward(hidden, weight, targets, lse_all)
+        ctx.chunk, ctx.lo = chunk, lo
+        return total / max(1, hidden.shape[0])
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        hidden, weight, targets, lse_all = ctx.saved_tensors
+        factor = grad_out.float() / max(1, hidden.shape[0])
+        dh = torch.empty_like(hidden)
+        mg = getattr(weight, "main_grad", None)
+        dw = mg if mg is not None else torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
+        n = weight.shape[0]
+        for start in range(0, hidden.shape[0], ctx.chunk):
+            h, t = hidden[start:start + ctx.chunk], targets[start:start + ctx.chunk]
+            lse = lse_all[start:start + ctx.chunk]
+            if h.is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "ce_grad_logits") \
+                    and h.dtype == torch.bfloat16:
+                grad = _ext.ops().ce_grad_logits(h.contiguous(), weight, t, lse, ctx.lo, factor)
+            else:
+                logits = gemm.linear(h, weight).float()
+                prob = torch.exp(logits - lse[:, None])
+                local = t - ctx.lo
+                owned = (local >= 0) & (local < n)
+                prob.scatter_add_(1, local.clamp(0, n - 1)[:, None], -owned[:, None].to(prob.dtype))
+                grad = (prob * factor).to(hidden.dtype)
+            dh[start:start + ctx.chunk] = gemm.matmul_nn(grad, weight).to(dh.dtype)
+            gemm.matmul_tn_accumulate(grad, h, dw)
+        if mg is not None:
+            cb = getattr(weight, "_grad_ready", None)
+            if cb is not None:
+                cb(weight)
+            return dh, None, None, None, None, None
+        return dh, dw.to(weight.dtype), None, None, None, None
+
+
+def linear_cross_entropy(hidden, weight, targets, chunk):
+    """Mean CE of ``hidden @ W_full^T`` against ``targets``; ``weight`` is this rank's vocab shard.
+
+    ``hidden`` must be identical on every TP rank; its gradient is the local-vocab part, which
+    the caller's row collective sums across ranks.
+    """
+    st = ps.state()
+    group = st.tp_group if st.tp > 1 else None
+    return _LinearCE.apply(hidden, weight, targets, chunk, group, st.tp_rank)

@@ -1,0 +1,120 @@
+"""Linear layers whose weight gradient accumulates straight into an FP32 ``main_grad``.
+
+``y = x W^T + b``. Backward computes ``dX = dY W`` and ``main_grad += dY^T X`` in FP32 without
+materialising a bf16 ``dW`` (reference ``ops/functional.py:31-36`` + ``distributed/megatron.py:45-49``,
+the ``gradient_accumulation_fusion`` contract). When a parameter has no ``main_grad`` (no
+optimizer wrapper) the gradient is returned normally. After accumulating, the parameter's
+``_grad_ready`` callback (set by the data-parallel wrapper) marks it ready so bucket
+reduce-scatters can start while backward continues.
+
+CUDA tensors run the sm_100a GEMM (``gemm.cu``); the fused TP variants run the
+all-gather->GEMM / GEMM->reduce-scatter kernels of ``parallel/fused.py`` when available.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import gemm
+
+
+def _accumulate(param, grad):
+    """Add ``grad`` (fp32 or bf16) into ``param.main_grad`` and fire readiness; returns the autograd grad."""
+    if param is None:
+        return None
+    mg = getattr(param, "main_grad", None)
+    if mg is None:
+        return grad.to(param.dtype)
+    mg.add_(grad.view_as(mg))
+    cb = getattr(param, "_grad_ready", None)
+    if cb is not None:
+        cb(param)
+    return None
+
+
+def _weight_grad(param, dy, x):
+    """``main_grad += dy^T x`` (fp32 accumulate) or return ``dy^T x``."""
+    mg = getattr(param, "main_grad", None)
+    if mg is not None:
+        gemm.matmul_tn_accumulate(dy, x, mg)
+        cb = getattr(param, "_grad_ready", None)
+        if cb is not None:
+            cb(param)
+        return None
+    return gemm.matmul_tn(dy, x).to(param.dtype)
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        ctx.save_for_backward(x, weight)
+        ctx.has_bias = bias is not None
+        ctx.bias = bias
+        return gemm.linear(x, weight, bias)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = gemm.matmul_nn(dy, weight) if ctx.needs_input_grad[0] else None
+        dw = _weight_grad(weight, dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])) if ctx.needs_input_grad[1] else None
+        db = _accumulate(ctx.bias, dy.reshape(-1, dy.shape[-1]).float().sum(0)) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
+def linear(x, weight, bias=None):
+    if not (x.requires_grad or weight.requires_grad or (bias is not None and bias.requires_grad)):
+        return gemm.linear(x, weight, bias)
+    return _Linear.apply(x, weight, bias)
+
+
+class _GatherLinear(torch.autograd.Function):
+    """Column-parallel: ``y = all_gather_rows(x) @ W^T (+ b)``; backward reduce-scatters dX."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        from ..parallel import fused
+        y, xg = fused.gather_linear(x, weight, bias)
+        ctx.save_for_backward(xg, weight)
+        ctx.has_bias, ctx.bias = bias is not None, bias
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..parallel import fused
+        xg, weight = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = fused.linear_scatter_grad(dy, weight) if ctx.needs_input_grad[0] else None
+        dw = _weight_grad(weight, dy, xg) if ctx.needs_input_grad[1] else None
+        db = _accumulate(ctx.bias, dy.float().sum(0)) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
+def gather_linear(x, weight, bias=None):
+    return _GatherLinear.apply(x, weight, bias)
+
+
+class _LinearScatter(torch.autograd.Function):
+    """Row-parallel: ``y = reduce_scatter_rows(x @ W^T) + b``; backward all-gathers dY."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        from ..parallel import fused
+        ctx.save_for_backward(x, weight)
+        ctx.has_bias, ctx.bias = bias is not None, bias
+        return fused.linear_scatter(x, weight, bias)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..parallel import fused
+        x, weight = ctx.saved_tensors
+        dyg = fused.gather_rows_raw(dy.contiguous())
+        dx = gemm.matmul_nn(dyg, weight) if ctx.needs_input_grad[0] else None
+        dw = _weight_grad(weight, dyg, x) if ctx.needs_input_grad[1] else None
+        db = _accumulate(ctx.bias, dy.float().sum(0)) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
+def linear_scatter(x, weight, bias=None):
+    return _LinearScatter.apply(x, weight, bias)

@@ -1,0 +1,109 @@
+"""Normalisation ops: Qwen RMSNorm (1+w), GDN gated RMSNorm, Wan adaLN modulate and gated residual.
+
+CUDA bf16/fp32 tensors run the row kernels of ``csrc/rowops.cu`` (one warp per row, fp32
+statistics, fused backward with an fp32 weight-gradient reduction); CPU runs ``reference``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+from . import reference as R
+
+
+def _use_kernel(x):
+    return x.is_cuda and _ext.has("rms_norm_fwd") and x.dtype in (torch.bfloat16, torch.float32)
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y, rstd = _ext.ops().rms_norm_fwd(x.contiguous(), weight.contiguous(), eps)
+        ctx.save_for_backward(x, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, rstd = ctx.saved_tensors
+        dx, dw = _ext.ops().rms_norm_bwd(dy.contiguous(), x.contiguous(), weight.contiguous(), rstd)
+        return dx, dw.to(weight.dtype), None
+
+
+def rms_norm(x, weight, eps):
+    """Qwen RMSNorm ``x rsqrt(mean x^2 + eps) (1 + w)``."""
+    if _use_kernel(x) and x.shape[-1] % 8 == 0:
+        shape = x.shape
+        return _RMSNorm.apply(x.reshape(-1, shape[-1]), weight, eps).reshape(shape)
+    return R.rms_norm(x, weight, eps)
+
+
+class _GatedNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, z, weight, eps):
+        y, rstd = _ext.ops().gated_norm_fwd(x.contiguous(), z.contiguous(), weight.contiguous(), eps)
+        ctx.save_for_backward(x, z, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, z, weight, rstd = ctx.saved_tensors
+        dx, dz, dw = _ext.ops().gated_norm_bwd(dy.contiguous(), x, z, weight, rstd)
+        return dx, dz, dw.to(weight.dtype), None
+
+
+def gated_rms_norm(x, z, weight, eps):
+    """``rms(x) * w * silu(z)`` over the last dim (one GDN head)."""
+    if _use_kernel(x) and x.shape[-1] % 8 == 0 and z.dtype == x.dtype:
+        shape = x.shape
+        return _GatedNorm.apply(x.reshape(-1, shape[-1]), z.reshape(-1, shape[-1]), weight, eps).reshape(shape)
+    return R.gated_rms_norm(x, z, weight, eps)
+
+
+class _Modulate(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, scale, shift, index, eps):
+        y, mean, rstd = _ext.ops().ln_modulate_fwd(x.contiguous(), scale.contiguous(), shift.contiguous(), index, eps)
+        ctx.save_for_backward(x, scale, index, mean, rstd)
+        ctx.nmod = scale.shape[0]
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, scale, index, mean, rstd = ctx.saved_tensors
+        dx, dscale, dshift = _ext.ops().ln_modulate_bwd(dy.contiguous(), x, scale, index, mean, rstd)
+        return dx, dscale, dshift, None, None
+
+
+def layer_norm_modulate(x, scale, shift, eps, index=None):
+    """``LN(x) (1 + scale[index]) + shift[index]`` in fp32; ``index`` maps rows to modulation rows."""
+    if _use_kernel(x) and x.shape[-1] % 8 == 0 and scale.dtype == torch.float32:
+        idx = index if index is not None else torch.arange(x.shape[0], device=x.device)
+        return _Modulate.apply(x, scale, shift, idx.to(torch.int32).contiguous(), eps)
+    if index is not None:
+        scale, shift = scale.index_select(0, index), shift.index_select(0, index)
+    return R.layer_norm_modulate(x, scale, shift, eps)
+
+
+class _GatedAdd(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, branch, gate, index):
+        y = _ext.ops().gated_add_fwd(x.contiguous(), branch.contiguous(), gate.contiguous(), index)
+        ctx.save_for_backward(branch, gate, index)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        branch, gate, index = ctx.saved_tensors
+        dbranch, dgate = _ext.ops().gated_add_bwd(dy.contiguous(), branch, gate, index)
+        return dy, dbranch, dgate, None
+
+
+def gated_add(x, branch, gate, index=None):
+    """fp32 ``x + gate[index] * branch``."""
+    if _use_kernel(x) and x.dtype == torch.float32 and gate.dtype == torch.float32 and x.shape[-1] % 8 == 0:
+        idx = index if index is not None else torch.arange(x.shape[0], device=x.device)
+        return _GatedAdd.apply(x, branch, gate, idx.to(torch.int32).contiguous())
+    if index is not None:
+        gate = gate.index_select(0, index)
+    return R.gated_add(x, branch, gate)

@@ -1,0 +1,303 @@
+"""Data parallelism with a ZeRO-1 distributed AdamW optimizer.
+
+Layout (reference ``distributed/megatron.py:210-240`` used Megatron DDP + distributed optimizer):
+
+* parameters of one dtype live as views of one flat buffer; gradients accumulate in a flat
+  FP32 ``main_grad`` buffer with the same layout (``gradient_accumulation_fusion``);
+* the buffers are cut into buckets (about ``bucket_size`` elements, reverse registration
+  order = backward order), each padded to a multiple of the DP size;
+* each bucket is reduce-scattered over DP in FP32 (averaged), so rank ``r`` owns shard ``r``
+  of every bucket; AdamW updates the FP32 master copy of the owned shard; the updated shard
+  is cast and all-gathered back into the parameter buffer;
+* under sequence-parallel TP, parameters replicated across the TP group (norms, biases of
+  row-parallel linears, DiT modulation/time layers) receive partial gradients on each TP
+  rank; their gradients are summed over TP (one coalesced all-reduce) before DP reduction
+  (reference ``distributed/megatron.py:243-266`` did this for the Q/K norms);
+* bucket reduce-scatters are dispatched in one fixed index order on every rank, so ranks
+  whose batches skip a branch (no images, no text) still issue identical collective
+  sequences (reference ``distributed/communication.py:12-116``). With ``overlap=True`` a
+  bucket launches during backward once every parameter reported its gradient (counts learned
+  on the first step; ``suspend_readiness`` keeps non-final DiT chunks from triggering it).
+
+The grad-norm clip (1.0), betas (0.9, 0.95), eps 1e-8, decoupled weight decay (not on
+biases / 1-D parameters) and ``min_lr = 0.1 lr`` follow the reference optimizer config. On
+CUDA the update of all owned shards is one multi-tensor kernel (``csrc/adam.cu``) that also
+applies the renderer EMA to its shards.
+"""
+
+from __future__ import annotations
+
+import math
+from contextlib import contextmanager
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+from . import state as ps
+
+
+class Bucket:
+    def __init__(self, index, group, start, end, params):
+        self.index, self.group, self.start, self.end = index, group, start, end
+        self.params = params
+        self.handle = None
+        self.launched = False
+        self.counts = {}
+
+
+class ParamGroup:
+    """One dtype (and replication class): flat param + fp32 grad buffers."""
+
+    def __init__(self, name, dtype, params, device, dp, bucket_size, align=128):
+        self.name, self.dtype, self.params = name, dtype, params
+        offsets, cursor = {}, 0
+        bucket_bounds, bucket_start, bucket_params, current = [], 0, [], []
+        unit = dp * align
+        for p in params:
+            offsets[p] = cursor
+            cursor += p.numel()
+            current.append(p)
+            if cursor - bucket_start >= bucket_size:
+                end = -(-cursor // unit) * unit
+                bucket_bounds.append((bucket_start, end, current))
+                cursor = bucket_start = end
+                current = []
+        if current:
+            end = -(-cursor // unit) * unit
+            bucket_bounds.append((bucket_start, end, current))
+            cursor = end
+        self.numel = cursor
+        self.param_buffer = torch.zeros(cursor, dtype=dtype, device=device)
+        self.grad_buffer = torch.zeros(cursor, dtype=torch.float32, device=device)
+        self.offsets = offsets
+        self.bucket_bounds = bucket_bounds
+        for p in params:
+            o = offsets[p]
+            view = self.param_buffer[o:o + p.numel()].view_as(p)
+            view.copy_(p.data)
+            p.data = view
+            p.main_grad = self.grad_buffer[o:o + p.numel()].view_as(p)
+
+
+class DistributedOptimizer:
+    def __init__(self, model, lr, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8, clip_grad=1.0,
+                 bucket_size=40_000_000, overlap=False, ema_prefix=None, ema_decay=None):
+        st = ps.state()
+        self.model = model
+        self.lr, self.weight_decay, self.betas, self.eps, self.clip_grad = lr, weight_decay, betas, eps, clip_grad
+        self.dp, self.dp_rank, self.dp_group = st.dp, st.dp_rank, st.dp_group
+        self.tp, self.tp_group, self.tp_rank = st.tp, st.tp_group, st.tp_rank
+        self.overlap = overlap
+        named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+        self.names = {p: n for n, p in named}
+        device = named[0][1].device
+        groups: dict = {}
+        for n, p in reversed(named):
+            replicated = self.tp > 1 and not getattr(p, "tensor_model_parallel", False)
+            key = (p.dtype, replicated)
+            groups.setdefault(key, []).append(p)
+        self.groups = []
+        for (dtype, replicated), params in sorted(groups.items(), key=lambda kv: (kv[0][1], str(kv[0][0]))):
+            name = f"{str(dtype).split('.')[-1]}{'-replicated' if replicated else ''}"
+            g = ParamGroup(name, dtype, params, device, self.dp, bucket_size)
+            g.replicated = replicated
+            self.groups.append(g)
+        self.buckets = []
+        for g in self.groups:
+            for start, end, params in g.bucket_bounds:
+                self.buckets.append(Bucket(len(self.buckets), g, start, end, params))
+        self.param_bucket = {p: b for b in self.buckets for p in b.params}
+        # Owned shard state (fp32 master, exp_avg, exp_avg_sq, decay mask, ema shadow).
+        self.shards = []
+        for b in self.buckets:
+            n = (b.end - b.start) // self.dp
+            lo = b.start + self.dp_rank * n
+            master = b.group.param_buffer[lo:lo + n].float().clone()
+            decay = torch.zeros(n, dtype=torch.float32, device=device)
+            ema_mask = torch.zeros(n, dtype=torch.bool, device=device)
+            for p in b.params:
+                o = b.group.offsets[p]
+                a, e = max(o, lo), min(o + p.numel(), lo + n)
+                if a < e:
+                    name = self.names[p]
+                    if p.dim() > 1 and not name.endswith(".bias"):
+                        decay[a - lo:e - lo] = 1.0
+                    if ema_prefix and name.startswith(ema_prefix):
+                        ema_mask[a - lo:e - lo] = True
+            self.shards.append(dict(bucket=b, lo=lo, n=n, master=master, exp_avg=torch.zeros_like(master),
+                                    exp_avg_sq=torch.zeros_like(master), decay=decay, ema_mask=ema_mask))
+        self.step_count = 0
+        self.learned = False
+        self.suspended = 0
+        self.next_bucket = 0
+        for p in self.names:
+            p._grad_ready = self._mark
+            if not getattr(p, "_direct_main_grad", False):
+                p.register_post_accumulate_grad_hook(self._accumulate_hook)
+
+    # ---- gradient flow ---------------------------------------------------------------------------
+    def _accumulate_hook(self, p):
+        if p.grad is not None:
+            p.main_grad.add_(p.grad.view_as(p.main_grad))
+            p.grad = None
+        self._mark(p)
+
+    def _mark(self, p):
+        b = self.param_bucket.get(p)
+        if b is None:
+            return
+        if b.launched:
+            raise RuntimeError(f"gradient of {self.names[p]} arrived after its bucket reduce-scatter started")
+        if self.suspended:
+            return
+        b.counts[p] = b.counts.get(p, 0) + 1
+        if self.overlap and self.learned and not b.group.replicated:
+            self._dispatch_ready()
+
+    def _bucket_ready(self, b):
+        return all(b.counts.get(p, 0) >= self.expected.get(p, 1) for p in b.params)
+
+    def _dispatch_ready(self):
+        while self.next_bucket < len(self.buckets):
+            b = self.buckets[self.next_bucket]
+            if b.group.replicated or not self._bucket_ready(b):
+                return
+            self._launch(b)
+
+    def _launch(self, b):
+        n = (b.end - b.start) // self.dp
+        full = b.group.grad_buffer[b.start:b.end]
+        if self.dp > 1:
+            out = full[self.dp_rank * n:(self.dp_rank + 1) * n]
+            b.handle = dist.reduce_scatter_tensor(out, full, op=dist.ReduceOp.SUM, group=self.dp_group, async_op=True)
+        b.launched = True
+        self.next_bucket = max(self.next_bucket, b.index + 1)
+
+    @contextmanager
+    def suspend_readiness(self):
+        """Gradients accumulate but do not count toward bucket readiness (non-final DiT chunks)."""
+        self.suspended += 1
+        try:
+            yield
+        finally:
+            self.suspended -= 1
+
+    @contextmanager
+    def no_sync(self):
+        """Gradient accumulation micro-batch: accumulate only; nothing is reduced."""
+        previous = self.overlap
+        self.overlap = False
+        self.suspended += 1
+        try:
+            yield
+        finally:
+            self.suspended -= 1
+            self.overlap = previous
+
+    def zero_grad(self):
+        for g in self.groups:
+            g.grad_buffer.zero_()
+        for b in self.buckets:
+            b.launched, b.handle, b.counts = False, None, {}
+        self.next_bucket = 0
+
+    def finish_grad_sync(self):
+        """TP-sum replicated grads, then reduce-scatter every bucket over DP in fixed order."""
+        if not self.learned:
+            self.expected = {p: max(1, b.counts.get(p, 1)) for b in self.buckets for p in b.params}
+            self.learned = True
+        if self.tp > 1:
+            for g in self.groups:
+                if g.replicated:
+                    dist.all_reduce(g.grad_buffer, group=self.tp_group)
+        for b in self.buckets:
+            if not b.launched:
+                self._launch(b)
+        for b in self.buckets:
+            if b.handle is not None:
+                b.handle.wait()
+                b.handle = None
+
+    # ---- optimizer -----------------------------------------------------------------------------
+    def _grad_shard(self, s):
+        b = s["bucket"]
+        return b.group.grad_buffer[s["lo"]:s["lo"] + s["n"]]
+
+    def grad_norm(self):
+        total = torch.zeros((), dtype=torch.float32, device=self.shards[0]["master"].device)
+        for s in self.shards:
+            g = self._grad_shard(s)
+            if s["bucket"].group.replicated and self.tp_rank != 0:
+                continue
+            total += g.float().square().sum()
+        if self.dp > 1:
+            dist.all_reduce(total, group=self.dp_group)
+        if self.tp > 1:
+            dist.all_reduce(total, group=self.tp_group)
+        return total.sqrt()
+
+    @torch.no_grad()
+    def step(self, lr=None, ema_decay=None):
+        """Average, clip, AdamW-update owned shards, optional EMA, then all-gather parameters."""
+        lr = self.lr if lr is None else lr
+        self.step_count += 1
+        scale = 1.0 / self.dp
+        norm = self.grad_norm() * scale
+        coef = torch.clamp(self.clip_grad / (norm + 1e-6), max=1.0) if self.clip_grad else torch.ones_like(norm)
+        finite = torch.isfinite(norm)
+        b1, b2 = self.betas
+        bc1 = 1 - b1 ** self.step_count
+        bc2 = 1 - b2 ** self.step_count
+        grads = [self._grad_shard(s) for s in self.shards]
+        gscale = (coef * scale)
+        use_kernel = grads[0].is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "adamw_step")
+        if use_kernel:
+            _ext.ops().adamw_step([s["master"] for s in self.shards], grads, [s["exp_avg"] for s in self.shards],
+                                  [s["exp_avg_sq"] for s in self.shards], [s["decay"] for s in self.shards],
+                                  gscale, lr, b1, b2, self.eps, self.weight_decay, bc1, bc2)
+        else:
+            for s, g in zip(self.shards, grads):
+                g = g * gscale
+                m, v, p = s["exp_avg"], s["exp_avg_sq"], s["master"]
+                m.mul_(b1).add_(g, alpha=1 - b1)
+                v.mul_(b2).addcmul_(g, g, value=1 - b2)
+                update = (m / bc1) / ((v / bc2).sqrt() + self.eps)
+                p.mul_(1 - lr * self.weight_decay * s["decay"])
+                p.add_(update, alpha=-lr)
+        for s in self.shards:
+            b = s["bucket"]
+            b.group.param_buffer[s["lo"]:s["lo"] + s["n"]].copy_(s["master"])
+        self.all_gather_params()
+        return finite, norm
+
+    def all_gather_params(self):
+        if self.dp == 1:
+            return
+        handles = []
+        for b in self.buckets:
+            n = (b.end - b.start) // self.dp
+            full = b.group.param_buffer[b.start:b.end]
+            handles.append(dist.all_gather_into_tensor(full, full[self.dp_rank * n:(self.dp_rank + 1) * n].clone(),
+                                                       group=self.dp_group, async_op=True))
+        for h in handles:
+            h.wait()
+
+    # ---- checkpoint -------------------------------------------------------------------------
+    def state_dict(self):
+        return dict(step=self.step_count,
+                    shards=[dict(master=s["master"], exp_avg=s["exp_avg"], exp_avg_sq=s["exp_avg_sq"]) for s in self.shards],
+                    layout=[(s["bucket"].group.name, s["lo"], s["n"]) for s in self.shards])
+
+    @torch.no_grad()
+    def load_state_dict(self, state):
+        layout = [(s["bucket"].group.name, s["lo"], s["n"]) for s in self.shards]
+        if [tuple(x) for x in state["layout"]] != layout:
+            raise ValueError("optimizer shard layout differs from the checkpoint")
+        for s, saved in zip(self.shards, state["shards"]):
+            for key in ("master", "exp_avg", "exp_avg_sq"):
+                s[key].copy_(saved[key])
+            b = s["bucket"]
+            b.group.param_buffer[s["lo"]:s["lo"] + s["n"]].copy_(s["master"])
+        self.step_count = state["step"]
+        self.all_gather_params()

@@ -1,0 +1,240 @@
+"""Sequence-parallel tensor-parallel layers.
+
+Between modules every activation is row-sharded across the TP group (``[rows/tp, width]``).
+A column-parallel linear all-gathers the rows and multiplies by its output-column shard; a
+row-parallel linear multiplies by its input-row shard and reduce-scatters the rows. This is
+mathematically the reference's Megatron TP (column: identity fwd / all-reduce dX bwd; row:
+all-reduce fwd, ``distributed/megatron.py:118-196``) with the all-reduce split into
+reduce-scatter + all-gather around the row-local work (norms, residuals), which then runs on
+1/tp of the rows. On CUDA the gather and scatter are fused into the GEMM kernels
+(``parallel/fused.py``); NCCL is the baseline path.
+
+Parameters carry ``tensor_model_parallel``, ``partition_dim``, ``partition_stride`` and optional
+``_checkpoint_splits`` (logical fused-projection widths), as in the reference, so checkpoint
+slicing and TP resharding can reconstruct official tensors.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import state as ps
+from ..ops import linear as L
+
+
+def mark_sharded(parameter, dim=0, stride=1, splits=None):
+    parameter.tensor_model_parallel = True
+    parameter.partition_dim = dim
+    parameter.partition_stride = stride
+    if splits is not None:
+        parameter._checkpoint_splits = tuple(splits)
+    return parameter
+
+
+def normal_init(tensor, std=0.02, generator=None):
+    return nn.init.normal_(tensor, std=std, generator=generator)
+
+
+# ---- row (sequence) collectives -----------------------------------------------------------
+def _gather_rows(x, group, world):
+    out = x.new_empty((x.shape[0] * world, *x.shape[1:]))
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def _scatter_rows(x, group, world):
+    out = x.new_empty((x.shape[0] // world, *x.shape[1:]))
+    dist.reduce_scatter_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+class GatherRows(torch.autograd.Function):
+    """All-gather row shards (forward) / reduce-scatter row gradients (backward)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        st = ps.state()
+        return _gather_rows(x, st.tp_group, st.tp)
+
+    @staticmethod
+    def backward(ctx, grad):
+        st = ps.state()
+        return _scatter_rows(grad, st.tp_group, st.tp)
+
+
+class ScatterRows(torch.autograd.Function):
+    """Reduce-scatter partial rows (forward) / all-gather gradients (backward)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        st = ps.state()
+        return _scatter_rows(x, st.tp_group, st.tp)
+
+    @staticmethod
+    def backward(ctx, grad):
+        st = ps.state()
+        return _gather_rows(grad, st.tp_group, st.tp)
+
+
+class SplitRows(torch.autograd.Function):
+    """Keep this rank's row shard of a replicated tensor (forward) / all-gather (backward)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        st = ps.state()
+        n = x.shape[0] // st.tp
+        return x[st.tp_rank * n:(st.tp_rank + 1) * n].contiguous()
+
+    @staticmethod
+    def backward(ctx, grad):
+        st = ps.state()
+        return _gather_rows(grad, st.tp_group, st.tp)
+
+
+class ReduceTP(torch.autograd.Function):
+    """Sum over the TP group (forward) / identity (backward): partial statistics."""
+
+    @staticmethod
+    def forward(ctx, x):
+        x = x.clone()
+        dist.all_reduce(x, group=ps.state().tp_group)
+        return x
+
+    @staticmethod
+    def backward(ctx, grad):
+        return grad
+
+
+class ReplicatedUse(torch.autograd.Function):
+    """Identity forward; gradient divided by TP size.
+
+    Marks a branch that every TP rank evaluates identically on a gathered tensor, so the
+    gather's reduce-scatter backward (a sum over ranks) restores the exact gradient.
+    """
+
+    @staticmethod
+    def forward(ctx, x):
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, grad):
+        return grad / ps.tp_size()
+
+
+def replicated_use(x):
+    return ReplicatedUse.apply(x) if ps.tp_size() > 1 else x
+
+
+def gather_rows(x):
+    return GatherRows.apply(x) if ps.tp_size() > 1 else x
+
+
+def scatter_rows(x):
+    return ScatterRows.apply(x) if ps.tp_size() > 1 else x
+
+
+def split_rows(x):
+    return SplitRows.apply(x) if ps.tp_size() > 1 else x
+
+
+def reduce_tp(x):
+    return ReduceTP.apply(x) if ps.tp_size() > 1 else x
+
+
+def local_row_range(rows: int):
+    tp, r = ps.tp_size(), ps.tp_rank()
+    n = rows // tp
+    return r * n, (r + 1) * n
+
+
+# ---- layers -------------------------------------------------------------------------------
+class ColumnLinear(nn.Module):
+    """``y[:, shard] = gather(x) @ W[shard]^T``; ``out_features`` split over TP (``stride`` for fused pairs)."""
+
+    def __init__(self, in_features, out_features, bias=False, stride=1, splits=None):
+        super().__init__()
+        tp = ps.tp_size()
+        if out_features % tp:
+            raise ValueError(f"output width {out_features} not divisible by TP={tp}")
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = nn.Parameter(torch.empty(out_features // tp, in_features))
+        normal_init(self.weight)
+        mark_sharded(self.weight, 0, stride, splits)
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_features // tp))
+            mark_sharded(self.bias, 0, stride, splits)
+        else:
+            self.register_parameter("bias", None)
+
+    def forward(self, x, gathered=False):
+        if ps.tp_size() > 1 and not gathered:
+            return L.gather_linear(x, self.weight, self.bias)
+        return L.linear(x, self.weight, self.bias)
+
+
+class RowLinear(nn.Module):
+    """``y = scatter(x[:, shard] @ W[:, shard]^T) + b``; ``in_features`` split over TP."""
+
+    def __init__(self, in_features, out_features, bias=False):
+        super().__init__()
+        tp = ps.tp_size()
+        if in_features % tp:
+            raise ValueError(f"input width {in_features} not divisible by TP={tp}")
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = nn.Parameter(torch.empty(out_features, in_features // tp))
+        normal_init(self.weight)
+        mark_sharded(self.weight, 1)
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_features))
+        else:
+            self.register_parameter("bias", None)
+
+    def forward(self, x):
+        if ps.tp_size() > 1:
+            return L.linear_scatter(x, self.weight, self.bias)
+        return L.linear(x, self.weight, self.bias)
+
+
+class VocabEmbedding(nn.Module):
+    """Vocabulary-parallel embedding; output is row-sharded (partial lookups reduce-scattered)."""
+
+    def __init__(self, vocab, width):
+        super().__init__()
+        tp = ps.tp_size()
+        if vocab % tp:
+            raise ValueError("vocabulary must divide TP")
+        self.vocab, self.width = vocab, width
+        self.weight = nn.Parameter(torch.empty(vocab // tp, width))
+        normal_init(self.weight)
+        mark_sharded(self.weight, 0)
+
+    def partial(self, ids):
+        """This rank's masked lookup ``[n, width]`` (full rows, zero outside the local vocab range)."""
+        n = self.weight.shape[0]
+        lo = ps.tp_rank() * n
+        local = ids - lo
+        owned = (local >= 0) & (local < n)
+        out = nn.functional.embedding(local.clamp(0, n - 1), self.weight)
+        if ps.tp_size() > 1:
+            out = out * owned[:, None].to(out.dtype)
+        return out
+
+    def forward(self, ids):
+        return scatter_rows(self.partial(ids))
+
+
+def checkpoint_shard(value, parameter):
+    """Slice a full (official) tensor into this rank's TP view, honouring stride and logical splits."""
+    if ps.tp_size() == 1 or not getattr(parameter, "tensor_model_parallel", False):
+        return value
+    dim, rank, size = parameter.partition_dim, ps.tp_rank(), ps.tp_size()
+    splits = getattr(parameter, "_checkpoint_splits", None)
+    if splits is not None:
+        return torch.cat([part.chunk(size, dim=dim)[rank] for part in value.split(splits, dim=dim)], dim=dim)
+    stride = getattr(parameter, "partition_stride", 1)
+    chunks = value.split(value.shape[dim] // size // stride, dim=dim)
+    return torch.cat(chunks[rank::size], dim=dim)
