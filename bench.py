@@ -94,6 +94,7 @@ def main():
     parser.add_argument("--length", type=int, default=8192)
     parser.add_argument("--images", type=int, default=2)
     parser.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid as a bench value)")
+    parser.add_argument("--recompute", type=int, default=1, help="recompute backbone layers in backward")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_unavailable(args)
@@ -115,7 +116,8 @@ def main():
     tp = args.tp or (2 if args.gpus >= 2 else 1)
     st = ps.initialize(tp, timeout_s=600.0)
     rank = st.rank
-    cfg = qwen35_2b_wan(visual_query_mode="fixed", image_condition_queries=256)
+    cfg = qwen35_2b_wan(visual_query_mode="fixed", image_condition_queries=256,
+                        checkpoint_backbone=args.recompute)
     if args.layers:
         cfg.layers, cfg.dit_layers = args.layers, max(1, args.layers)
     cfg.validate(tp)

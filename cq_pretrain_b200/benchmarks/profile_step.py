@@ -1,0 +1,50 @@
+"""Per-kernel device-time breakdown of one joint training step (torch.profiler, CUPTI).
+
+``python -m cq_pretrain_b200.benchmarks.profile_step [--length 8192] [--recompute 1]`` runs the
+bench configuration (1 GPU), warms up, profiles one step and prints the kernels with the
+largest total device time, grouped by name, plus each group's share of the step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--length", type=int, default=8192)
+    parser.add_argument("--recompute", type=int, default=1)
+    parser.add_argument("--top", type=int, default=40)
+    parser.add_argument("--layers", type=int, default=None)
+    args = parser.parse_args()
+    from ..config import qwen35_2b_wan
+    from ..data.synthetic import synthetic_batch
+    from ..train.trainer import Trainer
+
+    cfg = qwen35_2b_wan(visual_query_mode="fixed", image_condition_queries=256, checkpoint_backbone=bool(args.recompute))
+    if args.layers:
+        cfg.layers = args.layers
+    host, receipt = synthetic_batch(cfg, args.length, seed=42, kind="joint", images=2, grid=(1, 64, 64),
+                                    latent_shape=(16, 1, 64, 64), understanding=False, pad_multiple=128)
+    host = host.pin_memory()
+    trainer = Trainer(cfg, tp=1, lr=5e-5, ema_decay=0.999)
+    for _ in range(3):
+        trainer.train_step([(host, receipt)])
+    torch.cuda.synchronize()
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        trainer.train_step([(host, receipt)])
+        torch.cuda.synchronize()
+    events = prof.key_averages()
+    total = sum(e.self_device_time_total for e in events)
+    rows = sorted(events, key=lambda e: -e.self_device_time_total)[: args.top]
+    print(json.dumps(dict(total_device_ms=round(total / 1000, 2), peak_gib=round(torch.cuda.max_memory_allocated() / 2**30, 1))))
+    for e in rows:
+        print(f"{e.self_device_time_total / 1000:9.2f} ms {100 * e.self_device_time_total / total:5.1f}% {e.count:6d}x  {e.key[:110]}")
+
+
+if __name__ == "__main__":
+    main()

@@ -23,6 +23,16 @@ at::Tensor gated_add_fwd(at::Tensor x, at::Tensor branch, at::Tensor gate, at::T
 std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tensor gate, at::Tensor idx);
 at::Tensor swiglu_fwd(at::Tensor x);
 at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x);
+// gemm.cu
+at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
+at::Tensor gemm_nn(at::Tensor a, at::Tensor b);
+void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out);
+int gemm_status(bool reset);
+// gdn.cu
+std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
+                                at::Tensor start, at::Tensor count);
+at::Tensor gdn_bwd(at::Tensor dO, at::Tensor W, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
+                   at::Tensor start, at::Tensor count);
 }  // namespace cqb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -38,4 +48,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_add_bwd", &cqb::gated_add_bwd);
   m.def("swiglu_fwd", &cqb::swiglu_fwd);
   m.def("swiglu_bwd", &cqb::swiglu_bwd);
+  m.def("gemm_nt", &cqb::gemm_nt, py::arg("x"), py::arg("w"), py::arg("bias") = py::none());
+  m.def("gemm_nn", &cqb::gemm_nn);
+  m.def("gemm_tn_acc", &cqb::gemm_tn_acc);
+  m.def("gemm_status", &cqb::gemm_status, py::arg("reset") = false);
+  m.def("gdn_fwd", &cqb::gdn_fwd);
+  m.def("gdn_bwd", &cqb::gdn_bwd);
 }

@@ -22,7 +22,7 @@ def _kernel_ok(*ts):
     if not _ext.cuda_kernels_enabled():
         return False
     for t in ts:
-        if not (t.is_cuda and t.dtype == torch.bfloat16):
+        if not (t.is_cuda and t.dtype == torch.bfloat16 and t.data_ptr() % 16 == 0):
             return False
     return True
 
@@ -61,8 +61,8 @@ def matmul_tn(a, b):
 
 def matmul_tn_accumulate(a, b, out):
     """``out += a^T @ b`` accumulated in fp32 (``out`` fp32 ``[N, K]``)."""
-    if _kernel_ok(a, b) and _ext.has("gemm_tn_acc") and out.is_cuda and out.dtype == torch.float32 and _aligned(a.shape[1], b.shape[1], a.shape[0]) \
-            and a.shape[0] % 16 == 0 and a.shape[0] > 0:
+    if _kernel_ok(a, b) and _ext.has("gemm_tn_acc") and out.is_cuda and out.dtype == torch.float32 \
+            and a.shape[1] % 16 == 0 and b.shape[1] % 16 == 0 and a.shape[0] > 0 and out.is_contiguous():
         _ext.ops().gemm_tn_acc(a.contiguous(), b.contiguous(), out)
         return out
     if a.is_cuda:

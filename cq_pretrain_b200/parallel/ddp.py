@@ -55,6 +55,7 @@ class ParamGroup:
         bucket_bounds, bucket_start, bucket_params, current = [], 0, [], []
         unit = dp * align
         for p in params:
+            cursor = -(-cursor // 64) * 64  # 128-byte aligned parameter views (TMA / vector loads)
             offsets[p] = cursor
             cursor += p.numel()
             current.append(p)
