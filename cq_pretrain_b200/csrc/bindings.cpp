@@ -33,6 +33,11 @@ std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Te
                                 at::Tensor start, at::Tensor count);
 at::Tensor gdn_bwd(at::Tensor dO, at::Tensor W, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                    at::Tensor start, at::Tensor count);
+// attention.cu
+std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor kstart, at::Tensor kend,
+                                 double scale);
+std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
+                                 at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale);
 }  // namespace cqb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -54,4 +59,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_status", &cqb::gemm_status, py::arg("reset") = false);
   m.def("gdn_fwd", &cqb::gdn_fwd);
   m.def("gdn_bwd", &cqb::gdn_bwd);
+  m.def("attn_fwd", &cqb::attn_fwd);
+  m.def("attn_bwd", &cqb::attn_bwd);
 }

@@ -85,8 +85,9 @@ def gated_delta_cuda(q, k, v, g, beta, bounds, chunk=CHUNK):
     if Dk != 128 or Dv % 64 or chunk != CHUNK:
         return R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk).to(v.dtype)
     idx, pad, keep, start, count, Nc = _layout(tuple(int(x) for x in bounds), chunk, q.device)
-    qn = R.l2norm(q) * Dk ** -0.5
-    kn = R.l2norm(k)
+    bf = torch.bfloat16
+    qn = (R.l2norm(q) * Dk ** -0.5).to(bf)
+    kn = R.l2norm(k).to(bf)
     padc = pad.view(-1, 1, 1)
 
     def gather(t):
@@ -95,30 +96,29 @@ def gated_delta_cuda(q, k, v, g, beta, bounds, chunk=CHUNK):
 
     Q = gather(qn).view(Nc, chunk, H, Dk).transpose(1, 2)
     K = gather(kn).view(Nc, chunk, H, Dk).transpose(1, 2)
-    V = gather(v.float()).view(Nc, chunk, H, Dv).transpose(1, 2)
+    V = gather(v.to(bf)).view(Nc, chunk, H, Dv).transpose(1, 2)
     G = gather(g.float()).view(Nc, chunk, H).transpose(1, 2)
     B = gather(beta.float()).view(Nc, chunk, H).transpose(1, 2)
     b = G.cumsum(-1)
     diff = b[..., :, None] - b[..., None, :]
     tri = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device)
     strict, incl = tri.tril(-1), tri.tril()
-    e_strict = torch.where(strict, diff, torch.full_like(diff, -math.inf)).exp()
-    e_incl = torch.where(incl, diff, torch.full_like(diff, -math.inf)).exp()
-    Kb, Qb = K.to(torch.bfloat16), Q.to(torch.bfloat16)
-    KK = torch.matmul(Kb, Kb.transpose(-1, -2)).float()
+    neg = torch.full_like(diff, -math.inf)
+    e_strict = torch.where(strict, diff, neg).exp()
+    e_incl = torch.where(incl, diff, neg).exp()
+    KK = torch.matmul(K, K.transpose(-1, -2)).float()
     A = KK * e_strict * B[..., :, None]
     eye = torch.eye(chunk, dtype=torch.float32, device=q.device)
-    T = torch.linalg.solve_triangular(eye + A, eye.expand_as(A), upper=False, unitriangular=True)
+    T = torch.linalg.solve_triangular(eye + A, eye.expand_as(A), upper=False, unitriangular=True).to(bf)
     eb = b.exp()
-    Wf = torch.matmul(T, K * (B * eb)[..., None])
-    Uf = torch.matmul(T, V * B[..., None])
-    Pf = torch.matmul(Qb, Kb.transpose(-1, -2)).float() * e_incl
-    Qd = Q * eb[..., None]
-    Kt = K * (b[..., -1:] - b).exp()[..., None]
+    Wf = torch.matmul(T, (K * (B * eb)[..., None].to(bf)).to(bf))
+    Uf = torch.matmul(T, (V * B[..., None].to(bf)).to(bf))
+    Pf = (torch.matmul(Q, K.transpose(-1, -2)).float() * e_incl).to(bf)
+    Qd = (Q * eb[..., None].to(bf)).to(bf)
+    Kt = (K * (b[..., -1:] - b).exp()[..., None].to(bf)).to(bf)
     gamma = b[..., -1].exp().contiguous()
-    bf = torch.bfloat16
-    O = _Recurrence.apply(Wf.to(bf).contiguous(), Uf.to(bf).contiguous(), Pf.to(bf).contiguous(),
-                          Qd.to(bf).contiguous(), Kt.to(bf).contiguous(), gamma, start, count)
+    O = _Recurrence.apply(Wf.contiguous(), Uf.contiguous(), Pf.contiguous(), Qd.contiguous(), Kt.contiguous(),
+                          gamma, start, count)
     out = O.transpose(1, 2).reshape(Nc * chunk, H, Dv)
     return out.index_select(0, keep)
 
