@@ -94,7 +94,7 @@ def main():
     parser.add_argument("--length", type=int, default=8192)
     parser.add_argument("--images", type=int, default=2)
     parser.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid as a bench value)")
-    parser.add_argument("--recompute", type=int, default=1, help="recompute backbone layers in backward")
+    parser.add_argument("--recompute", type=int, default=0, help="recompute backbone layers in backward")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_unavailable(args)
@@ -102,6 +102,7 @@ def main():
     if args.warmup < 3:
         raise SystemExit("at least 3 warm-up steps are required")
 
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     import torch
     import torch.distributed as dist
     from cq_pretrain_b200.config import qwen35_2b_wan
@@ -170,7 +171,7 @@ def main():
                        "visual_queries_per_image": 256, "latent": "16x1x64x64",
                        "rows_per_pack": int(host.mainline.rows), "gdn_events": host.mainline.delta.events,
                        "l2": "working set (weights + optimizer state) >> 126 MB L2; no flush",
-                       "layers_override": args.layers},
+                       "layers_override": args.layers, "recompute_backbone": bool(args.recompute)},
             "e2e": {"value": round(e2e, 1), "unit": "content tokens/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 16},
             "gpu_launches": int(launches),

@@ -637,7 +637,9 @@ std::vector<at::Tensor> ln_modulate_bwd(at::Tensor dy, at::Tensor x, at::Tensor 
   auto dshift = at::zeros_like(scale);
   if (!rows) return {dx, dscale, dshift};
   auto dyc = dy.to(at::kBFloat16).contiguous();
-  const int warps_total = std::min(rows, sm_count() * 64);
+  // >= 32 contiguous rows per warp: modulation rows repeat for whole samples, so per-warp
+  // register accumulation absorbs most of the reduction before any atomic.
+  const int warps_total = std::max(1, std::min((rows + 31) / 32, sm_count() * 16));
   const int per = (rows + warps_total - 1) / warps_total;
   const int warps_needed = (rows + per - 1) / per;
   const int blocks = (warps_needed + kWarps - 1) / kWarps;
@@ -687,7 +689,7 @@ std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tens
   auto dgate = at::zeros_like(gate);
   auto dbranch = at::empty_like(branch);
   if (!rows) return {dbranch, dgate};
-  const int warps_total = std::min(rows, sm_count() * 64);
+  const int warps_total = std::max(1, std::min((rows + 31) / 32, sm_count() * 16));
   const int per = (rows + warps_total - 1) / warps_total;
   const int warps_needed = (rows + per - 1) / per;
   const int blocks = (warps_needed + kWarps - 1) / kWarps;

@@ -1,0 +1,134 @@
+"""Request-local CQ text decoding with committed-content caches (TP = 1).
+
+Prefill runs the ordinary CQ plan of one document whose last content position is the
+placeholder of the first unknown token; that placeholder is *not* committed (its GDN write
+event becomes read-only, and its attention key is dropped). Each ``advance(token)`` then runs
+two rows through every layer: the sampled token as content (appends its KV, updates the fp32
+GDN state and the conv history) and a fresh text-mask query that reads the committed prefix
+(reference ``models/decoding.py:16-171``). No dense mask is ever built.
+"""
+
+from __future__ import annotations
+
+from dataclasses import replace
+
+import torch
+import torch.nn.functional as F
+
+from ..data.plan import mrope_tables
+from ..ops import reference as R
+
+
+def _delta_step(layer, x, cache):
+    cfg = layer.cfg
+    hk, h, d = cfg.linear_heads, cfg.value_heads, cfg.linear_head_dim
+    size = hk * d
+    raw, z, a, b = layer.project(x)           # rows: [content, query]
+    weight = layer.conv1d.weight[:, 0].to(raw.dtype)
+    history = cache["conv"]                   # [K-1, C] raw committed inputs (oldest first)
+    conv = raw[0] * weight[:, -1]
+    for j in range(history.shape[0]):
+        conv = conv + history[j] * weight[:, j]
+    conv = F.silu(conv.float()).to(raw.dtype) if raw.dtype != torch.float64 else F.silu(conv)
+    if history.shape[0]:
+        history = torch.cat((history[1:], raw[:1]))   # the query's history includes the new token
+        cache["conv"] = history
+    query = raw[1, :size] * weight[:size, -1]
+    for j in range(history.shape[0]):
+        query = query + history[j, :size] * weight[:size, j]
+    query = F.silu(query.float()).to(raw.dtype) if raw.dtype != torch.float64 else F.silu(query)
+    cq, k, v = conv.split((size, size, h * d), -1)
+    q = torch.stack((cq, query)).reshape(2, hk, d)
+    k = k.reshape(1, hk, d)
+    v = v.reshape(1, h, d)
+    if h != hk:
+        q, k = (t.repeat_interleave(h // hk, dim=1) for t in (q, k))
+    ctrl = torch.float64 if x.dtype == torch.float64 else torch.float32
+    g = -layer.A_log.to(ctrl).exp() * F.softplus(a[:1].to(ctrl) + layer.dt_bias.to(ctrl))
+    beta = b[:1].to(ctrl).sigmoid()
+    q = R.l2norm(q).to(ctrl) * d ** -0.5
+    k = R.l2norm(k).to(ctrl)
+    state = cache["state"][0].to(ctrl)        # [H, Dk, Dv]
+    state = state * g.exp()[0][:, None, None]
+    residual = v[0].to(ctrl) - torch.einsum("hkv,hk->hv", state, k[0])
+    state = state + k[0][:, :, None] * (residual * beta[0][:, None])[:, None, :]
+    cache["state"] = state[None]
+    y = torch.einsum("hkv,bhk->bhv", state, q).to(x.dtype)
+    return layer.out_proj(layer.norm(y, z.reshape(2, h, d)).flatten(-2))
+
+
+def _attention_step(layer, x, rope, cache):
+    cfg = layer.cfg
+    q, gate = layer.q_proj(x).reshape(2, cfg.heads, 2 * cfg.head_dim).chunk(2, -1)
+    q = layer.q_norm(q)
+    if cfg.qwen_fused_projections:
+        k, v = layer.kv_proj(x[:1]).reshape(1, cfg.kv_heads, 2 * cfg.head_dim).chunk(2, -1)
+    else:
+        k = layer.k_proj(x[:1]).reshape(1, cfg.kv_heads, cfg.head_dim)
+        v = layer.v_proj(x[:1]).reshape(1, cfg.kv_heads, cfg.head_dim)
+    k = layer.k_norm(k)
+    cos, sin = rope
+    q = R.rotary_half(q, cos, sin, cfg.rotary_dim)
+    k = R.rotary_half(k, cos[:1], sin[:1], cfg.rotary_dim)
+    cache["k"] = torch.cat((cache["k"], k))
+    cache["v"] = torch.cat((cache["v"], v.contiguous()))
+    n = cache["k"].shape[0]
+    # the content row sees the committed prefix including itself; so does the next query
+    y = R.range_attention(q, cache["k"], cache["v"], torch.zeros(2, dtype=torch.int32, device=x.device),
+                          torch.full((2,), n, dtype=torch.int32, device=x.device))
+    return layer.o_proj((y * gate.sigmoid()).flatten(-2))
+
+
+class CQDecoder:
+    """Prefill once, then ``advance(token)`` per sampled token; ``hidden`` is the query readout."""
+
+    @torch.no_grad()
+    def __init__(self, model, batch, max_new_tokens):
+        cfg = model.cfg
+        plan = batch.mainline
+        s = plan.content_length
+        if (cfg.method != "CQ_IT" or plan.queries != 1 or int(plan.query_positions[0]) != s - 1
+                or bool(plan.query_image.any()) or int(batch.segments.min()) < 0
+                or len(torch.unique(batch.segments)) != 1):
+            raise ValueError("CQ decoding needs one document whose only query reads its final placeholder")
+        self.model, self.limit, self.step = model, max_new_tokens, 0
+        device = model.embedding.weight.device
+        delta = plan.delta
+        writes = delta.event_write.clone()
+        last = len(delta.content_order) - 1
+        writes[writes == last] = len(delta.content_order)   # placeholder: read-only
+        local = replace(batch, mainline=replace(plan, delta=replace(delta, event_write=writes)))
+        local = local.to(device)
+        self.caches = [dict() for _ in model.layers]
+        output = model.backbone(local, cache=self.caches)
+        for layer, cache in zip(model.layers, self.caches):
+            if hasattr(layer, "self_attn"):
+                cache["k"], cache["v"] = cache["k"][: s - 1], cache["v"][: s - 1]
+        self.hidden = output.index_select(0, local.mainline.output_positions.to(device))
+        base = plan.query_rope.double()
+        steps = torch.arange(max_new_tokens + 1, dtype=torch.float64)
+        positions = base + steps[None]
+        cos, sin = mrope_tables(positions, cfg)
+        dtype = model.embedding.weight.dtype
+        self.rope = (cos.to(device=device, dtype=dtype), sin.to(device=device, dtype=dtype))
+        self.ids = torch.tensor([0, cfg.text_mask_token_id], device=device)
+
+    @torch.no_grad()
+    def advance(self, token):
+        if self.step >= self.limit:
+            raise ValueError("CQ decode capacity exceeded")
+        model = self.model
+        self.ids[0] = int(token)
+        hidden = model.embedding.partial(self.ids)
+        rope = tuple(t[self.step:self.step + 2] for t in self.rope)
+        for layer, cache in zip(model.layers, self.caches):
+            normed = layer.input_layernorm(hidden)
+            if hasattr(layer, "linear_attn"):
+                mixed = _delta_step(layer.linear_attn, normed, cache)
+            else:
+                mixed = _attention_step(layer.self_attn, normed, rope, cache)
+            hidden = hidden + mixed
+            hidden = hidden + layer.mlp(layer.post_attention_layernorm(hidden))
+        self.step += 1
+        self.hidden = model.final_norm(hidden[1:2])
+        return self.hidden

@@ -26,7 +26,8 @@ def _kernel(q):
 class _RangeAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, kstart, kend, scale):
-        o, lse = _ext.ops().attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), kstart, kend, scale)
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        o, lse = _ext.ops().attn_fwd(q, k, v, kstart, kend, scale)
         ctx.save_for_backward(q, k, v, o, lse, kstart, kend)
         ctx.scale = scale
         return o

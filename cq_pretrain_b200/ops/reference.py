@@ -12,47 +12,52 @@ import torch
 import torch.nn.functional as F
 
 
+def _f(x):
+    """fp32 compute copy (float64 stays float64 so the oracles are exact in double precision)."""
+    return x if x.dtype == torch.float64 else x.float()
+
+
 # ---- normalisation ------------------------------------------------------------------------
 def rms_norm(x, weight, eps, offset=True):
     """Qwen RMSNorm ``x * rsqrt(mean x^2 + eps) * (1 + w)`` computed in fp32 (reference ``backbone_qwen35.py:13-28``)."""
-    w = (1 + weight.float()) if offset else weight.float()
-    xf = x.float()
+    w = (1 + _f(weight)) if offset else _f(weight)
+    xf = _f(x)
     return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps) * w).to(x.dtype)
 
 
 def gated_rms_norm(x, z, weight, eps):
     """GDN output norm ``rms(x) * w * silu(z)`` per head (reference ``backbone_qwen35.py:101-114``)."""
-    xf = x.float()
+    xf = _f(x)
     normed = (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)).to(x.dtype)
-    return (normed * weight.to(x.dtype) * F.silu(z.float()).to(x.dtype)).to(x.dtype)
+    return (normed * weight.to(x.dtype) * F.silu(_f(z)).to(x.dtype)).to(x.dtype)
 
 
 def layer_norm_modulate(x, scale, shift, eps):
     """Wan adaLN: ``LayerNorm(x) (fp32, no affine) * (1 + scale) + shift`` (reference ``ops/torchair.py:8-12``)."""
-    normed = F.layer_norm(x.float(), (x.shape[-1],), eps=eps)
-    return normed * (1 + scale.float()) + shift.float()
+    normed = F.layer_norm(_f(x), (x.shape[-1],), eps=eps)
+    return normed * (1 + _f(scale)) + _f(shift)
 
 
 def gated_add(x, branch, gate):
     """FP32 gated residual ``x + gate * branch``."""
-    return x.float() + gate.float() * branch.float()
+    return _f(x) + _f(gate) * _f(branch)
 
 
 # ---- activations ---------------------------------------------------------------------------
 def swiglu(x):
     gate, up = x.chunk(2, -1)
-    return (F.silu(gate.float()) * up.float()).to(x.dtype)
+    return (F.silu(_f(gate)) * _f(up)).to(x.dtype)
 
 
 def gelu_tanh(x):
-    return F.gelu(x.float(), approximate="tanh").to(x.dtype)
+    return F.gelu(_f(x), approximate="tanh").to(x.dtype)
 
 
 # ---- rotary -------------------------------------------------------------------------------
 def rotary_half(x, cos, sin, dim):
     """Rotate-half RoPE on the first ``dim`` channels of each head; x ``[rows, heads, hd]``, cos ``[rows, dim]``."""
-    rot, rest = x[..., :dim].float(), x[..., dim:]
-    c, s = cos[:, None, :].float(), sin[:, None, :].float()
+    rot, rest = _f(x[..., :dim]), x[..., dim:]
+    c, s = cos[:, None, :].to(rot.dtype), sin[:, None, :].to(rot.dtype)
     a, b = rot.chunk(2, -1)
     out = rot * c + torch.cat((-b, a), -1) * s
     return torch.cat((out.to(x.dtype), rest), -1)
@@ -60,8 +65,8 @@ def rotary_half(x, cos, sin, dim):
 
 def rotary_pairs(x, cos, sin):
     """Wan complex-pair RoPE: pairs (x[2i], x[2i+1]) rotated by angle i; cos ``[rows, hd/2]``."""
-    real, imag = x.float().unflatten(-1, (-1, 2)).unbind(-1)
-    c, s = cos[:, None, :].float(), sin[:, None, :].float()
+    real, imag = _f(x).unflatten(-1, (-1, 2)).unbind(-1)
+    c, s = cos[:, None, :].to(real.dtype), sin[:, None, :].to(real.dtype)
     return torch.stack((real * c - imag * s, imag * c + real * s), -1).flatten(-2).to(x.dtype)
 
 
@@ -113,10 +118,6 @@ def varlen_attention(q, k, v, q_ends, k_ends, scale=None):
 
 
 # ---- gated delta rule ---------------------------------------------------------------------
-def _f(x):
-    return x if x.dtype == torch.float64 else x.float()
-
-
 def l2norm(x, eps=1e-6):
     xf = _f(x)
     return xf * torch.rsqrt(xf.square().sum(-1, keepdim=True) + eps)
@@ -231,18 +232,18 @@ def causal_conv_silu(x, weight, bounds):
     pos = torch.empty(n, dtype=torch.long, device=x.device)
     for a, b in zip(bounds, bounds[1:]):
         pos[a:b] = torch.arange(b - a, device=x.device)
-    xf = x.float()
-    y = xf * weight[:, K - 1].float()
+    xf = _f(x)
+    y = xf * _f(weight[:, K - 1])
     for i in range(K - 1):
         shift = K - 1 - i
         shifted = torch.zeros_like(xf)
         shifted[shift:] = xf[:-shift] if shift < n else shifted[shift:]
         shifted = shifted * (pos >= shift)[:, None]
-        y = y + shifted * weight[:, i].float()
+        y = y + shifted * _f(weight[:, i])
     return F.silu(y).to(x.dtype)
 
 
 # ---- loss ---------------------------------------------------------------------------------
 def cross_entropy_rows(hidden, weight, targets):
-    logits = hidden.float() @ weight.float().T
+    logits = _f(hidden) @ _f(weight).T
     return F.cross_entropy(logits, targets, reduction="none")

@@ -1,0 +1,68 @@
+"""Cached CQ decoding equals full-prefix recomputation (float64); flow sampler and suite plumbing."""
+
+import numpy as np
+import torch
+
+from cq_pretrain_b200.config import tiny_config
+from cq_pretrain_b200.data.packing import Packer
+from cq_pretrain_b200.data.synthetic import ListDocuments
+from cq_pretrain_b200.eval import sampling
+from cq_pretrain_b200.models.decoding import CQDecoder
+from cq_pretrain_b200.models.joint import JointModel
+
+
+def _one_doc(cfg, ids, length):
+    """One templated document whose last body token is the decode placeholder and the only query."""
+    doc = dict(id="d", elements=[dict(type="text", input_ids=np.asarray(ids), supervised=False)], templated=False)
+    packer = Packer(ListDocuments([doc]), cfg, length)
+    batch, _ = packer.next()
+    s = len(ids)
+    batch.ids, batch.segments = batch.ids[:, :s], batch.segments[:, :s]
+    batch.sigma, batch.positions = batch.sigma[:, :s], batch.positions[:, :s]
+    batch.image_queries = batch.image_queries[:, :s]
+    batch.text_indices = torch.tensor([s - 1])
+    from cq_pretrain_b200.data.plan import build_plan
+    batch.mainline = build_plan(batch, cfg)
+    return batch
+
+
+def test_cached_decode_matches_full_prefix():
+    torch.manual_seed(0)
+    cfg = tiny_config(layers=4, vocab_size=128, width=64, ffn=128, heads=4, kv_heads=2, head_dim=16,
+                      mrope_section=(1, 1, 0), linear_heads=2, linear_head_dim=16, dit_width=32, dit_heads=2,
+                      dit_ffn=64, dit_layers=1, text_mask_token_id=4, image_mask_token_id=5)
+    model = JointModel(cfg).double().eval()
+    prefix = [10, 11, 12, 13, 14, 15, 3]     # last id is the placeholder of the next token
+    decoder = CQDecoder(model, _one_doc(cfg, prefix, 32), max_new_tokens=3)
+    full = model.backbone(_one_doc(cfg, prefix, 32))[len(prefix) - 1]
+    torch.testing.assert_close(decoder.hidden[0], full, atol=1e-10, rtol=1e-9)
+    seq = list(prefix[:-1])
+    for token in (21, 22):
+        hidden = decoder.advance(token)[0]
+        seq.append(token)
+        batch = _one_doc(cfg, seq + [3], 32)
+        ref = model.backbone(batch)[len(seq)]
+        torch.testing.assert_close(hidden, ref, atol=1e-9, rtol=1e-8)
+
+
+def test_flow_sigmas_and_greedy():
+    s = sampling.flow_sigmas(4, 5.0)
+    assert s[0] == 1 and s[-1] == 0 and torch.all(s[1:] < s[:-1])
+    cfg = tiny_config(layers=4, vocab_size=64, width=32, ffn=64, heads=2, kv_heads=1, head_dim=16,
+                      mrope_section=(1, 1, 0), linear_heads=2, linear_head_dim=16, dit_width=32, dit_heads=2,
+                      dit_ffn=64, dit_layers=1, text_mask_token_id=4, image_mask_token_id=5)
+    model = JointModel(cfg)
+    h = torch.randn(1, 32)
+    token = sampling.greedy_token(model, h)
+    assert token == int((h @ model.embedding.weight.T).argmax())
+
+
+def test_generate_runs_on_cpu():
+    torch.manual_seed(1)
+    cfg = tiny_config(layers=4, dit_layers=1)
+    from cq_pretrain_b200.data.synthetic import synthetic_batch
+    batch, _ = synthetic_batch(cfg, 256, seed=0)
+    model = JointModel(cfg).eval()
+    out = sampling.generate(model, batch, steps=2, shift=5.0)
+    assert out["latent"].shape == (sum(batch.generation.lengths), 64)
+    assert torch.isfinite(out["latent"]).all()
