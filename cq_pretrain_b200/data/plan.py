@@ -52,6 +52,12 @@ class DeltaPlan(Movable):
     content_bounds: tuple = ()      # host copy of content_cu
     event_bounds: tuple = ()        # host copy of event_cu
     rows: int = 0
+    # Inverse gather maps (see ops/gather.py): backward of each gather is a gather too.
+    content_order_inv: tuple = ()
+    query_source_inv: tuple = ()
+    event_q_inv: tuple = ()
+    event_write_inv: tuple = ()
+    hidden_event_inv: tuple = ()
 
     @property
     def events(self) -> int:
@@ -326,13 +332,20 @@ def build_delta_plan(segments, sigma, query_positions, query_unconditional, s, r
     nc = len(order)
     eq = np.array([i if kind == "c" else nc + i for kind, i in event_q], dtype=np.int64)
     ew = np.array([nc if w == READ else w for w in event_write], dtype=np.int64)
-    hidden_event = np.zeros(rows, dtype=np.int64)
+    n_events = len(event_q)
+    hidden_event = np.full(rows, n_events, dtype=np.int64)   # rows without output read a zero row
     has = np.zeros(rows, dtype=bool)
     if out_hidden:
         hidden_event[np.array(out_hidden)] = np.array(out_event)
         has[np.array(out_hidden)] = True
     qh = np.array([[nc if x == READ else x for x in row] for row in q_history], dtype=np.int64).reshape(-1, hist_len)
-    return DeltaPlan(
+    from ..ops.gather import inverse_levels
+    order_np = np.array(order, dtype=np.int64)
+    qsrc_np = np.array(q_source, dtype=np.int64)
+    inverses = dict(content_order_inv=inverse_levels(order_np, rows), query_source_inv=inverse_levels(qsrc_np, rows),
+                    event_q_inv=inverse_levels(eq, nc + len(q_source)), event_write_inv=inverse_levels(ew, nc + 1, ignore=nc),
+                    hidden_event_inv=inverse_levels(hidden_event, n_events + 1, ignore=n_events))
+    return DeltaPlan(**inverses,
         content_order=torch.from_numpy(np.array(order, dtype=np.int64)),
         content_cu=torch.tensor(content_cu, dtype=torch.int32),
         event_q=torch.from_numpy(eq), event_write=torch.from_numpy(ew),

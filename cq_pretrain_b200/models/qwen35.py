@@ -18,6 +18,7 @@ from torch import nn
 
 from ..ops import activation as A
 from ..ops import attention as ATT
+from ..ops import gather as GA
 from ..ops import gdn as GDN
 from ..ops import norms as N
 from ..ops import reference as R
@@ -127,14 +128,14 @@ class GatedDelta(nn.Module):
         size = hk * d
         raw, z, a, b = self.project(x)                      # full rows, local heads
         dp = plan.delta
-        updates = raw.index_select(0, dp.content_order)    # content in write order
+        updates = GA.rows(raw, dp.content_order, dp.content_order_inv)    # content in write order
         conv = self.conv1d(updates, dp.content_bounds)
         q, k, v = conv.split((size, size, h * d), -1)
         # Query conv reads the previous k-1 real content inputs of its document; queries never
         # enter any other token's history.
         weight = self.conv1d.weight[:size, 0]
         history = torch.cat((updates[:, :size], updates.new_zeros(1, size)), 0)
-        qraw = raw[:, :size].index_select(0, dp.query_source)
+        qraw = GA.rows(raw[:, :size], dp.query_source, dp.query_source_inv)
         query = qraw * weight[:, -1].to(qraw.dtype)
         for j in range(cfg.linear_conv_kernel - 1):
             query = query + history.index_select(0, dp.query_history[:, j]) * weight[:, j].to(qraw.dtype)
@@ -143,17 +144,17 @@ class GatedDelta(nn.Module):
         v = v.reshape(-1, h, d)
         if h != hk:
             q, k, query = (t.repeat_interleave(h // hk, dim=1) for t in (q, k, query))
-        q = torch.cat((q, query), 0).index_select(0, dp.event_q)
+        q = GA.rows(torch.cat((q, query), 0), dp.event_q, dp.event_q_inv)
         zeros = k.new_zeros(1, h, d)
-        k = torch.cat((k, zeros), 0).index_select(0, dp.event_write)
-        v = torch.cat((v, zeros), 0).index_select(0, dp.event_write)
+        k = GA.rows(torch.cat((k, zeros), 0), dp.event_write, dp.event_write_inv)
+        v = GA.rows(torch.cat((v, zeros), 0), dp.event_write, dp.event_write_inv)
         ctrl = torch.float64 if x.dtype == torch.float64 else torch.float32
-        a = a.index_select(0, dp.content_order).to(ctrl)
+        a = GA.rows(a, dp.content_order, dp.content_order_inv).to(ctrl)
         g = -self.A_log.to(ctrl).exp() * F.softplus(a + self.dt_bias.to(ctrl))
-        beta = b.index_select(0, dp.content_order).to(ctrl).sigmoid()
+        beta = GA.rows(b, dp.content_order, dp.content_order_inv).to(ctrl).sigmoid()
         zero = g.new_zeros(1, h)
-        g = torch.cat((g, zero)).index_select(0, dp.event_write)
-        beta = torch.cat((beta, zero)).index_select(0, dp.event_write)
+        g = GA.rows(torch.cat((g, zero)), dp.event_write, dp.event_write_inv)
+        beta = GA.rows(torch.cat((beta, zero)), dp.event_write, dp.event_write_inv)
         if cache is not None:
             if torch.is_grad_enabled():
                 raise ValueError("CQ state caching is inference-only")
@@ -168,9 +169,8 @@ class GatedDelta(nn.Module):
             y = y.to(v.dtype)
         else:
             y = GDN.gated_delta(q, k, v, g, beta, dp.event_bounds)
-        selected = y.index_select(0, dp.hidden_event).to(x.dtype)
-        if dp.padding_hidden.numel():
-            selected = selected.index_fill(0, dp.padding_hidden, 0)
+        y = torch.cat((y, y.new_zeros(1, *y.shape[1:])))   # rows without a GDN output read zeros
+        selected = GA.rows(y, dp.hidden_event, dp.hidden_event_inv).to(x.dtype)
         out = self.norm(selected, z.reshape(-1, h, d)).flatten(-2)
         return self.out_proj(out)
 

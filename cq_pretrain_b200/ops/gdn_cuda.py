@@ -78,49 +78,165 @@ class _Recurrence(torch.autograd.Function):
         return dW, dDelta, dP, dQd, dKt, dgamma, None, None
 
 
+def _factors(Q, K, V, G, B, chunk):
+    """WY factors of every chunk (no autograd). Q, K, V bf16 ``[Nc,H,C,D]``; G, B fp32 ``[Nc,H,C]``."""
+    bf = torch.bfloat16
+    b = G.cumsum(-1)
+    diff = b[..., :, None] - b[..., None, :]
+    tri = torch.ones(chunk, chunk, dtype=torch.bool, device=Q.device)
+    neg = torch.full((), -math.inf, device=Q.device)
+    e_strict = torch.where(tri.tril(-1), diff, neg).exp_()
+    e_incl = torch.where(tri.tril(), diff, neg).exp_()
+    del diff
+    KK = torch.matmul(K, K.transpose(-1, -2)).float()
+    A = KK * e_strict
+    A.mul_(B[..., :, None])
+    eye = torch.eye(chunk, dtype=torch.float32, device=Q.device)
+    T = torch.linalg.solve_triangular(eye + A, eye.expand_as(A), upper=False, unitriangular=True)
+    Tb = T.to(bf)
+    eb = b.exp()
+    Kw = (K * (B * eb)[..., None].to(bf))
+    Vb = (V * B[..., None].to(bf))
+    W = torch.matmul(Tb, Kw)
+    U = torch.matmul(Tb, Vb)
+    QK = torch.matmul(Q, K.transpose(-1, -2)).float()
+    P = (QK * e_incl).to(bf)
+    Qd = Q * eb[..., None].to(bf)
+    kdec = (b[..., -1:] - b).exp()
+    Kt = K * kdec[..., None].to(bf)
+    gamma = b[..., -1].exp().contiguous()
+    return dict(b=b, eb=eb, kdec=kdec, e_strict=e_strict, e_incl=e_incl, KK=KK, A=A, T=T, Tb=Tb, Kw=Kw, Vb=Vb,
+                W=W.contiguous(), U=U.contiguous(), P=P.contiguous(), QK=QK, Qd=Qd.contiguous(), Kt=Kt.contiguous(),
+                gamma=gamma)
+
+
+def _l2_fwd(x, scale=1.0):
+    xf = x.float()
+    r = torch.rsqrt(xf.square().sum(-1, keepdim=True) + 1e-6)
+    return (xf * r * scale).to(torch.bfloat16), r
+
+
+def _l2_bwd(x, r, dy, scale=1.0):
+    """y = scale * x r,  r = (sum x^2 + eps)^-1/2  ->  dx = scale (r dy - r^3 x (x . dy))."""
+    xf, dyf = x.float(), dy.float()
+    dot = (xf * dyf).sum(-1, keepdim=True)
+    return scale * (r * dyf - r.pow(3) * xf * dot)
+
+
+class _GatedDelta(torch.autograd.Function):
+    """q, k, v ``[E,H,D]`` (bf16), g, beta ``[E,H]`` fp32 -> o ``[E,H,Dv]``; analytic chunked backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, layout, chunk):
+        idx, pad, keep, start, count, Nc = layout
+        E, H, Dk = q.shape
+        Dv = v.shape[-1]
+        qn, rq = _l2_fwd(q, Dk ** -0.5)
+        kn, rk = _l2_fwd(k)
+        Q, K, V, G, B = _to_chunks((qn, kn, v.to(torch.bfloat16), g.float(), beta.float()), idx, pad, Nc, chunk, H)
+        f = _factors(Q, K, V, G, B, chunk)
+        O, S = _ext.ops().gdn_fwd(f["W"], f["U"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
+        ctx.save_for_backward(q, k, v, g, beta, rq, rk, S)
+        ctx.layout, ctx.chunk = layout, chunk
+        return O.transpose(1, 2).reshape(Nc * chunk, H, Dv).index_select(0, keep)
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, g, beta, rq, rk, S = ctx.saved_tensors
+        idx, pad, keep, start, count, Nc = ctx.layout
+        chunk = ctx.chunk
+        bf = torch.bfloat16
+        E, H, Dk = q.shape
+        Dv = v.shape[-1]
+        qn = (q.float() * rq * Dk ** -0.5).to(bf)
+        kn = (k.float() * rk).to(bf)
+        Q, K, V, G, B, dO = _to_chunks((qn, kn, v.to(bf), g.float(), beta.float(), dout.to(bf)), idx, pad, Nc, chunk, H)
+        f = _factors(Q, K, V, G, B, chunk)
+        dO = dO.contiguous()
+        dS = _ext.ops().gdn_bwd(dO, f["W"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
+        Sb, dSb = S.to(bf), dS.to(bf)
+        Delta = (f["U"].float() - torch.matmul(f["W"], Sb).float()).to(bf)
+        dDelta = (torch.matmul(f["P"].transpose(-1, -2), dO).float() + torch.matmul(f["Kt"], dSb).float()).to(bf)
+        dW = -torch.matmul(dDelta, Sb.transpose(-1, -2)).float()
+        dQd = torch.matmul(dO, Sb.transpose(-1, -2)).float()
+        dP = torch.matmul(dO, Delta.transpose(-1, -2)).float()
+        dKt = torch.matmul(Delta, dSb.transpose(-1, -2)).float()
+        dgamma = (S * dS).sum((-1, -2))
+        dU = dDelta.float()
+        del Delta, dDelta, Sb, dSb, dS
+        b, eb, kdec = f["b"], f["eb"], f["kdec"]
+        Qf, Kf = Q.float(), K.float()
+        # Qd = e^b Q
+        dQ = dQd * eb[..., None]
+        db = (dQd * f["Qd"].float()).sum(-1)
+        # P = (Q K^T) * E_incl
+        dPm = dP * f["e_incl"]
+        dQ += torch.matmul(dPm.to(bf), K).float()
+        dK = torch.matmul(dPm.transpose(-1, -2).to(bf), Q).float()
+        Pfull = f["QK"] * f["e_incl"]
+        t = dP * Pfull
+        db += t.sum(-1) - t.sum(-2)
+        # Kt = e^{b_C - b} K
+        dK += dKt * kdec[..., None]
+        rkt = (dKt * f["Kt"].float()).sum(-1)
+        db -= rkt
+        dbC = rkt.sum(-1) + dgamma * f["gamma"]
+        # U = T Vb, W = T Kw
+        Tb = f["Tb"]
+        dT = torch.matmul(dU.to(bf), f["Vb"].transpose(-1, -2)).float() + torch.matmul(dW.to(bf), f["Kw"].transpose(-1, -2)).float()
+        dVb = torch.matmul(Tb.transpose(-1, -2), dU.to(bf)).float()
+        dKw = torch.matmul(Tb.transpose(-1, -2), dW.to(bf)).float()
+        dV = dVb * B[..., None]
+        dbeta = (dVb * V.float()).sum(-1)
+        sw = (dKw * Kf).sum(-1)
+        dbeta += sw * eb
+        db += sw * eb * B
+        dK += dKw * (B * eb)[..., None]
+        # T = (I + A)^-1  ->  dA = -T^T dT T^T (strict lower part)
+        T = f["T"]
+        dA = -torch.matmul(torch.matmul(T.transpose(-1, -2), dT), T.transpose(-1, -2))
+        dA = dA * torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(-1)
+        A = f["A"]
+        tA = dA * A
+        dbeta += (dA * f["KK"] * f["e_strict"]).sum(-1)
+        db += tA.sum(-1) - tA.sum(-2)
+        dKK = dA * f["e_strict"] * B[..., :, None]
+        dK += torch.matmul((dKK + dKK.transpose(-1, -2)).to(bf), K).float()
+        # b = cumsum(g) within the chunk: dg_i = sum_{j >= i} db_j ; b_C also feeds gamma/Kt
+        db[..., -1] += dbC
+        dG = db.flip(-1).cumsum(-1).flip(-1)
+
+        def back(t, width=None):
+            x = t.transpose(1, 2).reshape(Nc * chunk, H, *t.shape[3:]) if t.dim() == 4 else t.transpose(1, 2).reshape(Nc * chunk, H)
+            return x.index_select(0, keep)
+
+        dqn, dkn = back(dQ), back(dK)
+        dq = _l2_bwd(q, rq, dqn, Dk ** -0.5).to(q.dtype)
+        dk = _l2_bwd(k, rk, dkn).to(k.dtype)
+        dv = back(dV).to(v.dtype)
+        return dq, dk, dv, back(dG).to(g.dtype), back(dbeta).to(beta.dtype), None, None
+
+
+def _to_chunks(tensors, idx, pad, Nc, chunk, H):
+    out = []
+    for t in tensors:
+        x = t.index_select(0, idx)
+        x = x.masked_fill(pad.view(-1, *([1] * (x.dim() - 1))), 0)
+        if x.dim() == 3:
+            out.append(x.view(Nc, chunk, H, x.shape[-1]).transpose(1, 2).contiguous())
+        else:
+            out.append(x.view(Nc, chunk, H).transpose(1, 2).contiguous())
+    return out
+
+
 def gated_delta_cuda(q, k, v, g, beta, bounds, chunk=CHUNK):
     """Event-ordered inputs -> event-ordered outputs ``[E, H, Dv]`` (bf16)."""
     E, H, Dk = q.shape
     Dv = v.shape[-1]
     if Dk != 128 or Dv % 64 or chunk != CHUNK:
         return R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk).to(v.dtype)
-    idx, pad, keep, start, count, Nc = _layout(tuple(int(x) for x in bounds), chunk, q.device)
-    bf = torch.bfloat16
-    qn = (R.l2norm(q) * Dk ** -0.5).to(bf)
-    kn = R.l2norm(k).to(bf)
-    padc = pad.view(-1, 1, 1)
-
-    def gather(t):
-        x = t.index_select(0, idx)
-        return x.masked_fill(padc if x.dim() == 3 else pad.view(-1, 1), 0)
-
-    Q = gather(qn).view(Nc, chunk, H, Dk).transpose(1, 2)
-    K = gather(kn).view(Nc, chunk, H, Dk).transpose(1, 2)
-    V = gather(v.to(bf)).view(Nc, chunk, H, Dv).transpose(1, 2)
-    G = gather(g.float()).view(Nc, chunk, H).transpose(1, 2)
-    B = gather(beta.float()).view(Nc, chunk, H).transpose(1, 2)
-    b = G.cumsum(-1)
-    diff = b[..., :, None] - b[..., None, :]
-    tri = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device)
-    strict, incl = tri.tril(-1), tri.tril()
-    neg = torch.full_like(diff, -math.inf)
-    e_strict = torch.where(strict, diff, neg).exp()
-    e_incl = torch.where(incl, diff, neg).exp()
-    KK = torch.matmul(K, K.transpose(-1, -2)).float()
-    A = KK * e_strict * B[..., :, None]
-    eye = torch.eye(chunk, dtype=torch.float32, device=q.device)
-    T = torch.linalg.solve_triangular(eye + A, eye.expand_as(A), upper=False, unitriangular=True).to(bf)
-    eb = b.exp()
-    Wf = torch.matmul(T, (K * (B * eb)[..., None].to(bf)).to(bf))
-    Uf = torch.matmul(T, (V * B[..., None].to(bf)).to(bf))
-    Pf = (torch.matmul(Q, K.transpose(-1, -2)).float() * e_incl).to(bf)
-    Qd = (Q * eb[..., None].to(bf)).to(bf)
-    Kt = (K * (b[..., -1:] - b).exp()[..., None].to(bf)).to(bf)
-    gamma = b[..., -1].exp().contiguous()
-    O = _Recurrence.apply(Wf.contiguous(), Uf.contiguous(), Pf.contiguous(), Qd.contiguous(), Kt.contiguous(),
-                          gamma, start, count)
-    out = O.transpose(1, 2).reshape(Nc * chunk, H, Dv)
-    return out.index_select(0, keep)
+    layout = _layout(tuple(int(x) for x in bounds), chunk, q.device)
+    return _GatedDelta.apply(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g, beta, layout, chunk)
 
 
 def causal_conv_cuda(x, weight, bounds):
