@@ -1,0 +1,104 @@
+"""TP collective-fused ops vs NCCL + cuBLAS at 2/4/8 GPUs (bf16).
+
+``torchrun --nproc-per-node N -m cq_pretrain_b200.benchmarks.tp_fused`` times, with CUDA events
+and the max over ranks (median of 20 after 5 warm-ups):
+
+* column-parallel all-gather -> GEMM: ``[8192/tp, 2048] x [2048, 6144/tp]`` (each rank holds
+  ``8192/tp`` rows; the output is ``[8192, 6144/tp]``);
+* row-parallel GEMM -> reduce-scatter: ``[8192, 6144/tp] x [6144/tp, 2048]`` -> ``[8192/tp, 2048]``;
+
+and reports each fused path against its roofline: the slower of FLOPs / measured bf16 peak and
+bytes that must cross NVLink per GPU / 770 GB/s (measured peer-copy bandwidth).
+Also checks the fused results against the NCCL path.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import statistics
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+PEER_GBS = 770.0
+
+
+def bf16_peak_tflops():
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0
+
+
+def timed(fn, iters=20, warmup=5):
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(iters):
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    t = torch.tensor([statistics.median(times)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def main():
+    from ..parallel import fused
+    from ..parallel import state as ps
+    from ..parallel import symmetric
+    from ..ops import gemm
+
+    world = int(os.environ["WORLD_SIZE"])
+    st = ps.initialize(world, timeout_s=300.0)
+    tp = st.tp
+    ws = symmetric.enable()
+    torch.manual_seed(1 + st.rank)
+    peak = bf16_peak_tflops()
+    M, H, F = 8192, 2048, 6144
+    rows = M // tp
+    # all-gather -> GEMM
+    x = torch.randn(rows, H, device="cuda", dtype=torch.bfloat16)
+    w1 = (torch.randn(F // tp, H, device="cuda") * 0.02).to(torch.bfloat16)
+    y_f, xg = ws.gather_linear(x, w1)
+    y_n = gemm.linear(fused.gather_rows_raw(x), w1)
+    err1 = ((y_f.float() - y_n.float()).abs().max() / y_n.float().abs().max()).item()
+    t_fused = timed(lambda: ws.gather_linear(x, w1))
+    t_nccl = timed(lambda: gemm.linear(fused.gather_rows_raw(x), w1))
+    flops = 2.0 * M * H * (F // tp)
+    nv_bytes = (tp - 1) * rows * H * 2
+    roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
+    out = [dict(op="allgather_gemm", tp=tp, shape=[rows, H, F // tp], fused_ms=t_fused, nccl_cublas_ms=t_nccl,
+                roofline_ms=roof, roofline_fraction=roof / t_fused, speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err1)]
+    # GEMM -> reduce-scatter
+    xf = torch.randn(M, F // tp, device="cuda", dtype=torch.bfloat16)
+    w2 = (torch.randn(H, F // tp, device="cuda") * 0.02).to(torch.bfloat16)
+    z_f = ws.linear_scatter(xf, w2)
+    z_n = fused.scatter_rows_raw(gemm.linear(xf, w2))
+    err2 = ((z_f.float() - z_n.float()).abs().max() / z_n.float().abs().max()).item()
+    t_fused = timed(lambda: ws.linear_scatter(xf, w2))
+    t_nccl = timed(lambda: fused.scatter_rows_raw(gemm.linear(xf, w2)))
+    flops = 2.0 * M * H * (F // tp)
+    nv_bytes = (tp - 1) * rows * H * 2
+    roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
+    out.append(dict(op="gemm_reducescatter", tp=tp, shape=[M, F // tp, H], fused_ms=t_fused, nccl_cublas_ms=t_nccl,
+                    roofline_ms=roof, roofline_fraction=roof / t_fused, speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err2))
+    status = symmetric.status()
+    if st.rank == 0:
+        for row in out:
+            row["status"] = status
+            print(json.dumps(row), flush=True)
+    symmetric.disable()
+    ps.destroy()
+
+
+if __name__ == "__main__":
+    main()

@@ -28,6 +28,20 @@ at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
 at::Tensor gemm_nn(at::Tensor a, at::Tensor b);
 void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out);
 int gemm_status(bool reset);
+void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_out_ptrs, int64_t rows_per_rank,
+                  int64_t src_rank, int64_t tp);
+at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
+                       int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
+                       int64_t tp);
+// comm.cu
+std::vector<at::Tensor> symm_alloc(int64_t bytes);
+int64_t symm_open(at::Tensor handle_bytes);
+void symm_close(int64_t ptr);
+void symm_free(int64_t ptr);
+at::Tensor symm_view(int64_t base, int64_t offset, std::vector<int64_t> shape, at::ScalarType dtype);
+void signal_wait(at::Tensor peer_flag_ptrs, int64_t my_flags, int64_t rank, int64_t tp, int64_t epoch, bool wait);
+at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp, int64_t rows, int64_t cols);
+int comm_status_read(bool reset);
 // gdn.cu
 std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                                 at::Tensor start, at::Tensor count);
@@ -57,6 +71,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_nn", &cqb::gemm_nn);
   m.def("gemm_tn_acc", &cqb::gemm_tn_acc);
   m.def("gemm_status", &cqb::gemm_status, py::arg("reset") = false);
+  m.def("gemm_scatter", &cqb::gemm_scatter);
+  m.def("gather_gemm", &cqb::gather_gemm);
+  m.def("symm_alloc", &cqb::symm_alloc);
+  m.def("symm_open", &cqb::symm_open);
+  m.def("symm_close", &cqb::symm_close);
+  m.def("symm_free", &cqb::symm_free);
+  m.def("symm_view", &cqb::symm_view);
+  m.def("signal_wait", &cqb::signal_wait);
+  m.def("rs_reduce", &cqb::rs_reduce);
+  m.def("comm_status_read", &cqb::comm_status_read, py::arg("reset") = false);
   m.def("gdn_fwd", &cqb::gdn_fwd);
   m.def("gdn_bwd", &cqb::gdn_bwd);
   m.def("attn_fwd", &cqb::attn_fwd);

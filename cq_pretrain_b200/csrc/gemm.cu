@@ -8,8 +8,14 @@
 //    of tile i+1;
 //  * operands may be K-major (contraction dim contiguous) or MN-major (output dim
 //    contiguous), so y = x W^T, dX = dY W and dW += dY^T X all run without transposes;
-//  * epilogues: bf16 store (+ bias), or fp32 read-add-write into an existing fp32 matrix
-//    (the FP32 main_grad accumulation of weight gradients).
+//  * epilogues: 0 = bf16 TMA store (+ bias); 1 = fp32 TMA reduce-add into an existing fp32
+//    matrix (the main_grad accumulation of weight gradients); 2 = bf16 stores of each tile
+//    straight into the receive buffer of the TP rank that owns its rows, over NVLink peer
+//    memory (the communication half of GEMM -> reduce-scatter, overlapped tile by tile);
+//  * GATHER: two extra warps pull the A row blocks of every TP rank (peer memory, plain loads)
+//    into this GPU's gather buffer and publish a flag per 128-row block; the TMA producer waits
+//    for a block's flag before loading it, and tiles of this rank's own rows go first
+//    (all-gather -> GEMM in one kernel; each remote byte crosses NVLink once).
 //
 // Waits are bounded (tcgen05.cuh); on expiry the kernel records an error code, stops issuing,
 // waits for its outstanding TMA transactions (bounded), frees TMEM and exits.
@@ -17,7 +23,6 @@
 #include "tcgen05.cuh"
 
 #include <mutex>
-#include <unordered_map>
 
 namespace cqb {
 
@@ -28,7 +33,6 @@ constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTE
 constexpr int EPI_BOX = 32;                                   // 32 x 32 output box per warp store
 constexpr int STAGING_BYTES = 4 /*warps*/ * 2 /*buffers*/ * EPI_BOX * EPI_BOX * 4;  // sized for fp32
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int THREADS = 192;
 
 int* status_word() {
   static int* word = [] {
@@ -42,13 +46,63 @@ int* status_word() {
 
 struct GemmArgs {
   int M, N, K;
-  void* out;          // bf16 [M, ldo] or fp32 [M, ldo]
+  void* out;                  // EPI 0/1: bf16 / fp32 [M, ldo]
   int ldo;
   const __nv_bfloat16* bias;  // [N] or null
+  // EPI 2 (scatter to owners): tile rows belong to rank m / rows_per_rank and land at
+  //   peer_out[owner] + ((src_rank * rows_per_rank) + m - owner * rows_per_rank) * N + n
+  void* const* peer_out;
+  int rows_per_rank, src_rank, tp;
+  // GATHER: A rows of rank s live at peer_in[s] + local_row * K; gathered into a_local.
+  const __nv_bfloat16* const* peer_in;
+  __nv_bfloat16* a_local;
+  const long long* ready;     // this rank's flag area: ready[s] >= epoch when rank s published
+  long long* chunk_flags;     // [M / BM] per-block publication flags (local)
+  long long epoch;
 };
 
-template <bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
+__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ long long ld_acquire_gpu(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(long long* p, long long v) {
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded spin until *flag >= target; false (status recorded) on timeout or abort.
+template <bool SYS>
+__device__ __forceinline__ bool wait_flag(const long long* flag, long long target, int* status, volatile int* abort,
+                                          int code) {
+  const unsigned long long start = tc::globaltimer();
+  while ((SYS ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) < target) {
+    if (*abort) return false;
+    if (tc::globaltimer() - start > tc::kWaitNs) {
+      atomicCAS(status, 0, code);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// Tile order: m fastest; with GATHER the m index is rotated so this rank's own rows come first.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int rotate, int& m0, int& n0) {
+  const int mi = (t % tiles_m + rotate) % tiles_m;
+  m0 = mi * BM;
+  n0 = (t / tiles_m) * BN;
+}
+
+template <bool A_MN, bool B_MN, int EPI, bool GATHER>
+__global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_out, GemmArgs args, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -66,6 +120,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tiles_m = (args.M + BM - 1) / BM, tiles_n = (args.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
   const int kblocks = (args.K + BK - 1) / BK;
+  const int rotate = GATHER ? (args.src_rank * args.rows_per_rank) / BM : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -96,7 +151,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int s = 0; s < STAGES; ++s) armed[s] = -1;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int m0 = (t % tiles_m) * BM, n0 = (t / tiles_m) * BN;
+        int m0, n0;
+        tile_coords(t, tiles_m, rotate, m0, n0);
+        if (GATHER) {
+          if (!wait_flag<false>(args.chunk_flags + m0 / BM, args.epoch, status, abort_flag, 5)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, status, abort_flag, 1)) {
             ok = false;
@@ -176,22 +239,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
       }
     }
-  } else {
+  } else if (warp < 6) {
     // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4). Each warp owns 32 rows of the tile:
-    // TMEM -> registers (tcgen05.ld) -> dense 32x32 smem box -> TMA store (bf16) or TMA
-    // reduce-add (fp32 accumulate), double-buffered per warp so the next tcgen05.ld overlaps
-    // the previous bulk copy.
+    // TMEM -> registers (tcgen05.ld) -> dense 32x32 smem box -> TMA store (bf16), TMA reduce-add
+    // (fp32 accumulate) or coalesced stores into the owning rank's receive buffer (peer memory).
     const int quarter = warp & 3;
-    constexpr int ESIZE = EPI == 0 ? 2 : 4;
     uint8_t* my_stage = staging + quarter * 2 * EPI_BOX * EPI_BOX * 4;
     int local = 0, chunk = 0;
-    if (lane == 0) tc::prefetch_map(&map_out);
+    if (lane == 0 && EPI != 2) tc::prefetch_map(&map_out);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t use = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[buf], use, status, abort_flag, 4)) break;
       tc::fence_after();
-      const int m0 = (t % tiles_m) * BM, n0 = (t / tiles_m) * BN;
+      int m0, n0;
+      tile_coords(t, tiles_m, rotate, m0, n0);
       const uint32_t base = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += EPI_BOX, ++chunk) {
@@ -200,9 +262,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int col0 = n0 + c;
         if (col0 >= args.N) continue;  // whole box outside the matrix (uniform across the warp)
         uint8_t* box = my_stage + (chunk & 1) * EPI_BOX * EPI_BOX * 4;
-        if (lane == 0) tc::bulk_wait_read1();  // the store that last used this buffer finished reading
-        __syncwarp();
-        if (EPI == 0) {
+        if (EPI != 2) {
+          if (lane == 0) tc::bulk_wait_read1();  // the store that last used this buffer finished reading
+          __syncwarp();
+        }
+        if (EPI == 0 || EPI == 2) {
           __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(box) + lane * EPI_BOX;
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
@@ -218,23 +282,61 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int j = 0; j < 32; j += 4)
             *reinterpret_cast<float4*>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         }
-        tc::fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          if (EPI == 0)
-            tc::tma_store_2d(&map_out, box, col0, m0 + quarter * 32);
-          else
-            tc::tma_reduce_add_2d(&map_out, box, col0, m0 + quarter * 32);
-          tc::bulk_commit();
+        if (EPI == 2) {
+          __syncwarp();
+          const int owner = m0 / args.rows_per_rank;
+          const int lrow0 = args.src_rank * args.rows_per_rank + (m0 - owner * args.rows_per_rank) + quarter * 32;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.peer_out[owner]) + (size_t)lrow0 * args.N + col0;
+          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(box);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int cidx = lane + 32 * i;        // 128 16-byte pieces: 32 rows x 4
+            const int r = cidx >> 2, part = cidx & 3;
+            if (m0 + quarter * 32 + r < args.M && col0 + part * 8 < args.N)
+              *reinterpret_cast<uint4*>(dst + (size_t)r * args.N + part * 8) =
+                  *reinterpret_cast<const uint4*>(src + r * EPI_BOX + part * 8);
+          }
+          __syncwarp();
+        } else {
+          tc::fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (EPI == 0)
+              tc::tma_store_2d(&map_out, box, col0, m0 + quarter * 32);
+            else
+              tc::tma_reduce_add_2d(&map_out, box, col0, m0 + quarter * 32);
+            tc::bulk_commit();
+          }
         }
-        (void)ESIZE;
       }
       tc::fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[buf]);
     }
-    if (lane == 0) tc::bulk_wait_all();
+    if (EPI != 2 && lane == 0) tc::bulk_wait_all();
     __syncwarp();
+  } else if (GATHER) {
+    // Copy warps 6..7: pull 128-row blocks of A (own rows first) into the local gather buffer.
+    const int ct = threadIdx.x - 192;  // 0..63
+    const int blocks = args.M / BM;
+    const int per_rank = args.rows_per_rank / BM;
+    for (int i = blockIdx.x; i < blocks; i += gridDim.x) {
+      const int blk = (i + rotate) % blocks;
+      const int s = blk / per_rank;
+      const int lrow = blk * BM - s * args.rows_per_rank;
+      bool ok = true;
+      if (ct == 0 && s != args.src_rank) ok = wait_flag<true>(args.ready + s, args.epoch, status, abort_flag, 6);
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (*abort_flag || !ok) break;
+      const uint4* src = reinterpret_cast<const uint4*>(args.peer_in[s] + (size_t)lrow * args.K);
+      uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)blk * BM * args.K);
+      const int vecs = BM * args.K / 8;
+      for (int v = ct; v < vecs; v += 64) dst[v] = src[v];
+      fence_proxy_async_global();
+      __threadfence();
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (ct == 0) st_release_gpu(args.chunk_flags + blk, args.epoch);
+    }
   }
   __syncthreads();
   if (warp == 1) {
@@ -299,16 +401,17 @@ CUtensorMap make_out_map(const at::Tensor& t) {
   return map;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, bool GATHER>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmArgs args) {
-  auto kernel = gemm_kernel<A_MN, B_MN, EPI>;
+  auto kernel = gemm_kernel<A_MN, B_MN, EPI, GATHER>;
   static std::once_flag once;
   std::call_once(once, [&] {
     CQB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   });
   const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  // GATHER needs every CTA resident (copy blocks are handed out by CTA index): one per SM.
   const int grid = std::max(1, std::min(tiles, sm_count()));
-  kernel<<<grid, THREADS, SMEM_BYTES, stream()>>>(ma, mb, mo, args, status_word());
+  kernel<<<grid, GATHER ? 256 : 192, SMEM_BYTES, stream()>>>(ma, mb, mo, args, status_word());
   CQB_LAUNCH_CHECK();
   count_launch();
 }
@@ -318,6 +421,17 @@ void check_dims(int64_t m, int64_t n, int64_t k, bool k_inner = true) {
   TORCH_CHECK(m > 0 && n > 0 && k > 0, "empty GEMM");
   TORCH_CHECK(n % 16 == 0, "GEMM N must be a multiple of 16");
   TORCH_CHECK(!k_inner || k % 16 == 0, "GEMM K must be a multiple of 16");
+}
+
+GemmArgs plain_args(int64_t M, int64_t N, int64_t K, void* out, int64_t ldo, const __nv_bfloat16* bias) {
+  GemmArgs a{};
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.out = out;
+  a.ldo = (int)ldo;
+  a.bias = bias;
+  return a;
 }
 
 }  // namespace
@@ -332,9 +446,8 @@ at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias) {
   auto mb = make_map(w, BN);
   at::Tensor b;
   if (bias && bias->defined()) b = bias->to(at::kBFloat16).contiguous();
-  GemmArgs args{(int)M, (int)N, (int)K, y.data_ptr(), (int)N,
-                b.defined() ? reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()) : nullptr};
-  launch<false, false, 0>(ma, mb, make_out_map(y), args);
+  auto args = plain_args(M, N, K, y.data_ptr(), N, b.defined() ? (const __nv_bfloat16*)b.data_ptr() : nullptr);
+  launch<false, false, 0, false>(ma, mb, make_out_map(y), args);
   return y;
 }
 
@@ -346,8 +459,7 @@ at::Tensor gemm_nn(at::Tensor a, at::Tensor b) {
   auto y = at::empty({M, N}, a.options());
   auto ma = make_map(a, BM);
   auto mb = make_map(b, BK);
-  GemmArgs args{(int)M, (int)N, (int)K, y.data_ptr(), (int)N, nullptr};
-  launch<false, true, 0>(ma, mb, make_out_map(y), args);
+  launch<false, true, 0, false>(ma, mb, make_out_map(y), plain_args(M, N, K, y.data_ptr(), N, nullptr));
   return y;
 }
 
@@ -360,8 +472,54 @@ void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out) {
   check_dims(N, K, M, /*k_inner=*/false);
   auto ma = make_map(a, BK);
   auto mb = make_map(b, BK);
-  GemmArgs args{(int)N, (int)K, (int)M, out.data_ptr(), (int)K, nullptr};
-  launch<true, true, 1>(ma, mb, make_out_map(out.view({N, K})), args);
+  launch<true, true, 1, false>(ma, mb, make_out_map(out.view({N, K})), plain_args(N, K, M, out.data_ptr(), K, nullptr));
+}
+
+// GEMM -> reduce-scatter, communication half: every tile of x[M,K] w^T (w [N,K]) or x w
+// (w [K,N], w_mn_major) is stored into the receive buffer of the rank that owns its rows.
+void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_out_ptrs, int64_t rows_per_rank,
+                  int64_t src_rank, int64_t tp) {
+  const int64_t M = x.size(0), K = x.size(1), N = w_mn_major ? w.size(1) : w.size(0);
+  check_dims(M, N, K);
+  TORCH_CHECK(rows_per_rank % BM == 0 && M == rows_per_rank * tp, "rows per rank must be a multiple of 128");
+  TORCH_CHECK(peer_out_ptrs.is_cuda() && peer_out_ptrs.numel() == tp, "peer pointers: cuda int64 [tp]");
+  auto ma = make_map(x, BM);
+  auto mb = w_mn_major ? make_map(w, BK) : make_map(w, BN);
+  auto args = plain_args(M, N, K, nullptr, N, nullptr);
+  args.peer_out = reinterpret_cast<void* const*>(peer_out_ptrs.data_ptr());
+  args.rows_per_rank = (int)rows_per_rank;
+  args.src_rank = (int)src_rank;
+  args.tp = (int)tp;
+  if (w_mn_major)
+    launch<false, true, 2, false>(ma, mb, ma, args);
+  else
+    launch<false, false, 2, false>(ma, mb, ma, args);
+}
+
+// All-gather -> GEMM: y[M,N] = gather(x)[M,K] w[N,K]^T (+ bias); the gathered rows land in a_local.
+at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
+                       int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
+                       int64_t tp) {
+  const int64_t M = a_local.size(0), K = a_local.size(1), N = w.size(0);
+  check_dims(M, N, K);
+  TORCH_CHECK(rows_per_rank % BM == 0 && M == rows_per_rank * tp, "rows per rank must be a multiple of 128");
+  TORCH_CHECK(chunk_flags.scalar_type() == at::kLong && chunk_flags.numel() >= M / BM, "chunk flags too small");
+  auto y = at::empty({M, N}, a_local.options());
+  auto ma = make_map(a_local, BM);
+  auto mb = make_map(w, BN);
+  at::Tensor b;
+  if (bias && bias->defined()) b = bias->to(at::kBFloat16).contiguous();
+  auto args = plain_args(M, N, K, y.data_ptr(), N, b.defined() ? (const __nv_bfloat16*)b.data_ptr() : nullptr);
+  args.peer_in = reinterpret_cast<const __nv_bfloat16* const*>(peer_in_ptrs.data_ptr());
+  args.a_local = (__nv_bfloat16*)a_local.data_ptr();
+  args.ready = reinterpret_cast<const long long*>(ready_ptr);
+  args.chunk_flags = reinterpret_cast<long long*>(chunk_flags.data_ptr());
+  args.epoch = epoch;
+  args.rows_per_rank = (int)rows_per_rank;
+  args.src_rank = (int)src_rank;
+  args.tp = (int)tp;
+  launch<false, false, 0, true>(ma, mb, make_out_map(y), args);
+  return y;
 }
 
 int gemm_status(bool reset) {

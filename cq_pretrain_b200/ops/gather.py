@@ -21,6 +21,8 @@ def inverse_levels(index, n_src, ignore=None):
     sorted_src = index[order]
     first = np.searchsorted(sorted_src, np.arange(n_src), side="left")
     last = np.searchsorted(sorted_src, np.arange(n_src), side="right")
+    if ignore is not None and 0 <= ignore < n_src:
+        last[ignore] = first[ignore]   # its readers get no gradient, so it sets no level
     depth = int((last - first).max()) if n_src else 0
     for level in range(depth):
         inv = np.full(n_src, n, dtype=np.int64)

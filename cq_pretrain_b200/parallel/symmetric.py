@@ -1,13 +1,161 @@
-"""Symmetric-memory workspace for in-kernel TP collectives over NVLink peer memory.
+"""Symmetric peer-memory workspace for the in-kernel TP collectives (one process per GPU).
 
-Filled in with the fused GEMM/collective kernels; until a workspace is created, the fused
-entry points use NCCL + GEMM.
+Every rank of a TP group allocates one buffer with the same layout, exchanges CUDA IPC
+handles, and opens every peer's buffer (NVLink P2P). Layout::
+
+    [0, 512)        all-gather flags: slot s = last epoch rank s published its shard
+    [512, 1024)     reduce-scatter flags: slot s = last epoch rank s finished storing partials
+    send[0], send[1]   this rank's staged shard for all-gather (double-buffered by epoch parity)
+    recv[0], recv[1]   [tp, rows/tp, N] partial slabs written by peers for reduce-scatter
+
+Protocol (epochs count calls of each kind; every rank issues the same sequence):
+
+* all-gather -> GEMM (epoch e): copy the local shard into ``send[e % 2]``, publish flag e to
+  every peer, then one kernel pulls each peer's shard into local memory block by block (after
+  acquiring that peer's flag) while the tensor cores consume the blocks already present.
+* GEMM -> reduce-scatter (epoch e): one GEMM kernel stores every output tile into the owner's
+  ``recv[e % 2][src]``; a one-block kernel publishes flag e and acquires all peers' flags; a
+  bandwidth kernel sums the tp slabs.
+
+Double buffering plus the flag order makes buffer reuse safe: a rank can only overwrite a slot
+of parity p at epoch e after every peer has signalled epoch e-1, which each peer does only after
+its own epoch e-2 work (the last reader/writer of that slot) completed in stream order.
+All waits are bounded in the kernels and report a status code instead of hanging.
 """
 
 from __future__ import annotations
 
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+from . import state as ps
+
+FLAG_BYTES = 1024
 _WORKSPACE = None
+
+
+def _align(n, a=4096):
+    return -(-n // a) * a
+
+
+class SymmetricWorkspace:
+    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_blocks=4096):
+        st = ps.state()
+        if st.tp < 2:
+            raise ValueError("symmetric workspace needs TP >= 2")
+        ops = _ext.ops()
+        self.tp, self.rank, self.group = st.tp, st.tp_rank, st.tp_group
+        self.send_bytes, self.recv_bytes = _align(send_bytes), _align(recv_bytes)
+        self.off_send = [FLAG_BYTES * 4, FLAG_BYTES * 4 + self.send_bytes]
+        self.off_recv = [self.off_send[1] + self.send_bytes, self.off_send[1] + self.send_bytes + self.recv_bytes]
+        total = self.off_recv[1] + self.recv_bytes
+        ptr, handle = ops.symm_alloc(total)
+        self.base = int(ptr[0])
+        handles = [None] * self.tp
+        dist.all_gather_object(handles, handle.numpy().tobytes(), group=self.group)
+        bases = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bases.append(self.base)
+            else:
+                bases.append(ops.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+        self.bases = bases
+        dev = torch.device("cuda", torch.cuda.current_device())
+        as_dev = lambda xs: torch.tensor(xs, dtype=torch.int64, device=dev)
+        self.flag_ag = as_dev([b for b in bases])                       # slot array base of each peer
+        self.flag_rs = as_dev([b + 512 for b in bases])
+        self.send = [as_dev([b + self.off_send[p] for b in bases]) for p in range(2)]
+        self.recv = [as_dev([b + self.off_recv[p] for b in bases]) for p in range(2)]
+        self.chunk_flags = torch.zeros(max_blocks, dtype=torch.int64, device=dev)
+        self.epoch_ag = 0
+        self.epoch_rs = 0
+        dist.barrier(group=self.group)
+
+    # ---- eligibility --------------------------------------------------------------------------
+    def supports(self, x, w, transposed=False):
+        if not (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2):
+            return False
+        rows = x.shape[0]
+        if transposed:   # dY [M, N_local] @ W [N_local, K] -> reduce-scatter rows
+            n_out = w.shape[1]
+            return (rows % (128 * self.tp) == 0 and n_out % 16 == 0 and x.shape[1] % 16 == 0
+                    and rows * n_out * 2 <= self.recv_bytes)
+        return x.shape[1] % 16 == 0 and w.shape[0] % 16 == 0 and x.data_ptr() % 16 == 0
+
+    def _gather_ok(self, x):
+        rows = x.shape[0] * self.tp
+        return (x.shape[0] % 128 == 0 and x.numel() * 2 <= self.send_bytes and rows // 128 <= self.chunk_flags.numel())
+
+    # ---- fused ops --------------------------------------------------------------------------------
+    def gather_linear(self, x, weight, bias=None):
+        """``(all_gather(x) @ W^T + b, all_gather(x))`` in one all-gather->GEMM kernel."""
+        ops = _ext.ops()
+        if not self._gather_ok(x):
+            from .fused import gather_rows_raw
+            from ..ops import gemm
+            xg = gather_rows_raw(x)
+            return gemm.linear(xg, weight, bias), xg
+        self.epoch_ag += 1
+        e, p = self.epoch_ag, self.epoch_ag % 2
+        rows = x.shape[0]
+        stage = ops.symm_view(self.base, self.off_send[p], [rows, x.shape[1]], torch.bfloat16)
+        stage.copy_(x)
+        ops.signal_wait(self.flag_ag, self.base, self.rank, self.tp, e, False)
+        xg = torch.empty(rows * self.tp, x.shape[1], dtype=x.dtype, device=x.device)
+        y = ops.gather_gemm(xg, weight.contiguous(), bias, self.send[p], self.base, self.chunk_flags, e, rows,
+                            self.rank, self.tp)
+        return y, xg
+
+    def _scatter(self, x, weight, mn_major):
+        ops = _ext.ops()
+        self.epoch_rs += 1
+        e, p = self.epoch_rs, self.epoch_rs % 2
+        rows = x.shape[0] // self.tp
+        n_out = weight.shape[1] if mn_major else weight.shape[0]
+        ops.gemm_scatter(x.contiguous(), weight.contiguous(), mn_major, self.recv[p], rows, self.rank, self.tp)
+        ops.signal_wait(self.flag_rs, self.base + 512, self.rank, self.tp, e, True)
+        recv = ops.symm_view(self.base, self.off_recv[p], [self.tp, rows, n_out], torch.bfloat16)
+        return ops.rs_reduce(recv, None, self.tp, rows, n_out)
+
+    def linear_scatter(self, x, weight):
+        """``reduce_scatter_rows(x @ W^T)`` with the GEMM storing tiles into the owners' buffers."""
+        return self._scatter(x, weight, False)
+
+    def matmul_scatter(self, dy, weight):
+        """``reduce_scatter_rows(dY @ W)`` (column-parallel input gradient)."""
+        return self._scatter(dy, weight, True)
+
+    def close(self):
+        ops = _ext.ops()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for r, b in enumerate(self.bases):
+            if r != self.rank:
+                ops.symm_close(b)
+        dist.barrier(group=self.group)
+        ops.symm_free(self.base)
 
 
 def workspace():
     return _WORKSPACE
+
+
+def enable(**kwargs):
+    """Create the TP workspace (collective over the TP group); fused linears use it from now on."""
+    global _WORKSPACE
+    if _WORKSPACE is None and ps.tp_size() > 1 and _ext.has("gather_gemm"):
+        _WORKSPACE = SymmetricWorkspace(**kwargs)
+    return _WORKSPACE
+
+
+def disable():
+    global _WORKSPACE
+    if _WORKSPACE is not None:
+        _WORKSPACE.close()
+    _WORKSPACE = None
+
+
+def status(reset=True):
+    ops = _ext.ops()
+    return dict(gemm=ops.gemm_status(reset), comm=ops.comm_status_read(reset))

@@ -1,0 +1,66 @@
+"""In-kernel TP collectives (all-gather->GEMM, GEMM->reduce-scatter) vs NCCL on 2+ GPUs."""
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from cq_pretrain_b200.ops import gemm
+    from cq_pretrain_b200.parallel import fused, state as ps, symmetric
+    st = ps.initialize(world, timeout_s=120.0)
+    ws = symmetric.enable(send_bytes=8 << 20, recv_bytes=16 << 20)
+    torch.manual_seed(rank)
+    errors = []
+    for it in range(3):  # several epochs exercise both buffer parities
+        x = torch.randn(256, 512, device="cuda", dtype=torch.bfloat16)
+        w = (torch.randn(384, 512, device="cuda") * 0.05).to(torch.bfloat16)
+        y, xg = ws.gather_linear(x, w)
+        xg_ref = fused.gather_rows_raw(x)
+        errors.append(float((xg.float() - xg_ref.float()).abs().max()))
+        ref = gemm.linear(xg_ref, w)
+        errors.append(float((y.float() - ref.float()).abs().max() / ref.float().abs().max()))
+        xf = torch.randn(256 * world, 256, device="cuda", dtype=torch.bfloat16)
+        w2 = (torch.randn(512, 256, device="cuda") * 0.05).to(torch.bfloat16)
+        z = ws.linear_scatter(xf, w2)
+        zref = fused.scatter_rows_raw(gemm.linear(xf, w2))
+        errors.append(float((z.float() - zref.float()).abs().max() / zref.float().abs().max()))
+        dy = torch.randn(256 * world, 384, device="cuda", dtype=torch.bfloat16)
+        w3 = (torch.randn(384, 512, device="cuda") * 0.05).to(torch.bfloat16)
+        d = ws.matmul_scatter(dy, w3)
+        dref = fused.scatter_rows_raw(gemm.matmul_nn(dy, w3))
+        errors.append(float((d.float() - dref.float()).abs().max() / dref.float().abs().max()))
+    torch.cuda.synchronize()
+    status = symmetric.status()
+    symmetric.disable()
+    ps.destroy()
+    torch.save(dict(errors=errors, status=status), f"{out}.{rank}")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.timeout(300)
+def test_fused_tp_collectives_match_nccl():
+    world = min(torch.cuda.device_count(), 4)
+    with tempfile.TemporaryDirectory() as tmp:
+        out = os.path.join(tmp, "res")
+        mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
+        for r in range(world):
+            res = torch.load(f"{out}.{r}")
+            assert res["status"] == dict(gemm=0, comm=0), res["status"]
+            assert max(res["errors"]) < 2e-2, res["errors"]
