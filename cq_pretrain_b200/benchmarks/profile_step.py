@@ -35,15 +35,22 @@ def main():
         trainer.train_step([(host, receipt)])
     torch.cuda.synchronize()
     from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
         trainer.train_step([(host, receipt)])
         torch.cuda.synchronize()
     events = prof.key_averages()
-    total = sum(e.self_device_time_total for e in events)
-    rows = sorted(events, key=lambda e: -e.self_device_time_total)[: args.top]
+    kernels = [e for e in events if e.device_type.name == "CUDA"]
+    total = sum(e.self_device_time_total for e in kernels)
+    rows = sorted(kernels, key=lambda e: -e.self_device_time_total)[: args.top]
     print(json.dumps(dict(total_device_ms=round(total / 1000, 2), peak_gib=round(torch.cuda.max_memory_allocated() / 2**30, 1))))
+    print("== kernels ==")
     for e in rows:
         print(f"{e.self_device_time_total / 1000:9.2f} ms {100 * e.self_device_time_total / total:5.1f}% {e.count:6d}x  {e.key[:110]}")
+    print("== aten ops by input shape (device time of their kernels) ==")
+    shaped = [e for e in prof.key_averages(group_by_input_shape=True)
+              if e.key.startswith("aten::") and e.device_type.name == "CPU"]
+    for e in sorted(shaped, key=lambda e: -e.device_time_total)[: args.top]:
+        print(f"{e.device_time_total / 1000:9.2f} ms {e.count:6d}x  {e.key:28s} {str(e.input_shapes)[:120]}")
 
 
 if __name__ == "__main__":

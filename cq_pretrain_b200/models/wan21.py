@@ -144,7 +144,8 @@ class PatchEmbedding(nn.Module):
 class RowLayout:
     """Device-side row geometry of one DiT call, padded so rows divide evenly across TP."""
 
-    def __init__(self, gen, device, tp, tp_rank, pad_to=8):
+    def __init__(self, gen, device, tp, tp_rank, pad_to=None):
+        pad_to = pad_to or (128 if tp > 1 else 8)   # 128-row blocks per rank enable the fused TP kernels
         lengths = list(gen.lengths)
         total = sum(lengths)
         unit = tp * pad_to
@@ -191,7 +192,7 @@ class Wan21Generator(nn.Module):
         """conditions ``[targets, max_q, width]`` (replicated) -> row-sharded ``[sum q (padded), dit]``."""
         ctx = conditions.reshape(-1, self.cfg.width).index_select(0, gen.condition_indices.to(conditions.device))
         tp = ps.tp_size()
-        pad = (-ctx.shape[0]) % (8 * tp)
+        pad = (-ctx.shape[0]) % ((128 if tp > 1 else 8) * tp)
         if pad:
             ctx = torch.cat((ctx, ctx.new_zeros(pad, ctx.shape[1])))
         ctx = PL.split_rows(ctx)

@@ -46,7 +46,7 @@ def _symm():
 def gather_linear(x, weight, bias=None):
     """Return ``(all_gather(x) @ W^T + b, all_gather(x))``."""
     ws = _symm()
-    if ws is not None and ws.supports(x, weight):
+    if ws is not None and ws.supports_gather(x, weight):
         return ws.gather_linear(x, weight, bias)
     xg = gather_rows_raw(x)
     return gemm.linear(xg, weight, bias), xg

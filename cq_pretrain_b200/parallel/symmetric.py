@@ -77,11 +77,13 @@ class SymmetricWorkspace:
         if not (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2):
             return False
         rows = x.shape[0]
-        if transposed:   # dY [M, N_local] @ W [N_local, K] -> reduce-scatter rows
-            n_out = w.shape[1]
-            return (rows % (128 * self.tp) == 0 and n_out % 16 == 0 and x.shape[1] % 16 == 0
-                    and rows * n_out * 2 <= self.recv_bytes)
-        return x.shape[1] % 16 == 0 and w.shape[0] % 16 == 0 and x.data_ptr() % 16 == 0
+        n_out = w.shape[1] if transposed else w.shape[0]   # dY @ W (transposed) or x @ W^T
+        return (rows % (128 * self.tp) == 0 and n_out % 16 == 0 and x.shape[1] % 16 == 0
+                and rows * n_out * 2 <= self.recv_bytes and x.data_ptr() % 16 == 0)
+
+    def supports_gather(self, x, w):
+        return (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+                and x.shape[1] % 16 == 0 and w.shape[0] % 16 == 0 and self._gather_ok(x))
 
     def _gather_ok(self, x):
         rows = x.shape[0] * self.tp

@@ -50,7 +50,7 @@ class Trainer:
 
     def __init__(self, cfg: RunConfig, tp=1, lr=5e-5, warmup=0, total_steps=0, lr_style="cosine",
                  ema_decay=0.999, bucket_size=40_000_000, overlap=False, seed=871, device=None,
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, fused_tp=True):
         self.state = ps.initialize(tp) if ps.state().tp != tp or not dist.is_initialized() else ps.state()
         self.device = torch.device(device) if device is not None else self.state.device
         cfg.validate(tp)
@@ -61,6 +61,9 @@ class Trainer:
         self.ema = RendererEMA(self.model, self.optimizer, ema_decay) if ema_decay else None
         self.preparer = DevicePreparer(cfg, self.device, dtype)
         self.step_index = 0
+        if tp > 1 and fused_tp and self.device.type == "cuda":
+            from ..parallel import symmetric
+            symmetric.enable()
 
     def _micro(self, batch, scales, backward_scale):
         deferred = batch.generation is not None and bool(batch.generation.microbatches)
