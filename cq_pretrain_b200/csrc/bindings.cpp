@@ -52,6 +52,12 @@ std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::T
                                  double scale);
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
                                  at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale);
+// conv.cu
+at::Tensor conv_fwd(at::Tensor x, at::Tensor w, at::Tensor pos);
+std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor pos);
+std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunks, bool normalize, double scale);
+at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::Tensor rnorm, bool normalize,
+                         double scale);
 }  // namespace cqb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -85,4 +91,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_bwd", &cqb::gdn_bwd);
   m.def("attn_fwd", &cqb::attn_fwd);
   m.def("attn_bwd", &cqb::attn_bwd);
+  m.def("conv_fwd", &cqb::conv_fwd);
+  m.def("conv_bwd", &cqb::conv_bwd);
+  m.def("chunk_gather", &cqb::chunk_gather);
+  m.def("chunk_scatter", &cqb::chunk_scatter);
 }

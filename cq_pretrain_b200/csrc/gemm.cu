@@ -331,7 +331,18 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       const uint4* src = reinterpret_cast<const uint4*>(args.peer_in[s] + (size_t)lrow * args.K);
       uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)blk * BM * args.K);
       const int vecs = BM * args.K / 8;
-      for (int v = ct; v < vecs; v += 64) dst[v] = src[v];
+      // 16 independent 16-byte loads in flight per thread: NVLink latency is hidden by
+      // memory-level parallelism rather than by occupancy.
+      constexpr int UNROLL = 16;
+      int v = ct;
+      for (; v + 64 * (UNROLL - 1) < vecs; v += 64 * UNROLL) {
+        uint4 r[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) r[u] = __ldcg(src + v + 64 * u);
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) dst[v + 64 * u] = r[u];
+      }
+      for (; v < vecs; v += 64) dst[v] = __ldcg(src + v);
       fence_proxy_async_global();
       __threadfence();
       asm volatile("bar.sync 1, 64;" ::: "memory");

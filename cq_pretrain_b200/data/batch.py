@@ -49,6 +49,7 @@ class VisionInputs(Movable):
     content_indices: torch.Tensor
     features: torch.Tensor | None = None
     pixel_values: torch.Tensor | None = None
+    layout: object = None        # VisionLayout for the online tower (when features are not cached)
 
     @property
     def token_counts(self):

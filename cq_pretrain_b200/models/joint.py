@@ -42,6 +42,11 @@ class JointModel(nn.Module):
         self.final_norm = RMSNorm(cfg.width, cfg.norm_eps)
         self.renderer = Wan21Generator(cfg)
         self.lm_head = None if cfg.tie_word_embeddings else OutputHead(cfg)
+        if cfg.vision_encoder == "qwen35":
+            from .vision import VisionTower, vision_config
+            self.patch_embed = VisionTower(vision_config(cfg), cfg.width, cfg.freeze_vision, cfg.freeze_vision_merger)
+        else:
+            self.patch_embed = None
 
     # ---- backbone ---------------------------------------------------------------------------
     def embed(self, batch):
@@ -55,9 +60,12 @@ class JointModel(nn.Module):
         partial = self.embedding.partial(all_ids)
         vision = batch.vision
         if vision is not None and vision.content_indices.numel():
-            if vision.features is None:
-                raise ValueError("visual content needs merger features (cached or from the vision tower)")
-            feats = vision.features.to(partial.dtype)
+            if vision.features is not None:
+                feats = vision.features.to(partial.dtype)
+            elif vision.layout is not None and self.patch_embed is not None:
+                feats = self.patch_embed(vision.layout).to(partial.dtype)
+            else:
+                raise ValueError("visual content needs merger features (cached) or pixels for the vision tower")
             if ps.tp_size() > 1 and ps.tp_rank() != 0:
                 feats = torch.zeros_like(feats)  # the row reduce-scatter sums partial lookups
             partial = partial.index_copy(0, vision.content_indices, feats)

@@ -39,6 +39,7 @@ _DEVICE_LAYOUTS: dict = {}
 
 
 def _layout(bounds, chunk, device):
+    """Device chunk layout: (slot -> event index or -1, pad mask, event -> slot, doc chunk starts/counts, Nc)."""
     key = (bounds, chunk, str(device))
     hit = _DEVICE_LAYOUTS.get(key)
     if hit is None:
@@ -46,7 +47,7 @@ def _layout(bounds, chunk, device):
         idx = torch.tensor(index, dtype=torch.long)
         pad = idx < 0
         keep = (~pad).nonzero().flatten()
-        hit = (idx.clamp_min(0).to(device), pad.to(device), keep.to(device),
+        hit = (idx.to(device), pad.to(device), keep.to(device),
                torch.tensor(starts, dtype=torch.int32).to(device), torch.tensor(counts, dtype=torch.int32).to(device),
                len(index) // chunk)
         if len(_DEVICE_LAYOUTS) > 64:
@@ -110,19 +111,6 @@ def _factors(Q, K, V, G, B, chunk):
                 gamma=gamma)
 
 
-def _l2_fwd(x, scale=1.0):
-    xf = x.float()
-    r = torch.rsqrt(xf.square().sum(-1, keepdim=True) + 1e-6)
-    return (xf * r * scale).to(torch.bfloat16), r
-
-
-def _l2_bwd(x, r, dy, scale=1.0):
-    """y = scale * x r,  r = (sum x^2 + eps)^-1/2  ->  dx = scale (r dy - r^3 x (x . dy))."""
-    xf, dyf = x.float(), dy.float()
-    dot = (xf * dyf).sum(-1, keepdim=True)
-    return scale * (r * dyf - r.pow(3) * xf * dot)
-
-
 class _GatedDelta(torch.autograd.Function):
     """q, k, v ``[E,H,D]`` (bf16), g, beta ``[E,H]`` fp32 -> o ``[E,H,Dv]``; analytic chunked backward."""
 
@@ -130,15 +118,16 @@ class _GatedDelta(torch.autograd.Function):
     def forward(ctx, q, k, v, g, beta, layout, chunk):
         idx, pad, keep, start, count, Nc = layout
         E, H, Dk = q.shape
-        Dv = v.shape[-1]
-        qn, rq = _l2_fwd(q, Dk ** -0.5)
-        kn, rk = _l2_fwd(k)
-        Q, K, V, G, B = _to_chunks((qn, kn, v.to(torch.bfloat16), g.float(), beta.float()), idx, pad, Nc, chunk, H)
+        ops = _ext.ops()
+        Q, rq = ops.chunk_gather(q, idx, Nc, True, Dk ** -0.5)
+        K, rk = ops.chunk_gather(k, idx, Nc, True, 1.0)
+        V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
+        G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
         f = _factors(Q, K, V, G, B, chunk)
-        O, S = _ext.ops().gdn_fwd(f["W"], f["U"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
+        O, S = ops.gdn_fwd(f["W"], f["U"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
         ctx.save_for_backward(q, k, v, g, beta, rq, rk, S)
         ctx.layout, ctx.chunk = layout, chunk
-        return O.transpose(1, 2).reshape(Nc * chunk, H, Dv).index_select(0, keep)
+        return ops.chunk_scatter(O, keep, O, O, False, 1.0)
 
     @staticmethod
     def backward(ctx, dout):
@@ -148,12 +137,14 @@ class _GatedDelta(torch.autograd.Function):
         bf = torch.bfloat16
         E, H, Dk = q.shape
         Dv = v.shape[-1]
-        qn = (q.float() * rq * Dk ** -0.5).to(bf)
-        kn = (k.float() * rk).to(bf)
-        Q, K, V, G, B, dO = _to_chunks((qn, kn, v.to(bf), g.float(), beta.float(), dout.to(bf)), idx, pad, Nc, chunk, H)
+        ops = _ext.ops()
+        Q = ops.chunk_gather(q, idx, Nc, True, Dk ** -0.5)[0]
+        K = ops.chunk_gather(k, idx, Nc, True, 1.0)[0]
+        V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
+        dO = ops.chunk_gather(dout.to(bf).contiguous(), idx, Nc, False, 1.0)[0]
+        G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
         f = _factors(Q, K, V, G, B, chunk)
-        dO = dO.contiguous()
-        dS = _ext.ops().gdn_bwd(dO, f["W"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
+        dS = ops.gdn_bwd(dO, f["W"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
         Sb, dSb = S.to(bf), dS.to(bf)
         Delta = (f["U"].float() - torch.matmul(f["W"], Sb).float()).to(bf)
         dDelta = (torch.matmul(f["P"].transpose(-1, -2), dO).float() + torch.matmul(f["Kt"], dSb).float()).to(bf)
@@ -206,18 +197,18 @@ class _GatedDelta(torch.autograd.Function):
         db[..., -1] += dbC
         dG = db.flip(-1).cumsum(-1).flip(-1)
 
-        def back(t, width=None):
-            x = t.transpose(1, 2).reshape(Nc * chunk, H, *t.shape[3:]) if t.dim() == 4 else t.transpose(1, 2).reshape(Nc * chunk, H)
-            return x.index_select(0, keep)
+        def back(t):
+            return t.transpose(1, 2).reshape(Nc * chunk, H).index_select(0, keep)
 
-        dqn, dkn = back(dQ), back(dK)
-        dq = _l2_bwd(q, rq, dqn, Dk ** -0.5).to(q.dtype)
-        dk = _l2_bwd(k, rk, dkn).to(k.dtype)
-        dv = back(dV).to(v.dtype)
+        dq = ops.chunk_scatter(dQ.contiguous(), keep, q, rq, True, Dk ** -0.5)
+        dk = ops.chunk_scatter(dK.contiguous(), keep, k, rk, True, 1.0)
+        dv = ops.chunk_scatter(dV.contiguous(), keep, v, rk, False, 1.0)
         return dq, dk, dv, back(dG).to(g.dtype), back(dbeta).to(beta.dtype), None, None
 
 
 def _to_chunks(tensors, idx, pad, Nc, chunk, H):
+    """Per-event ``[E, H(, D)]`` tensors -> zero-padded chunk layout ``[Nc, H, C(, D)]``."""
+    idx = idx.clamp_min(0)
     out = []
     for t in tensors:
         x = t.index_select(0, idx)
@@ -233,11 +224,50 @@ def gated_delta_cuda(q, k, v, g, beta, bounds, chunk=CHUNK):
     """Event-ordered inputs -> event-ordered outputs ``[E, H, Dv]`` (bf16)."""
     E, H, Dk = q.shape
     Dv = v.shape[-1]
-    if Dk != 128 or Dv % 64 or chunk != CHUNK:
+    if Dk != 128 or Dv != 128 or chunk != CHUNK:
         return R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk).to(v.dtype)
     layout = _layout(tuple(int(x) for x in bounds), chunk, q.device)
-    return _GatedDelta.apply(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g, beta, layout, chunk)
+    bf = torch.bfloat16
+    return _GatedDelta.apply(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(), g, beta, layout,
+                             chunk)
+
+
+_POSITIONS: dict = {}
+
+
+def _positions(bounds, device):
+    """int32 index of each row inside its document (cached per packing)."""
+    key = (bounds, str(device))
+    hit = _POSITIONS.get(key)
+    if hit is None:
+        pos = torch.empty(bounds[-1] if bounds else 0, dtype=torch.int32)
+        for a, b in zip(bounds, bounds[1:]):
+            pos[a:b] = torch.arange(b - a, dtype=torch.int32)
+        hit = pos.to(device)
+        if len(_POSITIONS) > 64:
+            _POSITIONS.clear()
+        _POSITIONS[key] = hit
+    return hit
+
+
+class _CausalConv(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, pos):
+        ctx.save_for_backward(x, weight, pos)
+        return _ext.ops().conv_fwd(x, weight, pos)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, pos = ctx.saved_tensors
+        dx, dw = _ext.ops().conv_bwd(dy.contiguous(), x, weight, pos)
+        return dx, dw.to(weight.dtype), None
 
 
 def causal_conv_cuda(x, weight, bounds):
-    return R.causal_conv_silu(x, weight, bounds)
+    """Causal depthwise conv (kernel 4) + SiLU per document in ``csrc/conv.cu``; other kernels fall back."""
+    if weight.shape[-1] != 4 or x.shape[-1] % 8:
+        return R.causal_conv_silu(x, weight, bounds)
+    pos = _positions(tuple(int(b) for b in bounds), x.device)
+    if pos.numel() != x.shape[0]:
+        raise ValueError(f"document bounds cover {pos.numel()} rows, x has {x.shape[0]}")
+    return _CausalConv.apply(x.contiguous(), weight, pos)
