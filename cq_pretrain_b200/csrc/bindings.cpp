@@ -58,6 +58,11 @@ std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::
 std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunks, bool normalize, double scale);
 at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::Tensor rnorm, bool normalize,
                          double scale);
+// optim.cu
+void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avg,
+                std::vector<at::Tensor> exp_avg_sq, std::vector<at::Tensor> decay, std::vector<at::Tensor> params,
+                at::Tensor gscale, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2);
+at::Tensor sum_squares(std::vector<at::Tensor> xs);
 }  // namespace cqb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -91,6 +96,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_bwd", &cqb::gdn_bwd);
   m.def("attn_fwd", &cqb::attn_fwd);
   m.def("attn_bwd", &cqb::attn_bwd);
+  m.def("adamw_step", &cqb::adamw_step);
+  m.def("sum_squares", &cqb::sum_squares);
   m.def("conv_fwd", &cqb::conv_fwd);
   m.def("conv_bwd", &cqb::conv_bwd);
   m.def("chunk_gather", &cqb::chunk_gather);

@@ -4,7 +4,7 @@
 //  conv:   y[t, c] = silu( sum_i w[c, i] * x[t - (K-1) + i, c] ),  taps before the row's
 //          document start read zero (pos[t] = index of row t inside its document);
 //  bwd:    g = dy * silu'(pre);  dx[t, c] = sum_s w[c, K-1-s] g[t+s, c] (same document);
-//          dw[c, i] = sum_t g[t, c] x[t-(K-1)+i, c]  (per-thread partials, one atomic each).
+//          dw[c, i] = sum_t g[t, c] x[t-(K-1)+i, c]  (per-block partials, summed in a fixed order).
 //  chunks: rows of [E, H, D] events are gathered into the zero-padded chunk layout
 //          [Nc, H, 64, D], optionally L2-normalised on the way (rsqrt norms saved), and
 //          scattered back (with the L2-norm backward fused).
@@ -14,111 +14,190 @@ namespace cqb {
 
 namespace {
 
-template <int K>
-__global__ void conv_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
-                                const int* __restrict__ pos, __nv_bfloat16* __restrict__ y, int n, int C) {
-  const int vecs = C / 8;
-  const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (idx >= (size_t)n * vecs) return;
-  const int t = (int)(idx / vecs), c = (int)(idx % vecs) * 8;
-  const int p = pos[t];
-  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+// Block (32, 8): x -> 8-channel vector (256 channels per block), y -> row group of ROWS rows.
+// Taps come from a register window of the previous 3 rows, so every x row is read once per
+// thread (plus a 3-row halo); the transposed fp32 weight wT [4, C] is read once per thread.
+constexpr int CONV_K = 4;
+constexpr int CONV_ROWS = 32;
+constexpr int CONV_GROUPS = 8;
+
+struct ConvTaps {
+  float w[CONV_K][8];
+  __device__ __forceinline__ void load(const float* __restrict__ wT, int c, int C) {
 #pragma unroll
-  for (int i = 0; i < K; ++i) {
-    const int back = K - 1 - i;
-    if (back <= p) {
-      float xv[8];
-      load8(x + (size_t)(t - back) * C + c, xv);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += w[(c + j) * K + i] * xv[j];
-    }
+    for (int i = 0; i < CONV_K; ++i) load8(wT + (size_t)i * C + c, w[i]);
   }
+  // sum_i w_i x[t - (K-1) + i] over the taps inside the document (p = row index in document)
+  __device__ __forceinline__ void apply(float* acc, const float (*win)[8], const float* cur, int p) const {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = silu(acc[j]);
-  store8(y + (size_t)t * C + c, acc);
+    for (int j = 0; j < 8; ++j) acc[j] = w[CONV_K - 1][j] * cur[j];
+#pragma unroll
+    for (int back = 1; back < CONV_K; ++back)
+      if (back <= p)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += w[CONV_K - 1 - back][j] * win[CONV_K - 1 - back][j];
+  }
+};
+
+__device__ __forceinline__ void load_row_or_zero(const __nv_bfloat16* x, long row, int C, int c, float* out) {
+  if (row >= 0) {
+    load8(x + (size_t)row * C + c, out);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = 0.f;
+  }
 }
 
-template <int K>
-__global__ void conv_grad_pre_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                                     const float* __restrict__ w, const int* __restrict__ pos, float* __restrict__ g,
-                                     int n, int C) {
-  const int vecs = C / 8;
-  const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (idx >= (size_t)n * vecs) return;
-  const int t = (int)(idx / vecs), c = (int)(idx % vecs) * 8;
-  const int p = pos[t];
-  float pre[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-  for (int i = 0; i < K; ++i) {
-    const int back = K - 1 - i;
-    if (back <= p) {
-      float xv[8];
-      load8(x + (size_t)(t - back) * C + c, xv);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) pre[j] += w[(c + j) * K + i] * xv[j];
-    }
-  }
-  float d[8], o[8];
-  load8(dy + (size_t)t * C + c, d);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float sg = 1.f / (1.f + __expf(-pre[j]));
-    o[j] = d[j] * sg * (1.f + pre[j] * (1.f - sg));
-  }
-  store8(g + (size_t)t * C + c, o);
-}
-
-// One thread: 8 channels x ROWS consecutive rows; dw partials in registers.
-template <int K, int ROWS>
-__global__ void conv_bwd_kernel(const float* __restrict__ g, const __nv_bfloat16* __restrict__ x,
-                                const float* __restrict__ w, const int* __restrict__ pos,
-                                __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int n, int C) {
-  const int vecs = C / 8;
-  const int v = blockIdx.x * blockDim.x + threadIdx.x;
-  if (v >= vecs) return;
+__global__ void __launch_bounds__(256) conv_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                                       const float* __restrict__ wT, const int* __restrict__ pos,
+                                                       __nv_bfloat16* __restrict__ y, int n, int C) {
+  const int v = blockIdx.x * 32 + threadIdx.x;
+  if (v >= C / 8) return;
   const int c = v * 8;
-  const int t0 = blockIdx.y * ROWS, t1 = min(n, t0 + ROWS);
-  float wl[K][8];
+  const int t0 = (blockIdx.y * CONV_GROUPS + threadIdx.y) * CONV_ROWS;
+  const int t1 = min(n, t0 + CONV_ROWS);
+  if (t0 >= t1) return;
+  ConvTaps taps;
+  taps.load(wT, c, C);
+  float win[CONV_K - 1][8];  // rows t-3, t-2, t-1
 #pragma unroll
-  for (int i = 0; i < K; ++i)
+  for (int b = 0; b < CONV_K - 1; ++b) load_row_or_zero(x, (long)t0 - (CONV_K - 1) + b, C, c, win[b]);
+#pragma unroll 4
+  for (int t = t0; t < t1; ++t) {
+    float cur[8], acc[8];
+    load8(x + (size_t)t * C + c, cur);
+    taps.apply(acc, win, cur, pos[t]);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) wl[i][j] = w[(c + j) * K + i];
-  float part[K][8];
+    for (int j = 0; j < 8; ++j) acc[j] = silu(acc[j]);
+    store8(y + (size_t)t * C + c, acc);
 #pragma unroll
-  for (int i = 0; i < K; ++i)
+    for (int b = 0; b < CONV_K - 2; ++b)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) win[b][j] = win[b + 1][j];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) win[CONV_K - 2][j] = cur[j];
+  }
+}
+
+// Fused backward. Row u: pre_u (recomputed), g_u = dy_u silu'(pre_u); dw partials use rows of the
+// thread's own range; dx_t = sum_s w_{K-1-s} g_{t+s} (same document) is emitted K-1 rows behind
+// u, so the thread recomputes g for a (K-1)-row halo past its range. Per-block dw partials are
+// reduced over the 8 row groups in shared memory and written to partial[blockIdx.y, C, K].
+__global__ void __launch_bounds__(256) conv_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                       const __nv_bfloat16* __restrict__ x,
+                                                       const float* __restrict__ wT, const int* __restrict__ pos,
+                                                       __nv_bfloat16* __restrict__ dx, float* __restrict__ partial,
+                                                       int n, int C) {
+  __shared__ float red[CONV_GROUPS][CONV_K * 8][33];
+  const int v = blockIdx.x * 32 + threadIdx.x;
+  const bool active = v < C / 8;
+  const int c = v * 8;
+  const int t0 = (blockIdx.y * CONV_GROUPS + threadIdx.y) * CONV_ROWS;
+  const int t1 = min(n, t0 + CONV_ROWS);
+  float part[CONV_K][8];
+#pragma unroll
+  for (int i = 0; i < CONV_K; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) part[i][j] = 0.f;
-  for (int t = t0; t < t1; ++t) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (active && t0 < t1) {
+    ConvTaps taps;
+    taps.load(wT, c, C);
+    float xw[CONV_K - 1][8], gw[CONV_K - 1][8];
+    int pw[CONV_K - 1];
 #pragma unroll
-    for (int s = 0; s < K; ++s) {
-      const int tt = t + s;
-      if (tt < n && pos[tt] >= s) {
-        float gv[8];
-        load8(g + (size_t)tt * C + c, gv);
+    for (int b = 0; b < CONV_K - 1; ++b) {
+      load_row_or_zero(x, (long)t0 - (CONV_K - 1) + b, C, c, xw[b]);
+      pw[b] = -1;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += wl[K - 1 - s][j] * gv[j];
-      }
+      for (int j = 0; j < 8; ++j) gw[b][j] = 0.f;
     }
-    store8(dx + (size_t)t * C + c, acc);
-    float gt[8];
-    load8(g + (size_t)t * C + c, gt);
-    const int p = pos[t];
+    const int u_end = t1 + CONV_K - 1;
+#pragma unroll 2
+    for (int u = t0; u < u_end; ++u) {
+      float cur[8], g[8];
+      int p = -1;
+      if (u < n) {
+        p = pos[u];
+        load8(x + (size_t)u * C + c, cur);
+        float pre[8], d[8];
+        taps.apply(pre, xw, cur, p);
+        load8(dy + (size_t)u * C + c, d);
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-      const int back = K - 1 - i;
-      if (back <= p) {
-        float xv[8];
-        load8(x + (size_t)(t - back) * C + c, xv);
+        for (int j = 0; j < 8; ++j) {
+          const float sg = 1.f / (1.f + __expf(-pre[j]));
+          g[j] = d[j] * sg * (1.f + pre[j] * (1.f - sg));
+        }
+        if (u < t1) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) part[i][j] += gt[j] * xv[j];
+          for (int j = 0; j < 8; ++j) part[CONV_K - 1][j] += g[j] * cur[j];
+#pragma unroll
+          for (int back = 1; back < CONV_K; ++back)
+            if (back <= p)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) part[CONV_K - 1 - back][j] += g[j] * xw[CONV_K - 1 - back][j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cur[j] = g[j] = 0.f;
+      }
+      const int t = u - (CONV_K - 1);
+      if (t >= t0) {
+        // s = 0 is row t itself; s = 1..K-1 are gw[s] (rows t+1..t+K-2) and g (row u = t+K-1)
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = taps.w[CONV_K - 1][j] * gw[0][j];
+#pragma unroll
+        for (int s = 1; s < CONV_K - 1; ++s)
+          if (pw[s] >= s)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] += taps.w[CONV_K - 1 - s][j] * gw[s][j];
+        if (p >= CONV_K - 1)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += taps.w[0][j] * g[j];
+        store8(dx + (size_t)t * C + c, acc);
+      }
+#pragma unroll
+      for (int b = 0; b < CONV_K - 2; ++b) {
+        pw[b] = pw[b + 1];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xw[b][j] = xw[b + 1][j];
+          gw[b][j] = gw[b + 1][j];
+        }
+      }
+      pw[CONV_K - 2] = p;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xw[CONV_K - 2][j] = cur[j];
+        gw[CONV_K - 2][j] = g[j];
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < K; ++i)
+  for (int i = 0; i < CONV_K; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) atomicAdd(dw + (c + j) * K + i, part[i][j]);
+    for (int j = 0; j < 8; ++j) red[threadIdx.y][j * CONV_K + i][threadIdx.x] = part[i][j];
+  __syncthreads();
+  // 256 threads write the block's 32 vectors x 8 channels x K taps = 1024 values
+  const int tid = threadIdx.y * 32 + threadIdx.x;
+  for (int e = tid; e < 32 * 8 * CONV_K; e += 256) {
+    const int lane = e / (8 * CONV_K), r = e % (8 * CONV_K);
+    const int vv = blockIdx.x * 32 + lane;
+    if (vv >= C / 8) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int gi = 0; gi < CONV_GROUPS; ++gi) sum += red[gi][r][lane];
+    partial[((size_t)blockIdx.y * C + vv * 8) * CONV_K + r] = sum;
+  }
+}
+
+// dw[e] = sum_b partial[b, e]  (fixed order: deterministic)
+__global__ void sum_rows_kernel(const float* __restrict__ partial, float* __restrict__ out, int rows, int width) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= width) return;
+  float s = 0.f;
+  for (int b = 0; b < rows; ++b) s += partial[(size_t)b * width + e];
+  out[e] = s;
 }
 
 // out[n, h, c, :] = normalise?(x[idx[n*64 + c], h, :]) (zero when idx < 0); r[e, h] = rsqrt norm.
@@ -197,39 +276,48 @@ int blocks_for(size_t threads, int per = 256) { return (int)((threads + per - 1)
 
 }  // namespace
 
-at::Tensor conv_fwd(at::Tensor x, at::Tensor w, at::Tensor pos) {
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2 && x.size(1) % 8 == 0,
+dim3 conv_grid(int n, int C) {
+  return dim3((C / 8 + 31) / 32, (n + CONV_ROWS * CONV_GROUPS - 1) / (CONV_ROWS * CONV_GROUPS));
+}
+
+void check_conv(const at::Tensor& x, const at::Tensor& w, const at::Tensor& pos) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2 &&
+                  x.size(1) % 8 == 0,
               "x: contiguous bf16 [n, C], C % 8 == 0");
-  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.numel() == x.size(0), "pos: int32 [n]");
-  const int n = x.size(0), C = x.size(1), K = w.size(1);
-  auto wf = w.to(at::kFloat).contiguous();
+  TORCH_CHECK(w.dim() == 2 && w.size(0) == x.size(1) && w.size(1) == CONV_K, "w: [C, 4] (only kernel size 4)");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous() && pos.numel() == x.size(0), "pos: int32 [n]");
+}
+
+at::Tensor conv_fwd(at::Tensor x, at::Tensor w, at::Tensor pos) {
+  check_conv(x, w, pos);
+  const int n = x.size(0), C = x.size(1);
+  auto wT = w.to(at::kFloat).t().contiguous();
   auto y = at::empty_like(x);
   if (!n) return y;
-  TORCH_CHECK(K == 4, "only kernel size 4 is compiled");
-  conv_fwd_kernel<4><<<blocks_for((size_t)n * C / 8), 256, 0, stream()>>>(
-      (const __nv_bfloat16*)x.data_ptr(), wf.data_ptr<float>(), pos.data_ptr<int>(), (__nv_bfloat16*)y.data_ptr(), n, C);
+  conv_fwd_kernel<<<conv_grid(n, C), dim3(32, CONV_GROUPS), 0, stream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), wT.data_ptr<float>(), pos.data_ptr<int>(), (__nv_bfloat16*)y.data_ptr(), n,
+      C);
   CQB_LAUNCH_CHECK();
   count_launch();
   return y;
 }
 
 std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor pos) {
-  const int n = x.size(0), C = x.size(1), K = w.size(1);
-  auto wf = w.to(at::kFloat).contiguous();
+  check_conv(x, w, pos);
+  TORCH_CHECK(dy.scalar_type() == at::kBFloat16 && dy.is_contiguous() && dy.sizes() == x.sizes(), "dy: like x");
+  const int n = x.size(0), C = x.size(1);
+  auto wT = w.to(at::kFloat).t().contiguous();
   auto dx = at::empty_like(x);
-  auto dw = at::zeros({C, K}, x.options().dtype(at::kFloat));
-  if (!n) return {dx, dw};
-  TORCH_CHECK(K == 4, "only kernel size 4 is compiled");
-  auto g = at::empty({n, C}, x.options().dtype(at::kFloat));
-  auto d = dy.contiguous();
-  conv_grad_pre_kernel<4><<<blocks_for((size_t)n * C / 8), 256, 0, stream()>>>(
-      (const __nv_bfloat16*)d.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), wf.data_ptr<float>(),
-      pos.data_ptr<int>(), g.data_ptr<float>(), n, C);
-  constexpr int ROWS = 64;
-  dim3 grid((C / 8 + 127) / 128, (n + ROWS - 1) / ROWS);
-  conv_bwd_kernel<4, ROWS><<<grid, 128, 0, stream()>>>(g.data_ptr<float>(), (const __nv_bfloat16*)x.data_ptr(),
-                                                     wf.data_ptr<float>(), pos.data_ptr<int>(),
-                                                     (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), n, C);
+  auto dw = at::empty({C, CONV_K}, x.options().dtype(at::kFloat));
+  if (!n) return {dx, dw.zero_()};
+  const dim3 grid = conv_grid(n, C);
+  auto partial = at::empty({(long)grid.y, C, CONV_K}, x.options().dtype(at::kFloat));
+  conv_bwd_kernel<<<grid, dim3(32, CONV_GROUPS), 0, stream()>>>(
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), wT.data_ptr<float>(),
+      pos.data_ptr<int>(), (__nv_bfloat16*)dx.data_ptr(), partial.data_ptr<float>(), n, C);
+  CQB_LAUNCH_CHECK();
+  sum_rows_kernel<<<(C * CONV_K + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                  grid.y, C * CONV_K);
   CQB_LAUNCH_CHECK();
   count_launch(2);
   return {dx, dw};

@@ -115,7 +115,7 @@ class DistributedOptimizer:
             n = (b.end - b.start) // self.dp
             lo = b.start + self.dp_rank * n
             master = b.group.param_buffer[lo:lo + n].float().clone()
-            decay = torch.zeros(n, dtype=torch.float32, device=device)
+            decay = torch.zeros(n, dtype=torch.uint8, device=device)
             ema_mask = torch.zeros(n, dtype=torch.bool, device=device)
             for p in b.params:
                 o = b.group.offsets[p]
@@ -123,7 +123,7 @@ class DistributedOptimizer:
                 if a < e:
                     name = self.names[p]
                     if p.dim() > 1 and not name.endswith(".bias"):
-                        decay[a - lo:e - lo] = 1.0
+                        decay[a - lo:e - lo] = 1
                     if ema_prefix and name.startswith(ema_prefix):
                         ema_mask[a - lo:e - lo] = True
             self.shards.append(dict(bucket=b, lo=lo, n=n, master=master, exp_avg=torch.zeros_like(master),
@@ -225,13 +225,18 @@ class DistributedOptimizer:
         b = s["bucket"]
         return b.group.grad_buffer[s["lo"]:s["lo"] + s["n"]]
 
+    def _use_kernels(self):
+        return self.shards[0]["master"].is_cuda and _ext.cuda_kernels_enabled() and _ext.has("adamw_step")
+
     def grad_norm(self):
-        total = torch.zeros((), dtype=torch.float32, device=self.shards[0]["master"].device)
-        for s in self.shards:
-            g = self._grad_shard(s)
-            if s["bucket"].group.replicated and self.tp_rank != 0:
-                continue
-            total += g.float().square().sum()
+        counted = [self._grad_shard(s) for s in self.shards
+                   if not (s["bucket"].group.replicated and self.tp_rank != 0) and s["n"]]
+        if counted and self._use_kernels():
+            total = _ext.ops().sum_squares(counted)   # one multi-tensor pass, fixed reduction order
+        else:
+            total = torch.zeros((), dtype=torch.float32, device=self.shards[0]["master"].device)
+            for g in counted:
+                total += g.float().square().sum()
         if self.dp > 1:
             dist.all_reduce(total, group=self.dp_group)
         if self.tp > 1:
@@ -251,24 +256,23 @@ class DistributedOptimizer:
         bc1 = 1 - b1 ** self.step_count
         bc2 = 1 - b2 ** self.step_count
         grads = [self._grad_shard(s) for s in self.shards]
-        gscale = (coef * scale)
-        use_kernel = grads[0].is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "adamw_step")
-        if use_kernel:
+        gscale = (coef * scale).float().reshape(())
+        published = [s["bucket"].group.param_buffer[s["lo"]:s["lo"] + s["n"]] for s in self.shards]
+        if self._use_kernels():
+            # one launch: scale, moments, decoupled decay, update and the parameter write-back
             _ext.ops().adamw_step([s["master"] for s in self.shards], grads, [s["exp_avg"] for s in self.shards],
                                   [s["exp_avg_sq"] for s in self.shards], [s["decay"] for s in self.shards],
-                                  gscale, lr, b1, b2, self.eps, self.weight_decay, bc1, bc2)
+                                  published, gscale, lr, b1, b2, self.eps, self.weight_decay, bc1, bc2)
         else:
-            for s, g in zip(self.shards, grads):
+            for s, g, out in zip(self.shards, grads, published):
                 g = g * gscale
                 m, v, p = s["exp_avg"], s["exp_avg_sq"], s["master"]
                 m.mul_(b1).add_(g, alpha=1 - b1)
                 v.mul_(b2).addcmul_(g, g, value=1 - b2)
                 update = (m / bc1) / ((v / bc2).sqrt() + self.eps)
-                p.mul_(1 - lr * self.weight_decay * s["decay"])
+                p.mul_(1 - lr * self.weight_decay * s["decay"].float())
                 p.add_(update, alpha=-lr)
-        for s in self.shards:
-            b = s["bucket"]
-            b.group.param_buffer[s["lo"]:s["lo"] + s["n"]].copy_(s["master"])
+                out.copy_(p)
         self.all_gather_params()
         return finite, norm
 
