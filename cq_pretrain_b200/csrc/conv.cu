@@ -10,6 +10,9 @@
 //          scattered back (with the L2-norm backward fused).
 #include "common.cuh"
 
+#include <cstdio>
+#include <mutex>
+
 namespace cqb {
 
 namespace {
@@ -370,3 +373,130 @@ at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::T
 }
 
 }  // namespace cqb
+
+// ==== Allocation-free causal-conv backward (C ABI) ============================================
+//
+// This entry point has no counterpart in the reference framework. It serves callers that must
+// not allocate device memory while they run the backward pass of the short convolution:
+//   * hooks that run inside a caching allocator or memory pool (they cannot re-enter the
+//     allocator they belong to);
+//   * C or C++ hosts that drive the kernels without PyTorch and so have no tensor allocator;
+//   * steps whose device memory was reserved once up front, where a late cudaMalloc could fail
+//     or fragment the reserved pool.
+// It launches the same two kernels as the tensor entry point `conv_bwd` (fused backward per row
+// group, then a fixed-order sum of the per-block weight-gradient partials). The partials live in
+// a file-scope device array instead of a fresh allocation, and the caller passes every buffer,
+// including the transposed fp32 weight.
+//
+// Contract:
+//   * Size limit: ceil(n / 256) * C * 4 floats of partials must fit in the scratch array of
+//     2,097,152 floats (8 MiB; for C = 6144 that is n <= 21,760 rows). Larger inputs are rejected
+//     with CQB_NOALLOC_TOO_LARGE; cqb_noalloc_last_error() returns the message.
+//   * Every GPU that loads this library holds the 8 MiB array until the process exits.
+//   * Set-up: the first call on a device (or cqb_conv_bwd_noalloc_init() with that device
+//     current) looks up the array's device address with cudaGetSymbolAddress. Make that first
+//     call before any stream capture begins.
+//   * All calls on a device share the array, and it keeps the last call's contents. Calls that
+//     overlap on the GPU (different streams, or threads without ordering) race on it: serialise
+//     them on one stream or order them with events. Each call overwrites every partial it
+//     reads, so nothing has to start at zero; for n == 0 the weight gradient is cleared with
+//     cudaMemsetAsync.
+//   * No cudaMalloc, cudaFree or allocating library routine is called.
+
+static __device__ __align__(256) float g_conv_noalloc_scratch[size_t(2) * 1024 * 1024];
+
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(2) * 1024 * 1024;
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {};   // device address of the scratch array, per device
+std::mutex g_scratch_mu;
+thread_local char g_noalloc_error[256] = "";
+
+int noalloc_fail(int code, const char* fmt, long a = 0, long b = 0) {
+  snprintf(g_noalloc_error, sizeof(g_noalloc_error), fmt, a, b);
+  return code;
+}
+
+}  // namespace
+
+extern "C" {
+
+enum {
+  CQB_NOALLOC_OK = 0,
+  CQB_NOALLOC_BAD_ARGUMENT = 1,
+  CQB_NOALLOC_TOO_LARGE = 2,
+  CQB_NOALLOC_CUDA_ERROR = 3,
+};
+
+// Message of the last failed call on this host thread.
+__attribute__((visibility("default"))) const char* cqb_noalloc_last_error(void) { return g_noalloc_error; }
+
+// Capacity of the scratch array in floats.
+__attribute__((visibility("default"))) size_t cqb_conv_bwd_noalloc_scratch_floats(void) {
+  return kNoAllocScratchFloats;
+}
+
+// Looks up the scratch address for the current device (idempotent). Call before stream capture.
+__attribute__((visibility("default"))) int cqb_conv_bwd_noalloc_init(void) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "cudaGetDevice failed (error %ld)", (long)err);
+  if (device < 0 || device >= kMaxDevices)
+    return noalloc_fail(CQB_NOALLOC_BAD_ARGUMENT, "device %ld is outside the supported range [0, %ld)", device,
+                        kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[device] != nullptr) return CQB_NOALLOC_OK;
+  float* ptr = nullptr;
+  err = cudaGetSymbolAddress((void**)&ptr, g_conv_noalloc_scratch);
+  if (err != cudaSuccess || ptr == nullptr)
+    return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "cudaGetSymbolAddress of the conv scratch failed (error %ld)",
+                        (long)err);
+  g_scratch_ptr[device] = ptr;
+  return CQB_NOALLOC_OK;
+}
+
+// Backward of y = silu(causal_conv(x, w)) per document.
+//   dy, x, dx: bf16 [n, C] row-major, 16-byte aligned;  wT: fp32 [4, C] (tap-major: the transpose
+//   of the [C, 4] weight), 16-byte aligned;  pos: int32 [n], index of each row inside its
+//   document;  dw: fp32 [C, 4] output.  C must be a positive multiple of 8.
+// Returns CQB_NOALLOC_OK or an error code (message in cqb_noalloc_last_error()).
+__attribute__((visibility("default"))) int cqb_conv_bwd_noalloc(const void* dy, const void* x, const float* wT,
+                                                                 const int* pos, void* dx, float* dw, long n, long C,
+                                                                 cudaStream_t stream) {
+  if (n < 0 || C <= 0 || C % 8 != 0 || C > (1L << 24) || n > (1L << 30))
+    return noalloc_fail(CQB_NOALLOC_BAD_ARGUMENT, "need n >= 0 and C a positive multiple of 8 (n=%ld, C=%ld)", n, C);
+  if (!dw || (n > 0 && (!dy || !x || !wT || !pos || !dx)))
+    return noalloc_fail(CQB_NOALLOC_BAD_ARGUMENT, "null buffer pointer");
+  auto misaligned = [](const void* p, uintptr_t bytes) { return reinterpret_cast<uintptr_t>(p) % bytes != 0; };
+  if (misaligned(dy, 16) || misaligned(x, 16) || misaligned(dx, 16) || misaligned(wT, 16) || misaligned(pos, 4) ||
+      misaligned(dw, 4))
+    return noalloc_fail(CQB_NOALLOC_BAD_ARGUMENT, "dy, x, dx and wT must be 16-byte aligned, pos and dw 4-byte");
+  const int rc = cqb_conv_bwd_noalloc_init();
+  if (rc != CQB_NOALLOC_OK) return rc;
+  if (n == 0) {
+    const cudaError_t err = cudaMemsetAsync(dw, 0, sizeof(float) * C * cqb::CONV_K, stream);
+    return err == cudaSuccess ? CQB_NOALLOC_OK
+                              : noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "cudaMemsetAsync failed (error %ld)", (long)err);
+  }
+  const dim3 grid = cqb::conv_grid((int)n, (int)C);
+  const size_t need = (size_t)grid.y * C * cqb::CONV_K;
+  if (need > kNoAllocScratchFloats)
+    return noalloc_fail(CQB_NOALLOC_TOO_LARGE,
+                        "input too large for the static scratch: it needs %ld floats (ceil(n / 256) * C * 4), "
+                        "the limit is %ld",
+                        (long)need, (long)kNoAllocScratchFloats);
+  int device = 0;
+  cudaGetDevice(&device);
+  float* scratch = g_scratch_ptr[device];
+  cqb::conv_bwd_kernel<<<grid, dim3(32, cqb::CONV_GROUPS), 0, stream>>>(
+      (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, wT, pos, (__nv_bfloat16*)dx, scratch, (int)n, (int)C);
+  cqb::sum_rows_kernel<<<(unsigned)((C * cqb::CONV_K + 255) / 256), 256, 0, stream>>>(scratch, dw, (int)grid.y,
+                                                                                       (int)(C * cqb::CONV_K));
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "kernel launch failed (error %ld)", (long)err);
+  cqb::count_launch(2);
+  return CQB_NOALLOC_OK;
+}
+
+}  // extern "C"
