@@ -52,6 +52,10 @@ std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::T
                                  double scale);
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
                                  at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale);
+// gdn_chunk.cu
+std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor G, at::Tensor B);
+std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
+                                      at::Tensor B, at::Tensor S, at::Tensor dS);
 // conv.cu
 at::Tensor conv_fwd(at::Tensor x, at::Tensor w, at::Tensor pos);
 std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor pos);
@@ -98,6 +102,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &cqb::attn_bwd);
   m.def("adamw_step", &cqb::adamw_step);
   m.def("sum_squares", &cqb::sum_squares);
+  m.def("gdn_prep", &cqb::gdn_prep);
+  m.def("gdn_chunk_bwd", &cqb::gdn_chunk_bwd);
   m.def("conv_fwd", &cqb::conv_fwd);
   m.def("conv_bwd", &cqb::conv_bwd);
   m.def("chunk_gather", &cqb::chunk_gather);

@@ -1,0 +1,841 @@
+// Chunk-local work of the chunked gated delta rule: one CTA per (chunk, head), 8 warps,
+// bf16 tensor-core tiles (mma.sync m16n8k16, fp32 accumulate) in shared memory.
+//
+// Per chunk of C = 64 events (key/value dim 128), with b = cumsum(g) inside the chunk,
+// E_ij = exp(b_i - b_j):
+//   A  = tril(beta_i E_ij k_i.k_j, -1)          T = (I + A)^-1   (column substitution, fp32)
+//   W  = T diag(beta e^b) K                     U = T diag(beta) V
+//   P  = tril(Q K^T * E)                        Qd = diag(e^b) Q     Kt = diag(e^{b_C - b}) K
+//   gamma = e^{b_C}
+// These are the inputs of the per-document state recurrence (gdn.cu). The same algebra is the
+// chunked form used by the reference's GDN backends (ops/gated_delta_net.py:143-214).
+#include "common.cuh"
+#include "mma_sync.cuh"
+
+namespace cqb {
+
+namespace {
+
+using namespace ws;
+
+constexpr int CH = 64, DH = 128, THREADS_C = 256;
+constexpr int LD = DH + 8;     // bf16 row of a 128-wide tile (272 bytes: rows stay 16-byte aligned)
+constexpr int LD64 = CH + 8;   // bf16 row of a 64-wide tile
+constexpr int LDF = CH + 1;    // fp32 row of a 64x64 matrix
+constexpr int TILE = CH * LD;  // elements of one 64x128 bf16 tile
+
+struct PrepArgs {
+  const __nv_bfloat16* Q;  // [Nc*H, 64, 128] normalised, scaled queries
+  const __nv_bfloat16* K;  // [Nc*H, 64, 128] normalised keys
+  const __nv_bfloat16* V;  // [Nc*H, 64, 128]
+  const float* G;          // [Nc*H, 64] log decay
+  const float* B;          // [Nc*H, 64] beta
+  __nv_bfloat16* W;
+  __nv_bfloat16* U;
+  __nv_bfloat16* P;        // [Nc*H, 64, 64]
+  __nv_bfloat16* Qd;
+  __nv_bfloat16* Kt;
+  float* gamma;            // [Nc*H]
+};
+
+__device__ __forceinline__ void load_tile_async(__nv_bfloat16* dst, const __nv_bfloat16* src, int tid) {
+  for (int i = tid; i < CH * DH / 8; i += THREADS_C) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    cp_async16(dst + r * LD + c, src + r * DH + c);
+  }
+}
+
+// smem tile (row-major, ld LD) -> global [64][128] with 16-byte vectors, rows scaled by rs[] if given
+__device__ __forceinline__ void store_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, const float* rs, int tid,
+                                           int first, int stride) {
+  for (int i = tid - first; i < CH * DH / 8; i += stride) {
+    if (i < 0) continue;
+    const int r = i >> 4, c = (i & 15) * 8;
+    float v[8];
+    load8(src + r * LD + c, v);
+    if (rs) {
+      const float s = rs[r];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= s;
+    }
+    store8(dst + r * DH + c, v);
+  }
+}
+
+// Inclusive cumsum of g (64 values) by warp 0; fills b, e^b, e^{b_C - b}; returns b_C on lane 0.
+__device__ __forceinline__ float chunk_decay(const float* g, float* b, float* eb, float* kdec, int lane) {
+  const float g0 = g[2 * lane], g1 = g[2 * lane + 1];
+  float s = g0 + g1;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float v = __shfl_up_sync(0xffffffffu, s, off);
+    if (lane >= off) s += v;
+  }
+  const float excl = s - (g0 + g1);
+  const float b0 = excl + g0, b1 = excl + g0 + g1;
+  const float bc = __shfl_sync(0xffffffffu, s, 31);
+  b[2 * lane] = b0;
+  b[2 * lane + 1] = b1;
+  eb[2 * lane] = __expf(b0);
+  eb[2 * lane + 1] = __expf(b1);
+  kdec[2 * lane] = __expf(bc - b0);
+  kdec[2 * lane + 1] = __expf(bc - b1);
+  return bc;
+}
+
+// T = (I + A)^-1 for strictly lower-triangular A (fp32, ld LDF): thread c < 64 owns column c.
+// T[i][c] = -sum_{j=c}^{i-1} A[i][j] T[j][c]; every lane of a warp runs inner loops of equal length.
+__device__ __forceinline__ void unit_lower_inverse(const float* A, float* T, int c) {
+  for (int i = 0; i < c; ++i) T[i * LDF + c] = 0.f;
+  T[c * LDF + c] = 1.f;
+  for (int i = c + 1; i < CH; ++i) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int j = c;
+    for (; j + 3 < i; j += 4) {
+      s0 += A[i * LDF + j] * T[j * LDF + c];
+      s1 += A[i * LDF + j + 1] * T[(j + 1) * LDF + c];
+      s2 += A[i * LDF + j + 2] * T[(j + 2) * LDF + c];
+      s3 += A[i * LDF + j + 3] * T[(j + 3) * LDF + c];
+    }
+    for (; j < i; ++j) s0 += A[i * LDF + j] * T[j * LDF + c];
+    T[i * LDF + c] = -((s0 + s1) + (s2 + s3));
+  }
+}
+
+
+// ---- warp-tile products: acc[NT][4] (rows rs..rs+15, n-tiles c0 + 8j) += A x B over kdim ----
+// A row-major [m][k] (lda), B row-major [k][n] (ldb)
+template <int NT>
+__device__ __forceinline__ void mm_ab(float (*acc)[4], const __nv_bfloat16* A, int lda, const __nv_bfloat16* B,
+                                      int ldb, int rs, int c0, int kdim, int lane) {
+#pragma unroll 2
+  for (int k0 = 0; k0 < kdim; k0 += 16) {
+    uint32_t a[4];
+    frag_a(a, A, rs, k0, lda, lane);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      frag_b2(b, B, k0, c0 + 8 * j, ldb, lane);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+// A row-major [m][k], B = X^T with X row-major [n][k]
+template <int NT>
+__device__ __forceinline__ void mm_abt(float (*acc)[4], const __nv_bfloat16* A, int lda, const __nv_bfloat16* X,
+                                       int ldx, int rs, int c0, int kdim, int lane) {
+#pragma unroll 2
+  for (int k0 = 0; k0 < kdim; k0 += 16) {
+    uint32_t a[4];
+    frag_a(a, A, rs, k0, lda, lane);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      frag_bt2(b, X, k0, c0 + 8 * j, ldx, lane);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+// A = X^T with X row-major [k][m], B row-major [k][n]
+template <int NT>
+__device__ __forceinline__ void mm_atb(float (*acc)[4], const __nv_bfloat16* X, int ldx, const __nv_bfloat16* B,
+                                       int ldb, int rs, int c0, int kdim, int lane) {
+#pragma unroll 2
+  for (int k0 = 0; k0 < kdim; k0 += 16) {
+    uint32_t a[4];
+    frag_at(a, X, rs, k0, ldx, lane);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      frag_b2(b, B, k0, c0 + 8 * j, ldb, lane);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void zero_acc(float (*acc)[4]) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+}
+
+// Element e of n-tile j sits at row rs + g + 8 (e >> 1), column c0 + 8 j + 2 t + (e & 1).
+__device__ __forceinline__ int acc_row(int rs, int lane, int e) { return rs + (lane >> 2) + 8 * (e >> 1); }
+__device__ __forceinline__ int acc_col(int c0, int j, int lane, int e) { return c0 + 8 * j + 2 * (lane & 3) + (e & 1); }
+
+// Sum over the 4 lanes of a quad (same rows) / over the 8 lanes sharing t (same columns).
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+__device__ __forceinline__ float column_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  return v + __shfl_xor_sync(0xffffffffu, v, 16);
+}
+
+// Row sums (rows g, g+8 of the strip) of an accumulator-layout value added into dst[] (shared).
+template <int NT, typename F>
+__device__ __forceinline__ void add_row_sums(float* dst, int rs, int lane, F value) {
+  float lo = 0.f, hi = 0.f;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    lo += value(j, 0) + value(j, 1);
+    hi += value(j, 2) + value(j, 3);
+  }
+  lo = quad_sum(lo);
+  hi = quad_sum(hi);
+  if ((lane & 3) == 0) {
+    atomicAdd(dst + rs + (lane >> 2), lo);
+    atomicAdd(dst + rs + (lane >> 2) + 8, hi);
+  }
+}
+
+__device__ __forceinline__ void store_acc_f32(float* dst, int ld, const float (*acc)[4], int rs, int c0, int nt,
+                                              int lane) {
+  for (int j = 0; j < nt; ++j) {
+    const int col = c0 + 8 * j + 2 * (lane & 3);
+    const int r = rs + (lane >> 2);
+    *reinterpret_cast<float2*>(dst + (size_t)r * ld + col) = make_float2(acc[j][0], acc[j][1]);
+    *reinterpret_cast<float2*>(dst + (size_t)(r + 8) * ld + col) = make_float2(acc[j][2], acc[j][3]);
+  }
+}
+
+__device__ __forceinline__ void store_acc_bf16_tile(__nv_bfloat16* dst, int ld, const float (*acc)[4], int rs, int c0,
+                                                    int nt, int lane, float scale = 1.f) {
+  for (int j = 0; j < nt; ++j) {
+    const int col = c0 + 8 * j + 2 * (lane & 3);
+    const int r = rs + (lane >> 2);
+    *reinterpret_cast<__nv_bfloat162*>(dst + r * ld + col) =
+        __floats2bfloat162_rn(scale * acc[j][0], scale * acc[j][1]);
+    *reinterpret_cast<__nv_bfloat162*>(dst + (r + 8) * ld + col) =
+        __floats2bfloat162_rn(scale * acc[j][2], scale * acc[j][3]);
+  }
+}
+
+__device__ __forceinline__ float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+constexpr size_t PREP_SMEM = (size_t)3 * TILE * 2 + 2 * CH * LDF * 4 + 2 * CH * LD64 * 2 + 5 * CH * 4;
+
+__global__ void __launch_bounds__(THREADS_C, 2) gdn_prep_kernel(PrepArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  __nv_bfloat16* sK = sQ + TILE;
+  __nv_bfloat16* sV = sK + TILE;
+  float* sA = reinterpret_cast<float*>(sV + TILE);
+  float* sT = sA + CH * LDF;
+  __nv_bfloat16* sTw = reinterpret_cast<__nv_bfloat16*>(sT + CH * LDF);
+  __nv_bfloat16* sTv = sTw + CH * LD64;
+  float* sb = reinterpret_cast<float*>(sTv + CH * LD64);
+  float* seb = sb + CH;
+  float* skd = seb + CH;
+  float* sbeta = skd + CH;
+  float* sg = sbeta + CH;
+
+  const int cta = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const size_t tile_off = (size_t)cta * CH * DH;
+  load_tile_async(sQ, a.Q + tile_off, tid);
+  load_tile_async(sK, a.K + tile_off, tid);
+  load_tile_async(sV, a.V + tile_off, tid);
+  cp_commit();
+  if (tid < CH) {
+    sg[tid] = a.G[(size_t)cta * CH + tid];
+    sbeta[tid] = a.B[(size_t)cta * CH + tid];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float bc = chunk_decay(sg, sb, seb, skd, lane);
+    if (lane == 0) a.gamma[cta] = __expf(bc);
+  }
+  cp_wait_all();
+  __syncthreads();
+
+  // KK = K K^T and QK = Q K^T: warp -> rows rs..rs+15, cols cb..cb+31
+  const int rs = 16 * (warp & 3), cb = 32 * (warp >> 2);
+  {
+    float kk[4][4], qk[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < DH; k0 += 16) {
+      uint32_t ak[4], aq[4];
+      frag_a(ak, sK, rs, k0, LD, lane);
+      frag_a(aq, sQ, rs, k0, LD, lane);
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        uint32_t bk[4];
+        frag_bt2(bk, sK, k0, cb + 8 * j, LD, lane);
+        mma16816(kk[j], ak, bk[0], bk[1]);
+        mma16816(kk[j + 1], ak, bk[2], bk[3]);
+        mma16816(qk[j], aq, bk[0], bk[1]);
+        mma16816(qk[j + 1], aq, bk[2], bk[3]);
+      }
+    }
+    __nv_bfloat16* P = a.P + (size_t)cta * CH * CH;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int i = rs + gq + 8 * half;
+        const int c0 = cb + 8 * j + 2 * tq;
+        float av[2], pv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = c0 + e;
+          const float ev = col <= i ? __expf(sb[i] - sb[col]) : 0.f;
+          av[e] = col < i ? sbeta[i] * kk[j][2 * half + e] * ev : 0.f;
+          pv[e] = qk[j][2 * half + e] * ev;
+        }
+        sA[i * LDF + c0] = av[0];
+        sA[i * LDF + c0 + 1] = av[1];
+        *reinterpret_cast<__nv_bfloat162*>(P + i * CH + c0) = __floats2bfloat162_rn(pv[0], pv[1]);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < CH) {
+    unit_lower_inverse(sA, sT, tid);
+  } else {
+    // meanwhile: Qd = e^b Q and Kt = e^{b_C - b} K
+    const size_t off = (size_t)cta * CH * DH;
+    store_tile(a.Qd + off, sQ, seb, tid, CH, THREADS_C - CH);
+    store_tile(a.Kt + off, sK, skd, tid, CH, THREADS_C - CH);
+  }
+  __syncthreads();
+  for (int e = tid; e < CH * CH; e += THREADS_C) {
+    const int i = e >> 6, j = e & 63;
+    const float t = sT[i * LDF + j];
+    sTw[i * LD64 + j] = __float2bfloat16(t * sbeta[j] * seb[j]);
+    sTv[i * LD64 + j] = __float2bfloat16(t * sbeta[j]);
+  }
+  __syncthreads();
+  // W = Tw K, U = Tv V: warp -> rows rs..rs+15, cols cw..cw+63
+  const int cw = 64 * (warp >> 2);
+  float w[8][4], u[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w[j][e] = u[j][e] = 0.f;
+#pragma unroll
+  for (int k0 = 0; k0 < CH; k0 += 16) {
+    uint32_t aw[4], av[4];
+    frag_a(aw, sTw, rs, k0, LD64, lane);
+    frag_a(av, sTv, rs, k0, LD64, lane);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      uint32_t bk[4], bv[4];
+      frag_b2(bk, sK, k0, cw + 8 * j, LD, lane);
+      frag_b2(bv, sV, k0, cw + 8 * j, LD, lane);
+      mma16816(w[j], aw, bk[0], bk[1]);
+      mma16816(w[j + 1], aw, bk[2], bk[3]);
+      mma16816(u[j], av, bv[0], bv[1]);
+      mma16816(u[j + 1], av, bv[2], bv[3]);
+    }
+  }
+  __syncthreads();  // every read of sK / sV is done: stage W in sQ, U in sK
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int col = cw + 8 * j + 2 * tq;
+    *reinterpret_cast<__nv_bfloat162*>(sQ + (rs + gq) * LD + col) = __floats2bfloat162_rn(w[j][0], w[j][1]);
+    *reinterpret_cast<__nv_bfloat162*>(sQ + (rs + gq + 8) * LD + col) = __floats2bfloat162_rn(w[j][2], w[j][3]);
+    *reinterpret_cast<__nv_bfloat162*>(sK + (rs + gq) * LD + col) = __floats2bfloat162_rn(u[j][0], u[j][1]);
+    *reinterpret_cast<__nv_bfloat162*>(sK + (rs + gq + 8) * LD + col) = __floats2bfloat162_rn(u[j][2], u[j][3]);
+  }
+  __syncthreads();
+  store_tile(a.W + tile_off, sQ, nullptr, tid, 0, THREADS_C);
+  store_tile(a.U + tile_off, sK, nullptr, tid, 0, THREADS_C);
+}
+
+// ---- fused chunk backward -------------------------------------------------------------------
+//
+// Given dO, the entering state S and the gradient dS of the leaving state (both fp32 from the
+// recurrence kernels), one CTA computes the chunk's dQ, dK, dV (fp32) and dG, dBeta:
+//   Delta = U - W S          dDelta = P^T dO + Kt dS      (= dU)
+//   dW = -dDelta S^T         dQd = dO S^T        dP = dO Delta^T       dKt = Delta dS^T
+//   dT = dU Vb^T + dW Kw^T   dVb = T^T dU        dKw = T^T dW          dA = -T^T dT T^T
+// and the chain through e^b, E, beta and b = cumsum(g) (dg_i = sum_{j >= i} db_j).
+struct BwdArgs {
+  const __nv_bfloat16* Q;
+  const __nv_bfloat16* K;
+  const __nv_bfloat16* V;
+  const __nv_bfloat16* dO;  // [Nc*H, 64, 128]
+  const float* G;
+  const float* B;
+  const float* S;           // [Nc*H, 128, 128] state entering the chunk
+  const float* dS;          // [Nc*H, 128, 128] gradient of the state leaving the chunk
+  float* dQ;                // [Nc*H, 64, 128]
+  float* dK;
+  float* dV;
+  float* dG;                // [Nc*H, 64]
+  float* dB;
+};
+
+constexpr int LDS = DH + 8;                       // bf16 row of the 128x128 state tiles
+constexpr int STILE = DH * LDS;
+constexpr size_t OFF_Q = 0, OFF_K = OFF_Q + TILE * 2, OFF_V = OFF_K + TILE * 2, OFF_DO = OFF_V + TILE * 2;
+constexpr size_t OFF_W = OFF_DO + TILE * 2, OFF_U = OFF_W + TILE * 2, OFF_DD = OFF_U + TILE * 2;
+constexpr size_t OFF_S = OFF_DD + TILE * 2, OFF_DS = OFF_S + STILE * 2;
+constexpr size_t OFF_T = OFF_DS + STILE * 2, OFF_TB = OFF_T + CH * LDF * 4, OFF_P = OFF_TB + CH * LD64 * 2;
+constexpr size_t OFF_VEC = OFF_P + CH * LD64 * 2;
+constexpr size_t BWD_SMEM = OFF_VEC + 7 * CH * 4 + 16;
+static_assert(BWD_SMEM <= 232448, "chunk backward exceeds the shared memory of one CTA");
+static_assert(CH * LDF * 4 + 2 * CH * LD64 * 2 <= 2 * STILE * 2, "phase-0 scratch must fit in the state tiles");
+
+__global__ void __launch_bounds__(THREADS_C, 1) gdn_chunk_bwd_kernel(BwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_Q);
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_K);
+  __nv_bfloat16* sV = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_V);
+  __nv_bfloat16* sdO = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_DO);
+  __nv_bfloat16* sW = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_W);    // W, later dW
+  __nv_bfloat16* sU = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_U);    // U, later Delta
+  __nv_bfloat16* sdD = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_DD);  // dDelta = dU
+  __nv_bfloat16* sS = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_S);
+  __nv_bfloat16* sdS = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_DS);
+  float* sA = reinterpret_cast<float*>(smem_raw + OFF_S);                     // phase 0 (aliases sS)
+  __nv_bfloat16* sTw = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_DS);  // phase 0 (aliases sdS)
+  __nv_bfloat16* sTv = sTw + CH * LD64;
+  float* sdT = reinterpret_cast<float*>(smem_raw + OFF_S);                    // late phases (aliases sS)
+  float* sX = reinterpret_cast<float*>(smem_raw + OFF_DS);                    // late phases (aliases sdS)
+  float* sT = reinterpret_cast<float*>(smem_raw + OFF_T);
+  __nv_bfloat16* sTb = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_TB);  // bf16 T, later M
+  __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem_raw + OFF_P);    // P, later dP * E
+  float* sb = reinterpret_cast<float*>(smem_raw + OFF_VEC);
+  float* seb = sb + CH;
+  float* skd = seb + CH;
+  float* sbeta = skd + CH;
+  float* sg = sbeta + CH;
+  float* sdb = sg + CH;
+  float* sdbeta = sdb + CH;
+  float* sscal = sdbeta + CH;   // [0] = dgamma, [1] = d b_C from Kt
+
+  const int cta = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const size_t toff = (size_t)cta * CH * DH;
+  load_tile_async(sQ, a.Q + toff, tid);
+  load_tile_async(sK, a.K + toff, tid);
+  load_tile_async(sV, a.V + toff, tid);
+  load_tile_async(sdO, a.dO + toff, tid);
+  cp_commit();
+  if (tid < CH) {
+    sg[tid] = a.G[(size_t)cta * CH + tid];
+    sbeta[tid] = a.B[(size_t)cta * CH + tid];
+    sdb[tid] = 0.f;
+    sdbeta[tid] = 0.f;
+  }
+  if (tid < 2) sscal[tid] = 0.f;
+  __syncthreads();
+  float bc = 0.f;
+  if (warp == 0) bc = chunk_decay(sg, sb, seb, skd, lane);
+  cp_wait_all();
+  __syncthreads();
+  bc = sb[CH - 1];
+  const int rs = 16 * (warp & 3), cb = 32 * (warp >> 2), cw = 64 * (warp >> 2);
+
+  // ---- phase 0: recompute A (-> sA), P (-> sP), T, W, U ----
+  {
+    float kk[4][4], qk[4][4];
+    zero_acc<4>(kk);
+    zero_acc<4>(qk);
+    mm_abt<4>(kk, sK, LD, sK, LD, rs, cb, DH, lane);
+    mm_abt<4>(qk, sQ, LD, sK, LD, rs, cb, DH, lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cb, j, lane, e);
+        const float ev = c <= i ? __expf(sb[i] - sb[c]) : 0.f;
+        sA[i * LDF + c] = c < i ? sbeta[i] * kk[j][e] * ev : 0.f;
+        sP[i * LD64 + c] = __float2bfloat16(qk[j][e] * ev);
+      }
+  }
+  __syncthreads();
+  if (tid < CH) unit_lower_inverse(sA, sT, tid);
+  __syncthreads();
+  for (int e = tid; e < CH * CH; e += THREADS_C) {
+    const int i = e >> 6, j = e & 63;
+    const float t = sT[i * LDF + j];
+    sTb[i * LD64 + j] = __float2bfloat16(t);
+    sTw[i * LD64 + j] = __float2bfloat16(t * sbeta[j] * seb[j]);
+    sTv[i * LD64 + j] = __float2bfloat16(t * sbeta[j]);
+  }
+  __syncthreads();
+  {
+    float w[8][4], u[8][4];
+    zero_acc<8>(w);
+    zero_acc<8>(u);
+    mm_ab<8>(w, sTw, LD64, sK, LD, rs, cw, CH, lane);
+    mm_ab<8>(u, sTv, LD64, sV, LD, rs, cw, CH, lane);
+    store_acc_bf16_tile(sW, LD, w, rs, cw, 8, lane);
+    store_acc_bf16_tile(sU, LD, u, rs, cw, 8, lane);
+  }
+  __syncthreads();  // Tw / Tv / A are dead: the state tiles may be loaded over them
+
+  // ---- phase 1: S, dS -> bf16 tiles; dgamma = <S, dS> ----
+  {
+    const float4* gS = reinterpret_cast<const float4*>(a.S + (size_t)cta * DH * DH);
+    const float4* gdS = reinterpret_cast<const float4*>(a.dS + (size_t)cta * DH * DH);
+    float dg = 0.f;
+#pragma unroll 4
+    for (int i = tid; i < DH * DH / 4; i += THREADS_C) {
+      const float4 x = __ldcs(gS + i), y = __ldcs(gdS + i);
+      dg += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
+      const int r = i >> 5, c = (i & 31) * 4;
+      __nv_bfloat162* ps = reinterpret_cast<__nv_bfloat162*>(sS + r * LDS + c);
+      __nv_bfloat162* pd = reinterpret_cast<__nv_bfloat162*>(sdS + r * LDS + c);
+      ps[0] = __floats2bfloat162_rn(x.x, x.y);
+      ps[1] = __floats2bfloat162_rn(x.z, x.w);
+      pd[0] = __floats2bfloat162_rn(y.x, y.y);
+      pd[1] = __floats2bfloat162_rn(y.z, y.w);
+    }
+    dg = warp_sum(dg);
+    if (lane == 0) atomicAdd(sscal, dg);
+  }
+  __syncthreads();
+
+  // ---- phase 2: Delta (-> sU), dDelta (-> sdD), dQ from dQd ----
+  float dq[8][4];
+  {
+    float x[8][4];
+    zero_acc<8>(x);
+    mm_ab<8>(x, sW, LD, sS, LDS, rs, cw, DH, lane);   // W S
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cw, j, lane, e);
+        x[j][e] = bf(sU + i * LD + c) - x[j][e];
+      }
+    store_acc_bf16_tile(sU, LD, x, rs, cw, 8, lane);   // each thread rewrites only what it read
+    float y[8][4];
+    zero_acc<8>(x);
+    zero_acc<8>(y);
+    mm_atb<8>(x, sP, LD64, sdO, LD, rs, cw, CH, lane);  // P^T dO
+    mm_ab<8>(y, sK, LD, sdS, LDS, rs, cw, DH, lane);     // K dS
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[j][e] += skd[acc_row(rs, lane, e)] * y[j][e];
+    store_acc_bf16_tile(sdD, LD, x, rs, cw, 8, lane);
+    zero_acc<8>(dq);
+    mm_abt<8>(dq, sdO, LD, sS, LDS, rs, cw, DH, lane);  // dQd = dO S^T
+    add_row_sums<8>(sdb, rs, lane, [&](int j, int e) {
+      const int i = acc_row(rs, lane, e), c = acc_col(cw, j, lane, e);
+      return seb[i] * dq[j][e] * bf(sQ + i * LD + c);
+    });
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dq[j][e] *= seb[acc_row(rs, lane, e)];
+  }
+  __syncthreads();
+
+  // ---- phase 3: dW (-> sW), dK from dKt, dP * E (-> sP) with its b-gradient ----
+  float dk[8][4];
+  {
+    float x[8][4];
+    zero_acc<8>(x);
+    mm_abt<8>(x, sdD, LD, sS, LDS, rs, cw, DH, lane);   // dDelta S^T
+    store_acc_bf16_tile(sW, LD, x, rs, cw, 8, lane, -1.f);
+    zero_acc<8>(dk);
+    mm_abt<8>(dk, sU, LD, sdS, LDS, rs, cw, DH, lane);  // dKt = Delta dS^T
+    float rkt_lo = 0.f, rkt_hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cw, j, lane, e);
+        const float v = skd[i] * dk[j][e];
+        (e < 2 ? rkt_lo : rkt_hi) += v * bf(sK + i * LD + c);
+        dk[j][e] = v;
+      }
+    rkt_lo = quad_sum(rkt_lo);
+    rkt_hi = quad_sum(rkt_hi);
+    if ((lane & 3) == 0) {
+      atomicAdd(sdb + rs + (lane >> 2), -rkt_lo);
+      atomicAdd(sdb + rs + (lane >> 2) + 8, -rkt_hi);
+    }
+    float tot = (lane & 3) == 0 ? rkt_lo + rkt_hi : 0.f;
+    tot = warp_sum(tot);
+    if (lane == 0) atomicAdd(sscal + 1, tot);
+
+    float dp[4][4], qk[4][4];
+    zero_acc<4>(dp);
+    zero_acc<4>(qk);
+    mm_abt<4>(dp, sdO, LD, sU, LD, rs, cb, DH, lane);   // dP = dO Delta^T
+    mm_abt<4>(qk, sQ, LD, sK, LD, rs, cb, DH, lane);
+    float row_lo = 0.f, row_hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float col[2] = {0.f, 0.f};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cb, j, lane, e);
+        const float ev = c <= i ? __expf(sb[i] - sb[c]) : 0.f;
+        const float dpm = dp[j][e] * ev;
+        const float t = dpm * qk[j][e];
+        (e < 2 ? row_lo : row_hi) += t;
+        col[e & 1] += t;
+        sP[i * LD64 + c] = __float2bfloat16(dpm);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float v = column_sum(col[h]);
+        if ((lane >> 2) == 0) atomicAdd(sdb + cb + 8 * j + 2 * (lane & 3) + h, -v);
+      }
+    }
+    row_lo = quad_sum(row_lo);
+    row_hi = quad_sum(row_hi);
+    if ((lane & 3) == 0) {
+      atomicAdd(sdb + rs + (lane >> 2), row_lo);
+      atomicAdd(sdb + rs + (lane >> 2) + 8, row_hi);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 4: dQ += dPm K (store), dK += dPm^T Q, dT (-> sdT), dV (store), dK from dKw ----
+  mm_ab<8>(dq, sP, LD64, sK, LD, rs, cw, CH, lane);
+  store_acc_f32(a.dQ + toff, DH, dq, rs, cw, 8, lane);
+  mm_atb<8>(dk, sP, LD64, sQ, LD, rs, cw, CH, lane);
+  {
+    float t1[4][4], t2[4][4];
+    zero_acc<4>(t1);
+    zero_acc<4>(t2);
+    mm_abt<4>(t1, sdD, LD, sV, LD, rs, cb, DH, lane);   // dU V^T
+    mm_abt<4>(t2, sW, LD, sK, LD, rs, cb, DH, lane);    // dW K^T
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cb, j, lane, e);
+        sdT[i * LDF + c] = sbeta[c] * (t1[j][e] + seb[c] * t2[j][e]);
+      }
+  }
+  {
+    float x[8][4];
+    zero_acc<8>(x);
+    mm_atb<8>(x, sTb, LD64, sdD, LD, rs, cw, CH, lane);  // dVb = T^T dU
+    add_row_sums<8>(sdbeta, rs, lane, [&](int j, int e) {
+      return x[j][e] * bf(sV + acc_row(rs, lane, e) * LD + acc_col(cw, j, lane, e));
+    });
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[j][e] *= sbeta[acc_row(rs, lane, e)];
+    store_acc_f32(a.dV + toff, DH, x, rs, cw, 8, lane);
+    zero_acc<8>(x);
+    mm_atb<8>(x, sTb, LD64, sW, LD, rs, cw, CH, lane);   // dKw = T^T dW
+    float sw_lo = 0.f, sw_hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cw, j, lane, e);
+        (e < 2 ? sw_lo : sw_hi) += x[j][e] * bf(sK + i * LD + c);
+        dk[j][e] += x[j][e] * sbeta[i] * seb[i];
+      }
+    sw_lo = quad_sum(sw_lo);
+    sw_hi = quad_sum(sw_hi);
+    if ((lane & 3) == 0) {
+      const int i0 = rs + (lane >> 2), i1 = i0 + 8;
+      atomicAdd(sdbeta + i0, sw_lo * seb[i0]);
+      atomicAdd(sdbeta + i1, sw_hi * seb[i1]);
+      atomicAdd(sdb + i0, sw_lo * seb[i0] * sbeta[i0]);
+      atomicAdd(sdb + i1, sw_hi * seb[i1] * sbeta[i1]);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 5: dA = -T^T (dT T^T), fp32 on CUDA cores, 4x4 outputs per thread ----
+  {
+    const int i0 = 4 * (tid >> 4), j0 = 4 * (tid & 15);
+    float x[4][4] = {};
+    for (int k = 0; k < CH; ++k) {   // X = dT T^T: X[i][j] = sum_k dT[i][k] T[j][k]
+      float l[4], r[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        l[q] = sdT[(i0 + q) * LDF + k];
+        r[q] = sT[(j0 + q) * LDF + k];
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[p][q] += l[p] * r[q];
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sX[(i0 + p) * LDF + j0 + q] = x[p][q];
+  }
+  __syncthreads();
+  {
+    const int i0 = 4 * (tid >> 4), j0 = 4 * (tid & 15);
+    float x[4][4] = {};
+    for (int k = 0; k < CH; ++k) {   // dA[i][j] = -sum_k T[k][i] X[k][j]
+      float l[4], r[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        l[q] = sT[k * LDF + i0 + q];
+        r[q] = sX[k * LDF + j0 + q];
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[p][q] -= l[p] * r[q];
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sdT[(i0 + p) * LDF + j0 + q] = x[p][q];   // dT is dead: reuse for dA
+  }
+  __syncthreads();
+
+  // ---- phase 6: dA through A = beta_i KK E (strict lower): beta, b and M = dKK + dKK^T (-> sTb) ----
+  {
+    float kk[4][4];
+    zero_acc<4>(kk);
+    mm_abt<4>(kk, sK, LD, sK, LD, rs, cb, DH, lane);
+    float row_lo = 0.f, row_hi = 0.f, rb_lo = 0.f, rb_hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float col[2] = {0.f, 0.f};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(rs, lane, e), c = acc_col(cb, j, lane, e);
+        float m = 0.f;
+        if (c < i) {
+          const float ev = __expf(sb[i] - sb[c]);
+          const float da = sdT[i * LDF + c];
+          const float kke = kk[j][e] * ev;
+          const float ta = da * sbeta[i] * kke;
+          (e < 2 ? rb_lo : rb_hi) += da * kke;
+          (e < 2 ? row_lo : row_hi) += ta;
+          col[e & 1] += ta;
+          m = da * ev * sbeta[i];
+          sTb[c * LD64 + i] = __float2bfloat16(m);   // upper mirror
+        } else if (c == i) {
+          sTb[i * LD64 + i] = __float2bfloat16(0.f);
+        }
+        if (c <= i) sTb[i * LD64 + c] = __float2bfloat16(m);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float v = column_sum(col[h]);
+        if ((lane >> 2) == 0) atomicAdd(sdb + cb + 8 * j + 2 * (lane & 3) + h, -v);
+      }
+    }
+    row_lo = quad_sum(row_lo);
+    row_hi = quad_sum(row_hi);
+    rb_lo = quad_sum(rb_lo);
+    rb_hi = quad_sum(rb_hi);
+    if ((lane & 3) == 0) {
+      const int i0 = rs + (lane >> 2);
+      atomicAdd(sdb + i0, row_lo);
+      atomicAdd(sdb + i0 + 8, row_hi);
+      atomicAdd(sdbeta + i0, rb_lo);
+      atomicAdd(sdbeta + i0 + 8, rb_hi);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 7: dK += M K (store); dG = reverse cumsum(db) with db_C += d b_C; dBeta ----
+  mm_ab<8>(dk, sTb, LD64, sK, LD, rs, cw, CH, lane);
+  store_acc_f32(a.dK + toff, DH, dk, rs, cw, 8, lane);
+  if (warp == 0) {
+    const float gamma = __expf(bc);
+    float d0 = sdb[2 * lane], d1 = sdb[2 * lane + 1];
+    if (lane == 31) d1 += sscal[1] + sscal[0] * gamma;
+    // reverse inclusive scan: dg_i = sum_{j >= i} db_j
+    float s = d0 + d1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float v = __shfl_down_sync(0xffffffffu, s, off);
+      if (lane + off < 32) s += v;
+    }
+    const float after = s - (d0 + d1);   // sum over pairs to the right
+    a.dG[(size_t)cta * CH + 2 * lane + 1] = after + d1;
+    a.dG[(size_t)cta * CH + 2 * lane] = after + d1 + d0;
+    a.dB[(size_t)cta * CH + 2 * lane] = sdbeta[2 * lane];
+    a.dB[(size_t)cta * CH + 2 * lane + 1] = sdbeta[2 * lane + 1];
+  }
+}
+
+void check_tile(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.scalar_type() == at::kBFloat16 && t.dim() == 4 &&
+                  t.size(2) == CH && t.size(3) == DH,
+              name, ": contiguous bf16 [Nc, H, 64, 128]");
+}
+
+}  // namespace
+
+// Returns (W, U, P, Qd, Kt, gamma) of every (chunk, head).
+std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor G, at::Tensor B) {
+  check_tile(Q, "Q");
+  check_tile(K, "K");
+  check_tile(V, "V");
+  TORCH_CHECK(K.sizes() == Q.sizes() && V.sizes() == Q.sizes(), "Q, K, V shapes differ");
+  const long Nc = Q.size(0), H = Q.size(1);
+  for (const auto* t : {&G, &B})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat && t->numel() == Nc * H * CH,
+                "G, B: contiguous fp32 [Nc, H, 64]");
+  auto W = at::empty_like(Q), U = at::empty_like(Q), Qd = at::empty_like(Q), Kt = at::empty_like(Q);
+  auto P = at::empty({Nc, H, CH, CH}, Q.options());
+  auto gamma = at::empty({Nc, H}, G.options());
+  if (Nc * H == 0) return {W, U, P, Qd, Kt, gamma};
+  PrepArgs a{(const __nv_bfloat16*)Q.data_ptr(), (const __nv_bfloat16*)K.data_ptr(),
+             (const __nv_bfloat16*)V.data_ptr(), G.data_ptr<float>(), B.data_ptr<float>(),
+             (__nv_bfloat16*)W.data_ptr(), (__nv_bfloat16*)U.data_ptr(), (__nv_bfloat16*)P.data_ptr(),
+             (__nv_bfloat16*)Qd.data_ptr(), (__nv_bfloat16*)Kt.data_ptr(), gamma.data_ptr<float>()};
+  static bool once = [] {
+    CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)PREP_SMEM));
+    return true;
+  }();
+  (void)once;
+  gdn_prep_kernel<<<(unsigned)(Nc * H), THREADS_C, PREP_SMEM, stream()>>>(a);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {W, U, P, Qd, Kt, gamma};
+}
+
+// Returns (dQ, dK, dV fp32 [Nc, H, 64, 128], dG, dBeta fp32 [Nc, H, 64]).
+std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
+                                      at::Tensor B, at::Tensor S, at::Tensor dS) {
+  check_tile(Q, "Q");
+  check_tile(K, "K");
+  check_tile(V, "V");
+  check_tile(dO, "dO");
+  TORCH_CHECK(K.sizes() == Q.sizes() && V.sizes() == Q.sizes() && dO.sizes() == Q.sizes(), "Q, K, V, dO shapes differ");
+  const long Nc = Q.size(0), H = Q.size(1);
+  for (const auto* t : {&G, &B})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat && t->numel() == Nc * H * CH,
+                "G, B: contiguous fp32 [Nc, H, 64]");
+  for (const auto* t : {&S, &dS})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat && t->numel() == Nc * H * DH * DH,
+                "S, dS: contiguous fp32 [Nc, H, 128, 128]");
+  auto f32 = Q.options().dtype(at::kFloat);
+  auto dQ = at::empty({Nc, H, CH, DH}, f32), dK = at::empty({Nc, H, CH, DH}, f32), dV = at::empty({Nc, H, CH, DH}, f32);
+  auto dG = at::empty({Nc, H, CH}, f32), dB = at::empty({Nc, H, CH}, f32);
+  if (Nc * H == 0) return {dQ, dK, dV, dG, dB};
+  BwdArgs a{(const __nv_bfloat16*)Q.data_ptr(), (const __nv_bfloat16*)K.data_ptr(), (const __nv_bfloat16*)V.data_ptr(),
+            (const __nv_bfloat16*)dO.data_ptr(), G.data_ptr<float>(), B.data_ptr<float>(), S.data_ptr<float>(),
+            dS.data_ptr<float>(), dQ.data_ptr<float>(), dK.data_ptr<float>(), dV.data_ptr<float>(),
+            dG.data_ptr<float>(), dB.data_ptr<float>()};
+  static bool once = [] {
+    CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_chunk_bwd_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BWD_SMEM));
+    return true;
+  }();
+  (void)once;
+  gdn_chunk_bwd_kernel<<<(unsigned)(Nc * H), THREADS_C, BWD_SMEM, stream()>>>(a);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {dQ, dK, dV, dG, dB};
+}
+
+}  // namespace cqb

@@ -1,9 +1,11 @@
 """CUDA path of the chunked gated delta rule.
 
-Chunk-local WY factors (parallel over every chunk and head) are batched tensor-core GEMMs and
-a batched triangular solve; the two sequential passes over the chunks of each document, the
-forward state recurrence and the backward state-gradient recurrence, run in the hand-written
-sm_100a kernels of ``csrc/gdn.cu``. Per chunk (cumulative log-decay ``b``, ``E_ij = e^{b_i-b_j}``):
+Chunk-local work (parallel over every chunk and head) runs in ``csrc/gdn_chunk.cu``: the WY
+factors of the forward, and one fused kernel for the whole chunk-local backward. The two
+sequential passes over the chunks of each document, the forward state recurrence and the
+backward state-gradient recurrence, run in ``csrc/gdn.cu``. ``chunk_gather``/``chunk_scatter``
+(``csrc/conv.cu``) move events into the zero-padded chunk layout with the q/k L2 norm fused.
+Per chunk (cumulative log-decay ``b``, ``E_ij = e^{b_i-b_j}``):
 
     A = tril(beta_i E_ij k_i.k_j, -1)     T = (I + A)^-1
     W = T diag(beta e^b) K                U = T diag(beta) V
@@ -123,8 +125,8 @@ class _GatedDelta(torch.autograd.Function):
         K, rk = ops.chunk_gather(k, idx, Nc, True, 1.0)
         V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
         G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
-        f = _factors(Q, K, V, G, B, chunk)
-        O, S = ops.gdn_fwd(f["W"], f["U"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
+        W, U, P, Qd, Kt, gamma = ops.gdn_prep(Q, K, V, G, B)
+        O, S = ops.gdn_fwd(W, U, P, Qd, Kt, gamma, start, count)
         ctx.save_for_backward(q, k, v, g, beta, rq, rk, S)
         ctx.layout, ctx.chunk = layout, chunk
         return ops.chunk_scatter(O, keep, O, O, False, 1.0)
@@ -134,76 +136,85 @@ class _GatedDelta(torch.autograd.Function):
         q, k, v, g, beta, rq, rk, S = ctx.saved_tensors
         idx, pad, keep, start, count, Nc = ctx.layout
         chunk = ctx.chunk
-        bf = torch.bfloat16
         E, H, Dk = q.shape
-        Dv = v.shape[-1]
         ops = _ext.ops()
         Q = ops.chunk_gather(q, idx, Nc, True, Dk ** -0.5)[0]
         K = ops.chunk_gather(k, idx, Nc, True, 1.0)[0]
         V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
-        dO = ops.chunk_gather(dout.to(bf).contiguous(), idx, Nc, False, 1.0)[0]
+        dO = ops.chunk_gather(dout.to(torch.bfloat16).contiguous(), idx, Nc, False, 1.0)[0]
         G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
-        f = _factors(Q, K, V, G, B, chunk)
-        dS = ops.gdn_bwd(dO, f["W"], f["P"], f["Qd"], f["Kt"], f["gamma"], start, count)
-        Sb, dSb = S.to(bf), dS.to(bf)
-        Delta = (f["U"].float() - torch.matmul(f["W"], Sb).float()).to(bf)
-        dDelta = (torch.matmul(f["P"].transpose(-1, -2), dO).float() + torch.matmul(f["Kt"], dSb).float()).to(bf)
-        dW = -torch.matmul(dDelta, Sb.transpose(-1, -2)).float()
-        dQd = torch.matmul(dO, Sb.transpose(-1, -2)).float()
-        dP = torch.matmul(dO, Delta.transpose(-1, -2)).float()
-        dKt = torch.matmul(Delta, dSb.transpose(-1, -2)).float()
-        dgamma = (S * dS).sum((-1, -2))
-        dU = dDelta.float()
-        del Delta, dDelta, Sb, dSb, dS
-        b, eb, kdec = f["b"], f["eb"], f["kdec"]
-        Qf, Kf = Q.float(), K.float()
-        # Qd = e^b Q
-        dQ = dQd * eb[..., None]
-        db = (dQd * f["Qd"].float()).sum(-1)
-        # P = (Q K^T) * E_incl
-        dPm = dP * f["e_incl"]
-        dQ += torch.matmul(dPm.to(bf), K).float()
-        dK = torch.matmul(dPm.transpose(-1, -2).to(bf), Q).float()
-        Pfull = f["QK"] * f["e_incl"]
-        t = dP * Pfull
-        db += t.sum(-1) - t.sum(-2)
-        # Kt = e^{b_C - b} K
-        dK += dKt * kdec[..., None]
-        rkt = (dKt * f["Kt"].float()).sum(-1)
-        db -= rkt
-        dbC = rkt.sum(-1) + dgamma * f["gamma"]
-        # U = T Vb, W = T Kw
-        Tb = f["Tb"]
-        dT = torch.matmul(dU.to(bf), f["Vb"].transpose(-1, -2)).float() + torch.matmul(dW.to(bf), f["Kw"].transpose(-1, -2)).float()
-        dVb = torch.matmul(Tb.transpose(-1, -2), dU.to(bf)).float()
-        dKw = torch.matmul(Tb.transpose(-1, -2), dW.to(bf)).float()
-        dV = dVb * B[..., None]
-        dbeta = (dVb * V.float()).sum(-1)
-        sw = (dKw * Kf).sum(-1)
-        dbeta += sw * eb
-        db += sw * eb * B
-        dK += dKw * (B * eb)[..., None]
-        # T = (I + A)^-1  ->  dA = -T^T dT T^T (strict lower part)
-        T = f["T"]
-        dA = -torch.matmul(torch.matmul(T.transpose(-1, -2), dT), T.transpose(-1, -2))
-        dA = dA * torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(-1)
-        A = f["A"]
-        tA = dA * A
-        dbeta += (dA * f["KK"] * f["e_strict"]).sum(-1)
-        db += tA.sum(-1) - tA.sum(-2)
-        dKK = dA * f["e_strict"] * B[..., :, None]
-        dK += torch.matmul((dKK + dKK.transpose(-1, -2)).to(bf), K).float()
-        # b = cumsum(g) within the chunk: dg_i = sum_{j >= i} db_j ; b_C also feeds gamma/Kt
-        db[..., -1] += dbC
-        dG = db.flip(-1).cumsum(-1).flip(-1)
+        W, U, P, Qd, Kt, gamma = ops.gdn_prep(Q, K, V, G, B)
+        dS = ops.gdn_bwd(dO, W, P, Qd, Kt, gamma, start, count)
+        del W, U, P, Qd, Kt
+        dQ, dK, dV, dG, dB = ops.gdn_chunk_bwd(Q, K, V, dO, G, B, S, dS)
+        del dS
 
         def back(t):
             return t.transpose(1, 2).reshape(Nc * chunk, H).index_select(0, keep)
 
-        dq = ops.chunk_scatter(dQ.contiguous(), keep, q, rq, True, Dk ** -0.5)
-        dk = ops.chunk_scatter(dK.contiguous(), keep, k, rk, True, 1.0)
-        dv = ops.chunk_scatter(dV.contiguous(), keep, v, rk, False, 1.0)
-        return dq, dk, dv, back(dG).to(g.dtype), back(dbeta).to(beta.dtype), None, None
+        dq = ops.chunk_scatter(dQ, keep, q, rq, True, Dk ** -0.5)
+        dk = ops.chunk_scatter(dK, keep, k, rk, True, 1.0)
+        dv = ops.chunk_scatter(dV, keep, v, rk, False, 1.0)
+        return dq, dk, dv, back(dG).to(g.dtype), back(dB).to(beta.dtype), None, None
+
+
+def chunk_backward_reference(Q, K, V, dO, G, B, S, dS, chunk=CHUNK):
+    """PyTorch form of the fused chunk backward (``gdn_chunk_bwd``), used to test the kernel.
+
+    Inputs in chunk layout (``[Nc, H, C, D]`` bf16, ``[Nc, H, C]`` fp32, states fp32); returns
+    ``dQ, dK, dV`` (fp32) and ``dG, dBeta`` of every chunk.
+    """
+    bf = torch.bfloat16
+    f = _factors(Q, K, V, G, B, chunk)
+    Sb, dSb = S.to(bf), dS.to(bf)
+    Delta = (f["U"].float() - torch.matmul(f["W"], Sb).float()).to(bf)
+    dDelta = (torch.matmul(f["P"].transpose(-1, -2), dO).float() + torch.matmul(f["Kt"], dSb).float()).to(bf)
+    dW = -torch.matmul(dDelta, Sb.transpose(-1, -2)).float()
+    dQd = torch.matmul(dO, Sb.transpose(-1, -2)).float()
+    dP = torch.matmul(dO, Delta.transpose(-1, -2)).float()
+    dKt = torch.matmul(Delta, dSb.transpose(-1, -2)).float()
+    dgamma = (S * dS).sum((-1, -2))
+    dU = dDelta.float()
+    eb, kdec = f["eb"], f["kdec"]
+    # Qd = e^b Q
+    dQ = dQd * eb[..., None]
+    db = (dQd * f["Qd"].float()).sum(-1)
+    # P = (Q K^T) * E_incl
+    dPm = dP * f["e_incl"]
+    dQ += torch.matmul(dPm.to(bf), K).float()
+    dK = torch.matmul(dPm.transpose(-1, -2).to(bf), Q).float()
+    t = dP * (f["QK"] * f["e_incl"])
+    db += t.sum(-1) - t.sum(-2)
+    # Kt = e^{b_C - b} K
+    dK += dKt * kdec[..., None]
+    rkt = (dKt * f["Kt"].float()).sum(-1)
+    db -= rkt
+    dbC = rkt.sum(-1) + dgamma * f["gamma"]
+    # U = T Vb, W = T Kw
+    Tb = f["Tb"]
+    dT = (torch.matmul(dU.to(bf), f["Vb"].transpose(-1, -2)).float()
+          + torch.matmul(dW.to(bf), f["Kw"].transpose(-1, -2)).float())
+    dVb = torch.matmul(Tb.transpose(-1, -2), dU.to(bf)).float()
+    dKw = torch.matmul(Tb.transpose(-1, -2), dW.to(bf)).float()
+    dV = dVb * B[..., None]
+    dbeta = (dVb * V.float()).sum(-1)
+    sw = (dKw * K.float()).sum(-1)
+    dbeta += sw * eb
+    db += sw * eb * B
+    dK += dKw * (B * eb)[..., None]
+    # T = (I + A)^-1  ->  dA = -T^T dT T^T (strict lower part)
+    T = f["T"]
+    dA = -torch.matmul(torch.matmul(T.transpose(-1, -2), dT), T.transpose(-1, -2))
+    dA = dA * torch.ones(chunk, chunk, dtype=torch.bool, device=Q.device).tril(-1)
+    tA = dA * f["A"]
+    dbeta += (dA * f["KK"] * f["e_strict"]).sum(-1)
+    db += tA.sum(-1) - tA.sum(-2)
+    dKK = dA * f["e_strict"] * B[..., :, None]
+    dK += torch.matmul((dKK + dKK.transpose(-1, -2)).to(bf), K).float()
+    # b = cumsum(g) within the chunk: dg_i = sum_{j >= i} db_j ; b_C also feeds gamma and Kt
+    db[..., -1] += dbC
+    dG = db.flip(-1).cumsum(-1).flip(-1)
+    return dQ, dK, dV, dG, dbeta
 
 
 def _to_chunks(tensors, idx, pad, Nc, chunk, H):

@@ -44,3 +44,52 @@ def test_gdn_forward_backward(bounds):
     for name, a, b in zip("qkvgb", args, ref_args):
         rel = (a.grad.double() - b.grad).norm() / b.grad.norm().clamp_min(1e-12)
         assert rel < 5e-2, (name, rel.item())
+
+
+def test_gdn_prep_matches_factors():
+    """Fused chunk-local factors (csrc/gdn_chunk.cu) vs the PyTorch chunk algebra."""
+    from cq_pretrain_b200.ops.gdn_cuda import _factors
+    assert _ext.has("gdn_prep")
+    torch.manual_seed(3)
+    Nc, H = 7, 3
+    Q = torch.nn.functional.normalize(torch.randn(Nc, H, 64, 128, device="cuda"), dim=-1) * 128 ** -0.5
+    K = torch.nn.functional.normalize(torch.randn(Nc, H, 64, 128, device="cuda"), dim=-1)
+    V = torch.randn(Nc, H, 64, 128, device="cuda")
+    G = -torch.rand(Nc, H, 64, device="cuda") * 0.3
+    B = torch.rand(Nc, H, 64, device="cuda")
+    K[:, :, 50:] = 0   # padded tail slots of a document's last chunk
+    G[:, :, 50:] = 0
+    B[:, :, 50:] = 0
+    Q, K, V = (t.to(torch.bfloat16).contiguous() for t in (Q, K, V))
+    W, U, P, Qd, Kt, gamma = _ext.ops().gdn_prep(Q, K, V, G.contiguous(), B.contiguous())
+    f = _factors(Q, K, V, G, B, 64)
+    for name, got in (("W", W), ("U", U), ("P", P), ("Qd", Qd), ("Kt", Kt), ("gamma", gamma)):
+        want = f[name].float()
+        rel = (got.float() - want).norm() / want.norm().clamp_min(1e-12)
+        assert rel < 1.5e-2, (name, rel.item())
+
+
+def test_gdn_chunk_backward_matches_reference():
+    """Fused chunk backward (csrc/gdn_chunk.cu) vs its PyTorch form on random states."""
+    from cq_pretrain_b200.ops.gdn_cuda import chunk_backward_reference
+    assert _ext.has("gdn_chunk_bwd")
+    torch.manual_seed(4)
+    Nc, H = 5, 2
+    Q = torch.nn.functional.normalize(torch.randn(Nc, H, 64, 128, device="cuda"), dim=-1) * 128 ** -0.5
+    K = torch.nn.functional.normalize(torch.randn(Nc, H, 64, 128, device="cuda"), dim=-1)
+    V = torch.randn(Nc, H, 64, 128, device="cuda")
+    dO = torch.randn(Nc, H, 64, 128, device="cuda")
+    G = -torch.rand(Nc, H, 64, device="cuda") * 0.3
+    B = torch.rand(Nc, H, 64, device="cuda")
+    K[-1, :, 40:] = 0
+    V[-1, :, 40:] = 0
+    G[-1, :, 40:] = 0
+    B[-1, :, 40:] = 0
+    S = torch.randn(Nc, H, 128, 128, device="cuda") * 0.5
+    dS = torch.randn(Nc, H, 128, 128, device="cuda") * 0.5
+    Q, K, V, dO = (t.to(torch.bfloat16).contiguous() for t in (Q, K, V, dO))
+    got = _ext.ops().gdn_chunk_bwd(Q, K, V, dO, G.contiguous(), B.contiguous(), S, dS)
+    want = chunk_backward_reference(Q, K, V, dO, G, B, S, dS)
+    for name, a, b in zip(("dQ", "dK", "dV", "dG", "dBeta"), got, want):
+        rel = (a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)
+        assert rel < 2e-2, (name, rel.item())
