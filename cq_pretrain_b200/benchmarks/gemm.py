@@ -1,12 +1,15 @@
 """GEMM microbenchmark: the tcgen05 kernels vs cuBLAS (torch.matmul) on the model's shapes.
 
-``python -m cq_pretrain_b200.benchmarks.gemm`` prints one JSON line per shape with CUDA-event
-times (median of 20 after 5 warm-ups, operands larger than L2 rotate between iterations) and
-TFLOP/s for: forward ``x W^T``, input gradient ``dY W`` and fp32 weight-gradient accumulation.
+``python -m cq_pretrain_b200.benchmarks.gemm [--shapes M,N,K ...] [--only fwd|dgrad|wgrad]``
+prints one JSON line per shape with CUDA-event times (median of 20 after 5 warm-ups) and
+TFLOP/s for: forward ``x W^T``, input gradient ``dY W`` and fp32 weight-gradient accumulation,
+next to cuBLAS (``torch.matmul``) on the same operands. ``--iters 1 --warmup 1`` gives the
+small single-launch case used for ncu captures.
 """
 
 from __future__ import annotations
 
+import argparse
 import json
 import statistics
 
@@ -36,20 +39,31 @@ def timed(fn, iters=20, warmup=5):
 
 
 def main():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--shapes", nargs="+", default=None, help="M,N,K triples")
+    parser.add_argument("--only", choices=("fwd", "dgrad", "wgrad"), default=None)
+    parser.add_argument("--iters", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--no-cublas", action="store_true")
+    args = parser.parse_args()
+    shapes = [tuple(int(v) for v in s.split(",")) for s in args.shapes] if args.shapes else SHAPES
     ops = _ext.ops()
-    for m, n, k in SHAPES:
+    kinds = [args.only] if args.only else ["fwd", "dgrad", "wgrad"]
+    for m, n, k in shapes:
         x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16)
         dy = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
         acc = torch.zeros(n, k, device="cuda", dtype=torch.float32)
         flops = 2.0 * m * n * k
         row = dict(m=m, n=n, k=k)
-        row["fwd_ours_ms"] = timed(lambda: ops.gemm_nt(x, w, None))
-        row["fwd_cublas_ms"] = timed(lambda: x @ w.T)
-        row["dgrad_ours_ms"] = timed(lambda: ops.gemm_nn(dy, w))
-        row["dgrad_cublas_ms"] = timed(lambda: dy @ w)
-        row["wgrad_ours_ms"] = timed(lambda: ops.gemm_tn_acc(dy, x, acc))
-        row["wgrad_cublas_ms"] = timed(lambda: acc.add_(torch.mm(dy.T, x, out_dtype=torch.float32)))
+        ours = dict(fwd=lambda: ops.gemm_nt(x, w, None), dgrad=lambda: ops.gemm_nn(dy, w),
+                    wgrad=lambda: ops.gemm_tn_acc(dy, x, acc))
+        cublas = dict(fwd=lambda: x @ w.T, dgrad=lambda: dy @ w,
+                      wgrad=lambda: acc.add_(torch.mm(dy.T, x, out_dtype=torch.float32)))
+        for kind in kinds:
+            row[f"{kind}_ours_ms"] = timed(ours[kind], args.iters, args.warmup)
+            if not args.no_cublas:
+                row[f"{kind}_cublas_ms"] = timed(cublas[kind], args.iters, args.warmup)
         for key in list(row):
             if key.endswith("_ms"):
                 row[key.replace("_ms", "_tflops")] = round(flops / row[key] / 1e9, 1)

@@ -83,25 +83,66 @@ __device__ __forceinline__ float chunk_decay(const float* g, float* b, float* eb
   return bc;
 }
 
-// T = (I + A)^-1 for strictly lower-triangular A (fp32, ld LDF): thread c < 64 owns column c.
-// T[i][c] = -sum_{j=c}^{i-1} A[i][j] T[j][c]; every lane of a warp runs inner loops of equal length.
-__device__ __forceinline__ void unit_lower_inverse(const float* A, float* T, int c) {
-  for (int i = 0; i < c; ++i) T[i * LDF + c] = 0.f;
-  T[c * LDF + c] = 1.f;
-  for (int i = c + 1; i < CH; ++i) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int j = c;
-    for (; j + 3 < i; j += 4) {
-      s0 += A[i * LDF + j] * T[j * LDF + c];
-      s1 += A[i * LDF + j + 1] * T[(j + 1) * LDF + c];
-      s2 += A[i * LDF + j + 2] * T[(j + 2) * LDF + c];
-      s3 += A[i * LDF + j + 3] * T[(j + 3) * LDF + c];
+// T = (I + A)^-1 for strictly lower-triangular A (fp32, ld LDF), by 16x16 blocks; every thread of
+// the CTA calls it (it synchronises). Step 1: warps 0-3 invert the diagonal blocks D_k = I + A_kk
+// by forward substitution (lane c owns column c, unrolled over rows) while warps 4-7 clear the
+// upper blocks. Step 2, block rows bi = 1..3 in turn: Y_j = sum_{k=j}^{bi-1} A_{bi,k} T_{k,j},
+// then T_{bi,j} = -D_bi^-1 Y_j; two warps share each block (8 rows each, 4 columns per lane).
+// `scratch` holds 3 x 16 x 17 floats.
+__device__ void unit_lower_inverse(const float* A, float* T, float* scratch, int warp, int lane) {
+  if (warp < 4) {
+    const int k0 = 16 * warp, c = lane & 15;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) s += A[(k0 + r) * LDF + k0 + j] * x[j];
+      x[r] = r < c ? 0.f : (r == c ? 1.f : -s);
     }
-    for (; j < i; ++j) s0 += A[i * LDF + j] * T[j * LDF + c];
-    T[i * LDF + c] = -((s0 + s1) + (s2 + s3));
+    if (lane < 16)
+#pragma unroll
+      for (int r = 0; r < 16; ++r) T[(k0 + r) * LDF + k0 + c] = x[r];
+  } else {
+    for (int e = (warp - 4) * 32 + lane; e < 6 * 256; e += 128) {
+      const int blk = e >> 8, w = e & 255;   // upper blocks (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
+      const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+      const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+      T[(16 * bi + (w >> 4)) * LDF + 16 * bj + (w & 15)] = 0.f;
+    }
+  }
+  __syncthreads();
+  const int bj = warp >> 1, r = 8 * (warp & 1) + (lane >> 2), c0 = 4 * (lane & 3);
+  for (int bi = 1; bi < 4; ++bi) {
+    const bool active = bj < bi;
+    if (active) {
+      float y[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int k = bj; k < bi; ++k) {
+#pragma unroll 4
+        for (int m = 0; m < 16; ++m) {
+          const float av = A[(16 * bi + r) * LDF + 16 * k + m];
+          const float* tr = T + (16 * k + m) * LDF + 16 * bj + c0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) y[q] += av * tr[q];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) scratch[(bj * 16 + r) * 17 + c0 + q] = y[q];
+    }
+    __syncthreads();
+    if (active) {
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int m = 0; m <= r; ++m) {
+        const float dv = T[(16 * bi + r) * LDF + 16 * bi + m];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) t[q] += dv * scratch[(bj * 16 + m) * 17 + c0 + q];
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) T[(16 * bi + r) * LDF + 16 * bj + c0 + q] = -t[q];
+    }
+    __syncthreads();
   }
 }
-
 
 // ---- warp-tile products: acc[NT][4] (rows rs..rs+15, n-tiles c0 + 8j) += A x B over kdim ----
 // A row-major [m][k] (lda), B row-major [k][n] (ldb)
@@ -218,7 +259,7 @@ __device__ __forceinline__ void store_acc_bf16_tile(__nv_bfloat16* dst, int ld, 
 
 __device__ __forceinline__ float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-constexpr size_t PREP_SMEM = (size_t)3 * TILE * 2 + 2 * CH * LDF * 4 + 2 * CH * LD64 * 2 + 5 * CH * 4;
+constexpr size_t PREP_SMEM = (size_t)3 * TILE * 2 + 2 * CH * LDF * 4 + 2 * CH * LD64 * 2 + 5 * CH * 4 + 3 * 16 * 17 * 4;
 
 __global__ void __launch_bounds__(THREADS_C, 2) gdn_prep_kernel(PrepArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -234,6 +275,7 @@ __global__ void __launch_bounds__(THREADS_C, 2) gdn_prep_kernel(PrepArgs a) {
   float* skd = seb + CH;
   float* sbeta = skd + CH;
   float* sg = sbeta + CH;
+  float* sY = sg + CH;   // inverse scratch, 3 x 16 x 17
 
   const int cta = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
@@ -298,16 +340,11 @@ __global__ void __launch_bounds__(THREADS_C, 2) gdn_prep_kernel(PrepArgs a) {
       }
     }
   }
+  // Qd = e^b Q and Kt = e^{b_C - b} K (the decay vectors are ready since the first barrier)
+  store_tile(a.Qd + tile_off, sQ, seb, tid, 0, THREADS_C);
+  store_tile(a.Kt + tile_off, sK, skd, tid, 0, THREADS_C);
   __syncthreads();
-  if (tid < CH) {
-    unit_lower_inverse(sA, sT, tid);
-  } else {
-    // meanwhile: Qd = e^b Q and Kt = e^{b_C - b} K
-    const size_t off = (size_t)cta * CH * DH;
-    store_tile(a.Qd + off, sQ, seb, tid, CH, THREADS_C - CH);
-    store_tile(a.Kt + off, sK, skd, tid, CH, THREADS_C - CH);
-  }
-  __syncthreads();
+  unit_lower_inverse(sA, sT, sY, warp, lane);
   for (int e = tid; e < CH * CH; e += THREADS_C) {
     const int i = e >> 6, j = e & 63;
     const float t = sT[i * LDF + j];
@@ -385,7 +422,8 @@ constexpr size_t OFF_T = OFF_DS + STILE * 2, OFF_TB = OFF_T + CH * LDF * 4, OFF_
 constexpr size_t OFF_VEC = OFF_P + CH * LD64 * 2;
 constexpr size_t BWD_SMEM = OFF_VEC + 7 * CH * 4 + 16;
 static_assert(BWD_SMEM <= 232448, "chunk backward exceeds the shared memory of one CTA");
-static_assert(CH * LDF * 4 + 2 * CH * LD64 * 2 <= 2 * STILE * 2, "phase-0 scratch must fit in the state tiles");
+static_assert(CH * LDF * 4 <= STILE * 2 && 2 * CH * LD64 * 2 + 3 * 16 * 17 * 4 <= STILE * 2,
+              "phase-0 scratch must fit in the state tiles");
 
 __global__ void __launch_bounds__(THREADS_C, 1) gdn_chunk_bwd_kernel(BwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -455,8 +493,7 @@ __global__ void __launch_bounds__(THREADS_C, 1) gdn_chunk_bwd_kernel(BwdArgs a) 
       }
   }
   __syncthreads();
-  if (tid < CH) unit_lower_inverse(sA, sT, tid);
-  __syncthreads();
+  unit_lower_inverse(sA, sT, reinterpret_cast<float*>(sTv + CH * LD64), warp, lane);
   for (int e = tid; e < CH * CH; e += THREADS_C) {
     const int i = e >> 6, j = e & 63;
     const float t = sT[i * LDF + j];
@@ -651,11 +688,12 @@ __global__ void __launch_bounds__(THREADS_C, 1) gdn_chunk_bwd_kernel(BwdArgs a) 
   }
   __syncthreads();
 
-  // ---- phase 5: dA = -T^T (dT T^T), fp32 on CUDA cores, 4x4 outputs per thread ----
+  // ---- phase 5: dA = -T^T (dT T^T), fp32 on CUDA cores, 4x4 outputs per thread. T is lower
+  // triangular, so X[i][j] sums k <= j and dA[i][j] sums k >= i; each warp shares its bound. ----
   {
-    const int i0 = 4 * (tid >> 4), j0 = 4 * (tid & 15);
+    const int i0 = 4 * (tid & 15), j0 = 4 * (tid >> 4);
     float x[4][4] = {};
-    for (int k = 0; k < CH; ++k) {   // X = dT T^T: X[i][j] = sum_k dT[i][k] T[j][k]
+    for (int k = 0; k < j0 + 4; ++k) {   // X = dT T^T: X[i][j] = sum_k dT[i][k] T[j][k]
       float l[4], r[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -676,7 +714,7 @@ __global__ void __launch_bounds__(THREADS_C, 1) gdn_chunk_bwd_kernel(BwdArgs a) 
   {
     const int i0 = 4 * (tid >> 4), j0 = 4 * (tid & 15);
     float x[4][4] = {};
-    for (int k = 0; k < CH; ++k) {   // dA[i][j] = -sum_k T[k][i] X[k][j]
+    for (int k = i0; k < CH; ++k) {   // dA[i][j] = -sum_k T[k][i] X[k][j]
       float l[4], r[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {

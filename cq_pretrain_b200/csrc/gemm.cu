@@ -59,6 +59,7 @@ struct GemmArgs {
   const long long* ready;     // this rank's flag area: ready[s] >= epoch when rank s published
   long long* chunk_flags;     // [M / BM] per-block publication flags (local)
   long long epoch;
+  int group_m;                // tile raster: groups of group_m row blocks sweep all column blocks
 };
 
 __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
@@ -94,11 +95,20 @@ __device__ __forceinline__ bool wait_flag(const long long* flag, long long targe
   return true;
 }
 
-// Tile order: m fastest; with GATHER the m index is rotated so this rank's own rows come first.
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int rotate, int& m0, int& n0) {
-  const int mi = (t % tiles_m + rotate) % tiles_m;
+// Tile order: groups of `group_m` row blocks; inside a group m is fastest and the group sweeps
+// every column block before the next group starts, so the CTAs in flight share a few A row
+// blocks and B column blocks that stay in L2 (an m-fastest order over all rows re-reads A from
+// DRAM once per column block when A exceeds L2). With GATHER the m index is rotated so this
+// rank's own rows come first.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int rotate, int& m0,
+                                            int& n0) {
+  const int per_group = group_m * tiles_n;
+  const int first = (t / per_group) * group_m;
+  const int rows = min(group_m, tiles_m - first);
+  const int r = t % per_group;
+  const int mi = (first + r % rows + rotate) % tiles_m;
   m0 = mi * BM;
-  n0 = (t / tiles_m) * BN;
+  n0 = (r / rows) * BN;
 }
 
 template <bool A_MN, bool B_MN, int EPI, bool GATHER>
@@ -152,7 +162,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int m0, n0;
-        tile_coords(t, tiles_m, rotate, m0, n0);
+        tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
         if (GATHER) {
           if (!wait_flag<false>(args.chunk_flags + m0 / BM, args.epoch, status, abort_flag, 5)) {
             ok = false;
@@ -253,7 +263,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       if (!tc::mbar_wait(&tfull[buf], use, status, abort_flag, 4)) break;
       tc::fence_after();
       int m0, n0;
-      tile_coords(t, tiles_m, rotate, m0, n0);
+      tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
       const uint32_t base = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += EPI_BOX, ++chunk) {
@@ -419,7 +429,11 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
   std::call_once(once, [&] {
     CQB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   });
-  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  const int tiles_m = (args.M + BM - 1) / BM;
+  const int tiles = tiles_m * ((args.N + BN - 1) / BN);
+  // Row-block group: the group's A blocks (BM x K bf16 each) should fill about 48 MB of L2.
+  const long long a_block = (long long)BM * args.K * 2;
+  args.group_m = (int)std::max(1LL, std::min<long long>(tiles_m, (48LL << 20) / std::max(1LL, a_block)));
   // GATHER needs every CTA resident (copy blocks are handed out by CTA index): one per SM.
   const int grid = std::max(1, std::min(tiles, sm_count()));
   kernel<<<grid, GATHER ? 256 : 192, SMEM_BYTES, stream()>>>(ma, mb, mo, args, status_word());

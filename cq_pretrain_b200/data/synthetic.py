@@ -122,9 +122,29 @@ def tiny_pack_documents(cfg, length=512, seed=0, images=2, grid=(1, 16, 16), lat
 
 def synthetic_batch(cfg, length=512, seed=0, kind="tiny", pad_multiple=1, **kwargs):
     """One packed, planned batch (host memory) of a BASELINE configuration shape."""
-    maker = dict(tiny=tiny_pack_documents, joint=joint_pack_documents, video=video_pack_documents)[kind]
+    maker = dict(tiny=tiny_pack_documents, joint=joint_pack_documents, video=video_pack_documents,
+                 gdn=gdn_pack_documents)[kind]
     docs = maker(cfg, length, seed=seed, **kwargs)
     packer = Packer(ListDocuments(docs, dict(snapshot="synthetic", seed=seed, epoch=0, rank=0)), cfg, length,
                     row_multiple=pad_multiple)
     batch, receipt = packer.next()
     return batch, receipt
+
+
+def gdn_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), doc_length=1024, caption=32):
+    """BASELINE config 3 (GDN layer microbenchmark): T2I captions, then text documents of
+    ``doc_length`` tokens (a packed document boundary every 1024 tokens) up to ``length``."""
+    rng = np.random.default_rng(seed)
+    docs = []
+    for i in range(images):
+        docs.append(dict(id=f"gdn-vis-{seed}-{i}", direction="T2I", format="caption",
+                         elements=[dict(type="text", input_ids=text_ids(rng, caption, cfg.vocab_size)),
+                                   visual_element(cfg, rng, grid, (16, 1, 8, 8))]))
+    used = images * (caption + grid[0] * (grid[1] // 2) * (grid[2] // 2) + 4)
+    k = 0
+    while used < length:
+        n = max(1, min(doc_length - 2, length - used - 2))
+        docs.append(dict(id=f"gdn-text-{seed}-{k}", elements=[dict(type="text", input_ids=text_ids(rng, n, cfg.vocab_size))]))
+        used += n + 2
+        k += 1
+    return docs

@@ -55,7 +55,14 @@ def matmul_nn(a, b):
 
 
 def matmul_tn(a, b):
-    """``a^T @ b`` with a ``[M, N]``, b ``[M, K]`` -> ``[N, K]`` (the weight-gradient product), fp32."""
+    """``a^T @ b`` with a ``[M, N]``, b ``[M, K]`` -> ``[N, K]`` (the weight-gradient product), fp32.
+
+    On CUDA this is the tcgen05 TN kernel accumulating into a zeroed fp32 buffer (an fp32 copy of
+    the operands would run on CUDA cores, an order of magnitude slower).
+    """
+    if a.is_cuda and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16:
+        out = torch.zeros(a.shape[1], b.shape[1], dtype=torch.float32, device=a.device)
+        return matmul_tn_accumulate(a, b, out)
     return a.float().T @ b.float()
 
 
