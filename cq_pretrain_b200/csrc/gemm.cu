@@ -29,6 +29,7 @@ namespace cqb {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int GATHER_SUB = 16;   // rows per all-gather copy unit (and per publication flag)
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_BOX = 32;                                   // 32 x 32 output box per warp store
 constexpr int STAGING_BYTES = 4 /*warps*/ * 2 /*buffers*/ * EPI_BOX * EPI_BOX * 4;  // sized for fp32
@@ -57,7 +58,7 @@ struct GemmArgs {
   const __nv_bfloat16* const* peer_in;
   __nv_bfloat16* a_local;
   const long long* ready;     // this rank's flag area: ready[s] >= epoch when rank s published
-  long long* chunk_flags;     // [M / BM] per-block publication flags (local)
+  long long* chunk_flags;     // [M / 16] per-sub-chunk publication flags (local)
   long long epoch;
   int group_m;                // tile raster: groups of group_m row blocks sweep all column blocks
 };
@@ -164,10 +165,10 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         int m0, n0;
         tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
         if (GATHER) {
-          if (!wait_flag<false>(args.chunk_flags + m0 / BM, args.epoch, status, abort_flag, 5)) {
-            ok = false;
-            break;
-          }
+          // the row block is ready once all of its 16-row sub-chunks are published
+          for (int j = 0; j < BM / GATHER_SUB && ok; ++j)
+            ok = wait_flag<false>(args.chunk_flags + m0 / GATHER_SUB + j, args.epoch, status, abort_flag, 5);
+          if (!ok) break;
           fence_proxy_async_global();
         }
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -326,21 +327,24 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     if (EPI != 2 && lane == 0) tc::bulk_wait_all();
     __syncwarp();
   } else if (GATHER) {
-    // Copy warps 6..7: pull 128-row blocks of A (own rows first) into the local gather buffer.
+    // Copy warps 6..7 of every CTA pull 16-row sub-chunks of A into the local gather buffer,
+    // in tile order (this rank's rows first), and publish each sub-chunk with the call's epoch.
+    // Spreading sub-chunks over all CTAs keeps ~16 KB of NVLink loads in flight per SM.
     const int ct = threadIdx.x - 192;  // 0..63
-    const int blocks = args.M / BM;
-    const int per_rank = args.rows_per_rank / BM;
-    for (int i = blockIdx.x; i < blocks; i += gridDim.x) {
-      const int blk = (i + rotate) % blocks;
-      const int s = blk / per_rank;
-      const int lrow = blk * BM - s * args.rows_per_rank;
+    const int subs = args.M / GATHER_SUB;
+    const int rot = rotate * (BM / GATHER_SUB);
+    for (int i = blockIdx.x; i < subs; i += gridDim.x) {
+      const int sub = (i + rot) % subs;
+      const int row0 = sub * GATHER_SUB;
+      const int s = row0 / args.rows_per_rank;
+      const int lrow = row0 - s * args.rows_per_rank;
       bool ok = true;
       if (ct == 0 && s != args.src_rank) ok = wait_flag<true>(args.ready + s, args.epoch, status, abort_flag, 6);
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (*abort_flag || !ok) break;
       const uint4* src = reinterpret_cast<const uint4*>(args.peer_in[s] + (size_t)lrow * args.K);
-      uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)blk * BM * args.K);
-      const int vecs = BM * args.K / 8;
+      uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)row0 * args.K);
+      const int vecs = GATHER_SUB * args.K / 8;
       // 16 independent 16-byte loads in flight per thread: NVLink latency is hidden by
       // memory-level parallelism rather than by occupancy.
       constexpr int UNROLL = 16;
@@ -356,7 +360,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       fence_proxy_async_global();
       __threadfence();
       asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (ct == 0) st_release_gpu(args.chunk_flags + blk, args.epoch);
+      if (ct == 0) st_release_gpu(args.chunk_flags + sub, args.epoch);
     }
   }
   __syncthreads();
@@ -434,6 +438,9 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
   // Row-block group: the group's A blocks (BM x K bf16 each) should fill about 48 MB of L2.
   const long long a_block = (long long)BM * args.K * 2;
   args.group_m = (int)std::max(1LL, std::min<long long>(tiles_m, (48LL << 20) / std::max(1LL, a_block)));
+  // All-gather: tiles follow the ranks' row ranges (own rows first), so the first tiles need no
+  // peer data and the copy of the other ranks' rows overlaps them.
+  if (GATHER) args.group_m = std::min(args.group_m, std::max(1, args.rows_per_rank / BM));
   // GATHER needs every CTA resident (copy blocks are handed out by CTA index): one per SM.
   const int grid = std::max(1, std::min(tiles, sm_count()));
   kernel<<<grid, GATHER ? 256 : 192, SMEM_BYTES, stream()>>>(ma, mb, mo, args, status_word());
@@ -528,7 +535,8 @@ at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tenso
   const int64_t M = a_local.size(0), K = a_local.size(1), N = w.size(0);
   check_dims(M, N, K);
   TORCH_CHECK(rows_per_rank % BM == 0 && M == rows_per_rank * tp, "rows per rank must be a multiple of 128");
-  TORCH_CHECK(chunk_flags.scalar_type() == at::kLong && chunk_flags.numel() >= M / BM, "chunk flags too small");
+  TORCH_CHECK(chunk_flags.scalar_type() == at::kLong && chunk_flags.numel() >= M / GATHER_SUB,
+              "chunk flags too small: one per 16 rows");
   auto y = at::empty({M, N}, a_local.options());
   auto ma = make_map(a_local, BM);
   auto mb = make_map(w, BN);

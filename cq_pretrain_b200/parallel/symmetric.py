@@ -40,7 +40,7 @@ def _align(n, a=4096):
 
 
 class SymmetricWorkspace:
-    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_blocks=4096):
+    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192):
         st = ps.state()
         if st.tp < 2:
             raise ValueError("symmetric workspace needs TP >= 2")
@@ -67,7 +67,8 @@ class SymmetricWorkspace:
         self.flag_rs = as_dev([b + 512 for b in bases])
         self.send = [as_dev([b + self.off_send[p] for b in bases]) for p in range(2)]
         self.recv = [as_dev([b + self.off_recv[p] for b in bases]) for p in range(2)]
-        self.chunk_flags = torch.zeros(max_blocks, dtype=torch.int64, device=dev)
+        # one publication flag per 16 gathered rows (the all-gather copy unit)
+        self.chunk_flags = torch.zeros(max_subchunks, dtype=torch.int64, device=dev)
         self.epoch_ag = 0
         self.epoch_rs = 0
         dist.barrier(group=self.group)
@@ -87,7 +88,7 @@ class SymmetricWorkspace:
 
     def _gather_ok(self, x):
         rows = x.shape[0] * self.tp
-        return (x.shape[0] % 128 == 0 and x.numel() * 2 <= self.send_bytes and rows // 128 <= self.chunk_flags.numel())
+        return (x.shape[0] % 128 == 0 and x.numel() * 2 <= self.send_bytes and rows // 16 <= self.chunk_flags.numel())
 
     # ---- fused ops --------------------------------------------------------------------------------
     def gather_linear(self, x, weight, bias=None):

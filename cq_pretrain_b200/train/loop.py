@@ -24,6 +24,7 @@ import torch
 import torch.distributed as dist
 
 from ..config import RunConfig, load_sections
+from ..data.device import DeviceLoader
 from ..parallel import state as ps
 from . import catalog
 from . import checkpoint as ckpt
@@ -91,9 +92,11 @@ def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/
         if path:
             start_step = ckpt.load(path, trainer.model, trainer.optimizer, cfg, training_state, data_state, trainer.ema)
             trainer.step_index = start_step
-    loader = make_loader(cfg, length, synthetic, int(training.get("seed", 871)), st.dp_rank, dp,
-                         state=data_state.get("ranks", {}).get(str(st.dp_rank)), corpus=corpus,
-                         row_multiple=128 * tp)
+    host_loader = make_loader(cfg, length, synthetic, int(training.get("seed", 871)), st.dp_rank, dp,
+                              state=data_state.get("ranks", {}).get(str(st.dp_rank)), corpus=corpus,
+                              row_multiple=128 * tp)
+    # packs are copied to the GPU on a side stream ahead of their step; the cursor stays acknowledged-only
+    loader = DeviceLoader(host_loader, trainer.preparer, prefetch=int(training.get("device_prefetch", 2)))
     if rank0:
         output.mkdir(parents=True, exist_ok=True)
         from ..utils.experiment import source_digest
@@ -115,16 +118,16 @@ def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/
             raise RuntimeError("a DP rank ran out of data before the others; padding graphs are not configured")
         torch.cuda.reset_peak_memory_stats() if trainer.device.type == "cuda" else None
         t0 = time.perf_counter()
-        metrics = trainer.train_step(have)
+        metrics = trainer.train_step([loader.acquire(item) for item in have], prepared=True)
         if trainer.device.type == "cuda":
             torch.cuda.synchronize()
         seconds = time.perf_counter() - t0
-        for _, receipt in have:
-            loader.acknowledge(receipt)
+        for item in have:
+            loader.acknowledge(item.receipt)
         peak = torch.cuda.max_memory_allocated() / 2 ** 30 if trainer.device.type == "cuda" else 0.0
         seconds, peak = _all_max([seconds, peak], trainer.device)
         step += 1
-        tokens = sum(r["body_tokens"] for _, r in have)
+        tokens = sum(item.receipt["body_tokens"] for item in have)
         total_tokens = _all_sum([float(tokens)], trainer.device, st.dp_group if dp > 1 else None)[0]
         row = dict(step=step, seconds=seconds, tokens_per_second=total_tokens / seconds, peak_gib=peak, **metrics,
                    warmup=step - start_step <= warmup_steps)

@@ -77,14 +77,19 @@ class Trainer:
             (losses["loss"] * backward_scale).backward()
         return losses
 
-    def train_step(self, micro_batches, timing=False):
+    def train_step(self, micro_batches, timing=False, prepared=False):
         """``micro_batches``: list of (pinned host batch, receipt). Returns host-side metrics of the update.
 
         The step copies every micro-batch to the device, runs the update, and reads the loss back.
-        With ``timing`` it also reports ``compute_ms``: CUDA-event time from after the copies were
-        issued to the end of the optimizer/EMA work (excludes the host->device and device->host I/O).
+        With ``prepared=True`` the batches are already on the device (``data.device.DeviceLoader``
+        copied them on its side stream). With ``timing`` it also reports ``compute_ms``: CUDA-event
+        time from after the copies were issued to the end of the optimizer/EMA work (excludes the
+        host->device and device->host I/O).
         """
-        device_batches = [self.preparer(host, receipt, non_blocking=True) for host, receipt in micro_batches]
+        if prepared:
+            device_batches = [batch for batch, _ in micro_batches]
+        else:
+            device_batches = [self.preparer(host, receipt, non_blocking=True) for host, receipt in micro_batches]
         events = None
         if timing and self.device.type == "cuda":
             events = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
