@@ -124,3 +124,25 @@ def caches(cfg):
                       dict(common, max_pixels=cfg.generation_max_pixels, posterior="mode", spatial_stride=8,
                            temporal_stride=4))
     return qwen, wan
+
+
+def attach_cached(element, qwen, wan):
+    """Fill ``features`` / ``latent`` (+ ``latent_shape``) of an image element from the caches by its
+    ``source`` identity. A missing feature entry is an error (the tower is frozen, so training
+    must not silently recompute it); a missing latent only drops the generation target."""
+    if element.get("type") != "image" or "source" not in element:
+        return element
+    clip = element.get("clip")
+    if qwen is not None and element.get("features") is None:
+        found = qwen.load(qwen.identity(element["source"], clip))
+        if found is None:
+            raise KeyError(f"no cached merger features for {element['source']}")
+        element["features"] = found["features"]
+    if wan is not None and element.get("latent") is None:
+        found = wan.load(wan.identity(element["source"], clip))
+        if found is not None:
+            element["latent"] = found["latent"]
+            element["latent_shape"] = tuple(found["latent"].shape)
+        else:
+            element["generation_target"] = False
+    return element

@@ -80,8 +80,11 @@ class Catalog:
 
 
 class DocumentStream:
-    def __init__(self, root, seed=0, rank=0, world=1, block_rows=4, epochs=1):
+    """``caches=(qwen, wan)`` fills image elements that name a ``source`` from the visual caches."""
+
+    def __init__(self, root, seed=0, rank=0, world=1, block_rows=4, epochs=1, caches=None):
         self.catalog = Catalog(root)
+        self.caches = caches
         self.block_rows, self.rank, self.world, self.epochs = block_rows, rank, world, epochs
         self.blocks = -(-len(self.catalog) // block_rows)
         self.signature = dict(snapshot=self.catalog.snapshot, seed=seed, epoch=0, rank=rank)
@@ -103,7 +106,12 @@ class DocumentStream:
             if self.cursor["row"] >= self.block_rows or index >= len(self.catalog):
                 self.cursor = dict(epoch=self.cursor["epoch"], block=self.cursor["block"] + self.world, row=0)
                 continue
-            return self.catalog.rows[index]
+            row = self.catalog.rows[index]
+            if self.caches is not None:
+                from .cache import attach_cached
+                for element in row["elements"]:
+                    attach_cached(element, *self.caches)
+            return row
         return None
 
     def advance(self):

@@ -76,3 +76,46 @@ def test_device_loader_side_stream_gpu():
     assert loader.stats["acquired"] == 3
     loader.close()
     ref.close()
+
+
+def test_prepare_cache_fills_and_skips(tmp_path):
+    import json as _json
+    import numpy as np
+    from cq_pretrain_b200.data.cache import caches
+    from cq_pretrain_b200.data.prepare_cache import prepare
+    cfg = tiny_config(vision_min_pixels=32 * 32, vision_max_pixels=64 * 64)
+    rng = np.random.default_rng(0)
+    rows = []
+    for i in range(2):
+        pixels = (rng.random((40, 56, 3)) * 255).astype(np.uint8).tolist()
+        rows.append(dict(id=f"d{i}", elements=[dict(type="text", input_ids=[5, 6]),
+                                                dict(type="image", grid=[1, 2, 4], source=f"sha-{i}", pixels=pixels)]))
+    corpus = tmp_path / "corpus"
+    corpus.mkdir()
+    (corpus / "part.jsonl").write_text("\n".join(_json.dumps(r) for r in rows))
+    counts = prepare(cfg, corpus, tmp_path / "cache")
+    assert counts["features"] == 2 and counts["latents"] == 2
+    again = prepare(cfg, corpus, tmp_path / "cache")
+    assert again["features"] == 0 and again["latents"] == 0 and again["skipped"] == 2
+    qwen, wan = caches(cfg)
+    feats = qwen.load(qwen.identity("sha-0", None))["features"]
+    assert feats.shape[1] == cfg.width
+    assert wan.load(wan.identity("sha-1", None))["latent"].shape[0] == cfg.latent_channels
+
+
+def test_stream_attaches_cached_visuals(tmp_path):
+    import json as _json
+    from cq_pretrain_b200.data.cache import caches
+    from cq_pretrain_b200.data.stream import DocumentStream
+    cfg = tiny_config()
+    cfg.visual_cache = str(tmp_path / "cache")
+    qwen, wan = caches(cfg)
+    qwen.save(qwen.identity("img-a", None), features=torch.ones(4, cfg.width))
+    wan.save(wan.identity("img-a", None), latent=torch.zeros(16, 1, 4, 4))
+    corpus = tmp_path / "corpus"
+    corpus.mkdir()
+    (corpus / "p.jsonl").write_text(_json.dumps(dict(id="d", elements=[
+        dict(type="text", input_ids=[7]), dict(type="image", grid=[1, 4, 4], source="img-a")])))
+    stream = DocumentStream(corpus, caches=(qwen, wan))
+    image = stream.peek()["elements"][1]
+    assert torch.equal(image["features"], torch.ones(4, cfg.width)) and image["latent_shape"] == (16, 1, 4, 4)
