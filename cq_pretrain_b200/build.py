@@ -46,6 +46,14 @@ def build(verbose=False):
     return module
 
 
+def build_all(verbose=False):
+    """The sm_100a kernel library plus the host C++ libraries (SSCD graph)."""
+    module = build(verbose)
+    from .corpus.sscd import build_library
+    build_library()
+    return module
+
+
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv)
-    print("built", next(BUILD.glob("cqb_kernels*.so")))
+    build_all(verbose="-v" in sys.argv)
+    print("built", next(BUILD.glob("cqb_kernels*.so")), BUILD / "sscd_graph.so")

@@ -28,6 +28,9 @@ at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
 at::Tensor gemm_nn(at::Tensor a, at::Tensor b);
 void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out);
 int gemm_status(bool reset);
+std::vector<at::Tensor> ce_stats(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo);
+at::Tensor ce_grad_logits(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, int64_t lo,
+                          at::Tensor scale);
 void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_out_ptrs, int64_t rows_per_rank,
                   int64_t src_rank, int64_t tp);
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
@@ -86,6 +89,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_nn", &cqb::gemm_nn);
   m.def("gemm_tn_acc", &cqb::gemm_tn_acc);
   m.def("gemm_status", &cqb::gemm_status, py::arg("reset") = false);
+  m.def("ce_stats", &cqb::ce_stats);
+  m.def("ce_grad_logits", &cqb::ce_grad_logits);
   m.def("gemm_scatter", &cqb::gemm_scatter);
   m.def("gather_gemm", &cqb::gather_gemm);
   m.def("symm_alloc", &cqb::symm_alloc);

@@ -12,6 +12,10 @@
 //    matrix (the main_grad accumulation of weight gradients); 2 = bf16 stores of each tile
 //    straight into the receive buffer of the TP rank that owns its rows, over NVLink peer
 //    memory (the communication half of GEMM -> reduce-scatter, overlapped tile by tile);
+//    3 = cross-entropy statistics: nothing is stored; each thread (one output row) folds the
+//    tile's 256 logits into an online (max, sum exp) pair and picks out its target logit, and
+//    writes one partial per (row, column tile) (the LM-head forward never writes logits);
+//    4 = cross-entropy gradient: (exp(logit - lse) - [col == target]) * dloss as bf16 TMA stores;
 //  * GATHER: two extra warps pull the A row blocks of every TP rank (peer memory, plain loads)
 //    into this GPU's gather buffer and publish a flag per 128-row block; the TMA producer waits
 //    for a block's flag before loading it, and tiles of this rank's own rows go first
@@ -61,6 +65,13 @@ struct GemmArgs {
   long long* chunk_flags;     // [M / 16] per-sub-chunk publication flags (local)
   long long epoch;
   int group_m;                // tile raster: groups of group_m row blocks sweep all column blocks
+  // EPI 3/4 (cross-entropy over a vocabulary shard [lo, lo + N)):
+  const long long* targets;   // [M] global token ids
+  long long lo;
+  float2* ce_part;            // EPI 3: [M, tiles_n] (max, sum exp(x - max)) per column tile
+  float* ce_target;           // EPI 3: [M] target logit (rows whose target is in this shard)
+  const float* ce_lse;        // EPI 4: [M] log-sum-exp over the full vocabulary
+  const float* ce_scale;      // EPI 4: device scalar dloss / rows
 };
 
 __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
@@ -257,7 +268,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     const int quarter = warp & 3;
     uint8_t* my_stage = staging + quarter * 2 * EPI_BOX * EPI_BOX * 4;
     int local = 0, chunk = 0;
-    if (lane == 0 && EPI != 2) tc::prefetch_map(&map_out);
+    if (lane == 0 && EPI != 2 && EPI != 3) tc::prefetch_map(&map_out);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t use = (local >> 1) & 1;
@@ -266,6 +277,55 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       int m0, n0;
       tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
       const uint32_t base = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
+      if (EPI == 3) {
+        // online softmax statistics of this thread's row over the tile's columns
+        const int row = m0 + quarter * 32 + lane;
+        const long long tgt = row < args.M ? args.targets[row] - args.lo : -1;
+        float mx = -INFINITY, se = 0.f, tv = 0.f;
+        bool found = false;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += EPI_BOX) {
+          float v[32];
+          tc::tmem_ld32(base + c, v);
+          const int col0 = n0 + c;
+          if (col0 >= args.N) continue;
+          const int valid = min(32, args.N - col0);
+          float bm = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < valid) bm = fmaxf(bm, v[j]);
+            if (col0 + j == tgt) {
+              tv = v[j];
+              found = true;
+            }
+          }
+          const float nm = fmaxf(mx, bm);
+          float add = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < valid) add += __expf(v[j] - nm);
+          se = se * __expf(mx - nm) + add;
+          mx = nm;
+        }
+        if (row < args.M) {
+          args.ce_part[(size_t)row * tiles_n + n0 / BN] = make_float2(mx, se);
+          if (found) args.ce_target[row] = tv;
+        }
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[buf]);
+        continue;
+      }
+      float ce_l = 0.f, ce_f = 0.f;
+      long long ce_t = -1;
+      if (EPI == 4) {
+        const int row = m0 + quarter * 32 + lane;
+        if (row < args.M) {
+          ce_l = args.ce_lse[row];
+          ce_t = args.targets[row] - args.lo;
+        }
+        ce_f = *args.ce_scale;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += EPI_BOX, ++chunk) {
         float v[32];
@@ -277,7 +337,17 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           if (lane == 0) tc::bulk_wait_read1();  // the store that last used this buffer finished reading
           __syncwarp();
         }
-        if (EPI == 0 || EPI == 2) {
+        if (EPI == 4) {
+          __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(box) + lane * EPI_BOX;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float o[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              o[q] = (__expf(v[j + q] - ce_l) - (col0 + j + q == ce_t ? 1.f : 0.f)) * ce_f;
+            store8(row + j, o);
+          }
+        } else if (EPI == 0 || EPI == 2) {
           __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(box) + lane * EPI_BOX;
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
@@ -312,7 +382,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           tc::fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            if (EPI == 0)
+            if (EPI == 0 || EPI == 4)
               tc::tma_store_2d(&map_out, box, col0, m0 + quarter * 32);
             else
               tc::tma_reduce_add_2d(&map_out, box, col0, m0 + quarter * 32);
@@ -324,7 +394,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[buf]);
     }
-    if (EPI != 2 && lane == 0) tc::bulk_wait_all();
+    if (EPI != 2 && EPI != 3 && lane == 0) tc::bulk_wait_all();
     __syncwarp();
   } else if (GATHER) {
     // Copy warps 6..7 of every CTA pull 16-row sub-chunks of A into the local gather buffer,
@@ -552,6 +622,89 @@ at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tenso
   args.src_rank = (int)src_rank;
   args.tp = (int)tp;
   launch<false, false, 0, true>(ma, mb, make_out_map(y), args);
+  return y;
+}
+
+namespace {
+
+// (max, sum exp) merge of the per-tile partials of each row: one warp per row.
+__global__ void ce_merge_kernel(const float2* __restrict__ part, int rows, int tiles, float* __restrict__ mx_out,
+                                float* __restrict__ se_out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  float m = -INFINITY, s = 0.f;
+  for (int t = lane; t < tiles; t += 32) {
+    const float2 p = part[(size_t)warp * tiles + t];
+    const float nm = fmaxf(m, p.x);
+    s = s * __expf(m - nm) + p.y * __expf(p.x - nm);
+    m = nm;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = s * __expf(m - nm) + os * __expf(om - nm);
+    m = nm;
+  }
+  if (lane == 0) {
+    mx_out[warp] = m;
+    se_out[warp] = s;
+  }
+}
+
+void check_ce(const at::Tensor& h, const at::Tensor& w, const at::Tensor& targets) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.dim() == 2, "h: bf16 [rows, K]");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.size(1) == h.size(1), "w: bf16 [V, K]");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous() && targets.numel() == h.size(0),
+              "targets: int64 [rows]");
+  check_dims(h.size(0), w.size(0), h.size(1));
+}
+
+}  // namespace
+
+// Vocabulary-shard statistics of logits = h w^T without materialising them:
+// returns (row max, target logit (0 where the target is outside [lo, lo + V)), sum exp(logit - max)).
+std::vector<at::Tensor> ce_stats(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo) {
+  check_ce(h, w, targets);
+  const int64_t M = h.size(0), K = h.size(1), N = w.size(0);
+  const int tiles_n = (int)((N + BN - 1) / BN);
+  auto f32 = h.options().dtype(at::kFloat);
+  auto part = at::empty({M, tiles_n, 2}, f32);
+  auto tgt = at::zeros({M}, f32);
+  auto mx = at::empty({M}, f32), se = at::empty({M}, f32);
+  auto ma = make_map(h, BM);
+  auto mb = make_map(w, BN);
+  auto args = plain_args(M, N, K, nullptr, N, nullptr);
+  args.targets = reinterpret_cast<const long long*>(targets.data_ptr<int64_t>());
+  args.lo = lo;
+  args.ce_part = reinterpret_cast<float2*>(part.data_ptr<float>());
+  args.ce_target = tgt.data_ptr<float>();
+  launch<false, false, 3, false>(ma, mb, ma, args);
+  ce_merge_kernel<<<(unsigned)((M * 32 + 255) / 256), 256, 0, stream()>>>(
+      reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)M, tiles_n, mx.data_ptr<float>(),
+      se.data_ptr<float>());
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {mx, tgt, se};
+}
+
+// dlogits = (softmax(h w^T) - onehot(target - lo)) * scale as bf16 [rows, V] (scale: device scalar).
+at::Tensor ce_grad_logits(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, int64_t lo,
+                          at::Tensor scale) {
+  check_ce(h, w, targets);
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == h.size(0), "lse: fp32 [rows]");
+  auto sc = scale.to(at::kFloat).reshape({1}).contiguous();
+  TORCH_CHECK(sc.is_cuda(), "scale must live on the GPU");
+  const int64_t M = h.size(0), K = h.size(1), N = w.size(0);
+  auto y = at::empty({M, N}, h.options());
+  auto ma = make_map(h, BM);
+  auto mb = make_map(w, BN);
+  auto args = plain_args(M, N, K, y.data_ptr(), N, nullptr);
+  args.targets = reinterpret_cast<const long long*>(targets.data_ptr<int64_t>());
+  args.lo = lo;
+  args.ce_lse = lse.data_ptr<float>();
+  args.ce_scale = sc.data_ptr<float>();
+  launch<false, false, 4, false>(ma, mb, make_out_map(y), args);
   return y;
 }
 

@@ -8,8 +8,10 @@ present) and ``dh = dlogits W_local`` (summed over TP by the caller's row collec
 Reference: ``ops/cross_entropy.py:17-116``.
 
 On CUDA the per-chunk work is an LM-head GEMM whose epilogue computes the row statistics
-online (``csrc/ce.cu``), so logits are never written to memory in the forward; the TP combine
-of the three ``[rows]`` statistics uses one all-reduce of a packed ``[3, rows]`` buffer.
+online (``csrc/gemm.cu``, epilogue 3), so logits are never written to memory in the forward,
+and the backward recomputes each logits tile and stores ``(softmax - onehot) * dloss`` straight
+from the accumulator (epilogue 4). The TP combine of the ``[rows]`` statistics is one MAX and one
+SUM all-reduce.
 """
 
 from __future__ import annotations
@@ -33,10 +35,15 @@ def _stats_combine(mx, tgt, sexp, group):
     return gmax, packed[0], packed[1]
 
 
+def _kernel_shapes(h, w):
+    """The tcgen05 LM-head kernels need bf16 operands with K and the vocab shard multiples of 16."""
+    return (h.is_cuda and _ext.cuda_kernels_enabled() and h.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+            and h.shape[1] % 16 == 0 and w.shape[0] % 16 == 0 and h.shape[0] > 0 and w.is_contiguous())
+
+
 def _chunk_stats(h, w, targets, lo):
     """Local (max, target logit (0 if not owned), sum exp relative to local max) for one chunk."""
-    if h.is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "ce_stats") and h.dtype == torch.bfloat16 \
-            and w.shape[1] % 16 == 0:
+    if _kernel_shapes(h, w) and hasattr(_ext.ops(), "ce_stats"):
         return _ext.ops().ce_stats(h.contiguous(), w, targets, lo)
     logits = gemm.linear(h, w).float()
     mx = logits.max(-1).values
@@ -74,8 +81,7 @@ class _LinearCE(torch.autograd.Function):
         for start in range(0, hidden.shape[0], ctx.chunk):
             h, t = hidden[start:start + ctx.chunk], targets[start:start + ctx.chunk]
             lse = lse_all[start:start + ctx.chunk]
-            if h.is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "ce_grad_logits") \
-                    and h.dtype == torch.bfloat16:
+            if _kernel_shapes(h, weight) and hasattr(_ext.ops(), "ce_grad_logits"):
                 grad = _ext.ops().ce_grad_logits(h.contiguous(), weight, t, lse, ctx.lo, factor)
             else:
                 logits = gemm.linear(h, weight).float()

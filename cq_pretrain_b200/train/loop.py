@@ -136,6 +136,10 @@ def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/
             with (output / "steps.jsonl").open("a") as f:
                 f.write(json.dumps(row) + "\n")
             print(json.dumps(row), flush=True)
+        if training.get("validation_probes"):
+            probes = ckpt.validation_probes(trainer.model, trainer.optimizer)
+            (output / "probes").mkdir(parents=True, exist_ok=True)
+            torch.save(probes, output / "probes" / f"rank{st.rank}_step_{step:07d}.pt")
         if checkpoint_interval and step % checkpoint_interval == 0:
             states = [None] * st.world if dist.is_initialized() else None
             mine = dict(packer=None, loader=loader.state_dict())
@@ -178,8 +182,12 @@ def main(argv=None):
     parser.add_argument("--keep-checkpoints", type=int, default=2)
     parser.add_argument("--snapshot-interval", type=int, default=0)
     parser.add_argument("--resume", action="store_true")
+    parser.add_argument("--validation-probes", action="store_true",
+                        help="write parameter/master/Adam probes after every update (not a speed run)")
     args = parser.parse_args(argv)
     cfg, training, environment = load_sections(args.config)
+    if args.validation_probes:
+        training["validation_probes"] = True
     for key, value in environment.items():
         os.environ.setdefault(key, str(value))
     tp = args.tp or int(training.get("tp", 1))

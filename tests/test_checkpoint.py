@@ -153,3 +153,17 @@ def test_latest_refuses_only_corrupt_commits(tmp_path):
                                                      topology=dict(tp=1, dp=1), files={})))
     with pytest.raises(RuntimeError):
         catalog.latest(tmp_path)
+
+
+def test_validation_probes_layout():
+    import torch
+    from cq_pretrain_b200.config import tiny_config
+    from cq_pretrain_b200.train.checkpoint import validation_probes
+    from cq_pretrain_b200.train.trainer import Trainer
+    trainer = Trainer(tiny_config(), tp=1, lr=1e-3, device="cpu", dtype=torch.float32)
+    probes = validation_probes(trainer.model, trainer.optimizer)
+    names = [name for name, _, _ in probes["layout"]]
+    assert names[0].startswith("model/") and any(n.startswith("adam/") for n in names)
+    assert probes["values"].numel() == sum(c for _, _, c in probes["layout"])
+    again = validation_probes(trainer.model, trainer.optimizer)
+    assert torch.equal(probes["values"], again["values"])

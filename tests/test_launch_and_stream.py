@@ -103,3 +103,14 @@ def test_stream_shards_and_resumes(tmp_path):
     assert rest_a == rest_b
     with pytest.raises(ValueError):
         DocumentStream(tmp_path / "c", seed=2, rank=0, world=2).load_state_dict(state)
+
+
+def test_committed_yaml_configs_load_and_validate():
+    from pathlib import Path
+    from cq_pretrain_b200.config import load_sections, tiny_config
+    root = Path(__file__).resolve().parents[1] / "cq_pretrain_b200" / "configs"
+    cfg, training, env = load_sections(root / "qwen35_2b_wan.yaml")
+    cfg.validate(int(training["tp"]))
+    assert cfg.width == 2048 and training["sequence_length"] == 8192 and "PYTORCH_CUDA_ALLOC_CONF" in env
+    tiny, _, _ = load_sections(root / "tiny.yaml")
+    assert tiny.to_dict() == tiny_config().to_dict()
