@@ -63,6 +63,10 @@ std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, 
 at::Tensor conv_fwd(at::Tensor x, at::Tensor w, at::Tensor pos);
 std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor pos);
 std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunks, bool normalize, double scale);
+at::Tensor qconv_fwd(at::Tensor raw, at::Tensor updates, at::Tensor w, at::Tensor qs, at::Tensor qh);
+std::vector<at::Tensor> qconv_bwd(at::Tensor dy, at::Tensor raw, at::Tensor updates, at::Tensor w, at::Tensor qs,
+                                  at::Tensor qh, at::Tensor hist_rows, at::Tensor hist_offsets,
+                                  at::Tensor hist_entries);
 at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::Tensor rnorm, bool normalize,
                          double scale);
 // optim.cu
@@ -112,5 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_fwd", &cqb::conv_fwd);
   m.def("conv_bwd", &cqb::conv_bwd);
   m.def("chunk_gather", &cqb::chunk_gather);
+  m.def("qconv_fwd", &cqb::qconv_fwd);
+  m.def("qconv_bwd", &cqb::qconv_bwd);
   m.def("chunk_scatter", &cqb::chunk_scatter);
 }

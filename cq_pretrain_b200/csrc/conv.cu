@@ -203,6 +203,137 @@ __global__ void sum_rows_kernel(const float* __restrict__ partial, float* __rest
   out[e] = s;
 }
 
+
+// ---- query-side short conv (GDN read-only query events) -------------------------------------
+// A query event's conv input is its own projected row plus the last K-1 content inputs of its
+// document (or zeros): out[i, c] = silu(raw[qs[i], c] w[c, K-1] + sum_j hist_j(i)[c] w[c, j]),
+// hist_j(i) = updates[qh[i, j]] (qh == nc: zero row). Only the first `size` (q) channels of
+// the raw/updates rows are read (row strides ld_raw / ld_upd).
+constexpr int QROWS = 16;   // queries per thread in the backward row pass
+
+__global__ void __launch_bounds__(256) qconv_fwd_kernel(const __nv_bfloat16* __restrict__ raw, int ld_raw,
+                                                        const __nv_bfloat16* __restrict__ upd, int ld_upd,
+                                                        const long* __restrict__ qs, const long* __restrict__ qh,
+                                                        long nc, const float* __restrict__ wT,
+                                                        __nv_bfloat16* __restrict__ out, int nq, int size) {
+  const int vecs = size / 8;
+  const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (idx >= (size_t)nq * vecs) return;
+  const int i = (int)(idx / vecs), c = (int)(idx % vecs) * 8;
+  float acc[8], x[8], w[8];
+  load8(raw + (size_t)qs[i] * ld_raw + c, x);
+  load8(wT + (size_t)(CONV_K - 1) * size + c, w);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = x[j] * w[j];
+#pragma unroll
+  for (int t = 0; t < CONV_K - 1; ++t) {
+    const long r = qh[(size_t)i * (CONV_K - 1) + t];
+    if (r == nc) continue;
+    load8(upd + (size_t)r * ld_upd + c, x);
+    load8(wT + (size_t)t * size + c, w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] += x[j] * w[j];
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = silu(acc[j]);
+  store8(out + (size_t)i * size + c, acc);
+}
+
+// g = dy silu'(pre) -> gbuf (fp32); d_raw[qs[i]] = g w[K-1]; per-block dw partials.
+__global__ void __launch_bounds__(256) qconv_bwd_rows_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ raw, int ld_raw,
+    const __nv_bfloat16* __restrict__ upd, int ld_upd, const long* __restrict__ qs, const long* __restrict__ qh,
+    long nc, const float* __restrict__ wT, float* __restrict__ gbuf, __nv_bfloat16* __restrict__ d_raw, int ld_draw,
+    float* __restrict__ partial, int nq, int size) {
+  __shared__ float red[CONV_GROUPS][CONV_K * 8][33];
+  const int v = blockIdx.x * 32 + threadIdx.x;
+  const bool active = v < size / 8;
+  const int c = v * 8;
+  const int i0 = (blockIdx.y * CONV_GROUPS + threadIdx.y) * QROWS;
+  float part[CONV_K][8];
+#pragma unroll
+  for (int t = 0; t < CONV_K; ++t)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part[t][j] = 0.f;
+  if (active) {
+    float w[CONV_K][8];
+#pragma unroll
+    for (int t = 0; t < CONV_K; ++t) load8(wT + (size_t)t * size + c, w[t]);
+    for (int i = i0; i < min(nq, i0 + QROWS); ++i) {
+      float x[CONV_K][8], pre[8], d[8], g[8];
+      load8(raw + (size_t)qs[i] * ld_raw + c, x[CONV_K - 1]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pre[j] = x[CONV_K - 1][j] * w[CONV_K - 1][j];
+#pragma unroll
+      for (int t = 0; t < CONV_K - 1; ++t) {
+        const long r = qh[(size_t)i * (CONV_K - 1) + t];
+        if (r == nc) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[t][j] = 0.f;
+        } else {
+          load8(upd + (size_t)r * ld_upd + c, x[t]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pre[j] += x[t][j] * w[t][j];
+      }
+      load8(dy + (size_t)i * size + c, d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float sg = 1.f / (1.f + __expf(-pre[j]));
+        g[j] = d[j] * sg * (1.f + pre[j] * (1.f - sg));
+      }
+      store8(gbuf + (size_t)i * size + c, g);
+      float dr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dr[j] = g[j] * w[CONV_K - 1][j];
+      store8(d_raw + (size_t)qs[i] * ld_draw + c, dr);
+#pragma unroll
+      for (int t = 0; t < CONV_K; ++t)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) part[t][j] += g[j] * x[t][j];
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < CONV_K; ++t)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[threadIdx.y][j * CONV_K + t][threadIdx.x] = part[t][j];
+  __syncthreads();
+  const int tid = threadIdx.y * 32 + threadIdx.x;
+  for (int e = tid; e < 32 * 8 * CONV_K; e += 256) {
+    const int lane = e / (8 * CONV_K), r = e % (8 * CONV_K);
+    const int vv = blockIdx.x * 32 + lane;
+    if (vv >= size / 8) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int gi = 0; gi < CONV_GROUPS; ++gi) sum += red[gi][r][lane];
+    partial[((size_t)blockIdx.y * size + vv * 8) * CONV_K + r] = sum;
+  }
+}
+
+// d_upd[rows[k]] = sum over entries e of row k: gbuf[e / (K-1)] * w[e % (K-1)] (one block per row).
+__global__ void __launch_bounds__(256) qconv_bwd_hist_kernel(const float* __restrict__ gbuf,
+                                                             const float* __restrict__ wT,
+                                                             const int* __restrict__ rows,
+                                                             const int* __restrict__ offsets,
+                                                             const int* __restrict__ entries,
+                                                             __nv_bfloat16* __restrict__ d_upd, int ld_upd, int size) {
+  const int k = blockIdx.x;
+  const int e0 = offsets[k], e1 = offsets[k + 1];
+  for (int c = threadIdx.x * 8; c < size; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int e = e0; e < e1; ++e) {
+      const int ent = entries[e];
+      const int i = ent / (CONV_K - 1), t = ent % (CONV_K - 1);
+      float g[8], w[8];
+      load8(gbuf + (size_t)i * size + c, g);
+      load8(wT + (size_t)t * size + c, w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += g[j] * w[j];
+    }
+    store8(d_upd + (size_t)rows[k] * ld_upd + c, acc);
+  }
+}
+
 // out[n, h, c, :] = normalise?(x[idx[n*64 + c], h, :]) (zero when idx < 0); r[e, h] = rsqrt norm.
 template <int D>
 __global__ void chunk_gather_kernel(const __nv_bfloat16* __restrict__ x, const long* __restrict__ idx,
@@ -324,6 +455,80 @@ std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::
   CQB_LAUNCH_CHECK();
   count_launch(2);
   return {dx, dw};
+}
+
+
+namespace {
+void check_qconv(const at::Tensor& raw, const at::Tensor& upd, const at::Tensor& w, const at::Tensor& qs,
+                 const at::Tensor& qh) {
+  for (const auto* t : {&raw, &upd})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 &&
+                    t->stride(0) % 8 == 0,
+                "raw/updates: bf16 row-major, row stride a multiple of 8");
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == CONV_K && w.size(0) % 8 == 0, "w: [size, 4], size % 8 == 0");
+  TORCH_CHECK(raw.size(1) >= w.size(0) && upd.size(1) >= w.size(0), "rows narrower than the conv channels");
+  TORCH_CHECK(qs.scalar_type() == at::kLong && qh.scalar_type() == at::kLong && qh.is_contiguous() &&
+                  qh.dim() == 2 && qh.size(1) == CONV_K - 1 && qh.size(0) == qs.numel(),
+              "query_source int64 [nq], query_history int64 [nq, 3]");
+}
+}  // namespace
+
+// Query conv forward: [nq, size] bf16.
+at::Tensor qconv_fwd(at::Tensor raw, at::Tensor updates, at::Tensor w, at::Tensor qs, at::Tensor qh) {
+  check_qconv(raw, updates, w, qs, qh);
+  const int nq = qs.numel(), size = w.size(0);
+  auto wT = w.to(at::kFloat).t().contiguous();
+  auto qsc = qs.contiguous();
+  auto out = at::empty({nq, size}, raw.options());
+  if (!nq) return out;
+  qconv_fwd_kernel<<<blocks_for((size_t)nq * size / 8), 256, 0, stream()>>>(
+      (const __nv_bfloat16*)raw.data_ptr(), (int)raw.stride(0), (const __nv_bfloat16*)updates.data_ptr(),
+      (int)updates.stride(0), (const long*)qsc.data_ptr(), (const long*)qh.data_ptr(), (long)updates.size(0),
+      wT.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(), nq, size);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return out;
+}
+
+// Query conv backward: (d_raw like raw, d_updates like updates: zero outside the rows/channels the
+// queries read; dw [size, 4] fp32).
+std::vector<at::Tensor> qconv_bwd(at::Tensor dy, at::Tensor raw, at::Tensor updates, at::Tensor w, at::Tensor qs,
+                                  at::Tensor qh, at::Tensor hist_rows, at::Tensor hist_offsets,
+                                  at::Tensor hist_entries) {
+  check_qconv(raw, updates, w, qs, qh);
+  TORCH_CHECK(hist_rows.scalar_type() == at::kInt && hist_offsets.scalar_type() == at::kInt &&
+                  hist_entries.scalar_type() == at::kInt && hist_offsets.numel() == hist_rows.numel() + 1,
+              "history CSR: int32 rows [U], offsets [U+1], entries [E]");
+  const int nq = qs.numel(), size = w.size(0);
+  auto dyc = dy.contiguous();
+  TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.numel() == (int64_t)nq * size, "dy: bf16 [nq, size]");
+  auto wT = w.to(at::kFloat).t().contiguous();
+  auto qsc = qs.contiguous();
+  auto d_raw = at::zeros({raw.size(0), raw.size(1)}, raw.options());
+  auto d_upd = at::zeros({updates.size(0), updates.size(1)}, updates.options());
+  auto dw = at::zeros({size, CONV_K}, raw.options().dtype(at::kFloat));
+  if (!nq) return {d_raw, d_upd, dw};
+  auto gbuf = at::empty({nq, size}, raw.options().dtype(at::kFloat));
+  const dim3 grid((size / 8 + 31) / 32, (nq + QROWS * CONV_GROUPS - 1) / (QROWS * CONV_GROUPS));
+  auto partial = at::empty({(long)grid.y, size, CONV_K}, dw.options());
+  qconv_bwd_rows_kernel<<<grid, dim3(32, CONV_GROUPS), 0, stream()>>>(
+      (const __nv_bfloat16*)dyc.data_ptr(), (const __nv_bfloat16*)raw.data_ptr(), (int)raw.stride(0),
+      (const __nv_bfloat16*)updates.data_ptr(), (int)updates.stride(0), (const long*)qsc.data_ptr(),
+      (const long*)qh.data_ptr(), (long)updates.size(0), wT.data_ptr<float>(), gbuf.data_ptr<float>(),
+      (__nv_bfloat16*)d_raw.data_ptr(), (int)d_raw.stride(0), partial.data_ptr<float>(), nq, size);
+  CQB_LAUNCH_CHECK();
+  sum_rows_kernel<<<(size * CONV_K + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                     grid.y, size * CONV_K);
+  CQB_LAUNCH_CHECK();
+  const int U = hist_rows.numel();
+  if (U)
+    qconv_bwd_hist_kernel<<<U, 256, 0, stream()>>>(gbuf.data_ptr<float>(), wT.data_ptr<float>(),
+                                                   hist_rows.data_ptr<int>(), hist_offsets.data_ptr<int>(),
+                                                   hist_entries.data_ptr<int>(), (__nv_bfloat16*)d_upd.data_ptr(),
+                                                   (int)d_upd.stride(0), size);
+  CQB_LAUNCH_CHECK();
+  count_launch(3);
+  return {d_raw, d_upd, dw};
 }
 
 std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunks, bool normalize, double scale) {

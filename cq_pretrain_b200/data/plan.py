@@ -49,6 +49,11 @@ class DeltaPlan(Movable):
     padding_hidden: torch.Tensor    # [*] hidden rows that receive no GDN output (zeroed)
     query_source: torch.Tensor      # [nq] hidden row of each query event's own projection
     query_history: torch.Tensor     # [nq, K-1] conv history (content index or nc = zero)
+    # The same history as CSR keyed by content row (for the query-conv backward, no atomics):
+    # rows read by some query, entry offsets per row, entries = query * (K-1) + tap.
+    query_hist_rows: torch.Tensor = None
+    query_hist_offsets: torch.Tensor = None
+    query_hist_entries: torch.Tensor = None
     content_bounds: tuple = ()      # host copy of content_cu
     event_bounds: tuple = ()        # host copy of event_cu
     rows: int = 0
@@ -345,7 +350,15 @@ def build_delta_plan(segments, sigma, query_positions, query_unconditional, s, r
     inverses = dict(content_order_inv=inverse_levels(order_np, rows), query_source_inv=inverse_levels(qsrc_np, rows),
                     event_q_inv=inverse_levels(eq, nc + len(q_source)), event_write_inv=inverse_levels(ew, nc + 1, ignore=nc),
                     hidden_event_inv=inverse_levels(hidden_event, n_events + 1, ignore=n_events))
+    flat = qh.reshape(-1)
+    used = np.nonzero(flat != nc)[0]
+    order_h = used[np.argsort(flat[used], kind="stable")]
+    hist_rows, counts = np.unique(flat[order_h], return_counts=True)
+    hist_offsets = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
     return DeltaPlan(**inverses,
+        query_hist_rows=torch.from_numpy(hist_rows.astype(np.int32)),
+        query_hist_offsets=torch.from_numpy(hist_offsets),
+        query_hist_entries=torch.from_numpy(order_h.astype(np.int32)),
         content_order=torch.from_numpy(np.array(order, dtype=np.int64)),
         content_cu=torch.tensor(content_cu, dtype=torch.int32),
         event_q=torch.from_numpy(eq), event_write=torch.from_numpy(ew),

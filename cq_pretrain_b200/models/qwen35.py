@@ -133,13 +133,7 @@ class GatedDelta(nn.Module):
         q, k, v = conv.split((size, size, h * d), -1)
         # Query conv reads the previous k-1 real content inputs of its document; queries never
         # enter any other token's history.
-        weight = self.conv1d.weight[:size, 0]
-        history = torch.cat((updates[:, :size], updates.new_zeros(1, size)), 0)
-        qraw = GA.rows(raw[:, :size], dp.query_source, dp.query_source_inv)
-        query = qraw * weight[:, -1].to(qraw.dtype)
-        for j in range(cfg.linear_conv_kernel - 1):
-            query = query + history.index_select(0, dp.query_history[:, j]) * weight[:, j].to(qraw.dtype)
-        query = F.silu(query.float()).to(raw.dtype) if raw.dtype != torch.float64 else F.silu(query)
+        query = GDN.query_conv_silu(raw, updates, self.conv1d.weight[:size, 0], dp)
         q, k, query = q.reshape(-1, hk, d), k.reshape(-1, hk, d), query.reshape(-1, hk, d)
         v = v.reshape(-1, h, d)
         if h != hk:

@@ -35,3 +35,42 @@ def causal_conv_silu(x, weight, bounds):
         from .gdn_cuda import causal_conv_cuda
         return causal_conv_cuda(x, weight, bounds)
     return R.causal_conv_silu(x, weight, bounds)
+
+
+class _QueryConv(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, raw, updates, weight, qs, qh, rows, offsets, entries):
+        ctx.save_for_backward(raw, updates, weight, qs, qh, rows, offsets, entries)
+        return _ext.ops().qconv_fwd(raw, updates, weight, qs, qh)
+
+    @staticmethod
+    def backward(ctx, dy):
+        raw, updates, weight, qs, qh, rows, offsets, entries = ctx.saved_tensors
+        d_raw, d_upd, dw = _ext.ops().qconv_bwd(dy.to(torch.bfloat16), raw, updates, weight, qs, qh, rows, offsets,
+                                                entries)
+        return d_raw, d_upd, dw.to(weight.dtype), None, None, None, None, None
+
+
+def query_conv_silu(raw, updates, weight, plan):
+    """Short conv + SiLU of the read-only query events: each query's own projection (``raw`` row
+    ``plan.query_source``) plus the last K-1 content inputs of its document (``updates`` rows
+    ``plan.query_history``; the index ``len(updates)`` reads zeros). Only the first
+    ``weight.shape[0]`` channels of ``raw``/``updates`` are used. Returns ``[nq, channels]``.
+
+    CUDA runs ``qconv_fwd``/``qconv_bwd`` (``csrc/conv.cu``): the backward sums each content row's
+    history gradient over the CSR ``plan.query_hist_*`` (deterministic, no atomics).
+    """
+    size, K = weight.shape
+    if (raw.is_cuda and raw.dtype == torch.bfloat16 and K == 4 and size % 8 == 0 and _ext.has("qconv_fwd")
+            and plan.query_hist_rows is not None):
+        return _QueryConv.apply(raw, updates, weight, plan.query_source, plan.query_history, plan.query_hist_rows,
+                                plan.query_hist_offsets, plan.query_hist_entries)
+    from . import gather as GA
+    history = torch.cat((updates[:, :size], updates.new_zeros(1, size)), 0)
+    qraw = GA.rows(raw[:, :size], plan.query_source, plan.query_source_inv)
+    query = qraw * weight[:, -1].to(qraw.dtype)
+    for j in range(K - 1):
+        query = query + history.index_select(0, plan.query_history[:, j]) * weight[:, j].to(qraw.dtype)
+    if raw.dtype == torch.float64:
+        return torch.nn.functional.silu(query)
+    return torch.nn.functional.silu(query.float()).to(raw.dtype)

@@ -56,3 +56,31 @@ def test_chunk_gather_scatter_roundtrip():
     yr.backward(dy_events)
     rel = (dx.float() - xr.grad).norm() / xr.grad.norm()
     assert rel < 1e-2, rel.item()
+
+
+def test_query_conv_matches_torch_path():
+    from cq_pretrain_b200.config import tiny_config
+    from cq_pretrain_b200.data.synthetic import synthetic_batch
+    from cq_pretrain_b200.ops import gdn as GDN
+    assert _ext.has("qconv_fwd")
+    cfg = tiny_config()
+    host, _ = synthetic_batch(cfg, 512, seed=3)
+    dp = host.mainline.delta.to("cuda")
+    torch.manual_seed(0)
+    rows, nc, width, size = host.mainline.rows, len(dp.content_order), 640, 256
+    proj = torch.randn(rows, width + 64, device="cuda").to(torch.bfloat16)
+    raw = proj[:, :width]                       # strided view, like a split projection
+    updates = torch.randn(nc, width, device="cuda").to(torch.bfloat16)
+    w = torch.rand(size, 4, device="cuda") - 0.5
+    ra, ua, wa = raw.detach().clone().requires_grad_(), updates.clone().requires_grad_(), w.clone().requires_grad_()
+    ra_view = torch.cat((ra, proj[:, width:]), 1)[:, :width]   # keep the kernel path on a strided input
+    out = GDN.query_conv_silu(ra_view, ua, wa, dp)
+    rf, uf, wf = raw.float().requires_grad_(), updates.float().requires_grad_(), w.clone().requires_grad_()
+    ref = GDN.query_conv_silu(rf.double(), uf.double(), wf.double(), dp)   # torch path (float64)
+    assert (out.double() - ref).abs().max().item() < 2e-2
+    dy = torch.randn_like(ref)
+    out.backward(dy.to(out.dtype))
+    ref.backward(dy)
+    for got, want in ((ra.grad, rf.grad), (ua.grad, uf.grad), (wa.grad, wf.grad)):
+        rel = (got.double() - want.double()).norm() / want.double().norm()
+        assert rel < 1e-2, rel.item()
