@@ -632,19 +632,23 @@ __global__ void ce_merge_kernel(const float2* __restrict__ part, int rows, int t
                                 float* __restrict__ se_out) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
+  // (m, s) pairs merge as s = s e^{m - M} + s' e^{m' - M}; a lane without tiles holds (-inf, 0)
+  // and two such lanes must stay (-inf, 0) instead of forming e^{-inf - (-inf)}.
+  auto merge = [](float& m, float& s, float om, float os) {
+    const float nm = fmaxf(m, om);
+    if (nm == -INFINITY) return;
+    s = s * __expf(m - nm) + os * __expf(om - nm);
+    m = nm;
+  };
   float m = -INFINITY, s = 0.f;
   for (int t = lane; t < tiles; t += 32) {
     const float2 p = part[(size_t)warp * tiles + t];
-    const float nm = fmaxf(m, p.x);
-    s = s * __expf(m - nm) + p.y * __expf(p.x - nm);
-    m = nm;
+    merge(m, s, p.x, p.y);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
-    const float nm = fmaxf(m, om);
-    s = s * __expf(m - nm) + os * __expf(om - nm);
-    m = nm;
+    merge(m, s, om, os);
   }
   if (lane == 0) {
     mx_out[warp] = m;

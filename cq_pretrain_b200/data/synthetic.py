@@ -68,7 +68,8 @@ def joint_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), latent
     """
     rng = np.random.default_rng(seed)
     docs = []
-    half = images // 2 if understanding and images > 1 else 0
+    # understanding: True -> half of the visuals are I2T, "all" -> every visual is I2T
+    half = images if understanding == "all" else (images // 2 if understanding and images > 1 else 0)
     for i in range(images):
         direction = "I2T" if i >= images - half else "T2I"
         cap = dict(type="text", input_ids=text_ids(rng, caption, cfg.vocab_size))

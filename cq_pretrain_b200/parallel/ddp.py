@@ -21,8 +21,9 @@ Layout (reference ``distributed/megatron.py:210-240`` used Megatron DDP + distri
 
 The grad-norm clip (1.0), betas (0.9, 0.95), eps 1e-8, decoupled weight decay (not on
 biases / 1-D parameters) and ``min_lr = 0.1 lr`` follow the reference optimizer config. On
-CUDA the update of all owned shards is one multi-tensor kernel (``csrc/adam.cu``) that also
-applies the renderer EMA to its shards.
+CUDA the update of all owned shards is one multi-tensor kernel (``csrc/optim.cu``) that also
+writes the updated parameters in their training dtype, and the global gradient norm is one
+multi-tensor reduction.
 """
 
 from __future__ import annotations
@@ -170,8 +171,12 @@ class DistributedOptimizer:
         n = (b.end - b.start) // self.dp
         full = b.group.grad_buffer[b.start:b.end]
         if self.dp > 1:
-            out = full[self.dp_rank * n:(self.dp_rank + 1) * n]
-            b.handle = dist.reduce_scatter_tensor(out, full, op=dist.ReduceOp.SUM, group=self.dp_group, async_op=True)
+            if dist.get_backend(self.dp_group) == "gloo":   # CPU tests: gloo has no reduce-scatter
+                b.handle = dist.all_reduce(full, group=self.dp_group, async_op=True)
+            else:
+                out = full[self.dp_rank * n:(self.dp_rank + 1) * n]
+                b.handle = dist.reduce_scatter_tensor(out, full, op=dist.ReduceOp.SUM, group=self.dp_group,
+                                                      async_op=True)
         b.launched = True
         self.next_bucket = max(self.next_bucket, b.index + 1)
 
@@ -283,8 +288,11 @@ class DistributedOptimizer:
         for b in self.buckets:
             n = (b.end - b.start) // self.dp
             full = b.group.param_buffer[b.start:b.end]
-            handles.append(dist.all_gather_into_tensor(full, full[self.dp_rank * n:(self.dp_rank + 1) * n].clone(),
-                                                       group=self.dp_group, async_op=True))
+            mine = full[self.dp_rank * n:(self.dp_rank + 1) * n].clone()
+            if dist.get_backend(self.dp_group) == "gloo":
+                dist.all_gather(list(full.split(n)), mine, group=self.dp_group)
+                continue
+            handles.append(dist.all_gather_into_tensor(full, mine, group=self.dp_group, async_op=True))
         for h in handles:
             h.wait()
 

@@ -219,30 +219,3 @@ def initialize_model(path, model, config):
     return dict(path=str(root), source_step=manifest["step"], source_tp=source_tp, target_tp=st.tp,
                 restored=["model"], new_stage=True, optimizer="fresh", data_cursor="new dataset start")
 
-
-def validation_probes(model, optimizer):
-    """16 strided samples of every parameter, fp32 master shard and Adam moment, for checking that a
-    resumed run reproduces an uninterrupted one bit for bit (reference ``utils/checkpoint.py:36-51``).
-
-    Returns ``dict(layout=[(name, shape, count)], values=fp32 CPU tensor)``; compare two runs'
-    ``values`` with ``torch.equal``. Probing synchronises the device, so runs that write probes are
-    not throughput measurements.
-    """
-    import torch
-    values, layout = [], []
-
-    def add(name, tensor):
-        if not tensor.numel():
-            return
-        flat = tensor.detach().reshape(-1)
-        picked = flat[::max(1, flat.numel() // 16)][:16].float()
-        values.append(picked)
-        layout.append((name, tuple(tensor.shape), int(picked.numel())))
-
-    for name, p in model.named_parameters():
-        add("model/" + name, p)
-    for i, shard in enumerate(getattr(optimizer, "shards", [])):
-        add(f"master/{i}", shard["master"])
-        add(f"adam/{i}/exp_avg", shard["exp_avg"])
-        add(f"adam/{i}/exp_avg_sq", shard["exp_avg_sq"])
-    return dict(layout=layout, values=torch.cat(values).cpu() if values else torch.zeros(0))

@@ -49,7 +49,7 @@ class Trainer:
     """Owns model, optimizer, EMA and preparer for one rank; ``train_step`` runs one update."""
 
     def __init__(self, cfg: RunConfig, tp=1, lr=5e-5, warmup=0, total_steps=0, lr_style="cosine",
-                 ema_decay=0.999, bucket_size=40_000_000, overlap=False, seed=871, device=None,
+                 ema_decay=0.999, bucket_size=40_000_000, overlap=None, seed=871, device=None,
                  dtype=torch.bfloat16, fused_tp=True):
         self.state = ps.initialize(tp) if ps.state().tp != tp or not dist.is_initialized() else ps.state()
         self.device = torch.device(device) if device is not None else self.state.device
@@ -57,6 +57,8 @@ class Trainer:
         self.cfg = cfg
         self.lr, self.warmup, self.total_steps, self.lr_style = lr, warmup, total_steps, lr_style
         self.model = build_model(cfg, self.device, seed, dtype)
+        if overlap is None:   # launch each DP bucket's reduce-scatter during backward once it is complete
+            overlap = self.state.dp > 1
         self.optimizer = DistributedOptimizer(self.model, lr, bucket_size=bucket_size, overlap=overlap)
         self.ema = RendererEMA(self.model, self.optimizer, ema_decay) if ema_decay else None
         self.preparer = DevicePreparer(cfg, self.device, dtype)

@@ -163,7 +163,35 @@ def test_validation_probes_layout():
     trainer = Trainer(tiny_config(), tp=1, lr=1e-3, device="cpu", dtype=torch.float32)
     probes = validation_probes(trainer.model, trainer.optimizer)
     names = [name for name, _, _ in probes["layout"]]
-    assert names[0].startswith("model/") and any(n.startswith("adam/") for n in names)
+    assert names[0].startswith("model/") and any(n.startswith("exp_avg/") for n in names)
     assert probes["values"].numel() == sum(c for _, _, c in probes["layout"])
     again = validation_probes(trainer.model, trainer.optimizer)
     assert torch.equal(probes["values"], again["values"])
+
+
+def _dp_worker(rank, world, tp, store, out):
+    st = _init(rank, world, tp, store)
+    from cq_pretrain_b200.train.trainer import Trainer
+    batch = _batch(st)
+    results = {}
+    for overlap in (False, True):
+        trainer = Trainer(_cfg(), tp=tp, lr=1e-3, ema_decay=0.9, device="cpu", dtype=torch.float32, seed=5,
+                          overlap=overlap)
+        losses = [trainer.train_step([batch])["loss"] for _ in range(3)]
+        params = torch.cat([p.detach().flatten() for p in trainer.model.parameters()])
+        results[overlap] = (losses, params)
+    gathered = [None] * world
+    dist.all_gather_object(gathered, results[True][1])
+    if rank == 0:
+        torch.save(dict(plain=results[False], overlap=results[True], ranks=gathered), out)
+    dist.destroy_process_group()
+
+
+def test_data_parallel_overlap_matches_serial_dp2():
+    with tempfile.TemporaryDirectory() as tmp:
+        out = Path(tmp) / "dp.pt"
+        _spawn(_dp_worker, 2, 1, str(Path(tmp) / "store"), str(out))
+        r = torch.load(out, weights_only=False)
+    assert r["plain"][0] == r["overlap"][0]
+    assert torch.equal(r["plain"][1], r["overlap"][1])
+    assert torch.equal(r["ranks"][0], r["ranks"][1])   # DP replicas hold identical parameters
