@@ -117,6 +117,8 @@ class ModelConfig(RuntimeConfig):
         need(self.visual_query_mode in ("fixed", "native"), "visual_query_mode must be fixed or native")
         need(self.gdn_backend in GDN_BACKENDS, f"gdn_backend must be one of {GDN_BACKENDS}")
         need(self.renderer in ("wan", "legacy"), "renderer must be wan or legacy")
+        need(not ((self.renderer == "legacy" or self.vision_encoder == "rgb_patch") and tp > 1),
+             "the legacy renderer and RGB patch embedding run replicated (TP = 1)")
         if self.renderer == "wan":
             need(self.flow_draws == 1 and self.latent_channels == 16, "Wan uses one flow draw and 16-channel latents")
         q = self.image_condition_queries

@@ -100,6 +100,7 @@ class Packer:
         rope = np.zeros((3, s), np.float32)
         image_queries = np.zeros(s, bool)
         text_indices, spans, grids, features, latent_grids, latents = [], [], [], [], [], []
+        pixels = []
         gen_indices, gen_uncond = [], []
         records = []
         position = seg = body = 0
@@ -190,6 +191,7 @@ class Packer:
                 spans.append(visual)
                 grids.append(tuple(e["grid"]))
                 features.append(e.get("features"))
+                pixels.append(e.get("pixels"))
                 cursor += int(layout["positions"].max()) + 1
                 position = stop
                 self.element += 1
@@ -223,13 +225,19 @@ class Packer:
             if all(f is not None for f in features):
                 feats = torch.cat([torch.as_tensor(f) for f in features])
             vision = VisionInputs(tuple(grids), torch.from_numpy(np.concatenate(spans)), feats)
+            if pixels and all(px is not None for px in pixels):
+                vision.pixel_values = torch.stack([torch.as_tensor(px).float() for px in pixels])
         batch = Batch(ids=torch.from_numpy(ids[None]), segments=torch.from_numpy(segment[None]),
                       sigma=torch.from_numpy(sigma[None]), positions=torch.from_numpy(rope),
                       text_indices=torch.tensor(sorted(text_indices), dtype=torch.long),
                       image_indices=torch.from_numpy(indices), image_queries=torch.from_numpy(image_queries[None]),
                       vision=vision, generation_image_indices=torch.tensor(gen_indices, dtype=torch.long),
                       generation_unconditional=torch.tensor(gen_uncond, dtype=torch.bool))
-        if gen_indices:
+        if gen_indices and cfg.renderer == "legacy":
+            # legacy flow renderer: one [tokens, C] latent grid per target (no 2x2 patching)
+            if all(z is not None for z in latents):
+                batch.latents = torch.stack([torch.as_tensor(z).float().reshape(z.shape[0], -1).T for z in latents])
+        elif gen_indices:
             counts = [visual_query_count(grids[i], cfg) for i in gen_indices]
             batch.generation = WanGenerationInputs.prepare(latent_grids, counts, cfg.dit_head_dim,
                                                            cfg.generation_token_budget, cfg.generation_microbatch_images)

@@ -41,10 +41,17 @@ class DevicePreparer:
 
     def randomness(self, batch, receipt):
         layout = batch.generation
-        if layout is None:
+        legacy = self.cfg.renderer == "legacy" and batch.latents is not None
+        if layout is None and not legacy:
             return None
         signature = receipt["next_state"]["documents"].get("signature") or dict(snapshot="synthetic", seed=0, epoch=0, rank=0)
         gen = torch.Generator().manual_seed(consumption_seed(signature, receipt["serial"]))
+        if legacy:   # flow_draws noise draws per target, times ~ logit-normal
+            n, tokens, channels = batch.latents.shape
+            draws = self.cfg.flow_draws
+            noise = torch.randn(draws * n, tokens, channels, generator=gen)
+            times = torch.randn(draws * n, generator=gen).sigmoid().clamp(1e-5, 1 - 1e-5)
+            return noise, times, None
         noise = torch.randn(sum(layout.lengths), self.cfg.latent_channels * 4, generator=gen)
         times = torch.randn(len(layout.lengths), generator=gen).sigmoid().clamp(1e-5, 1 - 1e-5)
         return noise, times, time_features(times, self.cfg.wan_freq_dim)
@@ -54,7 +61,8 @@ class DevicePreparer:
         if extra is not None:
             noise, times, feats = extra
             batch.noise, batch.times = noise, times
-            batch.generation.time_features = feats
+            if batch.generation is not None:
+                batch.generation.time_features = feats
             if batch.latents is None:
                 raise ValueError("generation targets need latents (cached or encoded)")
         out = batch.to(self.device, non_blocking=non_blocking)

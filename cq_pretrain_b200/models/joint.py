@@ -40,11 +40,18 @@ class JointModel(nn.Module):
         self.embedding = PL.VocabEmbedding(cfg.vocab_size, cfg.width)
         self.layers = nn.ModuleList([QwenBlock(cfg, i) for i in range(cfg.layers)])
         self.final_norm = RMSNorm(cfg.width, cfg.norm_eps)
-        self.renderer = Wan21Generator(cfg)
+        if cfg.renderer == "legacy":
+            from .legacy import FlowRenderer
+            self.renderer = FlowRenderer(cfg)
+        else:
+            self.renderer = Wan21Generator(cfg)
         self.lm_head = None if cfg.tie_word_embeddings else OutputHead(cfg)
         if cfg.vision_encoder == "qwen35":
             from .vision import VisionTower, vision_config
             self.patch_embed = VisionTower(vision_config(cfg), cfg.width, cfg.freeze_vision, cfg.freeze_vision_merger)
+        elif cfg.vision_encoder == "rgb_patch":
+            from .legacy import RGBPatchLinear
+            self.patch_embed = RGBPatchLinear(cfg.width, cfg.patch_size)
         else:
             self.patch_embed = None
 
@@ -64,6 +71,9 @@ class JointModel(nn.Module):
                 feats = vision.features.to(partial.dtype)
             elif vision.layout is not None and self.patch_embed is not None:
                 feats = self.patch_embed(vision.layout).to(partial.dtype)
+            elif vision.pixel_values is not None and cfg.vision_encoder == "rgb_patch":
+                pixels = vision.pixel_values.to(self.patch_embed.weight.dtype)
+                feats = self.patch_embed(pixels).reshape(-1, cfg.width).to(partial.dtype)
             else:
                 raise ValueError("visual content needs merger features (cached) or pixels for the vision tower")
             if ps.tp_size() > 1 and ps.tp_rank() != 0:
