@@ -45,6 +45,12 @@ at::Tensor symm_view(int64_t base, int64_t offset, std::vector<int64_t> shape, a
 void signal_wait(at::Tensor peer_flag_ptrs, int64_t my_flags, int64_t rank, int64_t tp, int64_t epoch, bool wait);
 at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp, int64_t rows, int64_t cols);
 int comm_status_read(bool reset);
+std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_recv, int64_t my_recv,
+                                   at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
+                                   int64_t epoch, int64_t total_dim, double eps);
+std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor peer_recv,
+                                   int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
+                                   int64_t max_rows, int64_t epoch, int64_t total_dim);
 // gdn.cu
 std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                                 at::Tensor start, at::Tensor count);
@@ -105,6 +111,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("signal_wait", &cqb::signal_wait);
   m.def("rs_reduce", &cqb::rs_reduce);
   m.def("comm_status_read", &cqb::comm_status_read, py::arg("reset") = false);
+  m.def("tp_rms_fwd", &cqb::tp_rms_fwd);
+  m.def("tp_rms_bwd", &cqb::tp_rms_bwd);
   m.def("gdn_fwd", &cqb::gdn_fwd);
   m.def("gdn_bwd", &cqb::gdn_bwd);
   m.def("attn_fwd", &cqb::attn_fwd);

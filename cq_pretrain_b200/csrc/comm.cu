@@ -71,6 +71,162 @@ __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, const _
   }
 }
 
+
+// ---- TP RMSNorm with the cross-rank variance exchanged in-kernel ----------------------------
+// Rows of x hold this rank's slice of a full-width vector (heads spread over TP). Per block of
+// 64 rows: each warp sums its rows' local squares (fwd) or dy.w.x (bwd); the 64 partials are
+// stored into slot `rank` of every peer's receive slab (plain peer stores), a system-scope
+// release flag per (block, rank) publishes them, and after acquiring the peers' flags for the
+// same block (bounded wait) the block reduces the tp partials and finishes its rows. The grid
+// is persistent (<= one CTA per SM) and every rank walks the blocks in the same order.
+constexpr int STAT_ROWS = 64;          // rows per block
+constexpr int STAT_MAX_TP = 8;
+
+struct TpNormArgs {
+  const __nv_bfloat16* x;
+  int ld_x;
+  const __nv_bfloat16* dy;   // backward only (contiguous [rows, D])
+  const float* w;            // [D] fp32
+  __nv_bfloat16* y;          // fwd: y; bwd: dx (contiguous [rows, D])
+  float* rstd;               // [rows]
+  float* dw_partial;         // bwd: [gridDim.x, D]
+  int rows, D;
+  float inv_total, eps;
+  float* const* peer_recv;   // [tp] slab base of each peer (this call's parity): [tp][max_rows] fp32
+  float* my_recv;
+  long long* const* peer_flags;  // [tp] flag area of each peer: [blocks][STAT_MAX_TP]
+  long long* my_flags;
+  int rank, tp, max_rows;
+  long long epoch;
+  int* status;
+};
+
+template <bool BWD>
+__global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
+  __shared__ float part[STAT_ROWS];
+  __shared__ float stat[STAT_ROWS];
+  __shared__ int failed;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blocks = (a.rows + STAT_ROWS - 1) / STAT_ROWS;
+  float dw_acc[4][8];
+  if (BWD) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dw_acc[i][j] = 0.f;
+  }
+  if (threadIdx.x == 0) failed = 0;
+  for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
+    // 1) local partials: warp w handles rows 8w..8w+7 of the block
+    for (int rr = 0; rr < 8; ++rr) {
+      const int lr = warp * 8 + rr, row = b * STAT_ROWS + lr;
+      float acc = 0.f;
+      if (row < a.rows) {
+        for (int c = lane * 8; c < a.D; c += 256) {
+          float xv[8];
+          load8(a.x + (size_t)row * a.ld_x + c, xv);
+          if (BWD) {
+            float dv[8], wv[8];
+            load8(a.dy + (size_t)row * a.D + c, dv);
+            load8(a.w + c, wv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += dv[j] * wv[j] * xv[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += xv[j] * xv[j];
+          }
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) part[lr] = acc;
+    }
+    __syncthreads();
+    // 2) publish to every peer (including this rank's own slab)
+    if (threadIdx.x < STAT_ROWS * a.tp) {
+      const int t = threadIdx.x / STAT_ROWS, lr = threadIdx.x % STAT_ROWS;
+      a.peer_recv[t][(size_t)a.rank * a.max_rows + b * STAT_ROWS + lr] = part[lr];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < a.tp) st_release_sys(a.peer_flags[threadIdx.x] + (size_t)b * STAT_MAX_TP + a.rank, a.epoch);
+    // 3) acquire the peers' partials of this block
+    if (threadIdx.x < a.tp) {
+      const long long* f = a.my_flags + (size_t)b * STAT_MAX_TP + threadIdx.x;
+      const unsigned long long start = tc::globaltimer();
+      while (ld_acquire_sys(f) < a.epoch) {
+        if (tc::globaltimer() - start > tc::kWaitNs) {
+          atomicCAS(a.status, 0, 200 + threadIdx.x);
+          failed = 1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    if (failed) return;   // the host reads the status word; outputs of this call are invalid
+    if (threadIdx.x < STAT_ROWS) {
+      float sum = 0.f;
+      for (int t = 0; t < a.tp; ++t) sum += a.my_recv[(size_t)t * a.max_rows + b * STAT_ROWS + threadIdx.x];
+      stat[threadIdx.x] = sum;
+    }
+    __syncthreads();
+    // 4) finish the rows
+    for (int rr = 0; rr < 8; ++rr) {
+      const int lr = warp * 8 + rr, row = b * STAT_ROWS + lr;
+      if (row >= a.rows) continue;
+      float r;
+      if (!BWD) {
+        r = rsqrtf(stat[lr] * a.inv_total + a.eps);
+        if (lane == 0) a.rstd[row] = r;
+      } else {
+        r = a.rstd[row];
+      }
+      const float g = BWD ? stat[lr] * r * r * r * a.inv_total : 0.f;
+      int k = 0;
+      for (int c = lane * 8; c < a.D; c += 256, ++k) {
+        float xv[8], wv[8], o[8];
+        load8(a.x + (size_t)row * a.ld_x + c, xv);
+        load8(a.w + c, wv);
+        if (!BWD) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = xv[j] * r * wv[j];
+        } else {
+          float dv[8];
+          load8(a.dy + (size_t)row * a.D + c, dv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            o[j] = dv[j] * wv[j] * r - xv[j] * g;
+            if (k < 4) dw_acc[k][j] += dv[j] * xv[j] * r;
+          }
+        }
+        store8(a.y + (size_t)row * a.D + c, o);
+      }
+    }
+    __syncthreads();   // part/stat reused by the next block
+  }
+  if (BWD) {
+    // dw partial of this CTA: reduce the 8 warps through shared memory (fixed order)
+    __shared__ float red[8][4 * 256];
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[warp][k * 256 + lane * 8 + j] = dw_acc[k][j];
+    __syncthreads();
+    for (int c = threadIdx.x; c < a.D; c += blockDim.x) {
+      const int k = c / 256, off = c % 256;
+      float sum = 0.f;
+      for (int wi = 0; wi < 8; ++wi) sum += red[wi][k * 256 + off];
+      a.dw_partial[(size_t)blockIdx.x * a.D + c] = sum;
+    }
+  }
+}
+
+__global__ void column_sum_kernel(const float* __restrict__ partial, int rows, int cols, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int r = 0; r < rows; ++r) s += partial[(size_t)r * cols + c];
+  out[c] = s;
+}
+
 int* comm_status() {
   static int* word = [] {
     int* p = nullptr;
@@ -139,6 +295,81 @@ at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp
   CQB_LAUNCH_CHECK();
   count_launch();
   return out;
+}
+
+
+namespace {
+TpNormArgs tp_norm_args(const at::Tensor& x, const at::Tensor& w, at::Tensor peer_recv, int64_t my_recv,
+                        at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
+                        int64_t epoch, int64_t total_dim, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 &&
+                  x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "x: bf16 [rows, D] with 16-byte aligned rows");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.numel() == x.size(1), "w: fp32 [D]");
+  TORCH_CHECK(x.size(1) % 8 == 0 && x.size(1) <= 1024, "D must be a multiple of 8 and <= 1024");
+  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && x.size(0) <= max_rows, "rows exceed the exchange slab");
+  TpNormArgs a{};
+  a.x = (const __nv_bfloat16*)x.data_ptr();
+  a.ld_x = (int)x.stride(0);
+  a.w = w.data_ptr<float>();
+  a.rows = (int)x.size(0);
+  a.D = (int)x.size(1);
+  a.inv_total = 1.f / (float)total_dim;
+  a.eps = (float)eps;
+  a.peer_recv = reinterpret_cast<float* const*>(peer_recv.data_ptr());
+  a.my_recv = reinterpret_cast<float*>(my_recv);
+  a.peer_flags = reinterpret_cast<long long* const*>(peer_flags.data_ptr());
+  a.my_flags = reinterpret_cast<long long*>(my_flags);
+  a.rank = (int)rank;
+  a.tp = (int)tp;
+  a.max_rows = (int)max_rows;
+  a.epoch = epoch;
+  a.status = comm_status();
+  return a;
+}
+int tp_norm_grid(int rows) { return std::max(1, std::min((rows + STAT_ROWS - 1) / STAT_ROWS, sm_count())); }
+}  // namespace
+
+// y = x * rsqrt(sum_over_ranks(x^2) / total_dim + eps) * w; returns (y, rstd).
+std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_recv, int64_t my_recv,
+                                   at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
+                                   int64_t epoch, int64_t total_dim, double eps) {
+  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, eps);
+  auto y = at::empty({x.size(0), x.size(1)}, x.options());
+  auto rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  a.y = (__nv_bfloat16*)y.data_ptr();
+  a.rstd = rstd.data_ptr<float>();
+  if (a.rows) {
+    tp_norm_kernel<false><<<tp_norm_grid(a.rows), 256, 0, stream()>>>(a);
+    CQB_LAUNCH_CHECK();
+    count_launch();
+  }
+  return {y, rstd};
+}
+
+// Backward: returns (dx, dw fp32 [D]); the row dot products dy.w.x are summed over ranks.
+std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor peer_recv,
+                                   int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
+                                   int64_t max_rows, int64_t epoch, int64_t total_dim) {
+  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, 0.0);
+  auto dyc = dy.contiguous();
+  TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.sizes() == x.sizes(), "dy like x");
+  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() == x.size(0), "rstd: fp32 [rows]");
+  auto dx = at::empty({x.size(0), x.size(1)}, x.options());
+  auto dw = at::zeros({x.size(1)}, x.options().dtype(at::kFloat));
+  if (!a.rows) return {dx, dw};
+  const int grid = tp_norm_grid(a.rows);
+  auto partial = at::empty({grid, x.size(1)}, dw.options());
+  a.dy = (const __nv_bfloat16*)dyc.data_ptr();
+  a.y = (__nv_bfloat16*)dx.data_ptr();
+  a.rstd = rstd.data_ptr<float>();
+  a.dw_partial = partial.data_ptr<float>();
+  tp_norm_kernel<true><<<grid, 256, 0, stream()>>>(a);
+  CQB_LAUNCH_CHECK();
+  column_sum_kernel<<<(a.D + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), grid, a.D, dw.data_ptr<float>());
+  CQB_LAUNCH_CHECK();
+  count_launch(2);
+  return {dx, dw};
 }
 
 int comm_status_read(bool reset) {

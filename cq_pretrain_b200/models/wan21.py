@@ -43,11 +43,35 @@ class WanRMSNorm(nn.Module):
         self.weight = PL.mark_sharded(nn.Parameter(torch.ones(width // ps.tp_size())))
 
     def forward(self, x):
+        if ps.tp_size() > 1:
+            from ..parallel import symmetric
+            ws = symmetric.workspace()
+            if ws is not None and ws.supports_rms(x):
+                # in-kernel exchange of the per-row sums of squares over NVLink (no NCCL call)
+                return _TPRMSNorm.apply(x, self.weight, ws, x.shape[-1] * ps.tp_size(), self.eps)
         sq = x.float().square().sum(-1, keepdim=True)
         if ps.tp_size() > 1:
             sq = PL.reduce_tp(sq)
         variance = sq / (x.shape[-1] * ps.tp_size())
         return (x.float() * torch.rsqrt(variance + self.eps)).to(x.dtype) * self.weight.to(x.dtype)
+
+
+class _TPRMSNorm(torch.autograd.Function):
+    """RMSNorm over a width split across TP ranks; both passes exchange per-row sums in-kernel."""
+
+    @staticmethod
+    def forward(ctx, x, weight, ws, total_dim, eps):
+        w = weight.float().contiguous()
+        y, rstd = ws.rms_forward(x, w, total_dim, eps)
+        ctx.save_for_backward(x, w, rstd)
+        ctx.ws, ctx.total_dim, ctx.wdtype = ws, total_dim, weight.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dx, dw = ctx.ws.rms_backward(dy.to(torch.bfloat16), x, w, rstd, ctx.total_dim)
+        return dx, dw.to(ctx.wdtype), None, None, None
 
 
 class Attention(nn.Module):

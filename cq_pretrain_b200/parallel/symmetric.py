@@ -7,6 +7,8 @@ handles, and opens every peer's buffer (NVLink P2P). Layout::
     [512, 1024)     reduce-scatter flags: slot s = last epoch rank s finished storing partials
     send[0], send[1]   this rank's staged shard for all-gather (double-buffered by epoch parity)
     recv[0], recv[1]   [tp, rows/tp, N] partial slabs written by peers for reduce-scatter
+    stat flags         [row blocks][8] epoch flags of the row-statistic exchange (TP RMSNorm)
+    stat[0], stat[1]   [tp, max_rows] fp32 per-row partials written by peers (parity buffered)
 
 Protocol (epochs count calls of each kind; every rank issues the same sequence):
 
@@ -16,6 +18,9 @@ Protocol (epochs count calls of each kind; every rank issues the same sequence):
 * GEMM -> reduce-scatter (epoch e): one GEMM kernel stores every output tile into the owner's
   ``recv[e % 2][src]``; a one-block kernel publishes flag e and acquires all peers' flags; a
   bandwidth kernel sums the tp slabs.
+* row statistics (epoch e, Wan's full-width Q/K RMSNorm): one kernel per call; each 64-row block
+  stores its partial sums into ``stat[e % 2][rank]`` of every peer, publishes a per-block flag and
+  acquires the peers' flags of the same block before normalising its rows.
 
 Double buffering plus the flag order makes buffer reuse safe: a rank can only overwrite a slot
 of parity p at epoch e after every peer has signalled epoch e-1, which each peer does only after
@@ -40,7 +45,7 @@ def _align(n, a=4096):
 
 
 class SymmetricWorkspace:
-    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192):
+    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192, stat_rows=65536):
         st = ps.state()
         if st.tp < 2:
             raise ValueError("symmetric workspace needs TP >= 2")
@@ -49,7 +54,13 @@ class SymmetricWorkspace:
         self.send_bytes, self.recv_bytes = _align(send_bytes), _align(recv_bytes)
         self.off_send = [FLAG_BYTES * 4, FLAG_BYTES * 4 + self.send_bytes]
         self.off_recv = [self.off_send[1] + self.send_bytes, self.off_send[1] + self.send_bytes + self.recv_bytes]
-        total = self.off_recv[1] + self.recv_bytes
+        self.stat_rows = stat_rows
+        stat_blocks = -(-stat_rows // 64)
+        self.off_stat_flags = self.off_recv[1] + self.recv_bytes
+        stat_bytes = _align(self.tp * stat_rows * 4)
+        self.off_stat = [self.off_stat_flags + _align(stat_blocks * 8 * 8), 0]
+        self.off_stat[1] = self.off_stat[0] + stat_bytes
+        total = self.off_stat[1] + stat_bytes
         ptr, handle = ops.symm_alloc(total)
         self.base = int(ptr[0])
         handles = [None] * self.tp
@@ -67,6 +78,9 @@ class SymmetricWorkspace:
         self.flag_rs = as_dev([b + 512 for b in bases])
         self.send = [as_dev([b + self.off_send[p] for b in bases]) for p in range(2)]
         self.recv = [as_dev([b + self.off_recv[p] for b in bases]) for p in range(2)]
+        self.stat_flags = as_dev([b + self.off_stat_flags for b in bases])
+        self.stat = [as_dev([b + self.off_stat[p] for b in bases]) for p in range(2)]
+        self.epoch_stat = 0
         # one publication flag per 16 gathered rows (the all-gather copy unit)
         self.chunk_flags = torch.zeros(max_subchunks, dtype=torch.int64, device=dev)
         self.epoch_ag = 0
@@ -120,6 +134,26 @@ class SymmetricWorkspace:
         ops.signal_wait(self.flag_rs, self.base + 512, self.rank, self.tp, e, True)
         recv = ops.symm_view(self.base, self.off_recv[p], [self.tp, rows, n_out], torch.bfloat16)
         return ops.rs_reduce(recv, None, self.tp, rows, n_out)
+
+    # ---- row statistics ----------------------------------------------------------------------
+    def supports_rms(self, x):
+        return (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+                and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and x.shape[1] % 8 == 0
+                and x.shape[1] <= 1024 and x.shape[0] <= self.stat_rows)
+
+    def rms_forward(self, x, weight, total_dim, eps):
+        self.epoch_stat += 1
+        e, p = self.epoch_stat, self.epoch_stat % 2
+        return _ext.ops().tp_rms_fwd(x, weight, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
+                                     self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e,
+                                     total_dim, eps)
+
+    def rms_backward(self, dy, x, weight, rstd, total_dim):
+        self.epoch_stat += 1
+        e, p = self.epoch_stat, self.epoch_stat % 2
+        return _ext.ops().tp_rms_bwd(dy, x, weight, rstd, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
+                                     self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e,
+                                     total_dim)
 
     def linear_scatter(self, x, weight):
         """``reduce_scatter_rows(x @ W^T)`` with the GEMM storing tiles into the owners' buffers."""

@@ -6,6 +6,7 @@ import tempfile
 
 import pytest
 import torch
+import torch.distributed as dist
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
@@ -46,6 +47,24 @@ def _worker(rank, world, port, out):
         d = ws.matmul_scatter(dy, w3)
         dref = fused.scatter_rows_raw(gemm.matmul_nn(dy, w3))
         errors.append(float((d.float() - dref.float()).abs().max() / dref.float().abs().max()))
+        # Wan full-width RMSNorm: in-kernel exchange of the per-row sums vs NCCL all-reduce
+        from cq_pretrain_b200.models.wan21 import WanRMSNorm
+        norm = WanRMSNorm(384 * world, 1e-6).cuda()
+        with torch.no_grad():
+            norm.weight.copy_(1 + 0.1 * torch.randn_like(norm.weight))
+        xq = torch.randn(1000 + it, 384, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        yq = norm(xq)
+        gq = torch.randn_like(yq)
+        yq.backward(gq)
+        xr = xq.detach().float().requires_grad_()
+        wr = norm.weight.detach().float().requires_grad_()
+        sq = xr.square().sum(-1, keepdim=True)
+        dist.all_reduce(sq)   # reference: the NCCL all-reduce the fused kernel replaces
+        yr = xr * torch.rsqrt(sq / (384 * world) + 1e-6) * wr
+        yr.backward(gq.float())
+        errors.append(float((yq.float() - yr).abs().max() / yr.abs().max()))
+        errors.append(float((xq.grad.float() - xr.grad).norm() / xr.grad.norm()))
+        errors.append(float((norm.weight.grad.float() - wr.grad).norm() / wr.grad.norm()))
     torch.cuda.synchronize()
     status = symmetric.status()
     symmetric.disable()
