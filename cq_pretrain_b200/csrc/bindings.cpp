@@ -22,6 +22,7 @@ std::vector<at::Tensor> ln_modulate_bwd(at::Tensor dy, at::Tensor x, at::Tensor 
 at::Tensor gated_add_fwd(at::Tensor x, at::Tensor branch, at::Tensor gate, at::Tensor idx);
 std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tensor gate, at::Tensor idx);
 at::Tensor swiglu_fwd(at::Tensor x);
+at::Tensor column_sum(at::Tensor x);
 at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x);
 // gemm.cu
 at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
@@ -94,6 +95,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_add_fwd", &cqb::gated_add_fwd);
   m.def("gated_add_bwd", &cqb::gated_add_bwd);
   m.def("swiglu_fwd", &cqb::swiglu_fwd);
+  m.def("column_sum", &cqb::column_sum);
   m.def("swiglu_bwd", &cqb::swiglu_bwd);
   m.def("gemm_nt", &cqb::gemm_nt, py::arg("x"), py::arg("w"), py::arg("bias") = py::none());
   m.def("gemm_nn", &cqb::gemm_nn);

@@ -288,89 +288,6 @@ __global__ void __launch_bounds__(256) lnmod_fwd_kernel(const T* __restrict__ x,
   }
 }
 
-// Flush per-warp accumulators of modulation-row `m` into global fp32 gradients.
-template <int NV>
-__device__ __forceinline__ void flush(float (&a)[NV][8], float* dst, int lane, int width) {
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * 32 + lane) * 8;
-    if (c < width)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (a[i][j] != 0.f) atomicAdd(dst + c + j, a[i][j]);
-        a[i][j] = 0.f;
-      }
-  }
-}
-
-template <int NV, typename T>
-__global__ void __launch_bounds__(256) lnmod_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const T* __restrict__ x,
-                                                       const float* __restrict__ scale, const int* __restrict__ idx,
-                                                       const float* __restrict__ mean, const float* __restrict__ rstd,
-                                                       T* __restrict__ dx, float* __restrict__ dscale,
-                                                       float* __restrict__ dshift, int rows, int width, int per) {
-  const int warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int r0 = warp * per, r1 = min(rows, r0 + per);
-  if (r0 >= rows) return;
-  float as[NV][8], ah[NV][8];
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) as[i][j] = ah[i][j] = 0.f;
-  int cur = idx[r0];
-  for (int row = r0; row < r1; ++row) {
-    const int m = idx[row];
-    if (m != cur) {
-      flush<NV>(as, dscale + (size_t)cur * width, lane, width);
-      flush<NV>(ah, dshift + (size_t)cur * width, lane, width);
-      cur = m;
-    }
-    const float mu = mean[row], r = rstd[row];
-    const size_t off = (size_t)row * width, mo = (size_t)m * width;
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = (i * 32 + lane) * 8;
-      if (c < width) {
-        float xv[8], gv[8], sc[8];
-        load_vec(x + off + c, xv);
-        load8(dy + off + c, gv);
-        load8(scale + mo + c, sc);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = (xv[j] - mu) * r;
-          const float dn = gv[j] * (1.f + sc[j]);
-          as[i][j] += gv[j] * xh;
-          ah[i][j] += gv[j];
-          s1 += dn;
-          s2 += dn * xh;
-        }
-      }
-    }
-    s1 = warp_sum(s1) / width;
-    s2 = warp_sum(s2) / width;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = (i * 32 + lane) * 8;
-      if (c < width) {
-        float xv[8], gv[8], sc[8], o[8];
-        load_vec(x + off + c, xv);
-        load8(dy + off + c, gv);
-        load8(scale + mo + c, sc);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = (xv[j] - mu) * r;
-          o[j] = r * (gv[j] * (1.f + sc[j]) - s1 - xh * s2);
-        }
-        store8(dx + off + c, o);
-      }
-    }
-  }
-  flush<NV>(as, dscale + (size_t)cur * width, lane, width);
-  flush<NV>(ah, dshift + (size_t)cur * width, lane, width);
-}
-
 template <typename BT>
 __global__ void gated_add_fwd_kernel(const float* __restrict__ x, const BT* __restrict__ branch,
                                      const float* __restrict__ gate, const int* __restrict__ idx,
@@ -389,46 +306,163 @@ __global__ void gated_add_fwd_kernel(const float* __restrict__ x, const BT* __re
   }
 }
 
-template <int NV, typename BT>
-__global__ void __launch_bounds__(256) gated_add_bwd_kernel(const float* __restrict__ dy, const BT* __restrict__ branch,
-                                                           const float* __restrict__ gate, const int* __restrict__ idx,
-                                                           BT* __restrict__ dbranch, float* __restrict__ dgate, int rows,
-                                                           int width, int per) {
-  const int warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int r0 = warp * per, r1 = min(rows, r0 + per);
-  if (r0 >= rows) return;
-  float ag[NV][8];
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ag[i][j] = 0.f;
+
+// ---- per-sample column sums of the modulation backward -------------------------------------
+// dscale[m, c] = sum_{rows of sample m} dy * xhat (MODE 0, with dshift = sum dy) or
+// dgate[m, c] = sum dy * branch (MODE 1). Block (32, 8): x -> 8 columns, y -> a run of MOD_RB
+// rows; each thread accumulates its rows (flushing on a sample change) and adds its totals with
+// one atomic per column, so a [2048, 1536] input uses ~1500 blocks instead of a few long warps.
+constexpr int MOD_RB = 16;
+
+template <int MODE, typename AT>
+__global__ void __launch_bounds__(256) mod_colsum_kernel(const float* __restrict__ dy32,
+                                                         const __nv_bfloat16* __restrict__ dy16,
+                                                         const AT* __restrict__ a, const int* __restrict__ idx,
+                                                         const float* __restrict__ mean,
+                                                         const float* __restrict__ rstd, float* __restrict__ out_a,
+                                                         float* __restrict__ out_b, int rows, int width) {
+  const int c = (blockIdx.x * 32 + threadIdx.x) * 8;
+  if (c >= width) return;
+  const int r0 = (blockIdx.y * 8 + threadIdx.y) * MOD_RB;
+  const int r1 = min(rows, r0 + MOD_RB);
+  if (r0 >= r1) return;
+  float sa[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   int cur = idx[r0];
+  auto flush = [&](int m) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      atomicAdd(out_a + (size_t)m * width + c + j, sa[j]);
+      if (MODE == 0) atomicAdd(out_b + (size_t)m * width + c + j, sb[j]);
+      sa[j] = sb[j] = 0.f;
+    }
+  };
   for (int row = r0; row < r1; ++row) {
     const int m = idx[row];
     if (m != cur) {
-      flush<NV>(ag, dgate + (size_t)cur * width, lane, width);
+      flush(cur);
       cur = m;
     }
+    float g[8], av[8];
+    if (dy32) load8(dy32 + (size_t)row * width + c, g);
+    else load8(dy16 + (size_t)row * width + c, g);
+    load_vec(a + (size_t)row * width + c, av);
+    if (MODE == 0) {
+      const float mu = mean[row], r = rstd[row];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sa[j] += g[j] * (av[j] - mu) * r;
+        sb[j] += g[j];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sa[j] += g[j] * av[j];
+    }
+  }
+  flush(cur);
+}
+
+// dx of the modulated LayerNorm, one warp per row (grid-stride).
+template <int NV, typename T>
+__global__ void __launch_bounds__(256) lnmod_dx_kernel(const __nv_bfloat16* __restrict__ dy, const T* __restrict__ x,
+                                                      const float* __restrict__ scale, const int* __restrict__ idx,
+                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                      T* __restrict__ dx, int rows, int width) {
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kWarps) {
+    const int m = idx[row];
+    const float mu = mean[row], r = rstd[row];
     const size_t off = (size_t)row * width, mo = (size_t)m * width;
+    float xv[NV][8], gv[NV][8], sc[NV][8];
+    float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = (i * 32 + lane) * 8;
       if (c < width) {
-        float gv[8], bv[8], gt[8], o[8];
-        load8(dy + off + c, gv);
-        load_vec(branch + off + c, bv);
-        load8(gate + mo + c, gt);
+        load_vec(x + off + c, xv[i]);
+        load8(dy + off + c, gv[i]);
+        load8(scale + mo + c, sc[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          ag[i][j] += gv[j] * bv[j];
-          o[j] = gv[j] * gt[j];
+          const float dn = gv[i][j] * (1.f + sc[i][j]);
+          s1 += dn;
+          s2 += dn * (xv[i][j] - mu) * r;
         }
-        store8(dbranch + off + c, o);
+      }
+    }
+    s1 = warp_sum(s1) / width;
+    s2 = warp_sum(s2) / width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = (xv[i][j] - mu) * r;
+          o[j] = r * (gv[i][j] * (1.f + sc[i][j]) - s1 - xh * s2);
+        }
+        store8(dx + off + c, o);
       }
     }
   }
-  flush<NV>(ag, dgate + (size_t)cur * width, lane, width);
+}
+
+// dbranch = dy * gate[sample]
+template <typename BT>
+__global__ void gated_add_dbranch_kernel(const float* __restrict__ dy, const float* __restrict__ gate,
+                                         const int* __restrict__ idx, BT* __restrict__ dbranch, int rows, int width) {
+  const size_t vecs = (size_t)rows * width / 8;
+  for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < vecs; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;
+    const int row = (int)(e / width), c = (int)(e % width);
+    float g[8], gt[8], o[8];
+    load8(dy + e, g);
+    load8(gate + (size_t)idx[row] * width + c, gt);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = g[j] * gt[j];
+    store8(dbranch + e, o);
+  }
+}
+
+
+// Column sums of a bf16 / fp32 matrix (bias gradients) without an fp32 copy: block (32, 8)
+// reduces 8 x BIAS_RB rows of 256 columns into partial[blockIdx.y]; a second pass adds the
+// partials in a fixed order (deterministic).
+constexpr int BIAS_RB = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict__ x, int rows, int cols,
+                                                             float* __restrict__ partial) {
+  __shared__ float red[8][256 + 8];
+  const int c = (blockIdx.x * 32 + threadIdx.x) * 8;
+  const int r0 = (blockIdx.y * 8 + threadIdx.y) * BIAS_RB;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c < cols)
+    for (int r = r0; r < min(rows, r0 + BIAS_RB); ++r) {
+      float v[8];
+      load_vec(x + (size_t)r * cols + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[threadIdx.y][threadIdx.x * 8 + j] = acc[j];
+  __syncthreads();
+  const int t = threadIdx.y * 32 + threadIdx.x;   // 256 threads -> 256 columns of the block
+  const int col = blockIdx.x * 256 + t;
+  if (col < cols) {
+    float sum = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) sum += red[y][t];
+    partial[(size_t)blockIdx.y * cols + col] = sum;
+  }
+}
+
+__global__ void colsum_finish_kernel(const float* __restrict__ partial, int parts, int cols, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int p = 0; p < parts; ++p) s += partial[(size_t)p * cols + c];
+  out[c] = s;
 }
 
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int rows,
@@ -637,30 +671,34 @@ std::vector<at::Tensor> ln_modulate_bwd(at::Tensor dy, at::Tensor x, at::Tensor 
   auto dshift = at::zeros_like(scale);
   if (!rows) return {dx, dscale, dshift};
   auto dyc = dy.to(at::kBFloat16).contiguous();
-  // >= 32 contiguous rows per warp: modulation rows repeat for whole samples, so per-warp
-  // register accumulation absorbs most of the reduction before any atomic.
-  const int warps_total = std::max(1, std::min((rows + 31) / 32, sm_count() * 16));
-  const int per = (rows + warps_total - 1) / warps_total;
-  const int warps_needed = (rows + per - 1) / per;
-  const int blocks = (warps_needed + kWarps - 1) / kWarps;
+  const int row_blocks = std::min((rows + kWarps - 1) / kWarps, sm_count() * 16);
+  const dim3 cgrid((width / 8 + 31) / 32, (rows + 8 * MOD_RB - 1) / (8 * MOD_RB));
   AT_DISPATCH_SWITCH(x.scalar_type(), "ln_modulate_bwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
                        using T = __nv_bfloat16;
                        NV_DISPATCH(width, [&] {
-                         lnmod_bwd_kernel<NV, T><<<blocks, 256, 0, stream()>>>(
+                         lnmod_dx_kernel<NV, T><<<row_blocks, 256, 0, stream()>>>(
                              (const __nv_bfloat16*)dyc.data_ptr(), (const T*)x.data_ptr(), scale.data_ptr<float>(),
                              idx.data_ptr<int>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), (T*)dx.data_ptr(),
-                             dscale.data_ptr<float>(), dshift.data_ptr<float>(), rows, width, per);
+                             rows, width);
                        });
+                       mod_colsum_kernel<0, T><<<cgrid, dim3(32, 8), 0, stream()>>>(
+                           nullptr, (const __nv_bfloat16*)dyc.data_ptr(), (const T*)x.data_ptr(), idx.data_ptr<int>(),
+                           mean.data_ptr<float>(), rstd.data_ptr<float>(), dscale.data_ptr<float>(),
+                           dshift.data_ptr<float>(), rows, width);
                      }) AT_DISPATCH_CASE(at::kFloat, [&] {
                        NV_DISPATCH(width, [&] {
-                         lnmod_bwd_kernel<NV, float><<<blocks, 256, 0, stream()>>>(
+                         lnmod_dx_kernel<NV, float><<<row_blocks, 256, 0, stream()>>>(
                              (const __nv_bfloat16*)dyc.data_ptr(), x.data_ptr<float>(), scale.data_ptr<float>(),
                              idx.data_ptr<int>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(),
-                             dscale.data_ptr<float>(), dshift.data_ptr<float>(), rows, width, per);
+                             rows, width);
                        });
+                       mod_colsum_kernel<0, float><<<cgrid, dim3(32, 8), 0, stream()>>>(
+                           nullptr, (const __nv_bfloat16*)dyc.data_ptr(), x.data_ptr<float>(), idx.data_ptr<int>(),
+                           mean.data_ptr<float>(), rstd.data_ptr<float>(), dscale.data_ptr<float>(),
+                           dshift.data_ptr<float>(), rows, width);
                      }));
   CQB_LAUNCH_CHECK();
-  count_launch();
+  count_launch(2);
   return {dx, dscale, dshift};
 }
 
@@ -689,23 +727,29 @@ std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tens
   auto dgate = at::zeros_like(gate);
   auto dbranch = at::empty_like(branch);
   if (!rows) return {dbranch, dgate};
-  const int warps_total = std::max(1, std::min((rows + 31) / 32, sm_count() * 16));
-  const int per = (rows + warps_total - 1) / warps_total;
-  const int warps_needed = (rows + per - 1) / per;
-  const int blocks = (warps_needed + kWarps - 1) / kWarps;
   auto dyc = dy.to(at::kFloat).contiguous();
-  NV_DISPATCH(width, [&] {
-    if (branch.scalar_type() == at::kBFloat16)
-      gated_add_bwd_kernel<NV, __nv_bfloat16><<<blocks, 256, 0, stream()>>>(
-          dyc.data_ptr<float>(), (const __nv_bfloat16*)branch.data_ptr(), gate.data_ptr<float>(), idx.data_ptr<int>(),
-          (__nv_bfloat16*)dbranch.data_ptr(), dgate.data_ptr<float>(), rows, width, per);
-    else
-      gated_add_bwd_kernel<NV, float><<<blocks, 256, 0, stream()>>>(
-          dyc.data_ptr<float>(), branch.data_ptr<float>(), gate.data_ptr<float>(), idx.data_ptr<int>(),
-          dbranch.data_ptr<float>(), dgate.data_ptr<float>(), rows, width, per);
-  });
+  const int grid = grid_for((size_t)rows * width / 8);
+  const dim3 cgrid((width / 8 + 31) / 32, (rows + 8 * MOD_RB - 1) / (8 * MOD_RB));
+  if (branch.scalar_type() == at::kBFloat16) {
+    auto b = branch.contiguous();
+    gated_add_dbranch_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(
+        dyc.data_ptr<float>(), gate.data_ptr<float>(), idx.data_ptr<int>(), (__nv_bfloat16*)dbranch.data_ptr(), rows,
+        width);
+    mod_colsum_kernel<1, __nv_bfloat16><<<cgrid, dim3(32, 8), 0, stream()>>>(
+        dyc.data_ptr<float>(), nullptr, (const __nv_bfloat16*)b.data_ptr(), idx.data_ptr<int>(), nullptr, nullptr,
+        dgate.data_ptr<float>(), nullptr, rows, width);
+  } else {
+    auto b = branch.to(at::kFloat).contiguous();
+    gated_add_dbranch_kernel<float><<<grid, 256, 0, stream()>>>(dyc.data_ptr<float>(), gate.data_ptr<float>(),
+                                                                idx.data_ptr<int>(), dbranch.data_ptr<float>(), rows,
+                                                                width);
+    mod_colsum_kernel<1, float><<<cgrid, dim3(32, 8), 0, stream()>>>(dyc.data_ptr<float>(), nullptr,
+                                                                     b.data_ptr<float>(), idx.data_ptr<int>(), nullptr,
+                                                                     nullptr, dgate.data_ptr<float>(), nullptr, rows,
+                                                                     width);
+  }
   CQB_LAUNCH_CHECK();
-  count_launch();
+  count_launch(2);
   return {dbranch, dgate};
 }
 
@@ -733,6 +777,29 @@ at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x) {
   CQB_LAUNCH_CHECK();
   count_launch();
   return dx;
+}
+
+
+// fp32 [cols] = sum over rows of x (bf16 or fp32 [rows, cols], cols % 8 == 0).
+at::Tensor column_sum(at::Tensor x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.size(1) % 8 == 0, "column_sum: 2-D, cols % 8 == 0");
+  auto xc = x.contiguous();
+  const int rows = xc.size(0), cols = xc.size(1);
+  auto out = at::empty({cols}, xc.options().dtype(at::kFloat));
+  if (!rows) return out.zero_();
+  const dim3 grid((cols / 8 + 31) / 32, (rows + 8 * BIAS_RB - 1) / (8 * BIAS_RB));
+  auto partial = at::empty({(long)grid.y, cols}, out.options());
+  if (xc.scalar_type() == at::kBFloat16)
+    colsum_partial_kernel<__nv_bfloat16><<<grid, dim3(32, 8), 0, stream()>>>(
+        (const __nv_bfloat16*)xc.data_ptr(), rows, cols, partial.data_ptr<float>());
+  else
+    colsum_partial_kernel<float><<<grid, dim3(32, 8), 0, stream()>>>(xc.to(at::kFloat).data_ptr<float>(), rows, cols,
+                                                                      partial.data_ptr<float>());
+  colsum_finish_kernel<<<(cols + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), grid.y, cols,
+                                                                 out.data_ptr<float>());
+  CQB_LAUNCH_CHECK();
+  count_launch(2);
+  return out;
 }
 
 }  // namespace cqb

@@ -16,6 +16,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+from . import _ext
 from . import gemm
 
 
@@ -31,6 +32,14 @@ def _accumulate(param, grad):
     if cb is not None:
         cb(param)
     return None
+
+
+def _bias_grad(dy):
+    """Column sums of ``dy`` in fp32 (one kernel reading bf16 directly on CUDA)."""
+    dy2 = dy.reshape(-1, dy.shape[-1])
+    if dy2.is_cuda and _ext.cuda_kernels_enabled() and _ext.has("column_sum") and dy2.shape[1] % 8 == 0:
+        return _ext.ops().column_sum(dy2)
+    return dy2.float().sum(0)
 
 
 def _weight_grad(param, dy, x):
@@ -59,7 +68,7 @@ class _Linear(torch.autograd.Function):
         dy = dy.contiguous()
         dx = gemm.matmul_nn(dy, weight) if ctx.needs_input_grad[0] else None
         dw = _weight_grad(weight, dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])) if ctx.needs_input_grad[1] else None
-        db = _accumulate(ctx.bias, dy.reshape(-1, dy.shape[-1]).float().sum(0)) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        db = _accumulate(ctx.bias, _bias_grad(dy)) if ctx.has_bias and ctx.needs_input_grad[2] else None
         return dx, dw, db
 
 
@@ -87,7 +96,7 @@ class _GatherLinear(torch.autograd.Function):
         dy = dy.contiguous()
         dx = fused.linear_scatter_grad(dy, weight) if ctx.needs_input_grad[0] else None
         dw = _weight_grad(weight, dy, xg) if ctx.needs_input_grad[1] else None
-        db = _accumulate(ctx.bias, dy.float().sum(0)) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        db = _accumulate(ctx.bias, _bias_grad(dy)) if ctx.has_bias and ctx.needs_input_grad[2] else None
         return dx, dw, db
 
 
@@ -112,7 +121,7 @@ class _LinearScatter(torch.autograd.Function):
         dyg = fused.gather_rows_raw(dy.contiguous())
         dx = gemm.matmul_nn(dyg, weight) if ctx.needs_input_grad[0] else None
         dw = _weight_grad(weight, dyg, x) if ctx.needs_input_grad[1] else None
-        db = _accumulate(ctx.bias, dy.float().sum(0)) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        db = _accumulate(ctx.bias, _bias_grad(dy)) if ctx.has_bias and ctx.needs_input_grad[2] else None
         return dx, dw, db
 
 

@@ -101,3 +101,13 @@ def test_swiglu():
     (dxr,) = torch.autograd.grad(yr, (xr,), g.float())
     torch.testing.assert_close(y.float(), yr, atol=3e-2, rtol=2e-2)
     torch.testing.assert_close(dx.float(), dxr, atol=3e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("rows,cols", [(2048, 1536), (77, 40), (1, 8)])
+def test_column_sum(rows, cols):
+    torch.manual_seed(5)
+    x = torch.randn(rows, cols, device="cuda").to(torch.bfloat16)
+    got = _ext.ops().column_sum(x)
+    torch.testing.assert_close(got, x.float().sum(0), atol=1e-3, rtol=1e-4)
+    again = _ext.ops().column_sum(x)
+    assert torch.equal(got, again)   # fixed reduction order
