@@ -66,6 +66,9 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
 std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor G, at::Tensor B);
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
                                       at::Tensor B, at::Tensor S, at::Tensor dS);
+// gather.cu
+at::Tensor gather_rows(at::Tensor src0, c10::optional<at::Tensor> src1, at::Tensor idx);
+std::vector<at::Tensor> gather_rows_bwd(at::Tensor grad, at::Tensor inv, int64_t n0, int64_t n1);
 // conv.cu
 at::Tensor conv_fwd(at::Tensor x, at::Tensor w, at::Tensor pos);
 std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor pos);
@@ -123,6 +126,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sum_squares", &cqb::sum_squares);
   m.def("gdn_prep", &cqb::gdn_prep);
   m.def("gdn_chunk_bwd", &cqb::gdn_chunk_bwd);
+  m.def("gather_rows", &cqb::gather_rows);
+  m.def("gather_rows_bwd", &cqb::gather_rows_bwd);
   m.def("conv_fwd", &cqb::conv_fwd);
   m.def("conv_bwd", &cqb::conv_bwd);
   m.def("chunk_gather", &cqb::chunk_gather);

@@ -1,0 +1,142 @@
+// Row gathers of the CQ event streams and their atomic-free backward.
+//
+// gather: out[i] = src0[idx[i]] if idx[i] < n0, src1[idx[i] - n0] if idx[i] < n0 + n1, else 0
+//   (a sentinel index reads zeros, so callers never append a zero row, and two sources --
+//   e.g. content and query conv outputs -- need no concatenation).
+// backward: with the host-built inverse levels inv[l][j] = l-th output row that read source row
+//   j (or m = rows of the output when there is none), d_src[j] = sum_l grad[inv[l][j]]; a warp per
+//   source row sums the levels in fp32 and writes the gradient once (deterministic).
+#include "common.cuh"
+
+namespace cqb {
+
+namespace {
+
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ src0, long n0, const T* __restrict__ src1, long n1,
+                                   const long* __restrict__ idx, T* __restrict__ out, long m, int width) {
+  const int vecs = width * (int)sizeof(T) / 16;
+  const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (long i = warp; i < m; i += ((long)gridDim.x * blockDim.x) >> 5) {
+    const long s = idx[i];
+    const uint4* from = nullptr;
+    if (s < n0) from = reinterpret_cast<const uint4*>(src0 + s * width);
+    else if (s < n0 + n1) from = reinterpret_cast<const uint4*>(src1 + (s - n0) * width);
+    uint4* to = reinterpret_cast<uint4*>(out + i * width);
+    for (int v = lane; v < vecs; v += 32) to[v] = from ? __ldg(from + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ void load_any(const __nv_bfloat16* p, float* v) { load8(p, v); }
+__device__ __forceinline__ void load_any(const float* p, float* v) { load8(p, v); }
+
+template <typename T>
+__global__ void gather_rows_bwd_kernel(const T* __restrict__ grad, long m, const long* __restrict__ inv, int levels,
+                                       long inv_stride, T* __restrict__ out0, long n0, T* __restrict__ out1, long total,
+                                       int width) {
+  const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (long j = warp; j < total; j += ((long)gridDim.x * blockDim.x) >> 5) {
+    T* dst = j < n0 ? out0 + j * width : out1 + (j - n0) * width;
+    for (int c = lane * 8; c < width; c += 256) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int l = 0; l < levels; ++l) {
+        const long r = inv[(long)l * inv_stride + j];
+        if (r >= m) continue;
+        float v[8];
+        load_any(grad + r * width + c, v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += v[q];
+      }
+      store8(dst + c, acc);
+    }
+  }
+}
+
+int gather_grid(long rows) {
+  return (int)std::max<long>(1, std::min<long>((rows * 32 + 255) / 256, (long)sm_count() * 16));
+}
+
+}  // namespace
+
+// src1 may be undefined (one source). Rows are flattened to [n, width]; row bytes % 16 == 0.
+at::Tensor gather_rows(at::Tensor src0, c10::optional<at::Tensor> src1_opt, at::Tensor idx) {
+  TORCH_CHECK(src0.is_cuda() && src0.is_contiguous(), "gather_rows: contiguous CUDA source");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "gather_rows: int64 index");
+  const long n0 = src0.size(0);
+  const int width = (int)(src0.numel() / std::max<long>(n0, 1));
+  at::Tensor src1;
+  long n1 = 0;
+  if (src1_opt && src1_opt->defined()) {
+    src1 = *src1_opt;
+    TORCH_CHECK(src1.is_contiguous() && src1.scalar_type() == src0.scalar_type() &&
+                    src1.numel() == src1.size(0) * (long)width,
+                "gather_rows: second source must match the first's row shape and dtype");
+    n1 = src1.size(0);
+  }
+  TORCH_CHECK(width * src0.element_size() % 16 == 0, "gather_rows: row bytes must be a multiple of 16");
+  auto shape = src0.sizes().vec();
+  const long m = idx.numel();
+  shape[0] = m;
+  auto out = at::empty(shape, src0.options());
+  if (!m) return out;
+  const int grid = gather_grid(m);
+  if (src0.scalar_type() == at::kBFloat16)
+    gather_rows_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(
+        (const __nv_bfloat16*)src0.data_ptr(), n0, n1 ? (const __nv_bfloat16*)src1.data_ptr() : nullptr, n1,
+        (const long*)idx.data_ptr(), (__nv_bfloat16*)out.data_ptr(), m, width);
+  else if (src0.scalar_type() == at::kFloat)
+    gather_rows_kernel<float><<<grid, 256, 0, stream()>>>(src0.data_ptr<float>(), n0,
+                                                          n1 ? src1.data_ptr<float>() : nullptr, n1,
+                                                          (const long*)idx.data_ptr(), out.data_ptr<float>(), m, width);
+  else
+    TORCH_CHECK(false, "gather_rows: bf16 or fp32");
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return out;
+}
+
+// grad [m, ...]; inv [levels, n_src] int64 (values in [0, m], m = none); returns the gradients of the
+// first n0 source rows and (n1 > 0) of the next n1 rows; source rows past n0 + n1 (sentinels) are
+// dropped.
+std::vector<at::Tensor> gather_rows_bwd(at::Tensor grad, at::Tensor inv, int64_t n0, int64_t n1) {
+  TORCH_CHECK(grad.is_cuda() && grad.is_contiguous(), "gather_rows_bwd: contiguous grad");
+  TORCH_CHECK(inv.scalar_type() == at::kLong && inv.is_contiguous() && inv.dim() == 2, "inv: int64 [levels, n_src]");
+  const long m = grad.size(0);
+  const int width = (int)(grad.numel() / std::max<long>(m, 1));
+  TORCH_CHECK(width % 8 == 0, "gather_rows_bwd: row width must be a multiple of 8 elements");
+  const long n_src = inv.size(1);
+  TORCH_CHECK(n0 + n1 <= n_src, "inverse map smaller than the sources");
+  auto s0 = grad.sizes().vec();
+  s0[0] = n0;
+  auto out0 = at::empty(s0, grad.options());
+  at::Tensor out1;
+  if (n1) {
+    auto s1 = grad.sizes().vec();
+    s1[0] = n1;
+    out1 = at::empty(s1, grad.options());
+  }
+  const int levels = (int)inv.size(0);
+  if (!levels || !m) {
+    out0.zero_();
+    if (n1) out1.zero_();
+    return n1 ? std::vector<at::Tensor>{out0, out1} : std::vector<at::Tensor>{out0};
+  }
+  const int grid = gather_grid(n0 + n1);
+  if (grad.scalar_type() == at::kBFloat16)
+    gather_rows_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(
+        (const __nv_bfloat16*)grad.data_ptr(), m, (const long*)inv.data_ptr(), levels, n_src,
+        (__nv_bfloat16*)out0.data_ptr(), n0, n1 ? (__nv_bfloat16*)out1.data_ptr() : nullptr, n0 + n1, width);
+  else if (grad.scalar_type() == at::kFloat)
+    gather_rows_bwd_kernel<float><<<grid, 256, 0, stream()>>>(grad.data_ptr<float>(), m, (const long*)inv.data_ptr(),
+                                                              levels, n_src, out0.data_ptr<float>(), n0,
+                                                              n1 ? out1.data_ptr<float>() : nullptr, n0 + n1, width);
+  else
+    TORCH_CHECK(false, "gather_rows_bwd: bf16 or fp32");
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return n1 ? std::vector<at::Tensor>{out0, out1} : std::vector<at::Tensor>{out0};
+}
+
+}  // namespace cqb

@@ -138,17 +138,17 @@ class GatedDelta(nn.Module):
         v = v.reshape(-1, h, d)
         if h != hk:
             q, k, query = (t.repeat_interleave(h // hk, dim=1) for t in (q, k, query))
-        q = GA.rows(torch.cat((q, query), 0), dp.event_q, dp.event_q_inv)
-        zeros = k.new_zeros(1, h, d)
-        k = GA.rows(torch.cat((k, zeros), 0), dp.event_write, dp.event_write_inv)
-        v = GA.rows(torch.cat((v, zeros), 0), dp.event_write, dp.event_write_inv)
+        # event order: content and query conv outputs feed reads; index nc (write of a read-only
+        # event) gathers zeros
+        q = GA.rows(q.contiguous(), dp.event_q, dp.event_q_inv, second=query.contiguous())
+        k = GA.rows(k.contiguous(), dp.event_write, dp.event_write_inv)
+        v = GA.rows(v.contiguous(), dp.event_write, dp.event_write_inv)
         ctrl = torch.float64 if x.dtype == torch.float64 else torch.float32
         a = GA.rows(a, dp.content_order, dp.content_order_inv).to(ctrl)
         g = -self.A_log.to(ctrl).exp() * F.softplus(a + self.dt_bias.to(ctrl))
         beta = GA.rows(b, dp.content_order, dp.content_order_inv).to(ctrl).sigmoid()
-        zero = g.new_zeros(1, h)
-        g = GA.rows(torch.cat((g, zero)), dp.event_write, dp.event_write_inv)
-        beta = GA.rows(torch.cat((beta, zero)), dp.event_write, dp.event_write_inv)
+        g = GA.rows(g.contiguous(), dp.event_write, dp.event_write_inv)
+        beta = GA.rows(beta.contiguous(), dp.event_write, dp.event_write_inv)
         if cache is not None:
             if torch.is_grad_enabled():
                 raise ValueError("CQ state caching is inference-only")
@@ -163,8 +163,7 @@ class GatedDelta(nn.Module):
             y = y.to(v.dtype)
         else:
             y = GDN.gated_delta(q, k, v, g, beta, dp.event_bounds)
-        y = torch.cat((y, y.new_zeros(1, *y.shape[1:])))   # rows without a GDN output read zeros
-        selected = GA.rows(y, dp.hidden_event, dp.hidden_event_inv).to(x.dtype)
+        selected = GA.rows(y.contiguous(), dp.hidden_event, dp.hidden_event_inv).to(x.dtype)   # sentinel -> zeros
         out = self.norm(selected, z.reshape(-1, h, d)).flatten(-2)
         return self.out_proj(out)
 

@@ -11,6 +11,8 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import _ext
+
 
 def inverse_levels(index, n_src, ignore=None):
     """Host-side inverse of a gather index (``ignore``: a source id whose gradient is discarded)."""
@@ -53,7 +55,64 @@ class _Rows(torch.autograd.Function):
         return (out, None) + (None,) * len(ctx.inverse)
 
 
-def rows(src, index, inverse=None):
-    if inverse is None or not src.requires_grad:
-        return src.index_select(0, index)
-    return _Rows.apply(src, index, *inverse)
+_STACKED: dict = {}
+
+
+def _stacked(inverse):
+    """The inverse levels as one ``[levels, n_src]`` device tensor (cached per plan tensor)."""
+    key = (id(inverse[0]), len(inverse))
+    hit = _STACKED.get(key)
+    if hit is None or hit[0] is not inverse[0]:
+        if len(_STACKED) > 256:
+            _STACKED.clear()
+        hit = (inverse[0], torch.stack(inverse).contiguous())
+        _STACKED[key] = hit
+    return hit[1]
+
+
+class _RowsCuda(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, index, inv, src, second):
+        ctx.inv, ctx.n0 = inv, src.shape[0]
+        ctx.n1 = 0 if second is None else second.shape[0]
+        return _ext.ops().gather_rows(src, second, index)
+
+    @staticmethod
+    def backward(ctx, grad):
+        grads = _ext.ops().gather_rows_bwd(grad.contiguous(), ctx.inv, ctx.n0, ctx.n1)
+        return None, None, grads[0], (grads[1] if ctx.n1 else None)
+
+
+def _cuda_ok(src, second, inverse):
+    if not (src.is_cuda and _ext.cuda_kernels_enabled() and _ext.has("gather_rows") and src.is_contiguous()):
+        return False
+    if src.dtype not in (torch.bfloat16, torch.float32):
+        return False
+    if second is not None and (second.dtype != src.dtype or not second.is_contiguous()
+                               or second.shape[1:] != src.shape[1:]):
+        return False
+    width = src[0].numel() if src.shape[0] else 0
+    return width and (width * src.element_size()) % 16 == 0 and (inverse is None or width % 8 == 0)
+
+
+def rows(src, index, inverse=None, second=None):
+    """``cat(src, second)[index]`` where an index past the last source row reads zeros.
+
+    ``inverse`` (levels over the concatenated sources, optionally plus one sentinel row) makes
+    the backward a gather too. On CUDA one kernel gathers and one kernel sums the inverse levels
+    (``csrc/gather.cu``); no zero row or concatenation is materialised.
+    """
+    needs_grad = src.requires_grad or (second is not None and second.requires_grad)
+    if _cuda_ok(src, second, inverse if needs_grad else None):
+        if inverse is None or not needs_grad:
+            return _ext.ops().gather_rows(src, second, index)
+        return _RowsCuda.apply(index, _stacked(inverse), src, second)
+    parts = [src] + ([second] if second is not None else []) + [src.new_zeros(1, *src.shape[1:])]
+    full = torch.cat(parts, 0)
+    if inverse is None or not needs_grad:
+        return full.index_select(0, index)
+    n_src = inverse[0].numel() if inverse else full.shape[0]
+    if n_src < full.shape[0]:
+        full = full[:n_src]
+    out = _Rows.apply(full, index, *inverse)
+    return out
