@@ -13,16 +13,16 @@ namespace cqb {
 namespace {
 
 template <typename T>
-__global__ void gather_rows_kernel(const T* __restrict__ src0, long n0, const T* __restrict__ src1, long n1,
-                                   const long* __restrict__ idx, T* __restrict__ out, long m, int width) {
+__global__ void gather_rows_kernel(const T* __restrict__ src0, long n0, long ld0, const T* __restrict__ src1, long n1,
+                                   long ld1, const long* __restrict__ idx, T* __restrict__ out, long m, int width) {
   const int vecs = width * (int)sizeof(T) / 16;
   const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   for (long i = warp; i < m; i += ((long)gridDim.x * blockDim.x) >> 5) {
     const long s = idx[i];
     const uint4* from = nullptr;
-    if (s < n0) from = reinterpret_cast<const uint4*>(src0 + s * width);
-    else if (s < n0 + n1) from = reinterpret_cast<const uint4*>(src1 + (s - n0) * width);
+    if (s < n0) from = reinterpret_cast<const uint4*>(src0 + s * ld0);
+    else if (s < n0 + n1) from = reinterpret_cast<const uint4*>(src1 + (s - n0) * ld1);
     uint4* to = reinterpret_cast<uint4*>(out + i * width);
     for (int v = lane; v < vecs; v += 32) to[v] = from ? __ldg(from + v) : make_uint4(0, 0, 0, 0);
   }
@@ -60,36 +60,53 @@ int gather_grid(long rows) {
 
 }  // namespace
 
-// src1 may be undefined (one source). Rows are flattened to [n, width]; row bytes % 16 == 0.
+namespace {
+// Rows of a source: contiguous inside a row, any row stride (e.g. a column slice of a projection).
+long row_stride(const at::Tensor& t, long width) {
+  TORCH_CHECK(t.is_cuda() && t.dim() >= 1, "gather_rows: CUDA source");
+  if (t.size(0) <= 1) return width;
+  auto row = t[0];
+  TORCH_CHECK(row.is_contiguous() && row.numel() == width, "gather_rows: each source row must be contiguous");
+  return t.stride(0);
+}
+}  // namespace
+
+// src1 may be undefined (one source). Rows are [width] elements with a row stride; the row bytes,
+// the row stride in bytes and the base addresses must be multiples of 16.
 at::Tensor gather_rows(at::Tensor src0, c10::optional<at::Tensor> src1_opt, at::Tensor idx) {
-  TORCH_CHECK(src0.is_cuda() && src0.is_contiguous(), "gather_rows: contiguous CUDA source");
   TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "gather_rows: int64 index");
   const long n0 = src0.size(0);
-  const int width = (int)(src0.numel() / std::max<long>(n0, 1));
+  const long width = n0 ? src0.numel() / n0 : 0;
+  const long ld0 = row_stride(src0, width);
   at::Tensor src1;
-  long n1 = 0;
+  long n1 = 0, ld1 = width;
   if (src1_opt && src1_opt->defined()) {
     src1 = *src1_opt;
-    TORCH_CHECK(src1.is_contiguous() && src1.scalar_type() == src0.scalar_type() &&
-                    src1.numel() == src1.size(0) * (long)width,
+    TORCH_CHECK(src1.scalar_type() == src0.scalar_type() && src1.numel() == src1.size(0) * width,
                 "gather_rows: second source must match the first's row shape and dtype");
     n1 = src1.size(0);
+    ld1 = row_stride(src1, width);
   }
-  TORCH_CHECK(width * src0.element_size() % 16 == 0, "gather_rows: row bytes must be a multiple of 16");
+  const long es = src0.element_size();
+  TORCH_CHECK(width * es % 16 == 0 && ld0 * es % 16 == 0 && ld1 * es % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(src0.data_ptr()) % 16 == 0 &&
+                  (!n1 || reinterpret_cast<uintptr_t>(src1.data_ptr()) % 16 == 0),
+              "gather_rows: rows, strides and bases must be 16-byte aligned");
   auto shape = src0.sizes().vec();
   const long m = idx.numel();
   shape[0] = m;
-  auto out = at::empty(shape, src0.options());
+  auto out = at::empty(shape, src0.options().memory_format(at::MemoryFormat::Contiguous));
   if (!m) return out;
   const int grid = gather_grid(m);
   if (src0.scalar_type() == at::kBFloat16)
     gather_rows_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(
-        (const __nv_bfloat16*)src0.data_ptr(), n0, n1 ? (const __nv_bfloat16*)src1.data_ptr() : nullptr, n1,
-        (const long*)idx.data_ptr(), (__nv_bfloat16*)out.data_ptr(), m, width);
+        (const __nv_bfloat16*)src0.data_ptr(), n0, ld0, n1 ? (const __nv_bfloat16*)src1.data_ptr() : nullptr, n1, ld1,
+        (const long*)idx.data_ptr(), (__nv_bfloat16*)out.data_ptr(), m, (int)width);
   else if (src0.scalar_type() == at::kFloat)
-    gather_rows_kernel<float><<<grid, 256, 0, stream()>>>(src0.data_ptr<float>(), n0,
-                                                          n1 ? src1.data_ptr<float>() : nullptr, n1,
-                                                          (const long*)idx.data_ptr(), out.data_ptr<float>(), m, width);
+    gather_rows_kernel<float><<<grid, 256, 0, stream()>>>(src0.data_ptr<float>(), n0, ld0,
+                                                          n1 ? src1.data_ptr<float>() : nullptr, n1, ld1,
+                                                          (const long*)idx.data_ptr(), out.data_ptr<float>(), m,
+                                                          (int)width);
   else
     TORCH_CHECK(false, "gather_rows: bf16 or fp32");
   CQB_LAUNCH_CHECK();

@@ -140,9 +140,9 @@ class GatedDelta(nn.Module):
             q, k, query = (t.repeat_interleave(h // hk, dim=1) for t in (q, k, query))
         # event order: content and query conv outputs feed reads; index nc (write of a read-only
         # event) gathers zeros
-        q = GA.rows(q.contiguous(), dp.event_q, dp.event_q_inv, second=query.contiguous())
-        k = GA.rows(k.contiguous(), dp.event_write, dp.event_write_inv)
-        v = GA.rows(v.contiguous(), dp.event_write, dp.event_write_inv)
+        q = GA.rows(q, dp.event_q, dp.event_q_inv, second=query)
+        k = GA.rows(k, dp.event_write, dp.event_write_inv)
+        v = GA.rows(v, dp.event_write, dp.event_write_inv)
         ctrl = torch.float64 if x.dtype == torch.float64 else torch.float32
         a = GA.rows(a, dp.content_order, dp.content_order_inv).to(ctrl)
         g = -self.A_log.to(ctrl).exp() * F.softplus(a + self.dt_bias.to(ctrl))

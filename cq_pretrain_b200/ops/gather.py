@@ -83,16 +83,24 @@ class _RowsCuda(torch.autograd.Function):
         return None, None, grads[0], (grads[1] if ctx.n1 else None)
 
 
+def _rows_aligned(t):
+    """Rows contiguous inside, 16-byte aligned base and row stride (column slices qualify)."""
+    if t.shape[0] == 0 or not t[0].is_contiguous():
+        return False
+    es = t.element_size()
+    return t.data_ptr() % 16 == 0 and (t.shape[0] == 1 or (t.stride(0) * es) % 16 == 0)
+
+
 def _cuda_ok(src, second, inverse):
-    if not (src.is_cuda and _ext.cuda_kernels_enabled() and _ext.has("gather_rows") and src.is_contiguous()):
+    if not (src.is_cuda and _ext.cuda_kernels_enabled() and _ext.has("gather_rows")):
         return False
-    if src.dtype not in (torch.bfloat16, torch.float32):
+    if src.dtype not in (torch.bfloat16, torch.float32) or not _rows_aligned(src):
         return False
-    if second is not None and (second.dtype != src.dtype or not second.is_contiguous()
-                               or second.shape[1:] != src.shape[1:]):
+    if second is not None and (second.dtype != src.dtype or second.shape[1:] != src.shape[1:]
+                               or not _rows_aligned(second)):
         return False
-    width = src[0].numel() if src.shape[0] else 0
-    return width and (width * src.element_size()) % 16 == 0 and (inverse is None or width % 8 == 0)
+    width = src[0].numel()
+    return (width * src.element_size()) % 16 == 0 and (inverse is None or width % 8 == 0)
 
 
 def rows(src, index, inverse=None, second=None):

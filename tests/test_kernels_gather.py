@@ -30,3 +30,13 @@ def test_rows_two_sources_and_sentinel(dtype, shape):
     want = torch.zeros(n0 + n1 + 1, *shape, device="cuda").index_add_(0, idx, g.float())
     torch.testing.assert_close(a.grad.float(), want[:n0], atol=2e-2, rtol=1e-2)
     torch.testing.assert_close(b.grad.float(), want[n0:n0 + n1], atol=2e-2, rtol=1e-2)
+
+
+def test_rows_strided_source():
+    proj = torch.randn(500, 96, device="cuda").to(torch.bfloat16)
+    src = proj[:, 16:48].detach().requires_grad_(False)          # column slice: row stride 96
+    view = proj[:, 16:48]
+    idx = torch.randint(0, 501, (700,), device="cuda")
+    out = GA.rows(view, idx)
+    ref = torch.cat((src.float(), torch.zeros(1, 32, device="cuda")))[idx]
+    torch.testing.assert_close(out.float(), ref)
