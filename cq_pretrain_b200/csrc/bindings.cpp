@@ -23,6 +23,7 @@ at::Tensor gated_add_fwd(at::Tensor x, at::Tensor branch, at::Tensor gate, at::T
 std::vector<at::Tensor> gated_add_bwd(at::Tensor dy, at::Tensor branch, at::Tensor gate, at::Tensor idx);
 at::Tensor swiglu_fwd(at::Tensor x);
 at::Tensor column_sum(at::Tensor x);
+at::Tensor rope_pairs(at::Tensor x, at::Tensor cos_t, at::Tensor sin_t, bool inverse);
 at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x);
 // gemm.cu
 at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
@@ -99,6 +100,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_add_bwd", &cqb::gated_add_bwd);
   m.def("swiglu_fwd", &cqb::swiglu_fwd);
   m.def("column_sum", &cqb::column_sum);
+  m.def("rope_pairs", &cqb::rope_pairs);
   m.def("swiglu_bwd", &cqb::swiglu_bwd);
   m.def("gemm_nt", &cqb::gemm_nt, py::arg("x"), py::arg("w"), py::arg("bias") = py::none());
   m.def("gemm_nn", &cqb::gemm_nn);

@@ -465,6 +465,35 @@ __global__ void colsum_finish_kernel(const float* __restrict__ partial, int part
   out[c] = s;
 }
 
+
+// Complex-pair rotary embedding: (x[2i], x[2i+1]) of every head rotated by angle_i of the row
+// (cos/sin [rows, half]); the backward is the rotation by -angle (sign = -1).
+template <typename T>
+__global__ void rope_pairs_kernel(const T* __restrict__ x, const float* __restrict__ cos_t,
+                                  const float* __restrict__ sin_t, T* __restrict__ y, int rows, int heads, int hd,
+                                  float sign) {
+  const int half = hd / 2;
+  const size_t pairs4 = (size_t)rows * heads * half / 4;     // 4 pairs = 8 elements per thread
+  for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < pairs4; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;                                 // element offset
+    const size_t row = e / ((size_t)heads * hd);
+    const int i0 = (int)((e % hd) / 2);                     // first pair index within the head
+    float xv[8], o[8], c[4], s[4];
+    load_vec(x + e, xv);
+    const float4 cv = *reinterpret_cast<const float4*>(cos_t + row * half + i0);
+    const float4 sv = *reinterpret_cast<const float4*>(sin_t + row * half + i0);
+    c[0] = cv.x; c[1] = cv.y; c[2] = cv.z; c[3] = cv.w;
+    s[0] = sign * sv.x; s[1] = sign * sv.y; s[2] = sign * sv.z; s[3] = sign * sv.w;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float re = xv[2 * p], im = xv[2 * p + 1];
+      o[2 * p] = re * c[p] - im * s[p];
+      o[2 * p + 1] = im * c[p] + re * s[p];
+    }
+    store8(y + e, o);
+  }
+}
+
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int rows,
                                   int half) {
   const size_t vecs = (size_t)rows * half / 8;
@@ -800,6 +829,30 @@ at::Tensor column_sum(at::Tensor x) {
   CQB_LAUNCH_CHECK();
   count_launch(2);
   return out;
+}
+
+
+// x [rows, heads, hd] (bf16/fp32, contiguous, hd % 8 == 0), cos/sin fp32 [rows, hd/2].
+at::Tensor rope_pairs(at::Tensor x, at::Tensor cos_t, at::Tensor sin_t, bool inverse) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 3 && x.size(2) % 8 == 0, "rope_pairs: x [rows, H, hd]");
+  auto c = cos_t.to(at::kFloat).contiguous(), sn = sin_t.to(at::kFloat).contiguous();
+  TORCH_CHECK(c.dim() == 2 && c.size(0) == x.size(0) && c.size(1) == x.size(2) / 2 && sn.sizes() == c.sizes(),
+              "rope_pairs: cos/sin [rows, hd/2]");
+  auto y = at::empty_like(x);
+  const int rows = x.size(0), heads = x.size(1), hd = x.size(2);
+  if (!rows) return y;
+  const int grid = grid_for((size_t)rows * heads * hd / 8);
+  const float sign = inverse ? -1.f : 1.f;
+  if (x.scalar_type() == at::kBFloat16)
+    rope_pairs_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>((const __nv_bfloat16*)x.data_ptr(), c.data_ptr<float>(),
+                                                                sn.data_ptr<float>(), (__nv_bfloat16*)y.data_ptr(),
+                                                                rows, heads, hd, sign);
+  else
+    rope_pairs_kernel<float><<<grid, 256, 0, stream()>>>(x.data_ptr<float>(), c.data_ptr<float>(), sn.data_ptr<float>(),
+                                                         y.data_ptr<float>(), rows, heads, hd, sign);
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return y;
 }
 
 }  // namespace cqb

@@ -49,6 +49,9 @@ class WanRMSNorm(nn.Module):
             if ws is not None and ws.supports_rms(x):
                 # in-kernel exchange of the per-row sums of squares over NVLink (no NCCL call)
                 return _TPRMSNorm.apply(x, self.weight, ws, x.shape[-1] * ps.tp_size(), self.eps)
+        elif x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0:
+            # one kernel each way: the (1 + w) RMSNorm with w - 1 gives x r w
+            return N.rms_norm(x.contiguous(), self.weight - 1, self.eps)
         sq = x.float().square().sum(-1, keepdim=True)
         if ps.tp_size() > 1:
             sq = PL.reduce_tp(sq)

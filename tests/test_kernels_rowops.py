@@ -111,3 +111,37 @@ def test_column_sum(rows, cols):
     torch.testing.assert_close(got, x.float().sum(0), atol=1e-3, rtol=1e-4)
     again = _ext.ops().column_sum(x)
     assert torch.equal(got, again)   # fixed reduction order
+
+
+def test_rope_pairs_matches_reference():
+    from cq_pretrain_b200.ops import rope
+    torch.manual_seed(6)
+    x = torch.randn(300, 12, 128, device="cuda").to(torch.bfloat16).requires_grad_()
+    ang = torch.rand(300, 64, device="cuda") * 6
+    y = rope.rotary_pairs(x, ang.cos(), ang.sin())
+    xr = x.detach().float().requires_grad_()
+    yr = R.rotary_pairs(xr, ang.cos(), ang.sin())
+    torch.testing.assert_close(y.float(), yr, atol=2e-2, rtol=1e-2)
+    g = torch.randn_like(yr)
+    y.backward(g.to(y.dtype))
+    yr.backward(g)
+    torch.testing.assert_close(x.grad.float(), xr.grad, atol=3e-2, rtol=2e-2)
+
+
+def test_wan_rmsnorm_tp1_kernel_matches_torch():
+    from cq_pretrain_b200.models.wan21 import WanRMSNorm
+    torch.manual_seed(7)
+    norm = WanRMSNorm(1536, 1e-6).cuda()
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn_like(norm.weight))
+    x = torch.randn(500, 1536, device="cuda").to(torch.bfloat16).requires_grad_()
+    y = norm(x)
+    xr, wr = x.detach().float().requires_grad_(), norm.weight.detach().clone().requires_grad_()
+    yr = xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + 1e-6) * wr
+    torch.testing.assert_close(y.float(), yr, atol=3e-2, rtol=2e-2)
+    g = torch.randn_like(yr)
+    y.backward(g.to(y.dtype))
+    yr.backward(g)
+    torch.testing.assert_close(x.grad.float(), xr.grad, atol=5e-2, rtol=3e-2)
+    rel = (norm.weight.grad - wr.grad).norm() / wr.grad.norm()
+    assert rel < 2e-2
