@@ -54,9 +54,23 @@ def _chunk_stats(h, w, targets, lo):
     return mx, tgt, sexp
 
 
+DLOGITS_BUDGET = 4 << 30   # bytes of bf16 softmax gradients the kernel path may hold at once
+
+
+def _rows_per_pass(chunk, rows, vocab_shard, kernel):
+    """Rows per LM-head pass. ``chunk`` bounds memory on small devices; on the kernel path the
+    passes grow to a 4 GiB bf16 gradient buffer, because every pass's weight-gradient GEMM reads
+    and writes the whole fp32 ``main_grad`` of the head (2 GB at 248K x 2048)."""
+    if not kernel:
+        return chunk
+    fit = max(chunk, (DLOGITS_BUDGET // max(1, vocab_shard * 2)) // 128 * 128)
+    return max(1, min(rows, fit))
+
+
 class _LinearCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, weight, targets, chunk, group, rank):
+        chunk = _rows_per_pass(chunk, hidden.shape[0], weight.shape[0], _kernel_shapes(hidden, weight))
         lo = rank * weight.shape[0]
         total = torch.zeros((), dtype=torch.float32, device=hidden.device)
         lse_all = torch.empty(hidden.shape[0], dtype=torch.float32, device=hidden.device)

@@ -68,6 +68,6 @@ def test_flag_wait_times_out_with_status():
     assert 1.0 < elapsed < 30.0
     assert int(mine[0]) == 3 and int(elsewhere[0]) == 3
     # the context is still usable
-    a = torch.randn(256, 256, device="cuda", dtype=torch.bfloat16)
-    torch.testing.assert_close((a.float() @ a.float()).sum(), (a @ a).float().sum(), rtol=2e-2, atol=1.0)
+    x = torch.arange(1024, device="cuda", dtype=torch.float32)
+    assert torch.equal((x * 2).cpu(), torch.arange(0, 2048, 2, dtype=torch.float32))
     assert ops.comm_status_read(False) == 0
