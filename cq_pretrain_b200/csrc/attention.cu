@@ -1,239 +1,368 @@
-// Flash attention over per-row key ranges (forward, dQ, dK/dV) for sm_100a.
+// Tensor-core (tcgen05) flash attention over per-row key ranges for sm_100a: forward, dQ, dK/dV.
 //
-// Row r of a head reads keys [kstart[r], kend[r]) (the CQ visibility of a packed sequence, or
-// the sample of a varlen DiT row); empty ranges output zero. The mask is computed on the fly
-// from the two int32 vectors, and a 64-row block only visits key blocks inside the union of its
-// rows' ranges, so skipped work is exact. GQA: head h reads kv head h / (Hq / Hkv).
-// Online softmax in fp32 (exp2 domain); the forward stores the log-sum-exp per (head, row).
-// Backward (FlashAttention-2 split): a dQ kernel over row blocks and a dK/dV kernel over key
-// blocks (both recompute P from the saved LSE; no atomics). bf16 m16n8k16 tensor-core MMAs.
+// Row r of a head reads keys [kstart[r], kend[r]) (the CQ visibility of a packed sequence, or the
+// sample of a varlen DiT row); GQA (head h reads kv head h / (Hq / Hkv)); empty ranges output zero
+// with LSE = +inf; LSE in natural-log units. Key tiles outside the union of a block's ranges are
+// skipped, so skipped work is exact. Forward: one CTA per (128-row block, head):
+//  * warp 0 (one thread) streams the Q block once and K / V key tiles through a 2-deep ring
+//    with TMA (128-byte swizzle; D / 64 boxes per tile);
+//  * warp 1 allocates TMEM and issues the MMAs (one thread): S_j = Q K_j^T into one of two TMEM
+//    score buffers (so S_{j+1} runs while the softmax reads S_j) and O += P_j V_j into a TMEM
+//    accumulator that stays resident for the whole key loop (V is the MN-major B operand, so
+//    no transpose);
+//  * warps 2..5 own one query row per thread (TMEM lane = row): tcgen05.ld of the row's scores,
+//    range mask, exp2-domain softmax without any cross-thread reduction, P_j written to shared
+//    memory as bf16 in the 128B-swizzled K-major layout the MMA reads, and the epilogue
+//    (tcgen05.ld of O, 1/l, bf16 stores, LSE).
+// The running max is rescaled lazily: a row keeps its exponent reference until a tile's max
+// exceeds it by more than 8 (P <= 2^8), and only then rescales its O row in TMEM (tcgen05.ld /
+// st after the previous P V has retired). Numerator and denominator always share the
+// reference, so the result is exact up to rounding.
+// Tile sizes: BN = 64 keys at D = 256 (TMEM: 2 x 64 score + 256 O columns), 128 otherwise.
+// Every wait is bounded; on expiry the kernel records a code in the status word, stops
+// issuing, drains its TMA transactions and MMAs (bounded), frees TMEM and returns.
 #include "common.cuh"
-#include "mma_sync.cuh"
+#include "tcgen05.cuh"
 
 namespace cqb {
 
 namespace {
 
-using namespace ws;
+constexpr float LOG2E_TC = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.f;  // log2 units
 
-constexpr int BM = 64, BN = 64, THREADS = 128;
-constexpr float LOG2E = 1.4426950408889634f;
+int* attn_status_word() {
+  static int* word = [] {
+    int* p = nullptr;
+    CQB_CHECK_CUDA(cudaMalloc(&p, sizeof(int)));
+    CQB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+    return p;
+  }();
+  return word;
+}
 
-struct AttnArgs {
-  const __nv_bfloat16* q;   // [rows, Hq, D]
-  const __nv_bfloat16* k;   // [keys, Hkv, D]
-  const __nv_bfloat16* v;   // [keys, Hkv, D]
-  const __nv_bfloat16* o;   // [rows, Hq, D]   (backward)
-  const __nv_bfloat16* dout;  // [rows, Hq, D] (backward)
-  const int* kstart;        // [rows]
-  const int* kend;          // [rows]
-  const float* lse;         // [Hq, rows]      (backward)
-  const float* dsum;        // [Hq, rows]      (backward)
-  const int* qb_min;        // [q blocks]     (backward) key range union of each row block
-  const int* qb_max;
-  __nv_bfloat16* out;       // O / dQ / dK
-  __nv_bfloat16* out2;      // dV
-  float* lse_out;           // [Hq, rows]
+template <int D>
+struct FwdTc {
+  static constexpr int BM = 128;
+  static constexpr int BN = D == 256 ? 64 : 128;
+  static constexpr int KB = D / 64;                      // 64-wide boxes per row
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;            // one K or V tile
+  static constexpr int P_ATOM = BM * 128;                // 128 rows x 64 keys (bf16)
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int SMEM = Q_BYTES + 4 * KV_BYTES + 2 * P_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t O_COL = 2 * BN;
+};
+
+struct FwdTcArgs {
+  const int* kstart;
+  const int* kend;
+  __nv_bfloat16* out;  // [rows, Hq, D]
+  float* lse;          // [Hq, rows]
   int rows, keys, Hq, Hkv;
-  float scale;              // softmax scale
+  float scale;
 };
 
 template <int D>
-__device__ __forceinline__ void load_rows(__nv_bfloat16* dst, const __nv_bfloat16* src, int r0, int nrows, int stride,
-                                          int tid) {
-  constexpr int LD = D + 8;
-  constexpr int VPR = D / 8;  // 16-byte vectors per row
-  for (int i = tid; i < BM * VPR; i += THREADS) {
-    const int r = i / VPR, c = (i % VPR) * 8;
-    const bool ok = r0 + r < nrows;
-    cp_async16(dst + r * LD + c, src + (size_t)(ok ? r0 + r : 0) * stride + c, ok);
-  }
-}
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, FwdTcArgs a, int* status) {
+  using C = FwdTc<D>;
+  constexpr int BM = C::BM, BN = C::BN, KB = C::KB;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + C::Q_BYTES;            // [2][KV_BYTES]
+  uint8_t* sv = sk + 2 * C::KV_BYTES;       // [2][KV_BYTES]
+  uint8_t* sp = sv + 2 * C::KV_BYTES;       // [2][P_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * C::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;  // [2]
+  uint64_t* pv_done = bars + 13; // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_range = reinterpret_cast<int*>(tmem_slot + 2);
 
-// ---- forward ------------------------------------------------------------------------------
-template <int D>
-__global__ void __launch_bounds__(THREADS) attn_fwd_kernel(AttnArgs a) {
-  constexpr int LD = D + 8;
-  extern __shared__ __align__(16) __nv_bfloat16 sm[];
-  __nv_bfloat16* qs = sm;
-  __nv_bfloat16* ks = qs + BM * LD;   // [2][BN][LD]
-  __nv_bfloat16* vs = ks + 2 * BN * LD;
-  __shared__ int s_range[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = blockIdx.x, h = blockIdx.y, hk = h / (a.Hq / a.Hkv);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int r0 = qb * BM;
-  // union of the block's key ranges
-  {
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&k_full[b], 1);
+      tc::mbar_init(&k_empty[b], 1);
+      tc::mbar_init(&v_full[b], 1);
+      tc::mbar_init(&v_empty[b], 1);
+      tc::mbar_init(&s_full[b], 1);
+      tc::mbar_init(&p_full[b], 128);
+      tc::mbar_init(&pv_done[b], 1);
+    }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    s_range[0] = INT_MAX;
+    s_range[1] = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+  __syncthreads();
+  // union of the block's key ranges -> key tiles [kt0, kt0 + nt * BN)
+  if (threadIdx.x < BM) {
+    const int row = r0 + threadIdx.x;
     int lo = INT_MAX, hi = 0;
-    for (int r = tid; r < BM; r += THREADS) {
-      const int row = r0 + r;
-      if (row < a.rows) {
-        const int s = a.kstart[row], e = a.kend[row];
-        if (e > s) {
-          lo = min(lo, s);
-          hi = max(hi, e);
-        }
-      }
+    if (row < a.rows) {
+      const int s = a.kstart[row], e = a.kend[row];
+      if (e > s) lo = s, hi = e;
     }
-    for (int o = 16; o; o >>= 1) {
-      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-    }
-    if (tid == 0) s_range[0] = INT_MAX, s_range[1] = 0;
-    __syncthreads();
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
     if (lane == 0) {
       atomicMin(&s_range[0], lo);
       atomicMax(&s_range[1], hi);
     }
-    __syncthreads();
   }
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
   const int klo = s_range[0], khi = s_range[1];
-  const int row_a = r0 + warp * 16 + g, row_b = row_a + 8;
-  const int ks_a = row_a < a.rows ? a.kstart[row_a] : 0, ke_a = row_a < a.rows ? a.kend[row_a] : 0;
-  const int ks_b = row_b < a.rows ? a.kstart[row_b] : 0, ke_b = row_b < a.rows ? a.kend[row_b] : 0;
-  float acc[D / 8][4];
+  const int kt0 = klo < khi ? (klo / BN) * BN : 0;
+  const int nt = klo < khi ? (khi - kt0 + BN - 1) / BN : 0;
+
+  if (warp == 0) {
+    if (lane == 0 && nt > 0) {
+      tc::prefetch_map(&map_q);
+      tc::prefetch_map(&map_k);
+      tc::prefetch_map(&map_v);
+      int armed_k[2] = {-1, -1}, armed_v[2] = {-1, -1};
+      bool ok = true;
+      tc::mbar_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
-  for (int j = 0; j < D / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  const float sl2 = a.scale * LOG2E;
-  const int qstride = a.Hq * D, kstride = a.Hkv * D;
-  if (klo < khi) {
-    load_rows<D>(qs, a.q + (size_t)h * D, r0, a.rows, qstride, tid);
-    const int nb0 = (klo / BN) * BN;
-    load_rows<D>(ks, a.k + (size_t)hk * D, nb0, a.keys, kstride, tid);
-    load_rows<D>(vs, a.v + (size_t)hk * D, nb0, a.keys, kstride, tid);
-    cp_commit();
-    int buf = 0;
-    for (int n0 = nb0; n0 < khi; n0 += BN, buf ^= 1) {
-      if (n0 + BN < khi) {
-        load_rows<D>(ks + (buf ^ 1) * BN * LD, a.k + (size_t)hk * D, n0 + BN, a.keys, kstride, tid);
-        load_rows<D>(vs + (buf ^ 1) * BN * LD, a.v + (size_t)hk * D, n0 + BN, a.keys, kstride, tid);
-        cp_commit();
-        cp_wait_1();
-      } else {
-        cp_wait_all();
+      for (int i = 0; i < KB; ++i) tc::tma_load_2d(sq + i * BM * 128, &map_q, q_full, h * D + i * 64, r0);
+      for (int j = 0; j < nt && ok; ++j) {
+        const int b = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int n0 = kt0 + j * BN;
+        if (!tc::mbar_wait(&k_empty[b], ph ^ 1, status, abort_flag, 31)) { ok = false; break; }
+        tc::mbar_expect_tx(&k_full[b], C::KV_BYTES);
+#pragma unroll
+        for (int i = 0; i < KB; ++i)
+          tc::tma_load_2d(sk + b * C::KV_BYTES + i * BN * 128, &map_k, &k_full[b], hk * D + i * 64, n0);
+        armed_k[b] = (int)ph;
+        if (!tc::mbar_wait(&v_empty[b], ph ^ 1, status, abort_flag, 32)) { ok = false; break; }
+        tc::mbar_expect_tx(&v_full[b], C::KV_BYTES);
+#pragma unroll
+        for (int i = 0; i < KB; ++i)
+          tc::tma_load_2d(sv + b * C::KV_BYTES + i * BN * 128, &map_v, &v_full[b], hk * D + i * 64, n0);
+        armed_v[b] = (int)ph;
       }
-      __syncthreads();
-      const __nv_bfloat16* kt = ks + buf * BN * LD;
-      const __nv_bfloat16* vt = vs + buf * BN * LD;
-      float s[BN / 8][4];
+      // drain: every issued transaction lands before the CTA's shared memory is released
+      const unsigned long long t0 = tc::globaltimer();
+      while (!tc::mbar_try_wait(q_full, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+      for (int b = 0; b < 2; ++b) {
+        if (armed_k[b] >= 0)
+          while (!tc::mbar_try_wait(&k_full[b], (uint32_t)armed_k[b]) && tc::globaltimer() - t0 < tc::kWaitNs) {
+          }
+        if (armed_v[b] >= 0)
+          while (!tc::mbar_try_wait(&v_full[b], (uint32_t)armed_v[b]) && tc::globaltimer() - t0 < tc::kWaitNs) {
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t idesc_s = tc::idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_o = tc::idesc_bf16(BM, D, false, true);
+      const uint32_t q_addr = tc::smem_u32(sq), k_addr = tc::smem_u32(sk), v_addr = tc::smem_u32(sv),
+                     p_addr = tc::smem_u32(sp);
+      auto issue_s = [&](int j) -> bool {
+        const int b = j & 1;
+        if (!tc::mbar_wait(&k_full[b], (j >> 1) & 1, status, abort_flag, 33)) return false;
+        tc::fence_after();
+        const uint32_t kb_addr = k_addr + b * C::KV_BYTES;
 #pragma unroll
-      for (int j = 0; j < BN / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t ad = tc::smem_desc(q_addr + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc(kb_addr + (k >> 2) * (BN * 128) + (k & 3) * 32, 16, 1024);
+          tc::mma_bf16(tmem + b * BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&k_empty[b]);
+        tc::mma_commit(&s_full[b]);
+        return true;
+      };
+      bool ok = tc::mbar_wait(q_full, 0, status, abort_flag, 34);
+      if (ok) {
+        tc::fence_after();
+        ok = issue_s(0);
+      }
+      for (int j = 0; j < nt && ok; ++j) {
+        if (j + 1 < nt && !issue_s(j + 1)) break;
+        const int b = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!tc::mbar_wait(&p_full[b], ph, status, abort_flag, 35)) break;
+        if (!tc::mbar_wait(&v_full[b], ph, status, abort_flag, 36)) break;
+        tc::fence_after();
+        const uint32_t vb_addr = v_addr + b * C::KV_BYTES, pb_addr = p_addr + b * C::P_BYTES;
 #pragma unroll
-      for (int kk = 0; kk < D; kk += 16) {
-        uint32_t af[4];
-        frag_a(af, qs, warp * 16, kk, LD, lane);
+        for (int k = 0; k < BN / 16; ++k) {
+          const uint64_t ad = tc::smem_desc(pb_addr + (k >> 2) * C::P_ATOM + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc(vb_addr + k * 2048, BN * 128, 1024);
+          tc::mma_bf16(tmem + C::O_COL, ad, bd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&v_empty[b]);
+        tc::mma_commit(&pv_done[b]);
+      }
+      tc::mma_commit(drain);
+      const unsigned long long t0 = tc::globaltimer();
+      while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    }
+  } else {
+    // softmax / epilogue: one query row per thread
+    const int quarter = warp & 3;
+    const int rl = quarter * 32 + lane, row = r0 + rl;
+    const bool valid = row < a.rows;
+    const int rks = valid ? a.kstart[row] : 0, rke = valid ? a.kend[row] : 0;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float sl2 = a.scale * LOG2E_TC;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    // warp-uniform bounded wait (the TMEM loads and stores that follow are warp-collective)
+    auto wwait = [&](uint64_t* bar, uint32_t parity, int code) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, abort_flag, code));
+    };
+    for (int j = 0; j < nt; ++j) {
+      const int b = j & 1;
+      if (!wwait(&s_full[b], (j >> 1) & 1, 37)) { ok = false; break; }
+      tc::fence_after();
+      const int n0 = kt0 + j * BN;
+      float s[BN];
 #pragma unroll
-        for (int j = 0; j < BN / 8; j += 2) {
-          uint32_t bf[4];
-          frag_bt2(bf, kt, kk, j * 8, LD, lane);
-          mma16816(s[j], af, bf[0], bf[1]);
-          mma16816(s[j + 1], af, bf[2], bf[3]);
+      for (int c = 0; c < BN; c += 32) tc::tmem_ld32(lane_base + b * BN + c, s + c);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int key = n0 + c;
+        s[c] = (key >= rks && key < rke) ? s[c] * sl2 : -INFINITY;
+        mt = fmaxf(mt, s[c]);
+      }
+      const bool need = mt > m_ref + RESCALE_THRESHOLD;
+      const float corr = (need && m_ref != -INFINITY) ? exp2f(m_ref - mt) : 1.f;
+      if (__any_sync(0xffffffffu, corr != 1.f)) {
+        // O holds P_0..P_{j-1} V: wait for the last P V before rescaling this warp's rows
+        if (!wwait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 38)) { ok = false; break; }
+        tc::fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tc::tmem_ld32(lane_base + C::O_COL + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          tc::tmem_st32(lane_base + C::O_COL + c, o);
         }
       }
-      // mask + online softmax (log2 domain)
-      float mx_a = m_a, mx_b = m_b;
+      if (need) m_ref = mt;
+      l *= corr;
+      const float mr = m_ref == -INFINITY ? 0.f : m_ref;
+      // P buffer b was read by P_{j-2} V
+      if (j >= 2 && !wwait(&pv_done[b], ((j >> 1) + 1) & 1, 39)) { ok = false; break; }
+      uint8_t* prow = sp + b * C::P_BYTES + rl * 128;
 #pragma unroll
-      for (int j = 0; j < BN / 8; ++j) {
+      for (int c8 = 0; c8 < BN / 8; ++c8) {
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = n0 + j * 8 + 2 * t + e;
-          s[j][e] = (key >= ks_a && key < ke_a) ? s[j][e] * sl2 : -INFINITY;
-          s[j][2 + e] = (key >= ks_b && key < ke_b) ? s[j][2 + e] * sl2 : -INFINITY;
-          mx_a = fmaxf(mx_a, s[j][e]);
-          mx_b = fmaxf(mx_b, s[j][2 + e]);
+        for (int i = 0; i < 4; ++i) {
+          const float p0 = exp2f(s[c8 * 8 + 2 * i] - mr), p1 = exp2f(s[c8 * 8 + 2 * i + 1] - mr);
+          l += p0 + p1;
+          __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+          w[i] = *reinterpret_cast<uint32_t*>(&v2);
+        }
+        const int atom = c8 >> 3, chunk = (c8 & 7) ^ (rl & 7);
+        *reinterpret_cast<uint4*>(prow + atom * C::P_ATOM + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      tc::fence_proxy_async();
+      tc::fence_before();
+      tc::mbar_arrive(&p_full[b]);
+    }
+    if (ok && nt > 0 && !wwait(&pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, 40)) ok = false;
+    if (ok) {
+      tc::fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = a.out + ((size_t)row * a.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        if (nt > 0) {
+          tc::tmem_ld32(lane_base + C::O_COL + c, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(o[i + 2 * e] * inv, o[i + 2 * e + 1] * inv);
+              w[e] = *reinterpret_cast<uint32_t*>(&v2);
+            }
+            *reinterpret_cast<uint4*>(dst + c + i) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
         }
       }
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-      const float ref_a = mx_a == -INFINITY ? 0.f : mx_a, ref_b = mx_b == -INFINITY ? 0.f : mx_b;
-      const float corr_a = exp2f((m_a == -INFINITY ? ref_a : m_a) - ref_a);
-      const float corr_b = exp2f((m_b == -INFINITY ? ref_b : m_b) - ref_b);
-      m_a = mx_a;
-      m_b = mx_b;
-      l_a *= corr_a;
-      l_b *= corr_b;
-#pragma unroll
-      for (int j = 0; j < D / 8; ++j) {
-        acc[j][0] *= corr_a;
-        acc[j][1] *= corr_a;
-        acc[j][2] *= corr_b;
-        acc[j][3] *= corr_b;
-      }
-#pragma unroll
-      for (int j = 0; j < BN / 8; ++j) {
-        s[j][0] = exp2f(s[j][0] - ref_a);
-        s[j][1] = exp2f(s[j][1] - ref_a);
-        s[j][2] = exp2f(s[j][2] - ref_b);
-        s[j][3] = exp2f(s[j][3] - ref_b);
-        l_a += s[j][0] + s[j][1];
-        l_b += s[j][2] + s[j][3];
-      }
-      // O += P V
-#pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk) {
-        uint32_t af[4];
-        acc_to_a(af, s[2 * kk], s[2 * kk + 1]);
-#pragma unroll
-        for (int j = 0; j < D / 8; j += 2) {
-          uint32_t bf[4];
-          frag_b2(bf, vt, kk * 16, j * 8, LD, lane);
-          mma16816(acc[j], af, bf[0], bf[1]);
-          mma16816(acc[j + 1], af, bf[2], bf[3]);
-        }
-      }
-      __syncthreads();  // this buffer may be refilled by the next prefetch
+      if (valid) a.lse[(size_t)h * a.rows + row] = l > 0.f ? (m_ref + log2f(l)) / LOG2E_TC : INFINITY;
     }
   }
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f, inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
-  if (row_a < a.rows) {
-    __nv_bfloat16* dst = a.out + ((size_t)row_a * a.Hq + h) * D;
-#pragma unroll
-    for (int j = 0; j < D / 8; ++j)
-      *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t) = __floats2bfloat162_rn(acc[j][0] * inv_a, acc[j][1] * inv_a);
-    if (t == 0) a.lse_out[(size_t)h * a.rows + row_a] = l_a > 0.f ? (m_a + log2f(l_a)) / LOG2E : INFINITY;
-  }
-  if (row_b < a.rows) {
-    __nv_bfloat16* dst = a.out + ((size_t)row_b * a.Hq + h) * D;
-#pragma unroll
-    for (int j = 0; j < D / 8; ++j)
-      *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t) = __floats2bfloat162_rn(acc[j][2] * inv_b, acc[j][3] * inv_b);
-    if (t == 0) a.lse_out[(size_t)h * a.rows + row_b] = l_b > 0.f ? (m_b + log2f(l_b)) / LOG2E : INFINITY;
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
-// ---- backward prep: Dsum = rowsum(dO * O), row-block key ranges -----------------------------
-template <int D>
-__global__ void attn_bwd_prep_kernel(AttnArgs a, float* dsum, int* qb_min, int* qb_max) {
+// ---- backward -------------------------------------------------------------------------------
+// Prep: per (head, row) the exponent reference lse * log2(e) (+inf for empty rows and padding)
+// and Dsum = rowsum(dO * O), packed as float2 over rows padded to a multiple of 64; per row the
+// (kstart, kend) pair (0, 0 in padding); per 64-row block the union of its rows' key ranges.
+__global__ void attn_bwd_prep_tc_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                        const float* __restrict__ lse, const int* __restrict__ kstart,
+                                        const int* __restrict__ kend, float2* __restrict__ lsd, int2* __restrict__ kse,
+                                        int* __restrict__ qb_min, int* __restrict__ qb_max, int rows, int rows_pad,
+                                        int Hq, int D) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int total = a.rows * a.Hq;
-  if (warp < total) {
-    const int row = warp / a.Hq, h = warp % a.Hq;
-    const __nv_bfloat16* o = a.o + ((size_t)row * a.Hq + h) * D;
-    const __nv_bfloat16* d = a.dout + ((size_t)row * a.Hq + h) * D;
-    float s = 0.f;
-    for (int c = lane * 8; c < D; c += 256) {
-      float ov[8], dv[8];
-      load8(o + c, ov);
-      load8(d + c, dv);
+  if (warp < rows_pad * Hq) {
+    const int row = warp / Hq, h = warp % Hq;
+    float s = 0.f, l2 = INFINITY;
+    if (row < rows) {
+      const __nv_bfloat16* op = o + ((size_t)row * Hq + h) * D;
+      const __nv_bfloat16* dp = dout + ((size_t)row * Hq + h) * D;
+      for (int c = lane * 8; c < D; c += 256) {
+        float ov[8], dv[8];
+        load8(op + c, ov);
+        load8(dp + c, dv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s += ov[j] * dv[j];
+        for (int j = 0; j < 8; ++j) s += ov[j] * dv[j];
+      }
+      s = warp_sum(s);
+      const float l = lse[(size_t)h * rows + row];
+      l2 = l == INFINITY ? INFINITY : l * LOG2E_TC;
     }
-    s = warp_sum(s);
-    if (lane == 0) dsum[(size_t)h * a.rows + row] = s;
+    if (lane == 0) lsd[(size_t)h * rows_pad + row] = make_float2(l2, s);
+    if (lane == 0 && h == 0) kse[row] = row < rows ? make_int2(kstart[row], kend[row]) : make_int2(0, 0);
   }
-  // block ranges: one thread per row block
   const int qb = blockIdx.x * blockDim.x + threadIdx.x;
-  if (qb < (a.rows + BM - 1) / BM) {
+  if (qb < rows_pad / 64) {
     int lo = INT_MAX, hi = 0;
-    for (int r = qb * BM; r < min(a.rows, qb * BM + BM); ++r) {
-      const int s = a.kstart[r], e = a.kend[r];
+    for (int r = qb * 64; r < min(rows, qb * 64 + 64); ++r) {
+      const int s = kstart[r], e = kend[r];
       if (e > s) {
         lo = min(lo, s);
         hi = max(hi, e);
@@ -244,343 +373,681 @@ __global__ void attn_bwd_prep_kernel(AttnArgs a, float* dsum, int* qb_min, int* 
   }
 }
 
-// ---- backward dQ --------------------------------------------------------------------------
+struct BwdTcArgs {
+  const float2* lsd;   // [Hq, rows_pad]
+  const int2* kse;     // [rows_pad]
+  const int* qb_min;   // [rows_pad / 64]
+  const int* qb_max;
+  __nv_bfloat16* dq;   // [rows, Hq, D]
+  __nv_bfloat16* dk;   // [keys, Hkv, D]
+  __nv_bfloat16* dv;
+  int rows, rows_pad, keys, Hq, Hkv;
+  float scale;
+};
+
+// dQ: one CTA per (128-row block, head); key tiles of 64. S = Q K^T and dP = dO V^T land in
+// double-buffered TMEM; each softmax thread (one row) forms dS = P (dP - Dsum) and writes it to
+// shared memory (bf16, 128B-swizzled K-major); dQ += dS K accumulates in TMEM (K is the MN-major B
+// operand: the same shared tile that fed S).
 template <int D>
-__global__ void __launch_bounds__(THREADS) attn_bwd_dq_kernel(AttnArgs a) {
-  constexpr int LD = D + 8;
-  extern __shared__ __align__(16) __nv_bfloat16 sm[];
-  __nv_bfloat16* qs = sm;
-  __nv_bfloat16* dos = qs + BM * LD;
-  __nv_bfloat16* ks = dos + BM * LD;   // [2][BN][LD]
-  __nv_bfloat16* vs = ks + 2 * BN * LD;
+struct DqTc {
+  static constexpr int BM = 128, BN = 64, KB = D / 64;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int DS_BYTES = BM * BN * 2;
+  static constexpr int STAGES = D > 128 ? 1 : 2;
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * STAGES * KV_BYTES + 2 * DS_BYTES + 1024 + 256;
+  static constexpr uint32_t DP_COL = 2 * BN, DQ_COL = 4 * BN;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_do,
+                      const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                      BwdTcArgs a, int* status) {
+  using C = DqTc<D>;
+  constexpr int BM = C::BM, BN = C::BN, KB = C::KB, ST = C::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sdo = sq + C::Q_BYTES;
+  uint8_t* sk = sdo + C::Q_BYTES;            // [ST][KV_BYTES]
+  uint8_t* sv = sk + ST * C::KV_BYTES;       // [ST][KV_BYTES]
+  uint8_t* sds = sv + ST * C::KV_BYTES;      // [2][DS_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + 2 * C::DS_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* ds_full = bars + 11;  // [2]
+  uint64_t* dq_done = bars + 13;  // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_range = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = blockIdx.x, h = blockIdx.y, hk = h / (a.Hq / a.Hkv);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int r0 = qb * BM;
-  const int klo = a.qb_min[qb], khi = a.qb_max[qb];
-  const int row_a = r0 + warp * 16 + g, row_b = row_a + 8;
-  const bool va = row_a < a.rows, vb = row_b < a.rows;
-  const int ks_a = va ? a.kstart[row_a] : 0, ke_a = va ? a.kend[row_a] : 0;
-  const int ks_b = vb ? a.kstart[row_b] : 0, ke_b = vb ? a.kend[row_b] : 0;
-  const float lse_a = va ? a.lse[(size_t)h * a.rows + row_a] * LOG2E : INFINITY;
-  const float lse_b = vb ? a.lse[(size_t)h * a.rows + row_b] * LOG2E : INFINITY;
-  const float ds_a = va ? a.dsum[(size_t)h * a.rows + row_a] : 0.f;
-  const float ds_b = vb ? a.dsum[(size_t)h * a.rows + row_b] : 0.f;
-  float acc[D / 8][4];
-#pragma unroll
-  for (int j = 0; j < D / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const float sl2 = a.scale * LOG2E;
-  const int qstride = a.Hq * D, kstride = a.Hkv * D;
-  if (klo < khi) {
-    load_rows<D>(qs, a.q + (size_t)h * D, r0, a.rows, qstride, tid);
-    load_rows<D>(dos, a.dout + (size_t)h * D, r0, a.rows, qstride, tid);
-    const int nb0 = (klo / BN) * BN;
-    load_rows<D>(ks, a.k + (size_t)hk * D, nb0, a.keys, kstride, tid);
-    load_rows<D>(vs, a.v + (size_t)hk * D, nb0, a.keys, kstride, tid);
-    cp_commit();
-    int buf = 0;
-    for (int n0 = nb0; n0 < khi; n0 += BN, buf ^= 1) {
-      if (n0 + BN < khi) {
-        load_rows<D>(ks + (buf ^ 1) * BN * LD, a.k + (size_t)hk * D, n0 + BN, a.keys, kstride, tid);
-        load_rows<D>(vs + (buf ^ 1) * BN * LD, a.v + (size_t)hk * D, n0 + BN, a.keys, kstride, tid);
-        cp_commit();
-        cp_wait_1();
-      } else {
-        cp_wait_all();
-      }
-      __syncthreads();
-      const __nv_bfloat16* kt = ks + buf * BN * LD;
-      const __nv_bfloat16* vt = vs + buf * BN * LD;
-      float s[BN / 8][4], dp[BN / 8][4];
-#pragma unroll
-      for (int j = 0; j < BN / 8; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s[j][e] = dp[j][e] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < D; kk += 16) {
-        uint32_t aq[4], ad[4];
-        frag_a(aq, qs, warp * 16, kk, LD, lane);
-        frag_a(ad, dos, warp * 16, kk, LD, lane);
-#pragma unroll
-        for (int j = 0; j < BN / 8; j += 2) {
-          uint32_t bk[4], bv[4];
-          frag_bt2(bk, kt, kk, j * 8, LD, lane);
-          frag_bt2(bv, vt, kk, j * 8, LD, lane);
-          mma16816(s[j], aq, bk[0], bk[1]);
-          mma16816(s[j + 1], aq, bk[2], bk[3]);
-          mma16816(dp[j], ad, bv[0], bv[1]);
-          mma16816(dp[j + 1], ad, bv[2], bv[3]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < BN / 8; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = n0 + j * 8 + 2 * t + e;
-          const float pa = (key >= ks_a && key < ke_a) ? exp2f(s[j][e] * sl2 - lse_a) : 0.f;
-          const float pb = (key >= ks_b && key < ke_b) ? exp2f(s[j][2 + e] * sl2 - lse_b) : 0.f;
-          s[j][e] = pa * (dp[j][e] - ds_a);
-          s[j][2 + e] = pb * (dp[j][2 + e] - ds_b);
-        }
-      }
-      // dQ += dS K
-#pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk) {
-        uint32_t af[4];
-        acc_to_a(af, s[2 * kk], s[2 * kk + 1]);
-#pragma unroll
-        for (int j = 0; j < D / 8; j += 2) {
-          uint32_t bf[4];
-          frag_b2(bf, kt, kk * 16, j * 8, LD, lane);
-          mma16816(acc[j], af, bf[0], bf[1]);
-          mma16816(acc[j + 1], af, bf[2], bf[3]);
-        }
-      }
-      __syncthreads();
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&k_full[b], 1);
+      tc::mbar_init(&k_empty[b], 1);
+      tc::mbar_init(&v_full[b], 1);
+      tc::mbar_init(&v_empty[b], 1);
+      tc::mbar_init(&s_full[b], 1);
+      tc::mbar_init(&ds_full[b], 128);
+      tc::mbar_init(&dq_done[b], 1);
+    }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    s_range[0] = INT_MAX;
+    s_range[1] = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  if (threadIdx.x < BM) {
+    const int2 r = a.kse[min(r0 + (int)threadIdx.x, a.rows_pad - 1)];
+    int lo = INT_MAX, hi = 0;
+    if (r0 + (int)threadIdx.x < a.rows && r.y > r.x) lo = r.x, hi = r.y;
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    if (lane == 0) {
+      atomicMin(&s_range[0], lo);
+      atomicMax(&s_range[1], hi);
     }
   }
-  if (va) {
-    __nv_bfloat16* dst = a.out + ((size_t)row_a * a.Hq + h) * D;
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int klo = s_range[0], khi = s_range[1];
+  const int kt0 = klo < khi ? (klo / BN) * BN : 0;
+  const int nt = klo < khi ? (khi - kt0 + BN - 1) / BN : 0;
+
+  if (warp == 0) {
+    if (lane == 0 && nt > 0) {
+      tc::prefetch_map(&map_q);
+      tc::prefetch_map(&map_do);
+      tc::prefetch_map(&map_k);
+      tc::prefetch_map(&map_v);
+      int armed_k[2] = {-1, -1}, armed_v[2] = {-1, -1};
+      tc::mbar_expect_tx(q_full, 2 * C::Q_BYTES);
 #pragma unroll
-    for (int j = 0; j < D / 8; ++j)
-      *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t) =
-          __floats2bfloat162_rn(acc[j][0] * a.scale, acc[j][1] * a.scale);
+      for (int i = 0; i < KB; ++i) {
+        tc::tma_load_2d(sq + i * BM * 128, &map_q, q_full, h * D + i * 64, r0);
+        tc::tma_load_2d(sdo + i * BM * 128, &map_do, q_full, h * D + i * 64, r0);
+      }
+      for (int j = 0; j < nt; ++j) {
+        const int s = j % ST;
+        const uint32_t ph = (j / ST) & 1;
+        const int n0 = kt0 + j * BN;
+        if (!tc::mbar_wait(&v_empty[s], ph ^ 1, status, abort_flag, 41)) break;
+        tc::mbar_expect_tx(&v_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int i = 0; i < KB; ++i)
+          tc::tma_load_2d(sv + s * C::KV_BYTES + i * BN * 128, &map_v, &v_full[s], hk * D + i * 64, n0);
+        armed_v[s] = (int)ph;
+        if (!tc::mbar_wait(&k_empty[s], ph ^ 1, status, abort_flag, 42)) break;
+        tc::mbar_expect_tx(&k_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int i = 0; i < KB; ++i)
+          tc::tma_load_2d(sk + s * C::KV_BYTES + i * BN * 128, &map_k, &k_full[s], hk * D + i * 64, n0);
+        armed_k[s] = (int)ph;
+      }
+      const unsigned long long t0 = tc::globaltimer();
+      while (!tc::mbar_try_wait(q_full, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+      for (int s = 0; s < 2; ++s) {
+        if (armed_k[s] >= 0)
+          while (!tc::mbar_try_wait(&k_full[s], (uint32_t)armed_k[s]) && tc::globaltimer() - t0 < tc::kWaitNs) {
+          }
+        if (armed_v[s] >= 0)
+          while (!tc::mbar_try_wait(&v_full[s], (uint32_t)armed_v[s]) && tc::globaltimer() - t0 < tc::kWaitNs) {
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t idesc_s = tc::idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_q = tc::idesc_bf16(BM, D, false, true);
+      const uint32_t q_addr = tc::smem_u32(sq), do_addr = tc::smem_u32(sdo), k_addr = tc::smem_u32(sk),
+                     v_addr = tc::smem_u32(sv), ds_addr = tc::smem_u32(sds);
+      // X [BM x D] (K-major) times tile [BN x D]^T -> TMEM columns col
+      auto rows_x_tile = [&](uint32_t x_addr, uint32_t t_addr, uint32_t col) {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t ad = tc::smem_desc(x_addr + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc(t_addr + (k >> 2) * (BN * 128) + (k & 3) * 32, 16, 1024);
+          tc::mma_bf16(tmem + col, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_dp = [&](int j) -> bool {
+        const int s = j % ST;
+        if (!tc::mbar_wait(&v_full[s], (j / ST) & 1, status, abort_flag, 43)) return false;
+        tc::fence_after();
+        rows_x_tile(do_addr, v_addr + s * C::KV_BYTES, C::DP_COL + (j & 1) * BN);
+        tc::mma_commit(&v_empty[s]);
+        return true;
+      };
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % ST;
+        if (!tc::mbar_wait(&k_full[s], (j / ST) & 1, status, abort_flag, 44)) return false;
+        tc::fence_after();
+        rows_x_tile(q_addr, k_addr + s * C::KV_BYTES, (j & 1) * BN);
+        tc::mma_commit(&s_full[j & 1]);
+        return true;
+      };
+      auto issue_dq = [&](int j) -> bool {
+        const int b = j & 1, s = j % ST;
+        if (!tc::mbar_wait(&ds_full[b], (j >> 1) & 1, status, abort_flag, 45)) return false;
+        tc::fence_after();
+        const uint32_t kt = k_addr + s * C::KV_BYTES, dst = ds_addr + b * C::DS_BYTES;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          const uint64_t ad = tc::smem_desc(dst + k * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc(kt + k * 2048, BN * 128, 1024);
+          tc::mma_bf16(tmem + C::DQ_COL, ad, bd, idesc_q, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&k_empty[s]);
+        tc::mma_commit(&dq_done[b]);
+        return true;
+      };
+      bool ok = tc::mbar_wait(q_full, 0, status, abort_flag, 46);
+      if (ok) tc::fence_after();
+      for (int j = 0; j < nt && ok; ++j) {
+        // one K/V stage: dQ_{j-1} must release K before S_j can load it
+        ok = issue_dp(j);
+        if (ok && ST == 1 && j > 0) ok = issue_dq(j - 1);
+        if (ok) ok = issue_s(j);
+        if (ok && ST == 2 && j > 0) ok = issue_dq(j - 1);
+      }
+      if (ok) issue_dq(nt - 1);
+      tc::mma_commit(drain);
+      const unsigned long long t0 = tc::globaltimer();
+      while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int rl = quarter * 32 + lane, row = r0 + rl;
+    const bool valid = row < a.rows;
+    const float2 info = a.lsd[(size_t)h * a.rows_pad + min(row, a.rows_pad - 1)];
+    const int2 rng = valid ? a.kse[row] : make_int2(0, 0);
+    const float lse2 = valid ? info.x : INFINITY, dsum = info.y;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float sl2 = a.scale * LOG2E_TC;
+    auto wwait = [&](uint64_t* bar, uint32_t parity, int code) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, abort_flag, code));
+    };
+    bool ok = true;
+    for (int j = 0; j < nt && ok; ++j) {
+      const int b = j & 1;
+      if (!wwait(&s_full[b], (j >> 1) & 1, 47)) { ok = false; break; }
+      tc::fence_after();
+      if (j >= 2 && !wwait(&dq_done[b], ((j >> 1) + 1) & 1, 48)) { ok = false; break; }
+      const int n0 = kt0 + j * BN;
+      uint8_t* drow = sds + b * C::DS_BYTES + rl * 128;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        float sv[32], pv[32];
+        tc::tmem_ld32(lane_base + b * BN + c, sv);
+        tc::tmem_ld32(lane_base + C::DP_COL + b * BN + c, pv);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float d2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int i = c8 * 8 + 2 * e + u, key = n0 + c + i;
+              const float p = (key >= rng.x && key < rng.y) ? exp2f(sv[i] * sl2 - lse2) : 0.f;
+              d2[u] = p * (pv[i] - dsum);
+            }
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(d2[0], d2[1]);
+            w[e] = *reinterpret_cast<uint32_t*>(&v2);
+          }
+          const int chunk = ((c >> 3) + c8) ^ (rl & 7);
+          *reinterpret_cast<uint4*>(drow + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::fence_before();
+      tc::mbar_arrive(&ds_full[b]);
+    }
+    if (ok && nt > 0 && !wwait(&dq_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, 49)) ok = false;
+    if (ok) {
+      tc::fence_after();
+      __nv_bfloat16* dst = a.dq + ((size_t)row * a.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        float v[32];
+        if (nt > 0) {
+          tc::tmem_ld32(lane_base + C::DQ_COL + c, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(v[i + 2 * e] * a.scale, v[i + 2 * e + 1] * a.scale);
+              w[e] = *reinterpret_cast<uint32_t*>(&v2);
+            }
+            *reinterpret_cast<uint4*>(dst + c + i) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
   }
-  if (vb) {
-    __nv_bfloat16* dst = a.out + ((size_t)row_b * a.Hq + h) * D;
-#pragma unroll
-    for (int j = 0; j < D / 8; ++j)
-      *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t) =
-          __floats2bfloat162_rn(acc[j][2] * a.scale, acc[j][3] * a.scale);
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 512);
   }
 }
 
-// ---- backward dK / dV (key blocks; value-dim slice DS per CTA) ------------------------------
-template <int D, int DS>
-__global__ void __launch_bounds__(THREADS) attn_bwd_dkv_kernel(AttnArgs a) {
-  constexpr int LD = D + 8;
-  extern __shared__ __align__(16) __nv_bfloat16 sm[];
-  __nv_bfloat16* ks = sm;
-  __nv_bfloat16* vs = ks + BN * LD;
-  __nv_bfloat16* qs = vs + BN * LD;
-  __nv_bfloat16* dos = qs + BM * LD;
-  __shared__ float s_lse[BM], s_ds[BM];
-  __shared__ int s_ks[BM], s_ke[BM];
-  const int kb = blockIdx.x, hk = blockIdx.y, d0 = blockIdx.z * DS;
-  const int group = a.Hq / a.Hkv;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int n0 = kb * BN;
-  const int key_a = n0 + warp * 16 + g, key_b = key_a + 8;
-  const int qstride = a.Hq * D, kstride = a.Hkv * D;
-  const float sl2 = a.scale * LOG2E;
-  load_rows<D>(ks, a.k + (size_t)hk * D, n0, a.keys, kstride, tid);
-  load_rows<D>(vs, a.v + (size_t)hk * D, n0, a.keys, kstride, tid);
-  cp_commit();
-  float dk[DS / 8][4], dv[DS / 8][4];
-#pragma unroll
-  for (int j = 0; j < DS / 8; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) dk[j][e] = dv[j][e] = 0.f;
-  const int nqb = (a.rows + BM - 1) / BM;
-  for (int hh = 0; hh < group; ++hh) {
-    const int h = hk * group + hh;
-    for (int qb = 0; qb < nqb; ++qb) {
-      const int lo = a.qb_min[qb], hi = a.qb_max[qb];
-      if (!(lo < hi && lo < n0 + BN && hi > n0)) continue;  // uniform across the CTA
-      const int r0 = qb * BM;
-      __syncthreads();  // previous tiles consumed
-      load_rows<D>(qs, a.q + (size_t)h * D, r0, a.rows, qstride, tid);
-      load_rows<D>(dos, a.dout + (size_t)h * D, r0, a.rows, qstride, tid);
-      cp_commit();
-      for (int r = tid; r < BM; r += THREADS) {
-        const int row = r0 + r;
-        const bool ok = row < a.rows;
-        s_lse[r] = ok ? a.lse[(size_t)h * a.rows + row] * LOG2E : INFINITY;
-        s_ds[r] = ok ? a.dsum[(size_t)h * a.rows + row] : 0.f;
-        s_ks[r] = ok ? a.kstart[row] : 0;
-        s_ke[r] = ok ? a.kend[row] : 0;
-      }
-      cp_wait_all();
-      __syncthreads();
-      // S^T = K Q^T, dP^T = V dO^T  (16 keys x 64 rows per warp)
-      float s[BM / 8][4], dp[BM / 8][4];
-#pragma unroll
-      for (int j = 0; j < BM / 8; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s[j][e] = dp[j][e] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < D; kk += 16) {
-        uint32_t ak[4], av[4];
-        frag_a(ak, ks, warp * 16, kk, LD, lane);
-        frag_a(av, vs, warp * 16, kk, LD, lane);
-#pragma unroll
-        for (int j = 0; j < BM / 8; j += 2) {
-          uint32_t bq[4], bd[4];
-          frag_bt2(bq, qs, kk, j * 8, LD, lane);
-          frag_bt2(bd, dos, kk, j * 8, LD, lane);
-          mma16816(s[j], ak, bq[0], bq[1]);
-          mma16816(s[j + 1], ak, bq[2], bq[3]);
-          mma16816(dp[j], av, bd[0], bd[1]);
-          mma16816(dp[j + 1], av, bd[2], bd[3]);
-        }
-      }
-      // P^T and dS^T (columns are rows of the q block)
-#pragma unroll
-      for (int j = 0; j < BM / 8; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int r = j * 8 + 2 * t + e;
-          const int rs = s_ks[r], re = s_ke[r];
-          const float lse = s_lse[r], dsr = s_ds[r];
-          const float pa = (key_a >= rs && key_a < re) ? exp2f(s[j][e] * sl2 - lse) : 0.f;
-          const float pb = (key_b >= rs && key_b < re) ? exp2f(s[j][2 + e] * sl2 - lse) : 0.f;
-          s[j][e] = pa;
-          s[j][2 + e] = pb;
-          dp[j][e] = pa * (dp[j][e] - dsr);
-          dp[j][2 + e] = pb * (dp[j][2 + e] - dsr);
-        }
-      }
-      // dV += P^T dO[:, slice];  dK += dS^T Q[:, slice]
-#pragma unroll
-      for (int kk = 0; kk < BM / 16; ++kk) {
-        uint32_t ap[4], ad[4];
-        acc_to_a(ap, s[2 * kk], s[2 * kk + 1]);
-        acc_to_a(ad, dp[2 * kk], dp[2 * kk + 1]);
-#pragma unroll
-        for (int j = 0; j < DS / 8; j += 2) {
-          uint32_t bo[4], bq[4];
-          frag_b2(bo, dos, kk * 16, d0 + j * 8, LD, lane);
-          frag_b2(bq, qs, kk * 16, d0 + j * 8, LD, lane);
-          mma16816(dv[j], ap, bo[0], bo[1]);
-          mma16816(dv[j + 1], ap, bo[2], bo[3]);
-          mma16816(dk[j], ad, bq[0], bq[1]);
-          mma16816(dk[j + 1], ad, bq[2], bq[3]);
-        }
-      }
-    }
-  }
-  cp_wait_all();
-  if (key_a < a.keys) {
-    __nv_bfloat16* dkd = a.out + ((size_t)key_a * a.Hkv + hk) * D + d0;
-    __nv_bfloat16* dvd = a.out2 + ((size_t)key_a * a.Hkv + hk) * D + d0;
-#pragma unroll
-    for (int j = 0; j < DS / 8; ++j) {
-      *reinterpret_cast<__nv_bfloat162*>(dkd + j * 8 + 2 * t) = __floats2bfloat162_rn(dk[j][0] * a.scale, dk[j][1] * a.scale);
-      *reinterpret_cast<__nv_bfloat162*>(dvd + j * 8 + 2 * t) = __floats2bfloat162_rn(dv[j][0], dv[j][1]);
-    }
-  }
-  if (key_b < a.keys) {
-    __nv_bfloat16* dkd = a.out + ((size_t)key_b * a.Hkv + hk) * D + d0;
-    __nv_bfloat16* dvd = a.out2 + ((size_t)key_b * a.Hkv + hk) * D + d0;
-#pragma unroll
-    for (int j = 0; j < DS / 8; ++j) {
-      *reinterpret_cast<__nv_bfloat162*>(dkd + j * 8 + 2 * t) = __floats2bfloat162_rn(dk[j][2] * a.scale, dk[j][3] * a.scale);
-      *reinterpret_cast<__nv_bfloat162*>(dvd + j * 8 + 2 * t) = __floats2bfloat162_rn(dv[j][2], dv[j][3]);
-    }
-  }
-}
-
-template <typename F>
-void set_smem_once(F fn, size_t bytes) {
-  CQB_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-}
-
-AttnArgs base_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& kstart,
-                   const at::Tensor& kend, double scale) {
-  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q: [rows,Hq,D] bf16");
-  TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
-              "k/v: contiguous bf16");
-  TORCH_CHECK(kstart.scalar_type() == at::kInt && kend.scalar_type() == at::kInt && kstart.numel() == q.size(0) &&
-                  kend.numel() == q.size(0),
-              "kstart/kend: int32 [rows]");
-  TORCH_CHECK(q.size(1) % k.size(1) == 0, "GQA ratio must be integral");
-  AttnArgs a{};
-  a.q = (const __nv_bfloat16*)q.data_ptr();
-  a.k = (const __nv_bfloat16*)k.data_ptr();
-  a.v = (const __nv_bfloat16*)v.data_ptr();
-  a.kstart = kstart.data_ptr<int>();
-  a.kend = kend.data_ptr<int>();
-  a.rows = q.size(0);
-  a.keys = k.size(0);
-  a.Hq = q.size(1);
-  a.Hkv = k.size(1);
-  a.scale = (float)scale;
-  return a;
-}
+// dK / dV: one CTA per (128-key block, kv head, value-dim slice of DS). K and V stay in shared
+// memory; for every (q head of the group, 64-row block) whose key ranges meet the block, Q and dO
+// tiles (+ the rows' exponent references, Dsum and ranges) stream in by TMA. S^T = K Q^T and
+// dP^T = V dO^T land in double-buffered TMEM; each softmax thread (one key) forms P^T and
+// dS^T = P^T (dP^T - Dsum) into shared memory (bf16, 128B-swizzled K-major), and dV += P^T dO,
+// dK += dS^T Q accumulate in TMEM over the value-dim slice (dO and Q tiles are the MN-major B
+// operands). At D = 256 the slice is half the head (two CTAs per key block recompute S^T and
+// dP^T) and Q/dO and P^T/dS^T are single-buffered to fit shared memory.
+template <int D>
+struct DkvTc {
+  static constexpr int BN = 128, BQ = 64, KB = D / 64;
+  static constexpr int DS = D > 128 ? 128 : D;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int QT_BYTES = BQ * D * 2;
+  static constexpr int INFO_BYTES = BQ * 16;           // float2 lsd + int2 kse per row
+  static constexpr int STAGE_BYTES = 2 * QT_BYTES + INFO_BYTES;
+  static constexpr int PT_BYTES = BN * BQ * 2;
+  static constexpr int STAGES = D > 128 ? 1 : 2;
+  static constexpr int PBUF = D > 128 ? 1 : 2;
+  static constexpr int SMEM = 2 * KV_BYTES + STAGES * STAGE_BYTES + 2 * PBUF * PT_BYTES + 1024 + 256;
+  static constexpr uint32_t DP_COL = 2 * BQ, DV_COL = 4 * BQ, DK_COL = 4 * BQ + DS;
+};
 
 template <int D>
-size_t fwd_smem() { return (size_t)(BM + 4 * BN) * (D + 8) * 2; }
-template <int D>
-size_t dq_smem() { return (size_t)(2 * BM + 4 * BN) * (D + 8) * 2; }
-template <int D>
-size_t dkv_smem() { return (size_t)(2 * BN + 2 * BM) * (D + 8) * 2; }
+__global__ void __launch_bounds__(192, 1)
+    attn_dkv_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_do,
+                       const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                       BwdTcArgs a, int* status) {
+  using C = DkvTc<D>;
+  constexpr int BN = C::BN, BQ = C::BQ, KB = C::KB, DS = C::DS, ST = C::STAGES, PB = C::PBUF;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sk = smem;
+  uint8_t* sv = sk + C::KV_BYTES;
+  uint8_t* stages = sv + C::KV_BYTES;                 // [ST][Q | dO | info]
+  uint8_t* spt = stages + ST * C::STAGE_BYTES;        // [PB][P^T | dS^T]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(spt + 2 * PB * C::PT_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;    // [2]
+  uint64_t* pv_done = bars + 9;   // [2]
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_count = reinterpret_cast<int*>(tmem_slot + 2);
 
-#define ATTN_D_DISPATCH(D_, ...)                          \
-  [&] {                                                   \
-    if (D_ == 64) { constexpr int D = 64; __VA_ARGS__(); }  \
-    else if (D_ == 128) { constexpr int D = 128; __VA_ARGS__(); } \
-    else if (D_ == 256) { constexpr int D = 256; __VA_ARGS__(); } \
-    else TORCH_CHECK(false, "attention head dim must be 64, 128 or 256"); \
-  }()
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = blockIdx.x, hk = blockIdx.y, z = blockIdx.z;
+  const int n0 = kb * BN, d0 = z * DS;
+  const int group = a.Hq / a.Hkv, nqb = a.rows_pad / BQ;
+  auto meets = [&](int qb) {
+    const int lo = a.qb_min[qb], hi = a.qb_max[qb];
+    return lo < hi && lo < n0 + BN && hi > n0;
+  };
+  if (threadIdx.x == 0) {
+    tc::mbar_init(kv_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&qd_full[b], 1);
+      tc::mbar_init(&qd_empty[b], 1);
+      tc::mbar_init(&s_full[b], 1);
+      tc::mbar_init(&p_full[b], 128);
+      tc::mbar_init(&pv_done[b], 1);
+    }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    *s_count = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  {
+    int c = 0;
+    for (int qb = threadIdx.x; qb < nqb; qb += blockDim.x) c += meets(qb) ? 1 : 0;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0 && c) atomicAdd(s_count, c);
+  }
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int np = *s_count * group;   // (head, row block) pairs, heads outermost
+
+  if (warp == 0) {
+    if (lane == 0 && np > 0) {
+      tc::prefetch_map(&map_q);
+      tc::prefetch_map(&map_do);
+      tc::prefetch_map(&map_k);
+      tc::prefetch_map(&map_v);
+      int armed[2] = {-1, -1};
+      tc::mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
+#pragma unroll
+      for (int i = 0; i < KB; ++i) {
+        tc::tma_load_2d(sk + i * BN * 128, &map_k, kv_full, hk * D + i * 64, n0);
+        tc::tma_load_2d(sv + i * BN * 128, &map_v, kv_full, hk * D + i * 64, n0);
+      }
+      int i = 0;
+      for (int hh = 0; hh < group && i < np; ++hh) {
+        const int h = hk * group + hh;
+        bool ok = true;
+        for (int qb = 0; qb < nqb && ok; ++qb) {
+          if (!meets(qb)) continue;
+          const int s = i % ST;
+          const uint32_t ph = (i / ST) & 1;
+          if (!tc::mbar_wait(&qd_empty[s], ph ^ 1, status, abort_flag, 51)) { ok = false; break; }
+          uint8_t* st = stages + s * C::STAGE_BYTES;
+          tc::mbar_expect_tx(&qd_full[s], C::STAGE_BYTES);
+#pragma unroll
+          for (int c = 0; c < KB; ++c) {
+            tc::tma_load_2d(st + c * BQ * 128, &map_q, &qd_full[s], h * D + c * 64, qb * BQ);
+            tc::tma_load_2d(st + C::QT_BYTES + c * BQ * 128, &map_do, &qd_full[s], h * D + c * 64, qb * BQ);
+          }
+          tc::bulk_load(st + 2 * C::QT_BYTES, a.lsd + (size_t)h * a.rows_pad + qb * BQ, BQ * 8, &qd_full[s]);
+          tc::bulk_load(st + 2 * C::QT_BYTES + BQ * 8, a.kse + qb * BQ, BQ * 8, &qd_full[s]);
+          armed[s] = (int)ph;
+          ++i;
+        }
+        if (!ok) break;
+      }
+      const unsigned long long t0 = tc::globaltimer();
+      while (!tc::mbar_try_wait(kv_full, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+      for (int s = 0; s < 2; ++s)
+        if (armed[s] >= 0)
+          while (!tc::mbar_try_wait(&qd_full[s], (uint32_t)armed[s]) && tc::globaltimer() - t0 < tc::kWaitNs) {
+          }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && np > 0) {
+      constexpr uint32_t idesc_s = tc::idesc_bf16(BN, BQ, false, false);
+      constexpr uint32_t idesc_g = tc::idesc_bf16(BN, DS, false, true);
+      const uint32_t k_addr = tc::smem_u32(sk), v_addr = tc::smem_u32(sv), st_addr = tc::smem_u32(stages),
+                     pt_addr = tc::smem_u32(spt);
+      auto issue_scores = [&](int i) -> bool {
+        const int s = i % ST, b = i & 1;
+        if (!tc::mbar_wait(&qd_full[s], (i / ST) & 1, status, abort_flag, 52)) return false;
+        tc::fence_after();
+        const uint32_t qt = st_addr + s * C::STAGE_BYTES, dt = qt + C::QT_BYTES;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * (BN * 128) + (k & 3) * 32, toff = (k >> 2) * (BQ * 128) + (k & 3) * 32;
+          tc::mma_bf16(tmem + b * BQ, tc::smem_desc(k_addr + off, 16, 1024), tc::smem_desc(qt + toff, 16, 1024),
+                       idesc_s, k > 0 ? 1u : 0u);
+          tc::mma_bf16(tmem + C::DP_COL + b * BQ, tc::smem_desc(v_addr + off, 16, 1024),
+                       tc::smem_desc(dt + toff, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&s_full[b]);
+        return true;
+      };
+      auto issue_grads = [&](int i) -> bool {
+        const int s = i % ST, pb = i % PB;
+        if (!tc::mbar_wait(&p_full[pb], (i / PB) & 1, status, abort_flag, 53)) return false;
+        tc::fence_after();
+        const uint32_t qt = st_addr + s * C::STAGE_BYTES + (d0 / 64) * (BQ * 128), dt = qt + C::QT_BYTES;
+        const uint32_t pt = pt_addr + pb * 2 * C::PT_BYTES, dst = pt + C::PT_BYTES;
+#pragma unroll
+        for (int k = 0; k < BQ / 16; ++k) {
+          tc::mma_bf16(tmem + C::DV_COL, tc::smem_desc(pt + k * 32, 16, 1024),
+                       tc::smem_desc(dt + k * 2048, BQ * 128, 1024), idesc_g, (i > 0 || k > 0) ? 1u : 0u);
+          tc::mma_bf16(tmem + C::DK_COL, tc::smem_desc(dst + k * 32, 16, 1024),
+                       tc::smem_desc(qt + k * 2048, BQ * 128, 1024), idesc_g, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&qd_empty[s]);
+        tc::mma_commit(&pv_done[pb]);
+        return true;
+      };
+      bool ok = tc::mbar_wait(kv_full, 0, status, abort_flag, 54);
+      if (ok) tc::fence_after();
+      for (int i = 0; i < np && ok; ++i) {
+        ok = issue_scores(i);
+        if (ok && ST == 2 && i > 0) ok = issue_grads(i - 1);
+        if (ok && ST == 1) ok = issue_grads(i);
+      }
+      if (ok && ST == 2) issue_grads(np - 1);
+      tc::mma_commit(drain);
+      const unsigned long long t0 = tc::globaltimer();
+      while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    }
+  } else {
+    // one key per thread
+    const int quarter = warp & 3;
+    const int kl = quarter * 32 + lane, key = n0 + kl;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float sl2 = a.scale * LOG2E_TC;
+    auto wwait = [&](uint64_t* bar, uint32_t parity, int code) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, abort_flag, code));
+    };
+    bool ok = true;
+    for (int i = 0; i < np && ok; ++i) {
+      const int b = i & 1, s = i % ST, pb = i % PB;
+      if (!wwait(&s_full[b], (i >> 1) & 1, 55)) { ok = false; break; }
+      tc::fence_after();
+      if (i >= PB && !wwait(&pv_done[pb], ((i - PB) / PB) & 1, 56)) { ok = false; break; }
+      const uint8_t* info = stages + s * C::STAGE_BYTES + 2 * C::QT_BYTES;
+      const float2* lsd = reinterpret_cast<const float2*>(info);
+      const int2* kse = reinterpret_cast<const int2*>(info + BQ * 8);
+      uint8_t* prow = spt + pb * 2 * C::PT_BYTES + kl * 128;
+      uint8_t* drow = prow + C::PT_BYTES;
+#pragma unroll
+      for (int c = 0; c < BQ; c += 32) {
+        float sv[32], dv[32];
+        tc::tmem_ld32(lane_base + b * BQ + c, sv);
+        tc::tmem_ld32(lane_base + C::DP_COL + b * BQ + c, dv);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint32_t wp[4], wd[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float p2[2], d2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int r = c + c8 * 8 + 2 * e + u, i2 = c8 * 8 + 2 * e + u;
+              const float2 ld = lsd[r];
+              const int2 rg = kse[r];
+              const float p = (key >= rg.x && key < rg.y) ? exp2f(sv[i2] * sl2 - ld.x) : 0.f;
+              p2[u] = p;
+              d2[u] = p * (dv[i2] - ld.y);
+            }
+            __nv_bfloat162 a2 = __floats2bfloat162_rn(p2[0], p2[1]);
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(d2[0], d2[1]);
+            wp[e] = *reinterpret_cast<uint32_t*>(&a2);
+            wd[e] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          const int chunk = ((c >> 3) + c8) ^ (kl & 7);
+          *reinterpret_cast<uint4*>(prow + chunk * 16) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
+          *reinterpret_cast<uint4*>(drow + chunk * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::fence_before();
+      tc::mbar_arrive(&p_full[pb]);
+    }
+    if (ok && np > 0 && !wwait(&pv_done[(np - 1) % PB], ((np - 1) / PB) & 1, 57)) ok = false;
+    if (ok) {
+      tc::fence_after();
+      const bool valid = key < a.keys;
+      __nv_bfloat16* dkd = a.dk + ((size_t)key * a.Hkv + hk) * D + d0;
+      __nv_bfloat16* dvd = a.dv + ((size_t)key * a.Hkv + hk) * D + d0;
+#pragma unroll 1
+      for (int c = 0; c < DS; c += 32) {
+        float gk[32], gv[32];
+        if (np > 0) {
+          tc::tmem_ld32(lane_base + C::DK_COL + c, gk);
+          tc::tmem_ld32(lane_base + C::DV_COL + c, gv);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) gk[i] = gv[i] = 0.f;
+        }
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint32_t wk[4], wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 k2 = __floats2bfloat162_rn(gk[i + 2 * e] * a.scale, gk[i + 2 * e + 1] * a.scale);
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(gv[i + 2 * e], gv[i + 2 * e + 1]);
+              wk[e] = *reinterpret_cast<uint32_t*>(&k2);
+              wv[e] = *reinterpret_cast<uint32_t*>(&v2);
+            }
+            *reinterpret_cast<uint4*>(dkd + c + i) = make_uint4(wk[0], wk[1], wk[2], wk[3]);
+            *reinterpret_cast<uint4*>(dvd + c + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
 
 }  // namespace
 
+// q [rows, Hq, D], k/v [keys, Hkv, D] bf16 contiguous, kstart/kend int32 [rows]; D in {64, 128,
+// 256}. Returns {O [rows, Hq, D] bf16, LSE [Hq, rows] fp32}.
 std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor kstart, at::Tensor kend,
-                                 double scale) {
-  AttnArgs a = base_args(q, k, v, kstart, kend, scale);
+                                    double scale) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q: [rows,Hq,D] bf16");
+  TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && k.scalar_type() == at::kBFloat16 &&
+                  v.scalar_type() == at::kBFloat16 && k.dim() == 3 && v.sizes() == k.sizes(),
+              "k/v: contiguous bf16 [keys, Hkv, D]");
+  TORCH_CHECK(kstart.scalar_type() == at::kInt && kend.scalar_type() == at::kInt && kstart.numel() == q.size(0) &&
+                  kend.numel() == q.size(0) && kstart.is_contiguous() && kend.is_contiguous(),
+              "kstart/kend: int32 [rows]");
+  const int rows = q.size(0), Hq = q.size(1), D = q.size(2), keys = k.size(0), Hkv = k.size(1);
+  TORCH_CHECK(k.size(2) == D && Hq % Hkv == 0, "head dims / GQA ratio");
   auto o = at::empty_like(q);
-  auto lse = at::empty({q.size(1), q.size(0)}, q.options().dtype(at::kFloat));
-  a.out = (__nv_bfloat16*)o.data_ptr();
-  a.lse_out = lse.data_ptr<float>();
-  if (a.rows == 0) return {o, lse};
-  const int D_ = q.size(2);
-  ATTN_D_DISPATCH(D_, [&] {
-    static bool once = (set_smem_once(attn_fwd_kernel<D>, fwd_smem<D>()), true);
+  auto lse = at::empty({Hq, rows}, q.options().dtype(at::kFloat));
+  if (rows == 0) return {o, lse};
+  FwdTcArgs a{kstart.data_ptr<int>(), kend.data_ptr<int>(), (__nv_bfloat16*)o.data_ptr(), lse.data_ptr<float>(),
+              rows, keys, Hq, Hkv, (float)scale};
+  auto launch = [&](auto dtag) {
+    constexpr int DD = decltype(dtag)::value;
+    using C = FwdTc<DD>;
+    auto mq = tma_map_bf16(q.view({rows, Hq * DD}), C::BM);
+    auto mk = tma_map_bf16(k.view({keys, Hkv * DD}), C::BN);
+    auto mv = tma_map_bf16(v.view({keys, Hkv * DD}), C::BN);
+    static bool once = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      return true;
+    }();
     (void)once;
-    dim3 grid((a.rows + BM - 1) / BM, a.Hq);
-    attn_fwd_kernel<D><<<grid, THREADS, fwd_smem<D>(), stream()>>>(a);
-  });
+    attn_fwd_tc_kernel<DD><<<dim3((rows + C::BM - 1) / C::BM, Hq), 192, C::SMEM, stream()>>>(mq, mk, mv, a,
+                                                                                           attn_status_word());
+  };
+  if (D == 64) launch(std::integral_constant<int, 64>{});
+  else if (D == 128) launch(std::integral_constant<int, 128>{});
+  else if (D == 256) launch(std::integral_constant<int, 256>{});
+  else TORCH_CHECK(false, "attn_fwd: head dim must be 64, 128 or 256");
   CQB_LAUNCH_CHECK();
   count_launch();
   return {o, lse};
 }
 
+// Gradients of attn_fwd from dO, the inputs and the forward's O and LSE: returns {dq, dk, dv}. Deterministic (no atomics): a dQ kernel over row blocks and a dK/dV kernel over
+// key blocks, both on tcgen05.
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
-                                 at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale) {
-  AttnArgs a = base_args(q, k, v, kstart, kend, scale);
+                                    at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q: [rows,Hq,D] bf16");
+  TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && k.scalar_type() == at::kBFloat16 &&
+                  v.scalar_type() == at::kBFloat16 && k.dim() == 3 && v.sizes() == k.sizes(),
+              "k/v: contiguous bf16 [keys, Hkv, D]");
+  TORCH_CHECK(o.sizes() == q.sizes() && dout.sizes() == q.sizes() && o.is_contiguous() && dout.is_contiguous() &&
+                  o.scalar_type() == at::kBFloat16 && dout.scalar_type() == at::kBFloat16,
+              "o / dout: contiguous bf16 like q");
+  TORCH_CHECK(kstart.scalar_type() == at::kInt && kend.scalar_type() == at::kInt && kstart.numel() == q.size(0) &&
+                  kend.numel() == q.size(0) && kstart.is_contiguous() && kend.is_contiguous(),
+              "kstart/kend: int32 [rows]");
+  const int rows = q.size(0), Hq = q.size(1), D = q.size(2), keys = k.size(0), Hkv = k.size(1);
+  TORCH_CHECK(k.size(2) == D && Hq % Hkv == 0, "head dims / GQA ratio");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == (int64_t)Hq * rows,
+              "lse: fp32 [Hq, rows]");
   auto dq = at::empty_like(q);
   auto dk = at::empty_like(k);
   auto dv = at::empty_like(v);
-  if (a.rows == 0) return {dq.zero_(), dk.zero_(), dv.zero_()};
-  a.o = (const __nv_bfloat16*)o.data_ptr();
-  a.dout = (const __nv_bfloat16*)dout.data_ptr();
-  a.lse = lse.data_ptr<float>();
-  const int nqb = (a.rows + BM - 1) / BM;
-  auto dsum = at::empty({q.size(1), q.size(0)}, q.options().dtype(at::kFloat));
-  auto qb_min = at::empty({nqb}, q.options().dtype(at::kInt));
-  auto qb_max = at::empty({nqb}, q.options().dtype(at::kInt));
-  a.dsum = dsum.data_ptr<float>();
-  a.qb_min = qb_min.data_ptr<int>();
-  a.qb_max = qb_max.data_ptr<int>();
-  const int D_ = q.size(2);
-  ATTN_D_DISPATCH(D_, [&] {
-    const int warps = a.rows * a.Hq;
-    const int blocks = std::max((warps * 32 + 255) / 256, (nqb + 255) / 256);
-    attn_bwd_prep_kernel<D><<<blocks, 256, 0, stream()>>>(a, dsum.data_ptr<float>(), qb_min.data_ptr<int>(),
-                                                          qb_max.data_ptr<int>());
-    static bool once_q = (set_smem_once(attn_bwd_dq_kernel<D>, dq_smem<D>()), true);
-    (void)once_q;
-    a.out = (__nv_bfloat16*)dq.data_ptr();
-    attn_bwd_dq_kernel<D><<<dim3(nqb, a.Hq), THREADS, dq_smem<D>(), stream()>>>(a);
-    constexpr int DS = D > 128 ? 128 : D;
-    static bool once_kv = (set_smem_once(attn_bwd_dkv_kernel<D, DS>, dkv_smem<D>()), true);
-    (void)once_kv;
-    a.out = (__nv_bfloat16*)dk.data_ptr();
-    a.out2 = (__nv_bfloat16*)dv.data_ptr();
-    attn_bwd_dkv_kernel<D, DS><<<dim3((a.keys + BN - 1) / BN, a.Hkv, D / DS), THREADS, dkv_smem<D>(), stream()>>>(a);
-  });
-  CQB_LAUNCH_CHECK();
+  if (rows == 0 || keys == 0) return {dq.zero_(), dk.zero_(), dv.zero_()};
+  const int rows_pad = (rows + 63) / 64 * 64;
+  auto lsd = at::empty({Hq, rows_pad, 2}, q.options().dtype(at::kFloat));
+  auto kse = at::empty({rows_pad, 2}, q.options().dtype(at::kInt));
+  auto qb_min = at::empty({rows_pad / 64}, q.options().dtype(at::kInt));
+  auto qb_max = at::empty({rows_pad / 64}, q.options().dtype(at::kInt));
+  {
+    const long warps = (long)rows_pad * Hq;
+    const int blocks = (int)std::max<long>((warps * 32 + 255) / 256, (rows_pad / 64 + 255) / 256);
+    attn_bwd_prep_tc_kernel<<<blocks, 256, 0, stream()>>>(
+        (const __nv_bfloat16*)o.data_ptr(), (const __nv_bfloat16*)dout.data_ptr(), lse.data_ptr<float>(),
+        kstart.data_ptr<int>(), kend.data_ptr<int>(), reinterpret_cast<float2*>(lsd.data_ptr<float>()),
+        reinterpret_cast<int2*>(kse.data_ptr<int>()), qb_min.data_ptr<int>(), qb_max.data_ptr<int>(), rows, rows_pad,
+        Hq, D);
+    CQB_LAUNCH_CHECK();
+  }
+  BwdTcArgs a{reinterpret_cast<const float2*>(lsd.data_ptr<float>()), reinterpret_cast<const int2*>(kse.data_ptr<int>()),
+              qb_min.data_ptr<int>(), qb_max.data_ptr<int>(), (__nv_bfloat16*)dq.data_ptr(),
+              (__nv_bfloat16*)dk.data_ptr(), (__nv_bfloat16*)dv.data_ptr(), rows, rows_pad, keys, Hq, Hkv,
+              (float)scale};
+  auto launch = [&](auto dtag) {
+    constexpr int DD = decltype(dtag)::value;
+    using Q = DqTc<DD>;
+    using K = DkvTc<DD>;
+    auto q2 = q.view({rows, Hq * DD}), do2 = dout.view({rows, Hq * DD});
+    auto k2 = k.view({keys, Hkv * DD}), v2 = v.view({keys, Hkv * DD});
+    static bool once = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute(attn_dq_tc_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM));
+      CQB_CHECK_CUDA(cudaFuncSetAttribute(attn_dkv_tc_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM));
+      return true;
+    }();
+    (void)once;
+    attn_dq_tc_kernel<DD><<<dim3((rows + Q::BM - 1) / Q::BM, Hq), 192, Q::SMEM, stream()>>>(
+        tma_map_bf16(q2, Q::BM), tma_map_bf16(do2, Q::BM), tma_map_bf16(k2, Q::BN), tma_map_bf16(v2, Q::BN), a,
+        attn_status_word());
+    CQB_LAUNCH_CHECK();
+    attn_dkv_tc_kernel<DD><<<dim3((keys + K::BN - 1) / K::BN, Hkv, DD / K::DS), 192, K::SMEM, stream()>>>(
+        tma_map_bf16(q2, K::BQ), tma_map_bf16(do2, K::BQ), tma_map_bf16(k2, K::BN), tma_map_bf16(v2, K::BN), a,
+        attn_status_word());
+    CQB_LAUNCH_CHECK();
+  };
+  if (D == 64) launch(std::integral_constant<int, 64>{});
+  else if (D == 128) launch(std::integral_constant<int, 128>{});
+  else if (D == 256) launch(std::integral_constant<int, 256>{});
+  else TORCH_CHECK(false, "attn_bwd: head dim must be 64, 128 or 256");
   count_launch(3);
   return {dq, dk, dv};
+}
+
+int attn_status(bool reset) {
+  int v = 0;
+  CQB_CHECK_CUDA(cudaMemcpy(&v, attn_status_word(), sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset && v) CQB_CHECK_CUDA(cudaMemset(attn_status_word(), 0, sizeof(int)));
+  return v;
 }
 
 }  // namespace cqb

@@ -60,9 +60,10 @@ at::Tensor gdn_bwd(at::Tensor dO, at::Tensor W, at::Tensor P, at::Tensor Qd, at:
                    at::Tensor start, at::Tensor count);
 // attention.cu
 std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor kstart, at::Tensor kend,
-                                 double scale);
+                                    double scale);
 std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
-                                 at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale);
+                                    at::Tensor lse, at::Tensor kstart, at::Tensor kend, double scale);
+int attn_status(bool reset);
 // gdn_chunk.cu
 std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor G, at::Tensor B);
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
@@ -124,6 +125,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_bwd", &cqb::gdn_bwd);
   m.def("attn_fwd", &cqb::attn_fwd);
   m.def("attn_bwd", &cqb::attn_bwd);
+  m.def("attn_status", &cqb::attn_status, py::arg("reset") = false);
   m.def("adamw_step", &cqb::adamw_step);
   m.def("sum_squares", &cqb::sum_squares);
   m.def("gdn_prep", &cqb::gdn_prep);

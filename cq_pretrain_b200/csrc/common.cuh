@@ -27,6 +27,10 @@ inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// TMA map over a row-major 2-D bf16 matrix (cols contiguous): 128B-swizzled boxes of
+// 64 cols x box_rows rows, out-of-bounds rows and cols read as zero (gemm.cu).
+CUtensorMap tma_map_bf16(const at::Tensor& t, int box_rows);
+
 inline int sm_count() {
   static int count = [] {
     int dev = 0, n = 0;

@@ -475,6 +475,12 @@ CUtensorMap make_map(const at::Tensor& t, int box_rows) {
   return map;
 }
 
+}  // namespace
+
+CUtensorMap tma_map_bf16(const at::Tensor& t, int box_rows) { return make_map(t, box_rows); }
+
+namespace {
+
 // Output map: dense 32x32 boxes (no swizzle) over a row-major [rows, cols] bf16 or fp32 matrix.
 CUtensorMap make_out_map(const at::Tensor& t) {
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, "output must be row-major 2-D");

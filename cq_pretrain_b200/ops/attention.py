@@ -5,9 +5,11 @@ range ``[kstart[r], kend[r])`` (the planner's exact visibility); GQA; rows with 
 output zero. ``varlen_attention``: non-causal packed attention inside each sample (Wan self
 and cross attention; ``q_ends``/``k_ends`` cumulative).
 
-CUDA runs the flash-attention kernels of ``csrc/attention.cu`` (on-the-fly mask from the two
-range vectors, exact key-tile skipping, fp32 online softmax; backward recomputes P and
-accumulates dK/dV in fp32). CPU runs ``reference`` (SDPA with the mask built per row tile).
+CUDA runs the tcgen05 flash-attention kernels of ``csrc/attention.cu``: TMA-fed tiles, scores
+and accumulators in tensor memory, the mask computed on the fly from the two range vectors with
+exact key-tile skipping, fp32 softmax; the backward recomputes P from the saved LSE in a dQ
+kernel over row blocks and a dK/dV kernel over key blocks (deterministic, no atomics). CPU runs
+``reference`` (SDPA with the mask built per row tile).
 """
 
 from __future__ import annotations
