@@ -41,6 +41,59 @@ int* attn_status_word() {
   return word;
 }
 
+// Longest-first launch order. Job 0 ranks the 128-row blocks by the number of `tile`-key tiles
+// their rows' key-range union spans; job 1 ranks the 128-key blocks by the number of qblk-row
+// blocks (qb_min / qb_max unions) that meet them. order[rank] = block, descending work, ties by
+// index; CTAs take their block from the order, so the hardware's in-order dispatch starts the
+// longest blocks first and the short ones fill the tail. Past kMaxScheduled blocks the order is
+// the identity.
+constexpr int kMaxScheduled = 4096;
+
+__global__ void __launch_bounds__(1024) attn_schedule_kernel(const int* __restrict__ kstart, const int* __restrict__ kend,
+                                                             int rows, int tile, int* __restrict__ order_rows,
+                                                             const int* __restrict__ qb_min,
+                                                             const int* __restrict__ qb_max, int nqb, int keys,
+                                                             int* __restrict__ order_keys) {
+  __shared__ int work[kMaxScheduled];
+  const int job = blockIdx.x;
+  const int n = job == 0 ? (rows + 127) / 128 : (keys + 127) / 128;
+  int* order = job == 0 ? order_rows : order_keys;
+  if (n > kMaxScheduled) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) order[i] = i;
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (job == 0) {
+    for (int b = warp; b < n; b += 32) {
+      int lo = INT_MAX, hi = 0;
+      for (int r = b * 128 + lane; r < min(rows, b * 128 + 128); r += 32) {
+        const int s = kstart[r], e = kend[r];
+        if (e > s) lo = min(lo, s), hi = max(hi, e);
+      }
+      lo = __reduce_min_sync(0xffffffffu, lo);
+      hi = __reduce_max_sync(0xffffffffu, hi);
+      if (lane == 0) work[b] = lo < hi ? (hi - (lo / tile) * tile + tile - 1) / tile : 0;
+    }
+  } else {
+    for (int b = warp; b < n; b += 32) {
+      int c = 0;
+      for (int q = lane; q < nqb; q += 32) {
+        const int lo = qb_min[q], hi = qb_max[q];
+        c += (lo < hi && lo < b * 128 + 128 && hi > b * 128) ? 1 : 0;
+      }
+      c = __reduce_add_sync(0xffffffffu, c);
+      if (lane == 0) work[b] = c;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int w = work[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += (work[j] > w || (work[j] == w && j < i)) ? 1 : 0;
+    order[rank] = i;
+  }
+}
+
 template <int D>
 struct FwdTc {
   static constexpr int BM = 128;
@@ -58,6 +111,7 @@ struct FwdTc {
 struct FwdTcArgs {
   const int* kstart;
   const int* kend;
+  const int* order;    // row blocks, longest first (null: index order, when all CTAs fit one wave)
   __nv_bfloat16* out;  // [rows, Hq, D]
   float* lse;          // [Hq, rows]
   int rows, keys, Hq, Hkv;
@@ -91,7 +145,8 @@ __global__ void __launch_bounds__(192, 1)
   int* s_range = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, h = blockIdx.y, hk = h / (a.Hq / a.Hkv);
+  const int slot = blockIdx.x / a.Hq, qb = a.order ? a.order[slot] : slot;
+  const int h = blockIdx.x % a.Hq, hk = h / (a.Hq / a.Hkv);
   const int r0 = qb * BM;
 
   if (threadIdx.x == 0) {
@@ -374,6 +429,8 @@ __global__ void attn_bwd_prep_tc_kernel(const __nv_bfloat16* __restrict__ o, con
 }
 
 struct BwdTcArgs {
+  const int* order_rows;  // 128-row blocks, longest first (dQ); null: index order
+  const int* order_keys;  // 128-key blocks, longest first (dK/dV); null: index order
   const float2* lsd;   // [Hq, rows_pad]
   const int2* kse;     // [rows_pad]
   const int* qb_min;   // [rows_pad / 64]
@@ -429,7 +486,8 @@ __global__ void __launch_bounds__(192, 1)
   int* s_range = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, h = blockIdx.y, hk = h / (a.Hq / a.Hkv);
+  const int slot = blockIdx.x / a.Hq, qb = a.order_rows ? a.order_rows[slot] : slot;
+  const int h = blockIdx.x % a.Hq, hk = h / (a.Hq / a.Hkv);
   const int r0 = qb * BM;
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
@@ -704,7 +762,9 @@ __global__ void __launch_bounds__(192, 1)
   int* s_count = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kb = blockIdx.x, hk = blockIdx.y, z = blockIdx.z;
+  constexpr int NZ = D / DS;
+  const int slot = blockIdx.x / (a.Hkv * NZ), kb = a.order_keys ? a.order_keys[slot] : slot;
+  const int hk = (blockIdx.x / NZ) % a.Hkv, z = blockIdx.x % NZ;
   const int n0 = kb * BN, d0 = z * DS;
   const int group = a.Hq / a.Hkv, nqb = a.rows_pad / BQ;
   auto meets = [&](int qb) {
@@ -948,8 +1008,11 @@ std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::T
   auto o = at::empty_like(q);
   auto lse = at::empty({Hq, rows}, q.options().dtype(at::kFloat));
   if (rows == 0) return {o, lse};
-  FwdTcArgs a{kstart.data_ptr<int>(), kend.data_ptr<int>(), (__nv_bfloat16*)o.data_ptr(), lse.data_ptr<float>(),
-              rows, keys, Hq, Hkv, (float)scale};
+  const int nqb = (rows + 127) / 128;
+  const bool schedule = (long)nqb * Hq > sm_count();
+  auto order = at::empty({schedule ? nqb : 0}, q.options().dtype(at::kInt));
+  FwdTcArgs a{kstart.data_ptr<int>(), kend.data_ptr<int>(), schedule ? order.data_ptr<int>() : nullptr,
+              (__nv_bfloat16*)o.data_ptr(), lse.data_ptr<float>(), rows, keys, Hq, Hkv, (float)scale};
   auto launch = [&](auto dtag) {
     constexpr int DD = decltype(dtag)::value;
     using C = FwdTc<DD>;
@@ -961,8 +1024,13 @@ std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::T
       return true;
     }();
     (void)once;
-    attn_fwd_tc_kernel<DD><<<dim3((rows + C::BM - 1) / C::BM, Hq), 192, C::SMEM, stream()>>>(mq, mk, mv, a,
-                                                                                           attn_status_word());
+    if (schedule) {
+      attn_schedule_kernel<<<1, 1024, 0, stream()>>>(kstart.data_ptr<int>(), kend.data_ptr<int>(), rows, C::BN,
+                                                     order.data_ptr<int>(), nullptr, nullptr, 0, 0, nullptr);
+      CQB_LAUNCH_CHECK();
+      count_launch();
+    }
+    attn_fwd_tc_kernel<DD><<<nqb * Hq, 192, C::SMEM, stream()>>>(mq, mk, mv, a, attn_status_word());
   };
   if (D == 64) launch(std::integral_constant<int, 64>{});
   else if (D == 128) launch(std::integral_constant<int, 128>{});
@@ -1010,7 +1078,12 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
         Hq, D);
     CQB_LAUNCH_CHECK();
   }
-  BwdTcArgs a{reinterpret_cast<const float2*>(lsd.data_ptr<float>()), reinterpret_cast<const int2*>(kse.data_ptr<int>()),
+  const int nqb128 = (rows + 127) / 128, nkb = (keys + 127) / 128;
+  // longest-first orders pay off once the two kernels' CTAs exceed one wave
+  const bool schedule = (long)nqb128 * Hq + (long)nkb * Hkv * (D > 128 ? 2 : 1) > sm_count();
+  auto orders = at::empty({schedule ? nqb128 + nkb : 0}, q.options().dtype(at::kInt));
+  BwdTcArgs a{schedule ? orders.data_ptr<int>() : nullptr, schedule ? orders.data_ptr<int>() + nqb128 : nullptr,
+              reinterpret_cast<const float2*>(lsd.data_ptr<float>()), reinterpret_cast<const int2*>(kse.data_ptr<int>()),
               qb_min.data_ptr<int>(), qb_max.data_ptr<int>(), (__nv_bfloat16*)dq.data_ptr(),
               (__nv_bfloat16*)dk.data_ptr(), (__nv_bfloat16*)dv.data_ptr(), rows, rows_pad, keys, Hq, Hkv,
               (float)scale};
@@ -1026,14 +1099,35 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
       return true;
     }();
     (void)once;
-    attn_dq_tc_kernel<DD><<<dim3((rows + Q::BM - 1) / Q::BM, Hq), 192, Q::SMEM, stream()>>>(
-        tma_map_bf16(q2, Q::BM), tma_map_bf16(do2, Q::BM), tma_map_bf16(k2, Q::BN), tma_map_bf16(v2, Q::BN), a,
-        attn_status_word());
-    CQB_LAUNCH_CHECK();
-    attn_dkv_tc_kernel<DD><<<dim3((keys + K::BN - 1) / K::BN, Hkv, DD / K::DS), 192, K::SMEM, stream()>>>(
+    if (schedule) {
+      attn_schedule_kernel<<<2, 1024, 0, stream()>>>(kstart.data_ptr<int>(), kend.data_ptr<int>(), rows, Q::BN,
+                                                     orders.data_ptr<int>(), qb_min.data_ptr<int>(),
+                                                     qb_max.data_ptr<int>(), rows_pad / 64, keys,
+                                                     orders.data_ptr<int>() + nqb128);
+      CQB_LAUNCH_CHECK();
+      count_launch();
+    }
+    // dK/dV (fewer, longer CTAs) first on this stream; dQ on a side stream fills the SMs its tail
+    // leaves idle (one CTA per SM each: their shared memory does not fit twice).
+    cudaStream_t main = stream();
+    at::cuda::CUDAStream side = at::cuda::getStreamFromPool(false, q.get_device());
+    cudaEvent_t ready, done;
+    CQB_CHECK_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+    CQB_CHECK_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+    CQB_CHECK_CUDA(cudaEventRecord(ready, main));
+    attn_dkv_tc_kernel<DD><<<nkb * Hkv * (DD / K::DS), 192, K::SMEM, main>>>(
         tma_map_bf16(q2, K::BQ), tma_map_bf16(do2, K::BQ), tma_map_bf16(k2, K::BN), tma_map_bf16(v2, K::BN), a,
         attn_status_word());
     CQB_LAUNCH_CHECK();
+    CQB_CHECK_CUDA(cudaStreamWaitEvent(side.stream(), ready, 0));
+    attn_dq_tc_kernel<DD><<<nqb128 * Hq, 192, Q::SMEM, side.stream()>>>(
+        tma_map_bf16(q2, Q::BM), tma_map_bf16(do2, Q::BM), tma_map_bf16(k2, Q::BN), tma_map_bf16(v2, Q::BN), a,
+        attn_status_word());
+    CQB_LAUNCH_CHECK();
+    CQB_CHECK_CUDA(cudaEventRecord(done, side.stream()));
+    CQB_CHECK_CUDA(cudaStreamWaitEvent(main, done, 0));
+    CQB_CHECK_CUDA(cudaEventDestroy(ready));
+    CQB_CHECK_CUDA(cudaEventDestroy(done));
   };
   if (D == 64) launch(std::integral_constant<int, 64>{});
   else if (D == 128) launch(std::integral_constant<int, 128>{});

@@ -184,18 +184,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return d;
 }
 
-// K-major descriptor for 64-byte swizzled rows (layout type 4): 8-row atoms of 512 bytes, each
-// row's 16-byte chunk c stored at c ^ ((row >> 1) & 3); sbo = stride between 8-row groups.
-__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)4 << 61;
-  return d;
-}
-
 // Instruction descriptor of kind::f16 with bf16 A/B, fp32 D.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |

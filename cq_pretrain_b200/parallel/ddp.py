@@ -12,7 +12,9 @@ Layout (reference ``distributed/megatron.py:210-240`` used Megatron DDP + distri
 * under sequence-parallel TP, parameters replicated across the TP group (norms, biases of
   row-parallel linears, DiT modulation/time layers) receive partial gradients on each TP
   rank; their gradients are summed over TP (one coalesced all-reduce) before DP reduction
-  (reference ``distributed/megatron.py:243-266`` did this for the Q/K norms);
+  (reference ``distributed/megatron.py:243-266`` did this for the Q/K norms); parameters marked
+  ``tp_duplicate`` (the vision tower's norms and biases under vision TP, which runs on replicated
+  activations) already hold the full gradient on every TP rank and skip that sum;
 * bucket reduce-scatters are dispatched in one fixed index order on every rank, so ranks
   whose batches skip a branch (no images, no text) still issue identical collective
   sequences (reference ``distributed/communication.py:12-116``). With ``overlap=True`` a
@@ -96,14 +98,16 @@ class DistributedOptimizer:
         device = named[0][1].device
         groups: dict = {}
         for n, p in reversed(named):
-            replicated = self.tp > 1 and not getattr(p, "tensor_model_parallel", False)
-            key = (p.dtype, replicated)
+            plain = self.tp > 1 and not getattr(p, "tensor_model_parallel", False)
+            duplicate = plain and getattr(p, "tp_duplicate", False)
+            key = (p.dtype, plain and not duplicate, duplicate)
             groups.setdefault(key, []).append(p)
         self.groups = []
-        for (dtype, replicated), params in sorted(groups.items(), key=lambda kv: (kv[0][1], str(kv[0][0]))):
-            name = f"{str(dtype).split('.')[-1]}{'-replicated' if replicated else ''}"
-            g = ParamGroup(name, dtype, params, device, self.dp, bucket_size)
-            g.replicated = replicated
+        for (dtype, replicated, duplicate), params in sorted(groups.items(),
+                                                             key=lambda kv: (kv[0][1], kv[0][2], str(kv[0][0]))):
+            suffix = "-replicated" if replicated else "-duplicate" if duplicate else ""
+            g = ParamGroup(f"{str(dtype).split('.')[-1]}{suffix}", dtype, params, device, self.dp, bucket_size)
+            g.replicated, g.duplicate = replicated, duplicate
             self.groups.append(g)
         self.buckets = []
         for g in self.groups:
@@ -235,7 +239,8 @@ class DistributedOptimizer:
 
     def grad_norm(self):
         counted = [self._grad_shard(s) for s in self.shards
-                   if not (s["bucket"].group.replicated and self.tp_rank != 0) and s["n"]]
+                   if not ((s["bucket"].group.replicated or s["bucket"].group.duplicate) and self.tp_rank != 0)
+                   and s["n"]]
         if counted and self._use_kernels():
             total = _ext.ops().sum_squares(counted)   # one multi-tensor pass, fixed reduction order
         else:

@@ -109,6 +109,25 @@ class ReduceTP(torch.autograd.Function):
         return grad
 
 
+class CopyToTP(torch.autograd.Function):
+    """Identity forward / sum over the TP group backward: a replicated input feeding
+    column-sharded weights (each rank's input gradient is a partial sum)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, grad):
+        grad = grad.clone()
+        dist.all_reduce(grad, group=ps.state().tp_group)
+        return grad
+
+
+def copy_to_tp(x):
+    return CopyToTP.apply(x) if ps.tp_size() > 1 else x
+
+
 class ReplicatedUse(torch.autograd.Function):
     """Identity forward; gradient divided by TP size.
 

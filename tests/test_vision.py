@@ -56,3 +56,45 @@ def test_frozen_tower_has_no_grad_and_blocks_are_independent():
     out = tower(both)
     assert not out.requires_grad
     assert torch.allclose(out[:4], tower(alone), atol=1e-5)
+
+
+def _vision_tp_worker(rank, world, store):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world)
+    from cq_pretrain_b200.parallel import layers as P
+    from cq_pretrain_b200.parallel import state as ps
+    ps.initialize(world, backend="gloo", device="cpu")
+    cfg = dict(depth=2, hidden_size=64, intermediate_size=128, num_heads=4, num_position_embeddings=64,
+               out_hidden_size=32)
+    torch.manual_seed(0)
+    full = VisionTower(cfg, freeze_encoder=False, freeze_merger=False)
+    sharded = VisionTower(dict(cfg, tensor_parallel=True), freeze_encoder=False, freeze_merger=False)
+    pairs = list(zip(sharded.named_parameters(), full.named_parameters()))
+    with torch.no_grad():
+        for (name, p), (name_full, q) in pairs:
+            assert name == name_full
+            p.copy_(P.checkpoint_shard(q, p))
+    assert sharded.blocks[0].qkv.weight.shape == (96, 64)          # column shard (stride 3)
+    assert sharded.blocks[0].proj.weight.shape == (64, 32)         # row shard
+    assert sharded.blocks[0].norm1.weight.tp_duplicate
+    torch.manual_seed(1)
+    layout = VisionLayout.prepare(torch.randn(32, 1536), [(1, 4, 4), (1, 4, 4)], num_positions=64, head_dim=16)
+    out_full, out_tp = full(layout), sharded(layout)
+    torch.testing.assert_close(out_tp, out_full, atol=1e-5, rtol=1e-5)
+    out_full.square().sum().backward()
+    out_tp.square().sum().backward()
+    for (name, p), (_, q) in pairs:
+        torch.testing.assert_close(p.grad, P.checkpoint_shard(q.grad, p), atol=1e-5, rtol=1e-4, msg=name)
+    dist.destroy_process_group()
+
+
+def test_vision_tp_matches_replicated(tmp_path):
+    """Vision TP (column qkv/fc1/merger fc1, row proj/fc2/merger fc2) on 2 gloo ranks: outputs
+    equal the replicated tower, sharded gradients equal slices of the full ones and replicated
+    (tp_duplicate) gradients equal the full ones on every rank."""
+    import torch.multiprocessing as mp
+    mp.spawn(_vision_tp_worker, args=(2, str(tmp_path / "store")), nprocs=2, join=True)
