@@ -116,13 +116,19 @@ class ModelConfig(RuntimeConfig):
         need(self.method in ("CQ_IT", "Bi_I+CQ_T"), "method must be CQ_IT or Bi_I+CQ_T")
         need(self.visual_query_mode in ("fixed", "native"), "visual_query_mode must be fixed or native")
         need(self.gdn_backend in GDN_BACKENDS, f"gdn_backend must be one of {GDN_BACKENDS}")
-        need(self.renderer in ("wan", "legacy"), "renderer must be wan or legacy")
+        need(self.renderer in ("wan", "legacy", "moss"), "renderer must be wan, legacy or moss")
         need(not ((self.renderer == "legacy" or self.vision_encoder == "rgb_patch") and tp > 1),
              "the legacy renderer and RGB patch embedding run replicated (TP = 1)")
         if self.renderer == "wan":
             need(self.flow_draws == 1 and self.latent_channels == 16, "Wan uses one flow draw and 16-channel latents")
+        if self.renderer == "moss":
+            need(self.flow_draws == 1, "the MOSS renderer trains one flow draw per target")
+            need(self.dit_width % self.dit_heads == 0 and (self.dit_width // self.dit_heads) % 8 == 0,
+                 "MOSS head width must be a multiple of 8 (four RoPE axes, rotate-half)")
+            need(self.dit_heads % tp == 0 and self.dit_ffn % tp == 0, "MOSS heads and FFN width must divide TP")
         q = self.image_condition_queries
-        need(q >= 1 and (self.renderer == "wan" or math.isqrt(q) ** 2 == q), "image query count must be a positive square")
+        need(q >= 1 and (self.renderer in ("wan", "moss") or math.isqrt(q) ** 2 == q),
+             "image query count must be a positive square")
         need(self.vision_encoder in ("rgb_patch", "qwen35"), "vision_encoder must be rgb_patch or qwen35")
         need(not ((self.freeze_vision or self.freeze_vision_merger) and self.vision_encoder != "qwen35"),
              "vision freezing is defined for the Qwen vision encoder and merger")

@@ -58,6 +58,9 @@ std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Te
                                 at::Tensor start, at::Tensor count);
 at::Tensor gdn_bwd(at::Tensor dO, at::Tensor W, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                    at::Tensor start, at::Tensor count);
+// moss.cu
+at::Tensor moss_pointwise_fwd(int64_t kind, at::Tensor a, at::Tensor b, at::Tensor c);
+std::vector<at::Tensor> moss_pointwise_bwd(int64_t kind, at::Tensor dy, at::Tensor a, at::Tensor b, at::Tensor c);
 // attention.cu
 std::vector<at::Tensor> attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor kstart, at::Tensor kend,
                                     double scale);
@@ -123,6 +126,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_rms_bwd", &cqb::tp_rms_bwd);
   m.def("gdn_fwd", &cqb::gdn_fwd);
   m.def("gdn_bwd", &cqb::gdn_bwd);
+  m.def("moss_pointwise_fwd", &cqb::moss_pointwise_fwd);
+  m.def("moss_pointwise_bwd", &cqb::moss_pointwise_bwd);
   m.def("attn_fwd", &cqb::attn_fwd);
   m.def("attn_bwd", &cqb::attn_bwd);
   m.def("attn_status", &cqb::attn_status, py::arg("reset") = false);

@@ -121,3 +121,126 @@ class WanGenerationSlice(Movable):
         return SimpleNamespace(generation=layout, latents=batch.latents[self.latent_start:self.latent_stop],
                                noise=batch.noise[self.latent_start:self.latent_stop],
                                times=batch.times[self.start:self.stop])
+
+
+# ---- MOSS-Image-Base renderer (legacy) ----------------------------------------------------------
+def moss_rope(height, width, text_length, head_dim, base=10000.0):
+    """Four-axis RoPE of one packed ``[image tokens, conditions]`` stream (rotate-half layout).
+
+    Axis coordinates per row: image token (y, x) -> (0, text_length, y - (h-1)/2, x - (w-1)/2);
+    condition j -> (0, j, 0, 0). Each axis owns ``head_dim / 8`` frequencies
+    ``base^(-i / (head_dim / 8))``; phases are fp32 (the pretrained MOSS convention) and cos / sin
+    are duplicated over the two halves -> ``[h*w + text_length, head_dim]`` each.
+    """
+    n = head_dim // 8
+    bands = 1.0 / (base ** (torch.arange(n, dtype=torch.float32) / n))
+    ys, xs = torch.meshgrid(torch.arange(height, dtype=torch.float32), torch.arange(width, dtype=torch.float32),
+                            indexing="ij")
+    image = torch.stack((torch.zeros_like(ys), torch.full_like(ys, float(text_length)),
+                         ys - (height - 1) / 2, xs - (width - 1) / 2), -1).reshape(-1, 4)
+    text = torch.zeros(text_length, 4)
+    text[:, 1] = torch.arange(text_length, dtype=torch.float32)
+    phase = (torch.cat((image, text))[:, :, None] * bands).reshape(-1, 4 * n)
+    return torch.cat((phase.cos(), phase.cos()), -1), torch.cat((phase.sin(), phase.sin()), -1)
+
+
+@dataclass
+class MossGenerationInputs(Movable):
+    """Packed MOSS streams: per target ``[h*w noisy latent tokens, q conditions]`` (reference
+    ``data/generation.py:49-136``). ``video_indices`` / ``text_indices`` are the rows of the
+    packed stream that hold latent tokens / conditions; ``sample_indices`` maps every packed row,
+    ``video_sample_indices`` every latent token, to its target."""
+
+    grids: tuple                        # (h, w) latent grid per target (16 pixels per token)
+    lengths: tuple                      # latent tokens per target
+    query_counts: tuple                 # conditions per target
+    ends: tuple                         # cumulative packed rows
+    text_ends: tuple                    # cumulative conditions
+    video_ends: tuple                   # cumulative latent tokens
+    video_indices: torch.Tensor         # [sum L] packed row of each latent token
+    text_indices: torch.Tensor          # [sum q] packed row of each condition
+    sample_indices: torch.Tensor        # [rows] target of each packed row
+    video_sample_indices: torch.Tensor  # [sum L] target of each latent token
+    loss_weights: torch.Tensor          # [sum L] 1 / (targets * tokens of that target)
+    cos: torch.Tensor                   # [rows, head_dim]
+    sin: torch.Tensor
+    time_features: torch.Tensor         # [n, 256]
+    microbatches: tuple = ()
+
+    @property
+    def count(self) -> int:
+        return len(self.lengths)
+
+    @property
+    def video_rows(self):
+        return self.video_indices
+
+    @classmethod
+    def prepare(cls, grids, query_counts, head_dim, token_budget=0, max_images=0):
+        grids = tuple((int(h), int(w)) for h, w in grids)
+        counts = tuple(int(q) for q in query_counts)
+        if not grids or min(counts, default=0) < 1:
+            raise ValueError("MOSS layouts need targets with at least one condition each")
+        lengths = tuple(h * w for h, w in grids)
+        video, text, samples, cos, sin, ends, cursor = [], [], [], [], [], [], 0
+        for i, ((h, w), n, q) in enumerate(zip(grids, lengths, counts)):
+            video.append(torch.arange(cursor, cursor + n))
+            text.append(torch.arange(cursor + n, cursor + n + q))
+            samples.append(torch.full((n + q,), i, dtype=torch.long))
+            c, s = moss_rope(h, w, q, head_dim)
+            cos.append(c)
+            sin.append(s)
+            cursor += n + q
+            ends.append(cursor)
+        out = cls(grids, lengths, counts, tuple(ends), tuple(accumulate(counts)), tuple(accumulate(lengths)),
+                  torch.cat(video), torch.cat(text), torch.cat(samples),
+                  torch.repeat_interleave(torch.arange(len(grids)), torch.tensor(lengths)),
+                  torch.cat([torch.full((n,), 1.0 / (len(grids) * n)) for n in lengths]),
+                  torch.cat(cos), torch.cat(sin), torch.zeros(0))
+        ranges, start, used = [], 0, 0
+        for i, (n, q) in enumerate(zip(lengths, counts)):
+            if token_budget and n + q > token_budget:
+                raise ValueError(f"target/condition stream needs {n + q} tokens, above the DiT budget {token_budget}")
+            if i > start and ((token_budget and used + n + q > token_budget) or (max_images and i - start >= max_images)):
+                ranges.append((start, i))
+                start, used = i, 0
+            used += n + q
+        ranges.append((start, len(lengths)))
+        if len(ranges) > 1:
+            out.microbatches = tuple(MossGenerationSlice.prepare(out, a, b) for a, b in ranges)
+        return out
+
+
+@dataclass
+class MossGenerationSlice(Movable):
+    """Targets ``[start, stop)`` of a MOSS layout with local indices; ``bind`` returns views."""
+
+    start: int
+    stop: int
+    latent_start: int
+    latent_stop: int
+    row_start: int
+    row_stop: int
+    layout: MossGenerationInputs
+
+    @classmethod
+    def prepare(cls, parent: MossGenerationInputs, a: int, b: int):
+        r0 = parent.ends[a - 1] if a else 0
+        r1 = parent.ends[b - 1]
+        l0, l1 = sum(parent.lengths[:a]), sum(parent.lengths[:b])
+        t0 = parent.text_ends[a - 1] if a else 0
+        t1 = parent.text_ends[b - 1]
+        layout = MossGenerationInputs(
+            parent.grids[a:b], parent.lengths[a:b], parent.query_counts[a:b],
+            tuple(e - r0 for e in parent.ends[a:b]), tuple(e - t0 for e in parent.text_ends[a:b]),
+            tuple(accumulate(parent.lengths[a:b])), parent.video_indices[l0:l1] - r0,
+            parent.text_indices[t0:t1] - r0, parent.sample_indices[r0:r1] - a,
+            parent.video_sample_indices[l0:l1] - a, parent.loss_weights[l0:l1],
+            parent.cos[r0:r1], parent.sin[r0:r1], torch.zeros(0))
+        return cls(a, b, l0, l1, r0, r1, layout)
+
+    def bind(self, batch):
+        layout = replace(self.layout, time_features=batch.generation.time_features[self.start:self.stop])
+        return SimpleNamespace(generation=layout, latents=batch.latents[self.latent_start:self.latent_stop],
+                               noise=batch.noise[self.latent_start:self.latent_stop],
+                               times=batch.times[self.start:self.stop])

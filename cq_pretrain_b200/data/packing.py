@@ -28,7 +28,7 @@ import numpy as np
 import torch
 
 from .batch import Batch, VisionInputs
-from .generation import WanGenerationInputs
+from .generation import MossGenerationInputs, WanGenerationInputs
 from .plan import build_plan, visual_query_count
 from .sequence import image_sequence, video_sequence
 
@@ -185,7 +185,8 @@ class Packer:
                                                      seed, epoch, "visual-uncond-v1")
                 if generate:
                     gen_indices.append(len(spans))
-                    latent_grids.append(latent_dit_grid(e))
+                    # MOSS latents are already 2x2-packed (16 pixels per token): grid = latent (h, w)
+                    latent_grids.append(tuple(e["latent_shape"][-2:]) if cfg.renderer == "moss" else latent_dit_grid(e))
                     latents.append(e.get("latent"))
                 gen_uncond.append(bool(generate and unconditional))
                 spans.append(visual)
@@ -237,6 +238,14 @@ class Packer:
             # legacy flow renderer: one [tokens, C] latent grid per target (no 2x2 patching)
             if all(z is not None for z in latents):
                 batch.latents = torch.stack([torch.as_tensor(z).float().reshape(z.shape[0], -1).T for z in latents])
+        elif gen_indices and cfg.renderer == "moss":
+            # MOSS: packed [latent tokens, conditions] streams; latents [C, (1,) h, w], 16 px per token
+            counts = [visual_query_count(grids[i], cfg) for i in gen_indices]
+            batch.generation = MossGenerationInputs.prepare(latent_grids, counts, cfg.dit_width // cfg.dit_heads,
+                                                            cfg.generation_token_budget,
+                                                            cfg.generation_microbatch_images)
+            if all(z is not None for z in latents):
+                batch.latents = torch.cat([torch.as_tensor(z).float().reshape(z.shape[0], -1).T for z in latents])
         elif gen_indices:
             counts = [visual_query_count(grids[i], cfg) for i in gen_indices]
             batch.generation = WanGenerationInputs.prepare(latent_grids, counts, cfg.dit_head_dim,

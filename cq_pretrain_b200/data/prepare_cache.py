@@ -74,7 +74,10 @@ def prepare(cfg, corpus, cache_root, rank=0, world=1, device="cpu", vision=None,
                 h = max(16, (x.shape[2] // 16) * 16)
                 w = max(16, (x.shape[3] // 16) * 16)
                 x = torch.nn.functional.interpolate(x, size=(h, w), mode="bilinear", align_corners=False)
-                latent = encoder.encode(x.to(device))[:, :, None]   # [1, C, T=1, h/8, w/8]
+                latent = encoder.encode(x.to(device))
+                if isinstance(latent, tuple):    # posterior (mean, std) encoders cache the mean
+                    latent = latent[0]
+                latent = latent[:, :, None]      # [1, C, T=1, h/stride, w/stride]
                 latent_cache.save(lkey, latent=latent[0].float().cpu())
                 counts["latents"] += 1
     stream.close()
@@ -89,11 +92,20 @@ def main(argv=None):
     parser.add_argument("--rank", type=int, default=0)
     parser.add_argument("--world", type=int, default=1)
     parser.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    parser.add_argument("--latent-encoder", choices=("fake", "kl16"), default="fake",
+                        help="kl16: the legacy renderer's KL16 VAE (needs --kl16-checkpoint)")
+    parser.add_argument("--kl16-checkpoint", default=None)
     args = parser.parse_args(argv)
     from ..config import load_sections, qwen35_2b_wan
     cfg = load_sections(args.config)[0] if args.config else qwen35_2b_wan()
     dtype = torch.bfloat16 if args.device.startswith("cuda") else torch.float32
-    counts = prepare(cfg, args.corpus, args.cache, args.rank, args.world, args.device, dtype=dtype)
+    encoder = None
+    if args.latent_encoder == "kl16":
+        if not args.kl16_checkpoint:
+            raise SystemExit("--latent-encoder kl16 needs --kl16-checkpoint")
+        from ..models.kl16 import FrozenKL16
+        encoder = FrozenKL16(args.kl16_checkpoint, dtype=torch.float32, device=args.device)
+    counts = prepare(cfg, args.corpus, args.cache, args.rank, args.world, args.device, encoder=encoder, dtype=dtype)
     print(json.dumps(dict(status="complete", **counts)), flush=True)
 
 

@@ -52,9 +52,11 @@ class DevicePreparer:
             noise = torch.randn(draws * n, tokens, channels, generator=gen)
             times = torch.randn(draws * n, generator=gen).sigmoid().clamp(1e-5, 1 - 1e-5)
             return noise, times, None
-        noise = torch.randn(sum(layout.lengths), self.cfg.latent_channels * 4, generator=gen)
+        channels = self.cfg.latent_channels if self.cfg.renderer == "moss" else self.cfg.latent_channels * 4
+        noise = torch.randn(sum(layout.lengths), channels, generator=gen)
         times = torch.randn(len(layout.lengths), generator=gen).sigmoid().clamp(1e-5, 1 - 1e-5)
-        return noise, times, time_features(times, self.cfg.wan_freq_dim)
+        freq_dim = 256 if self.cfg.renderer == "moss" else self.cfg.wan_freq_dim   # MOSS: fixed 256-wide sinusoid
+        return noise, times, time_features(times, freq_dim)
 
     def __call__(self, batch, receipt, non_blocking=False):
         extra = self.randomness(batch, receipt)

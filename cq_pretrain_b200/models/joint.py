@@ -43,6 +43,9 @@ class JointModel(nn.Module):
         if cfg.renderer == "legacy":
             from .legacy import FlowRenderer
             self.renderer = FlowRenderer(cfg)
+        elif cfg.renderer == "moss":
+            from .moss import MOSSRenderer
+            self.renderer = MOSSRenderer(cfg)
         else:
             self.renderer = Wan21Generator(cfg)
         self.lm_head = None if cfg.tie_word_embeddings else OutputHead(cfg)

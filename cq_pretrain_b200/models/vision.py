@@ -22,7 +22,6 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import attention as ATT
-from ..ops import linear as L
 from ..ops import reference as R
 from ..parallel import layers as P
 from ..parallel import state as ps
@@ -46,30 +45,14 @@ def _tp(cfg):
 
 
 def column(cfg, in_features, out_features, stride=1):
-    if _tp(cfg):
-        return P.ColumnLinear(in_features, out_features, bias=True, stride=stride)
-    return nn.Linear(in_features, out_features)
+    return P.column_linear(in_features, out_features, stride=stride, parallel=_tp(cfg))
 
 
 def row(cfg, in_features, out_features):
-    if _tp(cfg):
-        return P.RowLinear(in_features, out_features, bias=True)
-    return nn.Linear(in_features, out_features)
+    return P.row_linear(in_features, out_features, parallel=_tp(cfg))
 
 
-def apply_column(layer, x):
-    """Column shard on a replicated input: ``x W_shard^T + b_shard`` (input grad summed over TP)."""
-    if isinstance(layer, P.ColumnLinear):
-        return L.linear(P.copy_to_tp(x), layer.weight, layer.bias)
-    return layer(x)
-
-
-def apply_row(layer, x):
-    """Row shard: ``sum_TP(x_shard W_shard^T) + b`` (replicated output)."""
-    if isinstance(layer, P.RowLinear):
-        y = P.reduce_tp(L.linear(x, layer.weight))
-        return y + layer.bias.to(y.dtype)
-    return layer(x)
+apply_column, apply_row = P.apply_column, P.apply_row
 
 
 class VisionBlock(nn.Module):
@@ -117,10 +100,7 @@ class VisionTower(nn.Module):
         out_width = out_width or cfg["out_hidden_size"]
         self.bridge = nn.Identity() if out_width == cfg["out_hidden_size"] else nn.Linear(cfg["out_hidden_size"], out_width, bias=False)
         if _tp(cfg):
-            # replicated activations: every TP rank computes the full gradient of these
-            for p in self.parameters():
-                if not getattr(p, "tensor_model_parallel", False):
-                    p.tp_duplicate = True
+            P.mark_duplicates(self)   # replicated activations: full gradients on every TP rank
         self.freeze_encoder, self.freeze_merger = freeze_encoder, freeze_merger
         if freeze_encoder:
             for mod in (self.patch_embed, self.pos_embed, self.blocks):

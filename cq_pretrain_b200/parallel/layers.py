@@ -218,6 +218,45 @@ class RowLinear(nn.Module):
         return L.linear(x, self.weight, self.bias)
 
 
+# ---- Megatron-style TP on replicated activations (vision tower, MOSS renderer) --------------
+def column_linear(in_features, out_features, bias=True, stride=1, parallel=True):
+    """Output-sharded weights under TP (``parallel`` and TP > 1), else a plain ``nn.Linear``."""
+    if parallel and ps.tp_size() > 1:
+        return ColumnLinear(in_features, out_features, bias=bias, stride=stride)
+    return nn.Linear(in_features, out_features, bias=bias)
+
+
+def row_linear(in_features, out_features, bias=True, parallel=True):
+    if parallel and ps.tp_size() > 1:
+        return RowLinear(in_features, out_features, bias=bias)
+    return nn.Linear(in_features, out_features, bias=bias)
+
+
+def apply_column(layer, x):
+    """Column shard on a replicated input: ``x W_shard^T + b_shard`` (input grad summed over TP)."""
+    if isinstance(layer, ColumnLinear):
+        return L.linear(copy_to_tp(x), layer.weight, layer.bias)
+    return layer(x)
+
+
+def apply_row(layer, x):
+    """Row shard: ``sum_TP(x_shard W_shard^T) + b`` (replicated output)."""
+    if isinstance(layer, RowLinear):
+        y = reduce_tp(L.linear(x, layer.weight))
+        return y if layer.bias is None else y + layer.bias.to(y.dtype)
+    return layer(x)
+
+
+def mark_duplicates(module):
+    """Replicated-activation TP: every rank computes the full gradient of the module's
+    unsharded parameters, so the optimizer must not sum them over TP."""
+    if ps.tp_size() > 1:
+        for p in module.parameters():
+            if not getattr(p, "tensor_model_parallel", False):
+                p.tp_duplicate = True
+    return module
+
+
 class VocabEmbedding(nn.Module):
     """Vocabulary-parallel embedding; output is row-sharded (partial lookups reduce-scattered)."""
 

@@ -51,3 +51,26 @@ def test_legacy_renderer_training_step():
     assert renderer.output.weight.abs().sum() > 0          # zero-initialised output layer was trained
     second = trainer.train_step([(batch, receipt)])
     assert np.isfinite(second["loss"])
+
+
+def test_kl16_encoder_geometry_and_names():
+    """KL16 encoder: 16x downsampling to 2 x 16 moments, attention only at the 16x16 level,
+    checkpoint parameter names, clamped scaled posterior."""
+    from cq_pretrain_b200.models.kl16 import FrozenKL16
+    torch.manual_seed(0)
+    codec = FrozenKL16(chunk=1)
+    names = dict(codec.named_parameters())
+    for key in ("encoder.conv_in.weight", "encoder.down.0.block.0.norm1.weight", "encoder.down.2.block.0.nin_shortcut.weight",
+                "encoder.down.4.attn.1.proj_out.weight", "encoder.down.3.downsample.conv.weight",
+                "encoder.mid.attn_1.q.weight", "encoder.norm_out.weight", "quant_conv.weight"):
+        assert key in names, key
+    assert not any(k.startswith("encoder.down.3.attn") for k in names)
+    assert not any(k.startswith("encoder.down.4.downsample") for k in names)
+    pixels = torch.rand(2, 3, 64, 96) * 2 - 1
+    mean, std = codec.encode(pixels)
+    assert mean.shape == std.shape == (2, 16, 4, 6)
+    assert (std > 0).all() and torch.isfinite(mean).all()
+    # chunking does not change the result
+    one = FrozenKL16(chunk=2)
+    one.load_state_dict(codec.state_dict())
+    torch.testing.assert_close(one.encode(pixels)[0], mean, atol=1e-5, rtol=1e-5)
