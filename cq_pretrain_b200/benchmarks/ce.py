@@ -3,7 +3,7 @@
 ``[torchrun --nproc-per-node N] python -m cq_pretrain_b200.benchmarks.ce [--rows 8192] [--chunk 1024]``
 times forward+backward of ``ops.cross_entropy.linear_cross_entropy`` (GEMM epilogues that fold
 the logits into online softmax statistics and write softmax gradients, vocabulary split over TP
-ranks) against the same loss through materialised fp32 logits and ``F.cross_entropy``
+ranks; under TP the statistics cross NVLink inside one kernel unless ``--no-fused``) against the same loss through materialised fp32 logits and ``F.cross_entropy``
 (single GPU only). CUDA events, median of ``--iters`` after 3 warm-ups, max over ranks.
 """
 
@@ -23,6 +23,7 @@ def main():
     parser.add_argument("--chunk", type=int, default=1024)
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--no-reference", action="store_true")
+    parser.add_argument("--no-fused", action="store_true", help="TP: NCCL all-reduces instead of the in-kernel exchange")
     args = parser.parse_args()
     import torch
     import torch.distributed as dist
@@ -32,6 +33,9 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     st = ps.initialize(world, timeout_s=300.0)
+    if world > 1 and not args.no_fused:
+        from ..parallel import symmetric
+        symmetric.enable()
     torch.manual_seed(0)
     dev = st.device
     h = (torch.randn(args.rows, args.hidden, device=dev) * 0.5).to(torch.bfloat16).requires_grad_()
@@ -66,7 +70,8 @@ def main():
             dist.all_reduce(v, op=dist.ReduceOp.MAX)
         return v.item()
 
-    row = dict(rows=args.rows, hidden=args.hidden, vocab=args.vocab, tp=st.tp, fused_ms=round(timed(fused), 3))
+    row = dict(rows=args.rows, hidden=args.hidden, vocab=args.vocab, tp=st.tp, fused_ms=round(timed(fused), 3),
+               stats_exchange="nccl" if world == 1 or args.no_fused else "in-kernel")
     flops = 6.0 * args.rows * args.hidden * args.vocab / st.tp   # logits fwd + dh + dW
     row["fused_tflops"] = round(flops / row["fused_ms"] / 1e9, 1)
     if world == 1 and not args.no_reference:
@@ -75,6 +80,11 @@ def main():
         print(json.dumps(row), flush=True)
     if world > 1:
         dist.barrier()
+        if not args.no_fused:
+            from ..parallel import symmetric
+            row_status = symmetric.status()
+            assert row_status == dict(gemm=0, comm=0), row_status
+            symmetric.disable()
         ps.destroy()
 
 

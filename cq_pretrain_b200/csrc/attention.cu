@@ -435,6 +435,7 @@ struct BwdTcArgs {
   const int2* kse;     // [rows_pad]
   const int* qb_min;   // [rows_pad / 64]
   const int* qb_max;
+  const __nv_bfloat16* vsrc;  // V [keys, Hkv, D] (dK/dV at D = 256 stores it into TMEM)
   __nv_bfloat16* dq;   // [rows, Hq, D]
   __nv_bfloat16* dk;   // [keys, Hkv, D]
   __nv_bfloat16* dv;
@@ -720,9 +721,14 @@ __global__ void __launch_bounds__(192, 1)
 // dS^T = P^T (dP^T - Dsum) into shared memory (bf16, 128B-swizzled K-major), and dV += P^T dO,
 // dK += dS^T Q accumulate in TMEM over the value-dim slice (dO and Q tiles are the MN-major B
 // operands). At D = 256 the slice is half the head (two CTAs per key block recompute S^T and
-// dP^T) and Q/dO and P^T/dS^T are single-buffered to fit shared memory.
+// dP^T), and V lives in TMEM as the A operand of dP^T = V dO^T (lane = key, two bf16 per column)
+// while P^T and dS^T are written back over the S^T / dP^T columns with tcgen05.st and read by the
+// dV / dK MMAs as TMEM A operands: shared memory then holds K and two Q / dO stages, so the next
+// pair's tiles stream in while the current pair computes. The score columns are single-buffered
+// there, so the MMA thread waits for the previous pair's dV / dK MMAs before overwriting them.
 template <int D>
 struct DkvTc {
+  static constexpr bool VT = D > 128;                  // V, P^T, dS^T in TMEM (D = 256)
   static constexpr int BN = 128, BQ = 64, KB = D / 64;
   static constexpr int DS = D > 128 ? 128 : D;
   static constexpr int KV_BYTES = BN * D * 2;
@@ -730,10 +736,13 @@ struct DkvTc {
   static constexpr int INFO_BYTES = BQ * 16;           // float2 lsd + int2 kse per row
   static constexpr int STAGE_BYTES = 2 * QT_BYTES + INFO_BYTES;
   static constexpr int PT_BYTES = BN * BQ * 2;
-  static constexpr int STAGES = D > 128 ? 1 : 2;
-  static constexpr int PBUF = D > 128 ? 1 : 2;
-  static constexpr int SMEM = 2 * KV_BYTES + STAGES * STAGE_BYTES + 2 * PBUF * PT_BYTES + 1024 + 256;
-  static constexpr uint32_t DP_COL = 2 * BQ, DV_COL = 4 * BQ, DK_COL = 4 * BQ + DS;
+  static constexpr int STAGES = 2;
+  static constexpr int PBUF = VT ? 0 : 2;              // shared-memory P^T / dS^T buffers
+  static constexpr int NSB = VT ? 1 : 2;               // TMEM score buffers
+  static constexpr int SMEM = (VT ? 1 : 2) * KV_BYTES + STAGES * STAGE_BYTES + 2 * PBUF * PT_BYTES + 1024 + 256;
+  static constexpr uint32_t DP_COL = NSB * BQ, DV_COL = 2 * NSB * BQ, DK_COL = 2 * NSB * BQ + DS;
+  static constexpr uint32_t VT_COL = DK_COL + DS;      // V (VT only): D / 2 columns
+  static_assert(!VT || VT_COL + D / 2 <= 512, "TMEM columns");
 };
 
 template <int D>
@@ -742,14 +751,15 @@ __global__ void __launch_bounds__(192, 1)
                        const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                        BwdTcArgs a, int* status) {
   using C = DkvTc<D>;
-  constexpr int BN = C::BN, BQ = C::BQ, KB = C::KB, DS = C::DS, ST = C::STAGES, PB = C::PBUF;
+  constexpr int BN = C::BN, BQ = C::BQ, KB = C::KB, DS = C::DS, ST = C::STAGES;
+  constexpr int PB = C::PBUF ? C::PBUF : 1;   // shared-memory P^T buffers (unused when VT)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sk = smem;
-  uint8_t* sv = sk + C::KV_BYTES;
-  uint8_t* stages = sv + C::KV_BYTES;                 // [ST][Q | dO | info]
-  uint8_t* spt = stages + ST * C::STAGE_BYTES;        // [PB][P^T | dS^T]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(spt + 2 * PB * C::PT_BYTES);
+  uint8_t* sv = sk + C::KV_BYTES;                     // (not VT)
+  uint8_t* stages = sv + (C::VT ? 0 : C::KV_BYTES);   // [ST][Q | dO | info]
+  uint8_t* spt = stages + ST * C::STAGE_BYTES;        // [PB][P^T | dS^T] (not VT)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(spt + 2 * C::PBUF * C::PT_BYTES);
   uint64_t* kv_full = bars;
   uint64_t* qd_full = bars + 1;   // [2]
   uint64_t* qd_empty = bars + 3;  // [2]
@@ -757,7 +767,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* p_full = bars + 7;    // [2]
   uint64_t* pv_done = bars + 9;   // [2]
   uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* v_ready = bars + 12;  // VT: V stored into TMEM by the 128 softmax threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_count = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -781,6 +792,7 @@ __global__ void __launch_bounds__(192, 1)
       tc::mbar_init(&pv_done[b], 1);
     }
     tc::mbar_init(drain, 1);
+    tc::mbar_init(v_ready, 128);
     *abort_flag = 0;
     *s_count = 0;
     tc::fence_mbar_init();
@@ -805,11 +817,11 @@ __global__ void __launch_bounds__(192, 1)
       tc::prefetch_map(&map_k);
       tc::prefetch_map(&map_v);
       int armed[2] = {-1, -1};
-      tc::mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
+      tc::mbar_expect_tx(kv_full, (C::VT ? 1 : 2) * C::KV_BYTES);
 #pragma unroll
       for (int i = 0; i < KB; ++i) {
         tc::tma_load_2d(sk + i * BN * 128, &map_k, kv_full, hk * D + i * 64, n0);
-        tc::tma_load_2d(sv + i * BN * 128, &map_v, kv_full, hk * D + i * 64, n0);
+        if (!C::VT) tc::tma_load_2d(sv + i * BN * 128, &map_v, kv_full, hk * D + i * 64, n0);
       }
       int i = 0;
       for (int hh = 0; hh < group && i < np; ++hh) {
@@ -849,7 +861,11 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t k_addr = tc::smem_u32(sk), v_addr = tc::smem_u32(sv), st_addr = tc::smem_u32(stages),
                      pt_addr = tc::smem_u32(spt);
       auto issue_scores = [&](int i) -> bool {
-        const int s = i % ST, b = i & 1;
+        const int s = i % ST, b = C::VT ? 0 : (i & 1);
+        if (C::VT && i > 0) {
+          // single score buffer: the previous pair's dV / dK MMAs read P^T / dS^T from it
+          if (!tc::mbar_wait(&pv_done[0], (i - 1) & 1, status, abort_flag, 58)) return false;
+        }
         if (!tc::mbar_wait(&qd_full[s], (i / ST) & 1, status, abort_flag, 52)) return false;
         tc::fence_after();
         const uint32_t qt = st_addr + s * C::STAGE_BYTES, dt = qt + C::QT_BYTES;
@@ -858,37 +874,47 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t off = (k >> 2) * (BN * 128) + (k & 3) * 32, toff = (k >> 2) * (BQ * 128) + (k & 3) * 32;
           tc::mma_bf16(tmem + b * BQ, tc::smem_desc(k_addr + off, 16, 1024), tc::smem_desc(qt + toff, 16, 1024),
                        idesc_s, k > 0 ? 1u : 0u);
-          tc::mma_bf16(tmem + C::DP_COL + b * BQ, tc::smem_desc(v_addr + off, 16, 1024),
-                       tc::smem_desc(dt + toff, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+          if (C::VT)
+            tc::mma_bf16_ts(tmem + C::DP_COL, tmem + C::VT_COL + k * 8, tc::smem_desc(dt + toff, 16, 1024), idesc_s,
+                            k > 0 ? 1u : 0u);
+          else
+            tc::mma_bf16(tmem + C::DP_COL + b * BQ, tc::smem_desc(v_addr + off, 16, 1024),
+                         tc::smem_desc(dt + toff, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
         }
         tc::mma_commit(&s_full[b]);
         return true;
       };
       auto issue_grads = [&](int i) -> bool {
-        const int s = i % ST, pb = i % PB;
-        if (!tc::mbar_wait(&p_full[pb], (i / PB) & 1, status, abort_flag, 53)) return false;
+        const int s = i % ST, pb = C::VT ? 0 : i % PB;
+        if (!tc::mbar_wait(&p_full[pb], (C::VT ? i : i / PB) & 1, status, abort_flag, 53)) return false;
         tc::fence_after();
         const uint32_t qt = st_addr + s * C::STAGE_BYTES + (d0 / 64) * (BQ * 128), dt = qt + C::QT_BYTES;
         const uint32_t pt = pt_addr + pb * 2 * C::PT_BYTES, dst = pt + C::PT_BYTES;
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {
-          tc::mma_bf16(tmem + C::DV_COL, tc::smem_desc(pt + k * 32, 16, 1024),
-                       tc::smem_desc(dt + k * 2048, BQ * 128, 1024), idesc_g, (i > 0 || k > 0) ? 1u : 0u);
-          tc::mma_bf16(tmem + C::DK_COL, tc::smem_desc(dst + k * 32, 16, 1024),
-                       tc::smem_desc(qt + k * 2048, BQ * 128, 1024), idesc_g, (i > 0 || k > 0) ? 1u : 0u);
+          const uint64_t bo = tc::smem_desc(dt + k * 2048, BQ * 128, 1024), bq = tc::smem_desc(qt + k * 2048, BQ * 128, 1024);
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          if (C::VT) {   // P^T / dS^T over the score columns, two bf16 per column
+            tc::mma_bf16_ts(tmem + C::DV_COL, tmem + k * 8, bo, idesc_g, acc);
+            tc::mma_bf16_ts(tmem + C::DK_COL, tmem + C::DP_COL + k * 8, bq, idesc_g, acc);
+          } else {
+            tc::mma_bf16(tmem + C::DV_COL, tc::smem_desc(pt + k * 32, 16, 1024), bo, idesc_g, acc);
+            tc::mma_bf16(tmem + C::DK_COL, tc::smem_desc(dst + k * 32, 16, 1024), bq, idesc_g, acc);
+          }
         }
         tc::mma_commit(&qd_empty[s]);
         tc::mma_commit(&pv_done[pb]);
         return true;
       };
       bool ok = tc::mbar_wait(kv_full, 0, status, abort_flag, 54);
+      if (ok && C::VT) ok = tc::mbar_wait(v_ready, 0, status, abort_flag, 59);
       if (ok) tc::fence_after();
       for (int i = 0; i < np && ok; ++i) {
         ok = issue_scores(i);
-        if (ok && ST == 2 && i > 0) ok = issue_grads(i - 1);
-        if (ok && ST == 1) ok = issue_grads(i);
+        if (ok && C::VT) ok = issue_grads(i);            // the next scores need these columns back
+        else if (ok && i > 0) ok = issue_grads(i - 1);   // S^T_i / dP^T_i overlap softmax_{i-1}
       }
-      if (ok && ST == 2) issue_grads(np - 1);
+      if (ok && !C::VT) issue_grads(np - 1);
       tc::mma_commit(drain);
       const unsigned long long t0 = tc::globaltimer();
       while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
@@ -904,14 +930,67 @@ __global__ void __launch_bounds__(192, 1)
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, abort_flag, code));
     };
     bool ok = true;
+    if (C::VT && np > 0) {
+      // V row of this thread's key -> TMEM columns VT_COL.. (two bf16 per column)
+      const bool kv = key < a.keys;
+      const __nv_bfloat16* vrow = a.vsrc + ((size_t)(kv ? key : 0) * a.Hkv + hk) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 2; c += 32) {
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const uint4 u = kv ? *reinterpret_cast<const uint4*>(vrow + 2 * (c + j)) : make_uint4(0, 0, 0, 0);
+          w[j] = __uint_as_float(u.x);
+          w[j + 1] = __uint_as_float(u.y);
+          w[j + 2] = __uint_as_float(u.z);
+          w[j + 3] = __uint_as_float(u.w);
+        }
+        tc::tmem_st32(lane_base + C::VT_COL + c, w);
+      }
+      tc::fence_before();
+      tc::mbar_arrive(v_ready);
+    }
     for (int i = 0; i < np && ok; ++i) {
-      const int b = i & 1, s = i % ST, pb = i % PB;
-      if (!wwait(&s_full[b], (i >> 1) & 1, 55)) { ok = false; break; }
+      const int b = C::VT ? 0 : (i & 1), s = i % ST, pb = C::VT ? 0 : i % PB;
+      if (!wwait(&s_full[b], (C::VT ? i : i >> 1) & 1, 55)) { ok = false; break; }
       tc::fence_after();
-      if (i >= PB && !wwait(&pv_done[pb], ((i - PB) / PB) & 1, 56)) { ok = false; break; }
+      if (!C::VT && i >= PB && !wwait(&pv_done[pb], ((i - PB) / PB) & 1, 56)) { ok = false; break; }
       const uint8_t* info = stages + s * C::STAGE_BYTES + 2 * C::QT_BYTES;
       const float2* lsd = reinterpret_cast<const float2*>(info);
       const int2* kse = reinterpret_cast<const int2*>(info + BQ * 8);
+      if (C::VT) {
+        // P^T and dS^T back into the first BQ / 2 columns of the score buffers; the 32-column
+        // halves of S^T / dP^T are read before anything is stored over them
+        float pw[BQ / 2], dw[BQ / 2];
+#pragma unroll
+        for (int c = 0; c < BQ; c += 32) {
+          float sv[32], dv[32];
+          tc::tmem_ld32(lane_base + c, sv);
+          tc::tmem_ld32(lane_base + C::DP_COL + c, dv);
+#pragma unroll
+          for (int r2 = 0; r2 < 16; ++r2) {
+            float p2[2], d2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int j = 2 * r2 + u, r = c + j;
+              const float2 ld = lsd[r];
+              const int2 rg = kse[r];
+              const float p = (key >= rg.x && key < rg.y) ? exp2f(sv[j] * sl2 - ld.x) : 0.f;
+              p2[u] = p;
+              d2[u] = p * (dv[j] - ld.y);
+            }
+            __nv_bfloat162 a2 = __floats2bfloat162_rn(p2[0], p2[1]);
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(d2[0], d2[1]);
+            pw[c / 2 + r2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&a2));
+            dw[c / 2 + r2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&b2));
+          }
+        }
+        tc::tmem_st32(lane_base, pw);
+        tc::tmem_st32(lane_base + C::DP_COL, dw);
+        tc::fence_before();
+        tc::mbar_arrive(&p_full[0]);
+        continue;
+      }
       uint8_t* prow = spt + pb * 2 * C::PT_BYTES + kl * 128;
       uint8_t* drow = prow + C::PT_BYTES;
 #pragma unroll
@@ -948,7 +1027,8 @@ __global__ void __launch_bounds__(192, 1)
       tc::fence_before();
       tc::mbar_arrive(&p_full[pb]);
     }
-    if (ok && np > 0 && !wwait(&pv_done[(np - 1) % PB], ((np - 1) / PB) & 1, 57)) ok = false;
+    if (ok && np > 0 && !wwait(&pv_done[C::VT ? 0 : (np - 1) % PB], (C::VT ? np - 1 : (np - 1) / PB) & 1, 57))
+      ok = false;
     if (ok) {
       tc::fence_after();
       const bool valid = key < a.keys;
@@ -1084,7 +1164,8 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
   auto orders = at::empty({schedule ? nqb128 + nkb : 0}, q.options().dtype(at::kInt));
   BwdTcArgs a{schedule ? orders.data_ptr<int>() : nullptr, schedule ? orders.data_ptr<int>() + nqb128 : nullptr,
               reinterpret_cast<const float2*>(lsd.data_ptr<float>()), reinterpret_cast<const int2*>(kse.data_ptr<int>()),
-              qb_min.data_ptr<int>(), qb_max.data_ptr<int>(), (__nv_bfloat16*)dq.data_ptr(),
+              qb_min.data_ptr<int>(), qb_max.data_ptr<int>(), (const __nv_bfloat16*)v.data_ptr(),
+              (__nv_bfloat16*)dq.data_ptr(),
               (__nv_bfloat16*)dk.data_ptr(), (__nv_bfloat16*)dv.data_ptr(), rows, rows_pad, keys, Hq, Hkv,
               (float)scale};
   auto launch = [&](auto dtag) {

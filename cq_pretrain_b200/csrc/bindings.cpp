@@ -30,6 +30,7 @@ at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
 at::Tensor gemm_nn(at::Tensor a, at::Tensor b);
 void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out);
 int gemm_status(bool reset);
+std::vector<at::Tensor> ce_partials(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo);
 std::vector<at::Tensor> ce_stats(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo);
 at::Tensor ce_grad_logits(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, int64_t lo,
                           at::Tensor scale);
@@ -47,6 +48,9 @@ at::Tensor symm_view(int64_t base, int64_t offset, std::vector<int64_t> shape, a
 void signal_wait(at::Tensor peer_flag_ptrs, int64_t my_flags, int64_t rank, int64_t tp, int64_t epoch, bool wait);
 at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp, int64_t rows, int64_t cols);
 int comm_status_read(bool reset);
+std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at::Tensor peer_recv, int64_t my_recv,
+                                      at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
+                                      int64_t max_rows, int64_t epoch);
 std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_recv, int64_t my_recv,
                                    at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
                                    int64_t epoch, int64_t total_dim, double eps);
@@ -87,7 +91,8 @@ at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::T
 // optim.cu
 void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avg,
                 std::vector<at::Tensor> exp_avg_sq, std::vector<at::Tensor> decay, std::vector<at::Tensor> params,
-                at::Tensor gscale, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2);
+                at::Tensor gscale, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                std::vector<at::Tensor> ema, double ema_weight);
 at::Tensor sum_squares(std::vector<at::Tensor> xs);
 }  // namespace cqb
 
@@ -111,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_acc", &cqb::gemm_tn_acc);
   m.def("gemm_status", &cqb::gemm_status, py::arg("reset") = false);
   m.def("ce_stats", &cqb::ce_stats);
+  m.def("ce_partials", &cqb::ce_partials);
   m.def("ce_grad_logits", &cqb::ce_grad_logits);
   m.def("gemm_scatter", &cqb::gemm_scatter);
   m.def("gather_gemm", &cqb::gather_gemm);
@@ -123,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_reduce", &cqb::rs_reduce);
   m.def("comm_status_read", &cqb::comm_status_read, py::arg("reset") = false);
   m.def("tp_rms_fwd", &cqb::tp_rms_fwd);
+  m.def("ce_combine_tp", &cqb::ce_combine_tp);
   m.def("tp_rms_bwd", &cqb::tp_rms_bwd);
   m.def("gdn_fwd", &cqb::gdn_fwd);
   m.def("gdn_bwd", &cqb::gdn_bwd);
@@ -131,7 +138,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &cqb::attn_fwd);
   m.def("attn_bwd", &cqb::attn_bwd);
   m.def("attn_status", &cqb::attn_status, py::arg("reset") = false);
-  m.def("adamw_step", &cqb::adamw_step);
+  m.def("adamw_step", &cqb::adamw_step, py::arg("masters"), py::arg("grads"), py::arg("exp_avg"),
+        py::arg("exp_avg_sq"), py::arg("decay"), py::arg("params"), py::arg("gscale"), py::arg("lr"), py::arg("b1"),
+        py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("bc1"), py::arg("bc2"),
+        py::arg("ema") = std::vector<at::Tensor>{}, py::arg("ema_weight") = 0.0);
   m.def("sum_squares", &cqb::sum_squares);
   m.def("gdn_prep", &cqb::gdn_prep);
   m.def("gdn_chunk_bwd", &cqb::gdn_chunk_bwd);

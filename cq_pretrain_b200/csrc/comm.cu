@@ -299,6 +299,123 @@ at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp
 
 
 namespace {
+
+// Vocabulary-parallel cross-entropy statistics, combined over TP in one kernel: per 64-row block
+// the LM-head GEMM's per-tile (max, sum exp) partials are merged (one warp per row), this rank's
+// (max, sum exp, target logit) triples are stored into slot `rank` of every peer's statistics slab
+// (three floats per row), a per-block flag is released to every peer, and after acquiring the
+// peers' flags (bounded wait, status 300 + peer) each row's log-sum-exp over the full vocabulary and
+// its target logit are formed from the tp triples. Persistent grid, blocks in the same order on
+// every rank.
+__global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __restrict__ part, int tiles,
+                                                            const float* __restrict__ tgt_local, int rows,
+                                                            float* __restrict__ lse_out, float* __restrict__ tgt_out,
+                                                            float* const* peer_recv, const float* my_recv,
+                                                            long long* const* peer_flags, const long long* my_flags,
+                                                            int rank, int tp, int max_rows, long long epoch,
+                                                            int* status) {
+  __shared__ float trip[STAT_ROWS][3];
+  __shared__ int failed;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blocks = (rows + STAT_ROWS - 1) / STAT_ROWS;
+  auto merge = [](float& m, float& s, float om, float os) {
+    const float nm = fmaxf(m, om);
+    if (nm == -INFINITY) return;
+    s = s * __expf(m - nm) + os * __expf(om - nm);
+    m = nm;
+  };
+  if (threadIdx.x == 0) failed = 0;
+  for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
+    for (int rr = 0; rr < STAT_ROWS / 8; ++rr) {
+      const int lr = warp * (STAT_ROWS / 8) + rr, row = b * STAT_ROWS + lr;
+      float m = -INFINITY, sum = 0.f;
+      if (row < rows) {
+        for (int t = lane; t < tiles; t += 32) {
+          const float2 p = part[(size_t)row * tiles + t];
+          merge(m, sum, p.x, p.y);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, sum, o);
+        merge(m, sum, om, os);
+      }
+      if (lane == 0) {
+        trip[lr][0] = m;
+        trip[lr][1] = sum;
+        trip[lr][2] = row < rows ? tgt_local[row] : 0.f;
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < STAT_ROWS * tp; i += blockDim.x) {
+      const int t = i / STAT_ROWS, lr = i % STAT_ROWS;
+      float* dst = peer_recv[t] + (size_t)rank * max_rows + 3 * (size_t)(b * STAT_ROWS + lr);
+      dst[0] = trip[lr][0];
+      dst[1] = trip[lr][1];
+      dst[2] = trip[lr][2];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < tp) st_release_sys(peer_flags[threadIdx.x] + (size_t)b * STAT_MAX_TP + rank, epoch);
+    if (threadIdx.x < tp) {
+      const long long* f = my_flags + (size_t)b * STAT_MAX_TP + threadIdx.x;
+      const unsigned long long start = tc::globaltimer();
+      while (ld_acquire_sys(f) < epoch) {
+        if (tc::globaltimer() - start > tc::kWaitNs) {
+          atomicCAS(status, 0, 300 + threadIdx.x);
+          failed = 1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    if (failed) return;   // the host reads the status word; outputs of this call are invalid
+    if (threadIdx.x < STAT_ROWS) {
+      const int row = b * STAT_ROWS + threadIdx.x;
+      float m = -INFINITY, sum = 0.f, tg = 0.f;
+      for (int t = 0; t < tp; ++t) {
+        const float* src = my_recv + (size_t)t * max_rows + 3 * (size_t)row;
+        merge(m, sum, src[0], src[1]);
+        tg += src[2];
+      }
+      if (row < rows) {
+        lse_out[row] = m + __logf(sum);
+        tgt_out[row] = tg;
+      }
+    }
+    __syncthreads();   // trip[] is rewritten by the next block
+  }
+}
+
+}  // namespace
+
+// part: [rows, tiles] float2 from the LM-head GEMM (epilogue 3); tgt_local [rows]; returns the
+// full-vocabulary (lse, target logit) per row. The exchange uses three floats per row of the
+// statistics slab, so 3 * rows <= max_rows.
+std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at::Tensor peer_recv, int64_t my_recv,
+                                      at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
+                                      int64_t max_rows, int64_t epoch) {
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.dim() == 3 && part.size(2) == 2 &&
+                  part.is_contiguous(),
+              "part: fp32 [rows, tiles, 2]");
+  const int64_t rows = part.size(0);
+  TORCH_CHECK(tgt_local.scalar_type() == at::kFloat && tgt_local.numel() == rows && tgt_local.is_contiguous(),
+              "tgt_local: fp32 [rows]");
+  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && 3 * rows <= max_rows, "rows exceed the exchange slab");
+  auto lse = at::empty({rows}, part.options()), tgt = at::empty({rows}, part.options());
+  if (!rows) return {lse, tgt};
+  const int grid = std::max(1, std::min((int)((rows + STAT_ROWS - 1) / STAT_ROWS), sm_count()));
+  ce_combine_tp_kernel<<<grid, 256, 0, stream()>>>(
+      reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)part.size(1), tgt_local.data_ptr<float>(),
+      (int)rows, lse.data_ptr<float>(), tgt.data_ptr<float>(), reinterpret_cast<float* const*>(peer_recv.data_ptr()),
+      reinterpret_cast<const float*>(my_recv), reinterpret_cast<long long* const*>(peer_flags.data_ptr()),
+      reinterpret_cast<const long long*>(my_flags), (int)rank, (int)tp, (int)max_rows, epoch, comm_status());
+  CQB_LAUNCH_CHECK();
+  count_launch();
+  return {lse, tgt};
+}
+
+namespace {
 TpNormArgs tp_norm_args(const at::Tensor& x, const at::Tensor& w, at::Tensor peer_recv, int64_t my_recv,
                         at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
                         int64_t epoch, int64_t total_dim, double eps) {

@@ -672,16 +672,15 @@ void check_ce(const at::Tensor& h, const at::Tensor& w, const at::Tensor& target
 
 }  // namespace
 
-// Vocabulary-shard statistics of logits = h w^T without materialising them:
-// returns (row max, target logit (0 where the target is outside [lo, lo + V)), sum exp(logit - max)).
-std::vector<at::Tensor> ce_stats(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo) {
+// LM-head GEMM with the statistics epilogue only: returns the per-(row, column tile) (max, sum exp)
+// partials [rows, tiles, 2] and the target logit [rows] (0 where the target is outside [lo, lo + V)).
+std::vector<at::Tensor> ce_partials(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo) {
   check_ce(h, w, targets);
   const int64_t M = h.size(0), K = h.size(1), N = w.size(0);
   const int tiles_n = (int)((N + BN - 1) / BN);
   auto f32 = h.options().dtype(at::kFloat);
   auto part = at::empty({M, tiles_n, 2}, f32);
   auto tgt = at::zeros({M}, f32);
-  auto mx = at::empty({M}, f32), se = at::empty({M}, f32);
   auto ma = make_map(h, BM);
   auto mb = make_map(w, BN);
   auto args = plain_args(M, N, K, nullptr, N, nullptr);
@@ -690,6 +689,17 @@ std::vector<at::Tensor> ce_stats(at::Tensor h, at::Tensor w, at::Tensor targets,
   args.ce_part = reinterpret_cast<float2*>(part.data_ptr<float>());
   args.ce_target = tgt.data_ptr<float>();
   launch<false, false, 3, false>(ma, mb, ma, args);
+  return {part, tgt};
+}
+
+// Vocabulary-shard statistics of logits = h w^T without materialising them:
+// returns (row max, target logit (0 where the target is outside [lo, lo + V)), sum exp(logit - max)).
+std::vector<at::Tensor> ce_stats(at::Tensor h, at::Tensor w, at::Tensor targets, int64_t lo) {
+  auto pt = ce_partials(h, w, targets, lo);
+  auto part = pt[0], tgt = pt[1];
+  const int64_t M = h.size(0);
+  const int tiles_n = (int)part.size(1);
+  auto mx = at::empty({M}, tgt.options()), se = at::empty({M}, tgt.options());
   ce_merge_kernel<<<(unsigned)((M * 32 + 255) / 256), 256, 0, stream()>>>(
       reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)M, tiles_n, mx.data_ptr<float>(),
       se.data_ptr<float>());

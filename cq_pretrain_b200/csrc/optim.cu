@@ -24,6 +24,7 @@ struct AdamTensor {
   float* v;
   const uint8_t* decay;
   void* out;      // parameter in its training dtype (bf16 or fp32); may be null
+  float* ema;     // EMA shadow of the master (fp32), lerped toward the updated master; may be null
   long n;
   int out_bf16;
   int vec;        // every pointer is 16-byte aligned (8-byte for the bf16 output)
@@ -37,6 +38,7 @@ struct Chunk {
 
 struct AdamScalars {
   float lr, b1, b2, eps, wd, bc1, bc2;
+  float ema_w;    // 1 - EMA decay
 };
 
 __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, uint8_t decay, float gs,
@@ -71,6 +73,14 @@ __global__ void __launch_bounds__(OPT_THREADS) adamw_kernel(const AdamTensor* __
           *reinterpret_cast<float4*>(t.p + i) = p;
           *reinterpret_cast<float4*>(t.m + i) = m;
           *reinterpret_cast<float4*>(t.v + i) = v;
+          if (t.ema) {
+            float4 e = *reinterpret_cast<const float4*>(t.ema + i);
+            e.x += a.ema_w * (p.x - e.x);
+            e.y += a.ema_w * (p.y - e.y);
+            e.z += a.ema_w * (p.z - e.z);
+            e.w += a.ema_w * (p.w - e.w);
+            *reinterpret_cast<float4*>(t.ema + i) = e;
+          }
           if (t.out) {
             if (t.out_bf16) {
               __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
@@ -87,6 +97,7 @@ __global__ void __launch_bounds__(OPT_THREADS) adamw_kernel(const AdamTensor* __
             float p = t.p[j], m = t.m[j], v = t.v[j];
             adam_one(p, t.g[j], m, v, t.decay[j], gs, a);
             t.p[j] = p; t.m[j] = m; t.v[j] = v;
+            if (t.ema) t.ema[j] += a.ema_w * (p - t.ema[j]);
             if (t.out) {
               if (t.out_bf16) static_cast<__nv_bfloat16*>(t.out)[j] = __float2bfloat16(p);
               else static_cast<float*>(t.out)[j] = p;
@@ -99,6 +110,7 @@ __global__ void __launch_bounds__(OPT_THREADS) adamw_kernel(const AdamTensor* __
         float p = t.p[j], m = t.m[j], v = t.v[j];
         adam_one(p, t.g[j], m, v, t.decay[j], gs, a);
         t.p[j] = p; t.m[j] = m; t.v[j] = v;
+        if (t.ema) t.ema[j] += a.ema_w * (p - t.ema[j]);
         if (t.out) {
           if (t.out_bf16) static_cast<__nv_bfloat16*>(t.out)[j] = __float2bfloat16(p);
           else static_cast<float*>(t.out)[j] = p;
@@ -197,12 +209,16 @@ int grid_for(size_t chunks) { return (int)std::max<size_t>(1, std::min<size_t>(c
 
 }  // namespace
 
+// ema: empty, or one fp32 tensor per master (numel 0 = no EMA for that tensor), lerped toward the
+// updated master with weight ema_weight (= 1 - decay) in the same pass.
 void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avg,
                 std::vector<at::Tensor> exp_avg_sq, std::vector<at::Tensor> decay, std::vector<at::Tensor> params,
-                at::Tensor gscale, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2) {
+                at::Tensor gscale, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                std::vector<at::Tensor> ema, double ema_weight) {
   const size_t count = masters.size();
   TORCH_CHECK(grads.size() == count && exp_avg.size() == count && exp_avg_sq.size() == count &&
-                  decay.size() == count && (params.empty() || params.size() == count),
+                  decay.size() == count && (params.empty() || params.size() == count) &&
+                  (ema.empty() || ema.size() == count),
               "adamw_step: list lengths differ");
   TORCH_CHECK(gscale.scalar_type() == at::kFloat && gscale.numel() == 1 && gscale.is_cuda(), "gscale: fp32 scalar");
   std::vector<AdamTensor> tensors;
@@ -222,10 +238,16 @@ void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, 
       out = params[i].data_ptr();
       out_bf16 = params[i].scalar_type() == at::kBFloat16;
     }
+    float* shadow = nullptr;
+    if (!ema.empty() && ema[i].numel()) {
+      TORCH_CHECK(ema[i].scalar_type() == at::kFloat && ema[i].is_contiguous() && ema[i].numel() == n,
+                  "adamw_step: EMA shadow fp32 contiguous like the master");
+      shadow = ema[i].data_ptr<float>();
+    }
     AdamTensor t{masters[i].data_ptr<float>(), grads[i].data_ptr<float>(), exp_avg[i].data_ptr<float>(),
-                 exp_avg_sq[i].data_ptr<float>(), decay[i].data_ptr<uint8_t>(), out, n, out_bf16, 0};
+                 exp_avg_sq[i].data_ptr<float>(), decay[i].data_ptr<uint8_t>(), out, shadow, n, out_bf16, 0};
     t.vec = aligned(t.p, 16) && aligned(t.g, 16) && aligned(t.m, 16) && aligned(t.v, 16) && aligned(t.decay, 4) &&
-            aligned(out, out_bf16 ? 8 : 16);
+            aligned(out, out_bf16 ? 8 : 16) && aligned(shadow, 16);
     tensors.push_back(t);
   }
   if (tensors.empty()) return;
@@ -234,7 +256,7 @@ void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, 
   const auto* dt = reinterpret_cast<const AdamTensor*>(table.data_ptr());
   const auto* dc = reinterpret_cast<const Chunk*>(static_cast<const char*>(table.data_ptr()) +
                                                   sizeof(AdamTensor) * tensors.size());
-  AdamScalars a{(float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2};
+  AdamScalars a{(float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2, (float)ema_weight};
   adamw_kernel<<<grid_for(num_chunks), OPT_THREADS, 0, stream()>>>(dt, dc, num_chunks, gscale.data_ptr<float>(), a);
   CQB_LAUNCH_CHECK();
   count_launch();

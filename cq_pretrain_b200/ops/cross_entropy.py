@@ -10,8 +10,10 @@ Reference: ``ops/cross_entropy.py:17-116``.
 On CUDA the per-chunk work is an LM-head GEMM whose epilogue computes the row statistics
 online (``csrc/gemm.cu``, epilogue 3), so logits are never written to memory in the forward,
 and the backward recomputes each logits tile and stores ``(softmax - onehot) * dloss`` straight
-from the accumulator (epilogue 4). The TP combine of the ``[rows]`` statistics is one MAX and one
-SUM all-reduce.
+from the accumulator (epilogue 4). Under TP the per-tile partials go straight into one kernel that
+merges them, exchanges each row's (max, sum exp, target logit) with the other ranks over NVLink peer
+memory and forms the full-vocabulary log-sum-exp (``csrc/comm.cu``, ``parallel/symmetric.py``); the
+NCCL MAX + SUM all-reduce pair remains only for other devices or without the TP workspace.
 """
 
 from __future__ import annotations
@@ -54,6 +56,15 @@ def _chunk_stats(h, w, targets, lo):
     return mx, tgt, sexp
 
 
+def _fused_workspace(hidden, weight, group, chunk):
+    """The TP workspace when the in-kernel statistics exchange applies (CUDA kernels, TP > 1)."""
+    if group is None or not _kernel_shapes(hidden, weight) or not _ext.has("ce_partials"):
+        return None
+    from ..parallel import symmetric
+    ws = symmetric.workspace()
+    return ws if ws is not None and ws.supports_ce(min(chunk, hidden.shape[0])) else None
+
+
 DLOGITS_BUDGET = 4 << 30   # bytes of bf16 softmax gradients the kernel path may hold at once
 
 
@@ -74,10 +85,14 @@ class _LinearCE(torch.autograd.Function):
         lo = rank * weight.shape[0]
         total = torch.zeros((), dtype=torch.float32, device=hidden.device)
         lse_all = torch.empty(hidden.shape[0], dtype=torch.float32, device=hidden.device)
+        ws = _fused_workspace(hidden, weight, group, chunk)
         for start in range(0, hidden.shape[0], chunk):
             h, t = hidden[start:start + chunk], targets[start:start + chunk]
-            mx, tgt, sexp = _stats_combine(*_chunk_stats(h, weight, t, lo), group)
-            lse = mx + torch.log(sexp)
+            if ws is not None:
+                lse, tgt = ws.ce_combine(*_ext.ops().ce_partials(h.contiguous(), weight, t, lo))
+            else:
+                mx, tgt, sexp = _stats_combine(*_chunk_stats(h, weight, t, lo), group)
+                lse = mx + torch.log(sexp)
             lse_all[start:start + chunk] = lse
             total += (lse - tgt).sum()
         ctx.save_for_backward(hidden, weight, targets, lse_all)

@@ -93,6 +93,7 @@ class DistributedOptimizer:
         self.dp, self.dp_rank, self.dp_group = st.dp, st.dp_rank, st.dp_group
         self.tp, self.tp_group, self.tp_rank = st.tp, st.tp_group, st.tp_rank
         self.overlap = overlap
+        self.ema, self.ema_fused = None, False
         named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
         self.names = {p: n for n, p in named}
         device = named[0][1].device
@@ -269,10 +270,12 @@ class DistributedOptimizer:
         gscale = (coef * scale).float().reshape(())
         published = [s["bucket"].group.param_buffer[s["lo"]:s["lo"] + s["n"]] for s in self.shards]
         if self._use_kernels():
-            # one launch: scale, moments, decoupled decay, update and the parameter write-back
-            _ext.ops().adamw_step([s["master"] for s in self.shards], grads, [s["exp_avg"] for s in self.shards],
-                                  [s["exp_avg_sq"] for s in self.shards], [s["decay"] for s in self.shards],
-                                  published, gscale, lr, b1, b2, self.eps, self.weight_decay, bc1, bc2)
+            # one launch: scale, moments, decoupled decay, update, the parameter write-back and (when
+            # a renderer EMA is attached) the shadow lerp toward the updated masters
+            lists = self._kernel_lists(grads, published)
+            _ext.ops().adamw_step(*lists[:6], gscale, lr, b1, b2, self.eps, self.weight_decay, bc1, bc2,
+                                  lists[6], 1.0 - self.ema.decay if self.ema is not None else 0.0)
+            self.ema_fused = self.ema is not None
         else:
             for s, g, out in zip(self.shards, grads, published):
                 g = g * gscale
@@ -285,6 +288,36 @@ class DistributedOptimizer:
                 out.copy_(p)
         self.all_gather_params()
         return finite, norm
+
+    def attach_ema(self, ema):
+        """Let the AdamW kernel update ``ema``'s shadows (``shadow += (1 - decay)(master - shadow)``)."""
+        self.ema, self.ema_fused = ema, False
+
+    def _kernel_lists(self, grads, published):
+        """Per-shard tensors for the AdamW kernel, split at the EMA slices so that each renderer
+        slice carries its shadow (an empty tensor marks slices without one)."""
+        ema = getattr(self, "ema", None)
+        ranges = {}
+        if ema is not None:
+            for (si, a, b), shadow in zip(ema.index, ema.shadows):
+                ranges.setdefault(si, []).append((a, b, shadow))
+        out = [[] for _ in range(7)]
+        none = self.shards[0]["master"].new_empty(0)
+        for si, (s, g, pub) in enumerate(zip(self.shards, grads, published)):
+            tensors = (s["master"], g, s["exp_avg"], s["exp_avg_sq"], s["decay"], pub)
+            cuts, cursor = [], 0
+            for a, b, shadow in sorted(ranges.get(si, []), key=lambda r: r[0]):
+                if a > cursor:
+                    cuts.append((cursor, a, none))
+                cuts.append((a, b, shadow))
+                cursor = b
+            if cursor < s["n"]:
+                cuts.append((cursor, s["n"], none))
+            for a, b, shadow in cuts:
+                for lst, t in zip(out, tensors):
+                    lst.append(t[a:b])
+                out[6].append(shadow)
+        return out
 
     def all_gather_params(self):
         if self.dp == 1:

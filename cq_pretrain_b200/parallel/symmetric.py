@@ -18,7 +18,8 @@ Protocol (epochs count calls of each kind; every rank issues the same sequence):
 * GEMM -> reduce-scatter (epoch e): one GEMM kernel stores every output tile into the owner's
   ``recv[e % 2][src]``; a one-block kernel publishes flag e and acquires all peers' flags; a
   bandwidth kernel sums the tp slabs.
-* row statistics (epoch e, Wan's full-width Q/K RMSNorm): one kernel per call; each 64-row block
+* row statistics (epoch e, Wan's full-width Q/K RMSNorm, and the vocabulary-parallel cross-entropy's
+  (max, sum exp, target logit) triples): one kernel per call; each 64-row block
   stores its partial sums into ``stat[e % 2][rank]`` of every peer, publishes a per-block flag and
   acquires the peers' flags of the same block before normalising its rows.
 
@@ -154,6 +155,17 @@ class SymmetricWorkspace:
         return _ext.ops().tp_rms_bwd(dy, x, weight, rstd, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
                                      self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e,
                                      total_dim)
+
+    def supports_ce(self, rows):
+        return 3 * rows <= self.stat_rows and _ext.has("ce_combine_tp")
+
+    def ce_combine(self, part, tgt_local):
+        """Full-vocabulary (lse, target logit) per row from this rank's LM-head partials: the
+        (max, sum exp, target) triples cross NVLink inside one kernel (no NCCL call)."""
+        self.epoch_stat += 1
+        e, p = self.epoch_stat, self.epoch_stat % 2
+        return _ext.ops().ce_combine_tp(part, tgt_local, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
+                                        self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e)
 
     def linear_scatter(self, x, weight):
         """``reduce_scatter_rows(x @ W^T)`` with the GEMM storing tiles into the owners' buffers."""

@@ -2,7 +2,8 @@
 
 ``shadow += (1 - decay) (master - shadow)`` on the slice of every owned shard that belongs
 to ``renderer.*`` parameters: no collectives, and no rank holds a full DiT copy (reference
-``training/ema.py:17-119``). ``average_parameters`` temporarily installs the shadows into the
+``training/ema.py:17-119``). On CUDA the lerp runs inside the optimizer's AdamW kernel (the
+updated master is still in registers); ``update`` then only counts the step. ``average_parameters`` temporarily installs the shadows into the
 masters and republishes the parameters (all-gather), restoring the online weights after.
 """
 
@@ -45,6 +46,8 @@ class RendererEMA:
             dist.all_reduce(covered, group=optimizer.dp_group)
         if int(covered) != sum(p.numel() for p in names):
             raise ValueError("EMA shards do not cover the renderer exactly once")
+        if hasattr(optimizer, "attach_ema"):
+            optimizer.attach_ema(self)    # the AdamW kernel lerps the shadows in its own pass
 
     def masters(self):
         return [self.optimizer.shards[si]["master"][a:b] for si, a, b in self.index]
@@ -53,7 +56,9 @@ class RendererEMA:
     def update(self):
         if self.active:
             raise RuntimeError("cannot update EMA while EMA weights are installed")
-        if self.shadows:
+        if getattr(self.optimizer, "ema_fused", False):
+            self.optimizer.ema_fused = False      # the optimizer step already lerped the shadows
+        elif self.shadows:
             torch._foreach_lerp_(self.shadows, self.masters(), 1.0 - self.decay)
         self.num_updates += 1
 

@@ -58,3 +58,27 @@ def test_sum_squares_multi_tensor():
     assert abs(got.item() - want.item()) < 1e-4 * want.item()
     again = _ext.ops().sum_squares(xs)
     assert got.item() == again.item()  # fixed reduction order
+
+
+def test_adamw_fused_ema_matches_lerp():
+    """EMA shadows lerped inside the AdamW pass equal a separate lerp toward the updated masters;
+    tensors without a shadow (empty entry) are untouched, unaligned slices take the scalar path."""
+    torch.manual_seed(2)
+    sizes = [7, 4096, 10_001]
+    masters = [torch.randn(n, device="cuda") for n in sizes]
+    grads = [torch.randn(n, device="cuda") for n in sizes]
+    ms = [torch.randn(n, device="cuda") * 0.1 for n in sizes]
+    vs = [torch.rand(n, device="cuda") * 0.01 for n in sizes]
+    decays = [torch.ones(n, device="cuda", dtype=torch.uint8) for n in sizes]
+    outs = [torch.empty(n, device="cuda", dtype=torch.bfloat16) for n in sizes]
+    store = torch.randn(sum(sizes) + 1, device="cuda")
+    shadows = [store[1:8].clone(), torch.empty(0, device="cuda"), store[9:9 + 10_001]]   # unaligned view
+    before = [s.clone() for s in shadows]
+    args = dict(lr=1e-3, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, bc1=0.1, bc2=0.05)
+    expect = [_reference(p.clone(), g, m.clone(), v.clone(), d, 1.0, **args)[0]
+              for p, g, m, v, d in zip(masters, grads, ms, vs, decays)]
+    _ext.ops().adamw_step(masters, grads, ms, vs, decays, outs, torch.tensor(1.0, device="cuda"), *args.values(),
+                          shadows, 0.25)
+    for p_new, shadow, old in zip(expect, shadows, before):
+        if shadow.numel():
+            torch.testing.assert_close(shadow, old + 0.25 * (p_new - old), rtol=1e-5, atol=1e-6)

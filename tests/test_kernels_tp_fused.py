@@ -1,4 +1,5 @@
-"""In-kernel TP collectives (all-gather->GEMM, GEMM->reduce-scatter) vs NCCL on 2+ GPUs."""
+"""In-kernel TP collectives (all-gather->GEMM, GEMM->reduce-scatter, RMSNorm and cross-entropy
+statistics exchanges) vs NCCL / full-precision references on 2+ GPUs."""
 
 import os
 import socket
@@ -65,6 +66,25 @@ def _worker(rank, world, port, out):
         errors.append(float((yq.float() - yr).abs().max() / yr.abs().max()))
         errors.append(float((xq.grad.float() - xr.grad).norm() / xr.grad.norm()))
         errors.append(float((norm.weight.grad.float() - wr.grad).norm() / wr.grad.norm()))
+        # vocabulary-parallel CE: in-kernel (max, sum exp, target) exchange vs full fp32 logits
+        from cq_pretrain_b200.ops import cross_entropy as CE
+        gen = torch.Generator(device="cuda").manual_seed(100 + it)        # same rows on every rank
+        rows, vocab = 400 + 64 * it, 1024 * world
+        hid = torch.randn(rows, 256, device="cuda", generator=gen).to(torch.bfloat16).requires_grad_()
+        tgts = torch.randint(0, vocab, (rows,), device="cuda", generator=gen)
+        w_shard = (torch.randn(vocab // world, 256, device="cuda") * 0.05).to(torch.bfloat16)
+        assert CE._fused_workspace(hid, w_shard, st.tp_group, rows) is not None
+        loss = CE.linear_cross_entropy(hid, w_shard, tgts, rows)
+        loss.backward()
+        shards = [torch.empty_like(w_shard) for _ in range(world)]
+        dist.all_gather(shards, w_shard)
+        href = hid.detach().float().requires_grad_()
+        ref_loss = torch.nn.functional.cross_entropy(href @ torch.cat(shards).float().T, tgts)
+        ref_loss.backward()
+        dh = hid.grad.float().clone()
+        dist.all_reduce(dh)                 # each rank holds its vocabulary shard's part of dh
+        errors.append(float((loss.float() - ref_loss).abs() / ref_loss.abs()))
+        errors.append(float((dh - href.grad).norm() / href.grad.norm()))
     torch.cuda.synchronize()
     status = symmetric.status()
     symmetric.disable()
