@@ -61,8 +61,9 @@ def query_conv_silu(raw, updates, weight, plan):
     history gradient over the CSR ``plan.query_hist_*`` (deterministic, no atomics).
     """
     size, K = weight.shape
-    if (raw.is_cuda and raw.dtype == torch.bfloat16 and K == 4 and size % 8 == 0 and _ext.has("qconv_fwd")
-            and plan.query_hist_rows is not None):
+    rows_ok = all(t.stride(-1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0 for t in (raw, updates))
+    if (raw.is_cuda and raw.dtype == torch.bfloat16 and K == 4 and size % 8 == 0 and rows_ok
+            and _ext.has("qconv_fwd") and plan.query_hist_rows is not None):
         return _QueryConv.apply(raw, updates, weight, plan.query_source, plan.query_history, plan.query_hist_rows,
                                 plan.query_hist_offsets, plan.query_hist_entries)
     from . import gather as GA

@@ -1,6 +1,7 @@
 """Cached CQ decoding equals full-prefix recomputation (float64); flow sampler and suite plumbing."""
 
 import numpy as np
+import pytest
 import torch
 
 from cq_pretrain_b200.config import tiny_config
@@ -66,3 +67,25 @@ def test_generate_runs_on_cpu():
     out = sampling.generate(model, batch, steps=2, shift=5.0)
     assert out["latent"].shape == (sum(batch.generation.lengths), 64)
     assert torch.isfinite(out["latent"]).all()
+
+
+@pytest.mark.gpu
+def test_graphed_decode_matches_eager_cuda():
+    """CUDA-graph replay of the decode step (fixed KV buffers, device-side count and position)
+    follows the eager decoder token by token (bf16 model, tcgen05 attention vs SDPA)."""
+    from cq_pretrain_b200.models.decoding import GraphedCQDecoder
+    torch.manual_seed(0)
+    cfg = tiny_config(layers=4, vocab_size=128, width=128, ffn=256, heads=4, kv_heads=2, head_dim=64,
+                      mrope_section=(4, 4, 0), linear_heads=2, linear_value_heads=8, linear_head_dim=64, dit_width=32, dit_heads=2,
+                      dit_ffn=64, dit_layers=1, text_mask_token_id=4, image_mask_token_id=5)
+    model = JointModel(cfg).cuda().to(torch.bfloat16).eval()
+    prefix = [10, 11, 12, 13, 14, 15, 3]
+    eager = CQDecoder(model, _one_doc(cfg, prefix, 32), max_new_tokens=5)
+    graphed = GraphedCQDecoder(model, _one_doc(cfg, prefix, 32), max_new_tokens=5)
+    torch.testing.assert_close(graphed.hidden.float(), eager.hidden.float())
+    for token in (21, 22, 23, 24):
+        want = eager.advance(token).float().clone()
+        got = graphed.advance(token).float().clone()
+        rel = ((got - want).norm() / want.norm()).item()
+        assert rel < 3e-2, (token, rel)
+    assert graphed.graph is not None
