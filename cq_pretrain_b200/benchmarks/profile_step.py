@@ -1,7 +1,7 @@
 """Per-kernel device-time breakdown of one joint training step (torch.profiler, CUPTI).
 
-``python -m cq_pretrain_b200.benchmarks.profile_step [--length 8192] [--recompute 1]`` runs the
-bench configuration (1 GPU), warms up, profiles one step and prints the kernels with the
+``[torchrun --nproc-per-node N] python -m cq_pretrain_b200.benchmarks.profile_step [--length 8192]
+[--recompute 1]`` runs the bench configuration (TP = N, rank 0 reports), warms up, profiles one step and prints the kernels with the
 largest total device time, grouped by name, plus each group's share of the step.
 """
 
@@ -20,17 +20,24 @@ def main():
     parser.add_argument("--top", type=int, default=40)
     parser.add_argument("--layers", type=int, default=None)
     args = parser.parse_args()
+    import os
+
     from ..config import qwen35_2b_wan
     from ..data.synthetic import synthetic_batch
+    from ..parallel import state as ps
     from ..train.trainer import Trainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    st = ps.initialize(world, timeout_s=600.0) if world > 1 else None   # TP = world (torchrun)
+    tp = world
 
     cfg = qwen35_2b_wan(visual_query_mode="fixed", image_condition_queries=256, checkpoint_backbone=bool(args.recompute))
     if args.layers:
         cfg.layers = args.layers
     host, receipt = synthetic_batch(cfg, args.length, seed=42, kind="joint", images=2, grid=(1, 64, 64),
-                                    latent_shape=(16, 1, 64, 64), understanding=False, pad_multiple=128)
+                                    latent_shape=(16, 1, 64, 64), understanding=False, pad_multiple=128 * tp)
     host = host.pin_memory()
-    trainer = Trainer(cfg, tp=1, lr=5e-5, ema_decay=0.999)
+    trainer = Trainer(cfg, tp=tp, lr=5e-5, ema_decay=0.999)
     for _ in range(3):
         trainer.train_step([(host, receipt)])
     torch.cuda.synchronize()
@@ -38,6 +45,9 @@ def main():
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
         trainer.train_step([(host, receipt)])
         torch.cuda.synchronize()
+    if st is not None and st.rank != 0:
+        ps.destroy()
+        return
     events = prof.key_averages()
     kernels = [e for e in events if e.device_type.name == "CUDA"]
     total = sum(e.self_device_time_total for e in kernels)
@@ -51,6 +61,8 @@ def main():
               if e.key.startswith("aten::") and e.device_type.name == "CPU"]
     for e in sorted(shaped, key=lambda e: -e.device_time_total)[: args.top]:
         print(f"{e.device_time_total / 1000:9.2f} ms {e.count:6d}x  {e.key:28s} {str(e.input_shapes)[:120]}")
+    if st is not None:
+        ps.destroy()
 
 
 if __name__ == "__main__":

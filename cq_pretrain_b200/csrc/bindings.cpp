@@ -38,7 +38,7 @@ void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_o
                   int64_t src_rank, int64_t tp);
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
                        int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
-                       int64_t tp);
+                       int64_t tp, bool mn_major);
 // comm.cu
 std::vector<at::Tensor> symm_alloc(int64_t bytes);
 int64_t symm_open(at::Tensor handle_bytes);
@@ -119,7 +119,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_partials", &cqb::ce_partials);
   m.def("ce_grad_logits", &cqb::ce_grad_logits);
   m.def("gemm_scatter", &cqb::gemm_scatter);
-  m.def("gather_gemm", &cqb::gather_gemm);
+  m.def("gather_gemm", &cqb::gather_gemm, py::arg("a_local"), py::arg("w"), py::arg("bias"), py::arg("peer_in_ptrs"),
+        py::arg("ready_ptr"), py::arg("chunk_flags"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),
+        py::arg("tp"), py::arg("mn_major") = false);
   m.def("symm_alloc", &cqb::symm_alloc);
   m.def("symm_open", &cqb::symm_open);
   m.def("symm_close", &cqb::symm_close);

@@ -605,17 +605,19 @@ void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_o
 }
 
 // All-gather -> GEMM: y[M,N] = gather(x)[M,K] w[N,K]^T (+ bias); the gathered rows land in a_local.
+// mn_major: w is [K, N] (the row-parallel backward dX = all_gather(dY) @ W), else [N, K].
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
                        int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
-                       int64_t tp) {
-  const int64_t M = a_local.size(0), K = a_local.size(1), N = w.size(0);
+                       int64_t tp, bool mn_major) {
+  const int64_t M = a_local.size(0), K = a_local.size(1), N = mn_major ? w.size(1) : w.size(0);
+  TORCH_CHECK(!mn_major || w.size(0) == K, "gather_gemm: inner dims differ");
   check_dims(M, N, K);
   TORCH_CHECK(rows_per_rank % BM == 0 && M == rows_per_rank * tp, "rows per rank must be a multiple of 128");
   TORCH_CHECK(chunk_flags.scalar_type() == at::kLong && chunk_flags.numel() >= M / GATHER_SUB,
               "chunk flags too small: one per 16 rows");
   auto y = at::empty({M, N}, a_local.options());
   auto ma = make_map(a_local, BM);
-  auto mb = make_map(w, BN);
+  auto mb = make_map(w, mn_major ? BK : BN);
   at::Tensor b;
   if (bias && bias->defined()) b = bias->to(at::kBFloat16).contiguous();
   auto args = plain_args(M, N, K, y.data_ptr(), N, b.defined() ? (const __nv_bfloat16*)b.data_ptr() : nullptr);
@@ -627,7 +629,10 @@ at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tenso
   args.rows_per_rank = (int)rows_per_rank;
   args.src_rank = (int)src_rank;
   args.tp = (int)tp;
-  launch<false, false, 0, true>(ma, mb, make_out_map(y), args);
+  if (mn_major)
+    launch<false, true, 0, true>(ma, mb, make_out_map(y), args);
+  else
+    launch<false, false, 0, true>(ma, mb, make_out_map(y), args);
   return y;
 }
 

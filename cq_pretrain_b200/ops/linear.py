@@ -105,7 +105,8 @@ def gather_linear(x, weight, bias=None):
 
 
 class _LinearScatter(torch.autograd.Function):
-    """Row-parallel: ``y = reduce_scatter_rows(x @ W^T) + b``; backward all-gathers dY."""
+    """Row-parallel: ``y = reduce_scatter_rows(x @ W^T) + b``; backward all-gathers dY inside the
+    input-gradient GEMM (``all_gather(dY) @ W``) and reuses the gathered rows for the weight gradient."""
 
     @staticmethod
     def forward(ctx, x, weight, bias):
@@ -118,8 +119,10 @@ class _LinearScatter(torch.autograd.Function):
     def backward(ctx, dy):
         from ..parallel import fused
         x, weight = ctx.saved_tensors
-        dyg = fused.gather_rows_raw(dy.contiguous())
-        dx = gemm.matmul_nn(dyg, weight) if ctx.needs_input_grad[0] else None
+        if ctx.needs_input_grad[0]:
+            dx, dyg = fused.gather_matmul(dy.contiguous(), weight)   # one all-gather->GEMM kernel
+        else:
+            dx, dyg = None, fused.gather_rows_raw(dy.contiguous())
         dw = _weight_grad(weight, dyg, x) if ctx.needs_input_grad[1] else None
         db = _accumulate(ctx.bias, _bias_grad(dy)) if ctx.has_bias and ctx.needs_input_grad[2] else None
         return dx, dw, db

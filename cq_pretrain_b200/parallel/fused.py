@@ -52,6 +52,15 @@ def gather_linear(x, weight, bias=None):
     return gemm.linear(xg, weight, bias), xg
 
 
+def gather_matmul(dy, weight):
+    """Return ``(all_gather(dY) @ W, all_gather(dY))`` (input gradient of a row-parallel linear)."""
+    ws = _symm()
+    if ws is not None and ws.supports_gather(dy, weight, transposed=True):
+        return ws.gather_matmul(dy, weight)
+    dyg = gather_rows_raw(dy)
+    return gemm.matmul_nn(dyg, weight), dyg
+
+
 def linear_scatter(x, weight, bias=None):
     """Return ``reduce_scatter(x @ W^T) + b``."""
     ws = _symm()

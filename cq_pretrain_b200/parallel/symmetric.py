@@ -97,9 +97,10 @@ class SymmetricWorkspace:
         return (rows % (128 * self.tp) == 0 and n_out % 16 == 0 and x.shape[1] % 16 == 0
                 and rows * n_out * 2 <= self.recv_bytes and x.data_ptr() % 16 == 0)
 
-    def supports_gather(self, x, w):
+    def supports_gather(self, x, w, transposed=False):
+        n_out = w.shape[1] if transposed else w.shape[0]   # all_gather(x) @ W (transposed) or @ W^T
         return (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
-                and x.shape[1] % 16 == 0 and w.shape[0] % 16 == 0 and self._gather_ok(x))
+                and x.shape[1] % 16 == 0 and n_out % 16 == 0 and self._gather_ok(x))
 
     def _gather_ok(self, x):
         rows = x.shape[0] * self.tp
@@ -108,12 +109,20 @@ class SymmetricWorkspace:
     # ---- fused ops --------------------------------------------------------------------------------
     def gather_linear(self, x, weight, bias=None):
         """``(all_gather(x) @ W^T + b, all_gather(x))`` in one all-gather->GEMM kernel."""
+        return self._gather(x, weight, bias, False)
+
+    def gather_matmul(self, dy, weight):
+        """``(all_gather(dY) @ W, all_gather(dY))`` for ``W [K, N]``: the input gradient of a
+        row-parallel linear, gathered inside the GEMM (the gathered rows feed the weight gradient)."""
+        return self._gather(dy, weight, None, True)
+
+    def _gather(self, x, weight, bias, mn_major):
         ops = _ext.ops()
         if not self._gather_ok(x):
             from .fused import gather_rows_raw
             from ..ops import gemm
             xg = gather_rows_raw(x)
-            return gemm.linear(xg, weight, bias), xg
+            return (gemm.matmul_nn(xg, weight) if mn_major else gemm.linear(xg, weight, bias)), xg
         self.epoch_ag += 1
         e, p = self.epoch_ag, self.epoch_ag % 2
         rows = x.shape[0]
@@ -122,7 +131,7 @@ class SymmetricWorkspace:
         ops.signal_wait(self.flag_ag, self.base, self.rank, self.tp, e, False)
         xg = torch.empty(rows * self.tp, x.shape[1], dtype=x.dtype, device=x.device)
         y = ops.gather_gemm(xg, weight.contiguous(), bias, self.send[p], self.base, self.chunk_flags, e, rows,
-                            self.rank, self.tp)
+                            self.rank, self.tp, mn_major)
         return y, xg
 
     def _scatter(self, x, weight, mn_major):

@@ -48,6 +48,14 @@ def _worker(rank, world, port, out):
         d = ws.matmul_scatter(dy, w3)
         dref = fused.scatter_rows_raw(gemm.matmul_nn(dy, w3))
         errors.append(float((d.float() - dref.float()).abs().max() / dref.float().abs().max()))
+        # row-parallel input gradient: all_gather(dY) @ W with W [K, N] (MN-major B) in one kernel
+        dy_local = torch.randn(256, 384, device="cuda", dtype=torch.bfloat16)
+        w4 = (torch.randn(384, 320, device="cuda") * 0.05).to(torch.bfloat16)
+        g, dyg = ws.gather_matmul(dy_local, w4)
+        dyg_ref = fused.gather_rows_raw(dy_local)
+        errors.append(float((dyg.float() - dyg_ref.float()).abs().max()))
+        gref = gemm.matmul_nn(dyg_ref, w4)
+        errors.append(float((g.float() - gref.float()).abs().max() / gref.float().abs().max()))
         # Wan full-width RMSNorm: in-kernel exchange of the per-row sums vs NCCL all-reduce
         from cq_pretrain_b200.models.wan21 import WanRMSNorm
         norm = WanRMSNorm(384 * world, 1e-6).cuda()
