@@ -6,6 +6,11 @@ and the max over ranks (median of 20 after 5 warm-ups):
 * column-parallel all-gather -> GEMM: ``[8192/tp, 2048] x [2048, 6144/tp]`` (each rank holds
   ``8192/tp`` rows; the output is ``[8192, 6144/tp]``);
 * row-parallel GEMM -> reduce-scatter: ``[8192, 6144/tp] x [6144/tp, 2048]`` -> ``[8192/tp, 2048]``;
+* row-parallel input gradient, all-gather -> GEMM with the weight as MN-major B:
+  ``all_gather(dY [8192/tp, 2048]) @ W [2048, 6144/tp]``;
+* vocabulary-parallel LM-head cross-entropy statistics: the statistics GEMM ``[8192, 2048] x
+  [248320/tp, 2048]^T`` plus the in-kernel (max, sum exp, target) exchange vs the same GEMM plus
+  the NCCL MAX + SUM all-reduce pair;
 
 and reports each fused path against its roofline: the slower of FLOPs / measured bf16 peak and
 bytes that must cross NVLink per GPU / 770 GB/s (measured peer-copy bandwidth).
@@ -91,6 +96,46 @@ def main():
     roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
     out.append(dict(op="gemm_reducescatter", tp=tp, shape=[M, F // tp, H], fused_ms=t_fused, nccl_cublas_ms=t_nccl,
                     roofline_ms=roof, roofline_fraction=roof / t_fused, speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err2))
+    # row-parallel input gradient: all_gather(dY) @ W, W [2048, 6144/tp] read as the MN-major B operand
+    dy = torch.randn(rows, H, device="cuda", dtype=torch.bfloat16)
+    w3 = (torch.randn(H, F // tp, device="cuda") * 0.02).to(torch.bfloat16)
+    g_f, _ = ws.gather_matmul(dy, w3)
+    g_n = gemm.matmul_nn(fused.gather_rows_raw(dy), w3)
+    err3 = ((g_f.float() - g_n.float()).abs().max() / g_n.float().abs().max()).item()
+    t_fused = timed(lambda: ws.gather_matmul(dy, w3))
+    t_nccl = timed(lambda: gemm.matmul_nn(fused.gather_rows_raw(dy), w3))
+    flops = 2.0 * M * H * (F // tp)
+    nv_bytes = (tp - 1) * rows * H * 2
+    roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
+    out.append(dict(op="allgather_gemm_mn (row-parallel dX)", tp=tp, shape=[M, H, F // tp], fused_ms=t_fused,
+                    nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
+                    speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err3))
+    # vocabulary-parallel CE statistics: LM-head partials -> in-kernel exchange vs NCCL MAX + SUM
+    from ..ops import _ext
+    from ..ops.cross_entropy import _stats_combine
+    vocab = 248320
+    hid = torch.randn(M, H, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5)).to(torch.bfloat16)
+    wv = (torch.randn(vocab // tp, H, device="cuda") * 0.02).to(torch.bfloat16)
+    tg = torch.randint(0, vocab, (M,), device="cuda", generator=torch.Generator(device="cuda").manual_seed(6))
+    lo = st.tp_rank * (vocab // tp)
+    ops = _ext.ops()
+
+    def fused_ce():
+        return ws.ce_combine(*ops.ce_partials(hid, wv, tg, lo))
+
+    def nccl_ce():
+        mx, tgt, sexp = _stats_combine(*ops.ce_stats(hid, wv, tg, lo), st.tp_group)
+        return mx + torch.log(sexp), tgt
+
+    (l_f, t_f), (l_n, t_n) = fused_ce(), nccl_ce()
+    err4 = max((l_f - l_n).abs().max().item(), (t_f - t_n).abs().max().item())
+    t_fused, t_nccl = timed(fused_ce), timed(nccl_ce)
+    flops = 2.0 * M * H * (vocab // tp)
+    nv_bytes = (tp - 1) * M * 12
+    roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
+    out.append(dict(op="lm_head_ce_stats (vocab-parallel)", tp=tp, shape=[M, H, vocab // tp], fused_ms=t_fused,
+                    nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
+                    speedup_vs_nccl=t_nccl / t_fused, max_abs_err=err4))
     status = symmetric.status()
     if st.rank == 0:
         for row in out:
