@@ -335,75 +335,80 @@ __global__ void __launch_bounds__(256) qconv_bwd_hist_kernel(const float* __rest
 }
 
 // out[n, h, c, :] = normalise?(x[idx[n*64 + c], h, :]) (zero when idx < 0); r[e, h] = rsqrt norm.
+// 16 lanes per (slot, head) row, 8 elements (one 16-byte vector) per lane, two rows per warp; the
+// row reductions are width-16 shuffles, so every lane of a warp takes part (rows past the end too).
 template <int D>
 __global__ void chunk_gather_kernel(const __nv_bfloat16* __restrict__ x, const long* __restrict__ idx,
                                     __nv_bfloat16* __restrict__ out, float* __restrict__ rnorm, int slots, int H,
                                     float scale, int normalize) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= slots * H) return;
-  const int slot = warp / H, h = warp % H;
-  const int chunk = slot / 64, c = slot % 64;
-  const long e = idx[slot];
-  constexpr int PER = D / 32;  // elements per lane (4 for D=128)
-  float v[PER];
+  static_assert(D == 16 * 8, "16 lanes x 8 elements per row");
+  const long row = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 4;
+  const int sub = threadIdx.x & 15;
+  const bool valid = row < (long)slots * H;
+  const int slot = valid ? (int)(row / H) : 0, h = valid ? (int)(row % H) : 0;
+  const long e = valid ? idx[slot] : -1;
+  float v[8];
   if (e >= 0) {
-    const __nv_bfloat16* src = x + ((size_t)e * H + h) * D + lane * PER;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) v[j] = __bfloat162float(src[j]);
+    load8(x + ((size_t)e * H + h) * D + sub * 8, v);
   } else {
 #pragma unroll
-    for (int j = 0; j < PER; ++j) v[j] = 0.f;
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
   }
   if (normalize) {
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) ss += v[j] * v[j];
-    ss = warp_sum(ss);
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o, 16);
     const float r = rsqrtf(ss + 1e-6f);
 #pragma unroll
-    for (int j = 0; j < PER; ++j) v[j] *= r * scale;
-    if (lane == 0 && e >= 0) rnorm[(size_t)e * H + h] = r;
+    for (int j = 0; j < 8; ++j) v[j] *= r * scale;
+    if (sub == 0 && e >= 0) rnorm[(size_t)e * H + h] = r;
   }
-  __nv_bfloat16* dst = out + (((size_t)chunk * H + h) * 64 + c) * D + lane * PER;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) dst[j] = __float2bfloat16(v[j]);
+  if (valid) {
+    const int chunk = slot / 64, c = slot % 64;
+    store8(out + (((size_t)chunk * H + h) * 64 + c) * D + sub * 8, v);
+  }
 }
 
-// dx[e, h, :] = L2-norm backward of dy_chunks[slot(e)] (fp32) or a plain copy when !normalize.
-__device__ __forceinline__ float as_float(float v) { return v; }
-__device__ __forceinline__ float as_float(__nv_bfloat16 v) { return __bfloat162float(v); }
-
+// dx[e, h, :] = L2-norm backward of dy_chunks[slot(e)] (fp32) or a plain copy when !normalize
+// (same 16-lanes-per-row layout as the gather).
 template <int D, typename T>
 __global__ void chunk_scatter_kernel(const T* __restrict__ dyc, const long* __restrict__ slot_of,
                                      const __nv_bfloat16* __restrict__ x, const float* __restrict__ rnorm,
                                      __nv_bfloat16* __restrict__ dx, int events, int H, float scale, int normalize) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= events * H) return;
-  const int e = warp / H, h = warp % H;
-  const long slot = slot_of[e];
-  const int chunk = (int)(slot / 64), c = (int)(slot % 64);
-  constexpr int PER = D / 32;
-  const T* src = dyc + (((size_t)chunk * H + h) * 64 + c) * D + lane * PER;
-  float g[PER];
-#pragma unroll
-  for (int j = 0; j < PER; ++j) g[j] = as_float(src[j]);
-  __nv_bfloat16* dst = dx + ((size_t)e * H + h) * D + lane * PER;
-  if (normalize) {
-    const float r = rnorm[(size_t)e * H + h];
-    const __nv_bfloat16* xs = x + ((size_t)e * H + h) * D + lane * PER;
-    float xv[PER], dot = 0.f;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      xv[j] = __bfloat162float(xs[j]);
-      dot += xv[j] * g[j];
-    }
-    dot = warp_sum(dot);
-#pragma unroll
-    for (int j = 0; j < PER; ++j) dst[j] = __float2bfloat16(scale * (r * g[j] - r * r * r * xv[j] * dot));
+  static_assert(D == 16 * 8, "16 lanes x 8 elements per row");
+  const long row = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 4;
+  const int sub = threadIdx.x & 15;
+  const bool valid = row < (long)events * H;
+  const int e = valid ? (int)(row / H) : 0, h = valid ? (int)(row % H) : 0;
+  float g[8];
+  if (valid) {
+    const long slot = slot_of[e];
+    const int chunk = (int)(slot / 64), c = (int)(slot % 64);
+    load8(dyc + (((size_t)chunk * H + h) * 64 + c) * D + sub * 8, g);
   } else {
 #pragma unroll
-    for (int j = 0; j < PER; ++j) dst[j] = __float2bfloat16(g[j]);
+    for (int j = 0; j < 8; ++j) g[j] = 0.f;
   }
+  if (normalize) {
+    float xv[8], dot = 0.f;
+    float r = 0.f;
+    if (valid) {
+      r = rnorm[(size_t)e * H + h];
+      load8(x + ((size_t)e * H + h) * D + sub * 8, xv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dot += xv[j] * g[j];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, 16);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = scale * (r * g[j] - r * r * r * xv[j] * dot);
+  }
+  if (valid) store8(dx + ((size_t)e * H + h) * D + sub * 8, g);
 }
 
 int blocks_for(size_t threads, int per = 256) { return (int)((threads + per - 1) / per); }
@@ -535,12 +540,13 @@ std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunk
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 3 && x.size(2) == 128,
               "x: bf16 [E, H, 128]");
   TORCH_CHECK(idx.scalar_type() == at::kLong && idx.numel() == chunks * 64, "idx: int64 [chunks * 64]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x: 16-byte aligned base");
   const int E = x.size(0), H = x.size(1);
   const int slots = idx.numel();
   auto out = at::empty({chunks, H, 64, 128}, x.options());
   auto r = at::empty({E, H}, x.options().dtype(at::kFloat));
   if (!slots) return {out, r};
-  const size_t threads = (size_t)slots * H * 32;
+  const size_t threads = (size_t)slots * H * 16;
   chunk_gather_kernel<128><<<blocks_for(threads), 256, 0, stream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), (const long*)idx.data_ptr(), (__nv_bfloat16*)out.data_ptr(),
       r.data_ptr<float>(), slots, H, (float)scale, normalize ? 1 : 0);
@@ -555,13 +561,16 @@ at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::T
                   dyc.dim() == 4 && dyc.size(2) == 64 && dyc.size(3) == 128,
               "chunks: fp32/bf16 [Nc, H, 64, 128]");
   TORCH_CHECK(slot_of.scalar_type() == at::kLong, "slot_of: int64");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(dyc.data_ptr()) % 16 == 0 &&
+                  (!normalize || reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0),
+              "chunks / x: 16-byte aligned bases");
   if (normalize)
     TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && rnorm.scalar_type() == at::kFloat,
                 "normalize needs bf16 x and fp32 rnorm");
   const int E = slot_of.numel(), H = dyc.size(1);
   auto dx = at::empty({E, H, 128}, dyc.options().dtype(at::kBFloat16));
   if (!E) return dx;
-  const size_t threads = (size_t)E * H * 32;
+  const size_t threads = (size_t)E * H * 16;
   const long* so = (const long*)slot_of.data_ptr();
   const __nv_bfloat16* xp = normalize ? (const __nv_bfloat16*)x.data_ptr() : nullptr;
   const float* rp = normalize ? rnorm.data_ptr<float>() : nullptr;
