@@ -436,6 +436,7 @@ struct BwdTcArgs {
   const int* qb_min;   // [rows_pad / 64]
   const int* qb_max;
   const __nv_bfloat16* vsrc;  // V [keys, Hkv, D] (dK/dV at D = 256 stores it into TMEM)
+  const __nv_bfloat16* dosrc; // dO [rows, Hq, D] (dQ at D = 256 stores it into TMEM)
   __nv_bfloat16* dq;   // [rows, Hq, D]
   __nv_bfloat16* dk;   // [keys, Hkv, D]
   __nv_bfloat16* dv;
@@ -449,13 +450,19 @@ struct BwdTcArgs {
 // operand: the same shared tile that fed S).
 template <int D>
 struct DqTc {
+  // D = 256: dO lives in TMEM as the A operand of dP = dO V^T and dS is written back over the S
+  // columns as the A operand of dQ += dS K, so shared memory holds Q and two K / V stages.
+  static constexpr bool DT = D > 128;
   static constexpr int BM = 128, BN = 64, KB = D / 64;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int DS_BYTES = BM * BN * 2;
-  static constexpr int STAGES = D > 128 ? 1 : 2;
-  static constexpr int SMEM = 2 * Q_BYTES + 2 * STAGES * KV_BYTES + 2 * DS_BYTES + 1024 + 256;
-  static constexpr uint32_t DP_COL = 2 * BN, DQ_COL = 4 * BN;
+  static constexpr int STAGES = 2;
+  static constexpr int NSB = DT ? 1 : 2;               // TMEM score buffers
+  static constexpr int SMEM = (DT ? 1 : 2) * Q_BYTES + 2 * STAGES * KV_BYTES + (DT ? 0 : 2 * DS_BYTES) + 1024 + 256;
+  static constexpr uint32_t DP_COL = NSB * BN, DQ_COL = 2 * NSB * BN;
+  static constexpr uint32_t DO_COL = DQ_COL + D;       // DT only: D / 2 columns
+  static_assert(!DT || DO_COL + D / 2 <= 512, "TMEM columns");
 };
 
 template <int D>
@@ -468,11 +475,11 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;
-  uint8_t* sdo = sq + C::Q_BYTES;
-  uint8_t* sk = sdo + C::Q_BYTES;            // [ST][KV_BYTES]
+  uint8_t* sdo = sq + C::Q_BYTES;            // (not DT)
+  uint8_t* sk = sdo + (C::DT ? 0 : C::Q_BYTES);  // [ST][KV_BYTES]
   uint8_t* sv = sk + ST * C::KV_BYTES;       // [ST][KV_BYTES]
-  uint8_t* sds = sv + ST * C::KV_BYTES;      // [2][DS_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + 2 * C::DS_BYTES);
+  uint8_t* sds = sv + ST * C::KV_BYTES;      // [2][DS_BYTES] (not DT)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + (C::DT ? 0 : 2 * C::DS_BYTES));
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* k_empty = bars + 3;   // [2]
@@ -482,7 +489,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* ds_full = bars + 11;  // [2]
   uint64_t* dq_done = bars + 13;  // [2]
   uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* do_ready = bars + 16; // DT: dO stored into TMEM by the 128 softmax threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_range = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -502,6 +510,7 @@ __global__ void __launch_bounds__(192, 1)
       tc::mbar_init(&dq_done[b], 1);
     }
     tc::mbar_init(drain, 1);
+    tc::mbar_init(do_ready, 128);
     *abort_flag = 0;
     s_range[0] = INT_MAX;
     s_range[1] = 0;
@@ -534,11 +543,11 @@ __global__ void __launch_bounds__(192, 1)
       tc::prefetch_map(&map_k);
       tc::prefetch_map(&map_v);
       int armed_k[2] = {-1, -1}, armed_v[2] = {-1, -1};
-      tc::mbar_expect_tx(q_full, 2 * C::Q_BYTES);
+      tc::mbar_expect_tx(q_full, (C::DT ? 1 : 2) * C::Q_BYTES);
 #pragma unroll
       for (int i = 0; i < KB; ++i) {
         tc::tma_load_2d(sq + i * BM * 128, &map_q, q_full, h * D + i * 64, r0);
-        tc::tma_load_2d(sdo + i * BM * 128, &map_do, q_full, h * D + i * 64, r0);
+        if (!C::DT) tc::tma_load_2d(sdo + i * BM * 128, &map_do, q_full, h * D + i * 64, r0);
       }
       for (int j = 0; j < nt; ++j) {
         const int s = j % ST;
@@ -588,43 +597,68 @@ __global__ void __launch_bounds__(192, 1)
         const int s = j % ST;
         if (!tc::mbar_wait(&v_full[s], (j / ST) & 1, status, abort_flag, 43)) return false;
         tc::fence_after();
-        rows_x_tile(do_addr, v_addr + s * C::KV_BYTES, C::DP_COL + (j & 1) * BN);
+        if (C::DT) {   // dO [BM x D] in TMEM (two bf16 per column) times V_j^T
+          const uint32_t vt = v_addr + s * C::KV_BYTES;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k)
+            tc::mma_bf16_ts(tmem + C::DP_COL, tmem + C::DO_COL + k * 8,
+                            tc::smem_desc(vt + (k >> 2) * (BN * 128) + (k & 3) * 32, 16, 1024), idesc_s,
+                            k > 0 ? 1u : 0u);
+        } else {
+          rows_x_tile(do_addr, v_addr + s * C::KV_BYTES, C::DP_COL + (j & 1) * BN);
+        }
         tc::mma_commit(&v_empty[s]);
         return true;
       };
       auto issue_s = [&](int j) -> bool {
-        const int s = j % ST;
+        const int s = j % ST, b = C::DT ? 0 : (j & 1);
         if (!tc::mbar_wait(&k_full[s], (j / ST) & 1, status, abort_flag, 44)) return false;
         tc::fence_after();
-        rows_x_tile(q_addr, k_addr + s * C::KV_BYTES, (j & 1) * BN);
-        tc::mma_commit(&s_full[j & 1]);
+        rows_x_tile(q_addr, k_addr + s * C::KV_BYTES, b * BN);
+        tc::mma_commit(&s_full[b]);
         return true;
       };
       auto issue_dq = [&](int j) -> bool {
-        const int b = j & 1, s = j % ST;
-        if (!tc::mbar_wait(&ds_full[b], (j >> 1) & 1, status, abort_flag, 45)) return false;
+        const int b = C::DT ? 0 : (j & 1), s = j % ST;
+        if (!tc::mbar_wait(&ds_full[b], (C::DT ? j : j >> 1) & 1, status, abort_flag, 45)) return false;
         tc::fence_after();
         const uint32_t kt = k_addr + s * C::KV_BYTES, dst = ds_addr + b * C::DS_BYTES;
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
-          const uint64_t ad = tc::smem_desc(dst + k * 32, 16, 1024);
           const uint64_t bd = tc::smem_desc(kt + k * 2048, BN * 128, 1024);
-          tc::mma_bf16(tmem + C::DQ_COL, ad, bd, idesc_q, (j > 0 || k > 0) ? 1u : 0u);
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          if (C::DT)   // dS over the S columns, two bf16 per column
+            tc::mma_bf16_ts(tmem + C::DQ_COL, tmem + k * 8, bd, idesc_q, acc);
+          else
+            tc::mma_bf16(tmem + C::DQ_COL, tc::smem_desc(dst + k * 32, 16, 1024), bd, idesc_q, acc);
         }
         tc::mma_commit(&k_empty[s]);
         tc::mma_commit(&dq_done[b]);
         return true;
       };
       bool ok = tc::mbar_wait(q_full, 0, status, abort_flag, 46);
+      if (ok && C::DT) ok = tc::mbar_wait(do_ready, 0, status, abort_flag, 60);
       if (ok) tc::fence_after();
-      for (int j = 0; j < nt && ok; ++j) {
-        // one K/V stage: dQ_{j-1} must release K before S_j can load it
-        ok = issue_dp(j);
-        if (ok && ST == 1 && j > 0) ok = issue_dq(j - 1);
-        if (ok) ok = issue_s(j);
-        if (ok && ST == 2 && j > 0) ok = issue_dq(j - 1);
+      if (C::DT) {
+        // single score buffer: dP_{j+1} (its columns are free once the softmax released dS_j) runs
+        // while dQ_j does; S_{j+1} waits until dQ_j has read dS_j out of the S columns
+        if (ok) ok = issue_dp(0);
+        if (ok) ok = issue_s(0);
+        for (int j = 0; j < nt && ok; ++j) {
+          ok = issue_dq(j);
+          if (ok && j + 1 < nt) ok = issue_dp(j + 1);
+          if (ok && j + 1 < nt) ok = tc::mbar_wait(&dq_done[0], j & 1, status, abort_flag, 61);
+          if (ok && j + 1 < nt) ok = issue_s(j + 1);
+        }
+      } else {
+        for (int j = 0; j < nt && ok; ++j) {
+          // S_j and dP_j run while the softmax threads turn S_{j-1} into dS_{j-1}
+          ok = issue_dp(j);
+          if (ok) ok = issue_s(j);
+          if (ok && j > 0) ok = issue_dq(j - 1);
+        }
+        if (ok) issue_dq(nt - 1);
       }
-      if (ok) issue_dq(nt - 1);
       tc::mma_commit(drain);
       const unsigned long long t0 = tc::globaltimer();
       while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
@@ -643,12 +677,57 @@ __global__ void __launch_bounds__(192, 1)
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, abort_flag, code));
     };
     bool ok = true;
+    if (C::DT && nt > 0) {
+      // dO row of this thread -> TMEM columns DO_COL.. (two bf16 per column)
+      const __nv_bfloat16* drow_src = a.dosrc + ((size_t)(valid ? row : 0) * a.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 2; c += 32) {
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const uint4 u = valid ? *reinterpret_cast<const uint4*>(drow_src + 2 * (c + j)) : make_uint4(0, 0, 0, 0);
+          w[j] = __uint_as_float(u.x);
+          w[j + 1] = __uint_as_float(u.y);
+          w[j + 2] = __uint_as_float(u.z);
+          w[j + 3] = __uint_as_float(u.w);
+        }
+        tc::tmem_st32(lane_base + C::DO_COL + c, w);
+      }
+      tc::fence_before();
+      tc::mbar_arrive(do_ready);
+    }
     for (int j = 0; j < nt && ok; ++j) {
-      const int b = j & 1;
-      if (!wwait(&s_full[b], (j >> 1) & 1, 47)) { ok = false; break; }
+      const int b = C::DT ? 0 : (j & 1);
+      if (!wwait(&s_full[b], (C::DT ? j : j >> 1) & 1, 47)) { ok = false; break; }
       tc::fence_after();
-      if (j >= 2 && !wwait(&dq_done[b], ((j >> 1) + 1) & 1, 48)) { ok = false; break; }
       const int n0 = kt0 + j * BN;
+      if (C::DT) {
+        // dS back into the first BN / 2 columns of the score buffer (halves read before writing)
+        float dw[BN / 2];
+#pragma unroll
+        for (int c = 0; c < BN; c += 32) {
+          float sv[32], pv[32];
+          tc::tmem_ld32(lane_base + c, sv);
+          tc::tmem_ld32(lane_base + C::DP_COL + c, pv);
+#pragma unroll
+          for (int i2 = 0; i2 < 16; ++i2) {
+            float d2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int i = 2 * i2 + u, key = n0 + c + i;
+              const float p = (key >= rng.x && key < rng.y) ? exp2f(sv[i] * sl2 - lse2) : 0.f;
+              d2[u] = p * (pv[i] - dsum);
+            }
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(d2[0], d2[1]);
+            dw[c / 2 + i2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&v2));
+          }
+        }
+        tc::tmem_st32(lane_base, dw);
+        tc::fence_before();
+        tc::mbar_arrive(&ds_full[0]);
+        continue;
+      }
+      if (j >= 2 && !wwait(&dq_done[b], ((j >> 1) + 1) & 1, 48)) { ok = false; break; }
       uint8_t* drow = sds + b * C::DS_BYTES + rl * 128;
 #pragma unroll
       for (int c = 0; c < BN; c += 32) {
@@ -678,7 +757,8 @@ __global__ void __launch_bounds__(192, 1)
       tc::fence_before();
       tc::mbar_arrive(&ds_full[b]);
     }
-    if (ok && nt > 0 && !wwait(&dq_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, 49)) ok = false;
+    if (ok && nt > 0 && !wwait(&dq_done[C::DT ? 0 : (nt - 1) & 1], (C::DT ? nt - 1 : (nt - 1) >> 1) & 1, 49))
+      ok = false;
     if (ok) {
       tc::fence_after();
       __nv_bfloat16* dst = a.dq + ((size_t)row * a.Hq + h) * D;
@@ -1165,7 +1245,7 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
   BwdTcArgs a{schedule ? orders.data_ptr<int>() : nullptr, schedule ? orders.data_ptr<int>() + nqb128 : nullptr,
               reinterpret_cast<const float2*>(lsd.data_ptr<float>()), reinterpret_cast<const int2*>(kse.data_ptr<int>()),
               qb_min.data_ptr<int>(), qb_max.data_ptr<int>(), (const __nv_bfloat16*)v.data_ptr(),
-              (__nv_bfloat16*)dq.data_ptr(),
+              (const __nv_bfloat16*)dout.data_ptr(), (__nv_bfloat16*)dq.data_ptr(),
               (__nv_bfloat16*)dk.data_ptr(), (__nv_bfloat16*)dv.data_ptr(), rows, rows_pad, keys, Hq, Hkv,
               (float)scale};
   auto launch = [&](auto dtag) {
