@@ -13,7 +13,8 @@ long long launch_count() { return launch_counter().load(); }
 
 // rowops.cu
 std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps);
-std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd);
+std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                                     c10::optional<at::Tensor> dres);
 std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w, double eps);
 std::vector<at::Tensor> gated_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor z, at::Tensor w, at::Tensor rstd);
 std::vector<at::Tensor> ln_modulate_fwd(at::Tensor x, at::Tensor scale, at::Tensor shift, at::Tensor idx, double eps);
@@ -100,7 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "cq_pretrain_b200 sm_100a kernels";
   m.def("launch_count", &cqb::launch_count);
   m.def("rms_norm_fwd", &cqb::rms_norm_fwd);
-  m.def("rms_norm_bwd", &cqb::rms_norm_bwd);
+  m.def("rms_norm_bwd", &cqb::rms_norm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("dres") = py::none());
   m.def("gated_norm_fwd", &cqb::gated_norm_fwd);
   m.def("gated_norm_bwd", &cqb::gated_norm_bwd);
   m.def("ln_modulate_fwd", &cqb::ln_modulate_fwd);

@@ -55,11 +55,13 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const T* __restrict__ x, c
   if (lane == 0) rstd[row] = r;
 }
 
-// dx = r * (g - xhat * mean(g * xhat)), g = dy * (1 + w);  dw += dy * xhat
+// dx = r * (g - xhat * mean(g * xhat)) (+ dres), g = dy * (1 + w);  dw += dy * xhat. dres (may be
+// null) is the gradient the same x receives through a residual connection, summed in here.
 template <int NV, typename T, typename WT>
 __global__ void __launch_bounds__(512) rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x,
                                                      const WT* __restrict__ w, const float* __restrict__ rstd,
-                                                     T* __restrict__ dx, float* __restrict__ dw, int rows, int width) {
+                                                     const T* __restrict__ dres, T* __restrict__ dx,
+                                                     float* __restrict__ dw, int rows, int width) {
   extern __shared__ float smem[];  // [width]
   const int warps = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,6 +109,12 @@ __global__ void __launch_bounds__(512) rms_bwd_kernel(const T* __restrict__ dy, 
         load_vec(w + c, wv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * (1.f + wv[j]) - xv[j] * r * dot);
+        if (dres) {
+          float rv[8];
+          load_vec(dres + (size_t)row * width + c, rv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] += rv[j];
+        }
         store8(dr + c, o);
       }
     }
@@ -589,8 +597,14 @@ std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps) {
 
 static int bwd_grid(int rows) { return std::max(1, std::min(sm_count(), (rows + 15) / 16)); }
 
-std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd) {
+std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                                     c10::optional<at::Tensor> dres_opt) {
   check_rows(x);
+  at::Tensor dres;
+  if (dres_opt && dres_opt->defined()) {
+    dres = dres_opt->contiguous();
+    TORCH_CHECK(dres.sizes() == x.sizes() && dres.scalar_type() == x.scalar_type(), "dres must match x");
+  }
   const int rows = x.size(0), width = x.size(1);
   auto dx = at::empty_like(x);
   auto dw = at::zeros({width}, x.options().dtype(at::kFloat));
@@ -604,18 +618,21 @@ std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, 
                          if (wc.scalar_type() == at::kFloat)
                            rms_bwd_kernel<NV, T, float><<<grid, 512, sm, stream()>>>(
                                (const T*)dy.data_ptr(), (const T*)x.data_ptr(), wc.data_ptr<float>(),
-                               rstd.data_ptr<float>(), (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
+                               rstd.data_ptr<float>(), dres.defined() ? (const T*)dres.data_ptr() : nullptr,
+                               (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
                          else
                            rms_bwd_kernel<NV, T, T><<<grid, 512, sm, stream()>>>(
                                (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)wc.data_ptr(),
-                               rstd.data_ptr<float>(), (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
+                               rstd.data_ptr<float>(), dres.defined() ? (const T*)dres.data_ptr() : nullptr,
+                               (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
                        });
                      }) AT_DISPATCH_CASE(at::kFloat, [&] {
                        NV_DISPATCH(width, [&] {
                          auto wf = wc.to(at::kFloat);
                          rms_bwd_kernel<NV, float, float><<<grid, 512, sm, stream()>>>(
                              dy.data_ptr<float>(), x.data_ptr<float>(), wf.data_ptr<float>(), rstd.data_ptr<float>(),
-                             dx.data_ptr<float>(), dw.data_ptr<float>(), rows, width);
+                             dres.defined() ? dres.data_ptr<float>() : nullptr, dx.data_ptr<float>(),
+                             dw.data_ptr<float>(), rows, width);
                        });
                      }));
   CQB_LAUNCH_CHECK();

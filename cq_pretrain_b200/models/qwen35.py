@@ -40,6 +40,13 @@ class RMSNorm(nn.Module):
             return x * torch.rsqrt(x.square().mean(-1, keepdim=True) + self.eps) * (1 + self.weight)
         return N.rms_norm(x, self.weight, self.eps)
 
+    def residual(self, x):
+        """``(x, norm(x))`` for an ``x`` that also continues along the residual stream: on CUDA the
+        backward adds the residual gradient inside the norm's backward kernel."""
+        if x.dtype == torch.float64:
+            return x, self(x)
+        return N.rms_norm_residual(x, self.weight, self.eps)
+
 
 class MLP(nn.Module):
     def __init__(self, cfg):
@@ -221,13 +228,13 @@ class QwenBlock(nn.Module):
         self.mlp = MLP(cfg)
 
     def forward(self, hidden, rope, plan, cache=None):
-        normed = self.input_layernorm(hidden)
+        hidden, normed = self.input_layernorm.residual(hidden)
         if hasattr(self, "linear_attn"):
             mixed = self.linear_attn(normed, plan, cache)
         else:
             mixed = self.self_attn(normed, rope, plan, cache)
-        hidden = hidden + mixed
-        return hidden + self.mlp(self.post_attention_layernorm(hidden))
+        hidden, normed = self.post_attention_layernorm.residual(hidden + mixed)
+        return hidden + self.mlp(normed)
 
 
 def unfused_parameters(name, tensor, cfg):

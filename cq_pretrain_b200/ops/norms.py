@@ -38,6 +38,33 @@ def rms_norm(x, weight, eps):
     return R.rms_norm(x, weight, eps)
 
 
+class _RMSNormResidual(torch.autograd.Function):
+    """``(x, rms_norm(x))`` where ``x`` also feeds a residual connection: the backward receives the
+    residual's gradient and the norm's, and one kernel returns their sum (no separate add)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y, rstd = _ext.ops().rms_norm_fwd(x.contiguous(), weight.contiguous(), eps)
+        ctx.save_for_backward(x, weight, rstd)
+        return x.view_as(x), y
+
+    @staticmethod
+    def backward(ctx, dres, dy):
+        x, weight, rstd = ctx.saved_tensors
+        if dy is None:
+            return dres, None, None
+        dx, dw = _ext.ops().rms_norm_bwd(dy.contiguous(), x.contiguous(), weight.contiguous(), rstd,
+                                         None if dres is None else dres.contiguous())
+        return dx, dw.to(weight.dtype), None
+
+
+def rms_norm_residual(x, weight, eps):
+    """``(x, rms_norm(x))`` for a 2-D ``x`` that is also a residual input (see ``_RMSNormResidual``)."""
+    if _use_kernel(x) and x.dim() == 2 and x.shape[-1] % 8 == 0 and x.is_contiguous():
+        return _RMSNormResidual.apply(x, weight, eps)
+    return x, rms_norm(x, weight, eps)
+
+
 class _GatedNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, z, weight, eps):

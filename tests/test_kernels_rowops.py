@@ -145,3 +145,22 @@ def test_wan_rmsnorm_tp1_kernel_matches_torch():
     torch.testing.assert_close(x.grad.float(), xr.grad, atol=5e-2, rtol=3e-2)
     rel = (norm.weight.grad - wr.grad).norm() / wr.grad.norm()
     assert rel < 2e-2
+
+
+def test_rms_norm_residual_fuses_the_residual_gradient():
+    """``(x, norm(x))`` with both outputs used: the input gradient (residual + norm paths, summed in
+    the norm's backward kernel) and the weight gradient match fp32 autograd."""
+    torch.manual_seed(3)
+    x = torch.randn(1000, 2048, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(2048, device="cuda") * 0.1).requires_grad_()
+    res, y = norms.rms_norm_residual(x, w, 1e-6)
+    assert res.data_ptr() == x.data_ptr()
+    g_res, g_y = torch.randn_like(res), torch.randn_like(y)
+    (res.float() * g_res.float()).sum().add_((y.float() * g_y.float()).sum()).backward()
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    yr = R.rms_norm(xr, wr, 1e-6)
+    (xr * g_res.float()).sum().add_((yr * g_y.float()).sum()).backward()
+    torch.testing.assert_close(y.float(), yr, atol=3e-2, rtol=3e-2)
+    assert ((x.grad.float() - xr.grad).norm() / xr.grad.norm()).item() < 1e-2
+    assert ((w.grad.float() - wr.grad).norm() / wr.grad.norm()).item() < 1e-2
