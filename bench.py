@@ -2,8 +2,11 @@
 
 ``python bench.py --gpus N --steps K --warmup W`` (N > 1 under ``torch.distributed.run``). Each
 DP rank trains on one synthetic 8192-token pack per step (random-init weights, synthetic
-merger features and latents of the BASELINE config-2 shape). TP is 2 from N = 2 up
-(TP2 x DP N/2; the BASELINE target is TP2 x DP4 on 8 GPUs) and 1 on a single GPU.
+merger features and latents of the BASELINE config-2 shape). The pack is a joint T2I + I2T pack:
+two T2I documents (caption -> 512x512 image: 1024 merger tokens, 256 visual queries and a
+16x1x64x64 Wan target each), one I2T document (image -> caption) and log-uniform text documents
+filling the rest. TP is 2 from N = 2 up (TP2 x DP N/2; the BASELINE target is TP2 x DP4 on 8
+GPUs) and 1 on a single GPU.
 
 Reported: ``value`` = content tokens/s of the whole job, from CUDA-event device time of the
 compute of K steps (max over ranks); ``e2e`` = the same metric from host wall time of K calls of
@@ -11,6 +14,11 @@ the public ``Trainer.train_step`` API, each including the pinned host->device co
 and the device->host read of the loss. Working set per step (weights, optimizer state) is
 far larger than the 126 MB L2, so no explicit flush is needed between iterations.
 ``--impl reference`` reports why the reference cannot run here.
+
+Extra keys: ``gdn_fwd_bwd_ms`` (one GDN layer forward+backward at 2048 and
+8192 content tokens with 32 and 16 value heads, median of 12 after 3 warm-ups, heads split over
+TP when N > 1) and, for N > 1, ``fused_tp_check``: the maximum relative error of every in-kernel
+TP collective against NCCL on the live process group, run once before the warm-up.
 """
 
 from __future__ import annotations
@@ -21,6 +29,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 METRIC = "joint train step s & tokens/s at 8K (box, max over ranks) 1/2/4/8 B200; GDN fwd+bwd ms"
@@ -92,7 +101,9 @@ def main():
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
     parser.add_argument("--tp", type=int, default=None)
     parser.add_argument("--length", type=int, default=8192)
-    parser.add_argument("--images", type=int, default=2)
+    parser.add_argument("--images", type=int, default=3, help="visual documents per pack (all but one are T2I)")
+    parser.add_argument("--no-gdn", action="store_true", help="skip the config-3 GDN layer timings")
+    parser.add_argument("--clocks-csv", default=None, help="where to keep the nvidia-smi samples (default: a temp file)")
     parser.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid as a bench value)")
     parser.add_argument("--recompute", type=int, default=0, help="recompute backbone layers in backward")
     args = parser.parse_args()
@@ -124,15 +135,19 @@ def main():
     cfg.validate(tp)
     grid, latent = (1, 64, 64), (16, 1, 64, 64)
     host, receipt = synthetic_batch(cfg, args.length, seed=42 + st.dp_rank, kind="joint", images=args.images,
-                                    grid=grid, latent_shape=latent, understanding=False, pad_multiple=128 * tp)
+                                    grid=grid, latent_shape=latent, understanding=True, pad_multiple=128 * tp)
     host = host.pin_memory()
     trainer = Trainer(cfg, tp=tp, lr=5e-5, ema_decay=0.999)
     h2d = sum(t.numel() * t.element_size() for t in _tensors(host))
+    check = None
+    if world > 1:
+        from cq_pretrain_b200.parallel.selfcheck import fused_vs_nccl
+        check = fused_vs_nccl()
     for _ in range(args.warmup):
         trainer.train_step([(host, receipt)])
     torch.cuda.synchronize()
-    sampler = ClockSampler(f"gpurun_out/clocks_bench_n{args.gpus}.csv" if os.path.isdir("gpurun_out") else "/tmp/clocks.csv",
-                           args.gpus) if st.tp_rank == 0 and st.dp_rank == 0 else None
+    clocks_path = args.clocks_csv or os.path.join(tempfile.gettempdir(), f"cqb_clocks_n{args.gpus}_{os.getpid()}.csv")
+    sampler = ClockSampler(clocks_path, args.gpus) if st.tp_rank == 0 and st.dp_rank == 0 else None
     if sampler:
         sampler.start()
     launches0 = _ext.launches()
@@ -156,6 +171,16 @@ def main():
     compute_ms, wall_ms = timing.tolist()
     tokens_per_step = args.length * st.dp
     ms_per_step = compute_ms / args.steps
+    pack = _composition(host)
+    del trainer
+    torch.cuda.empty_cache()
+    gdn = None
+    if not args.no_gdn and not args.layers:
+        from cq_pretrain_b200.benchmarks import gdn as gdn_bench
+        gdn = {f"{r['content_tokens']}_v{r['value_heads']}": r["median_ms"]
+               for heads in (32, 16) for r in gdn_bench.measure([2048, 8192], heads)}
+        gdn["tp"] = tp
+        gdn["reference_910b_ms"] = {"2048": 10.46, "8192": 38.60}
     value = tokens_per_step / (ms_per_step / 1000.0)
     e2e = tokens_per_step / (wall_ms / args.steps / 1000.0)
     if rank == 0:
@@ -167,7 +192,7 @@ def main():
             "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) merger features and latents)",
             "config": {"model": "Qwen3.5-2B-hybrid(24L: 18 GDN + 6 gated-attn) + Wan2.1-T2V-1.3B",
                        "global_batch": st.dp, "seq_len": args.length, "parallelism": f"tp{tp}xdp{st.dp}",
-                       "images_per_pack": args.images, "merger_tokens_per_image": 1024,
+                       "pack": pack, "images_per_pack": args.images, "merger_tokens_per_image": 1024,
                        "visual_queries_per_image": 256, "latent": "16x1x64x64",
                        "rows_per_pack": int(host.mainline.rows), "gdn_events": host.mainline.delta.events,
                        "l2": "working set (weights + optimizer state) >> 126 MB L2; no flush",
@@ -177,14 +202,26 @@ def main():
             "gpu_launches": int(launches),
             "clocks": clocks,
             "loss": metrics["loss"],
+            "gdn_fwd_bwd_ms": gdn,
+            "fused_tp_check": check,
             "baseline": {"tokens_per_s_per_gpu": round(BASELINE_TOKENS_PER_GPU, 1),
                          "source": "reference 1.946 s joint 8K step on 16x 910B TP2xDP8, global batch 8"},
         }
         print(json.dumps(line), flush=True)
-    del trainer
     if world > 1:
         dist.barrier()
         ps.destroy()
+
+
+def _composition(batch):
+    """Document mix of one pack: T2I targets, I2T images, text documents, rows and queries."""
+    gen = batch.generation
+    targets = int(batch.generation_image_count)
+    images = int(batch.image_indices.shape[0])
+    return dict(t2i_targets=targets, i2t_images=images - targets,
+                dit_tokens=int(sum(gen.lengths)) if gen is not None else 0,
+                rows=int(batch.mainline.rows), queries=int(batch.mainline.queries),
+                text_targets=int(batch.text_indices.numel()))
 
 
 def _tensors(batch):

@@ -8,6 +8,10 @@ and the max over ranks (median of 20 after 5 warm-ups):
 * row-parallel GEMM -> reduce-scatter: ``[8192, 6144/tp] x [6144/tp, 2048]`` -> ``[8192/tp, 2048]``;
 * row-parallel input gradient, all-gather -> GEMM with the weight as MN-major B:
   ``all_gather(dY [8192/tp, 2048]) @ W [2048, 6144/tp]``;
+* the input gradient of two column-parallel projections of one gathered input (Qwen's q/gate
+  over all rows plus kv over the content rows) as one GEMM -> reduce-scatter;
+* Wan's QKV projection ``[32760, 1536] x [1536, 3 x 1536]`` with the full-width Q/K RMSNorm whose
+  per-row sums of squares are exchanged across ranks in-kernel;
 * vocabulary-parallel LM-head cross-entropy statistics: the statistics GEMM ``[8192, 2048] x
   [248320/tp, 2048]^T`` plus the in-kernel (max, sum exp, target) exchange vs the same GEMM plus
   the NCCL MAX + SUM all-reduce pair;
@@ -38,19 +42,23 @@ def bf16_peak_tflops():
         return 1590.0
 
 
-def timed(fn, iters=20, warmup=5):
+def timed(fn, iters=20, warmup=5, reps=5):
+    """Per-call device time: ``iters`` calls back to back between two CUDA events (so the host's
+    launch skew between ranks after the barrier is spread over the loop, as in a training step),
+    median over ``reps`` loops, max over ranks."""
     for _ in range(warmup):
         fn()
     times = []
-    for _ in range(iters):
+    for _ in range(reps):
         dist.barrier()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        for _ in range(iters):
+            fn()
         b.record()
         torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
+        times.append(a.elapsed_time(b) / iters)
     t = torch.tensor([statistics.median(times)], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t)
@@ -110,6 +118,64 @@ def main():
     out.append(dict(op="allgather_gemm_mn (row-parallel dX)", tp=tp, shape=[M, H, F // tp], fused_ms=t_fused,
                     nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
                     speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err3))
+    # input gradient of two column-parallel projections of one gathered input (Qwen q/gate + kv over
+    # the content rows): reduce_scatter(dY1 W1 + pad(dY2) W2) in one kernel
+    n1, n2, rows2 = 2 * 8 * 256 // tp, 2 * 2 * 256 // tp, M // 2
+    dq = torch.randn(M, n1, device="cuda", dtype=torch.bfloat16)
+    dkv = torch.randn(rows2, n2, device="cuda", dtype=torch.bfloat16)
+    wq = (torch.randn(n1, H, device="cuda") * 0.02).to(torch.bfloat16)
+    wkv = (torch.randn(n2, H, device="cuda") * 0.02).to(torch.bfloat16)
+
+    def pair_nccl():
+        full = gemm.matmul_nn(dq, wq)
+        full[:rows2] += gemm.matmul_nn(dkv, wkv)
+        return fused.scatter_rows_raw(full)
+
+    p_f, p_n = ws.matmul_scatter(dq, wq, dkv, wkv), pair_nccl()
+    err5 = ((p_f.float() - p_n.float()).abs().max() / p_n.float().abs().max()).item()
+    t_fused, t_nccl = timed(lambda: ws.matmul_scatter(dq, wq, dkv, wkv)), timed(pair_nccl)
+    flops = 2.0 * H * (M * n1 + rows2 * n2)
+    nv_bytes = (tp - 1) * rows * H * 2
+    roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
+    out.append(dict(op="pair_input_grad_reducescatter (q/gate + kv)", tp=tp, shape=[M, n1, rows2, n2, H],
+                    fused_ms=t_fused, nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
+                    speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err5))
+    # Wan QKV projection with the cross-rank Q/K RMSNorm: [32760, 1536] x [1536, 3 x 1536] (rows padded
+    # to 128 x tp), q and kv sharing one in-kernel all-gather, then the full-width RMSNorm of q and k
+    # with the per-row sums exchanged in-kernel; baseline: NCCL all-gather + GEMMs + NCCL all-reduce.
+    from ..models.wan21 import Attention
+    from ..config import qwen35_2b_wan
+    wan_rows = -(-32760 // (128 * tp)) * 128 * tp
+    attn = Attention(qwen35_2b_wan()).cuda().to(torch.bfloat16)
+    xw = torch.randn(wan_rows // tp, 1536, device="cuda", dtype=torch.bfloat16)
+
+    def wan_fused():
+        from ..parallel import layers as PL
+        q, kv = PL.column_pair(xw, attn.q, attn.kv)
+        k, v = kv.chunk(2, -1)
+        return attn.norm_q(q), attn.norm_k(k), v
+
+    def wan_nccl():
+        xg_ = fused.gather_rows_raw(xw)
+        q = gemm.linear(xg_, attn.q.weight, attn.q.bias)
+        k, v = gemm.linear(xg_, attn.kv.weight, attn.kv.bias).chunk(2, -1)
+        out_ = []
+        for t, norm in ((q, attn.norm_q), (k, attn.norm_k)):
+            sq = t.float().square().sum(-1, keepdim=True)
+            dist.all_reduce(sq, group=st.tp_group)
+            out_.append((t.float() * torch.rsqrt(sq / 1536 + 1e-6)).to(t.dtype) * norm.weight.to(t.dtype))
+        return out_[0], out_[1], v
+
+    with torch.no_grad():
+        wf, wn = wan_fused(), wan_nccl()
+        err6 = max(((a.float() - b.float()).abs().max() / b.float().abs().max()).item() for a, b in zip(wf, wn))
+        t_fused, t_nccl = timed(wan_fused), timed(wan_nccl)
+    flops = 2.0 * wan_rows * 1536 * (3 * 1536 // tp)
+    nv_bytes = (tp - 1) * (wan_rows // tp) * 1536 * 2 + 2 * (tp - 1) * wan_rows * 4
+    roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
+    out.append(dict(op="wan_qkv_gemm + cross-rank q/k rmsnorm", tp=tp, shape=[wan_rows, 1536, 3 * 1536 // tp],
+                    fused_ms=t_fused, nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
+                    speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err6))
     # vocabulary-parallel CE statistics: LM-head partials -> in-kernel exchange vs NCCL MAX + SUM
     from ..ops import _ext
     from ..ops.cross_entropy import _stats_combine

@@ -39,7 +39,8 @@ void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_o
                   int64_t src_rank, int64_t tp);
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
                        int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
-                       int64_t tp, bool mn_major);
+                       int64_t tp, bool mn_major, c10::optional<at::Tensor> x_local, int64_t send_mine,
+                       c10::optional<at::Tensor> peer_ready, int64_t own_done);
 // comm.cu
 std::vector<at::Tensor> symm_alloc(int64_t bytes);
 int64_t symm_open(at::Tensor handle_bytes);
@@ -47,6 +48,10 @@ void symm_close(int64_t ptr);
 void symm_free(int64_t ptr);
 at::Tensor symm_view(int64_t base, int64_t offset, std::vector<int64_t> shape, at::ScalarType dtype);
 void signal_wait(at::Tensor peer_flag_ptrs, int64_t my_flags, int64_t rank, int64_t tp, int64_t epoch, bool wait);
+at::Tensor gemm_scatter_reduce(at::Tensor x, at::Tensor w, bool w_mn_major, c10::optional<at::Tensor> x2,
+                               c10::optional<at::Tensor> w2, c10::optional<at::Tensor> bias, at::Tensor peer_recv,
+                               int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t flag_slots,
+                               int64_t epoch, int64_t rows_per_rank, int64_t src_rank, int64_t tp);
 at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp, int64_t rows, int64_t cols);
 int comm_status_read(bool reset);
 std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at::Tensor peer_recv, int64_t my_recv,
@@ -123,13 +128,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_scatter", &cqb::gemm_scatter);
   m.def("gather_gemm", &cqb::gather_gemm, py::arg("a_local"), py::arg("w"), py::arg("bias"), py::arg("peer_in_ptrs"),
         py::arg("ready_ptr"), py::arg("chunk_flags"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),
-        py::arg("tp"), py::arg("mn_major") = false);
+        py::arg("tp"), py::arg("mn_major") = false, py::arg("x_local") = py::none(), py::arg("send_mine") = 0,
+        py::arg("peer_ready") = py::none(), py::arg("own_done") = 0);
   m.def("symm_alloc", &cqb::symm_alloc);
   m.def("symm_open", &cqb::symm_open);
   m.def("symm_close", &cqb::symm_close);
   m.def("symm_free", &cqb::symm_free);
   m.def("symm_view", &cqb::symm_view);
   m.def("signal_wait", &cqb::signal_wait);
+  m.def("gemm_scatter_reduce", &cqb::gemm_scatter_reduce, py::arg("x"), py::arg("w"), py::arg("w_mn_major"),
+        py::arg("x2"), py::arg("w2"), py::arg("bias"), py::arg("peer_recv"), py::arg("my_recv"), py::arg("peer_flags"),
+        py::arg("my_flags"), py::arg("flag_slots"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),
+        py::arg("tp"));
   m.def("rs_reduce", &cqb::rs_reduce);
   m.def("comm_status_read", &cqb::comm_status_read, py::arg("reset") = false);
   m.def("tp_rms_fwd", &cqb::tp_rms_fwd);

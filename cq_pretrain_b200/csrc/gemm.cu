@@ -16,6 +16,14 @@
 //    tile's 256 logits into an online (max, sum exp) pair and picks out its target logit, and
 //    writes one partial per (row, column tile) (the LM-head forward never writes logits);
 //    4 = cross-entropy gradient: (exp(logit - lse) - [col == target]) * dloss as bf16 TMA stores;
+//    5 = GEMM -> reduce-scatter in one kernel: tiles of rows owned by another TP rank are
+//    stored (bf16) into that rank's receive slab and published with a per-(tile, source, warp)
+//    epoch stamp; tiles of this rank's own rows come last in the tile order, and their epilogue
+//    waits for the peers' stamps, then adds the peers' partials to its own fp32 accumulator
+//    (still in TMEM) and the bias, and TMA-stores the reduced rows;
+//  * a second operand pair (A2, B2, contraction K2) may follow the first in the k loop, so
+//    D = A B^T + A2 B2^T runs as one accumulation (e.g. dX = dY1 W1 + dY2 W2 of two projections
+//    of one gathered input); rows of A2 past its own extent read as zero;
 //  * GATHER: two extra warps pull the A row blocks of every TP rank (peer memory, plain loads)
 //    into this GPU's gather buffer and publish a flag per 128-row block; the TMA producer waits
 //    for a block's flag before loading it, and tiles of this rank's own rows go first
@@ -26,6 +34,7 @@
 #include "common.cuh"
 #include "tcgen05.cuh"
 
+#include <cstdlib>
 #include <mutex>
 
 namespace cqb {
@@ -38,6 +47,7 @@ constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTE
 constexpr int EPI_BOX = 32;                                   // 32 x 32 output box per warp store
 constexpr int STAGING_BYTES = 4 /*warps*/ * 2 /*buffers*/ * EPI_BOX * EPI_BOX * 4;  // sized for fp32
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int RS_MAX_TP = 8;    // flag slots per tile: [tile][source < RS_MAX_TP][epilogue warp < 4]
 
 int* status_word() {
   static int* word = [] {
@@ -62,9 +72,18 @@ struct GemmArgs {
   const __nv_bfloat16* const* peer_in;
   __nv_bfloat16* a_local;
   const long long* ready;     // this rank's flag area: ready[s] >= epoch when rank s published
+  // GATHER with in-kernel staging: this rank's rows are read from x_local, written to both the
+  // gather buffer and send_mine (the symmetric send buffer the peers read), and once every own
+  // sub-chunk is staged (own_done counts them) epoch is published into slot src_rank of every
+  // peer's flag area (peer_ready[p]).
+  const __nv_bfloat16* x_local;
+  __nv_bfloat16* send_mine;
+  long long* const* peer_ready;
+  unsigned* own_done;
   long long* chunk_flags;     // [M / 16] per-sub-chunk publication flags (local)
   long long epoch;
   int group_m;                // tile raster: groups of group_m row blocks sweep all column blocks
+  int split_k;                // EPI 1 only: CTAs take balanced ranges of (tile, k block) units
   // EPI 3/4 (cross-entropy over a vocabulary shard [lo, lo + N)):
   const long long* targets;   // [M] global token ids
   long long lo;
@@ -72,6 +91,13 @@ struct GemmArgs {
   float* ce_target;           // EPI 3: [M] target logit (rows whose target is in this shard)
   const float* ce_lse;        // EPI 4: [M] log-sum-exp over the full vocabulary
   const float* ce_scale;      // EPI 4: device scalar dloss / rows
+  // Second operand pair (K2 > 0): k blocks [kb(K), kb(K) + kb(K2)) read map_a2 / map_b2.
+  int K2;
+  // EPI 5: receive slabs [tp][rows_per_rank][N] bf16 of this call's parity (peer bases and ours)
+  // and the per-tile stamp areas [tiles][RS_MAX_TP][4] int64 (peer bases and ours).
+  const __nv_bfloat16* my_recv;
+  long long* const* rs_flags_peer;
+  const long long* rs_flags_mine;
 };
 
 __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
@@ -86,6 +112,14 @@ __device__ __forceinline__ long long ld_acquire_gpu(const long long* p) {
 }
 __device__ __forceinline__ void st_release_gpu(long long* p, long long v) {
   asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_cg_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
 }
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -123,10 +157,44 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   n0 = (r / rows) * BN;
 }
 
+// Work of one CTA: whole tiles round-robin over the grid, or (split_k, epilogue 1 only) one
+// contiguous range of the tiles x k-blocks units, cut into per-tile segments. Partial sums of a
+// tile from several CTAs meet in the reduce-add epilogue, so the ranges need no fix-up pass and
+// every CTA gets the same amount of MMA work whatever the tile count.
+struct WorkIter {
+  long long u, end;
+  int kblocks, t, stride, tiles;
+  bool split;
+  __device__ WorkIter(bool split_k, int tiles_, int kblocks_) : kblocks(kblocks_), tiles(tiles_), split(split_k) {
+    const long long w = (long long)tiles_ * kblocks_;
+    u = w * blockIdx.x / gridDim.x;
+    end = w * (blockIdx.x + 1) / gridDim.x;
+    t = blockIdx.x;
+    stride = gridDim.x;
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (!split) {
+      if (t >= tiles) return false;
+      tile = t;
+      kb0 = 0;
+      kb1 = kblocks;
+      t += stride;
+      return true;
+    }
+    if (u >= end) return false;
+    tile = (int)(u / kblocks);
+    kb0 = (int)(u % kblocks);
+    kb1 = (int)min((long long)kblocks, kb0 + (end - u));
+    u += kb1 - kb0;
+    return true;
+  }
+};
+
 template <bool A_MN, bool B_MN, int EPI, bool GATHER>
 __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const __grid_constant__ CUtensorMap map_out, GemmArgs args, int* status) {
+                const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_a2,
+                const __grid_constant__ CUtensorMap map_b2, GemmArgs args, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
@@ -141,8 +209,11 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_m = (args.M + BM - 1) / BM, tiles_n = (args.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
-  const int kblocks = (args.K + BK - 1) / BK;
-  const int rotate = GATHER ? (args.src_rank * args.rows_per_rank) / BM : 0;
+  const int kb1 = (args.K + BK - 1) / BK;
+  const int kblocks = kb1 + (args.K2 > 0 ? (args.K2 + BK - 1) / BK : 0);
+  // GATHER: this rank's rows first; EPI 5: the next rank's rows first and this rank's rows last.
+  const int rotate = GATHER ? (args.src_rank * args.rows_per_rank) / BM
+                            : (EPI == 5 ? (((args.src_rank + 1) % args.tp) * args.rows_per_rank) / BM : 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -166,13 +237,19 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     if (lane == 0) {
       tc::prefetch_map(&map_a);
       tc::prefetch_map(&map_b);
+      if (args.K2 > 0) {
+        tc::prefetch_map(&map_a2);
+        tc::prefetch_map(&map_b2);
+      }
       int stage = 0;
       uint32_t phase = 0;
       int armed[STAGES];  // parity of the last armed phase of each stage, -1 = never armed
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      WorkIter work(EPI == 1 && args.split_k, tiles, kblocks);
+      int t, kb0, kb1;
+      while (ok && work.next(t, kb0, kb1)) {
         int m0, n0;
         tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
         if (GATHER) {
@@ -182,7 +259,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           if (!ok) break;
           fence_proxy_async_global();
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, status, abort_flag, 1)) {
             ok = false;
             break;
@@ -190,18 +267,21 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           tc::mbar_expect_tx(&full[stage], STAGE_BYTES);
-          const int k0 = kb * BK;
+          const bool second = kb >= kb1;
+          const CUtensorMap* ma = second ? &map_a2 : &map_a;
+          const CUtensorMap* mb = second ? &map_b2 : &map_b;
+          const int k0 = (second ? kb - kb1 : kb) * BK;
           if (A_MN) {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sa + j * (BK * 128), &map_a, &full[stage], m0 + j * 64, k0);
+            for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sa + j * (BK * 128), ma, &full[stage], m0 + j * 64, k0);
           } else {
-            tc::tma_load_2d(sa, &map_a, &full[stage], k0, m0);
+            tc::tma_load_2d(sa, ma, &full[stage], k0, m0);
           }
           if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sb + j * (BK * 128), &map_b, &full[stage], n0 + j * 64, k0);
+            for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sb + j * (BK * 128), mb, &full[stage], n0 + j * 64, k0);
           } else {
-            tc::tma_load_2d(sb, &map_b, &full[stage], k0, n0);
+            tc::tma_load_2d(sb, mb, &full[stage], k0, n0);
           }
           armed[stage] = (int)phase;
           if (++stage == STAGES) {
@@ -227,13 +307,15 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
+      WorkIter work(EPI == 1 && args.split_k, tiles, kblocks);
+      int t, kb0, kb1;
+      for (; ok && work.next(t, kb0, kb1); ++local) {
         const int buf = local & 1;
         const uint32_t use = (local >> 1) & 1;
         if (!tc::mbar_wait(&tempty[buf], use ^ 1, status, abort_flag, 2)) break;
         tc::fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, status, abort_flag, 3)) {
             ok = false;
             break;
@@ -245,7 +327,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? tc::smem_desc(sa + k * 2048, BK * 128, 1024) : tc::smem_desc(sa + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? tc::smem_desc(sb + k * 2048, BK * 128, 1024) : tc::smem_desc(sb + k * 32, 16, 1024);
-            tc::mma_bf16(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc::mma_bf16(d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           tc::mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -269,7 +351,9 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     uint8_t* my_stage = staging + quarter * 2 * EPI_BOX * EPI_BOX * 4;
     int local = 0, chunk = 0;
     if (lane == 0 && EPI != 2 && EPI != 3) tc::prefetch_map(&map_out);
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+    WorkIter work(EPI == 1 && args.split_k, tiles, kblocks);
+    int t, kb0, kb1;
+    for (; work.next(t, kb0, kb1); ++local) {
       const int buf = local & 1;
       const uint32_t use = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[buf], use, status, abort_flag, 4)) break;
@@ -316,6 +400,21 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         if (lane == 0) tc::mbar_arrive(&tempty[buf]);
         continue;
       }
+      // EPI 5: tiles of this rank's rows reduce the peers' partials; other tiles go to their owner.
+      const int owner = (EPI == 5 || EPI == 2) ? m0 / args.rows_per_rank : 0;
+      const bool own = EPI == 5 && owner == args.src_rank;
+      const int owner_tile = EPI == 5 ? ((m0 - owner * args.rows_per_rank) / BM) * tiles_n + n0 / BN : 0;
+      if (own) {
+        bool ok = true;
+        if (lane == 0)
+          for (int s = 0; s < args.tp && ok; ++s)
+            if (s != args.src_rank)
+              ok = wait_flag<true>(args.rs_flags_mine + ((size_t)owner_tile * RS_MAX_TP + s) * 4 + quarter,
+                                   args.epoch, status, abort_flag, 7);
+        ok = __shfl_sync(0xffffffffu, ok, 0) != 0;  // the warp barrier orders lane 0's acquire before all lanes' reads
+        if (!ok) break;
+      }
+      const __nv_bfloat16* bias = (EPI == 5 && !own) ? nullptr : args.bias;
       float ce_l = 0.f, ce_f = 0.f;
       long long ce_t = -1;
       if (EPI == 4) {
@@ -333,6 +432,28 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         const int col0 = n0 + c;
         if (col0 >= args.N) continue;  // whole box outside the matrix (uniform across the warp)
         uint8_t* box = my_stage + (chunk & 1) * EPI_BOX * EPI_BOX * 4;
+        if (own) {
+          // peers' bf16 partials of this thread's row (local memory, written by the peers' kernels)
+          const int lrow = m0 - args.src_rank * args.rows_per_rank + quarter * 32 + lane;
+          const int valid = min(32, args.N - col0);
+          for (int s = 0; s < args.tp; ++s) {
+            if (s == args.src_rank) continue;
+            const __nv_bfloat16* src = args.my_recv + ((size_t)s * args.rows_per_rank + lrow) * args.N + col0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              if (j < valid) {
+                const uint4 u = ld_cg_u4(src + j);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float2 f = __bfloat1622float2(h[q]);
+                  v[j + 2 * q] += f.x;
+                  v[j + 2 * q + 1] += f.y;
+                }
+              }
+            }
+          }
+        }
         if (EPI != 2) {
           if (lane == 0) tc::bulk_wait_read1();  // the store that last used this buffer finished reading
           __syncwarp();
@@ -347,14 +468,14 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
               o[q] = (__expf(v[j + q] - ce_l) - (col0 + j + q == ce_t ? 1.f : 0.f)) * ce_f;
             store8(row + j, o);
           }
-        } else if (EPI == 0 || EPI == 2) {
+        } else if (EPI == 0 || EPI == 2 || EPI == 5) {
           __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(box) + lane * EPI_BOX;
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             float o[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              o[q] = v[j + q] + ((args.bias && col0 + j + q < args.N) ? __bfloat162float(args.bias[col0 + j + q]) : 0.f);
+              o[q] = v[j + q] + ((bias && col0 + j + q < args.N) ? __bfloat162float(bias[col0 + j + q]) : 0.f);
             store8(row + j, o);
           }
         } else {
@@ -363,9 +484,8 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           for (int j = 0; j < 32; j += 4)
             *reinterpret_cast<float4*>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         }
-        if (EPI == 2) {
+        if (EPI == 2 || (EPI == 5 && !own)) {
           __syncwarp();
-          const int owner = m0 / args.rows_per_rank;
           const int lrow0 = args.src_rank * args.rows_per_rank + (m0 - owner * args.rows_per_rank) + quarter * 32;
           __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.peer_out[owner]) + (size_t)lrow0 * args.N + col0;
           const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(box);
@@ -382,13 +502,24 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           tc::fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            if (EPI == 0 || EPI == 4)
+            if (EPI == 5)
+              tc::tma_store_2d(&map_out, box, col0, m0 - args.src_rank * args.rows_per_rank + quarter * 32);
+            else if (EPI == 0 || EPI == 4)
               tc::tma_store_2d(&map_out, box, col0, m0 + quarter * 32);
             else
               tc::tma_reduce_add_2d(&map_out, box, col0, m0 + quarter * 32);
             tc::bulk_commit();
           }
         }
+      }
+      if (EPI == 5 && !own) {
+        // publish this warp's 32 rows of the tile to the owner: system-scope fence by every lane,
+        // then one release store of the epoch into the (tile, source, warp) slot
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0)
+          st_release_sys(args.rs_flags_peer[owner] + ((size_t)owner_tile * RS_MAX_TP + args.src_rank) * 4 + quarter,
+                         args.epoch);
       }
       tc::fence_before();
       __syncwarp();
@@ -408,12 +539,14 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       const int row0 = sub * GATHER_SUB;
       const int s = row0 / args.rows_per_rank;
       const int lrow = row0 - s * args.rows_per_rank;
+      const bool stage = s == args.src_rank && args.x_local != nullptr;
       bool ok = true;
       if (ct == 0 && s != args.src_rank) ok = wait_flag<true>(args.ready + s, args.epoch, status, abort_flag, 6);
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (*abort_flag || !ok) break;
-      const uint4* src = reinterpret_cast<const uint4*>(args.peer_in[s] + (size_t)lrow * args.K);
+      const uint4* src = reinterpret_cast<const uint4*>((stage ? args.x_local : args.peer_in[s]) + (size_t)lrow * args.K);
       uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)row0 * args.K);
+      uint4* dst2 = stage ? reinterpret_cast<uint4*>(args.send_mine + (size_t)lrow * args.K) : nullptr;
       const int vecs = GATHER_SUB * args.K / 8;
       // 16 independent 16-byte loads in flight per thread: NVLink latency is hidden by
       // memory-level parallelism rather than by occupancy.
@@ -425,12 +558,32 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         for (int u = 0; u < UNROLL; ++u) r[u] = __ldcg(src + v + 64 * u);
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) dst[v + 64 * u] = r[u];
+        if (stage) {
+#pragma unroll
+          for (int u = 0; u < UNROLL; ++u) dst2[v + 64 * u] = r[u];
+        }
       }
-      for (; v < vecs; v += 64) dst[v] = __ldcg(src + v);
+      for (; v < vecs; v += 64) {
+        const uint4 r = __ldcg(src + v);
+        dst[v] = r;
+        if (stage) dst2[v] = r;
+      }
       fence_proxy_async_global();
-      __threadfence();
+      if (stage) __threadfence_system(); else __threadfence();
       asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (ct == 0) st_release_gpu(args.chunk_flags + sub, args.epoch);
+      if (ct == 0) {
+        st_release_gpu(args.chunk_flags + sub, args.epoch);
+        if (stage) {
+          // the last own sub-chunk staged (over all CTAs) publishes this rank's shard to the peers
+          const unsigned own_subs = (unsigned)(args.rows_per_rank / GATHER_SUB);
+          if (atomicAdd(args.own_done, 1u) + 1u == own_subs) {
+            atomicExch(args.own_done, 0u);
+            __threadfence_system();
+            for (int p = 0; p < args.tp; ++p)
+              if (p != args.src_rank) st_release_sys(args.peer_ready[p] + args.src_rank, args.epoch);
+          }
+        }
+      }
     }
   }
   __syncthreads();
@@ -503,7 +656,8 @@ CUtensorMap make_out_map(const at::Tensor& t) {
 }
 
 template <bool A_MN, bool B_MN, int EPI, bool GATHER>
-void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmArgs args) {
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmArgs args,
+            const CUtensorMap* ma2 = nullptr, const CUtensorMap* mb2 = nullptr) {
   auto kernel = gemm_kernel<A_MN, B_MN, EPI, GATHER>;
   static std::once_flag once;
   std::call_once(once, [&] {
@@ -517,9 +671,22 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
   // All-gather: tiles follow the ranks' row ranges (own rows first), so the first tiles need no
   // peer data and the copy of the other ranks' rows overlaps them.
   if (GATHER) args.group_m = std::min(args.group_m, std::max(1, args.rows_per_rank / BM));
+  // GEMM -> reduce-scatter: groups must not straddle two owners, so that this rank's own row
+  // blocks (rotated to the end of the order) form the last groups.
+  if (EPI == 5) {
+    const int blocks = args.rows_per_rank / BM;
+    int g = std::min(args.group_m, blocks);
+    while (blocks % g) --g;
+    args.group_m = g;
+  }
+  if (args.K2 > 0) TORCH_CHECK(ma2 != nullptr && mb2 != nullptr, "second operand pair without tensor maps");
   // GATHER needs every CTA resident (copy blocks are handed out by CTA index): one per SM.
-  const int grid = std::max(1, std::min(tiles, sm_count()));
-  kernel<<<grid, GATHER ? 256 : 192, SMEM_BYTES, stream()>>>(ma, mb, mo, args, status_word());
+  // Split-K (reduce-add epilogue): every SM takes an equal share of the tiles x k-blocks units.
+  const int kblocks = (int)((args.K + BK - 1) / BK);
+  if (EPI == 1 && args.split_k) args.split_k = (long long)tiles * kblocks >= 2LL * sm_count() ? 1 : 0;
+  const int grid = (EPI == 1 && args.split_k) ? sm_count() : std::max(1, std::min(tiles, sm_count()));
+  kernel<<<grid, GATHER ? 256 : 192, SMEM_BYTES, stream()>>>(ma, mb, mo, ma2 ? *ma2 : ma, mb2 ? *mb2 : mb, args,
+                                                              status_word());
   CQB_LAUNCH_CHECK();
   count_launch();
 }
@@ -571,6 +738,17 @@ at::Tensor gemm_nn(at::Tensor a, at::Tensor b) {
   return y;
 }
 
+// Split-K for the reduce-add weight-gradient GEMM unless CQB_DETERMINISTIC=1: the fp32 partial sums
+// of a tile then reach main_grad in an order that varies from run to run (values differ in the
+// last bits); deterministic mode keeps one CTA per tile.
+bool split_k_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("CQB_DETERMINISTIC");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
 // out[N,K] (fp32) += a[M,N]^T b[M,K]   (contraction over rows: both operands MN-major)
 void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out) {
   const int64_t M = a.size(0), N = a.size(1), K = b.size(1);
@@ -580,7 +758,9 @@ void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out) {
   check_dims(N, K, M, /*k_inner=*/false);
   auto ma = make_map(a, BK);
   auto mb = make_map(b, BK);
-  launch<true, true, 1, false>(ma, mb, make_out_map(out.view({N, K})), plain_args(N, K, M, out.data_ptr(), K, nullptr));
+  auto args = plain_args(N, K, M, out.data_ptr(), K, nullptr);
+  args.split_k = split_k_enabled() ? 1 : 0;
+  launch<true, true, 1, false>(ma, mb, make_out_map(out.view({N, K})), args);
 }
 
 // GEMM -> reduce-scatter, communication half: every tile of x[M,K] w^T (w [N,K]) or x w
@@ -604,11 +784,71 @@ void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_o
     launch<false, false, 2, false>(ma, mb, ma, args);
 }
 
+// GEMM -> reduce-scatter in one kernel (epilogue 5). Returns this rank's reduced rows
+// out[rows_per_rank, N] = sum over ranks of (x w^T + x2 w2^T)[own rows] + bias, where the rank
+// order of x's rows is [rank 0 rows, rank 1 rows, ...]. w is [N, K] (or [K, N] with w_mn_major);
+// x2 / w2 (optional) form a second operand pair with the same layouts, contraction K2, and x2 may
+// have fewer rows than x (missing rows count as zero). peer_recv: int64 [tp] receive-slab bases
+// ([tp][rows_per_rank][N] bf16, this call's parity) of every rank; my_recv: ours. peer_flags:
+// int64 [tp] stamp-area bases; my_flags: ours (tiles * 8 * 4 int64 slots).
+at::Tensor gemm_scatter_reduce(at::Tensor x, at::Tensor w, bool w_mn_major, c10::optional<at::Tensor> x2,
+                               c10::optional<at::Tensor> w2, c10::optional<at::Tensor> bias, at::Tensor peer_recv,
+                               int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t flag_slots,
+                               int64_t epoch, int64_t rows_per_rank, int64_t src_rank, int64_t tp) {
+  const int64_t M = x.size(0), K = x.size(1), N = w_mn_major ? w.size(1) : w.size(0);
+  TORCH_CHECK(w_mn_major ? w.size(0) == K : w.size(1) == K, "gemm_scatter_reduce: inner dims differ");
+  check_dims(M, N, K);
+  TORCH_CHECK(tp >= 2 && tp <= RS_MAX_TP, "gemm_scatter_reduce: TP must be 2..", RS_MAX_TP);
+  TORCH_CHECK(rows_per_rank % BM == 0 && M == rows_per_rank * tp, "rows per rank must be a multiple of 128");
+  TORCH_CHECK(peer_recv.is_cuda() && peer_recv.numel() == tp && peer_flags.is_cuda() && peer_flags.numel() == tp,
+              "peer pointers: cuda int64 [tp]");
+  const int64_t own_tiles = (rows_per_rank / BM) * ((N + BN - 1) / BN);
+  TORCH_CHECK(own_tiles * RS_MAX_TP * 4 <= flag_slots, "gemm_scatter_reduce: too many tiles for the stamp area");
+  auto out = at::empty({rows_per_rank, N}, x.options());
+  auto ma = make_map(x, BM);
+  auto mb = w_mn_major ? make_map(w, BK) : make_map(w, BN);
+  at::Tensor b;
+  if (bias && bias->defined()) b = bias->to(at::kBFloat16).contiguous();
+  auto args = plain_args(M, N, K, out.data_ptr(), N, b.defined() ? (const __nv_bfloat16*)b.data_ptr() : nullptr);
+  args.peer_out = reinterpret_cast<void* const*>(peer_recv.data_ptr());
+  args.my_recv = reinterpret_cast<const __nv_bfloat16*>(my_recv);
+  args.rs_flags_peer = reinterpret_cast<long long* const*>(peer_flags.data_ptr());
+  args.rs_flags_mine = reinterpret_cast<const long long*>(my_flags);
+  args.epoch = epoch;
+  args.rows_per_rank = (int)rows_per_rank;
+  args.src_rank = (int)src_rank;
+  args.tp = (int)tp;
+  CUtensorMap ma2, mb2;
+  const bool dual = x2 && x2->defined();
+  if (dual) {
+    TORCH_CHECK(w2 && w2->defined(), "second operand pair needs both x2 and w2");
+    const int64_t K2 = x2->size(1);
+    TORCH_CHECK(x2->size(0) <= M && x2->size(0) > 0, "x2 rows must be in [1, rows of x]");
+    TORCH_CHECK(w_mn_major ? (w2->size(0) == K2 && w2->size(1) == N) : (w2->size(1) == K2 && w2->size(0) == N),
+                "gemm_scatter_reduce: second pair shapes");
+    TORCH_CHECK(K2 % 16 == 0, "K2 must be a multiple of 16");
+    ma2 = make_map(*x2, BM);
+    mb2 = w_mn_major ? make_map(*w2, BK) : make_map(*w2, BN);
+    args.K2 = (int)K2;
+  }
+  auto mo = make_out_map(out);
+  if (w_mn_major)
+    launch<false, true, 5, false>(ma, mb, mo, args, dual ? &ma2 : nullptr, dual ? &mb2 : nullptr);
+  else
+    launch<false, false, 5, false>(ma, mb, mo, args, dual ? &ma2 : nullptr, dual ? &mb2 : nullptr);
+  return out;
+}
+
 // All-gather -> GEMM: y[M,N] = gather(x)[M,K] w[N,K]^T (+ bias); the gathered rows land in a_local.
 // mn_major: w is [K, N] (the row-parallel backward dX = all_gather(dY) @ W), else [N, K].
+// With x_local (this rank's shard [rows_per_rank, K]) the kernel stages it itself: copy warps write
+// it into the gather buffer and into send_mine (this rank's symmetric send buffer, which the peers
+// read), then publish the epoch into slot src_rank of every peer's flag area (peer_ready bases,
+// own_done: a zeroed device counter). Without x_local the caller staged and published the shard.
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
                        int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
-                       int64_t tp, bool mn_major) {
+                       int64_t tp, bool mn_major, c10::optional<at::Tensor> x_local, int64_t send_mine,
+                       c10::optional<at::Tensor> peer_ready, int64_t own_done) {
   const int64_t M = a_local.size(0), K = a_local.size(1), N = mn_major ? w.size(1) : w.size(0);
   TORCH_CHECK(!mn_major || w.size(0) == K, "gather_gemm: inner dims differ");
   check_dims(M, N, K);
@@ -629,6 +869,18 @@ at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tenso
   args.rows_per_rank = (int)rows_per_rank;
   args.src_rank = (int)src_rank;
   args.tp = (int)tp;
+  if (x_local && x_local->defined()) {
+    TORCH_CHECK(x_local->is_contiguous() && x_local->size(0) == rows_per_rank && x_local->size(1) == K &&
+                    x_local->scalar_type() == at::kBFloat16 && reinterpret_cast<uintptr_t>(x_local->data_ptr()) % 16 == 0,
+                "gather_gemm: x_local must be a contiguous aligned bf16 [rows_per_rank, K]");
+    TORCH_CHECK(peer_ready && peer_ready->is_cuda() && peer_ready->numel() == tp && send_mine != 0 && own_done != 0,
+                "gather_gemm: in-kernel staging needs send_mine, peer_ready and own_done");
+    TORCH_CHECK(rows_per_rank % GATHER_SUB == 0 && K % 8 == 0, "gather_gemm: rows per rank / K alignment");
+    args.x_local = reinterpret_cast<const __nv_bfloat16*>(x_local->data_ptr());
+    args.send_mine = reinterpret_cast<__nv_bfloat16*>(send_mine);
+    args.peer_ready = reinterpret_cast<long long* const*>(peer_ready->data_ptr());
+    args.own_done = reinterpret_cast<unsigned*>(own_done);
+  }
   if (mn_major)
     launch<false, true, 0, true>(ma, mb, make_out_map(y), args);
   else

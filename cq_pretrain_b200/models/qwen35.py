@@ -195,11 +195,14 @@ class GatedAttention(nn.Module):
         cfg, tp = self.cfg, ps.tp_size()
         s = plan.content_length
         hq, hkv, hd = cfg.heads // tp, cfg.kv_heads // tp, cfg.head_dim
-        xg = PL.gather_rows(x) if tp > 1 else x
-        q, gate = self.q_proj(xg, gathered=True).reshape(-1, hq, 2 * hd).chunk(2, -1)
         if cfg.qwen_fused_projections:
-            k, v = self.kv_proj(xg[:s], gathered=True).reshape(s, hkv, 2 * hd).chunk(2, -1)
+            # q/gate over all rows and k/v over the content rows share one in-kernel all-gather
+            qg, kv = PL.column_pair(x, self.q_proj, self.kv_proj, rows2=s)
+            q, gate = qg.reshape(-1, hq, 2 * hd).chunk(2, -1)
+            k, v = kv.reshape(s, hkv, 2 * hd).chunk(2, -1)
         else:
+            xg = PL.gather_rows(x) if tp > 1 else x
+            q, gate = self.q_proj(xg, gathered=True).reshape(-1, hq, 2 * hd).chunk(2, -1)
             k = self.k_proj(xg[:s], gathered=True).reshape(s, hkv, hd)
             v = self.v_proj(xg[:s], gathered=True).reshape(s, hkv, hd)
         q = self.q_norm(q)

@@ -7,9 +7,11 @@ attention over the projected conditions -> modulated LN -> GELU-tanh FFN -> fp32
 residual], and a modulated head. The adapter ``text_embedding`` maps backbone width ->
 1536 -> 1536 with GELU.
 
-Sequence parallel: DiT tokens are row-sharded across TP between modules. The full-width Q/K
-RMSNorm needs the sum of squares over all heads, which live on different TP ranks; the
-per-row partial sums are all-reduced across TP (fused into the QKV GEMM epilogue on CUDA).
+Sequence parallel: DiT tokens are row-sharded across TP between modules. Self-attention's q and
+kv projections share one in-kernel all-gather of the rows; the cross-attention context is
+gathered once per DiT call and read by every block's kv projection. The full-width Q/K RMSNorm
+needs the sum of squares over all heads, which live on different TP ranks: on CUDA one kernel per
+call exchanges the per-row partial sums over NVLink peer memory (no NCCL call).
 """
 
 from __future__ import annotations
@@ -95,15 +97,17 @@ class Attention(nn.Module):
         return k, v.reshape(-1, self.heads, self.head_dim)
 
     def forward(self, x, layout, context=None, cached_kv=None):
-        xg = PL.gather_rows(x) if ps.tp_size() > 1 else x
-        q = self.norm_q(self.q(xg, gathered=True)).reshape(-1, self.heads, self.head_dim)
-        if cached_kv is not None:
-            k, v = cached_kv
-        elif context is None:
-            k, v = self.project_kv(xg)
+        """``x``: this rank's rows; ``context``: every rank's condition rows (gathered once per call)."""
+        if context is None and cached_kv is None:
+            q, kv = PL.column_pair(x, self.q, self.kv)
+            k, v = kv.chunk(2, -1)
+            k = self.norm_k(k).reshape(-1, self.heads, self.head_dim)
+            v = v.reshape(-1, self.heads, self.head_dim)
         else:
-            k, v = self.project_kv(PL.gather_rows(context) if ps.tp_size() > 1 else context)
-        if context is None:
+            q = self.q(x)
+            k, v = cached_kv if cached_kv is not None else self.project_kv(context)
+        q = self.norm_q(q).reshape(-1, self.heads, self.head_dim)
+        if context is None and cached_kv is None:
             q = ROPE.rotary_pairs(q, layout.cos_rows, layout.sin_rows)
             k = ROPE.rotary_pairs(k, layout.cos_rows, layout.sin_rows)
             y = ATT.varlen_attention(q, k, v, layout.row_ends, layout.row_ends, ranges=layout.self_ranges)
@@ -231,6 +235,11 @@ class Wan21Generator(nn.Module):
         ctx = PL.gather_rows(context) if ps.tp_size() > 1 else context
         return tuple(tuple(t.contiguous() for t in block.cross_attn.project_kv(ctx)) for block in self.blocks)
 
+    @staticmethod
+    def gather_context(context):
+        """All ranks' projected condition rows: one all-gather per DiT call, read by every block."""
+        return PL.gather_rows(context) if ps.tp_size() > 1 else context
+
     def predict(self, xt, conditions, gen, projected=None, cached_kv=None):
         """Velocity prediction for packed noisy patches ``xt [sum L, C*4]`` (all rows, every rank)."""
         out, layout = self.predict_local(xt, conditions, gen, projected, cached_kv)
@@ -245,6 +254,7 @@ class Wan21Generator(nn.Module):
         time = self.time_embedding(gen.time_features.float().to(device))
         e = self.time_projection(time).reshape(-1, 6, self.cfg.dit_width)
         context = self.project_conditions(conditions, gen) if projected is None else projected
+        context = self.gather_context(context) if cached_kv is None else None
         if layout.pad:
             xt = torch.cat((xt, xt.new_zeros(layout.pad, xt.shape[1])))
         x = self.patch_embedding(PL.split_rows(xt) if st.tp > 1 else xt)

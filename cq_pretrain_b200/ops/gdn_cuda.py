@@ -58,29 +58,6 @@ def _layout(bounds, chunk, device):
     return hit
 
 
-class _Recurrence(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, W, U, P, Qd, Kt, gamma, start, count):
-        O, S = _ext.ops().gdn_fwd(W, U, P, Qd, Kt, gamma, start, count)
-        ctx.save_for_backward(W, U, P, Qd, Kt, gamma, start, count, S)
-        return O
-
-    @staticmethod
-    def backward(ctx, dO):
-        W, U, P, Qd, Kt, gamma, start, count, S = ctx.saved_tensors
-        dO = dO.contiguous().to(torch.bfloat16)
-        dS = _ext.ops().gdn_bwd(dO, W, P, Qd, Kt, gamma, start, count)
-        Sb, dSb = S.to(torch.bfloat16), dS.to(torch.bfloat16)
-        Delta = (U.float() - torch.matmul(W, Sb).float()).to(torch.bfloat16)
-        dDelta = (torch.matmul(P.transpose(-1, -2), dO).float() + torch.matmul(Kt, dSb).float()).to(torch.bfloat16)
-        dW = -torch.matmul(dDelta, Sb.transpose(-1, -2))
-        dQd = torch.matmul(dO, Sb.transpose(-1, -2))
-        dP = torch.matmul(dO, Delta.transpose(-1, -2))
-        dKt = torch.matmul(Delta, dSb.transpose(-1, -2))
-        dgamma = (S * dS).sum((-1, -2))
-        return dW, dDelta, dP, dQd, dKt, dgamma, None, None
-
-
 def _factors(Q, K, V, G, B, chunk):
     """WY factors of every chunk (no autograd). Q, K, V bf16 ``[Nc,H,C,D]``; G, B fp32 ``[Nc,H,C]``."""
     bf = torch.bfloat16

@@ -104,6 +104,41 @@ def gather_linear(x, weight, bias=None):
     return _GatherLinear.apply(x, weight, bias)
 
 
+class _GatherLinearPair(torch.autograd.Function):
+    """Two column-parallel projections of one all-gathered input: ``y1 = xg W1^T + b1`` (the
+    all-gather runs inside this GEMM) and ``y2 = xg[:rows2] W2^T + b2`` on the gathered rows.
+    Backward: ``reduce_scatter(dY1 W1 + pad(dY2) W2)`` in one GEMM -> reduce-scatter kernel."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, rows2):
+        from ..parallel import fused
+        y1, xg = fused.gather_linear(x, w1, b1)
+        x2 = xg if rows2 is None else xg[:rows2]
+        y2 = gemm.linear(x2, w2, b2)
+        ctx.save_for_backward(xg, w1, w2)
+        ctx.rows2, ctx.b1, ctx.b2 = rows2, b1, b2
+        return y1, y2
+
+    @staticmethod
+    def backward(ctx, dy1, dy2):
+        from ..parallel import fused
+        xg, w1, w2 = ctx.saved_tensors
+        rows2 = xg.shape[0] if ctx.rows2 is None else ctx.rows2
+        dy1 = torch.zeros(xg.shape[0], w1.shape[0], dtype=xg.dtype, device=xg.device) if dy1 is None else dy1.contiguous()
+        dy2 = torch.zeros(rows2, w2.shape[0], dtype=xg.dtype, device=xg.device) if dy2 is None else dy2.contiguous()
+        dx = fused.linear_scatter_grad(dy1, w1, dy2, w2) if ctx.needs_input_grad[0] else None
+        dw1 = _weight_grad(w1, dy1, xg) if ctx.needs_input_grad[1] else None
+        dw2 = _weight_grad(w2, dy2, xg[:rows2]) if ctx.needs_input_grad[3] else None
+        db1 = _accumulate(ctx.b1, _bias_grad(dy1)) if ctx.b1 is not None and ctx.needs_input_grad[2] else None
+        db2 = _accumulate(ctx.b2, _bias_grad(dy2)) if ctx.b2 is not None and ctx.needs_input_grad[4] else None
+        return dx, dw1, db1, dw2, db2, None
+
+
+def gather_linear_pair(x, w1, b1, w2, b2, rows2=None):
+    """``(all_gather(x) W1^T + b1, all_gather(x)[:rows2] W2^T + b2)`` with one all-gather."""
+    return _GatherLinearPair.apply(x, w1, b1, w2, b2, rows2)
+
+
 class _LinearScatter(torch.autograd.Function):
     """Row-parallel: ``y = reduce_scatter_rows(x @ W^T) + b``; backward all-gathers dY inside the
     input-gradient GEMM (``all_gather(dY) @ W``) and reuses the gathered rows for the weight gradient."""

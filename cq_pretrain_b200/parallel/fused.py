@@ -62,18 +62,21 @@ def gather_matmul(dy, weight):
 
 
 def linear_scatter(x, weight, bias=None):
-    """Return ``reduce_scatter(x @ W^T) + b``."""
+    """Return ``reduce_scatter(x @ W^T) + b`` (the bias is added once, by the rows' owner)."""
     ws = _symm()
-    if ws is not None and ws.supports(x, weight):
-        y = ws.linear_scatter(x, weight)
-    else:
-        y = scatter_rows_raw(gemm.linear(x, weight))
+    if ws is not None and ws.supports_scatter(x, weight):
+        return ws.linear_scatter(x, weight, bias)
+    y = scatter_rows_raw(gemm.linear(x, weight))
     return y if bias is None else y + bias.to(y.dtype)
 
 
-def linear_scatter_grad(dy, weight):
-    """Return ``reduce_scatter(dY @ W)`` (input gradient of a column-parallel linear)."""
+def linear_scatter_grad(dy, weight, dy2=None, weight2=None):
+    """Return ``reduce_scatter(dY @ W [+ pad(dY2) @ W2])``: the input gradient of one column-parallel
+    linear, or of two that read the same gathered rows (``dY2`` covers the first ``len(dY2)`` rows)."""
     ws = _symm()
-    if ws is not None and ws.supports(dy, weight, transposed=True):
-        return ws.matmul_scatter(dy, weight)
-    return scatter_rows_raw(gemm.matmul_nn(dy, weight))
+    if ws is not None and ws.supports_scatter(dy, weight, True, dy2, weight2):
+        return ws.matmul_scatter(dy, weight, dy2, weight2)
+    dx = gemm.matmul_nn(dy, weight)
+    if dy2 is not None:
+        dx[: dy2.shape[0]] += gemm.matmul_nn(dy2, weight2)
+    return scatter_rows_raw(dx)

@@ -195,6 +195,15 @@ class ColumnLinear(nn.Module):
         return L.linear(x, self.weight, self.bias)
 
 
+def column_pair(x, first, second, rows2=None):
+    """Two column-parallel projections of the same row-sharded input: ``(first(gather(x)),
+    second(gather(x)[:rows2]))``. Under TP the rows are gathered once, inside the first GEMM, and
+    the backward sums both input gradients in one GEMM -> reduce-scatter kernel."""
+    if ps.tp_size() > 1:
+        return L.gather_linear_pair(x, first.weight, first.bias, second.weight, second.bias, rows2)
+    return first(x), second(x if rows2 is None else x[:rows2])
+
+
 class RowLinear(nn.Module):
     """``y = scatter(x[:, shard] @ W[:, shard]^T) + b``; ``in_features`` split over TP."""
 

@@ -4,20 +4,24 @@ Every rank of a TP group allocates one buffer with the same layout, exchanges CU
 handles, and opens every peer's buffer (NVLink P2P). Layout::
 
     [0, 512)        all-gather flags: slot s = last epoch rank s published its shard
-    [512, 1024)     reduce-scatter flags: slot s = last epoch rank s finished storing partials
+    [512, 1024)     (unused) reduce-scatter flags of the former three-kernel path
+    [2048, 2052)    all-gather staging counter (own sub-chunks staged in the running call)
     send[0], send[1]   this rank's staged shard for all-gather (double-buffered by epoch parity)
     recv[0], recv[1]   [tp, rows/tp, N] partial slabs written by peers for reduce-scatter
     stat flags         [row blocks][8] epoch flags of the row-statistic exchange (TP RMSNorm)
     stat[0], stat[1]   [tp, max_rows] fp32 per-row partials written by peers (parity buffered)
+    rs stamps          [tiles][8 sources][4 warps] int64 epoch stamps of GEMM -> reduce-scatter tiles
 
 Protocol (epochs count calls of each kind; every rank issues the same sequence):
 
-* all-gather -> GEMM (epoch e): copy the local shard into ``send[e % 2]``, publish flag e to
-  every peer, then one kernel pulls each peer's shard into local memory block by block (after
-  acquiring that peer's flag) while the tensor cores consume the blocks already present.
-* GEMM -> reduce-scatter (epoch e): one GEMM kernel stores every output tile into the owner's
-  ``recv[e % 2][src]``; a one-block kernel publishes flag e and acquires all peers' flags; a
-  bandwidth kernel sums the tp slabs.
+* all-gather -> GEMM (epoch e): one kernel. Its copy warps stage the local shard into the gather
+  buffer and into ``send[e % 2]`` (own rows first), publish flag e to every peer once the whole
+  shard is staged, and pull each peer's shard into local memory block by block (after acquiring
+  that peer's flag) while the tensor cores consume the blocks already present.
+* GEMM -> reduce-scatter (epoch e): one kernel. Tiles of rows owned by another rank are stored
+  into the owner's ``recv[e % 2][src]`` and stamped with e in the owner's (tile, src, warp) slot;
+  this rank's own tiles come last, wait for the peers' stamps of the same tile, and add the
+  peers' bf16 partials to their fp32 accumulator (and the bias) before storing the result.
 * row statistics (epoch e, Wan's full-width Q/K RMSNorm, and the vocabulary-parallel cross-entropy's
   (max, sum exp, target logit) triples): one kernel per call; each 64-row block
   stores its partial sums into ``stat[e % 2][rank]`` of every peer, publishes a per-block flag and
@@ -46,7 +50,8 @@ def _align(n, a=4096):
 
 
 class SymmetricWorkspace:
-    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192, stat_rows=65536):
+    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192, stat_rows=65536,
+                 rs_tiles=8192):
         st = ps.state()
         if st.tp < 2:
             raise ValueError("symmetric workspace needs TP >= 2")
@@ -61,7 +66,9 @@ class SymmetricWorkspace:
         stat_bytes = _align(self.tp * stat_rows * 4)
         self.off_stat = [self.off_stat_flags + _align(stat_blocks * 8 * 8), 0]
         self.off_stat[1] = self.off_stat[0] + stat_bytes
-        total = self.off_stat[1] + stat_bytes
+        self.rs_slots = rs_tiles * 8 * 4
+        self.off_rs_flags = self.off_stat[1] + stat_bytes
+        total = self.off_rs_flags + _align(self.rs_slots * 8)
         ptr, handle = ops.symm_alloc(total)
         self.base = int(ptr[0])
         handles = [None] * self.tp
@@ -81,6 +88,7 @@ class SymmetricWorkspace:
         self.recv = [as_dev([b + self.off_recv[p] for b in bases]) for p in range(2)]
         self.stat_flags = as_dev([b + self.off_stat_flags for b in bases])
         self.stat = [as_dev([b + self.off_stat[p] for b in bases]) for p in range(2)]
+        self.rs_flags = as_dev([b + self.off_rs_flags for b in bases])
         self.epoch_stat = 0
         # one publication flag per 16 gathered rows (the all-gather copy unit)
         self.chunk_flags = torch.zeros(max_subchunks, dtype=torch.int64, device=dev)
@@ -104,7 +112,8 @@ class SymmetricWorkspace:
 
     def _gather_ok(self, x):
         rows = x.shape[0] * self.tp
-        return (x.shape[0] % 128 == 0 and x.numel() * 2 <= self.send_bytes and rows // 16 <= self.chunk_flags.numel())
+        return (x.shape[0] % 128 == 0 and x.numel() * 2 <= self.send_bytes and rows // 16 <= self.chunk_flags.numel()
+                and x.shape[1] % 8 == 0 and (not x.is_contiguous() or x.data_ptr() % 16 == 0))
 
     # ---- fused ops --------------------------------------------------------------------------------
     def gather_linear(self, x, weight, bias=None):
@@ -126,24 +135,36 @@ class SymmetricWorkspace:
         self.epoch_ag += 1
         e, p = self.epoch_ag, self.epoch_ag % 2
         rows = x.shape[0]
-        stage = ops.symm_view(self.base, self.off_send[p], [rows, x.shape[1]], torch.bfloat16)
-        stage.copy_(x)
-        ops.signal_wait(self.flag_ag, self.base, self.rank, self.tp, e, False)
         xg = torch.empty(rows * self.tp, x.shape[1], dtype=x.dtype, device=x.device)
         y = ops.gather_gemm(xg, weight.contiguous(), bias, self.send[p], self.base, self.chunk_flags, e, rows,
-                            self.rank, self.tp, mn_major)
+                            self.rank, self.tp, mn_major, x_local=x.contiguous(),
+                            send_mine=self.base + self.off_send[p], peer_ready=self.flag_ag,
+                            own_done=self.base + 2 * FLAG_BYTES)
         return y, xg
 
-    def _scatter(self, x, weight, mn_major):
-        ops = _ext.ops()
+    def _scatter(self, x, weight, mn_major, x2=None, w2=None, bias=None):
         self.epoch_rs += 1
         e, p = self.epoch_rs, self.epoch_rs % 2
         rows = x.shape[0] // self.tp
-        n_out = weight.shape[1] if mn_major else weight.shape[0]
-        ops.gemm_scatter(x.contiguous(), weight.contiguous(), mn_major, self.recv[p], rows, self.rank, self.tp)
-        ops.signal_wait(self.flag_rs, self.base + 512, self.rank, self.tp, e, True)
-        recv = ops.symm_view(self.base, self.off_recv[p], [self.tp, rows, n_out], torch.bfloat16)
-        return ops.rs_reduce(recv, None, self.tp, rows, n_out)
+        if x2 is not None:
+            x2, w2 = x2.contiguous(), w2.contiguous()
+        return _ext.ops().gemm_scatter_reduce(
+            x.contiguous(), weight.contiguous(), mn_major, x2, w2, bias, self.recv[p], self.base + self.off_recv[p],
+            self.rs_flags, self.base + self.off_rs_flags, self.rs_slots, e, rows, self.rank, self.tp)
+
+    def supports_scatter(self, x, w, transposed=False, x2=None, w2=None):
+        """Eligibility of the one-kernel GEMM -> reduce-scatter (optionally with a second operand pair)."""
+        if not self.supports(x, w, transposed):
+            return False
+        n_out = w.shape[1] if transposed else w.shape[0]
+        tiles = (x.shape[0] // self.tp // 128) * -(-n_out // 256)
+        if tiles * 32 > self.rs_slots or self.tp > 8:
+            return False
+        if x2 is None:
+            return True
+        return (x2.is_cuda and x2.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16 and x2.dim() == 2
+                and 0 < x2.shape[0] <= x.shape[0] and x2.shape[1] % 16 == 0 and x2.data_ptr() % 16 == 0
+                and (w2.shape[1] if transposed else w2.shape[0]) == n_out)
 
     # ---- row statistics ----------------------------------------------------------------------
     def supports_rms(self, x):
@@ -176,13 +197,14 @@ class SymmetricWorkspace:
         return _ext.ops().ce_combine_tp(part, tgt_local, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
                                         self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e)
 
-    def linear_scatter(self, x, weight):
-        """``reduce_scatter_rows(x @ W^T)`` with the GEMM storing tiles into the owners' buffers."""
-        return self._scatter(x, weight, False)
+    def linear_scatter(self, x, weight, bias=None):
+        """``reduce_scatter_rows(x @ W^T) + b`` in one GEMM -> reduce-scatter kernel."""
+        return self._scatter(x, weight, False, bias=bias)
 
-    def matmul_scatter(self, dy, weight):
-        """``reduce_scatter_rows(dY @ W)`` (column-parallel input gradient)."""
-        return self._scatter(dy, weight, True)
+    def matmul_scatter(self, dy, weight, dy2=None, weight2=None):
+        """``reduce_scatter_rows(dY @ W [+ dY2 @ W2])`` (input gradient of one or two column-parallel
+        projections of the same gathered input; ``dY2`` may cover only its first rows)."""
+        return self._scatter(dy, weight, True, dy2, weight2)
 
     def close(self):
         ops = _ext.ops()

@@ -43,11 +43,23 @@ def _worker(rank, world, port, out):
         z = ws.linear_scatter(xf, w2)
         zref = fused.scatter_rows_raw(gemm.linear(xf, w2))
         errors.append(float((z.float() - zref.float()).abs().max() / zref.float().abs().max()))
+        # the owner adds the bias once, inside the same kernel
+        bias = torch.randn(512, device="cuda", dtype=torch.bfloat16)
+        zb = ws.linear_scatter(xf, w2, bias)
+        errors.append(float((zb.float() - zref.float() - bias.float()).abs().max() / zref.float().abs().max()))
         dy = torch.randn(256 * world, 384, device="cuda", dtype=torch.bfloat16)
         w3 = (torch.randn(384, 512, device="cuda") * 0.05).to(torch.bfloat16)
         d = ws.matmul_scatter(dy, w3)
         dref = fused.scatter_rows_raw(gemm.matmul_nn(dy, w3))
         errors.append(float((d.float() - dref.float()).abs().max() / dref.float().abs().max()))
+        # two projections of one gathered input: reduce_scatter(dY1 W1 + pad(dY2) W2), dY2 over fewer rows
+        dy2 = torch.randn(256 * world - 72, 160, device="cuda", dtype=torch.bfloat16)
+        w5 = (torch.randn(160, 512, device="cuda") * 0.05).to(torch.bfloat16)
+        d2 = ws.matmul_scatter(dy, w3, dy2, w5)
+        full = gemm.matmul_nn(dy, w3).float()
+        full[: dy2.shape[0]] += gemm.matmul_nn(dy2, w5).float()
+        d2ref = fused.scatter_rows_raw(full)
+        errors.append(float((d2.float() - d2ref).abs().max() / d2ref.abs().max()))
         # row-parallel input gradient: all_gather(dY) @ W with W [K, N] (MN-major B) in one kernel
         dy_local = torch.randn(256, 384, device="cuda", dtype=torch.bfloat16)
         w4 = (torch.randn(384, 320, device="cuda") * 0.05).to(torch.bfloat16)
@@ -93,11 +105,39 @@ def _worker(rank, world, port, out):
         dist.all_reduce(dh)                 # each rank holds its vocabulary shard's part of dh
         errors.append(float((loss.float() - ref_loss).abs() / ref_loss.abs()))
         errors.append(float((dh - href.grad).norm() / href.grad.norm()))
+    # autograd pair (Qwen q/kv projection shape): forward and all gradients vs the NCCL path
+    from cq_pretrain_b200.ops import linear as L
+    xs = torch.randn(256, 512, device="cuda", dtype=torch.bfloat16)
+    wa = (torch.randn(384, 512, device="cuda") * 0.05).to(torch.bfloat16)
+    wb = (torch.randn(128, 512, device="cuda") * 0.05).to(torch.bfloat16)
+    ba = torch.randn(384, device="cuda", dtype=torch.bfloat16)
+    rows2 = 256 * world - 200
+    ga = torch.randn(256 * world, 384, device="cuda", dtype=torch.bfloat16)
+    gb = torch.randn(rows2, 128, device="cuda", dtype=torch.bfloat16)
+    results = []
+    for use_fused in (True, False):
+        leaves = [t.clone().requires_grad_() for t in (xs, wa, ba, wb)]
+        if use_fused:
+            ya, yb = L.gather_linear_pair(leaves[0], leaves[1], leaves[2], leaves[3], None, rows2)
+        else:
+            xg_all = torch.cat([t for t in _all_gather(leaves[0])])
+            ya = xg_all @ leaves[1].T + leaves[2]
+            yb = xg_all[:rows2] @ leaves[3].T
+        torch.autograd.backward([ya, yb], [ga, gb])
+        results.append([ya.detach().float(), yb.detach().float()] + [t.grad.float() for t in leaves])
+    for a, b in zip(*results):
+        errors.append(float((a - b).norm() / b.norm().clamp_min(1e-6)))
     torch.cuda.synchronize()
     status = symmetric.status()
     symmetric.disable()
     ps.destroy()
     torch.save(dict(errors=errors, status=status), f"{out}.{rank}")
+
+
+def _all_gather(x):
+    """Differentiable row all-gather (NCCL) for the reference path."""
+    from torch.distributed.nn.functional import all_gather
+    return all_gather(x)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
