@@ -1,8 +1,9 @@
 """Per-kernel device-time breakdown of one joint training step (torch.profiler, CUPTI).
 
 ``[torchrun --nproc-per-node N] python -m cq_pretrain_b200.benchmarks.profile_step [--length 8192]
-[--recompute 1]`` runs the bench configuration (TP = N, rank 0 reports), warms up, profiles one step and prints the kernels with the
-largest total device time, grouped by name, plus each group's share of the step.
+[--recompute 1] [--tp T]`` runs the bench configuration (TP = T, default N; DP = N / T; rank 0
+reports), warms up, profiles one step and prints the kernels with the largest total device time,
+grouped by name, plus each group's share of the step.
 """
 
 from __future__ import annotations
@@ -19,6 +20,8 @@ def main():
     parser.add_argument("--recompute", type=int, default=1)
     parser.add_argument("--top", type=int, default=40)
     parser.add_argument("--layers", type=int, default=None)
+    parser.add_argument("--tp", type=int, default=None, help="TP size under torchrun (default: the world size)")
+    parser.add_argument("--images", type=int, default=3)
     args = parser.parse_args()
     import os
 
@@ -28,14 +31,15 @@ def main():
     from ..train.trainer import Trainer
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    st = ps.initialize(world, timeout_s=600.0) if world > 1 else None   # TP = world (torchrun)
-    tp = world
+    tp = args.tp or world
+    st = ps.initialize(tp, timeout_s=600.0) if world > 1 else None   # DP = world / TP
 
     cfg = qwen35_2b_wan(visual_query_mode="fixed", image_condition_queries=256, checkpoint_backbone=bool(args.recompute))
     if args.layers:
         cfg.layers = args.layers
-    host, receipt = synthetic_batch(cfg, args.length, seed=42, kind="joint", images=2, grid=(1, 64, 64),
-                                    latent_shape=(16, 1, 64, 64), understanding=False, pad_multiple=128 * tp)
+    seed = 42 + (st.dp_rank if st is not None else 0)
+    host, receipt = synthetic_batch(cfg, args.length, seed=seed, kind="joint", images=args.images, grid=(1, 64, 64),
+                                    latent_shape=(16, 1, 64, 64), understanding=True, pad_multiple=128 * tp)
     host = host.pin_memory()
     trainer = Trainer(cfg, tp=tp, lr=5e-5, ema_decay=0.999)
     for _ in range(3):

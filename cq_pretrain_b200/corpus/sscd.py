@@ -1,9 +1,10 @@
 """SSCD near-duplicate graph and exact all-pairs search (corpus side, off the training path).
 
 * ``build_library()`` compiles ``sscd_graph.cpp`` (host C++17, ``-O3``) into
-  ``cq_pretrain_b200/_build/sscd_graph.so``; ``Graph`` drives it through ctypes on NumPy arrays:
-  components, CSR adjacency and greedy one-hop representatives over thresholded edges
-  (reference ``corpus_pipeline/dedup/_sscd_graph.cpp:1-92``, ``sscd_graph.py:229-253``).
+  ``cq_pretrain_b200/_build/sscd_graph.so``; ``Graph`` owns one native graph object (CSR
+  adjacency by counting sort, BFS components) and copies components, adjacency, statistics and
+  greedy one-hop representatives out into NumPy arrays (the behaviour of the reference's
+  ``corpus_pipeline/dedup/_sscd_graph.cpp:1-92`` / ``sscd_graph.py:229-253``).
 * ``exact_pairs(left, right, threshold)`` finds every pair with cosine >= threshold: tiled
   ``left @ right^T`` on the tcgen05 GEMM in bf16 with a safety margin, threshold compaction on
   the GPU, then an fp32 rerank of the candidates (reference
@@ -24,9 +25,18 @@ import numpy as np
 SOURCE = Path(__file__).resolve().with_name("sscd_graph.cpp")
 LIBRARY = Path(__file__).resolve().parents[1] / "_build" / "sscd_graph.so"
 EDGE_DTYPE = np.dtype([("a", "<u4"), ("b", "<u4"), ("score", "<f4")])
-ERRORS = {1: "too many vertices", 2: "malformed edge or score below threshold", 3: "malformed edge",
-          4: "adjacency row overflow", 5: "priority order out of range", 6: "bad neighbour or score",
-          7: "inconsistent representatives"}
+NO_REPRESENTATIVE = np.iinfo(np.uint32).max
+
+
+class _Stats(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_uint64) for name in ("components", "nontrivial_components", "largest_component",
+                                                     "vertices_with_edges", "isolated_vertices", "max_degree")] \
+        + [("size_histogram", ctypes.c_uint64 * 32)]
+
+
+class _Selection(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_uint64) for name in ("eligible", "representatives", "suppressed", "ineligible",
+                                                     "protected_vertices")]
 
 
 def build_library(force=False) -> Path:
@@ -44,66 +54,89 @@ _LIB = None
 def _lib():
     global _LIB
     if _LIB is None:
-        _LIB = ctypes.CDLL(str(build_library()))
+        lib = ctypes.CDLL(str(build_library()))
+        vp, u64 = ctypes.c_void_p, ctypes.c_uint64
+        lib.sscd_last_error.restype = ctypes.c_char_p
+        lib.sscd_graph_build.argtypes = [u64, vp, u64, ctypes.c_float, ctypes.POINTER(vp)]
+        lib.sscd_graph_free.argtypes = [vp]
+        lib.sscd_graph_free.restype = None
+        lib.sscd_graph_edges.argtypes = [vp]
+        lib.sscd_graph_edges.restype = u64
+        lib.sscd_graph_components.argtypes = [vp, vp, vp]
+        lib.sscd_graph_adjacency.argtypes = [vp, vp, vp, vp]
+        lib.sscd_graph_stats.argtypes = [vp, ctypes.POINTER(_Stats)]
+        lib.sscd_graph_select.argtypes = [vp, vp, vp, vp, vp, vp, vp, ctypes.POINTER(_Selection)]
+        _LIB = lib
     return _LIB
 
 
-def _call(name, *args):
-    conv = []
-    for a in args:
-        if isinstance(a, np.ndarray):
-            if not a.flags.c_contiguous:
-                raise ValueError(f"{name}: arrays must be C-contiguous")
-            conv.append(ctypes.c_void_p(a.ctypes.data))
-        elif isinstance(a, float):
-            conv.append(ctypes.c_float(a))
-        else:
-            conv.append(ctypes.c_uint64(int(a)))
-    rc = getattr(_lib(), name)(*conv)
+def _ptr(array):
+    if array is None:
+        return None
+    if not array.flags.c_contiguous:
+        raise ValueError("arrays passed to the graph library must be C-contiguous")
+    return ctypes.c_void_p(array.ctypes.data)
+
+
+def _check(rc):
     if rc != 0:
-        raise ValueError(f"{name} failed ({rc}): {ERRORS.get(rc, 'unknown error')}")
+        raise ValueError(f"SSCD graph library: {_lib().sscd_last_error().decode()} (status {rc})")
 
 
 class Graph:
-    """Thresholded similarity graph over ``n`` vertices."""
+    """Thresholded similarity graph over ``n`` vertices, held by the native library.
+
+    Attributes copied out at construction: ``label`` (smallest vertex id of each vertex's
+    component), ``component_size``, the CSR adjacency ``offsets`` / ``neighbors`` / ``scores``
+    (neighbours in edge order), ``summary`` and the log2 component-size ``histogram``.
+    """
 
     def __init__(self, n, edges, threshold):
         edges = np.ascontiguousarray(edges, dtype=EDGE_DTYPE)
-        self.n, self.threshold, self.edges = int(n), float(threshold), edges
-        self.parent = np.empty(n, np.uint32)
-        self.size = np.empty(n, np.uint32)
-        self.degree = np.empty(n, np.uint64)
-        _call("sscd_init", n, self.parent, self.size, self.degree)
-        _call("sscd_union", n, len(edges), edges, self.parent, self.size, self.degree, self.threshold)
-        self.label = np.empty(n, np.uint32)
-        self.component_size = np.empty(n, np.uint32)
-        self.offsets = np.empty(n + 1, np.uint64)
-        summary = np.empty(6, np.uint64)
-        self.histogram = np.empty(32, np.uint64)
-        _call("sscd_components", n, self.parent, self.size, self.degree, self.label, self.component_size,
-              self.offsets, summary, self.histogram)
-        self.summary = dict(zip(("components", "nontrivial_components", "largest_component", "vertices_with_edges",
-                                 "isolated_vertices", "max_degree"), summary.tolist()))
-        self.neighbors = np.empty(int(self.offsets[-1]), np.uint32)
-        self.scores = np.empty(int(self.offsets[-1]), np.float32)
-        cursor = self.offsets[:-1].copy()
-        _call("sscd_fill", n, len(edges), edges, self.offsets, cursor, self.neighbors, self.scores)
+        self.n, self.threshold = int(n), float(threshold)
+        lib = _lib()
+        handle = ctypes.c_void_p()
+        _check(lib.sscd_graph_build(self.n, _ptr(edges) if len(edges) else None, len(edges), self.threshold,
+                                    ctypes.byref(handle)))
+        self._handle = handle
+        self.label = np.empty(self.n, np.uint32)
+        self.component_size = np.empty(self.n, np.uint32)
+        _check(lib.sscd_graph_components(handle, _ptr(self.label), _ptr(self.component_size)))
+        m = int(lib.sscd_graph_edges(handle))
+        self.offsets = np.empty(self.n + 1, np.uint64)
+        self.neighbors = np.empty(2 * m, np.uint32)
+        self.scores = np.empty(2 * m, np.float32)
+        _check(lib.sscd_graph_adjacency(handle, _ptr(self.offsets), _ptr(self.neighbors), _ptr(self.scores)))
+        stats = _Stats()
+        _check(lib.sscd_graph_stats(handle, ctypes.byref(stats)))
+        self.summary = {name: int(getattr(stats, name)) for name, _ in _Stats._fields_[:6]}
+        self.histogram = np.array(list(stats.size_histogram), np.uint64)
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle is not None and _LIB is not None:
+            _LIB.sscd_graph_free(handle)
+            self._handle = None
 
     def representatives(self, order=None, eligible=None, protect=None):
         """Greedy one-hop selection in ``order`` (default: vertex id). Returns
-        ``(representative, direct_score, group_size, summary)``."""
+        ``(representative, direct_score, group_size, summary)``; ineligible vertices get
+        ``NO_REPRESENTATIVE``."""
         n = self.n
         order = np.arange(n, dtype=np.uint32) if order is None else np.ascontiguousarray(order, np.uint32)
-        eligible = np.ones(n, np.uint8) if eligible is None else np.ascontiguousarray(eligible, np.uint8)
-        protect = np.zeros(n, np.uint8) if protect is None else np.ascontiguousarray(protect, np.uint8)
+        if order.shape != (n,):
+            raise ValueError("the priority order must list n vertices")
+        eligible = None if eligible is None else np.ascontiguousarray(eligible, np.uint8)
+        protect = None if protect is None else np.ascontiguousarray(protect, np.uint8)
         rep = np.empty(n, np.uint32)
         direct = np.empty(n, np.float32)
         group = np.empty(n, np.uint32)
-        summary = np.empty(5, np.uint64)
-        _call("sscd_representatives", n, self.offsets, self.neighbors, self.scores, order, eligible, protect, rep,
-              direct, group, summary, self.threshold)
-        return rep, direct, group, dict(zip(("eligible", "representatives", "suppressed", "ineligible", "protected"),
-                                             summary.tolist()))
+        sel = _Selection()
+        _check(_lib().sscd_graph_select(self._handle, _ptr(order), _ptr(eligible), _ptr(protect), _ptr(rep),
+                                        _ptr(direct), _ptr(group), ctypes.byref(sel)))
+        summary = dict(eligible=sel.eligible, representatives=sel.representatives, suppressed=sel.suppressed,
+                       ineligible=sel.ineligible, protected=sel.protected_vertices)
+        return rep, direct, group, summary
 
 
 def exact_pairs(left, right, threshold, tile=8192, margin=0.02, device=None):

@@ -8,6 +8,7 @@
 //  chunks: rows of [E, H, D] events are gathered into the zero-padded chunk layout
 //          [Nc, H, 64, D], optionally L2-normalised on the way (rsqrt norms saved), and
 //          scattered back (with the L2-norm backward fused).
+#include "noalloc.h"
 #include "common.cuh"
 
 #include <cstdio>
@@ -588,7 +589,7 @@ at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::T
 
 }  // namespace cqb
 
-// ==== Allocation-free causal-conv backward (C ABI) ============================================
+// ==== Allocation-free causal-conv backward (C ABI, declared in noalloc.h) =====================
 //
 // This entry point has no counterpart in the reference framework. It serves callers that must
 // not allocate device memory while they run the backward pass of the short convolution:
@@ -635,13 +636,6 @@ int noalloc_fail(int code, const char* fmt, long a = 0, long b = 0) {
 }  // namespace
 
 extern "C" {
-
-enum {
-  CQB_NOALLOC_OK = 0,
-  CQB_NOALLOC_BAD_ARGUMENT = 1,
-  CQB_NOALLOC_TOO_LARGE = 2,
-  CQB_NOALLOC_CUDA_ERROR = 3,
-};
 
 // Message of the last failed call on this host thread.
 __attribute__((visibility("default"))) const char* cqb_noalloc_last_error(void) { return g_noalloc_error; }
@@ -700,15 +694,28 @@ __attribute__((visibility("default"))) int cqb_conv_bwd_noalloc(const void* dy, 
                         "input too large for the static scratch: it needs %ld floats (ceil(n / 256) * C * 4), "
                         "the limit is %ld",
                         (long)need, (long)kNoAllocScratchFloats);
+  if (grid.y > 65535u || grid.x > 2147483647u)
+    return noalloc_fail(CQB_NOALLOC_TOO_LARGE, "input too large for one launch: %ld row blocks (limit %ld)",
+                        (long)grid.y, 65535L);
   int device = 0;
-  cudaGetDevice(&device);
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "cudaGetDevice failed (error %ld)", (long)err);
   float* scratch = g_scratch_ptr[device];
+  // Do not launch over (or clear) an error the caller left pending: report it instead.
+  err = cudaPeekAtLastError();
+  if (err != cudaSuccess)
+    return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "an earlier CUDA error is pending (error %ld); nothing was launched",
+                        (long)err);
   cqb::conv_bwd_kernel<<<grid, dim3(32, cqb::CONV_GROUPS), 0, stream>>>(
       (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, wT, pos, (__nv_bfloat16*)dx, scratch, (int)n, (int)C);
+  err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "launch of the conv backward failed (error %ld)", (long)err);
   cqb::sum_rows_kernel<<<(unsigned)((C * cqb::CONV_K + 255) / 256), 256, 0, stream>>>(scratch, dw, (int)grid.y,
                                                                                        (int)(C * cqb::CONV_K));
-  const cudaError_t err = cudaGetLastError();
-  if (err != cudaSuccess) return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "kernel launch failed (error %ld)", (long)err);
+  err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return noalloc_fail(CQB_NOALLOC_CUDA_ERROR, "launch of the partial sum failed (error %ld)", (long)err);
   cqb::count_launch(2);
   return CQB_NOALLOC_OK;
 }

@@ -83,7 +83,7 @@ struct GemmArgs {
   long long* chunk_flags;     // [M / 16] per-sub-chunk publication flags (local)
   long long epoch;
   int group_m;                // tile raster: groups of group_m row blocks sweep all column blocks
-  int split_k;                // EPI 1 only: CTAs take balanced ranges of (tile, k block) units
+  int split_k;                // EPI 1 only: equal k-ranges per tile (1 = whole tiles), chosen by launch()
   // EPI 3/4 (cross-entropy over a vocabulary shard [lo, lo + N)):
   const long long* targets;   // [M] global token ids
   long long lo;
@@ -157,35 +157,22 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   n0 = (r / rows) * BN;
 }
 
-// Work of one CTA: whole tiles round-robin over the grid, or (split_k, epilogue 1 only) one
-// contiguous range of the tiles x k-blocks units, cut into per-tile segments. Partial sums of a
-// tile from several CTAs meet in the reduce-add epilogue, so the ranges need no fix-up pass and
-// every CTA gets the same amount of MMA work whatever the tile count.
+// Work of one CTA: units handed out round-robin over the grid. A unit is a whole tile, or (split_k
+// = S > 1, epilogue 1 only) one of S equal k-ranges of a tile, numbered split-major (unit u is
+// range u / tiles of tile u % tiles), so the CTAs of one wave sweep the same contraction range and
+// share its A/B slices in L2. Partial sums of a tile from several units meet in the reduce-add
+// epilogue, so no fix-up pass is needed; S is picked on the host to even out the last wave.
 struct WorkIter {
-  long long u, end;
-  int kblocks, t, stride, tiles;
-  bool split;
-  __device__ WorkIter(bool split_k, int tiles_, int kblocks_) : kblocks(kblocks_), tiles(tiles_), split(split_k) {
-    const long long w = (long long)tiles_ * kblocks_;
-    u = w * blockIdx.x / gridDim.x;
-    end = w * (blockIdx.x + 1) / gridDim.x;
-    t = blockIdx.x;
-    stride = gridDim.x;
-  }
+  int u, units, kblocks, tiles, splits;
+  __device__ WorkIter(int splits_, int tiles_, int kblocks_)
+      : u(blockIdx.x), units(tiles_ * max(1, splits_)), kblocks(kblocks_), tiles(tiles_), splits(max(1, splits_)) {}
   __device__ bool next(int& tile, int& kb0, int& kb1) {
-    if (!split) {
-      if (t >= tiles) return false;
-      tile = t;
-      kb0 = 0;
-      kb1 = kblocks;
-      t += stride;
-      return true;
-    }
-    if (u >= end) return false;
-    tile = (int)(u / kblocks);
-    kb0 = (int)(u % kblocks);
-    kb1 = (int)min((long long)kblocks, kb0 + (end - u));
-    u += kb1 - kb0;
+    if (u >= units) return false;
+    const int s = u / tiles;
+    tile = u % tiles;
+    kb0 = (int)((long long)s * kblocks / splits);
+    kb1 = (int)((long long)(s + 1) * kblocks / splits);
+    u += gridDim.x;
     return true;
   }
 };
@@ -247,7 +234,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) armed[s] = -1;
       bool ok = true;
-      WorkIter work(EPI == 1 && args.split_k, tiles, kblocks);
+      WorkIter work(EPI == 1 ? args.split_k : 1, tiles, kblocks);
       int t, kb0, kb1;
       while (ok && work.next(t, kb0, kb1)) {
         int m0, n0;
@@ -307,7 +294,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      WorkIter work(EPI == 1 && args.split_k, tiles, kblocks);
+      WorkIter work(EPI == 1 ? args.split_k : 1, tiles, kblocks);
       int t, kb0, kb1;
       for (; ok && work.next(t, kb0, kb1); ++local) {
         const int buf = local & 1;
@@ -351,7 +338,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     uint8_t* my_stage = staging + quarter * 2 * EPI_BOX * EPI_BOX * 4;
     int local = 0, chunk = 0;
     if (lane == 0 && EPI != 2 && EPI != 3) tc::prefetch_map(&map_out);
-    WorkIter work(EPI == 1 && args.split_k, tiles, kblocks);
+    WorkIter work(EPI == 1 ? args.split_k : 1, tiles, kblocks);
     int t, kb0, kb1;
     for (; work.next(t, kb0, kb1); ++local) {
       const int buf = local & 1;
@@ -682,9 +669,27 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
   if (args.K2 > 0) TORCH_CHECK(ma2 != nullptr && mb2 != nullptr, "second operand pair without tensor maps");
   // GATHER needs every CTA resident (copy blocks are handed out by CTA index): one per SM.
   // Split-K (reduce-add epilogue): every SM takes an equal share of the tiles x k-blocks units.
+  // Split-K (reduce-add epilogue only): S equal k-ranges per tile, S in 1..4 with at least 16 k
+  // blocks per range, chosen for the best fill of the last wave (ties go to the smaller S).
   const int kblocks = (int)((args.K + BK - 1) / BK);
-  if (EPI == 1 && args.split_k) args.split_k = (long long)tiles * kblocks >= 2LL * sm_count() ? 1 : 0;
-  const int grid = (EPI == 1 && args.split_k) ? sm_count() : std::max(1, std::min(tiles, sm_count()));
+  if (EPI == 1 && args.split_k) {
+    int best = 1;
+    double best_fill = 0.0;
+    for (int s = 1; s <= 4; ++s) {
+      if (s > 1 && kblocks / s < 16) break;
+      const long long units = (long long)tiles * s;
+      const long long waves = (units + sm_count() - 1) / sm_count();
+      const double fill = (double)units / (double)(waves * sm_count());
+      if (fill > best_fill + 0.02) {
+        best_fill = fill;
+        best = s;
+      }
+    }
+    args.split_k = best;
+  } else {
+    args.split_k = 1;
+  }
+  const int grid = std::max(1, std::min(tiles * args.split_k, sm_count()));
   kernel<<<grid, GATHER ? 256 : 192, SMEM_BYTES, stream()>>>(ma, mb, mo, ma2 ? *ma2 : ma, mb2 ? *mb2 : mb, args,
                                                               status_word());
   CQB_LAUNCH_CHECK();

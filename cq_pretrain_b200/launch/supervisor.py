@@ -1,17 +1,27 @@
 """Production supervisor: one fresh launch generation per platform (re)start, auto-resume.
 
-Per node (reference ``train_production.py:39-154``):
+Per node (behaviour of the reference ``train_production.py:39-154``):
 
 1. take an exclusive per-node ``flock`` (never two attempts on one checkpoint stream);
-2. ``join_attempt``: node 0 writes a new generation id; every node acknowledges it with a fresh
-   per-process token; node 0 writes the cohort once all nodes acknowledged the same
-   generation; a node proceeds only when the cohort lists its token (stale receipts from an
-   earlier process can never be accepted); a changed node count is rejected;
+2. ``join_attempt`` agrees on a launch generation (protocol below);
 3. start the training launcher in its own process group, logging under the attempt directory;
 4. watch: if the generation changes, a peer reports a non-zero exit, or a signal arrives,
    SIGTERM the child group, then SIGKILL after 30 s;
 5. publish ``exit_node_XXX.json``; when every node exited cleanly, node 0 writes
    ``complete.json`` (the finite dataset was consumed).
+
+Generation protocol (files under the coordination directory):
+
+* ``LATEST`` (JSON ``{generation, nodes}``): node 0 points it at a new random generation id each
+  time it starts; a changed node count is refused by every node;
+* ``generations/<id>/members/<rank>.json``: each node registers once per generation with a fresh
+  per-process token, by exclusive create (a second registration of the same node fails; a
+  sealed generation takes no registrations, it belongs to an earlier attempt);
+* ``generations/<id>/sealed.json``: node 0 seals the generation with every member's token once
+  all nodes registered. A node proceeds when the sealed list holds its own token, so a process
+  that registered in an older generation can never pass for a member of the current one; a node
+  that sees ``LATEST`` move on re-registers in the newer generation, and node 0 stops if another
+  controller replaced its generation.
 """
 
 from __future__ import annotations
@@ -27,40 +37,68 @@ import time
 import uuid
 from pathlib import Path
 
-from ..train.catalog import durable_json
 from ..utils.files import atomic_json, read_json
 
 
+def current_generation(root):
+    """``(generation, nodes)`` that ``LATEST`` names, or ``(None, None)`` before node 0 wrote it."""
+    latest = read_json(Path(root) / "LATEST")
+    return (latest["generation"], latest["nodes"]) if latest else (None, None)
+
+
+def _register(root, generation, node_rank, token):
+    members = Path(root) / "generations" / generation / "members"
+    members.mkdir(parents=True, exist_ok=True)
+    path = members / f"{node_rank:03d}.json"
+    try:
+        fd = os.open(path, os.O_WRONLY | os.O_CREAT | os.O_EXCL, 0o644)
+    except FileExistsError:
+        raise RuntimeError(f"node {node_rank} is already registered in generation {generation} "
+                           "by another process") from None
+    with os.fdopen(fd, "w") as handle:
+        json.dump(dict(token=token, pid=os.getpid()), handle)
+    return path
+
+
+def _seal_if_complete(root, generation, nodes):
+    gen = Path(root) / "generations" / generation
+    if (gen / "sealed.json").exists():
+        return
+    members = [read_json(gen / "members" / f"{r:03d}.json") for r in range(nodes)]
+    if all(m is not None for m in members):
+        atomic_json(gen / "sealed.json", dict(generation=generation, members=[m["token"] for m in members]))
+
+
 def join_attempt(root, node_rank, nodes, timeout=1800.0, interval=0.5):
+    """Block until every node joined one launch generation; returns its id."""
     root = Path(root)
     root.mkdir(parents=True, exist_ok=True)
     token = uuid.uuid4().hex
-    generation = uuid.uuid4().hex if node_rank == 0 else None
+    mine = None
     if node_rank == 0:
-        atomic_json(root / "current.json", dict(generation=generation, nodes=nodes))
-    deadline = time.monotonic() + timeout
-    acknowledged = None
-    while time.monotonic() < deadline:
-        current = read_json(root / "current.json")
-        if current is not None:
-            if current["nodes"] != nodes:
-                raise ValueError("restart node topology changed")
-            active = current["generation"]
-            if node_rank == 0 and active != generation:
-                raise RuntimeError("another controller replaced this launch generation")
-            if active != acknowledged:
-                atomic_json(root / f"ack_{node_rank:03d}.json", dict(generation=active, token=token))
-                acknowledged = active
-            cohort_path = root / "attempts" / active / "cohort.json"
+        mine = uuid.uuid4().hex
+        atomic_json(root / "LATEST", dict(generation=mine, nodes=nodes))
+    registered = None
+    give_up = time.monotonic() + timeout
+    while time.monotonic() < give_up:
+        generation, planned = current_generation(root)
+        if generation is not None:
+            if planned != nodes:
+                raise ValueError(f"the job was planned for {planned} nodes, this node expects {nodes}")
+            if mine is not None and generation != mine:
+                raise RuntimeError("another controller started a newer launch generation")
+            sealed_path = root / "generations" / generation / "sealed.json"
+            if generation != registered and not sealed_path.exists():
+                # a sealed generation belongs to an earlier attempt: wait for node 0 to start a new one
+                _register(root, generation, node_rank, token)
+                registered = generation
             if node_rank == 0:
-                peers = [read_json(root / f"ack_{i:03d}.json") for i in range(nodes)]
-                if all(p and p["generation"] == active for p in peers):
-                    atomic_json(cohort_path, dict(generation=active, members=[p["token"] for p in peers]))
-            cohort = read_json(cohort_path)
-            if cohort and cohort["members"][node_rank] == token:
-                return active
+                _seal_if_complete(root, generation, nodes)
+            sealed = read_json(sealed_path)
+            if sealed is not None and sealed["members"][node_rank] == token:
+                return generation
         time.sleep(interval)
-    raise TimeoutError("a platform restart did not start every node of the fixed-size job")
+    raise TimeoutError(f"not every node of the {nodes}-node job joined a launch generation within {timeout:.0f} s")
 
 
 def supervise(command, attempt, coordination, generation, node_rank, nodes, env=None, cwd=None, poll=0.5,
@@ -83,9 +121,9 @@ def supervise(command, attempt, coordination, generation, node_rank, nodes, env=
         old = {sig: signal.signal(sig, terminate) for sig in (signal.SIGTERM, signal.SIGINT)}
         try:
             while child.poll() is None:
-                current = read_json(Path(coordination) / "current.json")
+                latest, _ = current_generation(coordination)
                 peers = [read_json(attempt / f"exit_node_{i:03d}.json") for i in range(nodes)]
-                if stopped[0] or (current and current["generation"] != generation) or any(p and p["exit_code"] for p in peers):
+                if stopped[0] or (latest is not None and latest != generation) or any(p and p["exit_code"] for p in peers):
                     terminate()
                     try:
                         child.wait(timeout=grace)
@@ -111,7 +149,8 @@ def finish(output, attempt, generation, node_rank, nodes, timeout=1800.0, interv
             return 1
         if all(p is not None for p in peers):
             if node_rank == 0:
-                durable_json(Path(output) / "complete.json", dict(generation=generation, status="finite_dataset_complete"))
+                atomic_json(Path(output) / "complete.json", dict(generation=generation, status="finite_dataset_complete"),
+                            durable=True)
             return 0
         time.sleep(interval)
     raise TimeoutError("training exited but peer nodes did not complete")

@@ -5,7 +5,9 @@ rank writes ``rank_XXXXX.pt`` (step, config, tp_rank, topology, CPU and device R
 data cursor, optimizer shards, EMA shards), then rank 0 writes ``manifest.json`` (the commit
 marker) after a barrier. ``load`` requires the identical TP/DP topology, config and training
 state, restores model tensors (DP-broadcast from DP rank 0), optimizer shards, EMA and RNG.
-``initialize_model`` is the model-only new stage and may change TP by exact resharding.
+``initialize_model`` is the model-only new stage and may change TP by exact resharding. A resume
+compares a ``RunIdentity`` (world, topology, config, training state, EMA presence) of the
+manifest with the running job and reports every difference in one error.
 Reference: ``utils/checkpoint.py:15-204``. The device RNG is stored under ``device_rng``; the
 reference's ``npu_rng`` key is accepted on load for files written by it.
 """
@@ -14,6 +16,7 @@ from __future__ import annotations
 
 import json
 import os
+from dataclasses import dataclass, fields
 from pathlib import Path
 
 import torch
@@ -33,17 +36,6 @@ def _cpu(value):
     return value
 
 
-def _save_file(value, path):
-    path = Path(path)
-    tmp = path.with_name(path.name + ".tmp")
-    with tmp.open("wb") as handle:
-        torch.save(_cpu(value), handle)
-        handle.flush()
-        os.fsync(handle.fileno())
-    os.replace(tmp, path)
-    fsync_directory(path.parent)
-
-
 def topology():
     st = ps.state()
     return dict(world=st.world, tp=st.tp, dp=st.dp, pp=1, cp=1)
@@ -60,6 +52,77 @@ def _rank():
 
 def _world():
     return dist.get_world_size() if dist.is_initialized() else 1
+
+
+class _Files:
+    """Names and crash-safe writers of one checkpoint directory (schema 7 file layout)."""
+
+    def __init__(self, root):
+        self.root = Path(root)
+        self.manifest = self.root / "manifest.json"
+
+    def model(self, tp_rank):
+        return self.root / f"model_tp_{tp_rank:03d}.pt"
+
+    def rank(self, rank):
+        return self.root / f"rank_{rank:05d}.pt"
+
+    def begin(self):
+        if self.manifest.exists():
+            raise FileExistsError(f"{self.root} is already committed; a checkpoint is never overwritten")
+        self.root.mkdir(parents=True, exist_ok=True)
+
+    def write(self, path, value):
+        scratch = path.with_name(path.name + ".partial")
+        with scratch.open("wb") as handle:
+            torch.save(_cpu(value), handle)
+            handle.flush()
+            os.fsync(handle.fileno())
+        os.replace(scratch, path)
+        fsync_directory(self.root)
+
+    def commit(self, manifest):
+        durable_json(self.manifest, manifest)
+
+    def read_manifest(self):
+        return json.loads(self.manifest.read_text())
+
+    def load(self, path):
+        return torch.load(path, map_location="cpu", weights_only=False)
+
+
+@dataclass
+class RunIdentity:
+    """What a restart must reproduce exactly: rank layout, model config, training schedule and
+    data identity, and whether a renderer EMA is kept."""
+
+    world: int
+    topology: dict
+    config: dict
+    training_state: object
+    ema: bool
+
+    @classmethod
+    def current(cls, config, training_state, ema):
+        return cls(_world(), topology(), config.to_dict(), training_state, ema is not None)
+
+    @classmethod
+    def saved(cls, manifest):
+        return cls(manifest.get("world"), manifest.get("topology"), manifest.get("config"),
+                   manifest.get("training_state"), "ema" in manifest)
+
+    def mismatches(self, now):
+        out = []
+        for f in fields(self):
+            then, current = getattr(self, f.name), getattr(now, f.name)
+            if then == current:
+                continue
+            if isinstance(then, dict) and isinstance(current, dict):
+                keys = sorted(k for k in then.keys() | current.keys() if then.get(k) != current.get(k))
+                out.append(f"{f.name} differs in {keys[:8]}")
+            else:
+                out.append(f"{f.name} was {then!r}, now {current!r}")
+        return out
 
 
 def validation_probes(model, optimizer):
@@ -83,31 +146,33 @@ def validation_probes(model, optimizer):
 
 
 def save(path, model, optimizer, step, config, training_state=None, data_state=None, ema=None):
-    root = Path(path)
-    if (root / "manifest.json").exists():
-        raise FileExistsError(f"refusing to overwrite a committed checkpoint: {root}")
-    root.mkdir(parents=True, exist_ok=True)
+    """Write this rank's shards; rank 0 commits the manifest once every rank has written."""
+    files = _Files(path)
+    files.begin()
     st = ps.state()
-    topo = topology()
-    if st.dp_rank == 0:
-        _save_file(model.state_dict(), root / f"model_tp_{st.tp_rank:03d}.pt")
-    payload = dict(step=step, config=config.to_dict(), tp_rank=st.tp_rank, topology=topo,
-                   cpu_rng=torch.get_rng_state(),
-                   device_rng=torch.cuda.get_rng_state() if torch.cuda.is_available() and st.device.type == "cuda" else None,
-                   schema=SCHEMA, data_state=data_state, optimizer=[optimizer.state_dict()])
+    identity = RunIdentity.current(config, training_state, ema)
+    if st.dp_rank == 0:                      # one model shard per TP rank
+        files.write(files.model(st.tp_rank), model.state_dict())
+    cuda = torch.cuda.is_available() and st.device.type == "cuda"
+    shard = dict(step=step, config=identity.config, tp_rank=st.tp_rank, topology=identity.topology,
+                 schema=SCHEMA, cpu_rng=torch.get_rng_state(), device_rng=torch.cuda.get_rng_state() if cuda else None,
+                 data_state=data_state, optimizer=[optimizer.state_dict()])
     if ema is not None:
-        payload["ema"] = ema.state_dict()
-    _save_file(payload, root / f"rank_{_rank():05d}.pt")
+        shard["ema"] = ema.state_dict()
+    files.write(files.rank(_rank()), shard)
     _barrier()
     if _rank() == 0:
-        files = {name: (root / name).stat().st_size for name in shard_names(_world(), topo["tp"])}
-        if any(size <= 0 for size in files.values()):
-            raise RuntimeError("cannot commit an incomplete checkpoint")
-        manifest = dict(schema=SCHEMA, step=step, world=_world(), topology=topo, config=config.to_dict(),
-                        training_state=training_state, files=files)
+        sizes = {}
+        for name in shard_names(identity.world, identity.topology["tp"]):
+            size = (files.root / name).stat().st_size
+            if size <= 0:
+                raise RuntimeError(f"{name} is empty; the checkpoint is not committed")
+            sizes[name] = size
+        manifest = dict(schema=SCHEMA, step=step, world=identity.world, topology=identity.topology,
+                        config=identity.config, training_state=training_state, files=sizes)
         if ema is not None:
             manifest["ema"] = ema.metadata()
-        durable_json(root / "manifest.json", manifest)
+        files.commit(manifest)
     _barrier()
 
 
@@ -122,46 +187,42 @@ def _broadcast_model(model):
 
 
 def load(path, model, optimizer, config, training_state=None, data_state_out=None, ema=None):
-    root = Path(path)
-    manifest = json.loads((root / "manifest.json").read_text())
+    """Restore a restart checkpoint; every incompatibility is collected and reported at once."""
+    files = _Files(path)
+    manifest = files.read_manifest()
+    shard = files.load(files.rank(_rank()))
+    problems = []
     if manifest.get("schema") != SCHEMA:
-        raise ValueError("unsupported checkpoint schema; refusing a partial optimizer restore")
-    if ("ema" in manifest) != (ema is not None):
-        raise ValueError("resume must preserve whether renderer EMA is enabled")
-    if manifest["world"] != _world() or manifest["topology"] != topology():
-        raise ValueError("resume requires the saved TP/DP topology")
-    if manifest["config"] != config.to_dict():
-        raise ValueError("resume model configuration differs from the checkpoint")
-    if manifest.get("training_state") != training_state:
-        raise ValueError("resume schedule, batch or data seed differs from the checkpoint")
-    saved = torch.load(root / f"rank_{_rank():05d}.pt", map_location="cpu", weights_only=False)
-    if saved.get("schema") != manifest["schema"]:
-        raise ValueError("checkpoint shard and manifest schemas disagree")
-    if ("ema" in saved) != ("ema" in manifest):
-        raise ValueError("renderer EMA shard and manifest disagree")
+        problems.append(f"schema {manifest.get('schema')!r} (this build reads {SCHEMA})")
+    if shard.get("schema") != manifest.get("schema"):
+        problems.append("the rank shard and the manifest carry different schemas")
+    problems += RunIdentity.saved(manifest).mismatches(RunIdentity.current(config, training_state, ema))
+    if ("ema" in shard) != ("ema" in manifest):
+        problems.append("the rank shard and the manifest disagree on the renderer EMA")
+    if data_state_out is not None and shard.get("data_state") is None:
+        problems.append("no consumed-data cursor was saved, so a corpus run cannot resume from it")
+    if len(shard.get("optimizer", ())) != 1:
+        problems.append("the optimizer partition differs")
+    if problems:
+        raise ValueError(f"cannot resume from {files.root}: " + "; ".join(problems))
     if data_state_out is not None:
-        if saved.get("data_state") is None:
-            raise ValueError("real-data resume needs a checkpoint with the consumed data state")
-        data_state_out.update(saved["data_state"])
+        data_state_out.update(shard["data_state"])
     st = ps.state()
     if st.dp_rank == 0:
-        state = torch.load(root / f"model_tp_{saved['tp_rank']:03d}.pt", map_location="cpu", weights_only=False)
         with torch.no_grad():
-            model.load_state_dict(state, strict=True)
+            model.load_state_dict(files.load(files.model(shard["tp_rank"])), strict=True)
     _broadcast_model(model)
-    if len(saved["optimizer"]) != 1:
-        raise ValueError("optimizer partition differs from the checkpoint")
-    device_state = {k: v for k, v in saved["optimizer"][0].items()}
-    optimizer.load_state_dict(_to_device(device_state, optimizer.shards[0]["master"].device))
+    device = optimizer.shards[0]["master"].device
+    optimizer.load_state_dict(_to_device(dict(shard["optimizer"][0]), device))
     if ema is not None:
-        ema.load_state_dict(_to_device(saved["ema"], optimizer.shards[0]["master"].device))
+        ema.load_state_dict(_to_device(shard["ema"], device))
         if ema.metadata() != manifest["ema"]:
-            raise ValueError("EMA metadata differs across checkpoint shards")
-    torch.set_rng_state(saved["cpu_rng"])
-    rng = saved.get("device_rng", saved.get("npu_rng"))
+            raise ValueError("the restored EMA's metadata differs from the manifest's")
+    torch.set_rng_state(shard["cpu_rng"])
+    rng = shard.get("device_rng", shard.get("npu_rng"))
     if rng is not None and torch.cuda.is_available() and st.device.type == "cuda":
         torch.cuda.set_rng_state(rng)
-    return saved["step"]
+    return shard["step"]
 
 
 def _to_device(value, device):

@@ -19,7 +19,7 @@ import torch.distributed as dist
 
 from ..parallel import state as ps
 from .catalog import durable_json
-from .checkpoint import _save_file, topology
+from .checkpoint import _Files, topology
 
 SCHEMA = "cq_eval_snapshot_v2"
 KIND = "inference_weights"
@@ -79,7 +79,8 @@ def save(path, model, step, config, ema=None, provenance=None):
         try:
             root.mkdir(parents=True, exist_ok=True)
             if st.dp_rank == 0:
-                _save_file(model.state_dict(), root / f"model_tp_{st.tp_rank:03d}.pt")
+                files = _Files(root)
+                files.write(files.model(st.tp_rank), model.state_dict())
         except Exception as exc:  # noqa: BLE001 - propagated collectively
             error = f"{type(exc).__name__}: {exc}"
         _gather_errors(error, "write")

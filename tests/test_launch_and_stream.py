@@ -24,12 +24,20 @@ def test_two_nodes_agree_on_one_generation(tmp_path):
     for t in threads:
         t.join()
     assert results[0] == results[1]
-    cohort = json.loads((tmp_path / "attempts" / results[0] / "cohort.json").read_text())
-    assert len(cohort["members"]) == 2
+    sealed = json.loads((tmp_path / "generations" / results[0] / "sealed.json").read_text())
+    assert len(sealed["members"]) == 2
+
+
+def test_second_registration_of_a_node_is_refused(tmp_path):
+    (tmp_path / "LATEST").write_text(json.dumps(dict(generation="g", nodes=2)))
+    (tmp_path / "generations" / "g" / "members").mkdir(parents=True)
+    (tmp_path / "generations" / "g" / "members" / "001.json").write_text(json.dumps(dict(token="other")))
+    with pytest.raises(RuntimeError, match="already registered"):
+        supervisor.join_attempt(tmp_path, 1, 2, timeout=5, interval=0.05)
 
 
 def test_topology_change_is_rejected(tmp_path):
-    (tmp_path / "current.json").write_text(json.dumps(dict(generation="g", nodes=3)))
+    (tmp_path / "LATEST").write_text(json.dumps(dict(generation="g", nodes=3)))
     with pytest.raises(ValueError):
         supervisor.join_attempt(tmp_path, 1, 2, timeout=5, interval=0.05)
 
@@ -37,7 +45,7 @@ def test_topology_change_is_rejected(tmp_path):
 def test_peer_failure_stops_the_local_child(tmp_path):
     attempt = tmp_path / "attempt"
     attempt.mkdir()
-    (tmp_path / "current.json").write_text(json.dumps(dict(generation="g", nodes=2)))
+    (tmp_path / "LATEST").write_text(json.dumps(dict(generation="g", nodes=2)))
     (attempt / "exit_node_001.json").write_text(json.dumps(dict(exit_code=1)))
     code = supervisor.supervise([sys.executable, "-c", "import time; time.sleep(60)"], attempt, tmp_path, "g", 0, 2,
                                 poll=0.05, grace=5)
@@ -48,7 +56,7 @@ def test_peer_failure_stops_the_local_child(tmp_path):
 def test_clean_exit_marks_complete(tmp_path):
     attempt = tmp_path / "attempt"
     attempt.mkdir()
-    (tmp_path / "current.json").write_text(json.dumps(dict(generation="g", nodes=1)))
+    (tmp_path / "LATEST").write_text(json.dumps(dict(generation="g", nodes=1)))
     code = supervisor.supervise([sys.executable, "-c", "pass"], attempt, tmp_path, "g", 0, 1, poll=0.05)
     assert code == 0
     assert supervisor.finish(tmp_path, attempt, "g", 0, 1, timeout=5) == 0
@@ -114,3 +122,18 @@ def test_committed_yaml_configs_load_and_validate():
     assert cfg.width == 2048 and training["sequence_length"] == 8192 and "PYTORCH_CUDA_ALLOC_CONF" in env
     tiny, _, _ = load_sections(root / "tiny.yaml")
     assert tiny.to_dict() == tiny_config().to_dict()
+
+
+def test_launcher_receipts_must_agree(tmp_path):
+    mine = launcher.Receipt("a", "10.0.0.1", "eth0", {"x.py": "1", "y.py": "2"}, 8)
+    other = launcher.Receipt("b", "10.0.0.2", "eth0", {"x.py": "1", "y.py": "3"}, 4)
+    problems = launcher.disagreements([mine, other], mine)
+    assert len(problems) == 2 and "y.py" in problems[1] and "4 processes" in problems[0]
+    r = launcher.Rendezvous(tmp_path / "r", 2, 0)
+    r.publish(mine)
+    with pytest.raises(FileExistsError):
+        r.publish(mine)
+    launcher.Rendezvous(tmp_path / "r", 2, 1).publish(other)
+    assert [x.hostname for x in r.collect(timeout=5)] == ["a", "b"]
+    env = launcher.launch_environment({"RANK": "3", "PATH": "/bin"}, "10.0.0.1", 29500, "eth0")
+    assert "RANK" not in env and env["NCCL_SOCKET_IFNAME"] == "eth0" and env["MASTER_ADDR"] == "10.0.0.1"
