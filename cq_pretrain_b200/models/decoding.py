@@ -66,7 +66,7 @@ def _attention_step(layer, x, rope, cache):
     q, gate = layer.q_proj(x).reshape(2, cfg.heads, 2 * cfg.head_dim).chunk(2, -1)
     q = layer.q_norm(q)
     if cfg.qwen_fused_projections:
-        k, v = layer.kv_proj(x[:1]).reshape(1, cfg.kv_heads, 2 * cfg.head_dim).chunk(2, -1)
+        k, v = (t.reshape(1, cfg.kv_heads, cfg.head_dim) for t in layer.kv_proj(x[:1]).chunk(2, -1))
     else:
         k = layer.k_proj(x[:1]).reshape(1, cfg.kv_heads, cfg.head_dim)
         v = layer.v_proj(x[:1]).reshape(1, cfg.kv_heads, cfg.head_dim)
@@ -91,7 +91,7 @@ def _attention_step_static(layer, x, rope, cache, count, starts):
     q, gate = layer.q_proj(x).reshape(2, cfg.heads, 2 * cfg.head_dim).chunk(2, -1)
     q = layer.q_norm(q)
     if cfg.qwen_fused_projections:
-        k, v = layer.kv_proj(x[:1]).reshape(1, cfg.kv_heads, 2 * cfg.head_dim).chunk(2, -1)
+        k, v = (t.reshape(1, cfg.kv_heads, cfg.head_dim) for t in layer.kv_proj(x[:1]).chunk(2, -1))
     else:
         k = layer.k_proj(x[:1]).reshape(1, cfg.kv_heads, cfg.head_dim)
         v = layer.v_proj(x[:1]).reshape(1, cfg.kv_heads, cfg.head_dim)

@@ -199,7 +199,8 @@ class GatedAttention(nn.Module):
             # q/gate over all rows and k/v over the content rows share one in-kernel all-gather
             qg, kv = PL.column_pair(x, self.q_proj, self.kv_proj, rows2=s)
             q, gate = qg.reshape(-1, hq, 2 * hd).chunk(2, -1)
-            k, v = kv.reshape(s, hkv, 2 * hd).chunk(2, -1)
+            # kv_proj = [k_proj; v_proj] (all key heads, then all value heads)
+            k, v = (t.reshape(s, hkv, hd) for t in kv.chunk(2, -1))
         else:
             xg = PL.gather_rows(x) if tp > 1 else x
             q, gate = self.q_proj(xg, gathered=True).reshape(-1, hq, 2 * hd).chunk(2, -1)

@@ -56,7 +56,7 @@ class WanRMSNorm(nn.Module):
             return N.rms_norm(x.contiguous(), self.weight - 1, self.eps)
         sq = x.float().square().sum(-1, keepdim=True)
         if ps.tp_size() > 1:
-            sq = PL.reduce_tp(sq)
+            sq = PL.sum_tp(sq)     # every rank normalises its own heads with the full-width sum
         variance = sq / (x.shape[-1] * ps.tp_size())
         return (x.float() * torch.rsqrt(variance + self.eps)).to(x.dtype) * self.weight.to(x.dtype)
 

@@ -20,6 +20,10 @@ Layout (reference ``distributed/megatron.py:210-240`` used Megatron DDP + distri
   sequences (reference ``distributed/communication.py:12-116``). With ``overlap=True`` a
   bucket launches during backward once every parameter reported its gradient (counts learned
   on the first step; ``suspend_readiness`` keeps non-final DiT chunks from triggering it).
+* with ``overlap_param_gather`` (default under NCCL with DP > 1; the reference's
+  ``overlap_param_gather=True``) the bf16 parameter all-gather after the update is left running:
+  buckets are issued in forward order and forward pre-hooks make the compute stream wait for a
+  bucket only when the first module reading it is about to run.
 
 The grad-norm clip (1.0), betas (0.9, 0.95), eps 1e-8, decoupled weight decay (not on
 biases / 1-D parameters) and ``min_lr = 0.1 lr`` follow the reference optimizer config. On
@@ -47,6 +51,7 @@ class Bucket:
         self.handle = None
         self.launched = False
         self.counts = {}
+        self.gather = None        # pending parameter all-gather (work handle, source shard)
 
 
 class ParamGroup:
@@ -86,7 +91,7 @@ class ParamGroup:
 
 class DistributedOptimizer:
     def __init__(self, model, lr, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8, clip_grad=1.0,
-                 bucket_size=40_000_000, overlap=False, ema_prefix=None, ema_decay=None):
+                 bucket_size=40_000_000, overlap=False, ema_prefix=None, ema_decay=None, overlap_param_gather=None):
         st = ps.state()
         self.model = model
         self.lr, self.weight_decay, self.betas, self.eps, self.clip_grad = lr, weight_decay, betas, eps, clip_grad
@@ -138,6 +143,10 @@ class DistributedOptimizer:
         self.learned = False
         self.suspended = 0
         self.next_bucket = 0
+        if overlap_param_gather is None:
+            overlap_param_gather = self.dp > 1 and dist.get_backend(self.dp_group) == "nccl"
+        self.overlap_param_gather = bool(overlap_param_gather)
+        self._gather_hooks = self._install_gather_hooks(model) if self.overlap_param_gather else []
         for p in self.names:
             p._grad_ready = self._mark
             if not getattr(p, "_direct_main_grad", False):
@@ -256,7 +265,9 @@ class DistributedOptimizer:
 
     @torch.no_grad()
     def step(self, lr=None, ema_decay=None):
-        """Average, clip, AdamW-update owned shards, optional EMA, then all-gather parameters."""
+        """Average, clip, AdamW-update owned shards, optional EMA, then all-gather parameters
+        (asynchronously when ``overlap_param_gather``: the next forward waits per bucket)."""
+        self.wait_params()      # the update writes into buffers a pending gather may still fill
         lr = self.lr if lr is None else lr
         self.step_count += 1
         scale = 1.0 / self.dp
@@ -286,7 +297,7 @@ class DistributedOptimizer:
                 p.mul_(1 - lr * self.weight_decay * s["decay"].float())
                 p.add_(update, alpha=-lr)
                 out.copy_(p)
-        self.all_gather_params()
+        self.all_gather_params(blocking=not self.overlap_param_gather)
         return finite, norm
 
     def attach_ema(self, ema):
@@ -319,20 +330,66 @@ class DistributedOptimizer:
                 out[6].append(shadow)
         return out
 
-    def all_gather_params(self):
+    def all_gather_params(self, blocking=True):
+        """Publish every rank's updated shards to all DP ranks.
+
+        Buckets are issued in forward order (the reverse of the bucket order, which follows the
+        backward), so the first layers' parameters arrive first. With ``blocking=False`` the
+        gathers stay pending: the forward pre-hooks make the compute stream wait for a bucket
+        right before the first module that reads it, and ``wait_params`` waits for the rest."""
         if self.dp == 1:
             return
-        handles = []
-        for b in self.buckets:
+        self.wait_params()
+        for b in reversed(self.buckets):
             n = (b.end - b.start) // self.dp
             full = b.group.param_buffer[b.start:b.end]
             mine = full[self.dp_rank * n:(self.dp_rank + 1) * n].clone()
             if dist.get_backend(self.dp_group) == "gloo":
                 dist.all_gather(list(full.split(n)), mine, group=self.dp_group)
                 continue
-            handles.append(dist.all_gather_into_tensor(full, mine, group=self.dp_group, async_op=True))
-        for h in handles:
-            h.wait()
+            b.gather = (dist.all_gather_into_tensor(full, mine, group=self.dp_group, async_op=True), mine)
+        if blocking:
+            self.wait_params()
+
+    def _await(self, buckets):
+        for b in buckets:
+            if b.gather is not None:
+                b.gather[0].wait()      # stream-side wait: the host does not block
+                b.gather = None
+
+    def wait_params(self):
+        """Make the current stream wait for every pending parameter all-gather."""
+        self._await(self.buckets)
+
+    def _install_gather_hooks(self, model):
+        """Forward pre-hooks on the outermost modules whose parameters span at most two buckets
+        (and on every leaf module): each waits for its parameters' buckets. Parameters no hooked
+        module covers are waited for when the model itself is called."""
+        covered, hooks = set(), []
+
+        def add(module, buckets):
+            hooks.append(module.register_forward_pre_hook(lambda m, args, bs=tuple(buckets): self._await(bs)))
+
+        def visit(module):
+            params = [p for p in module.parameters() if p in self.param_bucket]
+            buckets = sorted({self.param_bucket[p].index for p in params})
+            children = list(module.children())
+            if buckets and module is not model and (not children or len(buckets) <= 2):
+                add(module, [self.buckets[i] for i in buckets])
+                covered.update(params)
+                return
+            for child in children:
+                visit(child)
+            direct = [p for p in module.parameters(recurse=False) if p in self.param_bucket]
+            if direct and module is not model:
+                add(module, sorted({self.param_bucket[p] for p in direct}, key=lambda b: b.index))
+                covered.update(direct)
+
+        visit(model)
+        rest = sorted({self.param_bucket[p] for p in self.param_bucket if p not in covered}, key=lambda b: b.index)
+        if rest:
+            add(model, rest)
+        return hooks
 
     # ---- checkpoint -------------------------------------------------------------------------
     def state_dict(self):
@@ -351,4 +408,4 @@ class DistributedOptimizer:
             b = s["bucket"]
             b.group.param_buffer[s["lo"]:s["lo"] + s["n"]].copy_(s["master"])
         self.step_count = state["step"]
-        self.all_gather_params()
+        self.all_gather_params(blocking=True)

@@ -96,7 +96,9 @@ class SplitRows(torch.autograd.Function):
 
 
 class ReduceTP(torch.autograd.Function):
-    """Sum over the TP group (forward) / identity (backward): partial statistics."""
+    """Sum over the TP group (forward) / identity (backward): partial sums whose result every rank
+    then uses identically (a loss, a replicated activation), so each rank's gradient of the sum is
+    already the full one."""
 
     @staticmethod
     def forward(ctx, x):
@@ -107,6 +109,28 @@ class ReduceTP(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad):
         return grad
+
+
+class SumTP(torch.autograd.Function):
+    """Sum over the TP group whose result each rank consumes differently (forward and backward
+    both sum): e.g. per-row partial statistics that every rank applies to its own columns, so the
+    gradient of the sum is the sum of every rank's contribution."""
+
+    @staticmethod
+    def forward(ctx, x):
+        x = x.clone()
+        dist.all_reduce(x, group=ps.state().tp_group)
+        return x
+
+    @staticmethod
+    def backward(ctx, grad):
+        grad = grad.clone()
+        dist.all_reduce(grad, group=ps.state().tp_group)
+        return grad
+
+
+def sum_tp(x):
+    return SumTP.apply(x) if ps.tp_size() > 1 else x
 
 
 class CopyToTP(torch.autograd.Function):

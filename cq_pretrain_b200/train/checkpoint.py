@@ -150,6 +150,8 @@ def save(path, model, optimizer, step, config, training_state=None, data_state=N
     files = _Files(path)
     files.begin()
     st = ps.state()
+    if hasattr(optimizer, "wait_params"):
+        optimizer.wait_params()             # parameters of the last update must have arrived
     identity = RunIdentity.current(config, training_state, ema)
     if st.dp_rank == 0:                      # one model shard per TP rank
         files.write(files.model(st.tp_rank), model.state_dict())

@@ -87,6 +87,7 @@ class RendererEMA:
 
     @torch.no_grad()
     def _publish(self):
+        self.optimizer.wait_params()
         for s in self.optimizer.shards:
             b = s["bucket"]
             b.group.param_buffer[s["lo"]:s["lo"] + s["n"]].copy_(s["master"])

@@ -24,12 +24,19 @@ def compose_losses(outputs, cfg, scales=None):
     return dict(outputs, loss=loss, image_loss=image)
 
 
+def scales_from_counts(local_text, local_images, total_text, total_images, dp_size):
+    """``(s_t, s_i)`` of one micro-batch: its share of all supervised text tokens / generation
+    images summed over DP ranks and accumulation steps, times the DP size (the DP gradient is
+    averaged over ranks). An objective with no global targets gets scale 0."""
+    s_t = dp_size * local_text / total_text if total_text else 0.0
+    s_i = dp_size * local_images / total_images if total_images else 0.0
+    return s_t, s_i
+
+
 def loss_scales(local_text, local_images, dp_size, group=None, device="cpu"):
     """Return (s_t, s_i) from local counts; all-reduces the counts over ``group`` when DP > 1."""
     counts = torch.tensor([float(local_text), float(local_images)], dtype=torch.float64, device=device)
     if dp_size > 1:
         dist.all_reduce(counts, group=group)
     total_text, total_images = counts.tolist()
-    s_t = dp_size * local_text / total_text if total_text else 0.0
-    s_i = dp_size * local_images / total_images if total_images else 0.0
-    return s_t, s_i
+    return scales_from_counts(local_text, local_images, total_text, total_images, dp_size)

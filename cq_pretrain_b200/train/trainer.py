@@ -28,7 +28,7 @@ from ..models.qwen35 import cast_for_training
 from ..parallel import state as ps
 from ..parallel.ddp import DistributedOptimizer
 from .ema import RendererEMA
-from .loss import compose_losses
+from .loss import compose_losses, scales_from_counts
 from .renderer_schedule import backward_deferred_renderer
 from .schedule import learning_rate
 
@@ -109,8 +109,8 @@ class Trainer:
         for i, host in enumerate(device_batches):
             # Global-average weights: each micro-batch's mean losses count by its share of all
             # text targets / generation images across DP ranks and accumulation steps.
-            scales = (dp * int(host.text_indices.numel()) / max(1.0, total_text),
-                      dp * host.generation_image_count / max(1.0, total_img))
+            scales = scales_from_counts(int(host.text_indices.numel()), host.generation_image_count, total_text,
+                                        total_img, dp)
             ctx = self.optimizer.no_sync() if i + 1 < ga else nullcontext()
             with ctx:
                 losses = self._micro(host, scales, 1.0)
