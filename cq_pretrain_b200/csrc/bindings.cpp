@@ -65,7 +65,9 @@ std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at
                                    int64_t max_rows, int64_t epoch, int64_t total_dim);
 // gdn.cu
 std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
-                                at::Tensor start, at::Tensor count);
+                                at::Tensor start, at::Tensor count, bool want_final);
+void gdn_decode_step(at::Tensor state, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
+                     at::Tensor out);
 at::Tensor gdn_bwd(at::Tensor dO, at::Tensor W, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                    at::Tensor start, at::Tensor count);
 // moss.cu
@@ -145,7 +147,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_rms_fwd", &cqb::tp_rms_fwd);
   m.def("ce_combine_tp", &cqb::ce_combine_tp);
   m.def("tp_rms_bwd", &cqb::tp_rms_bwd);
-  m.def("gdn_fwd", &cqb::gdn_fwd);
+  m.def("gdn_fwd", &cqb::gdn_fwd, py::arg("W"), py::arg("U"), py::arg("P"), py::arg("Qd"), py::arg("Kt"),
+        py::arg("gamma"), py::arg("start"), py::arg("count"), py::arg("want_final") = false);
+  m.def("gdn_decode_step", &cqb::gdn_decode_step);
   m.def("gdn_bwd", &cqb::gdn_bwd);
   m.def("moss_pointwise_fwd", &cqb::moss_pointwise_fwd);
   m.def("moss_pointwise_bwd", &cqb::moss_pointwise_bwd);

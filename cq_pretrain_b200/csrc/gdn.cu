@@ -83,6 +83,7 @@ struct GdnArgs {
   const int* chunk_count;   // [docs]
   __nv_bfloat16* out;       // forward: O [Nc, H, C, DV] bf16
   float* states;            // [Nc, H, DK, DV] fp32: S entering (fwd) / dS entering from the right (bwd)
+  float* final;             // forward, optional: [docs, H, DK, DV] fp32 state after each document
   int H, DV;
 };
 
@@ -122,7 +123,12 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_fwd_kernel(GdnArgs a) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int c0 = a.chunk_start[doc], nc = a.chunk_count[doc];
-  if (nc == 0) return;
+  if (nc == 0) {
+    if (a.final)   // an empty document leaves the zero state
+      for (int i = tid; i < DK * BV; i += THREADS)
+        a.final[(((size_t)doc * a.H + h) * DK + i / BV) * a.DV + v0 + i % BV] = 0.f;
+    return;
+  }
   // state rows [16*warp, 16*warp+16) x BV columns, 8 n-tiles
   float st[BV / 8][4];
 #pragma unroll
@@ -238,6 +244,15 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_fwd_kernel(GdnArgs a) {
     __syncthreads();  // every read of s_bf (steps 1, 3) is done
 #pragma unroll
     for (int j = 0; j < BV / 8; ++j) store_acc_bf16(s_bf, warp * 16, j * 8, LDV, st[j], lane);
+  }
+  if (a.final) {   // prefill: the fp32 state leaving the document's last chunk
+    float* dst = a.final + ((size_t)doc * a.H + h) * DK * a.DV;
+#pragma unroll
+    for (int j = 0; j < BV / 8; ++j) {
+      const int col = v0 + j * 8 + 2 * t;
+      *reinterpret_cast<float2*>(dst + (size_t)(warp * 16 + g) * a.DV + col) = make_float2(st[j][0], st[j][1]);
+      *reinterpret_cast<float2*>(dst + (size_t)(warp * 16 + g + 8) * a.DV + col) = make_float2(st[j][2], st[j][3]);
+    }
   }
 }
 
@@ -385,20 +400,27 @@ void set_smem(const void* fn) {
 
 }  // namespace
 
-// Returns (O [Nc,H,C,DV] bf16, S_entering [Nc,H,DK,DV] fp32).
+// Returns (O [Nc,H,C,DV] bf16, S_entering [Nc,H,DK,DV] fp32) and, with want_final, the fp32 state
+// after each document [docs,H,DK,DV] (the prefill state of CQ decoding).
 std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt,
-                                at::Tensor gamma, at::Tensor start, at::Tensor count) {
+                                at::Tensor gamma, at::Tensor start, at::Tensor count, bool want_final) {
   GdnArgs a = make_args(W, Qd, Kt, P, U, gamma, start, count);
   auto O = at::empty_like(U);
   auto S = at::empty({W.size(0), W.size(1), DK, U.size(3)}, W.options().dtype(at::kFloat));
   a.out = (__nv_bfloat16*)O.data_ptr();
   a.states = S.data_ptr<float>();
+  at::Tensor F;
+  if (want_final) {
+    F = at::empty({start.size(0), W.size(1), DK, U.size(3)}, W.options().dtype(at::kFloat));
+    a.final = F.data_ptr<float>();
+  }
   static bool once = (set_smem((const void*)gdn_fwd_kernel), true);
   (void)once;
   dim3 grid(a.DV / BV, a.H, start.size(0));
   gdn_fwd_kernel<<<grid, THREADS, SMEM, stream()>>>(a);
   CQB_LAUNCH_CHECK();
   count_launch();
+  if (want_final) return {O, S, F};
   return {O, S};
 }
 

@@ -149,3 +149,20 @@ def gdn_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), doc_leng
         used += n + 2
         k += 1
     return docs
+
+
+def decode_prompt(cfg, ids, length=None):
+    """One unsupervised text document ``ids`` planned for CQ decoding: its last token is the
+    placeholder of the first unknown token and the plan's only query reads it."""
+    from .plan import build_plan
+    doc = dict(id="prompt", elements=[dict(type="text", input_ids=np.asarray(ids), supervised=False)],
+               templated=False)
+    packer = Packer(ListDocuments([doc]), cfg, length or (len(ids) + 8))
+    batch, _ = packer.next()
+    s = len(ids)
+    batch.ids, batch.segments = batch.ids[:, :s], batch.segments[:, :s]
+    batch.sigma, batch.positions = batch.sigma[:, :s], batch.positions[:, :s]
+    batch.image_queries = batch.image_queries[:, :s]
+    batch.text_indices = torch.tensor([s - 1])
+    batch.mainline = build_plan(batch, cfg)
+    return batch

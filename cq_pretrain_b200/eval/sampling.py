@@ -88,7 +88,7 @@ def greedy_token(model, hidden):
     weight = model.embedding.weight if model.lm_head is None else model.lm_head.weight
     logits = F.linear(hidden.reshape(1, -1).to(weight.dtype), weight).float().flatten()
     local = int(logits.argmax())
-    pair = torch.tensor([float(logits[local]), float(local + ps.tp_rank() * weight.shape[0])], device=hidden.device)
+    pair = torch.tensor([float(logits[local].detach()), float(local + ps.tp_rank() * weight.shape[0])], device=hidden.device)
     if ps.tp_size() > 1:
         pairs = [torch.empty_like(pair) for _ in range(ps.tp_size())]
         dist.all_gather(pairs, pair, group=ps.state().tp_group)

@@ -21,6 +21,7 @@ import torch
 import torch.nn.functional as F
 
 from ..data.plan import mrope_tables
+from ..ops import gdn as GDN
 from ..ops import reference as R
 
 
@@ -50,14 +51,8 @@ def _delta_step(layer, x, cache):
     ctrl = torch.float64 if x.dtype == torch.float64 else torch.float32
     g = -layer.A_log.to(ctrl).exp() * F.softplus(a[:1].to(ctrl) + layer.dt_bias.to(ctrl))
     beta = b[:1].to(ctrl).sigmoid()
-    q = R.l2norm(q).to(ctrl) * d ** -0.5
-    k = R.l2norm(k).to(ctrl)
-    state = cache["state"][0].to(ctrl)        # [H, Dk, Dv]
-    state = state * g.exp()[0][:, None, None]
-    residual = v[0].to(ctrl) - torch.einsum("hkv,hk->hv", state, k[0])
-    state = state + k[0][:, :, None] * (residual * beta[0][:, None])[:, None, :]
-    cache["state"].copy_(state[None])
-    y = torch.einsum("hkv,bhk->bhv", state, q).to(x.dtype)
+    # fused recurrent step on the cached fp32 state [H, Dk, Dv] (in place; one kernel on CUDA)
+    y = GDN.decode_step(cache["state"][0], q, k[0], v[0], g[0], beta[0]).to(x.dtype)
     return layer.out_proj(layer.norm(y, z.reshape(2, h, d)).flatten(-2))
 
 

@@ -159,7 +159,7 @@ class GatedDelta(nn.Module):
         if cache is not None:
             if torch.is_grad_enabled():
                 raise ValueError("CQ state caching is inference-only")
-            y, state = R.chunk_gated_delta(q, k, v, g, beta, dp.event_bounds, final=True)
+            y, state = GDN.prefill(q, k, v, g, beta, dp.event_bounds)
             cache["state"] = state  # [docs, H, Dk, Dv]
             count = cfg.linear_conv_kernel - 1
             hist = raw.new_zeros(count, raw.shape[-1])

@@ -29,6 +29,35 @@ def gated_delta(q, k, v, g, beta, bounds, chunk=64):
     return R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk).to(v.dtype)
 
 
+def prefill(q, k, v, g, beta, bounds, chunk=64):
+    """Inference prefill: ``(outputs [E, H, Dv], final state per document [docs, H, Dk, Dv] fp32)``;
+    on CUDA the forward recurrence kernel writes the final states (reference
+    ``ops/gated_delta_net.py:293-312``)."""
+    if _kernel(q):
+        from .gdn_cuda import gated_delta_cuda
+        return gated_delta_cuda(q, k, v, g, beta, bounds, chunk, final=True)
+    y, state = R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk, final=True)
+    return y.to(v.dtype), state
+
+
+def decode_step(state, q, k, v, g, beta):
+    """One recurrent step of every head: ``state`` ``[H, Dk, Dv]`` (fp32, in place) takes the write
+    ``k [H, Dk]``, ``v [H, Dv]`` with log-decay ``g`` and ``beta`` ``[H]``; the rows of ``q``
+    ``[rows, H, Dk]`` read the updated state. q/k are raw (L2-normalised here). Returns fp32
+    ``[rows, H, Dv]`` (reference ``ops/gated_delta_net.py:315-352``)."""
+    if state.is_cuda and _ext.cuda_kernels_enabled() and _ext.has("gdn_decode_step") and state.shape[1] == 128 \
+            and state.shape[2] % 32 == 0 and q.shape[0] <= 4:
+        from .gdn_cuda import decode_step as cuda_step
+        return cuda_step(state, q, k, v, g, beta)
+    ctrl = state.dtype
+    qn = R.l2norm(q).to(ctrl) * q.shape[-1] ** -0.5
+    kn = R.l2norm(k).to(ctrl)
+    state.mul_(g.to(ctrl).exp()[:, None, None])
+    residual = v.to(ctrl) - torch.einsum("hkv,hk->hv", state, kn)
+    state.add_(kn[:, :, None] * (residual * beta.to(ctrl)[:, None])[:, None, :])
+    return torch.einsum("hkv,bhk->bhv", state, qn)
+
+
 def causal_conv_silu(x, weight, bounds):
     """Causal depthwise conv + SiLU per document over content order; x ``[n, C]``, weight ``[C, K]``."""
     if x.is_cuda and _ext.cuda_kernels_enabled() and hasattr(_ext.ops(), "conv_fwd") and x.dtype == torch.bfloat16:

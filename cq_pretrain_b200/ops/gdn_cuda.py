@@ -103,7 +103,7 @@ class _GatedDelta(torch.autograd.Function):
         V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
         G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
         W, U, P, Qd, Kt, gamma = ops.gdn_prep(Q, K, V, G, B)
-        O, S = ops.gdn_fwd(W, U, P, Qd, Kt, gamma, start, count)
+        O, S = ops.gdn_fwd(W, U, P, Qd, Kt, gamma, start, count, want_final=False)
         ctx.save_for_backward(q, k, v, g, beta, rq, rk, S)
         ctx.layout, ctx.chunk = layout, chunk
         return ops.chunk_scatter(O, keep, O, O, False, 1.0)
@@ -208,16 +208,48 @@ def _to_chunks(tensors, idx, pad, Nc, chunk, H):
     return out
 
 
-def gated_delta_cuda(q, k, v, g, beta, bounds, chunk=CHUNK):
-    """Event-ordered inputs -> event-ordered outputs ``[E, H, Dv]`` (bf16)."""
+def gated_delta_cuda(q, k, v, g, beta, bounds, chunk=CHUNK, final=False):
+    """Event-ordered inputs -> event-ordered outputs ``[E, H, Dv]`` (bf16). With ``final`` (prefill,
+    no autograd) also the fp32 state after each document ``[docs, H, Dk, Dv]``, produced by the
+    forward recurrence kernel itself."""
     E, H, Dk = q.shape
     Dv = v.shape[-1]
     if Dk != 128 or Dv != 128 or chunk != CHUNK:
+        if final:
+            y, state = R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk, final=True)
+            return y.to(v.dtype), state
         return R.chunk_gated_delta(q, k, v, g, beta, bounds, chunk).to(v.dtype)
     layout = _layout(tuple(int(x) for x in bounds), chunk, q.device)
     bf = torch.bfloat16
+    if final:
+        return _prefill(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(), g, beta, layout, chunk)
     return _GatedDelta.apply(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(), g, beta, layout,
                              chunk)
+
+
+@torch.no_grad()
+def _prefill(q, k, v, g, beta, layout, chunk):
+    idx, pad, keep, start, count, Nc = layout
+    E, H, Dk = q.shape
+    ops = _ext.ops()
+    Q = ops.chunk_gather(q, idx, Nc, True, Dk ** -0.5)[0]
+    K = ops.chunk_gather(k, idx, Nc, True, 1.0)[0]
+    V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
+    G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
+    W, U, P, Qd, Kt, gamma = ops.gdn_prep(Q, K, V, G, B)
+    O, _, state = ops.gdn_fwd(W, U, P, Qd, Kt, gamma, start, count, want_final=True)
+    return ops.chunk_scatter(O, keep, O, O, False, 1.0), state
+
+
+def decode_step(state, q, k, v, g, beta):
+    """One fused recurrent step for all heads (``csrc/gdn_decode.cu``): ``state`` fp32 ``[H, Dk, Dv]``
+    updated in place by the write of ``k``/``v`` (raw, L2-normalised inside), then every row of
+    ``q`` ``[rows, H, Dk]`` reads it. Returns fp32 ``[rows, H, Dv]``."""
+    f = torch.float32
+    out = torch.empty(q.shape[0], state.shape[0], state.shape[2], dtype=f, device=state.device)
+    _ext.ops().gdn_decode_step(state, q.to(f).contiguous(), k.to(f).contiguous(), v.to(f).contiguous(),
+                               g.to(f).contiguous(), beta.to(f).contiguous(), out)
+    return out
 
 
 _POSITIONS: dict = {}

@@ -6,7 +6,12 @@ exhausted), run ``Trainer.train_step``, then acknowledge the packs (the resumabl
 moves after a committed update), write ``steps.jsonl`` (step time = max over ranks, content
 tokens/s, peak memory, losses, grad norm, lr), and checkpoint / snapshot / prune on interval.
 Startup writes ``run.json`` (versions, topology, parameter counts, source digest); shutdown
-writes ``summary.json`` (mean / median / p95 over post-warm-up steps). ``--auto-resume`` restores
+writes ``summary.json`` (mean / median / p95 over post-warm-up steps) and, per rank,
+``backend_rank_XXXXX.json`` (native library path and sha256, devices, versions, launch counts).
+Every rank appends ``timing_rank_XXXXX.jsonl`` (step seconds, data-wait seconds, and with
+``--phase-timing`` forward / backward / optimizer milliseconds) and ``consumed_rank_XXXXX.jsonl``
+(acknowledged receipts); ``--profile`` records two steps after the warm-up with ``torch.profiler``
+and writes the traces after the process group is destroyed. ``--auto-resume`` restores
 the newest intact committed checkpoint (model, optimizer shards, EMA, RNG, data cursor).
 """
 
@@ -30,6 +35,10 @@ from . import catalog
 from . import checkpoint as ckpt
 from . import eval_snapshot
 from .trainer import Trainer
+from ..utils.observe import PhaseTimer, RankLog, StepProfiler, backend_provenance
+
+
+_LAST_PROFILER = None     # the profiler of the last run(), exported by main() after shutdown
 
 
 def _all_max(values, device):
@@ -65,7 +74,7 @@ def make_loader(cfg, length, synthetic, seed, dp_rank, dp, prefetch=2, state=Non
 
 def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/default"), training=None,
         synthetic="joint", checkpoint_interval=0, resume=False, global_batch=None, checkpoint_dir=None,
-        keep_checkpoints=2, warmup_steps=3, corpus=None, snapshot_interval=0):
+        keep_checkpoints=2, warmup_steps=3, corpus=None, snapshot_interval=0, phase_timing=False, profile=False):
     training = dict(training or {})
     output = Path(output)
     trainer = Trainer(cfg, tp=tp, lr=lr, warmup=int(training.get("lr_warmup_steps", 0)), total_steps=steps,
@@ -108,8 +117,12 @@ def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/
             source_digest=source_digest(), start_step=start_step), indent=2))
     rows = []
     step = start_step
+    logs = RankLog(output, st.rank)
+    profiler = StepProfiler(profile, wait=warmup_steps)
     while step < steps:
+        wait0 = time.perf_counter()
         group = [loader.next() for _ in range(grad_accum)]
+        data_wait = time.perf_counter() - wait0
         have = [g for g in group if g is not None]
         alive = _all_sum([float(len(have))], trainer.device)[0]
         if alive == 0:
@@ -118,14 +131,24 @@ def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/
             raise RuntimeError("a DP rank ran out of data before the others; padding graphs are not configured")
         torch.cuda.reset_peak_memory_stats() if trainer.device.type == "cuda" else None
         t0 = time.perf_counter()
-        metrics = trainer.train_step([loader.acquire(item) for item in have], prepared=True)
+        timer = PhaseTimer(trainer.device) if phase_timing else None
+        metrics = trainer.train_step([loader.acquire(item) for item in have], prepared=True, phases=timer)
         if trainer.device.type == "cuda":
             torch.cuda.synchronize()
         seconds = time.perf_counter() - t0
+        profiler.step()
         for item in have:
             loader.acknowledge(item.receipt)
+        logs.acknowledged(step + 1, [item.receipt for item in have])
+        phases = metrics.pop("phases", {})
+        logs.step(dict(step=step + 1, seconds=seconds, data_wait_seconds=data_wait, phases_ms=phases))
         peak = torch.cuda.max_memory_allocated() / 2 ** 30 if trainer.device.type == "cuda" else 0.0
-        seconds, peak = _all_max([seconds, peak], trainer.device)
+        names = sorted(phases)
+        worst = _all_max([seconds, peak, data_wait] + [phases[k] for k in names], trainer.device)
+        seconds, peak, data_wait = worst[:3]
+        metrics["data_wait_seconds"] = data_wait
+        if names:
+            metrics["phases_ms"] = dict(zip(names, worst[3:]))    # max over ranks, like the step time
         step += 1
         tokens = sum(item.receipt["body_tokens"] for item in have)
         total_tokens = _all_sum([float(tokens)], trainer.device, st.dp_group if dp > 1 else None)[0]
@@ -155,6 +178,12 @@ def run(cfg: RunConfig, tp=1, length=8192, steps=10, lr=5e-5, output=Path("runs/
         if snapshot_interval and step % snapshot_interval == 0:
             eval_snapshot.save(output / "snapshots" / f"step_{step:07d}", trainer.model, step, cfg, trainer.ema)
     loader.close()
+    profiler.stop()
+    provenance = backend_provenance()
+    provenance.update(rank=st.rank, device_loader=dict(loader.stats) if hasattr(loader, "stats") else None)
+    (output / f"backend_rank_{st.rank:05d}.json").write_text(json.dumps(provenance, indent=2))
+    global _LAST_PROFILER
+    _LAST_PROFILER = profiler
     timed = [r["seconds"] for r in rows if not r["warmup"]] or [r["seconds"] for r in rows]
     if rank0 and rows:
         ordered = sorted(timed)
@@ -184,6 +213,10 @@ def main(argv=None):
     parser.add_argument("--resume", action="store_true")
     parser.add_argument("--validation-probes", action="store_true",
                         help="write parameter/master/Adam probes after every update (not a speed run)")
+    parser.add_argument("--phase-timing", action="store_true",
+                        help="CUDA-event forward/backward/optimizer times per step (NVTX ranges for timelines)")
+    parser.add_argument("--profile", action="store_true",
+                        help="torch.profiler over two steps after the warm-up; traces written after shutdown")
     args = parser.parse_args(argv)
     cfg, training, environment = load_sections(args.config)
     if args.validation_probes:
@@ -196,10 +229,15 @@ def main(argv=None):
     run(cfg, tp=tp, length=length, steps=args.steps, lr=lr, output=Path(args.output), training=training,
         synthetic=args.synthetic, checkpoint_interval=args.checkpoint_interval, resume=args.resume,
         global_batch=args.global_batch, checkpoint_dir=args.checkpoint_dir, keep_checkpoints=args.keep_checkpoints,
-        corpus=args.corpus, snapshot_interval=args.snapshot_interval)
+        corpus=args.corpus, snapshot_interval=args.snapshot_interval, phase_timing=args.phase_timing,
+        profile=args.profile)
+    rank = dist.get_rank() if dist.is_initialized() else 0
     if dist.is_initialized():
         dist.barrier()
         ps.destroy()
+    profiler = _LAST_PROFILER
+    if profiler is not None:     # exported only now: a slow export cannot stall a collective
+        profiler.export(Path(args.output) / "profile" / f"rank_{rank:05d}.json")
 
 
 if __name__ == "__main__":

@@ -14,7 +14,11 @@ from contextlib import nullcontext
 import torch
 
 
-def backward_deferred_renderer(model, batch, losses, backward_scale=1.0, optimizer=None, *, image_factor):
+def backward_deferred_renderer(model, batch, losses, backward_scale=1.0, optimizer=None, *, image_factor,
+                               timer=None):
+    """``timer`` (``utils.observe.PhaseTimer``, optional) counts each chunk's DiT forward as
+    forward time and the backward passes as backward time."""
+    from ..utils.observe import phase
     conditions = losses.pop("image_conditions")
     parts = batch.generation.microbatches
     if not parts:
@@ -26,8 +30,10 @@ def backward_deferred_renderer(model, batch, losses, backward_scale=1.0, optimiz
         last = index + 1 == len(parts)
         context = optimizer.suspend_readiness() if (optimizer is not None and not last) else nullcontext()
         with context:
-            chunk_loss = model.renderer(leaf, part.bind(batch))
-            (chunk_loss * (image_factor * backward_scale)).backward()
+            with phase(timer, "forward"):
+                chunk_loss = model.renderer(leaf, part.bind(batch))
+            with phase(timer, "backward"):
+                (chunk_loss * (image_factor * backward_scale)).backward()
         image_loss.add_(chunk_loss.detach().float())
         if gradient is not None:
             if leaf.grad is None:
@@ -38,7 +44,8 @@ def backward_deferred_renderer(model, batch, losses, backward_scale=1.0, optimiz
     if gradient is not None:
         roots.append(conditions)
         upstream.append(gradient)
-    torch.autograd.backward(roots, upstream)
+    with phase(timer, "backward"):
+        torch.autograd.backward(roots, upstream)
     losses["loss"] = losses["loss"].detach() + image_loss * image_factor
     losses["text_loss"] = losses["text_loss"].detach()
     losses["image_loss"] = image_loss

@@ -31,6 +31,7 @@ from .ema import RendererEMA
 from .loss import compose_losses, scales_from_counts
 from .renderer_schedule import backward_deferred_renderer
 from .schedule import learning_rate
+from ..utils.observe import phase
 
 
 def build_model(cfg, device, seed=871, dtype=torch.bfloat16):
@@ -67,26 +68,29 @@ class Trainer:
             from ..parallel import symmetric
             symmetric.enable()
 
-    def _micro(self, batch, scales, backward_scale):
+    def _micro(self, batch, scales, backward_scale, timer=None):
         deferred = batch.generation is not None and bool(batch.generation.microbatches)
-        out = self.model(batch, compute_image_loss=not deferred)
-        losses = compose_losses(out, self.cfg, scales)
+        with phase(timer, "forward"):
+            out = self.model(batch, compute_image_loss=not deferred)
+            losses = compose_losses(out, self.cfg, scales)
         if deferred:
             image_factor = self.cfg.image_weight * scales[1]
             losses = backward_deferred_renderer(self.model, batch, losses, backward_scale, self.optimizer,
-                                                image_factor=image_factor)
+                                                image_factor=image_factor, timer=timer)
         else:
-            (losses["loss"] * backward_scale).backward()
+            with phase(timer, "backward"):
+                (losses["loss"] * backward_scale).backward()
         return losses
 
-    def train_step(self, micro_batches, timing=False, prepared=False):
+    def train_step(self, micro_batches, timing=False, prepared=False, phases=None):
         """``micro_batches``: list of (pinned host batch, receipt). Returns host-side metrics of the update.
 
         The step copies every micro-batch to the device, runs the update, and reads the loss back.
         With ``prepared=True`` the batches are already on the device (``data.device.DeviceLoader``
         copied them on its side stream). With ``timing`` it also reports ``compute_ms``: CUDA-event
         time from after the copies were issued to the end of the optimizer/EMA work (excludes the
-        host->device and device->host I/O).
+        host->device and device->host I/O). With a ``phases`` timer (``utils.observe.PhaseTimer``)
+        it also reports ``phases``: forward / backward / optimizer milliseconds (NVTX-ranged).
         """
         if prepared:
             device_batches = [batch for batch, _ in micro_batches]
@@ -113,15 +117,16 @@ class Trainer:
                                         total_img, dp)
             ctx = self.optimizer.no_sync() if i + 1 < ga else nullcontext()
             with ctx:
-                losses = self._micro(host, scales, 1.0)
+                losses = self._micro(host, scales, 1.0, phases)
             accumulated += torch.stack((losses["loss"].detach().float(),
                                         losses["text_loss"].detach().float() * scales[0],
                                         losses["image_loss"].detach().float() * scales[1]))
-        self.optimizer.finish_grad_sync()
-        lr = learning_rate(self.step_index, self.lr, self.warmup, self.total_steps, self.lr_style)
-        updated, norm = self.optimizer.step(lr)
-        if self.ema is not None:
-            self.ema.update()
+        with phase(phases, "optimizer"):
+            self.optimizer.finish_grad_sync()
+            lr = learning_rate(self.step_index, self.lr, self.warmup, self.total_steps, self.lr_style)
+            updated, norm = self.optimizer.step(lr)
+            if self.ema is not None:
+                self.ema.update()
         self.step_index += 1
         if events is not None:
             events[1].record()
@@ -132,6 +137,8 @@ class Trainer:
         out = dict(loss=loss, text_loss=text, image_loss=image, grad_norm=gnorm, lr=lr)
         if events is not None:
             out["compute_ms"] = events[0].elapsed_time(events[1])
+        if phases is not None:
+            out["phases"] = phases.collect()
         return out
 
 

@@ -93,3 +93,42 @@ def test_gdn_chunk_backward_matches_reference():
     for name, a, b in zip(("dQ", "dK", "dV", "dG", "dBeta"), got, want):
         rel = (a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)
         assert rel < 2e-2, (name, rel.item())
+
+
+@pytest.mark.parametrize("bounds", [(0, 200), (0, 37, 37, 300, 520)])
+def test_gdn_prefill_final_state_from_kernel(bounds):
+    """Prefill (K8): outputs and the per-document final state come from the forward recurrence
+    kernel; compared with the float64 chunked oracle (an empty document keeps the zero state)."""
+    from cq_pretrain_b200.ops import gdn as GDN
+    q, k, v, g, beta = _inputs(bounds[-1], 4, seed=3)
+    y, state = GDN.prefill(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g, beta, bounds)
+    ref_y, ref_state = R.chunk_gated_delta(q.double(), k.double(), v.double(), g.double(), beta.double(), bounds,
+                                           final=True)
+    assert state.dtype == torch.float32 and state.shape == ref_state.shape
+    rel = (state.double() - ref_state).norm() / ref_state.norm()
+    assert rel < 2e-2, rel.item()
+    rel_y = (y.double() - ref_y).norm() / ref_y.norm()
+    assert rel_y < 2e-2, rel_y.item()
+
+
+def test_gdn_decode_step_matches_fp32_reference():
+    """Fused recurrent decode step (K7) vs the float64 recurrence, three steps in a row."""
+    from cq_pretrain_b200.ops import gdn as GDN
+    torch.manual_seed(5)
+    H, dk, dv = 16, 128, 128
+    state = torch.randn(H, dk, dv, device="cuda") * 0.1
+    ref = state.double().clone()
+    for _ in range(3):
+        q = torch.randn(2, H, dk, device="cuda")
+        k = torch.randn(H, dk, device="cuda")
+        v = torch.randn(H, dv, device="cuda")
+        g = -torch.rand(H, device="cuda")
+        beta = torch.rand(H, device="cuda")
+        y = GDN.decode_step(state, q, k, v, g, beta)
+        qn = R.l2norm(q.double()) * dk ** -0.5
+        kn = R.l2norm(k.double())
+        ref = ref * g.double().exp()[:, None, None]
+        ref = ref + kn[:, :, None] * ((v.double() - torch.einsum("hkv,hk->hv", ref, kn)) * beta.double()[:, None])[:, None, :]
+        ref_y = torch.einsum("hkv,bhk->bhv", ref, qn)
+        assert (state.double() - ref).abs().max() < 1e-4
+        assert (y.double() - ref_y).abs().max() < 1e-4 * max(1.0, ref_y.abs().max().item())
