@@ -61,3 +61,37 @@ def test_image_reader_ranges_integrity_and_exif(tmp_path):
     with pytest.raises(ValueError):
         reader.read_bytes(dict(locator, offset=shard.stat().st_size))
     reader.close()
+
+
+def test_asset_preparer_pins_verifies_and_checks_upstream(tmp_path):
+    import hashlib
+    import json
+    from cq_pretrain_b200.utils import prepare_assets as PA
+    src = tmp_path / "src"
+    src.mkdir()
+    (src / "config.json").write_text(json.dumps(dict(vision_config=dict(patch_size=16, temporal_patch_size=2,
+                                                                        spatial_merge_size=2,
+                                                                        hidden_act="gelu_pytorch_tanh"))))
+    (src / "tokenizer.json").write_text("{}")
+    (src / "model.safetensors.index.json").write_text(json.dumps(dict(weight_map={"a": "m-1.safetensors",
+                                                                                  "b": "m-2.safetensors"})))
+    for n in ("m-1.safetensors", "m-2.safetensors"):
+        (src / n).write_bytes(n.encode() * 10)
+    model_id, rev = "Qwen/Qwen3.5-2B-Base", "b1485b2fa6dfa1287294f269f5fb618e03d52d7c"
+    lfs = {n: hashlib.sha256((src / n).read_bytes()).hexdigest() for n in ("m-1.safetensors", "m-2.safetensors")}
+    blob = hashlib.sha1(b"blob 2\0{}").hexdigest()
+    meta = dict(sha=rev, siblings=[dict(rfilename=n, lfs=dict(sha256=h)) for n, h in lfs.items()]
+                + [dict(rfilename="tokenizer.json", blobId=blob)])
+    (tmp_path / "meta.json").write_text(json.dumps(meta))
+    out = PA.pin(src, tmp_path / "pinned", model_id, rev, upstream=tmp_path / "meta.json", vision=True)
+    assert out["upstream_checked"] and set(out["files"]) >= {"config.json", "m-1.safetensors", "m-2.safetensors"}
+    assert PA.verify(tmp_path / "pinned", vision=True)["revision"] == rev
+    (tmp_path / "pinned" / "m-2.safetensors").write_bytes(b"tampered")
+    with pytest.raises(ValueError, match="changed"):
+        PA.verify(tmp_path / "pinned")
+    with pytest.raises(ValueError, match="not a pinned"):
+        PA.pin(src, tmp_path / "other", model_id, "0" * 40)
+    meta["siblings"][0]["lfs"]["sha256"] = "0" * 64
+    (tmp_path / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(ValueError, match="upstream"):
+        PA.pin(src, tmp_path / "third", model_id, rev, upstream=tmp_path / "meta.json")
