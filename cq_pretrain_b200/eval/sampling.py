@@ -7,7 +7,9 @@
   empty (non-CFG) condition (reference ``evaluations/sampling.py:264-334``).
 * ``caption``: prefill + CQ cached decoding with greedy argmax over the vocabulary-parallel
   LM head (TP all-gather of the local maxima, reference ``evaluations/sampling.py:204-260``).
-* ``run_suite``: evaluates a list of cases sharded over DP ranks and writes JSON + HTML.
+* ``run_suite``: evaluates a list of cases sharded over DP ranks and writes JSON, the media
+  (PNG / MP4 or animated WebP, ``eval/media.py``) and an HTML report; ``eval.media.reference_scores``
+  gives the teacher-forced text NLL and flow MSE of a case's reference targets.
 """
 
 from __future__ import annotations
@@ -115,7 +117,15 @@ def caption(model, prefill_batch, max_new_tokens=48, stops=()):
 
 
 def run_suite(model, cases, output, runner):
-    """Evaluate ``cases`` sharded over DP ranks; ``runner(model, case) -> dict``. Writes results + HTML."""
+    """Evaluate ``cases`` sharded over DP ranks (case i on DP rank i mod dp; every TP rank of a DP
+    group runs the same cases, as the TP collectives need); ``runner(model, case) -> dict``.
+
+    A runner result may carry ``visuals`` (a list of ``[T, H, W, 3]`` pixel arrays) or ``latents``
+    (``[C, T, H, W]``, written as previews when no decoder produced pixels): DP-rank leaders (TP
+    rank 0) save them under ``output/media`` as PNG (one frame) or MP4 / animated WebP and the
+    results list the file names. Rank 0 writes ``results.json`` and an HTML report that embeds the
+    media."""
+    from .media import latent_preview, save_visual
     output = Path(output)
     output.mkdir(parents=True, exist_ok=True)
     st = ps.state()
@@ -123,7 +133,19 @@ def run_suite(model, cases, output, runner):
     rows = []
     for case in mine:
         try:
-            rows.append(dict(id=case.get("id"), task=case.get("task"), **runner(model, case)))
+            result = dict(runner(model, case))
+            visuals = result.pop("visuals", None)
+            latents = result.pop("latents", None)
+            media = []
+            if st.tp_rank == 0:
+                frames = visuals if visuals is not None else [latent_preview(x) for x in (latents or [])]
+                for k, pixels in enumerate(frames):
+                    written = save_visual(pixels, output / "media" / f"{case.get('id')}_{k}")
+                    media.append(written.name)
+            if media:
+                result["media"] = media
+                result["media_kind"] = "decoded" if visuals is not None else "latent preview"
+            rows.append(dict(id=case.get("id"), task=case.get("task"), **result))
         except Exception as error:  # noqa: BLE001 - reported per case
             rows.append(dict(id=case.get("id"), task=case.get("task"), error=f"{type(error).__name__}: {error}"))
     gathered = [rows]
@@ -133,7 +155,16 @@ def run_suite(model, cases, output, runner):
     results = [r for part in gathered for r in part]
     if not dist.is_initialized() or dist.get_rank() == 0:
         (output / "results.json").write_text(json.dumps(results, indent=2, default=str))
+        def media_html(r):
+            tags = []
+            for name in r.get("media", []):
+                src = html.escape(f"media/{name}")
+                tags.append(f"<video src='{src}' controls loop></video>" if name.endswith(".mp4")
+                            else f"<img src='{src}' style='max-width:320px'>")
+            return "".join(tags)
+
         body = "".join(f"<section><h3>{html.escape(str(r.get('id')))} ({html.escape(str(r.get('task')))})</h3>"
+                       f"{media_html(r)}"
                        f"<pre>{html.escape(json.dumps({k: v for k, v in r.items() if k not in ('id', 'task')}, default=str))}</pre></section>"
                        for r in results)
         (output / "report.html").write_text(f"<!doctype html><meta charset='utf-8'><title>CQ validation</title>{body}")

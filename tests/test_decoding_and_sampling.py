@@ -89,3 +89,31 @@ def test_graphed_decode_matches_eager_cuda():
         rel = ((got - want).norm() / want.norm()).item()
         assert rel < 3e-2, (token, rel)
     assert graphed.graph is not None
+
+
+def test_suite_writes_media_and_reference_scores(tmp_path):
+    import json as _json
+    from cq_pretrain_b200.data.preparer import DevicePreparer
+    from cq_pretrain_b200.data.synthetic import synthetic_batch
+    from cq_pretrain_b200.eval.media import latent_preview, reference_scores, save_visual
+    from cq_pretrain_b200.parallel import state as ps
+    ps.initialize(1)
+    cfg = tiny_config()
+    model = JointModel(cfg).eval()
+    host, receipt = synthetic_batch(cfg, 512, seed=0, pad_multiple=8)
+    batch = DevicePreparer(cfg, torch.device("cpu"), torch.float32)(host, receipt)
+    scores = reference_scores(model, batch)
+    assert scores["text_nll"] > 0 and scores["flow_mse"] > 0 and scores["generation_targets"] == 2
+    png = save_visual(np.zeros((8, 8, 3), np.uint8), tmp_path / "still")
+    anim = save_visual(np.random.rand(4, 8, 8, 3), tmp_path / "clip", fps=4)
+    assert png.suffix == ".png" and png.exists() and anim.suffix in (".mp4", ".webp") and anim.exists()
+    preview = latent_preview(torch.randn(16, 2, 6, 6))
+    assert preview.shape == (2, 6, 6, 3) and preview.dtype == np.uint8
+
+    def runner(model_, case):
+        return dict(score=case["id"], latents=[torch.randn(16, 1, 4, 4)])
+
+    results = sampling.run_suite(model, [dict(id="a", task="t2i"), dict(id="b", task="t2v")], tmp_path / "suite", runner)
+    assert [r["media_kind"] for r in results] == ["latent preview"] * 2
+    report = (tmp_path / "suite" / "report.html").read_text()
+    assert "media/a_0.png" in report and _json.loads((tmp_path / "suite" / "results.json").read_text())[1]["id"] == "b"
