@@ -104,6 +104,13 @@ void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, 
 at::Tensor sum_squares(std::vector<at::Tensor> xs);
 }  // namespace cqb
 
+#ifdef CQB_DEBUG_BOUNDS
+namespace cqb {
+std::vector<int64_t> debug_status_gather(bool reset);
+std::vector<int64_t> debug_status_conv(bool reset);
+}  // namespace cqb
+#endif
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "cq_pretrain_b200 sm_100a kernels";
   m.def("launch_count", &cqb::launch_count);
@@ -138,6 +145,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &cqb::symm_free);
   m.def("symm_view", &cqb::symm_view);
   m.def("signal_wait", &cqb::signal_wait);
+#ifdef CQB_DEBUG_BOUNDS
+  // First out-of-range index seen by the checked kernels: {site, index, bound} (zeros when none).
+  m.def("debug_bounds_status", [](bool reset) {
+    for (auto* fn : {&cqb::debug_status_gather, &cqb::debug_status_conv}) {
+      auto v = fn(reset);
+      if (v[0] != 0) return v;
+    }
+    return std::vector<int64_t>{0, 0, 0};
+  }, py::arg("reset") = true);
+#endif
   m.def("gemm_scatter_reduce", &cqb::gemm_scatter_reduce, py::arg("x"), py::arg("w"), py::arg("w_mn_major"),
         py::arg("x2"), py::arg("w2"), py::arg("bias"), py::arg("peer_recv"), py::arg("my_recv"), py::arg("peer_flags"),
         py::arg("my_flags"), py::arg("flag_slots"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),

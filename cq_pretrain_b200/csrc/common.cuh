@@ -89,4 +89,36 @@ __device__ __forceinline__ void store8(float* p, const float* in) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
+// ---- debug bounds checks ----------------------------------------------------------------------
+// Built with -DCQB_DEBUG_BOUNDS (`python -m cq_pretrain_b200.build --debug`), CQB_IN_RANGE(i, n, site)
+// tests 0 <= i < n; the first failure of a translation unit is recorded in its status block
+// {site, index, bound} and the caller skips the access (no trap: the context stays usable and the
+// host reads the block through debug_bounds_status()). Release builds compile the checks away.
+#ifdef CQB_DEBUG_BOUNDS
+namespace dbg {
+static __device__ long long status[3];
+__device__ __forceinline__ bool in_range(long long i, long long n, int site) {
+  if (i >= 0 && i < n) return true;
+  if (atomicCAS(reinterpret_cast<unsigned long long*>(&status[0]), 0ull, (unsigned long long)site) == 0ull) {
+    status[1] = i;
+    status[2] = n;
+  }
+  return false;
+}
+}  // namespace dbg
+#define CQB_IN_RANGE(i, n, site) ::cqb::dbg::in_range((long long)(i), (long long)(n), (site))
+#define CQB_DEBUG_STATUS_READER(fn)                                                              \
+  std::vector<int64_t> fn(bool reset) {                                                          \
+    long long h[3] = {0, 0, 0};                                                                  \
+    CQB_CHECK_CUDA(cudaMemcpyFromSymbol(h, ::cqb::dbg::status, sizeof(h)));                       \
+    if (reset) {                                                                                 \
+      long long z[3] = {0, 0, 0};                                                                \
+      CQB_CHECK_CUDA(cudaMemcpyToSymbol(::cqb::dbg::status, z, sizeof(z)));                       \
+    }                                                                                            \
+    return {h[0], h[1], h[2]};                                                                   \
+  }
+#else
+#define CQB_IN_RANGE(i, n, site) true
+#endif
+
 }  // namespace cqb

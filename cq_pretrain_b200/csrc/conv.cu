@@ -341,13 +341,14 @@ __global__ void __launch_bounds__(256) qconv_bwd_hist_kernel(const float* __rest
 template <int D>
 __global__ void chunk_gather_kernel(const __nv_bfloat16* __restrict__ x, const long* __restrict__ idx,
                                     __nv_bfloat16* __restrict__ out, float* __restrict__ rnorm, int slots, int H,
-                                    float scale, int normalize) {
+                                    float scale, int normalize, long events) {
   static_assert(D == 16 * 8, "16 lanes x 8 elements per row");
   const long row = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 4;
   const int sub = threadIdx.x & 15;
   const bool valid = row < (long)slots * H;
   const int slot = valid ? (int)(row / H) : 0, h = valid ? (int)(row % H) : 0;
-  const long e = valid ? idx[slot] : -1;
+  long e = valid ? idx[slot] : -1;
+  if (e >= 0 && !CQB_IN_RANGE(e, events, 11)) e = -1;    // -1 marks a padding slot
   float v[8];
   if (e >= 0) {
     load8(x + ((size_t)e * H + h) * D + sub * 8, v);
@@ -377,14 +378,15 @@ __global__ void chunk_gather_kernel(const __nv_bfloat16* __restrict__ x, const l
 template <int D, typename T>
 __global__ void chunk_scatter_kernel(const T* __restrict__ dyc, const long* __restrict__ slot_of,
                                      const __nv_bfloat16* __restrict__ x, const float* __restrict__ rnorm,
-                                     __nv_bfloat16* __restrict__ dx, int events, int H, float scale, int normalize) {
+                                     __nv_bfloat16* __restrict__ dx, int events, int H, float scale, int normalize,
+                                     long slots) {
   static_assert(D == 16 * 8, "16 lanes x 8 elements per row");
   const long row = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 4;
   const int sub = threadIdx.x & 15;
   const bool valid = row < (long)events * H;
   const int e = valid ? (int)(row / H) : 0, h = valid ? (int)(row % H) : 0;
   float g[8];
-  if (valid) {
+  if (valid && CQB_IN_RANGE(slot_of[e], slots, 12)) {
     const long slot = slot_of[e];
     const int chunk = (int)(slot / 64), c = (int)(slot % 64);
     load8(dyc + (((size_t)chunk * H + h) * 64 + c) * D + sub * 8, g);
@@ -550,7 +552,7 @@ std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunk
   const size_t threads = (size_t)slots * H * 16;
   chunk_gather_kernel<128><<<blocks_for(threads), 256, 0, stream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), (const long*)idx.data_ptr(), (__nv_bfloat16*)out.data_ptr(),
-      r.data_ptr<float>(), slots, H, (float)scale, normalize ? 1 : 0);
+      r.data_ptr<float>(), slots, H, (float)scale, normalize ? 1 : 0, (long)x.size(0));
   CQB_LAUNCH_CHECK();
   count_launch();
   return {out, r};
@@ -577,15 +579,20 @@ at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::T
   const float* rp = normalize ? rnorm.data_ptr<float>() : nullptr;
   if (dyc.scalar_type() == at::kFloat)
     chunk_scatter_kernel<128, float><<<blocks_for(threads), 256, 0, stream()>>>(
-        dyc.data_ptr<float>(), so, xp, rp, (__nv_bfloat16*)dx.data_ptr(), E, H, (float)scale, normalize ? 1 : 0);
+        dyc.data_ptr<float>(), so, xp, rp, (__nv_bfloat16*)dx.data_ptr(), E, H, (float)scale, normalize ? 1 : 0,
+        (long)dyc.size(0) * 64);
   else
     chunk_scatter_kernel<128, __nv_bfloat16><<<blocks_for(threads), 256, 0, stream()>>>(
         (const __nv_bfloat16*)dyc.data_ptr(), so, xp, rp, (__nv_bfloat16*)dx.data_ptr(), E, H, (float)scale,
-        normalize ? 1 : 0);
+        normalize ? 1 : 0, (long)dyc.size(0) * 64);
   CQB_LAUNCH_CHECK();
   count_launch();
   return dx;
 }
+
+#ifdef CQB_DEBUG_BOUNDS
+CQB_DEBUG_STATUS_READER(debug_status_conv)
+#endif
 
 }  // namespace cqb
 

@@ -21,7 +21,8 @@ __global__ void gather_rows_kernel(const T* __restrict__ src0, long n0, long ld0
   for (long i = warp; i < m; i += ((long)gridDim.x * blockDim.x) >> 5) {
     const long s = idx[i];
     const uint4* from = nullptr;
-    if (s < n0) from = reinterpret_cast<const uint4*>(src0 + s * ld0);
+    if (!CQB_IN_RANGE(s, n0 + n1 + 1, 1)) {   // valid: a source row or the zero sentinel n0 + n1
+    } else if (s < n0) from = reinterpret_cast<const uint4*>(src0 + s * ld0);
     else if (s < n0 + n1) from = reinterpret_cast<const uint4*>(src1 + (s - n0) * ld1);
     uint4* to = reinterpret_cast<uint4*>(out + i * width);
     for (int v = lane; v < vecs; v += 32) to[v] = from ? __ldg(from + v) : make_uint4(0, 0, 0, 0);
@@ -43,7 +44,7 @@ __global__ void gather_rows_bwd_kernel(const T* __restrict__ grad, long m, const
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int l = 0; l < levels; ++l) {
         const long r = inv[(long)l * inv_stride + j];
-        if (r >= m) continue;
+        if (!CQB_IN_RANGE(r, m + 1, 2) || r >= m) continue;   // r == m: no reader at this level
         float v[8];
         load_any(grad + r * width + c, v);
 #pragma unroll
@@ -155,5 +156,9 @@ std::vector<at::Tensor> gather_rows_bwd(at::Tensor grad, at::Tensor inv, int64_t
   count_launch();
   return n1 ? std::vector<at::Tensor>{out0, out1} : std::vector<at::Tensor>{out0};
 }
+
+#ifdef CQB_DEBUG_BOUNDS
+CQB_DEBUG_STATUS_READER(debug_status_gather)
+#endif
 
 }  // namespace cqb

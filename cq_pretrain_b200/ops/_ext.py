@@ -17,8 +17,11 @@ from pathlib import Path
 
 import torch
 
-BUILD_DIR = Path(__file__).resolve().parents[1] / "_build"
-NAME = "cqb_kernels"
+_DEBUG = os.environ.get("CQB_DEBUG_BOUNDS", "0") == "1"
+# CQB_DEBUG_BOUNDS=1 selects the bounds-checked build (``python -m cq_pretrain_b200.build --debug``):
+# out-of-range indices in the checked kernels are recorded (``debug_bounds_status``) and skipped.
+BUILD_DIR = Path(__file__).resolve().parents[1] / ("_build_debug" if _DEBUG else "_build")
+NAME = "cqb_kernels_debug" if _DEBUG else "cqb_kernels"
 _MODULE = None
 _ERROR = None
 
