@@ -12,7 +12,7 @@ std::atomic<long long>& launch_counter() {
 long long launch_count() { return launch_counter().load(); }
 
 // rowops.cu
-std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps);
+std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, c10::optional<at::Tensor> add);
 std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
                                      c10::optional<at::Tensor> dres);
 std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w, double eps);
@@ -104,6 +104,10 @@ void adamw_step(std::vector<at::Tensor> masters, std::vector<at::Tensor> grads, 
 at::Tensor sum_squares(std::vector<at::Tensor> xs);
 }  // namespace cqb
 
+namespace cqb {
+void rows_accumulate(at::Tensor grad, at::Tensor order, at::Tensor starts, at::Tensor ids, at::Tensor out);
+}  // namespace cqb
+
 #ifdef CQB_DEBUG_BOUNDS
 namespace cqb {
 std::vector<int64_t> debug_status_gather(bool reset);
@@ -114,7 +118,7 @@ std::vector<int64_t> debug_status_conv(bool reset);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "cq_pretrain_b200 sm_100a kernels";
   m.def("launch_count", &cqb::launch_count);
-  m.def("rms_norm_fwd", &cqb::rms_norm_fwd);
+  m.def("rms_norm_fwd", &cqb::rms_norm_fwd, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("add") = py::none());
   m.def("rms_norm_bwd", &cqb::rms_norm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
         py::arg("dres") = py::none());
   m.def("gated_norm_fwd", &cqb::gated_norm_fwd);
@@ -145,6 +149,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &cqb::symm_free);
   m.def("symm_view", &cqb::symm_view);
   m.def("signal_wait", &cqb::signal_wait);
+  m.def("rows_accumulate", &cqb::rows_accumulate);
 #ifdef CQB_DEBUG_BOUNDS
   // First out-of-range index seen by the checked kernels: {site, index, bound} (zeros when none).
   m.def("debug_bounds_status", [](bool reset) {

@@ -55,6 +55,36 @@ __global__ void gather_rows_bwd_kernel(const T* __restrict__ grad, long m, const
   }
 }
 
+// out[ids[r]] += sum over k in [starts[r], starts[r + 1]) of grad[order[k]] (fp32 accumulate, one
+// warp per run of equal ids, rows summed in `order` order: deterministic). The embedding backward:
+// `order` sorts the token positions by id, so every run is one vocabulary row.
+template <typename T>
+__global__ void rows_accumulate_kernel(const T* __restrict__ grad, const long* __restrict__ order,
+                                       const long* __restrict__ starts, const long* __restrict__ ids, long runs,
+                                       long rows_out, float* __restrict__ out, int width) {
+  const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (long r = warp; r < runs; r += ((long)gridDim.x * blockDim.x) >> 5) {
+    const long id = ids[r];
+    if (id >= rows_out || !CQB_IN_RANGE(id, rows_out, 3)) continue;   // ids >= rows_out: other shards
+    float* dst = out + id * width;
+    for (int c = lane * 8; c < width; c += 256) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (long k = starts[r]; k < starts[r + 1]; ++k) {
+        float v[8];
+        load_any(grad + order[k] * width + c, v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += v[q];
+      }
+      float cur[8];
+      load8(dst + c, cur);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cur[q] += acc[q];
+      store8(dst + c, cur);
+    }
+  }
+}
+
 int gather_grid(long rows) {
   return (int)std::max<long>(1, std::min<long>((rows * 32 + 255) / 256, (long)sm_count() * 16));
 }
@@ -155,6 +185,30 @@ std::vector<at::Tensor> gather_rows_bwd(at::Tensor grad, at::Tensor inv, int64_t
   CQB_LAUNCH_CHECK();
   count_launch();
   return n1 ? std::vector<at::Tensor>{out0, out1} : std::vector<at::Tensor>{out0};
+}
+
+// out fp32 [rows_out, width] += per-run sums of grad rows (see rows_accumulate_kernel).
+void rows_accumulate(at::Tensor grad, at::Tensor order, at::Tensor starts, at::Tensor ids, at::Tensor out) {
+  TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.is_contiguous() && grad.size(1) % 8 == 0,
+              "rows_accumulate: contiguous [m, width] grad, width a multiple of 8");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.dim() == 2 && out.size(1) == grad.size(1),
+              "rows_accumulate: fp32 [rows, width] output");
+  for (auto* t : {&order, &starts, &ids})
+    TORCH_CHECK(t->scalar_type() == at::kLong && t->is_contiguous() && t->is_cuda(), "rows_accumulate: int64 indices");
+  const long runs = ids.numel();
+  TORCH_CHECK(starts.numel() == runs + 1, "rows_accumulate: starts must hold runs + 1 offsets");
+  if (!runs) return;
+  const int blocks = gather_grid(runs);
+  if (grad.scalar_type() == at::kBFloat16)
+    rows_accumulate_kernel<__nv_bfloat16><<<blocks, 256, 0, stream()>>>(
+        (const __nv_bfloat16*)grad.data_ptr(), order.data_ptr<int64_t>(), starts.data_ptr<int64_t>(),
+        ids.data_ptr<int64_t>(), runs, out.size(0), out.data_ptr<float>(), (int)grad.size(1));
+  else
+    rows_accumulate_kernel<float><<<blocks, 256, 0, stream()>>>(
+        grad.data_ptr<float>(), order.data_ptr<int64_t>(), starts.data_ptr<int64_t>(), ids.data_ptr<int64_t>(), runs,
+        out.size(0), out.data_ptr<float>(), (int)grad.size(1));
+  CQB_LAUNCH_CHECK();
+  count_launch();
 }
 
 #ifdef CQB_DEBUG_BOUNDS

@@ -19,10 +19,12 @@ constexpr int kWarps = 8;  // rows per 256-thread block in forward kernels
 template <typename T>
 __device__ __forceinline__ void load_vec(const T* p, float* out) { load8(p, out); }
 
+// With `add` (may be null): the normalised row is s = x + add, and s is also written to `sum`
+// (a residual add fused into the norm that follows it).
 template <int NV, typename T, typename WT>
 __global__ void __launch_bounds__(256) rms_fwd_kernel(const T* __restrict__ x, const WT* __restrict__ w,
                                                      T* __restrict__ y, float* __restrict__ rstd, int rows, int width,
-                                                     float eps) {
+                                                     float eps, const T* __restrict__ add, T* __restrict__ sum) {
   const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -34,6 +36,16 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const T* __restrict__ x, c
     const int c = (i * 32 + lane) * 8;
     if (c < width) {
       load_vec(xr + c, v[i]);
+      if (add != nullptr) {
+        float a[8];
+        load_vec(add + (size_t)row * width + c, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += a[j];
+        store8(sum + (size_t)row * width + c, v[i]);
+        if (sizeof(T) == 2) {   // normalise the bf16-rounded sum that the residual stream carries on
+          load_vec(sum + (size_t)row * width + c, v[i]);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
     }
@@ -561,25 +573,34 @@ void check_rows(const at::Tensor& x) {
 
 }  // namespace
 
-std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps) {
+// Returns (y, rstd), or with `add` (same shape as x) (y, rstd, x + add) where y normalises x + add.
+std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, c10::optional<at::Tensor> add) {
   check_rows(x);
   const int rows = x.size(0), width = x.size(1);
   auto y = at::empty_like(x);
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
-  if (!rows) return {y, rstd};
+  at::Tensor a, sum;
+  if (add && add->defined()) {
+    a = add->contiguous();
+    TORCH_CHECK(a.sizes() == x.sizes() && a.scalar_type() == x.scalar_type(), "rms_norm_fwd: add must match x");
+    sum = at::empty_like(x);
+  }
+  if (!rows) return a.defined() ? std::vector<at::Tensor>{y, rstd, sum} : std::vector<at::Tensor>{y, rstd};
   auto wc = w.contiguous();
   const int blocks = (rows + kWarps - 1) / kWarps;
   AT_DISPATCH_SWITCH(x.scalar_type(), "rms_norm_fwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
                        using T = __nv_bfloat16;
                        NV_DISPATCH(width, [&] {
+                         const T* ap = a.defined() ? (const T*)a.data_ptr() : nullptr;
+                         T* sp = a.defined() ? (T*)sum.data_ptr() : nullptr;
                          if (wc.scalar_type() == at::kFloat)
                            rms_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>(
                                (const T*)x.data_ptr(), wc.data_ptr<float>(), (T*)y.data_ptr(), rstd.data_ptr<float>(),
-                               rows, width, (float)eps);
+                               rows, width, (float)eps, ap, sp);
                          else
                            rms_fwd_kernel<NV, T, T><<<blocks, 256, 0, stream()>>>(
                                (const T*)x.data_ptr(), (const T*)wc.data_ptr(), (T*)y.data_ptr(), rstd.data_ptr<float>(),
-                               rows, width, (float)eps);
+                               rows, width, (float)eps, ap, sp);
                        });
                      }) AT_DISPATCH_CASE(at::kFloat, [&] {
                        using T = float;
@@ -587,11 +608,13 @@ std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps) {
                          auto wf = wc.to(at::kFloat);
                          rms_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>(
                              x.data_ptr<float>(), wf.data_ptr<float>(), y.data_ptr<float>(), rstd.data_ptr<float>(), rows,
-                             width, (float)eps);
+                             width, (float)eps, a.defined() ? a.data_ptr<float>() : nullptr,
+                             a.defined() ? sum.data_ptr<float>() : nullptr);
                        });
                      }));
   CQB_LAUNCH_CHECK();
   count_launch();
+  if (a.defined()) return {y, rstd, sum};
   return {y, rstd};
 }
 

@@ -47,6 +47,13 @@ class RMSNorm(nn.Module):
             return x, self(x)
         return N.rms_norm_residual(x, self.weight, self.eps)
 
+    def residual_add(self, x, branch):
+        """``(x + branch, norm(x + branch))``: the residual add fused into the norm on CUDA."""
+        if x.dtype == torch.float64:
+            s = x + branch
+            return s, self(s)
+        return N.add_rms_norm_residual(x, branch, self.weight, self.eps)
+
 
 class MLP(nn.Module):
     def __init__(self, cfg):
@@ -237,7 +244,7 @@ class QwenBlock(nn.Module):
             mixed = self.linear_attn(normed, plan, cache)
         else:
             mixed = self.self_attn(normed, rope, plan, cache)
-        hidden, normed = self.post_attention_layernorm.residual(hidden + mixed)
+        hidden, normed = self.post_attention_layernorm.residual_add(hidden, mixed)
         return hidden + self.mlp(normed)
 
 

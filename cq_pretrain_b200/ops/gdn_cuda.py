@@ -104,25 +104,23 @@ class _GatedDelta(torch.autograd.Function):
         G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
         W, U, P, Qd, Kt, gamma = ops.gdn_prep(Q, K, V, G, B)
         O, S = ops.gdn_fwd(W, U, P, Qd, Kt, gamma, start, count, want_final=False)
-        ctx.save_for_backward(q, k, v, g, beta, rq, rk, S)
+        # the backward reuses the chunk-layout inputs and the recurrence factors instead of
+        # gathering and recomputing them (about 0.45 GB per layer at 8K tokens and 16 heads)
+        ctx.save_for_backward(q, k, v, rq, rk, S, Q, K, V, G, B, W, P, Qd, Kt, gamma)
         ctx.layout, ctx.chunk = layout, chunk
+        ctx.g_dtype, ctx.beta_dtype = g.dtype, beta.dtype
         return ops.chunk_scatter(O, keep, O, O, False, 1.0)
 
     @staticmethod
     def backward(ctx, dout):
-        q, k, v, g, beta, rq, rk, S = ctx.saved_tensors
+        q, k, v, rq, rk, S, Q, K, V, G, B, W, P, Qd, Kt, gamma = ctx.saved_tensors
         idx, pad, keep, start, count, Nc = ctx.layout
         chunk = ctx.chunk
         E, H, Dk = q.shape
         ops = _ext.ops()
-        Q = ops.chunk_gather(q, idx, Nc, True, Dk ** -0.5)[0]
-        K = ops.chunk_gather(k, idx, Nc, True, 1.0)[0]
-        V = ops.chunk_gather(v, idx, Nc, False, 1.0)[0]
         dO = ops.chunk_gather(dout.to(torch.bfloat16).contiguous(), idx, Nc, False, 1.0)[0]
-        G, B = _to_chunks((g.float(), beta.float()), idx, pad, Nc, chunk, H)
-        W, U, P, Qd, Kt, gamma = ops.gdn_prep(Q, K, V, G, B)
         dS = ops.gdn_bwd(dO, W, P, Qd, Kt, gamma, start, count)
-        del W, U, P, Qd, Kt
+        del W, P, Qd, Kt
         dQ, dK, dV, dG, dB = ops.gdn_chunk_bwd(Q, K, V, dO, G, B, S, dS)
         del dS
 
@@ -132,7 +130,7 @@ class _GatedDelta(torch.autograd.Function):
         dq = ops.chunk_scatter(dQ, keep, q, rq, True, Dk ** -0.5)
         dk = ops.chunk_scatter(dK, keep, k, rk, True, 1.0)
         dv = ops.chunk_scatter(dV, keep, v, rk, False, 1.0)
-        return dq, dk, dv, back(dG).to(g.dtype), back(dB).to(beta.dtype), None, None
+        return dq, dk, dv, back(dG).to(ctx.g_dtype), back(dB).to(ctx.beta_dtype), None, None
 
 
 def chunk_backward_reference(Q, K, V, dO, G, B, S, dS, chunk=CHUNK):

@@ -58,6 +58,36 @@ class _RMSNormResidual(torch.autograd.Function):
         return dx, dw.to(weight.dtype), None
 
 
+class _AddRMSNormResidual(torch.autograd.Function):
+    """``(s, rms_norm(s))`` with ``s = x + branch`` computed in the norm's kernel; backward: one
+    kernel gives ``ds`` (norm gradient plus the residual gradient of ``s``), which is the gradient
+    of both ``x`` and ``branch``."""
+
+    @staticmethod
+    def forward(ctx, x, branch, weight, eps):
+        y, rstd, s = _ext.ops().rms_norm_fwd(x.contiguous(), weight.contiguous(), eps, branch.contiguous())
+        ctx.save_for_backward(s, weight, rstd)
+        return s, y
+
+    @staticmethod
+    def backward(ctx, dres, dy):
+        s, weight, rstd = ctx.saved_tensors
+        if dy is None:
+            return dres, dres, None, None
+        ds, dw = _ext.ops().rms_norm_bwd(dy.contiguous(), s, weight.contiguous(), rstd,
+                                         None if dres is None else dres.contiguous())
+        return ds, ds, dw.to(weight.dtype), None
+
+
+def add_rms_norm_residual(x, branch, weight, eps):
+    """``(x + branch, rms_norm(x + branch))`` (the reference's ``add_rms_norm``) for 2-D tensors
+    whose sum continues along the residual stream: one kernel each way."""
+    if (_use_kernel(x) and x.dim() == 2 and x.shape[-1] % 8 == 0 and x.is_contiguous() and branch.shape == x.shape
+            and branch.dtype == x.dtype):
+        return _AddRMSNormResidual.apply(x, branch, weight, eps)
+    return rms_norm_residual(x + branch, weight, eps)
+
+
 def rms_norm_residual(x, weight, eps):
     """``(x, rms_norm(x))`` for a 2-D ``x`` that is also a residual input (see ``_RMSNormResidual``)."""
     if _use_kernel(x) and x.dim() == 2 and x.shape[-1] % 8 == 0 and x.is_contiguous():

@@ -23,6 +23,7 @@ import torch.distributed as dist
 from torch import nn
 
 from . import state as ps
+from ..ops import _ext
 from ..ops import linear as L
 
 
@@ -304,11 +305,19 @@ class VocabEmbedding(nn.Module):
         mark_sharded(self.weight, 0)
 
     def partial(self, ids):
-        """This rank's masked lookup ``[n, width]`` (full rows, zero outside the local vocab range)."""
+        """This rank's masked lookup ``[n, width]`` (full rows, zero outside the local vocab range).
+
+        On CUDA the lookup is the row-gather kernel (ids outside this shard hit the zero sentinel)
+        and the backward adds each token id's rows straight into the FP32 ``main_grad`` rows it
+        touches (``rows_accumulate``: a deterministic sum per id), instead of building a dense
+        vocabulary gradient and adding it."""
         n = self.weight.shape[0]
         lo = ps.tp_rank() * n
         local = ids - lo
         owned = (local >= 0) & (local < n)
+        if (ids.is_cuda and self.weight.dtype == torch.bfloat16 and self.weight.shape[1] % 8 == 0
+                and _ext.has("rows_accumulate")):
+            return _EmbeddingLookup.apply(torch.where(owned, local, torch.full_like(local, n)), self.weight)
         out = nn.functional.embedding(local.clamp(0, n - 1), self.weight)
         if ps.tp_size() > 1:
             out = out * owned[:, None].to(out.dtype)
@@ -316,6 +325,35 @@ class VocabEmbedding(nn.Module):
 
     def forward(self, ids):
         return scatter_rows(self.partial(ids))
+
+
+class _EmbeddingLookup(torch.autograd.Function):
+    """``weight[index]`` with ``index == len(weight)`` reading a zero row."""
+
+    @staticmethod
+    def forward(ctx, index, weight):
+        ctx.save_for_backward(index)
+        ctx.weight = weight
+        return _ext.ops().gather_rows(weight, None, index.contiguous())
+
+    @staticmethod
+    def backward(ctx, grad):
+        (index,) = ctx.saved_tensors
+        weight = ctx.weight
+        order = torch.argsort(index, stable=True)
+        ids, counts = torch.unique_consecutive(index.index_select(0, order), return_counts=True)
+        starts = torch.zeros(ids.numel() + 1, dtype=torch.long, device=index.device)
+        torch.cumsum(counts, 0, out=starts[1:])
+        # the sentinel run (ids of other shards, == len(weight)) is skipped by the kernel
+        mg = getattr(weight, "main_grad", None)
+        target = mg if mg is not None else torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
+        _ext.ops().rows_accumulate(grad.contiguous(), order, starts, ids.contiguous(), target)
+        if mg is not None:
+            cb = getattr(weight, "_grad_ready", None)
+            if cb is not None:
+                cb(weight)
+            return None, None
+        return None, target.to(weight.dtype)
 
 
 def checkpoint_shard(value, parameter):

@@ -40,3 +40,32 @@ def test_rows_strided_source():
     out = GA.rows(view, idx)
     ref = torch.cat((src.float(), torch.zeros(1, 32, device="cuda")))[idx]
     torch.testing.assert_close(out.float(), ref)
+
+
+def test_embedding_lookup_and_sparse_main_grad_backward():
+    """Vocabulary embedding on CUDA: row-gather lookup with the zero sentinel for other shards' ids,
+    and the deterministic per-id accumulation into main_grad, vs F.embedding + a dense gradient."""
+    from cq_pretrain_b200.parallel import layers as PL
+    from cq_pretrain_b200.parallel import state as ps
+    ps.initialize(1)
+    torch.manual_seed(0)
+    emb = PL.VocabEmbedding(5000, 256).cuda().to(torch.bfloat16)
+    ids = torch.randint(0, 5000, (3000,), device="cuda")
+    ids[:500] = 7                                        # a heavily repeated id
+    grad = torch.randn(3000, 256, device="cuda").to(torch.bfloat16)
+    ref_w = emb.weight.detach().float().requires_grad_()
+    ref = torch.nn.functional.embedding(ids, ref_w)
+    ref.backward(grad.float())
+    out = emb.partial(ids)
+    torch.testing.assert_close(out.float(), ref.detach())
+    out.backward(grad)                                   # no main_grad: a dense gradient comes back
+    torch.testing.assert_close(emb.weight.grad.float(), ref_w.grad, rtol=2e-2, atol=2e-2)
+    emb.weight.grad = None
+    emb.weight.main_grad = torch.full((5000, 256), 0.5, device="cuda")
+    emb.partial(ids).backward(grad)                      # with main_grad: accumulated in place
+    assert emb.weight.grad is None
+    torch.testing.assert_close(emb.weight.main_grad - 0.5, ref_w.grad, rtol=1e-4, atol=1e-3)
+    first = emb.weight.main_grad.clone()
+    emb.weight.main_grad.fill_(0.5)
+    emb.partial(ids).backward(grad)
+    assert torch.equal(first, emb.weight.main_grad)      # deterministic
