@@ -116,6 +116,17 @@ class Attention(nn.Module):
         return self.o(y.flatten(1))
 
 
+_ONES: dict = {}
+
+
+def _ones(width, device):
+    """A cached fp32 ``[1, width]`` ones row (the gate of an ungated residual add)."""
+    key = (width, str(device))
+    if key not in _ONES:
+        _ONES[key] = torch.ones(1, width, device=device)
+    return _ONES[key]
+
+
 class Block(nn.Module):
     def __init__(self, cfg):
         super().__init__()
@@ -136,8 +147,13 @@ class Block(nn.Module):
         dtype = self.self_attn.q.weight.dtype
         y = self.self_attn(N.layer_norm_modulate(x, scale, shift, self.eps, idx).to(dtype), layout)
         x = N.gated_add(x.float(), y, gate, idx)
-        normed = F.layer_norm(x.float(), (x.shape[-1],), self.norm3.weight.float(), self.norm3.bias.float(), self.eps)
-        x = x + self.cross_attn(normed.to(y.dtype), layout, context, cached_kv).float()
+        # norm3 (affine LayerNorm) as the modulated-LN kernel with one modulation row: scale = w - 1,
+        # shift = b (their gradients are the kernel's modulation gradients)
+        zeros = layout.zero_rows if x.is_cuda else None
+        normed = N.layer_norm_modulate(x, (self.norm3.weight.float() - 1)[None], self.norm3.bias.float()[None],
+                                       self.eps, zeros)
+        cross = self.cross_attn(normed.to(y.dtype), layout, context, cached_kv)
+        x = N.gated_add(x, cross, _ones(x.shape[-1], x.device), zeros) if x.is_cuda else x + cross.float()
         h = N.layer_norm_modulate(x, fscale, fshift, self.eps, idx).to(y.dtype)
         h = self.ffn[2](self.ffn[1](self.ffn[0](h)))
         return N.gated_add(x, h, fgate, idx)
@@ -197,6 +213,9 @@ class RowLayout:
         self.sample = sample.to(device)
         n = padded // tp
         self.local_sample = self.sample[tp_rank * n:(tp_rank + 1) * n]
+        # every local row -> modulation row 0, and an all-ones gate: the affine norm3 and the
+        # ungated cross-attention residual reuse the modulation / gated-add kernels
+        self.zero_rows = torch.zeros(n, dtype=torch.int32, device=device)
         cos, sin = gen.cos, gen.sin
         if self.pad:
             cos = torch.cat((cos, cos.new_ones(self.pad, cos.shape[1])))
