@@ -64,6 +64,25 @@ def timed(fn, iters=20, warmup=5, reps=5):
     return float(t)
 
 
+def kernel_times(fn, iters=10):
+    """Device time per call of each kernel ``fn`` launches (torch.profiler / CUPTI), so the time
+    inside the fused kernels can be told apart from host gaps between calls."""
+    from torch.profiler import ProfilerActivity, profile
+    fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(iters):
+            fn()
+        torch.cuda.synchronize()
+    out = {}
+    for e in prof.key_averages():
+        if e.device_type.name == "CUDA" and e.self_device_time_total > 0:
+            name = e.key.split("(")[0].replace("void cqb::(anonymous namespace)::", "")[:60]
+            out[name] = round(e.self_device_time_total / 1000 / iters, 4)
+    return out
+
+
 def main():
     from ..parallel import fused
     from ..parallel import state as ps
@@ -202,11 +221,20 @@ def main():
     out.append(dict(op="lm_head_ce_stats (vocab-parallel)", tp=tp, shape=[M, H, vocab // tp], fused_ms=t_fused,
                     nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
                     speedup_vs_nccl=t_nccl / t_fused, max_abs_err=err4))
+    kernels = {
+        "allgather_gemm": kernel_times(lambda: ws.gather_linear(x, w1)),
+        "gemm_reducescatter": kernel_times(lambda: ws.linear_scatter(xf, w2)),
+        "allgather_gemm_mn": kernel_times(lambda: ws.gather_matmul(dy, w3)),
+        "pair_input_grad_reducescatter": kernel_times(lambda: ws.matmul_scatter(dq, wq, dkv, wkv)),
+        "plain_gemm_reference": kernel_times(lambda: gemm.linear(torch.empty(M, H, device="cuda",
+                                                                             dtype=torch.bfloat16), w1)),
+    }
     status = symmetric.status()
     if st.rank == 0:
         for row in out:
             row["status"] = status
             print(json.dumps(row), flush=True)
+        print(json.dumps(dict(kernel_ms_per_call=kernels)), flush=True)
     symmetric.disable()
     ps.destroy()
 

@@ -94,6 +94,10 @@ at::Tensor qconv_fwd(at::Tensor raw, at::Tensor updates, at::Tensor w, at::Tenso
 std::vector<at::Tensor> qconv_bwd(at::Tensor dy, at::Tensor raw, at::Tensor updates, at::Tensor w, at::Tensor qs,
                                   at::Tensor qh, at::Tensor hist_rows, at::Tensor hist_offsets,
                                   at::Tensor hist_entries);
+std::vector<at::Tensor> qconv_bwd_into(at::Tensor dy, at::Tensor raw, at::Tensor updates, at::Tensor w,
+                                       at::Tensor qs, at::Tensor qh, at::Tensor hist_rows, at::Tensor hist_offsets,
+                                       at::Tensor hist_entries, at::Tensor d_upd);
+void qconv_raw_grad(at::Tensor g, at::Tensor w, at::Tensor qs, at::Tensor d_raw);
 at::Tensor chunk_scatter(at::Tensor dyc, at::Tensor slot_of, at::Tensor x, at::Tensor rnorm, bool normalize,
                          double scale);
 // optim.cu
@@ -105,7 +109,8 @@ at::Tensor sum_squares(std::vector<at::Tensor> xs);
 }  // namespace cqb
 
 namespace cqb {
-void rows_accumulate(at::Tensor grad, at::Tensor order, at::Tensor starts, at::Tensor ids, at::Tensor out);
+void rows_accumulate(at::Tensor grad, at::Tensor order, at::Tensor seg_start, at::Tensor run_seg, at::Tensor ids,
+                     at::Tensor out);
 }  // namespace cqb
 
 #ifdef CQB_DEBUG_BOUNDS
@@ -192,5 +197,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("chunk_gather", &cqb::chunk_gather);
   m.def("qconv_fwd", &cqb::qconv_fwd);
   m.def("qconv_bwd", &cqb::qconv_bwd);
+  m.def("qconv_bwd_into", &cqb::qconv_bwd_into);
+  m.def("qconv_raw_grad", &cqb::qconv_raw_grad);
   m.def("chunk_scatter", &cqb::chunk_scatter);
 }

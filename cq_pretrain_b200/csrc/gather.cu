@@ -55,33 +55,54 @@ __global__ void gather_rows_bwd_kernel(const T* __restrict__ grad, long m, const
   }
 }
 
-// out[ids[r]] += sum over k in [starts[r], starts[r + 1]) of grad[order[k]] (fp32 accumulate, one
-// warp per run of equal ids, rows summed in `order` order: deterministic). The embedding backward:
-// `order` sorts the token positions by id, so every run is one vocabulary row.
+// Embedding backward in two deterministic passes (no atomics). `order` lists the token positions
+// sorted by id; the sorted list is cut into segments of at most SEG positions that never span two
+// ids. Pass 1: one warp per segment sums its rows into partial[seg] (fp32). Pass 2: one warp per
+// (id, 256-column slice) adds the id's segment partials in order into out[id]. A repeated id
+// (e.g. the mask token of every query row) is thus summed by many warps instead of one.
 template <typename T>
-__global__ void rows_accumulate_kernel(const T* __restrict__ grad, const long* __restrict__ order,
-                                       const long* __restrict__ starts, const long* __restrict__ ids, long runs,
-                                       long rows_out, float* __restrict__ out, int width) {
+__global__ void segment_sum_kernel(const T* __restrict__ grad, const long* __restrict__ order,
+                                   const long* __restrict__ seg_start, long segments, long positions,
+                                   float* __restrict__ partial, int width) {
   const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  for (long r = warp; r < runs; r += ((long)gridDim.x * blockDim.x) >> 5) {
-    const long id = ids[r];
-    if (id >= rows_out || !CQB_IN_RANGE(id, rows_out, 3)) continue;   // ids >= rows_out: other shards
-    float* dst = out + id * width;
+  for (long sg = warp; sg < segments; sg += ((long)gridDim.x * blockDim.x) >> 5) {
+    const long k0 = seg_start[sg], k1 = seg_start[sg + 1];
     for (int c = lane * 8; c < width; c += 256) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (long k = starts[r]; k < starts[r + 1]; ++k) {
+      for (long k = k0; k < k1; ++k) {
+        const long row = order[k];
+        if (!CQB_IN_RANGE(row, positions, 4)) continue;
         float v[8];
-        load_any(grad + order[k] * width + c, v);
+        load_any(grad + row * width + c, v);
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[q] += v[q];
       }
-      float cur[8];
-      load8(dst + c, cur);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) cur[q] += acc[q];
-      store8(dst + c, cur);
+      store8(partial + sg * width + c, acc);
     }
+  }
+}
+
+__global__ void run_accumulate_kernel(const float* __restrict__ partial, const long* __restrict__ run_seg,
+                                      const long* __restrict__ ids, long runs, long rows_out,
+                                      float* __restrict__ out, int width) {
+  const int slices = (width + 255) / 256;
+  const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (long w = warp; w < runs * slices; w += ((long)gridDim.x * blockDim.x) >> 5) {
+    const long r = w / slices;
+    const int c = (int)(w % slices) * 256 + lane * 8;
+    const long id = ids[r];
+    if (c >= width || id >= rows_out || !CQB_IN_RANGE(id, rows_out, 3)) continue;   // >= rows_out: other shards
+    float acc[8];
+    load8(out + id * width + c, acc);
+    for (long sg = run_seg[r]; sg < run_seg[r + 1]; ++sg) {
+      float v[8];
+      load8(partial + sg * width + c, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += v[q];
+    }
+    store8(out + id * width + c, acc);
   }
 }
 
@@ -187,28 +208,37 @@ std::vector<at::Tensor> gather_rows_bwd(at::Tensor grad, at::Tensor inv, int64_t
   return n1 ? std::vector<at::Tensor>{out0, out1} : std::vector<at::Tensor>{out0};
 }
 
-// out fp32 [rows_out, width] += per-run sums of grad rows (see rows_accumulate_kernel).
-void rows_accumulate(at::Tensor grad, at::Tensor order, at::Tensor starts, at::Tensor ids, at::Tensor out) {
+// out fp32 [rows_out, width] += per-id sums of grad rows: order (positions sorted by id),
+// seg_start [segments + 1] (segment boundaries in `order`), run_seg [runs + 1] (first segment of
+// every id), ids [runs] (see segment_sum_kernel / run_accumulate_kernel).
+void rows_accumulate(at::Tensor grad, at::Tensor order, at::Tensor seg_start, at::Tensor run_seg, at::Tensor ids,
+                     at::Tensor out) {
   TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.is_contiguous() && grad.size(1) % 8 == 0,
               "rows_accumulate: contiguous [m, width] grad, width a multiple of 8");
   TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.dim() == 2 && out.size(1) == grad.size(1),
               "rows_accumulate: fp32 [rows, width] output");
-  for (auto* t : {&order, &starts, &ids})
+  for (auto* t : {&order, &seg_start, &run_seg, &ids})
     TORCH_CHECK(t->scalar_type() == at::kLong && t->is_contiguous() && t->is_cuda(), "rows_accumulate: int64 indices");
-  const long runs = ids.numel();
-  TORCH_CHECK(starts.numel() == runs + 1, "rows_accumulate: starts must hold runs + 1 offsets");
+  const long runs = ids.numel(), segments = seg_start.numel() - 1;
+  TORCH_CHECK(run_seg.numel() == runs + 1 && segments >= 0, "rows_accumulate: segment tables");
   if (!runs) return;
-  const int blocks = gather_grid(runs);
+  const int width = (int)grad.size(1);
+  auto partial = at::empty({std::max<long>(segments, 1), width}, out.options());
   if (grad.scalar_type() == at::kBFloat16)
-    rows_accumulate_kernel<__nv_bfloat16><<<blocks, 256, 0, stream()>>>(
-        (const __nv_bfloat16*)grad.data_ptr(), order.data_ptr<int64_t>(), starts.data_ptr<int64_t>(),
-        ids.data_ptr<int64_t>(), runs, out.size(0), out.data_ptr<float>(), (int)grad.size(1));
+    segment_sum_kernel<__nv_bfloat16><<<gather_grid(segments), 256, 0, stream()>>>(
+        (const __nv_bfloat16*)grad.data_ptr(), order.data_ptr<int64_t>(), seg_start.data_ptr<int64_t>(), segments,
+        grad.size(0), partial.data_ptr<float>(), width);
   else
-    rows_accumulate_kernel<float><<<blocks, 256, 0, stream()>>>(
-        grad.data_ptr<float>(), order.data_ptr<int64_t>(), starts.data_ptr<int64_t>(), ids.data_ptr<int64_t>(), runs,
-        out.size(0), out.data_ptr<float>(), (int)grad.size(1));
+    segment_sum_kernel<float><<<gather_grid(segments), 256, 0, stream()>>>(
+        grad.data_ptr<float>(), order.data_ptr<int64_t>(), seg_start.data_ptr<int64_t>(), segments, grad.size(0),
+        partial.data_ptr<float>(), width);
   CQB_LAUNCH_CHECK();
-  count_launch();
+  const long work = runs * ((width + 255) / 256);
+  run_accumulate_kernel<<<gather_grid(work), 256, 0, stream()>>>(partial.data_ptr<float>(), run_seg.data_ptr<int64_t>(),
+                                                               ids.data_ptr<int64_t>(), runs, out.size(0),
+                                                               out.data_ptr<float>(), width);
+  CQB_LAUNCH_CHECK();
+  count_launch(2);
 }
 
 #ifdef CQB_DEBUG_BOUNDS

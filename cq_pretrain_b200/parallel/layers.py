@@ -327,6 +327,20 @@ class VocabEmbedding(nn.Module):
         return scatter_rows(self.partial(ids))
 
 
+def _segments(counts, seg=16):
+    """Cut runs of ``counts`` sorted positions into segments of at most ``seg`` positions:
+    ``(segment boundaries [segments + 1], first segment of every run [runs + 1])`` (int64, host)."""
+    pieces = (counts + seg - 1) // seg
+    run_seg = torch.zeros(len(counts) + 1, dtype=torch.long)
+    torch.cumsum(pieces, 0, out=run_seg[1:])
+    run_start = torch.zeros(len(counts), dtype=torch.long)
+    run_start[1:] = torch.cumsum(counts, 0)[:-1]
+    owner = torch.repeat_interleave(torch.arange(len(counts)), pieces)
+    within = torch.arange(int(run_seg[-1])) - run_seg[:-1][owner]
+    starts = run_start[owner] + within * seg
+    return torch.cat((starts, counts.sum().reshape(1))), run_seg
+
+
 class _EmbeddingLookup(torch.autograd.Function):
     """``weight[index]`` with ``index == len(weight)`` reading a zero row."""
 
@@ -342,12 +356,13 @@ class _EmbeddingLookup(torch.autograd.Function):
         weight = ctx.weight
         order = torch.argsort(index, stable=True)
         ids, counts = torch.unique_consecutive(index.index_select(0, order), return_counts=True)
-        starts = torch.zeros(ids.numel() + 1, dtype=torch.long, device=index.device)
-        torch.cumsum(counts, 0, out=starts[1:])
+        seg_start, run_seg = _segments(counts.cpu())
+        dev = index.device
         # the sentinel run (ids of other shards, == len(weight)) is skipped by the kernel
         mg = getattr(weight, "main_grad", None)
         target = mg if mg is not None else torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
-        _ext.ops().rows_accumulate(grad.contiguous(), order, starts, ids.contiguous(), target)
+        _ext.ops().rows_accumulate(grad.contiguous(), order, seg_start.to(dev, non_blocking=True),
+                                   run_seg.to(dev, non_blocking=True), ids.contiguous(), target)
         if mg is not None:
             cb = getattr(weight, "_grad_ready", None)
             if cb is not None:
