@@ -240,7 +240,8 @@ __global__ void __launch_bounds__(256) qconv_fwd_kernel(const __nv_bfloat16* __r
   store8(out + (size_t)i * size + c, acc);
 }
 
-// g = dy silu'(pre) -> gbuf (fp32); d_raw[qs[i]] = g w[K-1]; per-block dw partials.
+// g = dy silu'(pre) -> gbuf (fp32); d_raw[qs[i]] = g w[K-1] (skipped when d_raw is null); per-block
+// dw partials.
 __global__ void __launch_bounds__(256) qconv_bwd_rows_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ raw, int ld_raw,
     const __nv_bfloat16* __restrict__ upd, int ld_upd, const long* __restrict__ qs, const long* __restrict__ qh,
@@ -284,10 +285,12 @@ __global__ void __launch_bounds__(256) qconv_bwd_rows_kernel(
         g[j] = d[j] * sg * (1.f + pre[j] * (1.f - sg));
       }
       store8(gbuf + (size_t)i * size + c, g);
-      float dr[8];
+      if (d_raw) {
+        float dr[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dr[j] = g[j] * w[CONV_K - 1][j];
-      store8(d_raw + (size_t)qs[i] * ld_draw + c, dr);
+        for (int j = 0; j < 8; ++j) dr[j] = g[j] * w[CONV_K - 1][j];
+        store8(d_raw + (size_t)qs[i] * ld_draw + c, dr);
+      }
 #pragma unroll
       for (int t = 0; t < CONV_K; ++t)
 #pragma unroll
@@ -311,17 +314,20 @@ __global__ void __launch_bounds__(256) qconv_bwd_rows_kernel(
   }
 }
 
-// d_upd[rows[k]] = sum over entries e of row k: gbuf[e / (K-1)] * w[e % (K-1)] (one block per row).
+// d_upd[rows[k]] (+)= sum over entries e of row k: gbuf[e / (K-1)] * w[e % (K-1)] (one block per
+// row; `accumulate` adds to the row already there, e.g. the causal conv's input gradient).
 __global__ void __launch_bounds__(256) qconv_bwd_hist_kernel(const float* __restrict__ gbuf,
                                                              const float* __restrict__ wT,
                                                              const int* __restrict__ rows,
                                                              const int* __restrict__ offsets,
                                                              const int* __restrict__ entries,
-                                                             __nv_bfloat16* __restrict__ d_upd, int ld_upd, int size) {
+                                                             __nv_bfloat16* __restrict__ d_upd, int ld_upd, int size,
+                                                             int accumulate) {
   const int k = blockIdx.x;
   const int e0 = offsets[k], e1 = offsets[k + 1];
   for (int c = threadIdx.x * 8; c < size; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (accumulate) load8(d_upd + (size_t)rows[k] * ld_upd + c, acc);
     for (int e = e0; e < e1; ++e) {
       const int ent = entries[e];
       const int i = ent / (CONV_K - 1), t = ent % (CONV_K - 1);
@@ -333,6 +339,25 @@ __global__ void __launch_bounds__(256) qconv_bwd_hist_kernel(const float* __rest
     }
     store8(d_upd + (size_t)rows[k] * ld_upd + c, acc);
   }
+}
+
+// d_raw[qs[i], :size] = gbuf[i] * w[:, K-1]: the query's own-projection gradient, written after the
+// content rows of d_raw (which leave every query row zero).
+__global__ void __launch_bounds__(256) qconv_raw_grad_kernel(const float* __restrict__ gbuf,
+                                                             const float* __restrict__ wlast,
+                                                             const long* __restrict__ qs,
+                                                             __nv_bfloat16* __restrict__ d_raw, int ld_draw, int nq,
+                                                             int size) {
+  const long v = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  const int per_row = size / 8;
+  if (v >= (long)nq * per_row) return;
+  const int i = (int)(v / per_row), c = (int)(v % per_row) * 8;
+  float g[8], w[8];
+  load8(gbuf + (size_t)i * size + c, g);
+  load8(wlast + c, w);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) g[j] *= w[j];
+  store8(d_raw + (size_t)qs[i] * ld_draw + c, g);
 }
 
 // out[n, h, c, :] = normalise?(x[idx[n*64 + c], h, :]) (zero when idx < 0); r[e, h] = rsqrt norm.
@@ -533,10 +558,76 @@ std::vector<at::Tensor> qconv_bwd(at::Tensor dy, at::Tensor raw, at::Tensor upda
     qconv_bwd_hist_kernel<<<U, 256, 0, stream()>>>(gbuf.data_ptr<float>(), wT.data_ptr<float>(),
                                                    hist_rows.data_ptr<int>(), hist_offsets.data_ptr<int>(),
                                                    hist_entries.data_ptr<int>(), (__nv_bfloat16*)d_upd.data_ptr(),
-                                                   (int)d_upd.stride(0), size);
+                                                   (int)d_upd.stride(0), size, 0);
   CQB_LAUNCH_CHECK();
   count_launch(3);
   return {d_raw, d_upd, dw};
+}
+
+// Query conv backward into existing buffers: adds the history gradient into `d_upd` (the causal
+// conv's input gradient, bf16 [nc, >= size]) and returns (dw [size, 4] fp32, g [nq, size] fp32); the
+// own-projection gradient goes to d_raw later through qconv_raw_grad(g, w, qs, d_raw).
+std::vector<at::Tensor> qconv_bwd_into(at::Tensor dy, at::Tensor raw, at::Tensor updates, at::Tensor w,
+                                       at::Tensor qs, at::Tensor qh, at::Tensor hist_rows, at::Tensor hist_offsets,
+                                       at::Tensor hist_entries, at::Tensor d_upd) {
+  check_qconv(raw, updates, w, qs, qh);
+  TORCH_CHECK(hist_rows.scalar_type() == at::kInt && hist_offsets.scalar_type() == at::kInt &&
+                  hist_entries.scalar_type() == at::kInt && hist_offsets.numel() == hist_rows.numel() + 1,
+              "history CSR: int32 rows [U], offsets [U+1], entries [E]");
+  const int nq = qs.numel(), size = w.size(0);
+  TORCH_CHECK(d_upd.is_cuda() && d_upd.scalar_type() == at::kBFloat16 && d_upd.dim() == 2 &&
+                  d_upd.size(0) == updates.size(0) && d_upd.size(1) >= size && d_upd.stride(1) == 1 &&
+                  d_upd.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(d_upd.data_ptr()) % 16 == 0,
+              "d_upd: bf16 [nc, >= size] with 16-byte aligned rows");
+  auto dyc = dy.contiguous();
+  TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.numel() == (int64_t)nq * size, "dy: bf16 [nq, size]");
+  auto wT = w.to(at::kFloat).t().contiguous();
+  auto qsc = qs.contiguous();
+  auto dw = at::zeros({size, CONV_K}, raw.options().dtype(at::kFloat));
+  auto gbuf = at::empty({nq, size}, raw.options().dtype(at::kFloat));
+  if (!nq) return {dw, gbuf};
+  const dim3 grid((size / 8 + 31) / 32, (nq + QROWS * CONV_GROUPS - 1) / (QROWS * CONV_GROUPS));
+  auto partial = at::empty({(long)grid.y, size, CONV_K}, dw.options());
+  qconv_bwd_rows_kernel<<<grid, dim3(32, CONV_GROUPS), 0, stream()>>>(
+      (const __nv_bfloat16*)dyc.data_ptr(), (const __nv_bfloat16*)raw.data_ptr(), (int)raw.stride(0),
+      (const __nv_bfloat16*)updates.data_ptr(), (int)updates.stride(0), (const long*)qsc.data_ptr(),
+      (const long*)qh.data_ptr(), (long)updates.size(0), wT.data_ptr<float>(), gbuf.data_ptr<float>(), nullptr, 0,
+      partial.data_ptr<float>(), nq, size);
+  CQB_LAUNCH_CHECK();
+  sum_rows_kernel<<<(size * CONV_K + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                     grid.y, size * CONV_K);
+  CQB_LAUNCH_CHECK();
+  const int U = hist_rows.numel();
+  if (U)
+    qconv_bwd_hist_kernel<<<U, 256, 0, stream()>>>(gbuf.data_ptr<float>(), wT.data_ptr<float>(),
+                                                   hist_rows.data_ptr<int>(), hist_offsets.data_ptr<int>(),
+                                                   hist_entries.data_ptr<int>(), (__nv_bfloat16*)d_upd.data_ptr(),
+                                                   (int)d_upd.stride(0), size, 1);
+  CQB_LAUNCH_CHECK();
+  count_launch(U ? 3 : 2);
+  return {dw, gbuf};
+}
+
+// d_raw[qs[i], :size] = g[i] * w[:, K-1] (see qconv_bwd_into).
+void qconv_raw_grad(at::Tensor g, at::Tensor w, at::Tensor qs, at::Tensor d_raw) {
+  const int nq = qs.numel(), size = w.size(0);
+  TORCH_CHECK(g.scalar_type() == at::kFloat && g.is_contiguous() && g.numel() == (int64_t)nq * size,
+              "g: fp32 [nq, size]");
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == CONV_K && size % 8 == 0, "w: [size, 4], size a multiple of 8");
+  TORCH_CHECK(qs.scalar_type() == at::kLong, "qs: int64");
+  TORCH_CHECK(d_raw.scalar_type() == at::kBFloat16 && d_raw.dim() == 2 && d_raw.size(1) >= size &&
+                  d_raw.stride(1) == 1 && d_raw.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(d_raw.data_ptr()) % 16 == 0,
+              "d_raw: bf16 [rows, >= size] with 16-byte aligned rows");
+  if (!nq) return;
+  auto wlast = w.select(1, CONV_K - 1).to(at::kFloat).contiguous();
+  auto qsc = qs.contiguous();
+  const long vectors = (long)nq * (size / 8);
+  qconv_raw_grad_kernel<<<(unsigned)((vectors + 255) / 256), 256, 0, stream()>>>(
+      g.data_ptr<float>(), wlast.data_ptr<float>(), (const long*)qsc.data_ptr(), (__nv_bfloat16*)d_raw.data_ptr(),
+      (int)d_raw.stride(0), nq, size);
+  CQB_LAUNCH_CHECK();
+  count_launch();
 }
 
 std::vector<at::Tensor> chunk_gather(at::Tensor x, at::Tensor idx, int64_t chunks, bool normalize, double scale) {

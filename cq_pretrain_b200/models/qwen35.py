@@ -142,12 +142,11 @@ class GatedDelta(nn.Module):
         size = hk * d
         raw, z, a, b = self.project(x)                      # full rows, local heads
         dp = plan.delta
-        updates = GA.rows(raw, dp.content_order, dp.content_order_inv)    # content in write order
-        conv = self.conv1d(updates, dp.content_bounds)
+        # updates: content rows in write order. The query conv reads each query's own projection
+        # and the previous k-1 real content inputs of its document; queries never enter any other
+        # token's history.
+        updates, conv, query = GDN.conv_and_query(raw, self.conv1d.weight[:, 0], dp, size)
         q, k, v = conv.split((size, size, h * d), -1)
-        # Query conv reads the previous k-1 real content inputs of its document; queries never
-        # enter any other token's history.
-        query = GDN.query_conv_silu(raw, updates, self.conv1d.weight[:size, 0], dp)
         q, k, query = q.reshape(-1, hk, d), k.reshape(-1, hk, d), query.reshape(-1, hk, d)
         v = v.reshape(-1, h, d)
         if h != hk:

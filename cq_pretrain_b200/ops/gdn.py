@@ -40,6 +40,67 @@ def prefill(q, k, v, g, beta, bounds, chunk=64):
     return y.to(v.dtype), state
 
 
+class _ConvAndQuery(torch.autograd.Function):
+    """``updates = raw[content_order]``, ``conv = causal_conv_silu(updates)`` and
+    ``query = query_conv_silu(raw, updates)`` as one node. Backward, with no zero-fill or add of a
+    full gradient: the conv backward writes d_updates, the query history gradient is added into it in
+    place, the inverse gather writes every row of d_raw (zero where no content row came from), and
+    the queries' own-projection gradient then overwrites their (zero) rows of d_raw; content and
+    query rows of ``raw`` are disjoint."""
+
+    @staticmethod
+    def forward(ctx, raw, weight, pos, order, inv, qs, qh, rows, offsets, entries, size):
+        ops = _ext.ops()
+        updates = ops.gather_rows(raw, None, order)
+        conv = ops.conv_fwd(updates, weight, pos)
+        query = ops.qconv_fwd(raw, updates, weight[:size], qs, qh)
+        ctx.save_for_backward(raw, updates, weight, pos, inv, qs, qh, rows, offsets, entries)
+        ctx.size, ctx.n_raw = size, raw.shape[0]
+        ctx.mark_non_differentiable(updates)
+        return updates, conv, query
+
+    @staticmethod
+    def backward(ctx, _d_updates, d_conv, d_query):
+        raw, updates, weight, pos, inv, qs, qh, rows, offsets, entries = ctx.saved_tensors
+        ops = _ext.ops()
+        if d_conv is None:
+            d_conv = torch.zeros_like(updates)
+        d_upd, dw = ops.conv_bwd(d_conv.contiguous(), updates, weight, pos)
+        g = None
+        if d_query is not None and qs.numel():
+            dwq, g = ops.qconv_bwd_into(d_query.to(torch.bfloat16).contiguous(), raw, updates, weight[:ctx.size], qs,
+                                        qh, rows, offsets, entries, d_upd)
+            dw[:ctx.size] += dwq
+        d_raw = ops.gather_rows_bwd(d_upd, inv, ctx.n_raw, 0)[0]
+        if g is not None:
+            ops.qconv_raw_grad(g, weight[:ctx.size], qs, d_raw)
+        return d_raw, dw.to(weight.dtype), None, None, None, None, None, None, None, None, None
+
+
+def conv_and_query(raw, weight, plan, size):
+    """``(updates, conv, query)`` of a GDN layer: ``updates = raw[plan.content_order]``, the causal
+    depthwise conv + SiLU of ``updates`` per document (``weight`` ``[C, K]``), and the query conv of
+    the read-only query events over the first ``size`` channels (``query_conv_silu``). CUDA bf16 with
+    K = 4 runs the fused node ``_ConvAndQuery``; otherwise the three ops run one by one."""
+    from . import gather as GA
+    C, K = weight.shape
+    fused = (raw.is_cuda and raw.dtype == torch.bfloat16 and K == 4 and size % 8 == 0 and C % 8 == 0
+             and raw.stride(-1) == 1 and raw.stride(0) % 8 == 0 and raw.data_ptr() % 16 == 0
+             and plan.query_hist_rows is not None and _ext.has("qconv_bwd_into"))
+    if fused:
+        from .gdn_cuda import _positions
+        pos = _positions(tuple(int(b) for b in plan.content_bounds), raw.device)
+        if pos.numel() == plan.content_order.numel():
+            inv = GA._stacked(plan.content_order_inv)
+            return _ConvAndQuery.apply(raw, weight, pos, plan.content_order, inv, plan.query_source,
+                                       plan.query_history, plan.query_hist_rows, plan.query_hist_offsets,
+                                       plan.query_hist_entries, size)
+    updates = GA.rows(raw, plan.content_order, plan.content_order_inv)
+    conv = causal_conv_silu(updates, weight, plan.content_bounds)
+    query = query_conv_silu(raw, updates, weight[:size], plan)
+    return updates, conv, query
+
+
 def decode_step(state, q, k, v, g, beta):
     """One recurrent step of every head: ``state`` ``[H, Dk, Dv]`` (fp32, in place) takes the write
     ``k [H, Dk]``, ``v [H, Dv]`` with log-decay ``g`` and ``beta`` ``[H]``; the rows of ``q``

@@ -277,17 +277,17 @@ class DistributedOptimizer:
         b1, b2 = self.betas
         bc1 = 1 - b1 ** self.step_count
         bc2 = 1 - b2 ** self.step_count
-        grads = [self._grad_shard(s) for s in self.shards]
         gscale = (coef * scale).float().reshape(())
-        published = [s["bucket"].group.param_buffer[s["lo"]:s["lo"] + s["n"]] for s in self.shards]
         if self._use_kernels():
             # one launch: scale, moments, decoupled decay, update, the parameter write-back and (when
             # a renderer EMA is attached) the shadow lerp toward the updated masters
-            lists = self._kernel_lists(grads, published)
+            lists = self._kernel_lists()
             _ext.ops().adamw_step(*lists[:6], gscale, lr, b1, b2, self.eps, self.weight_decay, bc1, bc2,
                                   lists[6], 1.0 - self.ema.decay if self.ema is not None else 0.0)
             self.ema_fused = self.ema is not None
         else:
+            grads = [self._grad_shard(s) for s in self.shards]
+            published = [s["bucket"].group.param_buffer[s["lo"]:s["lo"] + s["n"]] for s in self.shards]
             for s, g, out in zip(self.shards, grads, published):
                 g = g * gscale
                 m, v, p = s["exp_avg"], s["exp_avg_sq"], s["master"]
@@ -304,10 +304,18 @@ class DistributedOptimizer:
         """Let the AdamW kernel update ``ema``'s shadows (``shadow += (1 - decay)(master - shadow)``)."""
         self.ema, self.ema_fused = ema, False
 
-    def _kernel_lists(self, grads, published):
+    def _kernel_lists(self):
         """Per-shard tensors for the AdamW kernel, split at the EMA slices so that each renderer
-        slice carries its shadow (an empty tensor marks slices without one)."""
+        slice carries its shadow (an empty tensor marks slices without one). Every entry is a view
+        of a persistent buffer, so the lists are built once (thousands of slices: tens of ms of
+        host time per step otherwise) and rebuilt only when another EMA or shadow set is attached."""
         ema = getattr(self, "ema", None)
+        key = (id(ema), tuple(map(id, ema.shadows)) if ema is not None else ())
+        cached = getattr(self, "_lists_cache", None)
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        grads = [self._grad_shard(s) for s in self.shards]
+        published = [s["bucket"].group.param_buffer[s["lo"]:s["lo"] + s["n"]] for s in self.shards]
         ranges = {}
         if ema is not None:
             for (si, a, b), shadow in zip(ema.index, ema.shadows):
@@ -328,6 +336,7 @@ class DistributedOptimizer:
                 for lst, t in zip(out, tensors):
                     lst.append(t[a:b])
                 out[6].append(shadow)
+        self._lists_cache = (key, out)
         return out
 
     def all_gather_params(self, blocking=True):

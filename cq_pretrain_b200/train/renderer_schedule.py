@@ -30,9 +30,9 @@ def backward_deferred_renderer(model, batch, losses, backward_scale=1.0, optimiz
         last = index + 1 == len(parts)
         context = optimizer.suspend_readiness() if (optimizer is not None and not last) else nullcontext()
         with context:
-            with phase(timer, "forward"):
+            with phase(timer, "renderer_forward"):
                 chunk_loss = model.renderer(leaf, part.bind(batch))
-            with phase(timer, "backward"):
+            with phase(timer, "renderer_backward"):
                 (chunk_loss * (image_factor * backward_scale)).backward()
         image_loss.add_(chunk_loss.detach().float())
         if gradient is not None:

@@ -30,8 +30,9 @@ import torch
 
 
 class PhaseTimer:
-    def __init__(self, device):
+    def __init__(self, device, annotate=False):
         self.enabled = device is not None and torch.device(device).type == "cuda"
+        self.annotate = annotate   # also open a profiler range per phase (shows on the device timeline)
         self.pairs = []      # (name, start event, end event)
 
     @contextmanager
@@ -41,9 +42,11 @@ class PhaseTimer:
             return
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.nvtx.range_push(name)
+        scope = torch.profiler.record_function(name) if self.annotate else nullcontext()
         start.record()
         try:
-            yield
+            with scope:
+                yield
         finally:
             end.record()
             torch.cuda.nvtx.range_pop()

@@ -84,3 +84,38 @@ def test_query_conv_matches_torch_path():
     for got, want in ((ra.grad, rf.grad), (ua.grad, uf.grad), (wa.grad, wf.grad)):
         rel = (got.double() - want.double()).norm() / want.double().norm()
         assert rel < 1e-2, rel.item()
+
+
+def test_conv_and_query_node_matches_composed_ops():
+    """The fused conv + query conv node (in-place gradient accumulation, disjoint content/query
+    rows of d_raw) against the three ops composed in float64."""
+    from cq_pretrain_b200.config import tiny_config
+    from cq_pretrain_b200.data.synthetic import synthetic_batch
+    from cq_pretrain_b200.ops import gdn as GDN
+    from cq_pretrain_b200.ops import reference as R
+    assert _ext.has("qconv_bwd_into")
+    cfg = tiny_config()
+    host, _ = synthetic_batch(cfg, 512, seed=5)
+    dp = host.mainline.delta.to("cuda")
+    torch.manual_seed(1)
+    rows, width, size = host.mainline.rows, 768, 256
+    proj = torch.randn(rows, width + 64, device="cuda").to(torch.bfloat16)
+    w = torch.rand(width, 4, device="cuda") - 0.5
+    ra = proj[:, :width].detach().clone().requires_grad_()
+    wa = w.clone().requires_grad_()
+    ra_view = torch.cat((ra, proj[:, width:]), 1)[:, :width]   # strided rows, like a split projection
+    updates, conv, query = GDN.conv_and_query(ra_view, wa, dp, size)
+    rf = proj[:, :width].double().requires_grad_()
+    wf = w.double().requires_grad_()
+    uf = rf.index_select(0, dp.content_order)
+    conv_ref = R.causal_conv_silu(uf, wf, dp.content_bounds)
+    query_ref = GDN.query_conv_silu(rf, uf, wf[:size], dp)
+    assert (updates.double() - uf).abs().max().item() == 0
+    for got, want in ((conv, conv_ref), (query, query_ref)):
+        assert (got.double() - want).abs().max().item() < 2e-2
+    dc, dq = torch.randn_like(conv_ref), torch.randn_like(query_ref)
+    torch.autograd.backward((conv, query), (dc.to(conv.dtype), dq.to(query.dtype)))
+    torch.autograd.backward((conv_ref, query_ref), (dc, dq))
+    for got, want in ((ra.grad, rf.grad), (wa.grad, wf.grad)):
+        rel = (got.double() - want).norm() / want.norm()
+        assert rel < 1e-2, rel.item()
