@@ -21,6 +21,8 @@ def _move(value, fn):
         return value._map(fn)
     if isinstance(value, tuple) and value and all(isinstance(x, torch.Tensor) for x in value):
         return tuple(fn(x) for x in value)
+    if isinstance(value, tuple) and value and all(hasattr(x, "_map") for x in value):
+        return tuple(x._map(fn) for x in value)     # e.g. the planned DiT micro-batch layouts
     return value
 
 

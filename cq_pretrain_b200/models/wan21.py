@@ -225,6 +225,24 @@ class RowLayout:
         self.cross_ranges = ATT.ranges_from_ends(self.row_ends, self.cond_ends, device) if device.type == "cuda" else None
 
 
+_ROW_LAYOUTS: dict = {}
+
+
+def row_layout(gen, device, tp, tp_rank):
+    """The ``RowLayout`` of a DiT call, cached per geometry: every tensor in it (sample of each
+    row, RoPE rows, attention ranges) is a function of the targets' grids, lengths and condition
+    counts, so a repeated geometry reuses the device tensors instead of copying them again (and a
+    CUDA-graph capture finds them already on the device)."""
+    key = (gen.grids, gen.lengths, gen.query_counts, gen.video_ends, gen.text_ends, tuple(gen.cos.shape),
+           str(gen.cos.dtype), tp, tp_rank, str(device))
+    hit = _ROW_LAYOUTS.get(key)
+    if hit is None:
+        if len(_ROW_LAYOUTS) > 32:
+            _ROW_LAYOUTS.clear()
+        hit = _ROW_LAYOUTS[key] = RowLayout(gen, device, tp, tp_rank)
+    return hit
+
+
 class Wan21Generator(nn.Module):
     def __init__(self, cfg):
         super().__init__()
@@ -269,7 +287,7 @@ class Wan21Generator(nn.Module):
         """This rank's row shard of the prediction (fp32) and the row layout."""
         st = ps.state()
         device = xt.device
-        layout = RowLayout(gen, device, st.tp, st.tp_rank)
+        layout = row_layout(gen, device, st.tp, st.tp_rank)
         time = self.time_embedding(gen.time_features.float().to(device))
         e = self.time_projection(time).reshape(-1, 6, self.cfg.dit_width)
         context = self.project_conditions(conditions, gen) if projected is None else projected

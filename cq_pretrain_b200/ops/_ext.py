@@ -69,9 +69,20 @@ def has(name: str) -> bool:
     return cuda_kernels_enabled() and hasattr(_MODULE, name)
 
 
+_GRAPH_LAUNCHES = 0
+
+
+def add_graph_launches(n: int) -> None:
+    """Adjust the count by kernels that CUDA-graph replays run (or a capture recorded without running)."""
+    global _GRAPH_LAUNCHES
+    _GRAPH_LAUNCHES += int(n)
+
+
 def launches() -> int:
-    """Kernel launches issued by this library so far (0 when it is not loaded)."""
-    return int(_MODULE.launch_count()) if _MODULE is not None and hasattr(_MODULE, "launch_count") else 0
+    """Kernel launches of this library so far, graph replays included (0 when it is not loaded)."""
+    if _MODULE is None or not hasattr(_MODULE, "launch_count"):
+        return 0
+    return int(_MODULE.launch_count()) + _GRAPH_LAUNCHES
 
 
 def ops():

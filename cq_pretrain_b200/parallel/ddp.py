@@ -165,6 +165,9 @@ class DistributedOptimizer:
             return
         if b.launched:
             raise RuntimeError(f"gradient of {self.names[p]} arrived after its bucket reduce-scatter started")
+        if getattr(self, "_recorded", None) is not None:
+            self._recorded.append(p)
+            return
         if self.suspended:
             return
         b.counts[p] = b.counts.get(p, 0) + 1
@@ -193,6 +196,15 @@ class DistributedOptimizer:
                                                       async_op=True)
         b.launched = True
         self.next_bucket = max(self.next_bucket, b.index + 1)
+
+    def start_recording(self):
+        """Readiness marks from now on are recorded instead of counted (a CUDA-graph capture,
+        whose backward runs again on every replay); ``stop_recording`` returns them in order."""
+        self._recorded = []
+
+    def stop_recording(self):
+        marks, self._recorded = self._recorded, None
+        return marks or []
 
     @contextmanager
     def suspend_readiness(self):

@@ -28,6 +28,7 @@ from ..models.qwen35 import cast_for_training
 from ..parallel import state as ps
 from ..parallel.ddp import DistributedOptimizer
 from .ema import RendererEMA
+from .graphed import RendererGraphs, graphs_enabled
 from .loss import compose_losses, scales_from_counts
 from .renderer_schedule import backward_deferred_renderer
 from .schedule import learning_rate
@@ -64,19 +65,22 @@ class Trainer:
         self.ema = RendererEMA(self.model, self.optimizer, ema_decay) if ema_decay else None
         self.preparer = DevicePreparer(cfg, self.device, dtype)
         self.step_index = 0
+        # the DiT chunk (forward + backward) replays as a CUDA graph once its geometry repeats
+        self.renderer_graphs = RendererGraphs(self.optimizer) if graphs_enabled(cfg, self.device, tp) else None
         if tp > 1 and fused_tp and self.device.type == "cuda":
             from ..parallel import symmetric
             symmetric.enable()
 
     def _micro(self, batch, scales, backward_scale, timer=None):
-        deferred = batch.generation is not None and bool(batch.generation.microbatches)
+        deferred = batch.generation is not None and (bool(batch.generation.microbatches)
+                                                     or self.renderer_graphs is not None)
         with phase(timer, "forward"):
             out = self.model(batch, compute_image_loss=not deferred)
             losses = compose_losses(out, self.cfg, scales)
         if deferred:
             image_factor = self.cfg.image_weight * scales[1]
             losses = backward_deferred_renderer(self.model, batch, losses, backward_scale, self.optimizer,
-                                                image_factor=image_factor, timer=timer)
+                                                image_factor=image_factor, timer=timer, graphs=self.renderer_graphs)
         else:
             with phase(timer, "backward"):
                 (losses["loss"] * backward_scale).backward()
