@@ -11,6 +11,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass, fields, replace
 
+import numpy as np
 import torch
 
 
@@ -59,6 +60,44 @@ class VisionInputs(Movable):
 
 
 @dataclass
+class EmbeddingPlan(Movable):
+    """Sort plan of the backbone's input ids for the embedding backward, built on the host with the
+    batch so that the backward needs no device-to-host round trip: ``order`` (row positions sorted
+    by id, stable), ``run_ids`` (each distinct id once, ascending), ``seg_start`` (boundaries in
+    ``order`` of segments of at most ``seg`` positions that never cross an id) and ``run_seg``
+    (first segment of every id, plus the total)."""
+
+    order: torch.Tensor
+    run_ids: torch.Tensor
+    seg_start: torch.Tensor
+    run_seg: torch.Tensor
+
+    @classmethod
+    def build(cls, ids, seg=16):
+        ids = np.asarray(ids, dtype=np.int64).reshape(-1)
+        order = np.argsort(ids, kind="stable")
+        run_ids, counts = np.unique(ids[order], return_counts=True)
+        pieces = (counts + seg - 1) // seg
+        run_seg = np.concatenate(([0], np.cumsum(pieces)))
+        run_start = np.concatenate(([0], np.cumsum(counts)[:-1]))
+        owner = np.repeat(np.arange(len(counts)), pieces)
+        within = np.arange(int(run_seg[-1])) - run_seg[:-1][owner]
+        seg_start = np.concatenate((run_start[owner] + within * seg, [len(ids)]))
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int64))
+        return cls(t(order), t(run_ids), t(seg_start), t(run_seg))
+
+
+def backbone_ids(batch, text_mask_id, image_mask_id):
+    """Input token of every backbone row: the content ids, each query's mask token (image or text
+    query) and text-mask tokens on the padding rows."""
+    plan = batch.mainline
+    ids = batch.ids.reshape(-1)
+    qids = torch.where(plan.query_image.to(ids.device), image_mask_id, text_mask_id).to(ids.dtype)
+    pad = plan.rows - plan.content_length - plan.queries
+    return torch.cat((ids, qids, ids.new_full((pad,), text_mask_id)))
+
+
+@dataclass
 class Batch(Movable):
     ids: torch.Tensor                      # [1, S] content ids (visual placeholders included)
     segments: torch.Tensor                 # [1, S] packed document id, -1 for padding
@@ -75,6 +114,7 @@ class Batch(Movable):
     noise: torch.Tensor | None = None      # [sum L, C*4]
     times: torch.Tensor | None = None      # [n_targets] flow sigma in (0, 1)
     mainline: object = None                # CQPlan
+    embed_plan: object = None              # EmbeddingPlan of the backbone input ids (host-built)
 
     @property
     def length(self) -> int:

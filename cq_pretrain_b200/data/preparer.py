@@ -11,6 +11,7 @@ import hashlib
 
 import torch
 
+from .batch import EmbeddingPlan, backbone_ids
 from .generation import time_features
 
 
@@ -59,14 +60,21 @@ class DevicePreparer:
         return noise, times, time_features(times, freq_dim)
 
     def __call__(self, batch, receipt, non_blocking=False):
+        """The device copy of ``batch`` with its flow randomness and the host-built sort plan of
+        the backbone input ids (``EmbeddingPlan``); on CUDA the new host tensors are pinned so every
+        copy is asynchronous."""
         extra = self.randomness(batch, receipt)
+        pin = self.device.type == "cuda"
         if extra is not None:
-            noise, times, feats = extra
+            noise, times, feats = (t.pin_memory() if pin and t is not None else t for t in extra)
             batch.noise, batch.times = noise, times
             if batch.generation is not None:
                 batch.generation.time_features = feats
             if batch.latents is None:
                 raise ValueError("generation targets need latents (cached or encoded)")
+        if batch.mainline is not None and batch.embed_plan is None and batch.ids.device.type == "cpu":
+            plan = EmbeddingPlan.build(backbone_ids(batch, self.cfg.text_mask_token_id, self.cfg.image_mask_token_id))
+            batch.embed_plan = plan.pin_memory() if pin else plan
         out = batch.to(self.device, non_blocking=non_blocking)
         if out.vision is not None and out.vision.features is not None:
             out.vision.features = out.vision.features.to(self.dtype)

@@ -17,6 +17,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
+from ..data.batch import backbone_ids
 from ..ops import cross_entropy as CE
 from ..parallel import layers as PL
 from ..parallel import state as ps
@@ -61,13 +62,9 @@ class JointModel(nn.Module):
     # ---- backbone ---------------------------------------------------------------------------
     def embed(self, batch):
         """Row-sharded input hidden ``[rows/tp, width]`` for the packed sequence."""
-        cfg, plan = self.cfg, batch.mainline
-        s, rows = plan.content_length, plan.rows
-        ids = batch.ids.reshape(-1)
-        qids = torch.where(plan.query_image, cfg.image_mask_token_id, cfg.text_mask_token_id).to(ids.device)
-        pad = rows - s - plan.queries
-        all_ids = torch.cat((ids, qids, ids.new_full((pad,), cfg.text_mask_token_id)))
-        partial = self.embedding.partial(all_ids)
+        cfg = self.cfg
+        all_ids = backbone_ids(batch, cfg.text_mask_token_id, cfg.image_mask_token_id)
+        partial = self.embedding.partial(all_ids, batch.embed_plan)
         vision = batch.vision
         if vision is not None and vision.content_indices.numel():
             if vision.features is not None:

@@ -304,20 +304,27 @@ class VocabEmbedding(nn.Module):
         normal_init(self.weight)
         mark_sharded(self.weight, 0)
 
-    def partial(self, ids):
+    def partial(self, ids, plan=None):
         """This rank's masked lookup ``[n, width]`` (full rows, zero outside the local vocab range).
 
         On CUDA the lookup is the row-gather kernel (ids outside this shard hit the zero sentinel)
         and the backward adds each token id's rows straight into the FP32 ``main_grad`` rows it
         touches (``rows_accumulate``: a deterministic sum per id), instead of building a dense
-        vocabulary gradient and adding it."""
+        vocabulary gradient and adding it. ``plan`` (``data.batch.EmbeddingPlan`` of ``ids``, built
+        on the host) gives the backward its sort order; without it the backward sorts on the device
+        and reads the run lengths back to the host."""
         n = self.weight.shape[0]
         lo = ps.tp_rank() * n
         local = ids - lo
         owned = (local >= 0) & (local < n)
         if (ids.is_cuda and self.weight.dtype == torch.bfloat16 and self.weight.shape[1] % 8 == 0
                 and _ext.has("rows_accumulate")):
-            return _EmbeddingLookup.apply(torch.where(owned, local, torch.full_like(local, n)), self.weight)
+            sort = None
+            if plan is not None and plan.order.numel() == ids.numel():
+                runs = plan.run_ids - lo
+                runs = torch.where((runs >= 0) & (runs < n), runs, torch.full_like(runs, n))   # other shards: skipped
+                sort = (plan.order, plan.seg_start, plan.run_seg, runs)
+            return _EmbeddingLookup.apply(torch.where(owned, local, torch.full_like(local, n)), self.weight, sort)
         out = nn.functional.embedding(local.clamp(0, n - 1), self.weight)
         if ps.tp_size() > 1:
             out = out * owned[:, None].to(out.dtype)
@@ -345,30 +352,33 @@ class _EmbeddingLookup(torch.autograd.Function):
     """``weight[index]`` with ``index == len(weight)`` reading a zero row."""
 
     @staticmethod
-    def forward(ctx, index, weight):
+    def forward(ctx, index, weight, sort):
         ctx.save_for_backward(index)
-        ctx.weight = weight
+        ctx.weight, ctx.sort = weight, sort
         return _ext.ops().gather_rows(weight, None, index.contiguous())
 
     @staticmethod
     def backward(ctx, grad):
         (index,) = ctx.saved_tensors
         weight = ctx.weight
-        order = torch.argsort(index, stable=True)
-        ids, counts = torch.unique_consecutive(index.index_select(0, order), return_counts=True)
-        seg_start, run_seg = _segments(counts.cpu())
-        dev = index.device
-        # the sentinel run (ids of other shards, == len(weight)) is skipped by the kernel
+        if ctx.sort is not None:
+            order, seg_start, run_seg, ids = ctx.sort
+        else:
+            order = torch.argsort(index, stable=True)
+            ids, counts = torch.unique_consecutive(index.index_select(0, order), return_counts=True)
+            seg_start, run_seg = _segments(counts.cpu())
+            seg_start = seg_start.to(index.device, non_blocking=True)
+            run_seg = run_seg.to(index.device, non_blocking=True)
+        # runs of other shards' ids (== len(weight)) are skipped by the kernel
         mg = getattr(weight, "main_grad", None)
         target = mg if mg is not None else torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
-        _ext.ops().rows_accumulate(grad.contiguous(), order, seg_start.to(dev, non_blocking=True),
-                                   run_seg.to(dev, non_blocking=True), ids.contiguous(), target)
+        _ext.ops().rows_accumulate(grad.contiguous(), order, seg_start, run_seg, ids.contiguous(), target)
         if mg is not None:
             cb = getattr(weight, "_grad_ready", None)
             if cb is not None:
                 cb(weight)
-            return None, None
-        return None, target.to(weight.dtype)
+            return None, None, None
+        return None, target.to(weight.dtype), None
 
 
 def checkpoint_shard(value, parameter):

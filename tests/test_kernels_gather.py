@@ -69,3 +69,24 @@ def test_embedding_lookup_and_sparse_main_grad_backward():
     emb.weight.main_grad.fill_(0.5)
     emb.partial(ids).backward(grad)
     assert torch.equal(first, emb.weight.main_grad)      # deterministic
+
+
+def test_embedding_backward_with_host_plan_matches_device_sort():
+    """The host-built sort plan (``EmbeddingPlan``) gives the same main_grad as the on-device sort,
+    including a shard offset (ids of other shards are skipped)."""
+    from cq_pretrain_b200.data.batch import EmbeddingPlan
+    from cq_pretrain_b200.parallel import layers as PL
+    from cq_pretrain_b200.parallel import state as ps
+    ps.initialize(1)
+    torch.manual_seed(1)
+    emb = PL.VocabEmbedding(4000, 128).cuda().to(torch.bfloat16)
+    ids = torch.randint(0, 6000, (2500,))                # ids >= 4000 behave like another shard's
+    ids[:300] = 11
+    plan = EmbeddingPlan.build(ids.numpy()).to("cuda")
+    grad = torch.randn(2500, 128, device="cuda").to(torch.bfloat16)
+    outs = []
+    for p in (None, plan):
+        emb.weight.main_grad = torch.zeros(4000, 128, device="cuda")
+        emb.partial(ids.cuda(), p).backward(grad)
+        outs.append(emb.weight.main_grad.clone())
+    assert torch.equal(outs[0], outs[1])
