@@ -81,6 +81,7 @@ std::vector<at::Tensor> attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at
 int attn_status(bool reset);
 // gdn_chunk.cu
 std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor G, at::Tensor B);
+int64_t gdn_status(bool reset);
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
                                       at::Tensor B, at::Tensor S, at::Tensor dS);
 // gather.cu
@@ -189,6 +190,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ema") = std::vector<at::Tensor>{}, py::arg("ema_weight") = 0.0);
   m.def("sum_squares", &cqb::sum_squares);
   m.def("gdn_prep", &cqb::gdn_prep);
+  m.def("gdn_status", &cqb::gdn_status, py::arg("reset") = false);
   m.def("gdn_chunk_bwd", &cqb::gdn_chunk_bwd);
   m.def("gather_rows", &cqb::gather_rows);
   m.def("gather_rows_bwd", &cqb::gather_rows_bwd);

@@ -11,6 +11,7 @@
 // chunked form used by the reference's GDN backends (ops/gated_delta_net.py:143-214).
 #include "common.cuh"
 #include "mma_sync.cuh"
+#include "tcgen05.cuh"
 
 namespace cqb {
 
@@ -803,6 +804,240 @@ __global__ void __launch_bounds__(THREADS_C, 1) gdn_chunk_bwd_kernel(BwdArgs a) 
   }
 }
 
+// ---- tcgen05 chunk preparation ------------------------------------------------------------------
+//
+// Same outputs as gdn_prep_kernel. One CTA per (chunk, head), 256 threads, two CTAs per SM (about
+// 102 KB of shared memory and 256 TMEM columns each). Thread 0 loads K, Q and V with TMA (128-byte
+// swizzle, K and Q stacked as one 128-row tile) and issues the tensor-core products; all eight warps
+// run the element-wise steps on TMEM rows (warp w reads lanes 32 (w % 4) ..+31, and warps w and
+// w + 4 split the columns):
+//   1. G = [K; Q] K^T: one M = 128 product (rows 0-63 K K^T, rows 64-127 Q K^T; N = 64, K = 128)
+//      -> the masked, decayed A = tril(beta K K^T E, -1) (fp32, shared) and P = tril(Q K^T E) (bf16)
+//   2. T = (I + A)^-1 on the CUDA cores (fp32), then Tw = T diag(beta e^b), Tv = T diag(beta) as
+//      bf16 K-major tiles
+//   3. W^T = K^T Tw^T and U^T = V^T Tv^T (M = 128 key / value dims, N = 64 events, K = 64): K and V
+//      are read as the MN-major A operand, so no transposed copy is made; the rows leave through a
+//      row-major staging tile in [event][dim] order.
+// Qd = e^b Q and Kt = e^{b_C - b} K are written from the swizzled tiles while product 1 runs. Every
+// wait is bounded (status codes 41-43); on expiry the CTA stops issuing, waits (bounded) for what
+// it has in flight, frees its TMEM and returns.
+constexpr int TC_THREADS = 256;
+constexpr uint32_t TC_ATOM_KQ = 128 * 128;           // one 64-column atom of the stacked [K; Q] tile
+constexpr uint32_t TC_KQ = 0;                        // [2 atoms][128 rows][128 B]
+constexpr uint32_t TC_ATOM_V = 64 * 128;
+constexpr uint32_t TC_V = TC_KQ + 2 * TC_ATOM_KQ;    // [2 atoms][64 rows][128 B]
+constexpr uint32_t TC_TW = TC_V + 2 * TC_ATOM_V;     // [64 rows][128 B]
+constexpr uint32_t TC_TV = TC_TW + 64 * 128;
+constexpr uint32_t TC_A = TC_TV + 64 * 128;          // fp32 [64][LDF]
+constexpr uint32_t TC_T = TC_A + CH * LDF * 4;
+constexpr uint32_t TC_Y = TC_T + CH * LDF * 4;       // inverse scratch, 3 x 16 x 17 floats
+constexpr uint32_t TC_VEC = TC_Y + 3 * 16 * 17 * 4;  // b, e^b, e^{b_C - b}, beta, g
+constexpr uint32_t TC_BAR = (TC_VEC + 5 * CH * 4 + 7) & ~7u;
+constexpr uint32_t TC_SMEM = TC_BAR + 64 + 1024;     // + slack to align the base to 1024 bytes
+constexpr int TC_TMEM_COLS = 256;                    // G: 0-63, W^T: 64-127, U^T: 128-191
+constexpr int TC_OUT_LD = DH + 8;                    // bf16 row of the W / U staging tiles
+static_assert(2 * CH * TC_OUT_LD * 2 <= TC_TW, "W / U staging must fit in the K, Q, V tiles");
+static_assert(2 * TC_SMEM <= 232448, "two preparation CTAs must fit on one SM");
+
+int* gdn_status_word() {
+  static int* word = [] {
+    int* p = nullptr;
+    CQB_CHECK_CUDA(cudaMalloc(&p, sizeof(int)));
+    CQB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+    return p;
+  }();
+  return word;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 2)
+    gdn_prep_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, PrepArgs a, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kq = smem + TC_KQ;
+  uint8_t* sv = smem + TC_V;
+  uint8_t* tw = smem + TC_TW;
+  uint8_t* tv = smem + TC_TV;
+  float* sA = reinterpret_cast<float*>(smem + TC_A);
+  float* sT = reinterpret_cast<float*>(smem + TC_T);
+  float* sY = reinterpret_cast<float*>(smem + TC_Y);
+  float* sb = reinterpret_cast<float*>(smem + TC_VEC);
+  float* seb = sb + CH;
+  float* skd = seb + CH;
+  float* sbeta = skd + CH;
+  float* sg = sbeta + CH;
+  uint64_t* load_bar = reinterpret_cast<uint64_t*>(smem + TC_BAR);
+  uint64_t* mma_bar = load_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(load_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int unit = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const size_t tile_off = (size_t)unit * CH * DH;
+  if (tid == 0) {
+    tc::mbar_init(load_bar, 1);
+    tc::mbar_init(mma_bar, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) tc::tmem_alloc(tmem_slot, TC_TMEM_COLS);
+  if (tid < CH) {
+    sg[tid] = a.G[(size_t)unit * CH + tid];
+    sbeta[tid] = a.B[(size_t)unit * CH + tid];
+  }
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    tc::prefetch_map(&map_q);
+    tc::prefetch_map(&map_k);
+    tc::prefetch_map(&map_v);
+    tc::mbar_expect_tx(load_bar, 3 * CH * DH * 2);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      tc::tma_load_2d(kq + h * TC_ATOM_KQ, &map_k, load_bar, h * 64, unit * CH);
+      tc::tma_load_2d(kq + h * TC_ATOM_KQ + CH * 128, &map_q, load_bar, h * 64, unit * CH);
+      tc::tma_load_2d(sv + h * TC_ATOM_V, &map_v, load_bar, h * 64, unit * CH);
+    }
+  }
+  if (warp == 1) {
+    const float bc = chunk_decay(sg, sb, seb, skd, lane);
+    if (lane == 0) a.gamma[unit] = __expf(bc);
+  }
+  bool load_seen = tc::mbar_wait(load_bar, 0, status, abort_flag, 41);
+  bool ok = __syncthreads_and(load_seen);   // also publishes the decay vectors
+  bool mma1 = false, mma2 = false;
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
+    const uint32_t base = tc::smem_u32(kq);
+#pragma unroll
+    for (int k = 0; k < DH / 16; ++k) {
+      const uint32_t off = (k >> 2) * TC_ATOM_KQ + (k & 3) * 32;
+      tc::mma_bf16(tmem, tc::smem_desc(base + off, 16, 1024), tc::smem_desc(base + off, 16, 1024), idesc, k > 0);
+    }
+    tc::mma_commit(mma_bar);
+  }
+  mma1 = ok;
+  if (ok) {   // Qd = e^b Q (Q: rows 64-127 of the stacked tile), Kt = e^{b_C - b} K
+    for (int e = tid; e < 2 * CH * 16; e += TC_THREADS) {
+      const int kt = e >= CH * 16, r = (e >> 4) & (CH - 1), ch = e & 15;
+      const uint8_t* src = kq + (ch >> 3) * TC_ATOM_KQ + (kt ? 0 : CH * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+      float v[8];
+      load8(reinterpret_cast<const __nv_bfloat16*>(src), v);
+      const float sc = kt ? skd[r] : seb[r];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= sc;
+      store8((kt ? a.Kt : a.Qd) + tile_off + r * DH + ch * 8, v);
+    }
+  }
+  bool seen1 = !mma1 || tc::mbar_wait(mma_bar, 0, status, abort_flag, 42);
+  ok = __syncthreads_and(ok && seen1);
+  tc::fence_after();
+  const int quad = warp & 3, half = warp >> 2, row = 32 * quad + lane;
+  const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
+  if (ok) {
+    float v[32];
+    tc::tmem_ld32(lane_base + 32 * half, v);
+    if (row < CH) {   // A row i
+      const float bi = sb[row], be = sbeta[row];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int j = 32 * half + c;
+        sA[row * LDF + j] = j < row ? be * v[c] * __expf(bi - sb[j]) : 0.f;
+      }
+    } else {          // P row i
+      const int i = row - CH;
+      const float bi = sb[i];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int j = 32 * half + c;
+        v[c] = j <= i ? v[c] * __expf(bi - sb[j]) : 0.f;
+      }
+      __nv_bfloat16* dst = a.P + ((size_t)unit * CH + i) * CH + 32 * half;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) store8(dst + 8 * q, v + 8 * q);
+    }
+  }
+  __syncthreads();
+  unit_lower_inverse(sA, sT, sY, warp, lane);
+  for (int e = tid; e < CH * 8; e += TC_THREADS) {   // Tw, Tv: row i, 16-byte chunk ch (8 columns)
+    const int i = e >> 3, ch = e & 7;
+    float w8[8], v8[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = 8 * ch + q;
+      const float t = sT[i * LDF + j] * sbeta[j];
+      v8[q] = t;
+      w8[q] = t * seb[j];
+    }
+    const uint32_t off = i * 128 + ((ch ^ (i & 7)) << 4);
+    store8(reinterpret_cast<__nv_bfloat16*>(tw + off), w8);
+    store8(reinterpret_cast<__nv_bfloat16*>(tv + off), v8);
+  }
+  tc::fence_proxy_async();
+  __syncthreads();
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t idesc = tc::idesc_bf16(128, 64, true, false);   // A = K^T / V^T, MN-major
+    const uint32_t kb = tc::smem_u32(kq), vb = tc::smem_u32(sv), wb = tc::smem_u32(tw), ub = tc::smem_u32(tv);
+#pragma unroll
+    for (int k = 0; k < CH / 16; ++k) {
+      tc::mma_bf16(tmem + 64, tc::smem_desc(kb + k * 2048, TC_ATOM_KQ, 1024), tc::smem_desc(wb + k * 32, 16, 1024),
+                   idesc, k > 0);
+      tc::mma_bf16(tmem + 128, tc::smem_desc(vb + k * 2048, TC_ATOM_V, 1024), tc::smem_desc(ub + k * 32, 16, 1024),
+                   idesc, k > 0);
+    }
+    tc::mma_commit(mma_bar);
+  }
+  mma2 = ok;
+  bool seen2 = !mma2 || tc::mbar_wait(mma_bar, 1, status, abort_flag, 43);
+  ok = __syncthreads_and(ok && seen2);
+  tc::fence_after();
+  __nv_bfloat16* stw = reinterpret_cast<__nv_bfloat16*>(smem + TC_KQ);   // the products have retired
+  __nv_bfloat16* stu = stw + CH * TC_OUT_LD;
+  if (ok) {
+    float v[32];
+    tc::tmem_ld32(lane_base + 64 + 32 * half, v);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) stw[(32 * half + c) * TC_OUT_LD + row] = __float2bfloat16(v[c]);
+    tc::tmem_ld32(lane_base + 128 + 32 * half, v);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) stu[(32 * half + c) * TC_OUT_LD + row] = __float2bfloat16(v[c]);
+  }
+  __syncthreads();
+  if (ok) {
+    for (int e = tid; e < 2 * CH * 16; e += TC_THREADS) {
+      const int second = e >= CH * 16, r = (e >> 4) & (CH - 1), ch = e & 15;
+      const __nv_bfloat16* src = (second ? stu : stw) + r * TC_OUT_LD + ch * 8;
+      *reinterpret_cast<uint4*>((second ? a.U : a.W) + tile_off + r * DH + ch * 8) =
+          *reinterpret_cast<const uint4*>(src);
+    }
+  }
+  if (tid == 0) {   // nothing issued by this CTA is still in flight when it retires (bounded)
+    const unsigned long long t0 = tc::globaltimer();
+    if (!load_seen)
+      while (!tc::mbar_try_wait(load_bar, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    if (mma1 && !seen1)
+      while (!tc::mbar_try_wait(mma_bar, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    if (mma2 && !seen2)
+      while (!tc::mbar_try_wait(mma_bar, 1) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, TC_TMEM_COLS);
+}
+
+bool gdn_use_tc() {
+  static const bool on = [] {
+    const char* v = std::getenv("CQB_GDN_TC");
+    return v == nullptr || std::string(v) != "0";
+  }();
+  return on;
+}
+
 void check_tile(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.scalar_type() == at::kBFloat16 && t.dim() == 4 &&
                   t.size(2) == CH && t.size(3) == DH,
@@ -829,16 +1064,37 @@ std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::T
              (const __nv_bfloat16*)V.data_ptr(), G.data_ptr<float>(), B.data_ptr<float>(),
              (__nv_bfloat16*)W.data_ptr(), (__nv_bfloat16*)U.data_ptr(), (__nv_bfloat16*)P.data_ptr(),
              (__nv_bfloat16*)Qd.data_ptr(), (__nv_bfloat16*)Kt.data_ptr(), gamma.data_ptr<float>()};
-  static bool once = [] {
-    CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)PREP_SMEM));
-    return true;
-  }();
-  (void)once;
-  gdn_prep_kernel<<<(unsigned)(Nc * H), THREADS_C, PREP_SMEM, stream()>>>(a);
+  if (gdn_use_tc()) {
+    static bool once_tc = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_prep_tc_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+      return true;
+    }();
+    (void)once_tc;
+    const auto mq = tma_map_bf16(Q.view({Nc * H * CH, DH}), CH);
+    const auto mk = tma_map_bf16(K.view({Nc * H * CH, DH}), CH);
+    const auto mv = tma_map_bf16(V.view({Nc * H * CH, DH}), CH);
+    gdn_prep_tc_kernel<<<(unsigned)(Nc * H), TC_THREADS, TC_SMEM, stream()>>>(mq, mk, mv, a, gdn_status_word());
+  } else {
+    static bool once = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)PREP_SMEM));
+      return true;
+    }();
+    (void)once;
+    gdn_prep_kernel<<<(unsigned)(Nc * H), THREADS_C, PREP_SMEM, stream()>>>(a);
+  }
   CQB_LAUNCH_CHECK();
   count_launch();
   return {W, U, P, Qd, Kt, gamma};
+}
+
+// Status word of the tcgen05 GDN kernels (0 = no wait expired); optionally cleared.
+int64_t gdn_status(bool reset) {
+  int v = 0;
+  CQB_CHECK_CUDA(cudaMemcpy(&v, gdn_status_word(), sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset && v) CQB_CHECK_CUDA(cudaMemset(gdn_status_word(), 0, sizeof(int)));
+  return v;
 }
 
 // Returns (dQ, dK, dV fp32 [Nc, H, 64, 128], dG, dBeta fp32 [Nc, H, 64]).

@@ -67,6 +67,7 @@ def test_gdn_prep_matches_factors():
         want = f[name].float()
         rel = (got.float() - want).norm() / want.norm().clamp_min(1e-12)
         assert rel < 1.5e-2, (name, rel.item())
+    assert _ext.ops().gdn_status(True) == 0     # no bounded wait of the tcgen05 kernel expired
 
 
 def test_gdn_chunk_backward_matches_reference():
