@@ -60,7 +60,8 @@ def main():
         ps.destroy()
         return
     events = prof.key_averages()
-    kernels = [e for e in events if e.device_type.name == "CUDA"]
+    phase_names = {"forward", "backward", "renderer_forward", "renderer_backward", "optimizer"}
+    kernels = [e for e in events if e.device_type.name == "CUDA" and e.key not in phase_names]
     total = sum(e.self_device_time_total for e in kernels)
     rows = sorted(kernels, key=lambda e: -e.self_device_time_total)[: args.top]
     print(json.dumps(dict(total_device_ms=round(total / 1000, 2), peak_gib=round(torch.cuda.max_memory_allocated() / 2**30, 1))))
