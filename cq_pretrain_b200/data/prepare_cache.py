@@ -6,7 +6,7 @@ that carries pixels (``pixels`` uint8 ``[H, W, 3]`` or a ``path``) and a ``sourc
 (e.g. the image sha256) computes what is missing:
 
 * merger features: native-resolution preprocessing (``data/vision.py``) → frozen vision tower;
-* latents: pixels resized to the generation geometry → the latent encoder (the Wan VAE when its
+* latents: pixels resized to the generation geometry → the latent encoder (the Wan VAE, ``--latent-encoder wan``, when its
   weights are available; ``FakeLatentEncoder`` for pipeline runs without them).
 
 Entries are content-addressed and published atomically, so any number of ranks can run at once
@@ -74,7 +74,8 @@ def prepare(cfg, corpus, cache_root, rank=0, world=1, device="cpu", vision=None,
                 h = max(16, (x.shape[2] // 16) * 16)
                 w = max(16, (x.shape[3] // 16) * 16)
                 x = torch.nn.functional.interpolate(x, size=(h, w), mode="bilinear", align_corners=False)
-                latent = encoder.encode(x.to(device))
+                images = getattr(encoder, "encode_images", None)     # the Wan codec: one-frame videos
+                latent = images(x.to(device)) if images is not None else encoder.encode(x.to(device))
                 if isinstance(latent, tuple):    # posterior (mean, std) encoders cache the mean
                     latent = latent[0]
                 latent = latent[:, :, None]      # [1, C, T=1, h/stride, w/stride]
@@ -92,9 +93,11 @@ def main(argv=None):
     parser.add_argument("--rank", type=int, default=0)
     parser.add_argument("--world", type=int, default=1)
     parser.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
-    parser.add_argument("--latent-encoder", choices=("fake", "kl16"), default="fake",
-                        help="kl16: the legacy renderer's KL16 VAE (needs --kl16-checkpoint)")
+    parser.add_argument("--latent-encoder", choices=("fake", "kl16", "wan"), default="fake",
+                        help="kl16: the legacy renderer's KL16 VAE (needs --kl16-checkpoint); wan: the Wan2.1 VAE "
+                             "(needs --wan-vae)")
     parser.add_argument("--kl16-checkpoint", default=None)
+    parser.add_argument("--wan-vae", default=None, help="Wan2.1_VAE.pth or the directory holding it")
     args = parser.parse_args(argv)
     from ..config import load_sections, qwen35_2b_wan
     cfg = load_sections(args.config)[0] if args.config else qwen35_2b_wan()
@@ -105,6 +108,11 @@ def main(argv=None):
             raise SystemExit("--latent-encoder kl16 needs --kl16-checkpoint")
         from ..models.kl16 import FrozenKL16
         encoder = FrozenKL16(args.kl16_checkpoint, dtype=torch.float32, device=args.device)
+    elif args.latent_encoder == "wan":
+        if not args.wan_vae:
+            raise SystemExit("--latent-encoder wan needs --wan-vae")
+        from .wan_codec import WanVideoCodec
+        encoder = WanVideoCodec.from_pretrained(args.wan_vae, device=args.device)
     counts = prepare(cfg, args.corpus, args.cache, args.rank, args.world, args.device, encoder=encoder, dtype=dtype)
     print(json.dumps(dict(status="complete", **counts)), flush=True)
 
