@@ -90,12 +90,20 @@ def joint_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), latent
     return docs
 
 
-def video_pack_documents(cfg, length, seed=0, grid=(8, 60, 104), latent_shape=(16, 21, 60, 104), text=4096):
-    """one T2V target (81 frames at 480x832 -> 32,760 DiT tokens) plus text."""
+def video_pack_documents(cfg, length, seed=0, grid=(4, 30, 52), latent_shape=(16, 21, 60, 104), text=4096,
+                         understanding=True):
+    """one T2V target (81 frames at 480x832 -> 32,760 DiT tokens; Qwen content 8
+    frames -> 1,560 merged tokens and 1,560 queries), with ``understanding`` one V2T document of the
+    same geometry (video, then its caption as the text target), plus ``text`` tokens of text
+    documents."""
     rng = np.random.default_rng(seed)
     docs = [dict(id=f"video-{seed}", direction="T2V", format="caption",
                  elements=[dict(type="text", input_ids=text_ids(rng, 64, cfg.vocab_size)),
                            visual_element(cfg, rng, grid, latent_shape)])]
+    if understanding:
+        docs.append(dict(id=f"video-v2t-{seed}", direction="V2T", format="caption",
+                         elements=[visual_element(cfg, rng, grid, latent_shape, generate=False),
+                                   dict(type="text", input_ids=text_ids(rng, 64, cfg.vocab_size))]))
     lo, hi = math.log(64), math.log(4096)
     used, k = 0, 0
     while used < text:

@@ -87,11 +87,15 @@ class _Entry:
 
 
 class RendererGraphs:
-    def __init__(self, optimizer=None, capacity=4, capture_after=1):
-        """``capture_after``: eager sightings of a geometry before it is captured."""
+    def __init__(self, optimizer=None, capacity=4, capture_after=1, max_tokens=16384):
+        """``capture_after``: eager sightings of a geometry before it is captured. Chunks of more
+        than ``max_tokens`` DiT tokens run eagerly: a graph keeps its activations in its own memory
+        pool between replays, which the backbone backward could otherwise reuse, and such chunks
+        are long enough that launching from the host does not starve the GPU."""
         self.optimizer = optimizer
         self.capacity = capacity
         self.capture_after = capture_after
+        self.max_tokens = max_tokens
         self.entries: OrderedDict = OrderedDict()
         self.pool = None
         self.replays = 0
@@ -102,6 +106,9 @@ class RendererGraphs:
         return (spec, tuple(leaf.shape), str(leaf.dtype), torch.is_grad_enabled()), tensors
 
     def run(self, model, leaf, bound, factor):
+        lengths = getattr(getattr(bound, "generation", None), "lengths", ())
+        if sum(lengths) > self.max_tokens:
+            return self._eager(model, leaf, bound, factor)
         key, tensors = self._key(leaf, bound)
         entry = self.entries.get(key)
         if entry is None:
