@@ -9,8 +9,11 @@
 // fp32 accumulators; the fp32 state lives in registers, a bf16 copy in shared memory feeds
 // the next products; chunk inputs are double-buffered with cp.async.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace cqb {
+
+int* gdn_status_word();   // gdn_chunk.cu
 
 namespace {
 
@@ -361,6 +364,437 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_bwd_kernel(GdnArgs a) {
   }
 }
 
+// ---- forward on tcgen05 ---------------------------------------------------------------------
+//
+// Same contract as gdn_fwd_kernel for a value dim of 128: one CTA per (document, head), 256 threads,
+// one CTA per SM. The fp32 state S [dk x dv] stays in TMEM (lanes = dk, columns 0-127) for the whole
+// document; per chunk, with S's bf16 copy in shared memory as the MN-major A operand S^T:
+//   group 1: D^T = S^T W^T, O^T = S^T Qd^T                  (M = 128 value dims, N = 64 events)
+//   epilogue: D^T <- U^T - D^T (bf16 K-major tile); S entering is written out (fp32) and scaled by
+//             gamma in TMEM
+//   group 2: O^T += D^T P^T; S += Kt^T D                     (Kt as the MN-major A operand)
+//   epilogue: O leaves through a staging tile; the new S becomes the next chunk's bf16 operand.
+// Thread 0 streams each chunk's W, Qd, Kt, U (two 64-column TMA boxes each) and P into a two-deep
+// ring one chunk ahead and issues the MMAs; warp w reads TMEM lanes 32 (w % 4)..+31, warps w and
+// w + 4 split the columns. Bounded waits (status codes 51-53); on expiry the CTA stops issuing,
+// waits (bounded) for what it has in flight, frees its TMEM and returns.
+constexpr int TF_THREADS = 256;
+constexpr uint32_t TF_TILE = 64 * 128 * 2;                 // one [64][128] bf16 tile: 2 swizzle atoms of 8 KB
+constexpr uint32_t TF_P = 64 * 64 * 2;
+constexpr uint32_t TF_BUF = 4 * TF_TILE + TF_P;            // W, Qd, Kt, U, P
+constexpr uint32_t TF_S = 2 * TF_BUF;                      // bf16 S [2 atoms][128 rows dk][128 B]
+constexpr uint32_t TF_DT = TF_S + 2 * 128 * 128;           // bf16 D^T [128 rows dv][128 B (64 events)]
+constexpr uint32_t TF_O = TF_DT + 128 * 128;               // bf16 O staging [64][128] row-major
+constexpr uint32_t TF_BAR = TF_O + 64 * 128 * 2;
+constexpr uint32_t TF_SMEM = TF_BAR + 64 + 1024;
+constexpr int TF_TMEM_COLS = 256;                          // S 0-127, D^T 128-191, O^T 192-255
+static_assert(TF_SMEM <= 232448, "forward recurrence tile set exceeds one CTA's shared memory");
+
+__device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t col) {   // byte offset of (row, col) in a 64-col atom
+  return row * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2;
+}
+
+__global__ void __launch_bounds__(TF_THREADS, 1)
+    gdn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_q,
+                      const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_u,
+                      const __grid_constant__ CUtensorMap map_p, GdnArgs a, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sS = smem + TF_S;
+  uint8_t* sDT = smem + TF_DT;
+  __nv_bfloat16* sO = reinterpret_cast<__nv_bfloat16*>(smem + TF_O);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TF_BAR);   // [2]
+  uint64_t* bar1 = full + 2;
+  uint64_t* bar2 = full + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int doc = blockIdx.y, h = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, hf = warp >> 2, row = 32 * quad + lane;
+  const int c0 = a.chunk_start[doc], nc = a.chunk_count[doc];
+  if (nc == 0) {
+    if (a.final)   // an empty document leaves the zero state
+      for (int i = tid; i < DK * 128; i += TF_THREADS) a.final[((size_t)doc * a.H + h) * DK * 128 + i] = 0.f;
+    return;
+  }
+  if (tid == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_init(bar1, 1);
+    tc::mbar_init(bar2, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) tc::tmem_alloc(tmem_slot, TF_TMEM_COLS);
+  for (int i = tid; i < 2 * 128 * 128 / 16; i += TF_THREADS)   // S = 0: bf16 copy
+    reinterpret_cast<uint4*>(sS)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
+  {
+    float z[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) z[j] = 0.f;
+    tc::tmem_st32(lane_base + 64 * hf, z);         // S = 0 in TMEM (this warp's half of the columns)
+    tc::tmem_st32(lane_base + 64 * hf + 32, z);
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+
+  auto issue_load = [&](int ci) {
+    uint8_t* buf = smem + (ci & 1) * TF_BUF;
+    uint64_t* bar = &full[ci & 1];
+    const int r0 = ((c0 + ci) * a.H + h) * C;
+    tc::mbar_expect_tx(bar, TF_BUF);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      tc::tma_load_2d(buf + x * (TF_TILE / 2), &map_w, bar, 64 * x, r0);
+      tc::tma_load_2d(buf + TF_TILE + x * (TF_TILE / 2), &map_q, bar, 64 * x, r0);
+      tc::tma_load_2d(buf + 2 * TF_TILE + x * (TF_TILE / 2), &map_k, bar, 64 * x, r0);
+      tc::tma_load_2d(buf + 3 * TF_TILE + x * (TF_TILE / 2), &map_u, bar, 64 * x, r0);
+    }
+    tc::tma_load_2d(buf + 4 * TF_TILE, &map_p, bar, 0, r0);
+  };
+  int loads_issued = 0, loads_seen = 0;
+  uint64_t* pending = nullptr;   // barrier of the MMA group thread 0 issued and has not seen complete
+  uint32_t pending_parity = 0;
+  if (tid == 0) {
+    tc::prefetch_map(&map_w);
+    tc::prefetch_map(&map_q);
+    tc::prefetch_map(&map_k);
+    tc::prefetch_map(&map_u);
+    tc::prefetch_map(&map_p);
+    issue_load(0);
+    loads_issued = 1;
+  }
+  bool ok = true;
+  constexpr uint32_t idesc_g1 = tc::idesc_bf16(128, 64, true, false);
+  constexpr uint32_t idesc_o = tc::idesc_bf16(128, 64, false, false);
+  constexpr uint32_t idesc_s = tc::idesc_bf16(128, 128, true, false);
+  const uint32_t s_addr = tc::smem_u32(sS), dt_addr = tc::smem_u32(sDT);
+  for (int ci = 0; ci < nc && ok; ++ci) {
+    const int c = c0 + ci;
+    uint8_t* buf = smem + (ci & 1) * TF_BUF;
+    const uint32_t w_addr = tc::smem_u32(buf), q_addr = w_addr + TF_TILE, k_addr = w_addr + 2 * TF_TILE;
+    const uint32_t p_addr = w_addr + 4 * TF_TILE;
+    const uint8_t* sU = buf + 3 * TF_TILE;
+    if (tid == 0) {
+      if (ci + 1 < nc) {   // the other buffer's readers (chunk ci - 1) have all finished
+        issue_load(ci + 1);
+        ++loads_issued;
+      }
+      if (tc::mbar_wait(&full[ci & 1], (ci >> 1) & 1, status, abort_flag, 51)) {
+        ++loads_seen;
+        tc::fence_after();
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k) {
+          const uint64_t st = tc::smem_desc(s_addr + k * 2048, 16384, 1024);
+          const uint32_t boff = (k >> 2) * (TF_TILE / 2) + (k & 3) * 32;
+          tc::mma_bf16(tmem + 128, st, tc::smem_desc(w_addr + boff, 16, 1024), idesc_g1, k > 0);
+          tc::mma_bf16(tmem + 192, st, tc::smem_desc(q_addr + boff, 16, 1024), idesc_g1, k > 0);
+        }
+        tc::mma_commit(bar1);
+        pending = bar1;
+        pending_parity = (uint32_t)(ci & 1);
+      }
+    }
+    const bool seen1 = tc::mbar_wait(bar1, ci & 1, status, abort_flag, 52);
+    ok = __syncthreads_and(seen1);
+    if (!ok) break;
+    pending = nullptr;
+    tc::fence_after();
+    {
+      // D^T rows (value dim v = row), events [32 hf, 32 hf + 32): D^T = U^T - S^T W^T
+      float x[32];
+      tc::tmem_ld32(lane_base + 128 + 32 * hf, x);
+      const uint32_t uatom = (row >> 6) * (TF_TILE / 2), ucol = row & 63;
+#pragma unroll
+      for (int j8 = 0; j8 < 4; ++j8) {
+        float d[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int i = 32 * hf + 8 * j8 + q;
+          const float u = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(sU + uatom + sw128(i, ucol)));
+          d[q] = u - x[8 * j8 + q];
+        }
+        store8(reinterpret_cast<__nv_bfloat16*>(sDT + sw128(row, 32 * hf + 8 * j8)), d);
+      }
+      // S rows (key dim d = row), value columns [64 hf, 64 hf + 64): save S entering, scale by gamma
+      const float gm = a.gamma[(size_t)c * a.H + h];
+      float* dst = a.states + (((size_t)c * a.H + h) * DK + row) * 128 + 64 * hf;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float sv[32];
+        tc::tmem_ld32(lane_base + 64 * hf + 32 * half, sv);
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4*>(dst + 32 * half + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) sv[q] *= gm;
+        tc::tmem_st32(lane_base + 64 * hf + 32 * half, sv);
+      }
+    }
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after();
+#pragma unroll
+      for (int k = 0; k < C / 16; ++k) {
+        const uint64_t dt = tc::smem_desc(dt_addr + k * 32, 16, 1024);
+        tc::mma_bf16(tmem + 192, dt, tc::smem_desc(p_addr + k * 32, 16, 1024), idesc_o, 1u);
+        tc::mma_bf16(tmem, tc::smem_desc(k_addr + k * 2048, TF_TILE / 2, 1024), dt, idesc_s, 1u);
+      }
+      tc::mma_commit(bar2);
+      pending = bar2;
+      pending_parity = (uint32_t)(ci & 1);
+    }
+    const bool seen2 = tc::mbar_wait(bar2, ci & 1, status, abort_flag, 53);
+    ok = __syncthreads_and(seen2);
+    if (!ok) break;
+    pending = nullptr;
+    tc::fence_after();
+    {
+      float o[32];
+      tc::tmem_ld32(lane_base + 192 + 32 * hf, o);   // O^T row v = row, events [32 hf, +32)
+#pragma unroll
+      for (int q = 0; q < 32; ++q) sO[(32 * hf + q) * 128 + row] = __float2bfloat16(o[q]);
+      const bool last = ci + 1 == nc;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float sv[32];
+        tc::tmem_ld32(lane_base + 64 * hf + 32 * half, sv);   // new S, row d = row
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8)
+          store8(reinterpret_cast<__nv_bfloat16*>(sS + hf * 16384 + sw128(row, 32 * half + 8 * q8)), sv + 8 * q8);
+        if (last && a.final) {
+          float* fin = a.final + (((size_t)doc * a.H + h) * DK + row) * 128 + 64 * hf + 32 * half;
+#pragma unroll
+          for (int q = 0; q < 32; q += 4) *reinterpret_cast<float4*>(fin + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
+        }
+      }
+    }
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    {
+      __nv_bfloat16* out = a.out + ((size_t)c * a.H + h) * C * 128;
+      for (int e = tid; e < C * 128 / 8; e += TF_THREADS)
+        reinterpret_cast<uint4*>(out)[e] = reinterpret_cast<const uint4*>(sO)[e];
+    }
+    __syncthreads();   // sO and this buffer's U are free again
+  }
+  if (tid == 0) {   // nothing issued by this CTA is in flight when it retires (bounded)
+    const unsigned long long t0 = tc::globaltimer();
+    for (int l = loads_seen; l < loads_issued; ++l)
+      while (!tc::mbar_try_wait(&full[l & 1], (l >> 1) & 1) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    if (pending != nullptr)
+      while (!tc::mbar_try_wait(pending, pending_parity) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, TF_TMEM_COLS);
+}
+
+// ---- backward recurrence on tcgen05 -------------------------------------------------------------
+//
+// Same contract as gdn_bwd_kernel for a value dim of 128: one CTA per (document, head) walks the
+// chunks from last to first with dS [dk x dv] (fp32) in TMEM (lanes = dk, columns 0-127):
+//   group 1: dD^T = dO^T P + dS^T Kt^T      (M = 128 value dims, N = 64 events; dO, P and dS as
+//                                             MN-major operands)
+//   epilogue: -dD^T -> bf16 K-major tile; dS entering from the right is written out (fp32) and
+//             scaled by gamma in TMEM
+//   group 2: dS += Qd^T dO + W^T (-dD)       (Qd, W as MN-major A operands)
+//   epilogue: the new dS becomes the bf16 operand of the previous chunk.
+// Loads, warp roles and bounded waits (status codes 54-56) as in gdn_fwd_tc_kernel.
+__global__ void __launch_bounds__(TF_THREADS, 1)
+    gdn_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_q,
+                      const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_do,
+                      const __grid_constant__ CUtensorMap map_p, GdnArgs a, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sS = smem + TF_S;     // bf16 dS
+  uint8_t* sDT = smem + TF_DT;   // bf16 -dD^T
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TF_BAR);   // [2]
+  uint64_t* bar1 = full + 2;
+  uint64_t* bar2 = full + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int doc = blockIdx.y, h = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, hf = warp >> 2, row = 32 * quad + lane;
+  const int c0 = a.chunk_start[doc], nc = a.chunk_count[doc];
+  if (nc == 0) return;
+  if (tid == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_init(bar1, 1);
+    tc::mbar_init(bar2, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) tc::tmem_alloc(tmem_slot, TF_TMEM_COLS);
+  for (int i = tid; i < 2 * 128 * 128 / 16; i += TF_THREADS) reinterpret_cast<uint4*>(sS)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
+  {
+    float z[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) z[j] = 0.f;
+    tc::tmem_st32(lane_base + 64 * hf, z);
+    tc::tmem_st32(lane_base + 64 * hf + 32, z);
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+
+  auto issue_load = [&](int it) {   // iteration it processes chunk c0 + nc - 1 - it
+    uint8_t* buf = smem + (it & 1) * TF_BUF;
+    uint64_t* bar = &full[it & 1];
+    const int r0 = ((c0 + nc - 1 - it) * a.H + h) * C;
+    tc::mbar_expect_tx(bar, TF_BUF);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      tc::tma_load_2d(buf + x * (TF_TILE / 2), &map_w, bar, 64 * x, r0);
+      tc::tma_load_2d(buf + TF_TILE + x * (TF_TILE / 2), &map_q, bar, 64 * x, r0);
+      tc::tma_load_2d(buf + 2 * TF_TILE + x * (TF_TILE / 2), &map_k, bar, 64 * x, r0);
+      tc::tma_load_2d(buf + 3 * TF_TILE + x * (TF_TILE / 2), &map_do, bar, 64 * x, r0);
+    }
+    tc::tma_load_2d(buf + 4 * TF_TILE, &map_p, bar, 0, r0);
+  };
+  int loads_issued = 0, loads_seen = 0;
+  uint64_t* pending = nullptr;
+  uint32_t pending_parity = 0;
+  if (tid == 0) {
+    tc::prefetch_map(&map_w);
+    tc::prefetch_map(&map_q);
+    tc::prefetch_map(&map_k);
+    tc::prefetch_map(&map_do);
+    tc::prefetch_map(&map_p);
+    issue_load(0);
+    loads_issued = 1;
+  }
+  bool ok = true;
+  constexpr uint32_t idesc_dop = tc::idesc_bf16(128, 64, true, true);     // dO^T P (both MN-major)
+  constexpr uint32_t idesc_dsk = tc::idesc_bf16(128, 64, true, false);    // dS^T Kt^T
+  constexpr uint32_t idesc_qdo = tc::idesc_bf16(128, 128, true, true);    // Qd^T dO
+  constexpr uint32_t idesc_wdd = tc::idesc_bf16(128, 128, true, false);   // W^T (-dD)
+  const uint32_t s_addr = tc::smem_u32(sS), dt_addr = tc::smem_u32(sDT);
+  for (int it = 0; it < nc && ok; ++it) {
+    const int c = c0 + nc - 1 - it;
+    uint8_t* buf = smem + (it & 1) * TF_BUF;
+    const uint32_t w_addr = tc::smem_u32(buf), q_addr = w_addr + TF_TILE, k_addr = w_addr + 2 * TF_TILE;
+    const uint32_t do_addr = w_addr + 3 * TF_TILE, p_addr = w_addr + 4 * TF_TILE;
+    if (tid == 0) {
+      if (it + 1 < nc) {
+        issue_load(it + 1);
+        ++loads_issued;
+      }
+      if (tc::mbar_wait(&full[it & 1], (it >> 1) & 1, status, abort_flag, 54)) {
+        ++loads_seen;
+        tc::fence_after();
+#pragma unroll
+        for (int k = 0; k < C / 16; ++k)
+          tc::mma_bf16(tmem + 128, tc::smem_desc(do_addr + k * 2048, TF_TILE / 2, 1024),
+                       tc::smem_desc(p_addr + k * 2048, TF_TILE / 2, 1024), idesc_dop, k > 0);
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k)
+          tc::mma_bf16(tmem + 128, tc::smem_desc(s_addr + k * 2048, 16384, 1024),
+                       tc::smem_desc(k_addr + (k >> 2) * (TF_TILE / 2) + (k & 3) * 32, 16, 1024), idesc_dsk, 1u);
+        tc::mma_commit(bar1);
+        pending = bar1;
+        pending_parity = (uint32_t)(it & 1);
+      }
+    }
+    const bool seen1 = tc::mbar_wait(bar1, it & 1, status, abort_flag, 55);
+    ok = __syncthreads_and(seen1);
+    if (!ok) break;
+    pending = nullptr;
+    tc::fence_after();
+    {
+      float x[32];
+      tc::tmem_ld32(lane_base + 128 + 32 * hf, x);   // dD^T row v = row, events [32 hf, +32)
+#pragma unroll
+      for (int q = 0; q < 32; ++q) x[q] = -x[q];
+#pragma unroll
+      for (int j8 = 0; j8 < 4; ++j8) store8(reinterpret_cast<__nv_bfloat16*>(sDT + sw128(row, 32 * hf + 8 * j8)), x + 8 * j8);
+      const float gm = a.gamma[(size_t)c * a.H + h];
+      float* dst = a.states + (((size_t)c * a.H + h) * DK + row) * 128 + 64 * hf;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float sv[32];
+        tc::tmem_ld32(lane_base + 64 * hf + 32 * half, sv);
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4*>(dst + 32 * half + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) sv[q] *= gm;
+        tc::tmem_st32(lane_base + 64 * hf + 32 * half, sv);
+      }
+    }
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after();
+#pragma unroll
+      for (int k = 0; k < C / 16; ++k) {
+        tc::mma_bf16(tmem, tc::smem_desc(q_addr + k * 2048, TF_TILE / 2, 1024),
+                     tc::smem_desc(do_addr + k * 2048, TF_TILE / 2, 1024), idesc_qdo, 1u);
+        tc::mma_bf16(tmem, tc::smem_desc(w_addr + k * 2048, TF_TILE / 2, 1024), tc::smem_desc(dt_addr + k * 32, 16, 1024),
+                     idesc_wdd, 1u);
+      }
+      tc::mma_commit(bar2);
+      pending = bar2;
+      pending_parity = (uint32_t)(it & 1);
+    }
+    const bool seen2 = tc::mbar_wait(bar2, it & 1, status, abort_flag, 56);
+    ok = __syncthreads_and(seen2);
+    if (!ok) break;
+    pending = nullptr;
+    tc::fence_after();
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float sv[32];
+      tc::tmem_ld32(lane_base + 64 * hf + 32 * half, sv);
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8)
+        store8(reinterpret_cast<__nv_bfloat16*>(sS + hf * 16384 + sw128(row, 32 * half + 8 * q8)), sv + 8 * q8);
+    }
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();   // the new dS operand is visible; this buffer is free again
+  }
+  if (tid == 0) {
+    const unsigned long long t0 = tc::globaltimer();
+    for (int l = loads_seen; l < loads_issued; ++l)
+      while (!tc::mbar_try_wait(&full[l & 1], (l >> 1) & 1) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    if (pending != nullptr)
+      while (!tc::mbar_try_wait(pending, pending_parity) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, TF_TMEM_COLS);
+}
+
+bool gdn_fwd_use_tc(int dv) {
+  static const bool on = [] {
+    const char* v = std::getenv("CQB_GDN_TC");
+    return v == nullptr || std::string(v) != "0";
+  }();
+  return on && dv == 128;
+}
+
 constexpr size_t SMEM = (size_t)(2 * BUF + DK * LDV + C * LDV) * sizeof(__nv_bfloat16);
 
 void check(const at::Tensor& t, const char* name, at::ScalarType dtype) {
@@ -414,10 +848,27 @@ std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Te
     F = at::empty({start.size(0), W.size(1), DK, U.size(3)}, W.options().dtype(at::kFloat));
     a.final = F.data_ptr<float>();
   }
-  static bool once = (set_smem((const void*)gdn_fwd_kernel), true);
-  (void)once;
-  dim3 grid(a.DV / BV, a.H, start.size(0));
-  gdn_fwd_kernel<<<grid, THREADS, SMEM, stream()>>>(a);
+  if (gdn_fwd_use_tc(a.DV)) {
+    static bool once_tc = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)TF_SMEM));
+      return true;
+    }();
+    (void)once_tc;
+    const long rows = W.size(0) * W.size(1) * C;
+    const auto mw = tma_map_bf16(W.view({rows, DK}), C);
+    const auto mq = tma_map_bf16(Qd.view({rows, DK}), C);
+    const auto mk = tma_map_bf16(Kt.view({rows, DK}), C);
+    const auto mu = tma_map_bf16(U.view({rows, 128}), C);
+    const auto mp = tma_map_bf16(P.view({rows, C}), C);
+    gdn_fwd_tc_kernel<<<dim3(a.H, start.size(0)), TF_THREADS, TF_SMEM, stream()>>>(mw, mq, mk, mu, mp, a,
+                                                                                  gdn_status_word());
+  } else {
+    static bool once = (set_smem((const void*)gdn_fwd_kernel), true);
+    (void)once;
+    dim3 grid(a.DV / BV, a.H, start.size(0));
+    gdn_fwd_kernel<<<grid, THREADS, SMEM, stream()>>>(a);
+  }
   CQB_LAUNCH_CHECK();
   count_launch();
   if (want_final) return {O, S, F};
@@ -430,10 +881,27 @@ at::Tensor gdn_bwd(at::Tensor dO, at::Tensor W, at::Tensor P, at::Tensor Qd, at:
   GdnArgs a = make_args(W, Qd, Kt, P, dO, gamma, start, count);
   auto dS = at::empty({W.size(0), W.size(1), DK, dO.size(3)}, W.options().dtype(at::kFloat));
   a.states = dS.data_ptr<float>();
-  static bool once = (set_smem((const void*)gdn_bwd_kernel), true);
-  (void)once;
-  dim3 grid(a.DV / BV, a.H, start.size(0));
-  gdn_bwd_kernel<<<grid, THREADS, SMEM, stream()>>>(a);
+  if (gdn_fwd_use_tc(a.DV)) {
+    static bool once_tc = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)TF_SMEM));
+      return true;
+    }();
+    (void)once_tc;
+    const long rows = W.size(0) * W.size(1) * C;
+    const auto mw = tma_map_bf16(W.view({rows, DK}), C);
+    const auto mq = tma_map_bf16(Qd.view({rows, DK}), C);
+    const auto mk = tma_map_bf16(Kt.view({rows, DK}), C);
+    const auto mo = tma_map_bf16(dO.view({rows, 128}), C);
+    const auto mp = tma_map_bf16(P.view({rows, C}), C);
+    gdn_bwd_tc_kernel<<<dim3(a.H, start.size(0)), TF_THREADS, TF_SMEM, stream()>>>(mw, mq, mk, mo, mp, a,
+                                                                                  gdn_status_word());
+  } else {
+    static bool once = (set_smem((const void*)gdn_bwd_kernel), true);
+    (void)once;
+    dim3 grid(a.DV / BV, a.H, start.size(0));
+    gdn_bwd_kernel<<<grid, THREADS, SMEM, stream()>>>(a);
+  }
   CQB_LAUNCH_CHECK();
   count_launch();
   return dS;

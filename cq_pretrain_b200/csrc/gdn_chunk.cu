@@ -15,6 +15,18 @@
 
 namespace cqb {
 
+// Status word of the tcgen05 GDN kernels (gdn_chunk.cu and gdn.cu): the first expired bounded
+// wait records its code here.
+int* gdn_status_word() {
+  static int* word = [] {
+    int* p = nullptr;
+    CQB_CHECK_CUDA(cudaMalloc(&p, sizeof(int)));
+    CQB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+    return p;
+  }();
+  return word;
+}
+
 namespace {
 
 using namespace ws;
@@ -838,16 +850,6 @@ constexpr int TC_TMEM_COLS = 256;                    // G: 0-63, W^T: 64-127, U^
 constexpr int TC_OUT_LD = DH + 8;                    // bf16 row of the W / U staging tiles
 static_assert(2 * CH * TC_OUT_LD * 2 <= TC_TW, "W / U staging must fit in the K, Q, V tiles");
 static_assert(2 * TC_SMEM <= 232448, "two preparation CTAs must fit on one SM");
-
-int* gdn_status_word() {
-  static int* word = [] {
-    int* p = nullptr;
-    CQB_CHECK_CUDA(cudaMalloc(&p, sizeof(int)));
-    CQB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
-    return p;
-  }();
-  return word;
-}
 
 __global__ void __launch_bounds__(TC_THREADS, 2)
     gdn_prep_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
