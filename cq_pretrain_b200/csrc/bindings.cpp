@@ -83,7 +83,7 @@ int attn_status(bool reset);
 std::vector<at::Tensor> gdn_prep(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor G, at::Tensor B);
 int64_t gdn_status(bool reset);
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
-                                      at::Tensor B, at::Tensor S, at::Tensor dS);
+                                      at::Tensor B, at::Tensor S, at::Tensor dS, c10::optional<at::Tensor> dgamma);
 // gather.cu
 at::Tensor gather_rows(at::Tensor src0, c10::optional<at::Tensor> src1, at::Tensor idx);
 std::vector<at::Tensor> gather_rows_bwd(at::Tensor grad, at::Tensor inv, int64_t n0, int64_t n1);
@@ -191,7 +191,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sum_squares", &cqb::sum_squares);
   m.def("gdn_prep", &cqb::gdn_prep);
   m.def("gdn_status", &cqb::gdn_status, py::arg("reset") = false);
-  m.def("gdn_chunk_bwd", &cqb::gdn_chunk_bwd);
+  m.def("gdn_chunk_bwd", &cqb::gdn_chunk_bwd, py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("dO"), py::arg("G"),
+        py::arg("B"), py::arg("S"), py::arg("dS"), py::arg("dgamma") = py::none());
   m.def("gather_rows", &cqb::gather_rows);
   m.def("gather_rows_bwd", &cqb::gather_rows_bwd);
   m.def("conv_fwd", &cqb::conv_fwd);

@@ -840,6 +840,7 @@ std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Te
                                 at::Tensor gamma, at::Tensor start, at::Tensor count, bool want_final) {
   GdnArgs a = make_args(W, Qd, Kt, P, U, gamma, start, count);
   auto O = at::empty_like(U);
+  const bool tc_path = gdn_fwd_use_tc(a.DV);
   auto S = at::empty({W.size(0), W.size(1), DK, U.size(3)}, W.options().dtype(at::kFloat));
   a.out = (__nv_bfloat16*)O.data_ptr();
   a.states = S.data_ptr<float>();
@@ -848,7 +849,7 @@ std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Te
     F = at::empty({start.size(0), W.size(1), DK, U.size(3)}, W.options().dtype(at::kFloat));
     a.final = F.data_ptr<float>();
   }
-  if (gdn_fwd_use_tc(a.DV)) {
+  if (tc_path) {
     static bool once_tc = [] {
       CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)TF_SMEM));

@@ -424,6 +424,7 @@ struct BwdArgs {
   float* dV;
   float* dG;                // [Nc*H, 64]
   float* dB;
+  const float* dgamma;      // tcgen05 kernel: <S, dS> per (chunk, head), from the backward recurrence
 };
 
 constexpr int LDS = DH + 8;                       // bf16 row of the 128x128 state tiles
@@ -854,8 +855,8 @@ static_assert(2 * TC_SMEM <= 232448, "two preparation CTAs must fit on one SM");
 __global__ void __launch_bounds__(TC_THREADS, 2)
     gdn_prep_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, PrepArgs a, int* status) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_tc[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_tc) + 1023) & ~uintptr_t(1023));
   uint8_t* kq = smem + TC_KQ;
   uint8_t* sv = smem + TC_V;
   uint8_t* tw = smem + TC_TW;
@@ -1032,6 +1033,602 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
   if (warp == 0) tc::tmem_dealloc(tmem, TC_TMEM_COLS);
 }
 
+// ---- tcgen05 fused chunk backward ------------------------------------------------------------
+//
+// Same math and outputs as gdn_chunk_bwd_kernel (see its comment), one CTA per (chunk, head), 256
+// threads, one CTA per SM, all 512 TMEM columns. Every matrix product is a tcgen05.mma issued by
+// thread 0 with M = 128. Products whose result feeds another product as a [dim][event] operand
+// are computed transposed (M = the 128-wide key / value dim, N = 64 events: W^T, U^T, Delta^T,
+// dDelta^T); products whose epilogue reduces over the feature dim per event keep the event as M,
+// with the upper 64 rows of the A operand reading the next 8 KB of shared memory (their TMEM
+// lanes 64-127 are never read). Operand transposes are MN-major descriptors, never copies.
+// [Q; K] is one stacked 128-row TMA tile, so G = [Q; K] K^T gives Q K^T in lanes 0-63 (read by
+// the threads that own the same event rows of dP) and K K^T in lanes 64-127 (the A path).
+// TMEM columns: G 0-63 (kept to the end), then per group:
+//   P2  W^T 64-127, U^T 128-191
+//   P3  S^T W^T 192-255, dO^T P 256-319, dS^T K^T 320-383, dQ (natural) 384-511
+//   P4a dW 64-191, dK (natural, accumulated to the end) 192-319, dP 320-383
+//   P4b T1 = dDelta V^T 64-127, T2 = dW K^T 128-191, dQ += dPm K, dK += dPm^T Q
+//   P4c dVb = T^T dDelta 64-191, dKw = T^T dW 384-511
+//   P7  dK += M K
+// The fp32 T, dT and dA (the triangular inverse and dA = -T^T dT T^T) stay on the CUDA cores as
+// in the mma.sync kernel. Bounded waits, status codes 61-68.
+namespace cb {
+constexpr uint32_t ATOM_KQ = 128 * 128;          // one 64-column atom of a 128-row tile
+constexpr uint32_t ATOM64 = 64 * 128;            // one 64-column atom of a 64-row tile
+constexpr uint32_t KQ = 0;                       // [Q; K]: Q rows 0-63, K rows 64-127 of each atom
+constexpr uint32_t K_OFF = 64 * 128;
+constexpr uint32_t V = KQ + 2 * ATOM_KQ;
+constexpr uint32_t DO = V + 2 * ATOM64;
+constexpr uint32_t SB = DO + 2 * ATOM64;         // bf16 S [2 atoms (v)][128 rows (d)]; later fp32 dT
+constexpr uint32_t DSB = SB + 2 * ATOM_KQ;       // bf16 dS; later fp32 X
+constexpr uint32_t W = DSB + 2 * ATOM_KQ;        // W [i][d], later dW
+constexpr uint32_t DL = W + 2 * ATOM64;          // Delta^T [128 rows (v)][64 events]
+constexpr uint32_t P = DL + ATOM_KQ;             // P [i][j], later dPm
+constexpr uint32_t TB = P + ATOM64;              // bf16 T [i][j], later M
+constexpr uint32_t R1 = TB + ATOM64;             // fp32 A, then Tw | Tv, then dDelta^T [128 rows (v)][64]
+constexpr uint32_t R1_BYTES = 17408;
+constexpr uint32_t TF = R1 + R1_BYTES;           // fp32 T [64][LDF]
+constexpr uint32_t VEC = TF + 17408;             // b, eb, kd, beta, g, db, dbeta (64 each), scal[4], inverse scratch
+constexpr uint32_t BAR = VEC + 5120;
+constexpr uint32_t SMEM = BAR + 64 + 1024;
+static_assert(CH * LDF * 4 <= R1_BYTES && 2 * ATOM64 <= R1_BYTES && ATOM_KQ <= R1_BYTES, "R1 region");
+static_assert(CH * LDF * 4 <= 17408 && CH * LDF * 4 <= 2 * ATOM_KQ, "fp32 T / dT / X tiles");
+static_assert(7 * CH * 4 + 16 + 3 * 16 * 17 * 4 <= 5120, "vectors and inverse scratch");
+static_assert(SMEM <= 232448, "chunk backward exceeds one CTA's shared memory");
+}  // namespace cb
+
+// bf16 element (row, col) of a 128-byte-swizzled tile whose 64-column atoms are `atom` bytes apart.
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t col, uint32_t atom) {
+  return (col >> 6) * atom + row * 128 + (((((col & 63) >> 3) ^ row) & 7) << 4) + (col & 7) * 2;
+}
+__device__ __forceinline__ float ldsb(const uint8_t* base, uint32_t off) {
+  return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(base + off));
+}
+__device__ __forceinline__ void stsb(uint8_t* base, uint32_t off, float v) {
+  *reinterpret_cast<__nv_bfloat16*>(base + off) = __float2bfloat16(v);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gdn_chunk_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                            const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
+                            const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_ds,
+                            BwdArgs a, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_tc[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_tc) + 1023) & ~uintptr_t(1023));
+  uint8_t* kq = sm + cb::KQ;
+  uint8_t* sv = sm + cb::V;
+  uint8_t* sdo = sm + cb::DO;
+  uint8_t* ssb = sm + cb::SB;
+  uint8_t* sdsb = sm + cb::DSB;
+  uint8_t* sw = sm + cb::W;
+  uint8_t* sdl = sm + cb::DL;
+  uint8_t* sp = sm + cb::P;
+  uint8_t* stb = sm + cb::TB;
+  uint8_t* r1 = sm + cb::R1;
+  float* sA = reinterpret_cast<float*>(r1);
+  float* sT = reinterpret_cast<float*>(sm + cb::TF);
+  float* sdT = reinterpret_cast<float*>(ssb);
+  float* sX = reinterpret_cast<float*>(sdsb);
+  float* sb = reinterpret_cast<float*>(sm + cb::VEC);
+  float* seb = sb + CH;
+  float* skd = seb + CH;
+  float* sbeta = skd + CH;
+  float* sg = sbeta + CH;
+  float* sdb = sg + CH;
+  float* sdbeta = sdb + CH;
+  float* sscal = sdbeta + CH;    // [0] dgamma = <S, dS>, [1] d b_C from Kt
+  float* sinv = sscal + 4;       // triangular-inverse scratch, 3 x 16 x 17
+  uint64_t* load_bar = reinterpret_cast<uint64_t*>(sm + cb::BAR);
+  uint64_t* mma_bar = load_bar + 1;
+  uint64_t* state_bar = load_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(load_bar + 3);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int unit = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, hf = warp >> 2, row = 32 * quad + lane;
+  const size_t toff = (size_t)unit * CH * DH;
+  if (tid == 0) {
+    tc::mbar_init(load_bar, 1);
+    tc::mbar_init(mma_bar, 1);
+    tc::mbar_init(state_bar, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
+  if (tid < CH) {
+    sg[tid] = a.G[(size_t)unit * CH + tid];
+    sbeta[tid] = a.B[(size_t)unit * CH + tid];
+    sdb[tid] = 0.f;
+    sdbeta[tid] = 0.f;
+  }
+  if (tid == 0) {
+    sscal[0] = a.dgamma[unit];
+    sscal[1] = 0.f;
+  }
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lb = tmem + ((uint32_t)(32 * quad) << 16);   // this warp's TMEM lane quadrant
+  if (tid == 0) {
+    tc::prefetch_map(&map_q);
+    tc::prefetch_map(&map_k);
+    tc::prefetch_map(&map_v);
+    tc::prefetch_map(&map_do);
+    tc::prefetch_map(&map_s);
+    tc::prefetch_map(&map_ds);
+    tc::mbar_expect_tx(load_bar, 4 * CH * DH * 2);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      tc::tma_load_2d(kq + x * cb::ATOM_KQ, &map_q, load_bar, 64 * x, unit * CH);
+      tc::tma_load_2d(kq + x * cb::ATOM_KQ + cb::K_OFF, &map_k, load_bar, 64 * x, unit * CH);
+      tc::tma_load_2d(sv + x * cb::ATOM64, &map_v, load_bar, 64 * x, unit * CH);
+      tc::tma_load_2d(sdo + x * cb::ATOM64, &map_do, load_bar, 64 * x, unit * CH);
+    }
+    // the bf16 states [2 atoms (v)][128 rows (d)] land while the first products run
+    tc::mbar_expect_tx(state_bar, 2 * DH * DH * 2);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      tc::tma_load_2d(ssb + x * cb::ATOM_KQ, &map_s, state_bar, 64 * x, unit * DH);
+      tc::tma_load_2d(sdsb + x * cb::ATOM_KQ, &map_ds, state_bar, 64 * x, unit * DH);
+    }
+  }
+  if (warp == 1) chunk_decay(sg, sb, seb, skd, lane);
+  const bool loaded = tc::mbar_wait(load_bar, 0, status, abort_flag, 61);
+  bool ok = __syncthreads_and(loaded);   // also publishes the decay vectors
+  bool states_seen = false;
+  uint32_t phase = 0;
+  bool pending = false;
+  auto commit_wait = [&](int code) {
+    if (tid == 0 && ok) {
+      tc::mma_commit(mma_bar);
+      pending = true;
+    }
+    const bool seen = !ok || tc::mbar_wait(mma_bar, phase & 1, status, abort_flag, code);
+    ok = __syncthreads_and(ok && seen);
+    if (ok) pending = false;
+    ++phase;
+    tc::fence_after();
+  };
+  const uint32_t kq_a = tc::smem_u32(kq), v_a = tc::smem_u32(sv), do_a = tc::smem_u32(sdo);
+  const uint32_t sb_a = tc::smem_u32(ssb), dsb_a = tc::smem_u32(sdsb), w_a = tc::smem_u32(sw);
+  const uint32_t dl_a = tc::smem_u32(sdl), p_a = tc::smem_u32(sp), tb_a = tc::smem_u32(stb), r1_a = tc::smem_u32(r1);
+  const uint32_t k_a = kq_a + cb::K_OFF;
+  // K-major / MN-major descriptors of the k-th 16-wide K step
+  auto kmaj = [](uint32_t base, uint32_t atom, int k) { return tc::smem_desc(base + (k >> 2) * atom + (k & 3) * 32, 16, 1024); };
+  auto mnmaj = [](uint32_t base, uint32_t lbo, int k) { return tc::smem_desc(base + k * 2048, lbo, 1024); };
+
+  // ---- P1: G = [Q; K] K^T -> P (rows 0-63) and A (rows 64-127) ----
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+    for (int k = 0; k < DH / 16; ++k) tc::mma_bf16(tmem, kmaj(kq_a, cb::ATOM_KQ, k), kmaj(k_a, cb::ATOM_KQ, k), id, k > 0);
+  }
+  commit_wait(62);
+  if (ok) {
+    float x[32];
+    tc::tmem_ld32(lb + 32 * hf, x);
+    const int i = row & 63;
+    const float bi = sb[i];
+    if (row >= CH) {   // K K^T row i -> A
+      const float be = sbeta[i];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int j = 32 * hf + c;
+        sA[i * LDF + j] = j < i ? be * x[c] * __expf(bi - sb[j]) : 0.f;
+      }
+    } else {           // Q K^T row i -> P (bf16 [i][j])
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        float p[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int j = 32 * hf + 8 * c8 + q;
+          p[q] = j <= i ? x[8 * c8 + q] * __expf(bi - sb[j]) : 0.f;
+        }
+        store8(reinterpret_cast<__nv_bfloat16*>(sp + swz(i, 32 * hf + 8 * c8, cb::ATOM64)), p);
+      }
+    }
+  }
+  __syncthreads();
+  unit_lower_inverse(sA, sT, sinv, warp, lane);
+  // T (bf16), Tw = T diag(beta e^b), Tv = T diag(beta): [i][j] tiles (Tw, Tv over the dead A)
+  for (int e = tid; e < CH * 8; e += TC_THREADS) {
+    const int i = e >> 3, c8 = (e & 7) * 8;
+    float t[8], tw8[8], tv8[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = c8 + q;
+      t[q] = sT[i * LDF + j];
+      tv8[q] = t[q] * sbeta[j];
+      tw8[q] = tv8[q] * seb[j];
+    }
+    const uint32_t off = swz(i, c8, cb::ATOM64);
+    store8(reinterpret_cast<__nv_bfloat16*>(stb + off), t);
+    store8(reinterpret_cast<__nv_bfloat16*>(r1 + off), tw8);
+    store8(reinterpret_cast<__nv_bfloat16*>(r1 + cb::ATOM64 + off), tv8);
+  }
+  tc::fence_proxy_async();
+  __syncthreads();
+
+  // ---- P2: W^T = K^T Tw^T, U^T = V^T Tv^T (K, V as MN-major A) ----
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id = tc::idesc_bf16(128, 64, true, false);
+#pragma unroll
+    for (int k = 0; k < CH / 16; ++k) {
+      tc::mma_bf16(tmem + 64, mnmaj(k_a, cb::ATOM_KQ, k), kmaj(r1_a, cb::ATOM64, k), id, k > 0);
+      tc::mma_bf16(tmem + 128, mnmaj(v_a, cb::ATOM64, k), kmaj(r1_a + cb::ATOM64, cb::ATOM64, k), id, k > 0);
+    }
+  }
+  commit_wait(63);
+  if (ok) {   // W [i][d] from W^T row d = row (events 32 hf ..)
+    float x[32];
+    tc::tmem_ld32(lb + 64 + 32 * hf, x);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) stsb(sw, swz(32 * hf + c, row, cb::ATOM64), x[c]);
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+
+  // ---- P3: S^T W^T, dO^T P, dS^T K^T (transposed, lanes = v) and dQd = dO S^T (lanes = i) ----
+  if (ok && tid == 0) states_seen = tc::mbar_wait(state_bar, 0, status, abort_flag, 69);
+  ok = __syncthreads_and(ok && (tid != 0 || states_seen));
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_t = tc::idesc_bf16(128, 64, true, false);
+    constexpr uint32_t id_op = tc::idesc_bf16(128, 64, true, true);
+    constexpr uint32_t id_n = tc::idesc_bf16(128, 128, false, false);
+#pragma unroll
+    for (int k = 0; k < DH / 16; ++k) {
+      tc::mma_bf16(tmem + 192, mnmaj(sb_a, cb::ATOM_KQ, k), kmaj(w_a, cb::ATOM64, k), id_t, k > 0);
+      tc::mma_bf16(tmem + 320, mnmaj(dsb_a, cb::ATOM_KQ, k), kmaj(k_a, cb::ATOM_KQ, k), id_t, k > 0);
+      tc::mma_bf16(tmem + 384, kmaj(do_a, cb::ATOM64, k), kmaj(sb_a, cb::ATOM_KQ, k), id_n, k > 0);
+    }
+#pragma unroll
+    for (int k = 0; k < CH / 16; ++k)
+      tc::mma_bf16(tmem + 256, mnmaj(do_a, cb::ATOM64, k), mnmaj(p_a, cb::ATOM64, k), id_op, k > 0);
+  }
+  commit_wait(64);
+  if (ok) {
+    // Delta^T = U^T - S^T W^T and dDelta^T = dO^T P + kd dS^T K^T, rows v = row, events 32 hf ..
+    float u[32], x[32], y[32], z[32];
+    tc::tmem_ld32(lb + 128 + 32 * hf, u);
+    tc::tmem_ld32(lb + 192 + 32 * hf, x);
+    tc::tmem_ld32(lb + 256 + 32 * hf, y);
+    tc::tmem_ld32(lb + 320 + 32 * hf, z);
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) {
+      float dl[8], dd[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int c = 8 * c8 + q, i = 32 * hf + c;
+        dl[q] = u[c] - x[c];
+        dd[q] = y[c] + skd[i] * z[c];
+      }
+      const uint32_t off = row * 128 + ((((4 * hf + c8) ^ row) & 7) << 4);
+      store8(reinterpret_cast<__nv_bfloat16*>(sdl + off), dl);
+      store8(reinterpret_cast<__nv_bfloat16*>(r1 + off), dd);
+    }
+    if (row < CH) {   // dQd row i: db_i += e^b_i sum_d dQd Q, then dQ = e^b_i dQd (kept in TMEM)
+      const int i = row;
+      float part = 0.f;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int col = 64 * hf + 32 * h2;
+        tc::tmem_ld32(lb + 384 + col, x);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          part += x[c] * ldsb(kq, swz(i, col + c, cb::ATOM_KQ));
+          x[c] *= seb[i];
+        }
+        tc::tmem_st32(lb + 384 + col, x);
+      }
+      atomicAdd(sdb + i, seb[i] * part);
+    }
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+
+  // ---- P4a: dW = -dDelta S^T, dKt = Delta dS^T, dP = dO Delta^T (lanes = i) ----
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_n = tc::idesc_bf16(128, 128, true, false);
+    constexpr uint32_t id_p = tc::idesc_bf16(128, 64, false, true);
+#pragma unroll
+    for (int k = 0; k < DH / 16; ++k) {
+      tc::mma_bf16(tmem + 64, mnmaj(r1_a, cb::ATOM_KQ, k), kmaj(sb_a, cb::ATOM_KQ, k), id_n, k > 0);
+      tc::mma_bf16(tmem + 192, mnmaj(dl_a, cb::ATOM_KQ, k), kmaj(dsb_a, cb::ATOM_KQ, k), id_n, k > 0);
+      tc::mma_bf16(tmem + 320, kmaj(do_a, cb::ATOM64, k), mnmaj(dl_a, cb::ATOM_KQ, k), id_p, k > 0);
+    }
+  }
+  commit_wait(65);
+  if (ok && row < CH) {
+    const int i = row;
+    float x[32];
+    // dW row i (negated) -> bf16 tile over W
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int col = 64 * hf + 32 * h2;
+      tc::tmem_ld32(lb + 64 + col, x);
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        float w8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) w8[q] = -x[8 * c8 + q];
+        store8(reinterpret_cast<__nv_bfloat16*>(sw + swz(i, col + 8 * c8, cb::ATOM64)), w8);
+      }
+    }
+    // dK = e^{b_C - b_i} dKt (TMEM); d b from Kt = e^{b_C - b} K
+    float rkt = 0.f;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int col = 64 * hf + 32 * h2;
+      tc::tmem_ld32(lb + 192 + col, x);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        x[c] *= skd[i];
+        rkt += x[c] * ldsb(kq + cb::K_OFF, swz(i, col + c, cb::ATOM_KQ));
+      }
+      tc::tmem_st32(lb + 192 + col, x);
+    }
+    atomicAdd(sdb + i, -rkt);
+    atomicAdd(sscal + 1, rkt);
+    // dP row i, events 32 hf ..: dPm = dP E (j <= i) -> bf16 over P; t = dPm (Q K^T)
+    float qk[32];
+    tc::tmem_ld32(lb + 320 + 32 * hf, x);
+    tc::tmem_ld32(lb + 32 * hf, qk);
+    const float bi = sb[i];
+    float rsum = 0.f;
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) {
+      float m8[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int c = 8 * c8 + q, j = 32 * hf + c;
+        const float dpm = j <= i ? x[c] * __expf(bi - sb[j]) : 0.f;
+        m8[q] = dpm;
+        const float t = dpm * qk[c];
+        rsum += t;
+        x[c] = t;   // column contribution
+      }
+      store8(reinterpret_cast<__nv_bfloat16*>(sp + swz(i, 32 * hf + 8 * c8, cb::ATOM64)), m8);
+    }
+    atomicAdd(sdb + i, rsum);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {   // column sums over the rows of this warp
+      const float v = warp_sum(x[c]);
+      if (lane == 0) atomicAdd(sdb + 32 * hf + c, -v);
+    }
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+
+  // ---- P4b: T1 = dDelta V^T, T2 = dW K^T; dQ += dPm K; dK += dPm^T Q ----
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_t1 = tc::idesc_bf16(128, 64, true, false);
+    constexpr uint32_t id_t2 = tc::idesc_bf16(128, 64, false, false);
+    constexpr uint32_t id_q = tc::idesc_bf16(128, 128, false, true);
+    constexpr uint32_t id_k = tc::idesc_bf16(128, 128, true, true);
+#pragma unroll
+    for (int k = 0; k < DH / 16; ++k) {
+      tc::mma_bf16(tmem + 64, mnmaj(r1_a, cb::ATOM_KQ, k), kmaj(v_a, cb::ATOM64, k), id_t1, k > 0);
+      tc::mma_bf16(tmem + 128, kmaj(w_a, cb::ATOM64, k), kmaj(k_a, cb::ATOM_KQ, k), id_t2, k > 0);
+    }
+#pragma unroll
+    for (int k = 0; k < CH / 16; ++k) {
+      tc::mma_bf16(tmem + 384, kmaj(p_a, cb::ATOM64, k), mnmaj(k_a, cb::ATOM_KQ, k), id_q, 1u);
+      tc::mma_bf16(tmem + 192, mnmaj(p_a, cb::ATOM64, k), mnmaj(kq_a, cb::ATOM_KQ, k), id_k, 1u);
+    }
+  }
+  commit_wait(66);
+  if (ok && row < CH) {
+    const int i = row;
+    float x[32], y[32];
+    tc::tmem_ld32(lb + 64 + 32 * hf, x);
+    tc::tmem_ld32(lb + 128 + 32 * hf, y);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const int j = 32 * hf + c;
+      sdT[i * LDF + j] = sbeta[j] * (x[c] + seb[j] * y[c]);
+    }
+    float* dq = a.dQ + toff + (size_t)i * DH;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int col = 64 * hf + 32 * h2;
+      tc::tmem_ld32(lb + 384 + col, x);
+#pragma unroll
+      for (int q = 0; q < 32; q += 4) *reinterpret_cast<float4*>(dq + col + q) = make_float4(x[q], x[q + 1], x[q + 2], x[q + 3]);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+
+  // ---- P4c: dVb = T^T dDelta, dKw = T^T dW (lanes = j) ----
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_v = tc::idesc_bf16(128, 128, true, false);
+    constexpr uint32_t id_w = tc::idesc_bf16(128, 128, true, true);
+#pragma unroll
+    for (int k = 0; k < CH / 16; ++k) {
+      tc::mma_bf16(tmem + 64, mnmaj(tb_a, cb::ATOM64, k), tc::smem_desc(r1_a + k * 32, 16, 1024), id_v, k > 0);
+      tc::mma_bf16(tmem + 384, mnmaj(tb_a, cb::ATOM64, k), mnmaj(w_a, cb::ATOM64, k), id_w, k > 0);
+    }
+  }
+  commit_wait(67);
+  if (ok && row < CH) {
+    const int j = row;
+    float x[32];
+    float* dv = a.dV + toff + (size_t)j * DH;
+    float dbt = 0.f, swk = 0.f;
+    const float bj = sbeta[j], ej = seb[j];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int col = 64 * hf + 32 * h2;
+      tc::tmem_ld32(lb + 64 + col, x);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        dbt += x[c] * ldsb(sv, swz(j, col + c, cb::ATOM64));
+        x[c] *= bj;
+      }
+#pragma unroll
+      for (int q = 0; q < 32; q += 4) *reinterpret_cast<float4*>(dv + col + q) = make_float4(x[q], x[q + 1], x[q + 2], x[q + 3]);
+      float y[32];
+      tc::tmem_ld32(lb + 384 + col, x);
+      tc::tmem_ld32(lb + 192 + col, y);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        swk += x[c] * ldsb(kq + cb::K_OFF, swz(j, col + c, cb::ATOM_KQ));
+        y[c] += x[c] * bj * ej;
+      }
+      tc::tmem_st32(lb + 192 + col, y);
+    }
+    atomicAdd(sdbeta + j, dbt + swk * ej);
+    atomicAdd(sdb + j, swk * ej * bj);
+  }
+  tc::fence_before();
+  __syncthreads();
+
+  // ---- P5: dA = -T^T (dT T^T) on the CUDA cores (T lower triangular) ----
+  {
+    const int i0 = 4 * (tid & 15), j0 = 4 * (tid >> 4);
+    float x[4][4] = {};
+    for (int k = 0; k < j0 + 4; ++k) {
+      float l[4], r[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        l[q] = sdT[(i0 + q) * LDF + k];
+        r[q] = sT[(j0 + q) * LDF + k];
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[p][q] += l[p] * r[q];
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sX[(i0 + p) * LDF + j0 + q] = x[p][q];
+  }
+  __syncthreads();
+  {
+    const int i0 = 4 * (tid >> 4), j0 = 4 * (tid & 15);
+    float x[4][4] = {};
+    for (int k = i0; k < CH; ++k) {
+      float l[4], r[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        l[q] = sT[k * LDF + i0 + q];
+        r[q] = sX[k * LDF + j0 + q];
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[p][q] -= l[p] * r[q];
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sdT[(i0 + p) * LDF + j0 + q] = x[p][q];   // dT is dead: dA
+  }
+  // M = dKK + dKK^T is written over T (bf16): zero it first, then each thread of the A path
+  // writes its strictly-lower entries and their mirror
+  for (int e = tid; e < CH * CH / 8; e += TC_THREADS) reinterpret_cast<uint4*>(stb)[e] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+
+  // ---- P6: dA through A = beta_i (K K^T) E (strict lower), K K^T from TMEM lanes 64-127 ----
+  if (ok && row >= CH) {
+    const int i = row - CH;
+    float kk[32];
+    tc::tmem_ld32(lb + 32 * hf, kk);
+    const float bi = sb[i], be = sbeta[i];
+    float rowsum = 0.f, rb = 0.f, col[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const int j = 32 * hf + c;
+      col[c] = 0.f;
+      if (j < i) {
+        const float ev = __expf(bi - sb[j]);
+        const float da = sdT[i * LDF + j];
+        const float kke = kk[c] * ev;
+        const float ta = da * be * kke;
+        rb += da * kke;
+        rowsum += ta;
+        col[c] = ta;
+        const float m = da * ev * be;
+        stsb(stb, swz(i, j, cb::ATOM64), m);
+        stsb(stb, swz(j, i, cb::ATOM64), m);
+      }
+    }
+    atomicAdd(sdb + i, rowsum);
+    atomicAdd(sdbeta + i, rb);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const float v = warp_sum(col[c]);
+      if (lane == 0) atomicAdd(sdb + 32 * hf + c, -v);
+    }
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+
+  // ---- P7: dK += M K; dK out; dG = reverse cumsum(db) with the b_C terms; dBeta ----
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t id = tc::idesc_bf16(128, 128, false, true);
+#pragma unroll
+    for (int k = 0; k < CH / 16; ++k) tc::mma_bf16(tmem + 192, kmaj(tb_a, cb::ATOM64, k), mnmaj(k_a, cb::ATOM_KQ, k), id, 1u);
+  }
+  commit_wait(68);
+  if (ok && row < CH) {
+    float x[32];
+    float* dk = a.dK + toff + (size_t)row * DH;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int col = 64 * hf + 32 * h2;
+      tc::tmem_ld32(lb + 192 + col, x);
+#pragma unroll
+      for (int q = 0; q < 32; q += 4) *reinterpret_cast<float4*>(dk + col + q) = make_float4(x[q], x[q + 1], x[q + 2], x[q + 3]);
+    }
+  }
+  if (ok && warp == 0) {
+    const float gamma = __expf(sb[CH - 1]);
+    float d0 = sdb[2 * lane], d1 = sdb[2 * lane + 1];
+    if (lane == 31) d1 += sscal[1] + sscal[0] * gamma;
+    float s = d0 + d1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float v = __shfl_down_sync(0xffffffffu, s, off);
+      if (lane + off < 32) s += v;
+    }
+    const float after = s - (d0 + d1);
+    a.dG[(size_t)unit * CH + 2 * lane + 1] = after + d1;
+    a.dG[(size_t)unit * CH + 2 * lane] = after + d1 + d0;
+    a.dB[(size_t)unit * CH + 2 * lane] = sdbeta[2 * lane];
+    a.dB[(size_t)unit * CH + 2 * lane + 1] = sdbeta[2 * lane + 1];
+  }
+  if (tid == 0) {   // nothing issued by this CTA is in flight when it retires (bounded)
+    const unsigned long long t0 = tc::globaltimer();
+    if (!loaded)
+      while (!tc::mbar_try_wait(load_bar, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    if (!states_seen)
+      while (!tc::mbar_try_wait(state_bar, 0) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+    if (pending)
+      while (!tc::mbar_try_wait(mma_bar, (phase - 1) & 1) && tc::globaltimer() - t0 < tc::kWaitNs) {
+      }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 512);
+}
+
 bool gdn_use_tc() {
   static const bool on = [] {
     const char* v = std::getenv("CQB_GDN_TC");
@@ -1100,8 +1697,10 @@ int64_t gdn_status(bool reset) {
 }
 
 // Returns (dQ, dK, dV fp32 [Nc, H, 64, 128], dG, dBeta fp32 [Nc, H, 64]).
+// S, dS: fp32 (mma.sync kernel) or bf16 row-major [Nc, H, 128, 128] with dgamma = <S, dS> fp32 [Nc, H]
+// (tcgen05 kernel: S and dS arrive by TMA).
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, at::Tensor dO, at::Tensor G,
-                                      at::Tensor B, at::Tensor S, at::Tensor dS) {
+                                      at::Tensor B, at::Tensor S, at::Tensor dS, c10::optional<at::Tensor> dgamma) {
   check_tile(Q, "Q");
   check_tile(K, "K");
   check_tile(V, "V");
@@ -1111,24 +1710,47 @@ std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor Q, at::Tensor K, at::Tensor V, 
   for (const auto* t : {&G, &B})
     TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat && t->numel() == Nc * H * CH,
                 "G, B: contiguous fp32 [Nc, H, 64]");
+  const bool tc_path = S.scalar_type() == at::kBFloat16;
   for (const auto* t : {&S, &dS})
-    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat && t->numel() == Nc * H * DH * DH,
-                "S, dS: contiguous fp32 [Nc, H, 128, 128]");
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == S.scalar_type() &&
+                    (tc_path || t->scalar_type() == at::kFloat) && t->numel() == Nc * H * DH * DH,
+                "S, dS: contiguous [Nc, H, 128, 128], both fp32 or both bf16");
+  TORCH_CHECK(!tc_path || (dgamma.has_value() && dgamma->scalar_type() == at::kFloat && dgamma->is_contiguous() &&
+                           dgamma->numel() == Nc * H),
+              "bf16 states need dgamma: fp32 [Nc, H]");
   auto f32 = Q.options().dtype(at::kFloat);
   auto dQ = at::empty({Nc, H, CH, DH}, f32), dK = at::empty({Nc, H, CH, DH}, f32), dV = at::empty({Nc, H, CH, DH}, f32);
   auto dG = at::empty({Nc, H, CH}, f32), dB = at::empty({Nc, H, CH}, f32);
   if (Nc * H == 0) return {dQ, dK, dV, dG, dB};
   BwdArgs a{(const __nv_bfloat16*)Q.data_ptr(), (const __nv_bfloat16*)K.data_ptr(), (const __nv_bfloat16*)V.data_ptr(),
-            (const __nv_bfloat16*)dO.data_ptr(), G.data_ptr<float>(), B.data_ptr<float>(), S.data_ptr<float>(),
-            dS.data_ptr<float>(), dQ.data_ptr<float>(), dK.data_ptr<float>(), dV.data_ptr<float>(),
-            dG.data_ptr<float>(), dB.data_ptr<float>()};
-  static bool once = [] {
-    CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_chunk_bwd_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BWD_SMEM));
-    return true;
-  }();
-  (void)once;
-  gdn_chunk_bwd_kernel<<<(unsigned)(Nc * H), THREADS_C, BWD_SMEM, stream()>>>(a);
+            (const __nv_bfloat16*)dO.data_ptr(), G.data_ptr<float>(), B.data_ptr<float>(),
+            tc_path ? nullptr : S.data_ptr<float>(), tc_path ? nullptr : dS.data_ptr<float>(), dQ.data_ptr<float>(),
+            dK.data_ptr<float>(), dV.data_ptr<float>(), dG.data_ptr<float>(), dB.data_ptr<float>(),
+            tc_path ? dgamma->data_ptr<float>() : nullptr};
+  if (tc_path) {
+    static bool once_tc = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_chunk_bwd_tc_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cb::SMEM));
+      return true;
+    }();
+    (void)once_tc;
+    const auto mq = tma_map_bf16(Q.view({Nc * H * CH, DH}), CH);
+    const auto mk = tma_map_bf16(K.view({Nc * H * CH, DH}), CH);
+    const auto mv = tma_map_bf16(V.view({Nc * H * CH, DH}), CH);
+    const auto mo = tma_map_bf16(dO.view({Nc * H * CH, DH}), CH);
+    const auto ms = tma_map_bf16(S.view({Nc * H * DH, DH}), DH);
+    const auto mds = tma_map_bf16(dS.view({Nc * H * DH, DH}), DH);
+    gdn_chunk_bwd_tc_kernel<<<(unsigned)(Nc * H), TC_THREADS, cb::SMEM, stream()>>>(mq, mk, mv, mo, ms, mds, a,
+                                                                                   gdn_status_word());
+  } else {
+    static bool once = [] {
+      CQB_CHECK_CUDA(cudaFuncSetAttribute((const void*)gdn_chunk_bwd_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BWD_SMEM));
+      return true;
+    }();
+    (void)once;
+    gdn_chunk_bwd_kernel<<<(unsigned)(Nc * H), THREADS_C, BWD_SMEM, stream()>>>(a);
+  }
   CQB_LAUNCH_CHECK();
   count_launch();
   return {dQ, dK, dV, dG, dB};

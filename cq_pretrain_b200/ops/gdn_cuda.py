@@ -17,6 +17,7 @@ Per chunk (cumulative log-decay ``b``, ``E_ij = e^{b_i-b_j}``):
 from __future__ import annotations
 
 import math
+import os
 from functools import lru_cache
 
 import torch
@@ -90,6 +91,12 @@ def _factors(Q, K, V, G, B, chunk):
                 gamma=gamma)
 
 
+# The fused chunk backward has a tcgen05 form (``gdn_chunk_bwd_tc_kernel``: bf16 states by TMA); it is
+# correct but slower than the mma.sync form at one unit per SM (its per-unit chain of dependent MMA
+# groups is latency-bound), so the mma.sync form is the default and CQB_GDN_CHUNK_TC=1 selects it.
+_CHUNK_TC = os.environ.get("CQB_GDN_CHUNK_TC", "0") == "1"
+
+
 class _GatedDelta(torch.autograd.Function):
     """q, k, v ``[E,H,D]`` (bf16), g, beta ``[E,H]`` fp32 -> o ``[E,H,Dv]``; analytic chunked backward."""
 
@@ -121,7 +128,12 @@ class _GatedDelta(torch.autograd.Function):
         dO = ops.chunk_gather(dout.to(torch.bfloat16).contiguous(), idx, Nc, False, 1.0)[0]
         dS = ops.gdn_bwd(dO, W, P, Qd, Kt, gamma, start, count)
         del W, P, Qd, Kt
-        dQ, dK, dV, dG, dB = ops.gdn_chunk_bwd(Q, K, V, dO, G, B, S, dS)
+        if _CHUNK_TC:   # the tcgen05 chunk backward takes bf16 states and dgamma = <S, dS>
+            dgamma = (S * dS).sum((-1, -2))
+            dQ, dK, dV, dG, dB = ops.gdn_chunk_bwd(Q, K, V, dO, G, B, S.to(torch.bfloat16), dS.to(torch.bfloat16),
+                                                   dgamma)
+        else:
+            dQ, dK, dV, dG, dB = ops.gdn_chunk_bwd(Q, K, V, dO, G, B, S, dS)
         del dS
 
         def back(t):

@@ -71,8 +71,10 @@ def test_gdn_prep_matches_factors():
     assert _ext.ops().gdn_status(True) == 0     # no bounded wait of the tcgen05 kernel expired
 
 
-def test_gdn_chunk_backward_matches_reference():
-    """Fused chunk backward (csrc/gdn_chunk.cu) vs its PyTorch form on random states."""
+@pytest.mark.parametrize("states", ["fp32", "bf16"])
+def test_gdn_chunk_backward_matches_reference(states):
+    """Fused chunk backward (csrc/gdn_chunk.cu) vs its PyTorch form on random states: fp32 states
+    run the mma.sync kernel, bf16 states (with dgamma = <S, dS> given) the tcgen05 kernel."""
     from cq_pretrain_b200.ops.gdn_cuda import chunk_backward_reference
     assert _ext.has("gdn_chunk_bwd")
     torch.manual_seed(4)
@@ -90,7 +92,14 @@ def test_gdn_chunk_backward_matches_reference():
     S = torch.randn(Nc, H, 128, 128, device="cuda") * 0.5
     dS = torch.randn(Nc, H, 128, 128, device="cuda") * 0.5
     Q, K, V, dO = (t.to(torch.bfloat16).contiguous() for t in (Q, K, V, dO))
-    got = _ext.ops().gdn_chunk_bwd(Q, K, V, dO, G.contiguous(), B.contiguous(), S, dS)
+    if states == "bf16":
+        S, dS = S.to(torch.bfloat16), dS.to(torch.bfloat16)
+        dgamma = (S.float() * dS.float()).sum((-1, -2)).contiguous()
+        got = _ext.ops().gdn_chunk_bwd(Q, K, V, dO, G.contiguous(), B.contiguous(), S, dS, dgamma)
+        S, dS = S.float(), dS.float()
+        assert _ext.ops().gdn_status(True) == 0
+    else:
+        got = _ext.ops().gdn_chunk_bwd(Q, K, V, dO, G.contiguous(), B.contiguous(), S, dS)
     want = chunk_backward_reference(Q, K, V, dO, G, B, S, dS)
     for name, a, b in zip(("dQ", "dK", "dV", "dG", "dBeta"), got, want):
         rel = (a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)
