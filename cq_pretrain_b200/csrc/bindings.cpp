@@ -28,6 +28,7 @@ at::Tensor rope_pairs(at::Tensor x, at::Tensor cos_t, at::Tensor sin_t, bool inv
 at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor x);
 // gemm.cu
 at::Tensor gemm_nt(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias);
+at::Tensor gemm_dual(at::Tensor x, at::Tensor w, at::Tensor x2, at::Tensor w2, bool w_mn_major);
 at::Tensor gemm_nn(at::Tensor a, at::Tensor b);
 void gemm_tn_acc(at::Tensor a, at::Tensor b, at::Tensor out);
 int gemm_status(bool reset);
@@ -137,6 +138,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("column_sum", &cqb::column_sum);
   m.def("rope_pairs", &cqb::rope_pairs);
   m.def("swiglu_bwd", &cqb::swiglu_bwd);
+  m.def("gemm_dual", &cqb::gemm_dual);
   m.def("gemm_nt", &cqb::gemm_nt, py::arg("x"), py::arg("w"), py::arg("bias") = py::none());
   m.def("gemm_nn", &cqb::gemm_nn);
   m.def("gemm_tn_acc", &cqb::gemm_tn_acc);

@@ -196,8 +196,8 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_m = (args.M + BM - 1) / BM, tiles_n = (args.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
-  const int kb1 = (args.K + BK - 1) / BK;
-  const int kblocks = kb1 + (args.K2 > 0 ? (args.K2 + BK - 1) / BK : 0);
+  const int kb_first = (args.K + BK - 1) / BK;   // k blocks of the first operand pair
+  const int kblocks = kb_first + (args.K2 > 0 ? (args.K2 + BK - 1) / BK : 0);
   // GATHER: this rank's rows first; EPI 5: the next rank's rows first and this rank's rows last.
   const int rotate = GATHER ? (args.src_rank * args.rows_per_rank) / BM
                             : (EPI == 5 ? (((args.src_rank + 1) % args.tp) * args.rows_per_rank) / BM : 0);
@@ -254,10 +254,10 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           tc::mbar_expect_tx(&full[stage], STAGE_BYTES);
-          const bool second = kb >= kb1;
+          const bool second = kb >= kb_first;
           const CUtensorMap* ma = second ? &map_a2 : &map_a;
           const CUtensorMap* mb = second ? &map_b2 : &map_b;
-          const int k0 = (second ? kb - kb1 : kb) * BK;
+          const int k0 = (second ? kb - kb_first : kb) * BK;
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sa + j * (BK * 128), ma, &full[stage], m0 + j * 64, k0);
@@ -740,6 +740,31 @@ at::Tensor gemm_nn(at::Tensor a, at::Tensor b) {
   auto ma = make_map(a, BM);
   auto mb = make_map(b, BK);
   launch<false, true, 0, false>(ma, mb, make_out_map(y), plain_args(M, N, K, y.data_ptr(), N, nullptr));
+  return y;
+}
+
+// y[M,N] = x w (+) x2 w2 with two operand pairs in one k loop: w [N,K] (or [K,N] with w_mn_major), x2
+// may have fewer rows than x (missing rows count as zero). The single-GPU form of the pair that the
+// GEMM -> reduce-scatter kernel runs (the input gradient of two projections of one input).
+at::Tensor gemm_dual(at::Tensor x, at::Tensor w, at::Tensor x2, at::Tensor w2, bool w_mn_major) {
+  const int64_t M = x.size(0), K = x.size(1), N = w_mn_major ? w.size(1) : w.size(0);
+  const int64_t K2 = x2.size(1);
+  TORCH_CHECK(w_mn_major ? w.size(0) == K : w.size(1) == K, "gemm_dual: inner dims differ");
+  TORCH_CHECK(w_mn_major ? (w2.size(0) == K2 && w2.size(1) == N) : (w2.size(1) == K2 && w2.size(0) == N),
+              "gemm_dual: second pair shapes");
+  TORCH_CHECK(x2.size(0) <= M && x2.size(0) > 0 && K2 % 16 == 0, "gemm_dual: x2 rows in [1, M], K2 % 16 == 0");
+  check_dims(M, N, K);
+  auto y = at::empty({M, N}, x.options());
+  auto ma = make_map(x, BM);
+  auto mb = w_mn_major ? make_map(w, BK) : make_map(w, BN);
+  auto ma2 = make_map(x2, BM);
+  auto mb2 = w_mn_major ? make_map(w2, BK) : make_map(w2, BN);
+  auto args = plain_args(M, N, K, y.data_ptr(), N, nullptr);
+  args.K2 = (int)K2;
+  if (w_mn_major)
+    launch<false, true, 0, false>(ma, mb, make_out_map(y), args, &ma2, &mb2);
+  else
+    launch<false, false, 0, false>(ma, mb, make_out_map(y), args, &ma2, &mb2);
   return y;
 }
 

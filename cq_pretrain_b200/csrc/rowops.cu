@@ -43,7 +43,8 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const T* __restrict__ x, c
         for (int j = 0; j < 8; ++j) v[i][j] += a[j];
         store8(sum + (size_t)row * width + c, v[i]);
         if (sizeof(T) == 2) {   // normalise the bf16-rounded sum that the residual stream carries on
-          load_vec(sum + (size_t)row * width + c, v[i]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16(v[i][j]));
         }
       }
 #pragma unroll
@@ -69,6 +70,94 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const T* __restrict__ x, c
 
 // dx = r * (g - xhat * mean(g * xhat)) (+ dres), g = dy * (1 + w);  dw += dy * xhat. dres (may be
 // null) is the gradient the same x receives through a residual connection, summed in here.
+// Row-parallel form of the backward: one warp per row (x and dy stay in registers between the two
+// passes), RB_WARPS rows per block; the block's weight-gradient rows are summed in a fixed order
+// and written to partial[block], and rms_dw_reduce_kernel sums the partials over blocks in a fixed
+// order (deterministic, no atomics).
+constexpr int RB_WARPS = 4;
+
+template <int NV, typename T, typename WT>
+__global__ void __launch_bounds__(RB_WARPS * 32) rms_bwd_rows_kernel(
+    const T* __restrict__ dy, const T* __restrict__ x, const WT* __restrict__ w, const float* __restrict__ rstd,
+    const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ partial, int rows, int width) {
+  static_assert(sizeof(T) == 2, "bf16 rows (kept packed in registers between the passes)");
+  extern __shared__ float part[];   // [RB_WARPS][width]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * RB_WARPS + warp;
+  float* mine = part + warp * width;
+  if (row < rows) {
+    const float r = rstd[row];
+    const T* xr = x + (size_t)row * width;
+    const T* gr = dy + (size_t)row * width;
+    uint4 xraw[NV], graw[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {   // every load of the row in flight at once
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        xraw[i] = *reinterpret_cast<const uint4*>(xr + c);
+        graw[i] = *reinterpret_cast<const uint4*>(gr + c);
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float wv[8], xv[8], gv[8];
+        load_vec(w + c, wv);
+        load8(reinterpret_cast<const __nv_bfloat16*>(&xraw[i]), xv);
+        load8(reinterpret_cast<const __nv_bfloat16*>(&graw[i]), gv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = xv[j] * r;
+          dot += gv[j] * (1.f + wv[j]) * xh;
+          mine[c + j] = gv[j] * xh;
+        }
+      }
+    }
+    dot = warp_sum(dot) / width;
+    T* dr = dx + (size_t)row * width;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < width) {
+        float wv[8], xv[8], gv[8], o[8];
+        load_vec(w + c, wv);
+        load8(reinterpret_cast<const __nv_bfloat16*>(&xraw[i]), xv);
+        load8(reinterpret_cast<const __nv_bfloat16*>(&graw[i]), gv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * (1.f + wv[j]) - xv[j] * r * dot);
+        if (dres) {
+          float rv[8];
+          load_vec(dres + (size_t)row * width + c, rv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] += rv[j];
+        }
+        store8(dr + c, o);
+      }
+    }
+  } else {
+    for (int c = lane; c < width; c += 32) mine[c] = 0.f;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < RB_WARPS; ++k) acc += part[k * width + c];
+    partial[(size_t)blockIdx.x * width + c] = acc;
+  }
+}
+
+// dw[c] = sum over blocks b (in order) of partial[b][c]; one thread per column.
+__global__ void __launch_bounds__(256) rms_dw_reduce_kernel(const float* __restrict__ partial, int blocks, int width,
+                                                           float* __restrict__ dw) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= width) return;
+  float acc = 0.f;
+  for (int b = 0; b < blocks; ++b) acc += partial[(size_t)b * width + c];
+  dw[c] = acc;
+}
+
 template <int NV, typename T, typename WT>
 __global__ void __launch_bounds__(512) rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x,
                                                      const WT* __restrict__ w, const float* __restrict__ rstd,
@@ -637,18 +726,26 @@ std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, 
   const size_t sm = width * sizeof(float);
   AT_DISPATCH_SWITCH(x.scalar_type(), "rms_norm_bwd", AT_DISPATCH_CASE(at::kBFloat16, [&] {
                        using T = __nv_bfloat16;
+                       // bf16 rows: warp per row + deterministic two-stage weight gradient
+                       const int blocks = (rows + RB_WARPS - 1) / RB_WARPS;
+                       auto partial = at::empty({blocks, width}, x.options().dtype(at::kFloat));
+                       const size_t psm = (size_t)RB_WARPS * width * sizeof(float);
                        NV_DISPATCH(width, [&] {
                          if (wc.scalar_type() == at::kFloat)
-                           rms_bwd_kernel<NV, T, float><<<grid, 512, sm, stream()>>>(
+                           rms_bwd_rows_kernel<NV, T, float><<<blocks, RB_WARPS * 32, psm, stream()>>>(
                                (const T*)dy.data_ptr(), (const T*)x.data_ptr(), wc.data_ptr<float>(),
                                rstd.data_ptr<float>(), dres.defined() ? (const T*)dres.data_ptr() : nullptr,
-                               (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
+                               (T*)dx.data_ptr(), partial.data_ptr<float>(), rows, width);
                          else
-                           rms_bwd_kernel<NV, T, T><<<grid, 512, sm, stream()>>>(
+                           rms_bwd_rows_kernel<NV, T, T><<<blocks, RB_WARPS * 32, psm, stream()>>>(
                                (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)wc.data_ptr(),
                                rstd.data_ptr<float>(), dres.defined() ? (const T*)dres.data_ptr() : nullptr,
-                               (T*)dx.data_ptr(), dw.data_ptr<float>(), rows, width);
+                               (T*)dx.data_ptr(), partial.data_ptr<float>(), rows, width);
                        });
+                       CQB_LAUNCH_CHECK();
+                       rms_dw_reduce_kernel<<<(width + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), blocks,
+                                                                                       width, dw.data_ptr<float>());
+                       count_launch();
                      }) AT_DISPATCH_CASE(at::kFloat, [&] {
                        NV_DISPATCH(width, [&] {
                          auto wf = wc.to(at::kFloat);

@@ -65,3 +65,24 @@ def test_linear_autograd_uses_kernel():
     torch.testing.assert_close(y.float(), x.float() @ w.float().T, atol=3e-2, rtol=2e-2)
     torch.testing.assert_close(dx.float(), g.float() @ w.float(), atol=3e-2, rtol=2e-2)
     torch.testing.assert_close(w.main_grad, g.float().T @ x.float(), atol=0.5, rtol=1e-2)
+
+
+@pytest.mark.parametrize("mn_major", [False, True])
+def test_dual_operand_pair_gemm(mn_major):
+    """Two operand pairs in one k loop (x w + x2 w2, x2 over fewer rows): the pair the GEMM ->
+    reduce-scatter kernel runs for two projections of one input, here on one GPU vs fp32."""
+    assert _ext.has("gemm_dual")
+    torch.manual_seed(2)
+    M, N, K, K2, M2 = 640, 384, 256, 160, 440
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    x2 = torch.randn(M2, K2, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(K, N, device="cuda") * 0.05).to(torch.bfloat16)
+    w2 = (torch.randn(K2, N, device="cuda") * 0.05).to(torch.bfloat16)
+    if not mn_major:
+        w, w2 = w.t().contiguous(), w2.t().contiguous()
+    y = _ext.ops().gemm_dual(x, w, x2, w2, mn_major)
+    wf, w2f = (w.float(), w2.float()) if mn_major else (w.float().t(), w2.float().t())
+    ref = x.float() @ wf
+    ref[:M2] += x2.float() @ w2f
+    rel = (y.float() - ref).abs().max() / ref.abs().max()
+    assert rel < 1e-2, rel.item()
