@@ -107,12 +107,15 @@ __global__ void __launch_bounds__(RB_WARPS * 32) rms_bwd_rows_kernel(
         load_vec(w + c, wv);
         load8(reinterpret_cast<const __nv_bfloat16*>(&xraw[i]), xv);
         load8(reinterpret_cast<const __nv_bfloat16*>(&graw[i]), gv);
+        float pw[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float xh = xv[j] * r;
           dot += gv[j] * (1.f + wv[j]) * xh;
-          mine[c + j] = gv[j] * xh;
+          pw[j] = gv[j] * xh;
         }
+        *reinterpret_cast<float4*>(mine + c) = make_float4(pw[0], pw[1], pw[2], pw[3]);
+        *reinterpret_cast<float4*>(mine + c + 4) = make_float4(pw[4], pw[5], pw[6], pw[7]);
       }
     }
     dot = warp_sum(dot) / width;
@@ -148,14 +151,49 @@ __global__ void __launch_bounds__(RB_WARPS * 32) rms_bwd_rows_kernel(
   }
 }
 
-// dw[c] = sum over blocks b (in order) of partial[b][c]; one thread per column.
+// Deterministic sum of partial[blocks][width] over blocks in two launches. Stage 1: block
+// (column group cx of 32 columns, slice sy of RD_SLICES) has warp w sum the partial rows
+// g, g + G, g + 2G, ... with g = sy * 8 + w and G = 8 * RD_SLICES (coalesced 128-byte rows), then
+// the 8 warp sums are added in warp order into stage[sy][col]. Stage 2 adds the slices in order.
+constexpr int RD_SLICES = 16;
+
 __global__ void __launch_bounds__(256) rms_dw_reduce_kernel(const float* __restrict__ partial, int blocks, int width,
-                                                           float* __restrict__ dw) {
+                                                           float* __restrict__ stage) {
+  __shared__ float sums[8][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 32 + lane;
+  const int g0 = blockIdx.y * 8 + warp, step = 8 * RD_SLICES;
+  float acc = 0.f;
+  if (c < width) {
+    int b = g0;
+    for (; b + 3 * step < blocks; b += 4 * step) {   // four independent loads in flight
+      const float a0 = partial[(size_t)b * width + c], a1 = partial[(size_t)(b + step) * width + c];
+      const float a2 = partial[(size_t)(b + 2 * step) * width + c], a3 = partial[(size_t)(b + 3 * step) * width + c];
+      acc += a0;
+      acc += a1;
+      acc += a2;
+      acc += a3;
+    }
+    for (; b < blocks; b += step) acc += partial[(size_t)b * width + c];
+  }
+  sums[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < width) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += sums[w][lane];
+    stage[(size_t)blockIdx.y * width + c] = t;
+  }
+}
+
+__global__ void __launch_bounds__(256) rms_dw_final_kernel(const float* __restrict__ stage, int width,
+                                                          float* __restrict__ dw) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= width) return;
-  float acc = 0.f;
-  for (int b = 0; b < blocks; ++b) acc += partial[(size_t)b * width + c];
-  dw[c] = acc;
+  float t = 0.f;
+#pragma unroll
+  for (int sy = 0; sy < RD_SLICES; ++sy) t += stage[(size_t)sy * width + c];
+  dw[c] = t;
 }
 
 template <int NV, typename T, typename WT>
@@ -743,9 +781,13 @@ std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, 
                                (T*)dx.data_ptr(), partial.data_ptr<float>(), rows, width);
                        });
                        CQB_LAUNCH_CHECK();
-                       rms_dw_reduce_kernel<<<(width + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), blocks,
-                                                                                       width, dw.data_ptr<float>());
-                       count_launch();
+                       auto stage = at::empty({RD_SLICES, width}, x.options().dtype(at::kFloat));
+                       rms_dw_reduce_kernel<<<dim3((width + 31) / 32, RD_SLICES), 256, 0, stream()>>>(
+                           partial.data_ptr<float>(), blocks, width, stage.data_ptr<float>());
+                       CQB_LAUNCH_CHECK();
+                       rms_dw_final_kernel<<<(width + 255) / 256, 256, 0, stream()>>>(stage.data_ptr<float>(), width,
+                                                                                     dw.data_ptr<float>());
+                       count_launch(2);
                      }) AT_DISPATCH_CASE(at::kFloat, [&] {
                        NV_DISPATCH(width, [&] {
                          auto wf = wc.to(at::kFloat);
