@@ -89,13 +89,14 @@ __global__ void __launch_bounds__(RB_WARPS * 32) rms_bwd_rows_kernel(
     const float r = rstd[row];
     const T* xr = x + (size_t)row * width;
     const T* gr = dy + (size_t)row * width;
-    uint4 xraw[NV], graw[NV];
+    uint4 xraw[NV], graw[NV], rraw[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {   // every load of the row in flight at once
       const int c = (i * 32 + lane) * 8;
       if (c < width) {
         xraw[i] = *reinterpret_cast<const uint4*>(xr + c);
         graw[i] = *reinterpret_cast<const uint4*>(gr + c);
+        if (dres) rraw[i] = *reinterpret_cast<const uint4*>(dres + (size_t)row * width + c);
       }
     }
     float dot = 0.f;
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(RB_WARPS * 32) rms_bwd_rows_kernel(
         for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * (1.f + wv[j]) - xv[j] * r * dot);
         if (dres) {
           float rv[8];
-          load_vec(dres + (size_t)row * width + c, rv);
+          load8(reinterpret_cast<const __nv_bfloat16*>(&rraw[i]), rv);
 #pragma unroll
           for (int j = 0; j < 8; ++j) o[j] += rv[j];
         }
@@ -148,6 +149,115 @@ __global__ void __launch_bounds__(RB_WARPS * 32) rms_bwd_rows_kernel(
 #pragma unroll
     for (int k = 0; k < RB_WARPS; ++k) acc += part[k * width + c];
     partial[(size_t)blockIdx.x * width + c] = acc;
+  }
+}
+
+// Gated-norm backward at width 128 (a GDN head): one row per half-warp (16 lanes x 8 columns),
+// 16 rows per 256-thread block per step, a fixed grid striding over the rows; every thread keeps its
+// 8 columns' weight-gradient sums in registers, the block adds its 16 half-warps in order into
+// partial[block] (then the two-stage deterministic reduction below).
+constexpr int GB_BLOCKS_PER_SM = 4;
+
+// z row r lives at z + (r / heads) * z_stride + (r % heads) * 128 (the gate columns of a token's
+// projection row, read in place); x, dy, dx, dz are contiguous [rows, 128].
+__device__ __forceinline__ size_t gate_offset(int row, int heads, long z_stride) {
+  return (size_t)(row / heads) * z_stride + (size_t)(row % heads) * 128;
+}
+
+template <typename T, typename WT>
+__global__ void __launch_bounds__(256) gated_fwd_rows_kernel(const T* __restrict__ x, const T* __restrict__ z,
+                                                             const WT* __restrict__ w, T* __restrict__ y,
+                                                             float* __restrict__ rstd, int rows, int heads,
+                                                             long z_stride, float eps) {
+  constexpr int W = 128;
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, c = l * 8;
+  const int row = blockIdx.x * 16 + hw;
+  const bool live = row < rows;
+  float xv[8], zv[8], wv[8];
+  if (live) {
+    load_vec(x + (size_t)row * W + c, xv);
+    load_vec(z + gate_offset(row, heads, z_stride) + c, zv);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xv[j] = zv[j] = 0.f;
+  }
+  load_vec(w + c, wv);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += xv[j] * xv[j];
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o, 16);
+  const float r = rsqrtf(ss / W + eps);
+  if (live) {
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float n = __bfloat162float(__float2bfloat16(xv[j] * r));
+      o[j] = n * wv[j] * silu(zv[j]);
+    }
+    store8(y + (size_t)row * W + c, o);
+    if (l == 0) rstd[row] = r;
+  }
+}
+
+template <typename T, typename WT>
+__global__ void __launch_bounds__(256) gated_bwd_rows_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                             const T* __restrict__ z, const WT* __restrict__ w,
+                                                             const float* __restrict__ rstd, T* __restrict__ dx,
+                                                             T* __restrict__ dz, float* __restrict__ partial, int rows,
+                                                             int heads, long z_stride) {
+  constexpr int W = 128;
+  __shared__ float red[16][W];
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, c = l * 8;
+  float wv[8], acc[8];
+  load_vec(w + c, wv);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  const int warp_row0 = blockIdx.x * 16 + (hw & ~1);   // both half-warps of a warp run the same steps
+  for (int base = warp_row0; base < rows; base += gridDim.x * 16) {
+    const int row = base + (hw & 1);
+    const bool live = row < rows;
+    float xv[8], gv[8], zv[8];
+    float r = 0.f;
+    const size_t off = (size_t)(live ? row : 0) * W + c;
+    if (live) {
+      load_vec(x + off, xv);
+      load_vec(dy + off, gv);
+      load_vec(z + gate_offset(row, heads, z_stride) + c, zv);
+      r = rstd[row];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = gv[j] = zv[j] = 0.f;
+    }
+    float dot = 0.f, dzo[8], sv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float n = xv[j] * r;
+      const float sg = 1.f / (1.f + __expf(-zv[j]));
+      sv[j] = zv[j] * sg;
+      acc[j] += gv[j] * n * sv[j];
+      dot += gv[j] * wv[j] * sv[j] * n;
+      dzo[j] = gv[j] * n * wv[j] * sg * (1.f + zv[j] * (1.f - sg));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, 16);
+    dot /= W;
+    if (live) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * wv[j] * sv[j] - xv[j] * r * dot);
+      store8(dz + off, dzo);
+      store8(dx + off, o);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[hw][c + j] = acc[j];
+  __syncthreads();
+  if (threadIdx.x < W) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t += red[k][threadIdx.x];
+    partial[(size_t)blockIdx.x * W + threadIdx.x] = t;
   }
 }
 
@@ -802,6 +912,25 @@ std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, 
   return {dx, dw};
 }
 
+// z for the width-128 row kernels: contiguous [rows, 128], or [tokens, heads, 128] with unit inner
+// strides and any token stride (the gate slice of a projection output, read in place).
+static bool gate_layout(const at::Tensor& z, int rows, int width, int& heads, long& z_stride) {
+  if (width != 128 || z.scalar_type() != at::kBFloat16) return false;
+  if (z.dim() == 2 && z.is_contiguous() && z.size(0) == rows && z.size(1) == 128) {
+    heads = 1;
+    z_stride = 128;
+    return true;
+  }
+  if (z.dim() == 3 && z.size(2) == 128 && z.stride(2) == 1 && z.stride(1) == 128 && z.size(0) * z.size(1) == rows &&
+      z.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(z.data_ptr()) % 16 == 0) {
+    heads = (int)z.size(1);
+    z_stride = (long)z.stride(0);
+    return true;
+  }
+  return false;
+}
+
+// x [rows, width] contiguous; z as x, or for width 128 [tokens, heads, 128] read in place.
 std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w, double eps) {
   check_rows(x);
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && z.scalar_type() == at::kBFloat16, "gated norm expects bf16");
@@ -810,10 +939,21 @@ std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w,
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   if (!rows) return {y, rstd};
   auto wf = w.to(at::kFloat).contiguous();
-  const int blocks = (rows + kWarps - 1) / kWarps;
   using T = __nv_bfloat16;
+  int heads = 1;
+  long zs = width;
+  if (gate_layout(z, rows, width, heads, zs)) {
+    gated_fwd_rows_kernel<T, float><<<(rows + 15) / 16, 256, 0, stream()>>>(
+        (const T*)x.data_ptr(), (const T*)z.data_ptr(), wf.data_ptr<float>(), (T*)y.data_ptr(), rstd.data_ptr<float>(),
+        rows, heads, zs, (float)eps);
+    CQB_LAUNCH_CHECK();
+    count_launch();
+    return {y, rstd};
+  }
+  auto zc = z.reshape({rows, width}).contiguous();
+  const int blocks = (rows + kWarps - 1) / kWarps;
   NV_DISPATCH(width, [&] {
-    gated_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>((const T*)x.data_ptr(), (const T*)z.data_ptr(),
+    gated_fwd_kernel<NV, T, float><<<blocks, 256, 0, stream()>>>((const T*)x.data_ptr(), (const T*)zc.data_ptr(),
                                                                  wf.data_ptr<float>(), (T*)y.data_ptr(),
                                                                  rstd.data_ptr<float>(), rows, width, (float)eps);
   });
@@ -822,18 +962,39 @@ std::vector<at::Tensor> gated_norm_fwd(at::Tensor x, at::Tensor z, at::Tensor w,
   return {y, rstd};
 }
 
+// dz comes back contiguous [rows, width] whatever z's layout.
 std::vector<at::Tensor> gated_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor z, at::Tensor w, at::Tensor rstd) {
   const int rows = x.size(0), width = x.size(1);
   auto dx = at::empty_like(x);
-  auto dz = at::empty_like(z);
+  auto dz = at::empty({rows, width}, x.options());
   auto dw = at::zeros({width}, x.options().dtype(at::kFloat));
   if (!rows) return {dx, dz, dw};
   auto wf = w.to(at::kFloat).contiguous();
   using T = __nv_bfloat16;
+  int heads = 1;
+  long zs = width;
+  if (x.is_contiguous() && dy.is_contiguous() && gate_layout(z, rows, width, heads, zs)) {
+    // GDN head rows: half-warp rows and a deterministic two-stage weight gradient
+    const int blocks = std::max(1, std::min(sm_count() * GB_BLOCKS_PER_SM, (rows + 15) / 16));
+    auto partial = at::empty({blocks, width}, x.options().dtype(at::kFloat));
+    gated_bwd_rows_kernel<T, float><<<blocks, 256, 0, stream()>>>(
+        (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)z.data_ptr(), wf.data_ptr<float>(),
+        rstd.data_ptr<float>(), (T*)dx.data_ptr(), (T*)dz.data_ptr(), partial.data_ptr<float>(), rows, heads, zs);
+    CQB_LAUNCH_CHECK();
+    auto stage = at::empty({RD_SLICES, width}, x.options().dtype(at::kFloat));
+    rms_dw_reduce_kernel<<<dim3((width + 31) / 32, RD_SLICES), 256, 0, stream()>>>(partial.data_ptr<float>(), blocks,
+                                                                                  width, stage.data_ptr<float>());
+    CQB_LAUNCH_CHECK();
+    rms_dw_final_kernel<<<1, 256, 0, stream()>>>(stage.data_ptr<float>(), width, dw.data_ptr<float>());
+    CQB_LAUNCH_CHECK();
+    count_launch(3);
+    return {dx, dz, dw};
+  }
   const int grid = bwd_grid(rows);
+  auto zc = z.reshape({rows, width}).contiguous();
   NV_DISPATCH(width, [&] {
     gated_bwd_kernel<NV, T, float><<<grid, 512, width * sizeof(float), stream()>>>(
-        (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)z.data_ptr(), wf.data_ptr<float>(),
+        (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)zc.data_ptr(), wf.data_ptr<float>(),
         rstd.data_ptr<float>(), (T*)dx.data_ptr(), (T*)dz.data_ptr(), dw.data_ptr<float>(), rows, width);
   });
   CQB_LAUNCH_CHECK();

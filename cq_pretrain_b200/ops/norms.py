@@ -96,24 +96,30 @@ def rms_norm_residual(x, weight, eps):
 
 
 class _GatedNorm(torch.autograd.Function):
+    """x ``[rows, D]``; z either the same shape or, at D = 128, ``[tokens, heads, 128]`` with any token
+    stride (the gate slice of the GDN projection, read in place instead of copied)."""
+
     @staticmethod
     def forward(ctx, x, z, weight, eps):
-        y, rstd = _ext.ops().gated_norm_fwd(x.contiguous(), z.contiguous(), weight.contiguous(), eps)
+        y, rstd = _ext.ops().gated_norm_fwd(x.contiguous(), z, weight.contiguous(), eps)
         ctx.save_for_backward(x, z, weight, rstd)
+        ctx.z_shape = z.shape
         return y
 
     @staticmethod
     def backward(ctx, dy):
         x, z, weight, rstd = ctx.saved_tensors
         dx, dz, dw = _ext.ops().gated_norm_bwd(dy.contiguous(), x, z, weight, rstd)
-        return dx, dz, dw.to(weight.dtype), None
+        return dx, dz.view(ctx.z_shape), dw.to(weight.dtype), None
 
 
 def gated_rms_norm(x, z, weight, eps):
     """``rms(x) * w * silu(z)`` over the last dim (one GDN head)."""
     if _use_kernel(x) and x.shape[-1] % 8 == 0 and z.dtype == x.dtype:
         shape = x.shape
-        return _GatedNorm.apply(x.reshape(-1, shape[-1]), z.reshape(-1, shape[-1]), weight, eps).reshape(shape)
+        zk = z if (z.dim() == 3 and shape[-1] == 128 and z.stride(-1) == 1 and z.stride(-2) == 128) \
+            else z.reshape(-1, shape[-1])
+        return _GatedNorm.apply(x.reshape(-1, shape[-1]), zk, weight, eps).reshape(shape)
     return R.gated_rms_norm(x, z, weight, eps)
 
 

@@ -164,3 +164,31 @@ def test_rms_norm_residual_fuses_the_residual_gradient():
     torch.testing.assert_close(y.float(), yr, atol=3e-2, rtol=3e-2)
     assert ((x.grad.float() - xr.grad).norm() / xr.grad.norm()).item() < 1e-2
     assert ((w.grad.float() - wr.grad).norm() / wr.grad.norm()).item() < 1e-2
+
+
+def test_gated_norm_reads_strided_gate_in_place():
+    """The GDN output norm with the gate read in place from a wider projection row ([tokens, heads,
+    128] with a token stride) matches the fp32 reference, gradients included."""
+    from cq_pretrain_b200.ops import norms as N
+    torch.manual_seed(5)
+    tokens, heads = 777, 16
+    proj = torch.randn(tokens, heads * 128 + 96, device="cuda").to(torch.bfloat16)
+    z = proj[:, 64:64 + heads * 128].reshape(tokens, heads, 128)
+    x = torch.randn(tokens, heads, 128, device="cuda").to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(128, device="cuda")).to(torch.bfloat16)
+    xa, za, wa = x.clone().requires_grad_(), z.detach().clone(), w.clone().requires_grad_()
+    pa = proj.clone().requires_grad_()
+    zv = pa[:, 64:64 + heads * 128].reshape(tokens, heads, 128)
+    assert zv.stride(0) == heads * 128 + 96
+    y = N.gated_rms_norm(xa, zv, wa, 1e-6)
+    xr, zr, wr = x.float().requires_grad_(), za.float().requires_grad_(), w.float().requires_grad_()
+    yr = xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + 1e-6) * wr * torch.nn.functional.silu(zr)
+    assert ((y.float() - yr).norm() / yr.norm()).item() < 1e-2
+    g = torch.randn_like(yr)
+    y.backward(g.to(y.dtype))
+    yr.backward(g)
+    dz = pa.grad[:, 64:64 + heads * 128].reshape(tokens, heads, 128).float()
+    assert pa.grad[:, :64].abs().max().item() == 0 and pa.grad[:, 64 + heads * 128:].abs().max().item() == 0
+    for got, want in ((xa.grad.float(), xr.grad), (dz, zr.grad), (wa.grad.float(), wr.grad)):
+        rel = (got - want).norm() / want.norm()
+        assert rel < 2e-2, rel.item()
