@@ -236,15 +236,17 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       bool ok = true;
       WorkIter work(EPI == 1 ? args.split_k : 1, tiles, kblocks);
       int t, kb0, kb1;
+      int ready_m0 = -1;   // GATHER: the last row block seen published (consecutive tiles often share it)
       while (ok && work.next(t, kb0, kb1)) {
         int m0, n0;
         tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
-        if (GATHER) {
+        if (GATHER && m0 != ready_m0) {
           // the row block is ready once all of its 16-row sub-chunks are published
           for (int j = 0; j < BM / GATHER_SUB && ok; ++j)
             ok = wait_flag<false>(args.chunk_flags + m0 / GATHER_SUB + j, args.epoch, status, abort_flag, 5);
           if (!ok) break;
           fence_proxy_async_global();
+          ready_m0 = m0;
         }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, status, abort_flag, 1)) {
@@ -499,6 +501,11 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           }
         }
       }
+      // every TMEM read of this buffer is done: hand it back to the MMA warp before the publication
+      // below, so the next tile's accumulation is not held up by the system-scope fence
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty[buf]);
       if (EPI == 5 && !own) {
         // publish this warp's 32 rows of the tile to the owner: system-scope fence by every lane,
         // then one release store of the epoch into the (tile, source, warp) slot
@@ -508,9 +515,6 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           st_release_sys(args.rs_flags_peer[owner] + ((size_t)owner_tile * RS_MAX_TP + args.src_rank) * 4 + quarter,
                          args.epoch);
       }
-      tc::fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&tempty[buf]);
     }
     if (EPI != 2 && EPI != 3 && lane == 0) tc::bulk_wait_all();
     __syncwarp();

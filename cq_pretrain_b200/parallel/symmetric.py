@@ -35,6 +35,8 @@ All waits are bounded in the kernels and report a status code instead of hanging
 
 from __future__ import annotations
 
+from contextlib import contextmanager
+
 import torch
 import torch.distributed as dist
 
@@ -217,8 +219,23 @@ class SymmetricWorkspace:
         ops.symm_free(self.base)
 
 
+_SUSPENDED = 0
+
+
 def workspace():
-    return _WORKSPACE
+    return None if _SUSPENDED else _WORKSPACE
+
+
+@contextmanager
+def suspended():
+    """Route the TP linears through NCCL + the plain GEMM inside this block (the fused kernels
+    take a host-side epoch per call, which a CUDA-graph replay would repeat)."""
+    global _SUSPENDED
+    _SUSPENDED += 1
+    try:
+        yield
+    finally:
+        _SUSPENDED -= 1
 
 
 def enable(**kwargs):

@@ -19,9 +19,11 @@ replays:
 * kernel launches counted by the extension during the capture are added per replay, so
   ``_ext.launches()`` counts executed kernels.
 
-Graphs are used only where the captured work is position independent: CUDA, TP = 1 (the fused TP
-kernels take a per-call epoch), no activation recompute inside the DiT, and the Wan renderer.
-``CQB_GRAPHS=0`` turns them off.
+Graphs are used where the captured work is position independent: CUDA, no activation recompute
+inside the DiT, and the Wan renderer. At TP > 1 (opt-in, ``CQB_GRAPHS_TP=1``) the chunk runs its TP
+linears through NCCL and the plain GEMM (``parallel.symmetric.suspended``), because the fused TP
+kernels take a host-side epoch per call that a replay would repeat; NCCL collectives are captured
+with the rest. ``CQB_GRAPHS=0`` turns graphs off.
 """
 
 from __future__ import annotations
@@ -70,7 +72,9 @@ def _rebuild(spec, tensors):
 def graphs_enabled(cfg, device, tp):
     if os.environ.get("CQB_GRAPHS", "1") == "0":
         return False
-    return (torch.device(device).type == "cuda" and tp == 1 and cfg.renderer == "wan"
+    if tp > 1 and os.environ.get("CQB_GRAPHS_TP", "0") != "1":
+        return False
+    return (torch.device(device).type == "cuda" and cfg.renderer == "wan"
             and not getattr(cfg, "checkpoint_dit", 0) and not getattr(cfg, "checkpoint_dit_layers", 0))
 
 
@@ -106,6 +110,13 @@ class RendererGraphs:
         return (spec, tuple(leaf.shape), str(leaf.dtype), torch.is_grad_enabled()), tensors
 
     def run(self, model, leaf, bound, factor):
+        from ..parallel import state as ps, symmetric
+        if ps.tp_size() > 1:   # fused TP kernels stay out of captured work (see the module note)
+            with symmetric.suspended():
+                return self._run(model, leaf, bound, factor)
+        return self._run(model, leaf, bound, factor)
+
+    def _run(self, model, leaf, bound, factor):
         lengths = getattr(getattr(bound, "generation", None), "lengths", ())
         if sum(lengths) > self.max_tokens:
             return self._eager(model, leaf, bound, factor)
