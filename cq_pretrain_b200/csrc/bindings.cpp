@@ -41,7 +41,8 @@ void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_o
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
                        int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
                        int64_t tp, bool mn_major, c10::optional<at::Tensor> x_local, int64_t send_mine,
-                       c10::optional<at::Tensor> peer_ready, int64_t own_done);
+                       c10::optional<at::Tensor> peer_ready, int64_t own_done, int64_t epoch_ctr, int64_t epoch_done,
+                       c10::optional<at::Tensor> peer_in_odd, int64_t send_mine_odd);
 // comm.cu
 std::vector<at::Tensor> symm_alloc(int64_t bytes);
 int64_t symm_open(at::Tensor handle_bytes);
@@ -52,18 +53,23 @@ void signal_wait(at::Tensor peer_flag_ptrs, int64_t my_flags, int64_t rank, int6
 at::Tensor gemm_scatter_reduce(at::Tensor x, at::Tensor w, bool w_mn_major, c10::optional<at::Tensor> x2,
                                c10::optional<at::Tensor> w2, c10::optional<at::Tensor> bias, at::Tensor peer_recv,
                                int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t flag_slots,
-                               int64_t epoch, int64_t rows_per_rank, int64_t src_rank, int64_t tp);
+                               int64_t epoch, int64_t rows_per_rank, int64_t src_rank, int64_t tp,
+                               int64_t epoch_ctr, int64_t epoch_done, c10::optional<at::Tensor> peer_recv_odd,
+                               int64_t my_recv_odd);
 at::Tensor rs_reduce(at::Tensor recv, c10::optional<at::Tensor> bias, int64_t tp, int64_t rows, int64_t cols);
 int comm_status_read(bool reset);
 std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at::Tensor peer_recv, int64_t my_recv,
                                       at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
-                                      int64_t max_rows, int64_t epoch);
+                                      int64_t max_rows, int64_t epoch, int64_t epoch_ctr, int64_t epoch_done,
+                                      c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd);
 std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_recv, int64_t my_recv,
                                    at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
-                                   int64_t epoch, int64_t total_dim, double eps);
+                                   int64_t epoch, int64_t total_dim, double eps, int64_t epoch_ctr, int64_t epoch_done,
+                                   c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd);
 std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor peer_recv,
                                    int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
-                                   int64_t max_rows, int64_t epoch, int64_t total_dim);
+                                   int64_t max_rows, int64_t epoch, int64_t total_dim, int64_t epoch_ctr, int64_t epoch_done,
+                                   c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd);
 // gdn.cu
 std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                                 at::Tensor start, at::Tensor count, bool want_final);
@@ -150,7 +156,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_gemm", &cqb::gather_gemm, py::arg("a_local"), py::arg("w"), py::arg("bias"), py::arg("peer_in_ptrs"),
         py::arg("ready_ptr"), py::arg("chunk_flags"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),
         py::arg("tp"), py::arg("mn_major") = false, py::arg("x_local") = py::none(), py::arg("send_mine") = 0,
-        py::arg("peer_ready") = py::none(), py::arg("own_done") = 0);
+        py::arg("peer_ready") = py::none(), py::arg("own_done") = 0, py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0,
+        py::arg("peer_in_odd") = py::none(), py::arg("send_mine_odd") = 0);
   m.def("symm_alloc", &cqb::symm_alloc);
   m.def("symm_open", &cqb::symm_open);
   m.def("symm_close", &cqb::symm_close);
@@ -171,12 +178,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_scatter_reduce", &cqb::gemm_scatter_reduce, py::arg("x"), py::arg("w"), py::arg("w_mn_major"),
         py::arg("x2"), py::arg("w2"), py::arg("bias"), py::arg("peer_recv"), py::arg("my_recv"), py::arg("peer_flags"),
         py::arg("my_flags"), py::arg("flag_slots"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),
-        py::arg("tp"));
+        py::arg("tp"), py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0, py::arg("peer_recv_odd") = py::none(),
+        py::arg("my_recv_odd") = 0);
   m.def("rs_reduce", &cqb::rs_reduce);
   m.def("comm_status_read", &cqb::comm_status_read, py::arg("reset") = false);
-  m.def("tp_rms_fwd", &cqb::tp_rms_fwd);
-  m.def("ce_combine_tp", &cqb::ce_combine_tp);
-  m.def("tp_rms_bwd", &cqb::tp_rms_bwd);
+  m.def("tp_rms_fwd", &cqb::tp_rms_fwd, py::arg("x"), py::arg("w"), py::arg("peer_recv"), py::arg("my_recv"),
+        py::arg("peer_flags"), py::arg("my_flags"), py::arg("rank"), py::arg("tp"), py::arg("max_rows"),
+        py::arg("epoch"), py::arg("total_dim"), py::arg("eps"), py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0,
+        py::arg("peer_recv_odd") = py::none(), py::arg("my_recv_odd") = 0);
+  m.def("ce_combine_tp", &cqb::ce_combine_tp, py::arg("part"), py::arg("tgt_local"), py::arg("peer_recv"),
+        py::arg("my_recv"), py::arg("peer_flags"), py::arg("my_flags"), py::arg("rank"), py::arg("tp"),
+        py::arg("max_rows"), py::arg("epoch"), py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0,
+        py::arg("peer_recv_odd") = py::none(), py::arg("my_recv_odd") = 0);
+  m.def("tp_rms_bwd", &cqb::tp_rms_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("peer_recv"), py::arg("my_recv"), py::arg("peer_flags"), py::arg("my_flags"), py::arg("rank"),
+        py::arg("tp"), py::arg("max_rows"), py::arg("epoch"), py::arg("total_dim"), py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0,
+        py::arg("peer_recv_odd") = py::none(), py::arg("my_recv_odd") = 0);
   m.def("gdn_fwd", &cqb::gdn_fwd, py::arg("W"), py::arg("U"), py::arg("P"), py::arg("Qd"), py::arg("Kt"),
         py::arg("gamma"), py::arg("start"), py::arg("count"), py::arg("want_final") = false);
   m.def("gdn_decode_step", &cqb::gdn_decode_step);

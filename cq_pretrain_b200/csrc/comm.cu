@@ -99,6 +99,11 @@ struct TpNormArgs {
   int rank, tp, max_rows;
   long long epoch;
   int* status;
+  // graph-safe epochs (see epoch_begin): device counter, finished-CTA count, odd-parity slabs
+  long long* epoch_ctr;
+  unsigned* epoch_done;
+  float* const* peer_recv_odd;
+  float* my_recv_odd;
 };
 
 template <bool BWD>
@@ -106,6 +111,7 @@ __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
   __shared__ float part[STAT_ROWS];
   __shared__ float stat[STAT_ROWS];
   __shared__ int failed;
+  __shared__ long long s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blocks = (a.rows + STAT_ROWS - 1) / STAT_ROWS;
   float dw_acc[4][8];
@@ -115,7 +121,15 @@ __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) dw_acc[i][j] = 0.f;
   }
-  if (threadIdx.x == 0) failed = 0;
+  if (threadIdx.x == 0) {
+    failed = 0;
+    s_epoch = epoch_begin(a.epoch_ctr, a.epoch);
+  }
+  __syncthreads();
+  const long long epoch = s_epoch;
+  const bool odd = (epoch & 1) && a.peer_recv_odd;
+  float* const* peer_recv = odd ? a.peer_recv_odd : a.peer_recv;
+  const float* my_recv = odd ? a.my_recv_odd : a.my_recv;
   for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
     // 1) local partials: warp w handles rows 8w..8w+7 of the block
     for (int rr = 0; rr < 8; ++rr) {
@@ -144,16 +158,16 @@ __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
     // 2) publish to every peer (including this rank's own slab)
     if (threadIdx.x < STAT_ROWS * a.tp) {
       const int t = threadIdx.x / STAT_ROWS, lr = threadIdx.x % STAT_ROWS;
-      a.peer_recv[t][(size_t)a.rank * a.max_rows + b * STAT_ROWS + lr] = part[lr];
+      peer_recv[t][(size_t)a.rank * a.max_rows + b * STAT_ROWS + lr] = part[lr];
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < a.tp) st_release_sys(a.peer_flags[threadIdx.x] + (size_t)b * STAT_MAX_TP + a.rank, a.epoch);
+    if (threadIdx.x < a.tp) st_release_sys(a.peer_flags[threadIdx.x] + (size_t)b * STAT_MAX_TP + a.rank, epoch);
     // 3) acquire the peers' partials of this block
     if (threadIdx.x < a.tp) {
       const long long* f = a.my_flags + (size_t)b * STAT_MAX_TP + threadIdx.x;
       const unsigned long long start = tc::globaltimer();
-      while (ld_acquire_sys(f) < a.epoch) {
+      while (ld_acquire_sys(f) < epoch) {
         if (tc::globaltimer() - start > tc::kWaitNs) {
           atomicCAS(a.status, 0, 200 + threadIdx.x);
           failed = 1;
@@ -162,10 +176,10 @@ __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
       }
     }
     __syncthreads();
-    if (failed) return;   // the host reads the status word; outputs of this call are invalid
+    if (failed) break;   // the host reads the status word; outputs of this call are invalid
     if (threadIdx.x < STAT_ROWS) {
       float sum = 0.f;
-      for (int t = 0; t < a.tp; ++t) sum += a.my_recv[(size_t)t * a.max_rows + b * STAT_ROWS + threadIdx.x];
+      for (int t = 0; t < a.tp; ++t) sum += my_recv[(size_t)t * a.max_rows + b * STAT_ROWS + threadIdx.x];
       stat[threadIdx.x] = sum;
     }
     __syncthreads();
@@ -217,6 +231,8 @@ __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
       a.dw_partial[(size_t)blockIdx.x * a.D + c] = sum;
     }
   }
+  __syncthreads();   // every thread's peer stores and slab reads of the call are done
+  if (threadIdx.x == 0) epoch_end(a.epoch_ctr, a.epoch_done, epoch);
 }
 
 __global__ void column_sum_kernel(const float* __restrict__ partial, int rows, int cols, float* __restrict__ out) {
@@ -310,12 +326,14 @@ namespace {
 __global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __restrict__ part, int tiles,
                                                             const float* __restrict__ tgt_local, int rows,
                                                             float* __restrict__ lse_out, float* __restrict__ tgt_out,
-                                                            float* const* peer_recv, const float* my_recv,
+                                                            float* const* peer_recv_even, const float* my_recv_even,
                                                             long long* const* peer_flags, const long long* my_flags,
-                                                            int rank, int tp, int max_rows, long long epoch,
-                                                            int* status) {
+                                                            int rank, int tp, int max_rows, long long host_epoch,
+                                                            int* status, long long* epoch_ctr, unsigned* epoch_done,
+                                                            float* const* peer_recv_odd, const float* my_recv_odd) {
   __shared__ float trip[STAT_ROWS][3];
   __shared__ int failed;
+  __shared__ long long s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blocks = (rows + STAT_ROWS - 1) / STAT_ROWS;
   auto merge = [](float& m, float& s, float om, float os) {
@@ -324,7 +342,15 @@ __global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __rest
     s = s * __expf(m - nm) + os * __expf(om - nm);
     m = nm;
   };
-  if (threadIdx.x == 0) failed = 0;
+  if (threadIdx.x == 0) {
+    failed = 0;
+    s_epoch = epoch_begin(epoch_ctr, host_epoch);
+  }
+  __syncthreads();
+  const long long epoch = s_epoch;
+  const bool odd = (epoch & 1) && peer_recv_odd;
+  float* const* peer_recv = odd ? peer_recv_odd : peer_recv_even;
+  const float* my_recv = odd ? my_recv_odd : my_recv_even;
   for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
     for (int rr = 0; rr < STAT_ROWS / 8; ++rr) {
       const int lr = warp * (STAT_ROWS / 8) + rr, row = b * STAT_ROWS + lr;
@@ -369,7 +395,7 @@ __global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __rest
       }
     }
     __syncthreads();
-    if (failed) return;   // the host reads the status word; outputs of this call are invalid
+    if (failed) break;   // the host reads the status word; outputs of this call are invalid
     if (threadIdx.x < STAT_ROWS) {
       const int row = b * STAT_ROWS + threadIdx.x;
       float m = -INFINITY, sum = 0.f, tg = 0.f;
@@ -385,6 +411,7 @@ __global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __rest
     }
     __syncthreads();   // trip[] is rewritten by the next block
   }
+  if (threadIdx.x == 0) epoch_end(epoch_ctr, epoch_done, epoch);
 }
 
 }  // namespace
@@ -394,7 +421,8 @@ __global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __rest
 // statistics slab, so 3 * rows <= max_rows.
 std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at::Tensor peer_recv, int64_t my_recv,
                                       at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
-                                      int64_t max_rows, int64_t epoch) {
+                                      int64_t max_rows, int64_t epoch, int64_t epoch_ctr, int64_t epoch_done,
+                                      c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
   TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.dim() == 3 && part.size(2) == 2 &&
                   part.is_contiguous(),
               "part: fp32 [rows, tiles, 2]");
@@ -404,12 +432,17 @@ std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at:
   TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && 3 * rows <= max_rows, "rows exceed the exchange slab");
   auto lse = at::empty({rows}, part.options()), tgt = at::empty({rows}, part.options());
   if (!rows) return {lse, tgt};
+  TORCH_CHECK(!epoch_ctr || (epoch_done && my_recv_odd && peer_recv_odd && peer_recv_odd->numel() == tp),
+              "ce_combine_tp: device epochs need the done counter and the odd-parity slabs");
   const int grid = std::max(1, std::min((int)((rows + STAT_ROWS - 1) / STAT_ROWS), sm_count()));
   ce_combine_tp_kernel<<<grid, 256, 0, stream()>>>(
       reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)part.size(1), tgt_local.data_ptr<float>(),
       (int)rows, lse.data_ptr<float>(), tgt.data_ptr<float>(), reinterpret_cast<float* const*>(peer_recv.data_ptr()),
       reinterpret_cast<const float*>(my_recv), reinterpret_cast<long long* const*>(peer_flags.data_ptr()),
-      reinterpret_cast<const long long*>(my_flags), (int)rank, (int)tp, (int)max_rows, epoch, comm_status());
+      reinterpret_cast<const long long*>(my_flags), (int)rank, (int)tp, (int)max_rows, epoch, comm_status(),
+      reinterpret_cast<long long*>(epoch_ctr), reinterpret_cast<unsigned*>(epoch_done),
+      epoch_ctr ? reinterpret_cast<float* const*>(peer_recv_odd->data_ptr()) : nullptr,
+      reinterpret_cast<const float*>(my_recv_odd));
   CQB_LAUNCH_CHECK();
   count_launch();
   return {lse, tgt};
@@ -418,7 +451,8 @@ std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at:
 namespace {
 TpNormArgs tp_norm_args(const at::Tensor& x, const at::Tensor& w, at::Tensor peer_recv, int64_t my_recv,
                         at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
-                        int64_t epoch, int64_t total_dim, double eps) {
+                        int64_t epoch, int64_t total_dim, double eps, int64_t epoch_ctr, int64_t epoch_done,
+                        const c10::optional<at::Tensor>& peer_recv_odd, int64_t my_recv_odd) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 &&
                   x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
               "x: bf16 [rows, D] with 16-byte aligned rows");
@@ -442,6 +476,14 @@ TpNormArgs tp_norm_args(const at::Tensor& x, const at::Tensor& w, at::Tensor pee
   a.max_rows = (int)max_rows;
   a.epoch = epoch;
   a.status = comm_status();
+  if (epoch_ctr) {
+    TORCH_CHECK(epoch_done && my_recv_odd && peer_recv_odd && peer_recv_odd->numel() == tp,
+                "tp_rms: device epochs need the done counter and the odd-parity slabs");
+    a.epoch_ctr = reinterpret_cast<long long*>(epoch_ctr);
+    a.epoch_done = reinterpret_cast<unsigned*>(epoch_done);
+    a.peer_recv_odd = reinterpret_cast<float* const*>(peer_recv_odd->data_ptr());
+    a.my_recv_odd = reinterpret_cast<float*>(my_recv_odd);
+  }
   return a;
 }
 int tp_norm_grid(int rows) { return std::max(1, std::min((rows + STAT_ROWS - 1) / STAT_ROWS, sm_count())); }
@@ -450,8 +492,10 @@ int tp_norm_grid(int rows) { return std::max(1, std::min((rows + STAT_ROWS - 1) 
 // y = x * rsqrt(sum_over_ranks(x^2) / total_dim + eps) * w; returns (y, rstd).
 std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_recv, int64_t my_recv,
                                    at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
-                                   int64_t epoch, int64_t total_dim, double eps) {
-  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, eps);
+                                   int64_t epoch, int64_t total_dim, double eps, int64_t epoch_ctr,
+                                   int64_t epoch_done, c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
+  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, eps,
+                        epoch_ctr, epoch_done, peer_recv_odd, my_recv_odd);
   auto y = at::empty({x.size(0), x.size(1)}, x.options());
   auto rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
   a.y = (__nv_bfloat16*)y.data_ptr();
@@ -467,8 +511,10 @@ std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_r
 // Backward: returns (dx, dw fp32 [D]); the row dot products dy.w.x are summed over ranks.
 std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor peer_recv,
                                    int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
-                                   int64_t max_rows, int64_t epoch, int64_t total_dim) {
-  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, 0.0);
+                                   int64_t max_rows, int64_t epoch, int64_t total_dim, int64_t epoch_ctr,
+                                   int64_t epoch_done, c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
+  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, 0.0,
+                        epoch_ctr, epoch_done, peer_recv_odd, my_recv_odd);
   auto dyc = dy.contiguous();
   TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.sizes() == x.sizes(), "dy like x");
   TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() == x.size(0), "rstd: fp32 [rows]");

@@ -89,6 +89,25 @@ __device__ __forceinline__ void store8(float* p, const float* in) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
+// Graph-safe call epochs of the peer-memory collectives. With a device counter (`ctr` non-null)
+// a call's epoch is *ctr + 1, read by thread 0 of every CTA at the start (the previous call of the
+// same kind finished in stream order, so the counter is final); the last CTA to finish stores the
+// epoch back (`done` counts finished CTAs and is re-zeroed by that CTA). A captured CUDA graph
+// therefore advances the epoch on every replay, where a host-chosen epoch would repeat.
+__device__ __forceinline__ long long epoch_begin(const long long* ctr, long long host_epoch) {
+  return ctr ? *reinterpret_cast<volatile const long long*>(ctr) + 1 : host_epoch;
+}
+// Called by thread 0 of every CTA after the CTA's last access of the call's buffers and flags.
+__device__ __forceinline__ void epoch_end(long long* ctr, unsigned* done, long long epoch) {
+  if (!ctr) return;
+  __threadfence();
+  if (atomicAdd(done, 1u) == gridDim.x * gridDim.y * gridDim.z - 1) {
+    *reinterpret_cast<volatile long long*>(ctr) = epoch;
+    *reinterpret_cast<volatile unsigned*>(done) = 0u;
+    __threadfence();
+  }
+}
+
 // ---- debug bounds checks ----------------------------------------------------------------------
 // Built with -DCQB_DEBUG_BOUNDS (`python -m cq_pretrain_b200.build --debug`), CQB_IN_RANGE(i, n, site)
 // tests 0 <= i < n; the first failure of a translation unit is recorded in its status block

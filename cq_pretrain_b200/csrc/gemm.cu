@@ -98,6 +98,17 @@ struct GemmArgs {
   const __nv_bfloat16* my_recv;
   long long* const* rs_flags_peer;
   const long long* rs_flags_mine;
+  // Graph-safe epochs (epoch_ctr non-null): the call's epoch is *epoch_ctr + 1, read by every CTA at
+  // the start; the last CTA to finish stores it back (epoch_done counts finished CTAs), so the next
+  // call of the kind, ordered after this one on the stream, sees it, also inside a CUDA-graph
+  // replay. The epoch's parity then picks the double-buffered symmetric buffers on the device:
+  // the *_odd pointers are used for odd epochs (host-chosen epochs pass the call's buffers only).
+  long long* epoch_ctr;
+  unsigned* epoch_done;
+  const __nv_bfloat16* const* peer_in_odd;
+  __nv_bfloat16* send_mine_odd;
+  void* const* peer_out_odd;
+  const __nv_bfloat16* my_recv_odd;
 };
 
 __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
@@ -194,6 +205,9 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ long long s_epoch;
+  if (threadIdx.x == 0)
+    s_epoch = epoch_begin(args.epoch_ctr, args.epoch);
   const int tiles_m = (args.M + BM - 1) / BM, tiles_n = (args.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
   const int kb_first = (args.K + BK - 1) / BK;   // k blocks of the first operand pair
@@ -219,6 +233,12 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
+  const long long epoch = s_epoch;
+  const bool odd = (epoch & 1) != 0;
+  const __nv_bfloat16* const* peer_in = (odd && args.peer_in_odd) ? args.peer_in_odd : args.peer_in;
+  __nv_bfloat16* send_mine = (odd && args.send_mine_odd) ? args.send_mine_odd : args.send_mine;
+  void* const* peer_out = (odd && args.peer_out_odd) ? args.peer_out_odd : args.peer_out;
+  const __nv_bfloat16* my_recv = (odd && args.my_recv_odd) ? args.my_recv_odd : args.my_recv;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -243,7 +263,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         if (GATHER && m0 != ready_m0) {
           // the row block is ready once all of its 16-row sub-chunks are published
           for (int j = 0; j < BM / GATHER_SUB && ok; ++j)
-            ok = wait_flag<false>(args.chunk_flags + m0 / GATHER_SUB + j, args.epoch, status, abort_flag, 5);
+            ok = wait_flag<false>(args.chunk_flags + m0 / GATHER_SUB + j, epoch, status, abort_flag, 5);
           if (!ok) break;
           fence_proxy_async_global();
           ready_m0 = m0;
@@ -399,7 +419,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           for (int s = 0; s < args.tp && ok; ++s)
             if (s != args.src_rank)
               ok = wait_flag<true>(args.rs_flags_mine + ((size_t)owner_tile * RS_MAX_TP + s) * 4 + quarter,
-                                   args.epoch, status, abort_flag, 7);
+                                   epoch, status, abort_flag, 7);
         ok = __shfl_sync(0xffffffffu, ok, 0) != 0;  // the warp barrier orders lane 0's acquire before all lanes' reads
         if (!ok) break;
       }
@@ -427,7 +447,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           const int valid = min(32, args.N - col0);
           for (int s = 0; s < args.tp; ++s) {
             if (s == args.src_rank) continue;
-            const __nv_bfloat16* src = args.my_recv + ((size_t)s * args.rows_per_rank + lrow) * args.N + col0;
+            const __nv_bfloat16* src = my_recv + ((size_t)s * args.rows_per_rank + lrow) * args.N + col0;
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
               if (j < valid) {
@@ -476,7 +496,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         if (EPI == 2 || (EPI == 5 && !own)) {
           __syncwarp();
           const int lrow0 = args.src_rank * args.rows_per_rank + (m0 - owner * args.rows_per_rank) + quarter * 32;
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.peer_out[owner]) + (size_t)lrow0 * args.N + col0;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peer_out[owner]) + (size_t)lrow0 * args.N + col0;
           const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(box);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -513,7 +533,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         __syncwarp();
         if (lane == 0)
           st_release_sys(args.rs_flags_peer[owner] + ((size_t)owner_tile * RS_MAX_TP + args.src_rank) * 4 + quarter,
-                         args.epoch);
+                         epoch);
       }
     }
     if (EPI != 2 && EPI != 3 && lane == 0) tc::bulk_wait_all();
@@ -532,12 +552,12 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       const int lrow = row0 - s * args.rows_per_rank;
       const bool stage = s == args.src_rank && args.x_local != nullptr;
       bool ok = true;
-      if (ct == 0 && s != args.src_rank) ok = wait_flag<true>(args.ready + s, args.epoch, status, abort_flag, 6);
+      if (ct == 0 && s != args.src_rank) ok = wait_flag<true>(args.ready + s, epoch, status, abort_flag, 6);
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (*abort_flag || !ok) break;
-      const uint4* src = reinterpret_cast<const uint4*>((stage ? args.x_local : args.peer_in[s]) + (size_t)lrow * args.K);
+      const uint4* src = reinterpret_cast<const uint4*>((stage ? args.x_local : peer_in[s]) + (size_t)lrow * args.K);
       uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)row0 * args.K);
-      uint4* dst2 = stage ? reinterpret_cast<uint4*>(args.send_mine + (size_t)lrow * args.K) : nullptr;
+      uint4* dst2 = stage ? reinterpret_cast<uint4*>(send_mine + (size_t)lrow * args.K) : nullptr;
       const int vecs = GATHER_SUB * args.K / 8;
       // 16 independent 16-byte loads in flight per thread: NVLink latency is hidden by
       // memory-level parallelism rather than by occupancy.
@@ -563,7 +583,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       if (stage) __threadfence_system(); else __threadfence();
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (ct == 0) {
-        st_release_gpu(args.chunk_flags + sub, args.epoch);
+        st_release_gpu(args.chunk_flags + sub, epoch);
         if (stage) {
           // the last own sub-chunk staged (over all CTAs) publishes this rank's shard to the peers
           const unsigned own_subs = (unsigned)(args.rows_per_rank / GATHER_SUB);
@@ -571,7 +591,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
             atomicExch(args.own_done, 0u);
             __threadfence_system();
             for (int p = 0; p < args.tp; ++p)
-              if (p != args.src_rank) st_release_sys(args.peer_ready[p] + args.src_rank, args.epoch);
+              if (p != args.src_rank) st_release_sys(args.peer_ready[p] + args.src_rank, epoch);
           }
         }
       }
@@ -582,6 +602,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     tc::fence_after();
     tc::tmem_dealloc(tmem, 2 * BN);
   }
+  if (threadIdx.x == 0) epoch_end(args.epoch_ctr, args.epoch_done, epoch);   // last CTA publishes the epoch
 }
 
 // ---- host side ----------------------------------------------------------------------------
@@ -828,7 +849,9 @@ void gemm_scatter(at::Tensor x, at::Tensor w, bool w_mn_major, at::Tensor peer_o
 at::Tensor gemm_scatter_reduce(at::Tensor x, at::Tensor w, bool w_mn_major, c10::optional<at::Tensor> x2,
                                c10::optional<at::Tensor> w2, c10::optional<at::Tensor> bias, at::Tensor peer_recv,
                                int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t flag_slots,
-                               int64_t epoch, int64_t rows_per_rank, int64_t src_rank, int64_t tp) {
+                               int64_t epoch, int64_t rows_per_rank, int64_t src_rank, int64_t tp,
+                               int64_t epoch_ctr, int64_t epoch_done, c10::optional<at::Tensor> peer_recv_odd,
+                               int64_t my_recv_odd) {
   const int64_t M = x.size(0), K = x.size(1), N = w_mn_major ? w.size(1) : w.size(0);
   TORCH_CHECK(w_mn_major ? w.size(0) == K : w.size(1) == K, "gemm_scatter_reduce: inner dims differ");
   check_dims(M, N, K);
@@ -852,6 +875,15 @@ at::Tensor gemm_scatter_reduce(at::Tensor x, at::Tensor w, bool w_mn_major, c10:
   args.rows_per_rank = (int)rows_per_rank;
   args.src_rank = (int)src_rank;
   args.tp = (int)tp;
+  if (epoch_ctr) {   // graph-safe epochs: the kernel reads and advances the device counter
+    TORCH_CHECK(epoch_done != 0 && peer_recv_odd && peer_recv_odd->is_cuda() && peer_recv_odd->numel() == tp &&
+                    my_recv_odd != 0,
+                "gemm_scatter_reduce: device epochs need the done counter and the odd-parity buffers");
+    args.epoch_ctr = reinterpret_cast<long long*>(epoch_ctr);
+    args.epoch_done = reinterpret_cast<unsigned*>(epoch_done);
+    args.peer_out_odd = reinterpret_cast<void* const*>(peer_recv_odd->data_ptr());
+    args.my_recv_odd = reinterpret_cast<const __nv_bfloat16*>(my_recv_odd);
+  }
   CUtensorMap ma2, mb2;
   const bool dual = x2 && x2->defined();
   if (dual) {
@@ -882,7 +914,8 @@ at::Tensor gemm_scatter_reduce(at::Tensor x, at::Tensor w, bool w_mn_major, c10:
 at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor peer_in_ptrs,
                        int64_t ready_ptr, at::Tensor chunk_flags, int64_t epoch, int64_t rows_per_rank, int64_t src_rank,
                        int64_t tp, bool mn_major, c10::optional<at::Tensor> x_local, int64_t send_mine,
-                       c10::optional<at::Tensor> peer_ready, int64_t own_done) {
+                       c10::optional<at::Tensor> peer_ready, int64_t own_done, int64_t epoch_ctr, int64_t epoch_done,
+                       c10::optional<at::Tensor> peer_in_odd, int64_t send_mine_odd) {
   const int64_t M = a_local.size(0), K = a_local.size(1), N = mn_major ? w.size(1) : w.size(0);
   TORCH_CHECK(!mn_major || w.size(0) == K, "gather_gemm: inner dims differ");
   check_dims(M, N, K);
@@ -914,6 +947,15 @@ at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tenso
     args.send_mine = reinterpret_cast<__nv_bfloat16*>(send_mine);
     args.peer_ready = reinterpret_cast<long long* const*>(peer_ready->data_ptr());
     args.own_done = reinterpret_cast<unsigned*>(own_done);
+  }
+  if (epoch_ctr) {   // graph-safe epochs: the kernel reads and advances the device counter
+    TORCH_CHECK(epoch_done != 0 && peer_in_odd && peer_in_odd->is_cuda() && peer_in_odd->numel() == tp &&
+                    (!args.x_local || send_mine_odd != 0),
+                "gather_gemm: device epochs need the done counter and the odd-parity buffers");
+    args.epoch_ctr = reinterpret_cast<long long*>(epoch_ctr);
+    args.epoch_done = reinterpret_cast<unsigned*>(epoch_done);
+    args.peer_in_odd = reinterpret_cast<const __nv_bfloat16* const*>(peer_in_odd->data_ptr());
+    args.send_mine_odd = reinterpret_cast<__nv_bfloat16*>(send_mine_odd);
   }
   if (mn_major)
     launch<false, true, 0, true>(ma, mb, make_out_map(y), args);

@@ -31,6 +31,13 @@ Double buffering plus the flag order makes buffer reuse safe: a rank can only ov
 of parity p at epoch e after every peer has signalled epoch e-1, which each peer does only after
 its own epoch e-2 work (the last reader/writer of that slot) completed in stream order.
 All waits are bounded in the kernels and report a status code instead of hanging.
+
+Epochs live on the device: each kind (all-gather, reduce-scatter, statistics) has an int64 counter
+in local memory that a call's kernel reads at its start (epoch = counter + 1) and its last CTA
+advances at its end, and the kernel picks the parity buffers from the epoch it read. A CUDA graph
+that captured fused TP calls therefore takes fresh epochs on every replay, interleaved correctly
+with eager calls of the same kind. The host passes both parities' buffers and counts calls only
+for reporting.
 """
 
 from __future__ import annotations
@@ -91,12 +98,21 @@ class SymmetricWorkspace:
         self.stat_flags = as_dev([b + self.off_stat_flags for b in bases])
         self.stat = [as_dev([b + self.off_stat[p] for b in bases]) for p in range(2)]
         self.rs_flags = as_dev([b + self.off_rs_flags for b in bases])
-        self.epoch_stat = 0
         # one publication flag per 16 gathered rows (the all-gather copy unit)
         self.chunk_flags = torch.zeros(max_subchunks, dtype=torch.int64, device=dev)
-        self.epoch_ag = 0
-        self.epoch_rs = 0
+        # device epoch counters and finished-CTA counts of the three kinds (all-gather, RS, statistics)
+        self.ectr = torch.zeros(3, dtype=torch.int64, device=dev)
+        self.edone = torch.zeros(3, dtype=torch.int32, device=dev)
+        self._ctr = [self.ectr.data_ptr() + 8 * k for k in range(3)]
+        self._done = [self.edone.data_ptr() + 4 * k for k in range(3)]
+        self.epoch_ag = self.epoch_rs = self.epoch_stat = 0   # host-issued calls (reporting only)
         dist.barrier(group=self.group)
+
+    def device_epochs(self):
+        """The device counters (all_gather, reduce_scatter, statistics): calls completed on the
+        device, CUDA-graph replays included (reads the counters, so it synchronises)."""
+        ag, rs, stat = self.ectr.tolist()
+        return dict(all_gather=ag, reduce_scatter=rs, statistics=stat)
 
     # ---- eligibility --------------------------------------------------------------------------
     def supports(self, x, w, transposed=False):
@@ -135,24 +151,25 @@ class SymmetricWorkspace:
             xg = gather_rows_raw(x)
             return (gemm.matmul_nn(xg, weight) if mn_major else gemm.linear(xg, weight, bias)), xg
         self.epoch_ag += 1
-        e, p = self.epoch_ag, self.epoch_ag % 2
         rows = x.shape[0]
         xg = torch.empty(rows * self.tp, x.shape[1], dtype=x.dtype, device=x.device)
-        y = ops.gather_gemm(xg, weight.contiguous(), bias, self.send[p], self.base, self.chunk_flags, e, rows,
+        y = ops.gather_gemm(xg, weight.contiguous(), bias, self.send[0], self.base, self.chunk_flags, 0, rows,
                             self.rank, self.tp, mn_major, x_local=x.contiguous(),
-                            send_mine=self.base + self.off_send[p], peer_ready=self.flag_ag,
-                            own_done=self.base + 2 * FLAG_BYTES)
+                            send_mine=self.base + self.off_send[0], peer_ready=self.flag_ag,
+                            own_done=self.base + 2 * FLAG_BYTES, epoch_ctr=self._ctr[0], epoch_done=self._done[0],
+                            peer_in_odd=self.send[1], send_mine_odd=self.base + self.off_send[1])
         return y, xg
 
     def _scatter(self, x, weight, mn_major, x2=None, w2=None, bias=None):
         self.epoch_rs += 1
-        e, p = self.epoch_rs, self.epoch_rs % 2
         rows = x.shape[0] // self.tp
         if x2 is not None:
             x2, w2 = x2.contiguous(), w2.contiguous()
         return _ext.ops().gemm_scatter_reduce(
-            x.contiguous(), weight.contiguous(), mn_major, x2, w2, bias, self.recv[p], self.base + self.off_recv[p],
-            self.rs_flags, self.base + self.off_rs_flags, self.rs_slots, e, rows, self.rank, self.tp)
+            x.contiguous(), weight.contiguous(), mn_major, x2, w2, bias, self.recv[0], self.base + self.off_recv[0],
+            self.rs_flags, self.base + self.off_rs_flags, self.rs_slots, 0, rows, self.rank, self.tp,
+            epoch_ctr=self._ctr[1], epoch_done=self._done[1], peer_recv_odd=self.recv[1],
+            my_recv_odd=self.base + self.off_recv[1])
 
     def supports_scatter(self, x, w, transposed=False, x2=None, w2=None):
         """Eligibility of the one-kernel GEMM -> reduce-scatter (optionally with a second operand pair)."""
@@ -174,19 +191,18 @@ class SymmetricWorkspace:
                 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and x.shape[1] % 8 == 0
                 and x.shape[1] <= 1024 and x.shape[0] <= self.stat_rows)
 
-    def rms_forward(self, x, weight, total_dim, eps):
+    def _stat_kwargs(self):
         self.epoch_stat += 1
-        e, p = self.epoch_stat, self.epoch_stat % 2
-        return _ext.ops().tp_rms_fwd(x, weight, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
-                                     self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e,
-                                     total_dim, eps)
+        return dict(peer_recv=self.stat[0], my_recv=self.base + self.off_stat[0], peer_flags=self.stat_flags,
+                    my_flags=self.base + self.off_stat_flags, rank=self.rank, tp=self.tp, max_rows=self.stat_rows,
+                    epoch=0, epoch_ctr=self._ctr[2], epoch_done=self._done[2], peer_recv_odd=self.stat[1],
+                    my_recv_odd=self.base + self.off_stat[1])
+
+    def rms_forward(self, x, weight, total_dim, eps):
+        return _ext.ops().tp_rms_fwd(x, weight, total_dim=total_dim, eps=eps, **self._stat_kwargs())
 
     def rms_backward(self, dy, x, weight, rstd, total_dim):
-        self.epoch_stat += 1
-        e, p = self.epoch_stat, self.epoch_stat % 2
-        return _ext.ops().tp_rms_bwd(dy, x, weight, rstd, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
-                                     self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e,
-                                     total_dim)
+        return _ext.ops().tp_rms_bwd(dy, x, weight, rstd, total_dim=total_dim, **self._stat_kwargs())
 
     def supports_ce(self, rows):
         return 3 * rows <= self.stat_rows and _ext.has("ce_combine_tp")
@@ -194,10 +210,7 @@ class SymmetricWorkspace:
     def ce_combine(self, part, tgt_local):
         """Full-vocabulary (lse, target logit) per row from this rank's LM-head partials: the
         (max, sum exp, target) triples cross NVLink inside one kernel (no NCCL call)."""
-        self.epoch_stat += 1
-        e, p = self.epoch_stat, self.epoch_stat % 2
-        return _ext.ops().ce_combine_tp(part, tgt_local, self.stat[p], self.base + self.off_stat[p], self.stat_flags,
-                                        self.base + self.off_stat_flags, self.rank, self.tp, self.stat_rows, e)
+        return _ext.ops().ce_combine_tp(part, tgt_local, **self._stat_kwargs())
 
     def linear_scatter(self, x, weight, bias=None):
         """``reduce_scatter_rows(x @ W^T) + b`` in one GEMM -> reduce-scatter kernel."""
@@ -228,8 +241,8 @@ def workspace():
 
 @contextmanager
 def suspended():
-    """Route the TP linears through NCCL + the plain GEMM inside this block (the fused kernels
-    take a host-side epoch per call, which a CUDA-graph replay would repeat)."""
+    """Route the TP linears through NCCL + the plain GEMM inside this block (for comparisons
+    and for work that one rank runs without its peers)."""
     global _SUSPENDED
     _SUSPENDED += 1
     try:

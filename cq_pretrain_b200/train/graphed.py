@@ -20,10 +20,11 @@ replays:
   ``_ext.launches()`` counts executed kernels.
 
 Graphs are used where the captured work is position independent: CUDA, no activation recompute
-inside the DiT, and the Wan renderer. At TP > 1 (opt-in, ``CQB_GRAPHS_TP=1``) the chunk runs its TP
-linears through NCCL and the plain GEMM (``parallel.symmetric.suspended``), because the fused TP
-kernels take a host-side epoch per call that a replay would repeat; NCCL collectives are captured
-with the rest. ``CQB_GRAPHS=0`` turns graphs off.
+inside the DiT, and the Wan renderer. At TP > 1 (opt-in, ``CQB_GRAPHS_TP=1``) the fused TP kernels
+are captured with the rest: they read their call epochs from device counters, so every replay
+takes fresh epochs and parity buffers (``parallel.symmetric``). ``CQB_GRAPHS_TP_NCCL=1`` routes the
+captured TP linears through NCCL and the plain GEMM instead (``parallel.symmetric.suspended``; the
+NCCL collectives are captured). ``CQB_GRAPHS=0`` turns graphs off.
 """
 
 from __future__ import annotations
@@ -111,7 +112,7 @@ class RendererGraphs:
 
     def run(self, model, leaf, bound, factor):
         from ..parallel import state as ps, symmetric
-        if ps.tp_size() > 1:   # fused TP kernels stay out of captured work (see the module note)
+        if ps.tp_size() > 1 and os.environ.get("CQB_GRAPHS_TP_NCCL") == "1":
             with symmetric.suspended():
                 return self._run(model, leaf, bound, factor)
         return self._run(model, leaf, bound, factor)

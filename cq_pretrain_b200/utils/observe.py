@@ -119,8 +119,8 @@ def backend_provenance():
             info["nccl"] = None
     from ..parallel import symmetric
     ws = symmetric.workspace()
-    info["tp_symmetric_workspace"] = None if ws is None else dict(tp=ws.tp, epochs=dict(
-        all_gather=ws.epoch_ag, reduce_scatter=ws.epoch_rs, statistics=ws.epoch_stat))
+    info["tp_symmetric_workspace"] = None if ws is None else dict(tp=ws.tp, host_calls=dict(
+        all_gather=ws.epoch_ag, reduce_scatter=ws.epoch_rs, statistics=ws.epoch_stat), device_epochs=ws.device_epochs())
     info["deterministic_wgrad"] = os.environ.get("CQB_DETERMINISTIC") == "1"
     return info
 

@@ -127,6 +127,7 @@ def _worker(rank, world, port, out):
         results.append([ya.detach().float(), yb.detach().float()] + [t.grad.float() for t in leaves])
     for a, b in zip(*results):
         errors.append(float((a - b).norm() / b.norm().clamp_min(1e-6)))
+    errors += _graph_replays(ws, world)
     torch.cuda.synchronize()
     status = symmetric.status()
     symmetric.disable()
@@ -134,10 +135,99 @@ def _worker(rank, world, port, out):
     torch.save(dict(errors=errors, status=status), f"{out}.{rank}")
 
 
+def _graph_replays(ws, world):
+    """Fused calls captured in a CUDA graph take fresh device epochs on every replay, interleaved
+    with eager calls of the same kinds (odd counts, so replays alternate the buffer parities)."""
+    from cq_pretrain_b200.ops import gemm
+    from cq_pretrain_b200.parallel import fused
+    errors = []
+    x = torch.randn(256, 512, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(384, 512, device="cuda") * 0.05).to(torch.bfloat16)
+    xf = torch.randn(256 * world, 256, device="cuda", dtype=torch.bfloat16)
+    w2 = (torch.randn(512, 256, device="cuda") * 0.05).to(torch.bfloat16)
+    xr = torch.randn(700, 384, device="cuda", dtype=torch.bfloat16)
+    wr = torch.rand(384, device="cuda") + 0.5
+    before = ws.device_epochs()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y, _ = ws.gather_linear(x, w)
+        z = ws.linear_scatter(xf, w2)
+        yr, _ = ws.rms_forward(xr, wr, 384 * world, 1e-6)
+    assert ws.device_epochs() == before   # capture records work, it runs none
+    for rep in range(3):
+        x.copy_(torch.randn_like(x))
+        xf.copy_(torch.randn_like(xf))
+        xr.copy_(torch.randn_like(xr))
+        graph.replay()
+        ref = gemm.linear(fused.gather_rows_raw(x), w).float()
+        errors.append(float((y.float() - ref).abs().max() / ref.abs().max()))
+        zref = fused.scatter_rows_raw(gemm.linear(xf, w2)).float()
+        errors.append(float((z.float() - zref).abs().max() / zref.abs().max()))
+        sq = xr.float().square().sum(-1, keepdim=True)
+        dist.all_reduce(sq)
+        rref = xr.float() * torch.rsqrt(sq / (384 * world) + 1e-6) * wr
+        errors.append(float((yr.float() - rref).abs().max() / rref.abs().max()))
+        ye, _ = ws.gather_linear(x, w)   # an eager call between replays shifts the parity
+        errors.append(float((ye.float() - ref).abs().max() / ref.abs().max()))
+    after = ws.device_epochs()
+    assert after["all_gather"] - before["all_gather"] == 6, (before, after)
+    assert after["reduce_scatter"] - before["reduce_scatter"] == 3, (before, after)
+    assert after["statistics"] - before["statistics"] == 3, (before, after)
+    del graph
+    return errors
+
+
 def _all_gather(x):
     """Differentiable row all-gather (NCCL) for the reference path."""
     from torch.distributed.nn.functional import all_gather
     return all_gather(x)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_device_epochs_advance_in_graph_replays():
+    """One rank (tp = 1: the peer arrays hold this GPU's own buffers) runs the row-statistic
+    exchange with device epochs: eager calls and CUDA-graph replays each advance the counter, each
+    takes the buffers of its epoch's parity, and every call normalises correctly."""
+    from cq_pretrain_b200.ops import _ext
+    ops = _ext.ops()
+    dev = torch.device("cuda")
+    max_rows = 1024
+    flags = torch.zeros(-(-max_rows // 64) * 8, dtype=torch.int64, device=dev)
+    slabs = [torch.zeros(max_rows, dtype=torch.float32, device=dev) for _ in range(2)]
+    ptr = lambda t: torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev)
+    ctr = torch.zeros(1, dtype=torch.int64, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    x = torch.randn(700, 256, device=dev, dtype=torch.bfloat16)
+    w = torch.rand(256, device=dev) + 0.5
+
+    def call():
+        return ops.tp_rms_fwd(x, w, peer_recv=ptr(slabs[0]), my_recv=slabs[0].data_ptr(), peer_flags=ptr(flags),
+                              my_flags=flags.data_ptr(), rank=0, tp=1, max_rows=max_rows, epoch=0, total_dim=256,
+                              eps=1e-6, epoch_ctr=ctr.data_ptr(), epoch_done=done.data_ptr(),
+                              peer_recv_odd=ptr(slabs[1]), my_recv_odd=slabs[1].data_ptr())
+
+    def ref():
+        xf = x.float()
+        return xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + 1e-6) * w
+
+    y, _ = call()
+    torch.cuda.synchronize()
+    assert int(ctr) == 1 and int(done) == 0
+    torch.testing.assert_close(y.float(), ref(), rtol=2e-2, atol=2e-2)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        yg, _ = call()
+    assert int(ctr) == 1
+    for rep in range(4):
+        x.copy_(torch.randn_like(x))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert int(ctr) == 2 + rep and int(done) == 0
+        torch.testing.assert_close(yg.float(), ref(), rtol=2e-2, atol=2e-2)
+        # this epoch's partial sums went to the slab of its parity, the other one is stale
+        assert slabs[(2 + rep) % 2][:700].abs().sum() > 0
+    assert int(flags[:8].max()) == 5 and ops.comm_status_read(True) == 0
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
