@@ -70,6 +70,20 @@ std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at
                                    int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
                                    int64_t max_rows, int64_t epoch, int64_t total_dim, int64_t epoch_ctr, int64_t epoch_done,
                                    c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd);
+std::vector<at::Tensor> qk_norm_rope_fwd(at::Tensor q, at::Tensor k, at::Tensor wq, at::Tensor wk,
+                                         c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t,
+                                         int64_t head_dim, int64_t total_dim, double eps,
+                                         c10::optional<at::Tensor> peer_recv, int64_t my_recv,
+                                         c10::optional<at::Tensor> peer_flags, int64_t my_flags, int64_t rank,
+                                         int64_t tp, int64_t max_rows, int64_t epoch_ctr, int64_t epoch_done,
+                                         c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd);
+std::vector<at::Tensor> qk_norm_rope_bwd(at::Tensor dyq, at::Tensor dyk, at::Tensor q, at::Tensor k, at::Tensor wq,
+                                         at::Tensor wk, at::Tensor rstd, c10::optional<at::Tensor> cos_t,
+                                         c10::optional<at::Tensor> sin_t, int64_t head_dim, int64_t total_dim,
+                                         c10::optional<at::Tensor> peer_recv, int64_t my_recv,
+                                         c10::optional<at::Tensor> peer_flags, int64_t my_flags, int64_t rank,
+                                         int64_t tp, int64_t max_rows, int64_t epoch_ctr, int64_t epoch_done,
+                                         c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd);
 // gdn.cu
 std::vector<at::Tensor> gdn_fwd(at::Tensor W, at::Tensor U, at::Tensor P, at::Tensor Qd, at::Tensor Kt, at::Tensor gamma,
                                 at::Tensor start, at::Tensor count, bool want_final);
@@ -179,6 +193,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("x2"), py::arg("w2"), py::arg("bias"), py::arg("peer_recv"), py::arg("my_recv"), py::arg("peer_flags"),
         py::arg("my_flags"), py::arg("flag_slots"), py::arg("epoch"), py::arg("rows_per_rank"), py::arg("src_rank"),
         py::arg("tp"), py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0, py::arg("peer_recv_odd") = py::none(),
+        py::arg("my_recv_odd") = 0);
+  m.def("qk_norm_rope_fwd", &cqb::qk_norm_rope_fwd, py::arg("q"), py::arg("k"), py::arg("wq"), py::arg("wk"),
+        py::arg("cos") = py::none(), py::arg("sin") = py::none(), py::arg("head_dim") = 0, py::arg("total_dim"),
+        py::arg("eps"), py::arg("peer_recv") = py::none(), py::arg("my_recv") = 0, py::arg("peer_flags") = py::none(),
+        py::arg("my_flags") = 0, py::arg("rank") = 0, py::arg("tp") = 1, py::arg("max_rows") = 0,
+        py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0, py::arg("peer_recv_odd") = py::none(),
+        py::arg("my_recv_odd") = 0);
+  m.def("qk_norm_rope_bwd", &cqb::qk_norm_rope_bwd, py::arg("dyq"), py::arg("dyk"), py::arg("q"), py::arg("k"),
+        py::arg("wq"), py::arg("wk"), py::arg("rstd"), py::arg("cos") = py::none(), py::arg("sin") = py::none(),
+        py::arg("head_dim") = 0, py::arg("total_dim"), py::arg("peer_recv") = py::none(), py::arg("my_recv") = 0, py::arg("peer_flags") = py::none(),
+        py::arg("my_flags") = 0, py::arg("rank") = 0, py::arg("tp") = 1, py::arg("max_rows") = 0,
+        py::arg("epoch_ctr") = 0, py::arg("epoch_done") = 0, py::arg("peer_recv_odd") = py::none(),
         py::arg("my_recv_odd") = 0);
   m.def("rs_reduce", &cqb::rs_reduce);
   m.def("comm_status_read", &cqb::comm_status_read, py::arg("reset") = false);

@@ -78,21 +78,32 @@ __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, const _
 // stored into slot `rank` of every peer's receive slab (plain peer stores), a system-scope
 // release flag per (block, rank) publishes them, and after acquiring the peers' flags for the
 // same block (bounded wait) the block reduces the tp partials and finishes its rows. The grid
-// is persistent (<= one CTA per SM) and every rank walks the blocks in the same order.
+// is persistent (<= one CTA per SM per tensor) and every rank walks the blocks in the same order.
+//
+// One launch normalises up to two tensors of the same geometry (Wan's q and k: blockIdx.y picks
+// the tensor; tensor t uses rows [t * rows, (t + 1) * rows) of the slabs and flag blocks
+// [t * blocks, (t + 1) * blocks)). With `cos` set, the Wan complex-pair RoPE of head size `hd` is
+// applied to the normalised row in the forward, and the backward first rotates dy back (the
+// rotation by -angle) before the norm backward. Without `exchange` the partials are this rank's
+// own (TP = 1): no peer stores, flags or waits.
 constexpr int STAT_ROWS = 64;          // rows per block
 constexpr int STAT_MAX_TP = 8;
 
 struct TpNormArgs {
-  const __nv_bfloat16* x;
-  int ld_x;
-  const __nv_bfloat16* dy;   // backward only (contiguous [rows, D])
-  const float* w;            // [D] fp32
-  __nv_bfloat16* y;          // fwd: y; bwd: dx (contiguous [rows, D])
-  float* rstd;               // [rows]
-  float* dw_partial;         // bwd: [gridDim.x, D]
+  const __nv_bfloat16* x[2];
+  int ld_x[2];
+  const __nv_bfloat16* dy[2];   // backward only (contiguous [rows, D])
+  const float* w[2];            // [D] fp32
+  __nv_bfloat16* y[2];          // fwd: y; bwd: dx (contiguous [rows, D])
+  float* rstd[2];               // [rows]
+  float* dw_partial[2];         // bwd: [gridDim.x, D]
   int rows, D;
   float inv_total, eps;
-  float* const* peer_recv;   // [tp] slab base of each peer (this call's parity): [tp][max_rows] fp32
+  const float* cos;             // [rows, hd / 2] (RoPE after the norm) or null
+  const float* sin;
+  int hd;
+  bool exchange;
+  float* const* peer_recv;      // [tp] slab base of each peer (even epochs): [tp][max_rows] fp32
   float* my_recv;
   long long* const* peer_flags;  // [tp] flag area of each peer: [blocks][STAT_MAX_TP]
   long long* my_flags;
@@ -106,133 +117,197 @@ struct TpNormArgs {
   float* my_recv_odd;
 };
 
-template <bool BWD>
+// (v[2p], v[2p+1]) rotated by sign * angle_p for the four pairs of columns c..c+7 of `row`.
+__device__ __forceinline__ void rope_rotate8(float* v, const float* cos_t, const float* sin_t, int hd, int row, int c,
+                                             float sign) {
+  const int half = hd / 2, i0 = (c % hd) / 2;
+  const float4 cv = *reinterpret_cast<const float4*>(cos_t + (size_t)row * half + i0);
+  const float4 sv = *reinterpret_cast<const float4*>(sin_t + (size_t)row * half + i0);
+  const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sign * sv.x, sign * sv.y, sign * sv.z, sign * sv.w};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float re = v[2 * p], im = v[2 * p + 1];
+    v[2 * p] = re * cs[p] - im * sn[p];
+    v[2 * p + 1] = im * cs[p] + re * sn[p];
+  }
+}
+
+// NCH: 8-column chunks per lane (D <= NCH * 256).
+template <bool BWD, int NCH>
 __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
   __shared__ float part[STAT_ROWS];
   __shared__ float stat[STAT_ROWS];
   __shared__ int failed;
   __shared__ long long s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.y;
   const int blocks = (a.rows + STAT_ROWS - 1) / STAT_ROWS;
-  float dw_acc[4][8];
+  const __nv_bfloat16* __restrict__ x = a.x[t];
+  const __nv_bfloat16* __restrict__ dyp = a.dy[t];
+  const float* __restrict__ w = a.w[t];
+  const int ld_x = a.ld_x[t];
+  const bool rope = a.cos != nullptr;
+  float dw_acc[NCH][8];
   if (BWD) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < NCH; ++i)
 #pragma unroll
       for (int j = 0; j < 8; ++j) dw_acc[i][j] = 0.f;
   }
   if (threadIdx.x == 0) {
     failed = 0;
-    s_epoch = epoch_begin(a.epoch_ctr, a.epoch);
+    s_epoch = a.exchange ? epoch_begin(a.epoch_ctr, a.epoch) : 0;
   }
   __syncthreads();
   const long long epoch = s_epoch;
   const bool odd = (epoch & 1) && a.peer_recv_odd;
   float* const* peer_recv = odd ? a.peer_recv_odd : a.peer_recv;
   const float* my_recv = odd ? a.my_recv_odd : a.my_recv;
+  const size_t slab_row0 = (size_t)t * a.rows;   // this tensor's rows in the slabs
   for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
-    // 1) local partials: warp w handles rows 8w..8w+7 of the block
-    for (int rr = 0; rr < 8; ++rr) {
-      const int lr = warp * 8 + rr, row = b * STAT_ROWS + lr;
-      float acc = 0.f;
-      if (row < a.rows) {
-        for (int c = lane * 8; c < a.D; c += 256) {
-          float xv[8];
-          load8(a.x + (size_t)row * a.ld_x + c, xv);
-          if (BWD) {
-            float dv[8], wv[8];
-            load8(a.dy + (size_t)row * a.D + c, dv);
-            load8(a.w + c, wv);
+    // 1) local partials: warp w handles rows 8w..8w+7 of the block; the row loop is innermost and
+    // unrolled so a lane has the loads of all eight rows in flight (the pass is latency-bound
+    // with one row at a time)
+    const int row0 = b * STAT_ROWS + warp * 8;
+    const int nrow = min(8, a.rows - row0);
+    float acc[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc += dv[j] * wv[j] * xv[j];
+    for (int rr = 0; rr < 8; ++rr) acc[rr] = 0.f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = lane * 8 + k * 256;
+      if (c >= a.D) break;
+      float wv[8];
+      if (BWD) load8(w + c, wv);
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        if (rr < nrow) {
+          const int row = row0 + rr;
+          float xv[8];
+          load8(x + (size_t)row * ld_x + c, xv);
+          if (BWD) {
+            float dv[8];
+            load8(dyp + (size_t)row * a.D + c, dv);
+            if (rope) rope_rotate8(dv, a.cos, a.sin, a.hd, row, c, -1.f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[rr] += dv[j] * wv[j] * xv[j];
           } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc += xv[j] * xv[j];
+            for (int j = 0; j < 8; ++j) acc[rr] += xv[j] * xv[j];
           }
         }
       }
-      acc = warp_sum(acc);
-      if (lane == 0) part[lr] = acc;
     }
-    __syncthreads();
-    // 2) publish to every peer (including this rank's own slab)
-    if (threadIdx.x < STAT_ROWS * a.tp) {
-      const int t = threadIdx.x / STAT_ROWS, lr = threadIdx.x % STAT_ROWS;
-      peer_recv[t][(size_t)a.rank * a.max_rows + b * STAT_ROWS + lr] = part[lr];
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x < a.tp) st_release_sys(a.peer_flags[threadIdx.x] + (size_t)b * STAT_MAX_TP + a.rank, epoch);
-    // 3) acquire the peers' partials of this block
-    if (threadIdx.x < a.tp) {
-      const long long* f = a.my_flags + (size_t)b * STAT_MAX_TP + threadIdx.x;
-      const unsigned long long start = tc::globaltimer();
-      while (ld_acquire_sys(f) < epoch) {
-        if (tc::globaltimer() - start > tc::kWaitNs) {
-          atomicCAS(a.status, 0, 200 + threadIdx.x);
-          failed = 1;
-          break;
-        }
-      }
-    }
-    __syncthreads();
-    if (failed) break;   // the host reads the status word; outputs of this call are invalid
-    if (threadIdx.x < STAT_ROWS) {
-      float sum = 0.f;
-      for (int t = 0; t < a.tp; ++t) sum += my_recv[(size_t)t * a.max_rows + b * STAT_ROWS + threadIdx.x];
-      stat[threadIdx.x] = sum;
-    }
-    __syncthreads();
-    // 4) finish the rows
+#pragma unroll
     for (int rr = 0; rr < 8; ++rr) {
-      const int lr = warp * 8 + rr, row = b * STAT_ROWS + lr;
-      if (row >= a.rows) continue;
-      float r;
-      if (!BWD) {
-        r = rsqrtf(stat[lr] * a.inv_total + a.eps);
-        if (lane == 0) a.rstd[row] = r;
-      } else {
-        r = a.rstd[row];
+      const float v = warp_sum(acc[rr]);
+      if (lane == 0) part[warp * 8 + rr] = v;
+    }
+    __syncthreads();
+    if (a.exchange) {
+      // 2) publish to every peer (including this rank's own slab)
+      if (threadIdx.x < STAT_ROWS * a.tp) {
+        const int p = threadIdx.x / STAT_ROWS, lr = threadIdx.x % STAT_ROWS;
+        peer_recv[p][(size_t)a.rank * a.max_rows + slab_row0 + b * STAT_ROWS + lr] = part[lr];
       }
-      const float g = BWD ? stat[lr] * r * r * r * a.inv_total : 0.f;
-      int k = 0;
-      for (int c = lane * 8; c < a.D; c += 256, ++k) {
-        float xv[8], wv[8], o[8];
-        load8(a.x + (size_t)row * a.ld_x + c, xv);
-        load8(a.w + c, wv);
-        if (!BWD) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = xv[j] * r * wv[j];
-        } else {
-          float dv[8];
-          load8(a.dy + (size_t)row * a.D + c, dv);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            o[j] = dv[j] * wv[j] * r - xv[j] * g;
-            if (k < 4) dw_acc[k][j] += dv[j] * xv[j] * r;
+      __threadfence_system();
+      __syncthreads();
+      const size_t fb = (size_t)t * blocks + b;   // flag block
+      if (threadIdx.x < a.tp) st_release_sys(a.peer_flags[threadIdx.x] + fb * STAT_MAX_TP + a.rank, epoch);
+      // 3) acquire the peers' partials of this block
+      if (threadIdx.x < a.tp) {
+        const long long* f = a.my_flags + fb * STAT_MAX_TP + threadIdx.x;
+        const unsigned long long start = tc::globaltimer();
+        while (ld_acquire_sys(f) < epoch) {
+          if (tc::globaltimer() - start > tc::kWaitNs) {
+            atomicCAS(a.status, 0, 200 + threadIdx.x);
+            failed = 1;
+            break;
           }
         }
-        store8(a.y + (size_t)row * a.D + c, o);
+      }
+      __syncthreads();
+      if (failed) break;   // the host reads the status word; outputs of this call are invalid
+      if (threadIdx.x < STAT_ROWS) {
+        float sum = 0.f;
+        for (int p = 0; p < a.tp; ++p)
+          sum += my_recv[(size_t)p * a.max_rows + slab_row0 + b * STAT_ROWS + threadIdx.x];
+        stat[threadIdx.x] = sum;
+      }
+    } else if (threadIdx.x < STAT_ROWS) {
+      stat[threadIdx.x] = part[threadIdx.x];
+    }
+    __syncthreads();
+    // 4) finish the rows (chunk outer, the warp's rows inner and unrolled, as in 1)
+    float rr_r[8], rr_g[8];
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) {
+      const int lr = warp * 8 + rr;
+      rr_r[rr] = rr_g[rr] = 0.f;
+      if (rr < nrow) {
+        if (!BWD) {
+          rr_r[rr] = rsqrtf(stat[lr] * a.inv_total + a.eps);
+          if (lane == 0) a.rstd[t][row0 + rr] = rr_r[rr];
+        } else {
+          rr_r[rr] = a.rstd[t][row0 + rr];
+          rr_g[rr] = stat[lr] * rr_r[rr] * rr_r[rr] * rr_r[rr] * a.inv_total;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = lane * 8 + k * 256;
+      if (c >= a.D) break;
+      float wv[8];
+      load8(w + c, wv);
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        if (rr < nrow) {
+          const int row = row0 + rr;
+          const float r = rr_r[rr];
+          float xv[8], o[8];
+          load8(x + (size_t)row * ld_x + c, xv);
+          if (!BWD) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = xv[j] * r * wv[j];
+            if (rope) rope_rotate8(o, a.cos, a.sin, a.hd, row, c, 1.f);
+          } else {
+            float dv[8];
+            load8(dyp + (size_t)row * a.D + c, dv);
+            if (rope) rope_rotate8(dv, a.cos, a.sin, a.hd, row, c, -1.f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              o[j] = dv[j] * wv[j] * r - xv[j] * rr_g[rr];
+              dw_acc[k][j] += dv[j] * xv[j] * r;
+            }
+          }
+          store8(a.y[t] + (size_t)row * a.D + c, o);
+        }
       }
     }
     __syncthreads();   // part/stat reused by the next block
   }
   if (BWD) {
-    // dw partial of this CTA: reduce the 8 warps through shared memory (fixed order)
-    __shared__ float red[8][4 * 256];
-    for (int k = 0; k < 4; ++k)
+    // dw partial of this CTA: reduce the 8 warps through shared memory (fixed order), one
+    // 256-column chunk at a time
+    __shared__ float red[8][256];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) red[warp][k * 256 + lane * 8 + j] = dw_acc[k][j];
-    __syncthreads();
-    for (int c = threadIdx.x; c < a.D; c += blockDim.x) {
-      const int k = c / 256, off = c % 256;
-      float sum = 0.f;
-      for (int wi = 0; wi < 8; ++wi) sum += red[wi][k * 256 + off];
-      a.dw_partial[(size_t)blockIdx.x * a.D + c] = sum;
+    for (int k = 0; k < NCH; ++k) {
+      if (k * 256 >= a.D) break;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = dw_acc[k][j];
+      __syncthreads();
+      const int c = k * 256 + threadIdx.x;
+      if (c < a.D) {
+        float sum = 0.f;
+        for (int wi = 0; wi < 8; ++wi) sum += red[wi][threadIdx.x];
+        a.dw_partial[t][(size_t)blockIdx.x * a.D + c] = sum;
+      }
+      __syncthreads();
     }
   }
   __syncthreads();   // every thread's peer stores and slab reads of the call are done
-  if (threadIdx.x == 0) epoch_end(a.epoch_ctr, a.epoch_done, epoch);
+  if (threadIdx.x == 0 && a.exchange) epoch_end(a.epoch_ctr, a.epoch_done, epoch);
 }
 
 __global__ void column_sum_kernel(const float* __restrict__ partial, int rows, int cols, float* __restrict__ out) {
@@ -449,33 +524,52 @@ std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at:
 }
 
 namespace {
-TpNormArgs tp_norm_args(const at::Tensor& x, const at::Tensor& w, at::Tensor peer_recv, int64_t my_recv,
-                        at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
-                        int64_t epoch, int64_t total_dim, double eps, int64_t epoch_ctr, int64_t epoch_done,
-                        const c10::optional<at::Tensor>& peer_recv_odd, int64_t my_recv_odd) {
+void check_norm_input(const at::Tensor& x, const at::Tensor& w) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 &&
                   x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
               "x: bf16 [rows, D] with 16-byte aligned rows");
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.numel() == x.size(1), "w: fp32 [D]");
-  TORCH_CHECK(x.size(1) % 8 == 0 && x.size(1) <= 1024, "D must be a multiple of 8 and <= 1024");
-  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && x.size(0) <= max_rows, "rows exceed the exchange slab");
+  TORCH_CHECK(x.size(1) % 8 == 0 && x.size(1) <= 2048, "D must be a multiple of 8 and <= 2048");
+}
+
+// xs / ws: one or two tensors of the same geometry (the launch's blockIdx.y).
+TpNormArgs norm_args(const std::vector<at::Tensor>& xs, const std::vector<at::Tensor>& ws, int64_t total_dim,
+                     double eps) {
   TpNormArgs a{};
-  a.x = (const __nv_bfloat16*)x.data_ptr();
-  a.ld_x = (int)x.stride(0);
-  a.w = w.data_ptr<float>();
-  a.rows = (int)x.size(0);
-  a.D = (int)x.size(1);
+  for (size_t t = 0; t < xs.size(); ++t) {
+    check_norm_input(xs[t], ws[t]);
+    TORCH_CHECK(xs[t].sizes() == xs[0].sizes(), "normalised tensors must share one geometry");
+    a.x[t] = (const __nv_bfloat16*)xs[t].data_ptr();
+    a.ld_x[t] = (int)xs[t].stride(0);
+    a.w[t] = ws[t].data_ptr<float>();
+  }
+  a.rows = (int)xs[0].size(0);
+  a.D = (int)xs[0].size(1);
   a.inv_total = 1.f / (float)total_dim;
   a.eps = (float)eps;
-  a.peer_recv = reinterpret_cast<float* const*>(peer_recv.data_ptr());
+  a.status = comm_status();
+  return a;
+}
+
+// The peer exchange (TP > 1): slabs of both parities, flag areas, the device epoch counter.
+void set_exchange(TpNormArgs& a, int ntens, const c10::optional<at::Tensor>& peer_recv, int64_t my_recv,
+                  const c10::optional<at::Tensor>& peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
+                  int64_t max_rows, int64_t epoch, int64_t epoch_ctr, int64_t epoch_done,
+                  const c10::optional<at::Tensor>& peer_recv_odd, int64_t my_recv_odd) {
+  if (!peer_recv) return;
+  TORCH_CHECK(peer_flags && my_recv && my_flags, "the row-statistic exchange needs slabs and flags");
+  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && (int64_t)ntens * a.rows <= max_rows, "rows exceed the exchange slab");
+  TORCH_CHECK(peer_recv->is_cuda() && peer_recv->numel() == tp && peer_flags->numel() == tp,
+              "peer arrays: cuda int64 [tp]");
+  a.exchange = true;
+  a.peer_recv = reinterpret_cast<float* const*>(peer_recv->data_ptr());
   a.my_recv = reinterpret_cast<float*>(my_recv);
-  a.peer_flags = reinterpret_cast<long long* const*>(peer_flags.data_ptr());
+  a.peer_flags = reinterpret_cast<long long* const*>(peer_flags->data_ptr());
   a.my_flags = reinterpret_cast<long long*>(my_flags);
   a.rank = (int)rank;
   a.tp = (int)tp;
   a.max_rows = (int)max_rows;
   a.epoch = epoch;
-  a.status = comm_status();
   if (epoch_ctr) {
     TORCH_CHECK(epoch_done && my_recv_odd && peer_recv_odd && peer_recv_odd->numel() == tp,
                 "tp_rms: device epochs need the done counter and the odd-parity slabs");
@@ -484,9 +578,80 @@ TpNormArgs tp_norm_args(const at::Tensor& x, const at::Tensor& w, at::Tensor pee
     a.peer_recv_odd = reinterpret_cast<float* const*>(peer_recv_odd->data_ptr());
     a.my_recv_odd = reinterpret_cast<float*>(my_recv_odd);
   }
-  return a;
 }
+
+void set_rope(TpNormArgs& a, const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t,
+              int64_t head_dim) {
+  if (!cos_t) return;
+  TORCH_CHECK(sin_t && head_dim % 8 == 0 && head_dim > 0 && a.D % head_dim == 0,
+              "rope: head_dim a multiple of 8 dividing D");
+  TORCH_CHECK(cos_t->scalar_type() == at::kFloat && cos_t->is_contiguous() && sin_t->scalar_type() == at::kFloat &&
+                  sin_t->is_contiguous() && cos_t->dim() == 2 && cos_t->size(0) == a.rows &&
+                  cos_t->size(1) == head_dim / 2 && sin_t->sizes() == cos_t->sizes(),
+              "rope: cos / sin fp32 [rows, head_dim / 2]");
+  a.cos = cos_t->data_ptr<float>();
+  a.sin = sin_t->data_ptr<float>();
+  a.hd = (int)head_dim;
+}
+
 int tp_norm_grid(int rows) { return std::max(1, std::min((rows + STAT_ROWS - 1) / STAT_ROWS, sm_count())); }
+
+// Forward of one or two tensors: returns (y per tensor, rstd [ntens, rows]).
+std::vector<at::Tensor> norm_fwd(TpNormArgs& a, int ntens, const at::TensorOptions& opts) {
+  auto rstd = at::empty({ntens, a.rows}, opts.dtype(at::kFloat));
+  std::vector<at::Tensor> out;
+  for (int t = 0; t < ntens; ++t) {
+    out.push_back(at::empty({a.rows, a.D}, opts));
+    a.y[t] = (__nv_bfloat16*)out.back().data_ptr();
+    a.rstd[t] = rstd.data_ptr<float>() + (size_t)t * a.rows;
+  }
+  if (a.rows) {
+    const dim3 grid(tp_norm_grid(a.rows), ntens);
+    if (a.D <= 1024)
+      tp_norm_kernel<false, 4><<<grid, 256, 0, stream()>>>(a);
+    else
+      tp_norm_kernel<false, 8><<<grid, 256, 0, stream()>>>(a);
+    CQB_LAUNCH_CHECK();
+    count_launch();
+  }
+  out.push_back(rstd);
+  return out;
+}
+
+// Backward: returns (dx per tensor, dw fp32 [D] per tensor).
+std::vector<at::Tensor> norm_bwd(TpNormArgs& a, int ntens, const std::vector<at::Tensor>& dys, const at::Tensor& rstd,
+                                 const at::TensorOptions& opts) {
+  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.is_contiguous() && rstd.numel() == (int64_t)ntens * a.rows,
+              "rstd: fp32 [ntens, rows]");
+  std::vector<at::Tensor> dx, dw, keep;
+  const int grid = tp_norm_grid(a.rows);
+  for (int t = 0; t < ntens; ++t) {
+    auto dyc = dys[t].contiguous();
+    TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.numel() == (int64_t)a.rows * a.D, "dy like x");
+    keep.push_back(dyc);
+    dx.push_back(at::empty({a.rows, a.D}, opts));
+    dw.push_back(at::zeros({a.D}, opts.dtype(at::kFloat)));
+    a.dy[t] = (const __nv_bfloat16*)dyc.data_ptr();
+    a.y[t] = (__nv_bfloat16*)dx.back().data_ptr();
+    a.rstd[t] = const_cast<float*>(rstd.data_ptr<float>()) + (size_t)t * a.rows;
+  }
+  if (a.rows) {
+    auto partial = at::empty({ntens, grid, a.D}, opts.dtype(at::kFloat));
+    for (int t = 0; t < ntens; ++t) a.dw_partial[t] = partial.data_ptr<float>() + (size_t)t * grid * a.D;
+    if (a.D <= 1024)
+      tp_norm_kernel<true, 4><<<dim3(grid, ntens), 256, 0, stream()>>>(a);
+    else
+      tp_norm_kernel<true, 8><<<dim3(grid, ntens), 256, 0, stream()>>>(a);
+    CQB_LAUNCH_CHECK();
+    for (int t = 0; t < ntens; ++t) {
+      column_sum_kernel<<<(a.D + 255) / 256, 256, 0, stream()>>>(a.dw_partial[t], grid, a.D, dw[t].data_ptr<float>());
+      CQB_LAUNCH_CHECK();
+    }
+    count_launch(1 + ntens);
+  }
+  for (auto& t : dw) dx.push_back(t);
+  return dx;
+}
 }  // namespace
 
 // y = x * rsqrt(sum_over_ranks(x^2) / total_dim + eps) * w; returns (y, rstd).
@@ -494,18 +659,11 @@ std::vector<at::Tensor> tp_rms_fwd(at::Tensor x, at::Tensor w, at::Tensor peer_r
                                    at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp, int64_t max_rows,
                                    int64_t epoch, int64_t total_dim, double eps, int64_t epoch_ctr,
                                    int64_t epoch_done, c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
-  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, eps,
-                        epoch_ctr, epoch_done, peer_recv_odd, my_recv_odd);
-  auto y = at::empty({x.size(0), x.size(1)}, x.options());
-  auto rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
-  a.y = (__nv_bfloat16*)y.data_ptr();
-  a.rstd = rstd.data_ptr<float>();
-  if (a.rows) {
-    tp_norm_kernel<false><<<tp_norm_grid(a.rows), 256, 0, stream()>>>(a);
-    CQB_LAUNCH_CHECK();
-    count_launch();
-  }
-  return {y, rstd};
+  auto a = norm_args({x}, {w}, total_dim, eps);
+  set_exchange(a, 1, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, epoch_ctr, epoch_done,
+               peer_recv_odd, my_recv_odd);
+  auto out = norm_fwd(a, 1, x.options());
+  return {out[0], out[1].view({-1})};
 }
 
 // Backward: returns (dx, dw fp32 [D]); the row dot products dy.w.x are summed over ranks.
@@ -513,26 +671,43 @@ std::vector<at::Tensor> tp_rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at
                                    int64_t my_recv, at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
                                    int64_t max_rows, int64_t epoch, int64_t total_dim, int64_t epoch_ctr,
                                    int64_t epoch_done, c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
-  auto a = tp_norm_args(x, w, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, total_dim, 0.0,
-                        epoch_ctr, epoch_done, peer_recv_odd, my_recv_odd);
-  auto dyc = dy.contiguous();
-  TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.sizes() == x.sizes(), "dy like x");
-  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() == x.size(0), "rstd: fp32 [rows]");
-  auto dx = at::empty({x.size(0), x.size(1)}, x.options());
-  auto dw = at::zeros({x.size(1)}, x.options().dtype(at::kFloat));
-  if (!a.rows) return {dx, dw};
-  const int grid = tp_norm_grid(a.rows);
-  auto partial = at::empty({grid, x.size(1)}, dw.options());
-  a.dy = (const __nv_bfloat16*)dyc.data_ptr();
-  a.y = (__nv_bfloat16*)dx.data_ptr();
-  a.rstd = rstd.data_ptr<float>();
-  a.dw_partial = partial.data_ptr<float>();
-  tp_norm_kernel<true><<<grid, 256, 0, stream()>>>(a);
-  CQB_LAUNCH_CHECK();
-  column_sum_kernel<<<(a.D + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), grid, a.D, dw.data_ptr<float>());
-  CQB_LAUNCH_CHECK();
-  count_launch(2);
-  return {dx, dw};
+  auto a = norm_args({x}, {w}, total_dim, 0.0);
+  set_exchange(a, 1, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, epoch, epoch_ctr, epoch_done,
+               peer_recv_odd, my_recv_odd);
+  TORCH_CHECK(dy.sizes() == x.sizes(), "dy like x");
+  return norm_bwd(a, 1, {dy}, rstd.contiguous(), x.options());
+}
+
+// Wan self-attention q / k: full-width RMSNorm of both (the per-row sums exchanged over the TP
+// group when `peer_recv` is given) followed by the complex-pair RoPE (when `cos` is given), one
+// launch. Returns (q_out, k_out, rstd [2, rows]).
+std::vector<at::Tensor> qk_norm_rope_fwd(at::Tensor q, at::Tensor k, at::Tensor wq, at::Tensor wk,
+                                         c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t,
+                                         int64_t head_dim, int64_t total_dim, double eps,
+                                         c10::optional<at::Tensor> peer_recv, int64_t my_recv,
+                                         c10::optional<at::Tensor> peer_flags, int64_t my_flags, int64_t rank,
+                                         int64_t tp, int64_t max_rows, int64_t epoch_ctr, int64_t epoch_done,
+                                         c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
+  auto a = norm_args({q, k}, {wq, wk}, total_dim, eps);
+  set_rope(a, cos_t, sin_t, head_dim);
+  set_exchange(a, 2, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, 0, epoch_ctr, epoch_done,
+               peer_recv_odd, my_recv_odd);
+  return norm_fwd(a, 2, q.options());
+}
+
+// Backward of qk_norm_rope_fwd: (dq, dk, dwq, dwk) from the gradients of its two outputs.
+std::vector<at::Tensor> qk_norm_rope_bwd(at::Tensor dyq, at::Tensor dyk, at::Tensor q, at::Tensor k, at::Tensor wq,
+                                         at::Tensor wk, at::Tensor rstd, c10::optional<at::Tensor> cos_t,
+                                         c10::optional<at::Tensor> sin_t, int64_t head_dim, int64_t total_dim,
+                                         c10::optional<at::Tensor> peer_recv, int64_t my_recv,
+                                         c10::optional<at::Tensor> peer_flags, int64_t my_flags, int64_t rank,
+                                         int64_t tp, int64_t max_rows, int64_t epoch_ctr, int64_t epoch_done,
+                                         c10::optional<at::Tensor> peer_recv_odd, int64_t my_recv_odd) {
+  auto a = norm_args({q, k}, {wq, wk}, total_dim, 0.0);
+  set_rope(a, cos_t, sin_t, head_dim);
+  set_exchange(a, 2, peer_recv, my_recv, peer_flags, my_flags, rank, tp, max_rows, 0, epoch_ctr, epoch_done,
+               peer_recv_odd, my_recv_odd);
+  return norm_bwd(a, 2, {dyq, dyk}, rstd.contiguous(), q.options());
 }
 
 int comm_status_read(bool reset) {

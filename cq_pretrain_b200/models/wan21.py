@@ -91,6 +91,24 @@ class Attention(nn.Module):
         self.norm_q = WanRMSNorm(dim, cfg.norm_eps)
         self.norm_k = WanRMSNorm(dim, cfg.norm_eps)
 
+    def _fused_qk(self, q, k, layout):
+        """Self-attention q / k through one kernel each way: the full-width RMSNorm of both (per-row
+        sums exchanged over NVLink in-kernel at TP > 1) and the complex-pair RoPE. None where the
+        kernel does not apply (CPU, or TP > 1 without the peer workspace)."""
+        if not N.qk_norm_rope_supported(q, k):
+            return None
+        exchange = None
+        if ps.tp_size() > 1:
+            from ..parallel import symmetric
+            ws = symmetric.workspace()
+            if ws is None or not ws.supports_qk(q, k):
+                return None
+            exchange = ws.exchange_kwargs
+        total = q.shape[-1] * ps.tp_size()
+        qo, ko = N.qk_norm_rope(q, k, self.norm_q.weight, self.norm_k.weight, layout.cos_rows, layout.sin_rows,
+                                self.head_dim, total, self.norm_q.eps, exchange)
+        return qo.view(-1, self.heads, self.head_dim), ko.view(-1, self.heads, self.head_dim)
+
     def project_kv(self, context_full):
         k, v = self.kv(context_full, gathered=True).chunk(2, -1)
         k = self.norm_k(k).reshape(-1, self.heads, self.head_dim)
@@ -101,8 +119,13 @@ class Attention(nn.Module):
         if context is None and cached_kv is None:
             q, kv = PL.column_pair(x, self.q, self.kv)
             k, v = kv.chunk(2, -1)
-            k = self.norm_k(k).reshape(-1, self.heads, self.head_dim)
             v = v.reshape(-1, self.heads, self.head_dim)
+            fused = self._fused_qk(q, k, layout)
+            if fused is not None:
+                q, k = fused
+                y = ATT.varlen_attention(q, k, v, layout.row_ends, layout.row_ends, ranges=layout.self_ranges)
+                return self.o(y.flatten(1))
+            k = self.norm_k(k).reshape(-1, self.heads, self.head_dim)
         else:
             q = self.q(x)
             k, v = cached_kv if cached_kv is not None else self.project_kv(context)

@@ -170,3 +170,48 @@ def gated_add(x, branch, gate, index=None):
     if index is not None:
         gate = gate.index_select(0, index)
     return R.gated_add(x, branch, gate)
+
+
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, wq, wk, cos, sin, head_dim, total_dim, eps, exchange):
+        wqf, wkf = wq.float().contiguous(), wk.float().contiguous()
+        yq, yk, rstd = _ext.ops().qk_norm_rope_fwd(q, k, wqf, wkf, cos=cos, sin=sin, head_dim=head_dim,
+                                                   total_dim=total_dim, eps=eps, **(exchange() if exchange else {}))
+        ctx.save_for_backward(q, k, wqf, wkf, rstd, cos, sin)
+        ctx.meta = (head_dim, total_dim, exchange, wq.dtype)
+        return yq, yk
+
+    @staticmethod
+    def backward(ctx, dyq, dyk):
+        q, k, wqf, wkf, rstd, cos, sin = ctx.saved_tensors
+        head_dim, total_dim, exchange, wdtype = ctx.meta
+        zeros = lambda: torch.zeros(q.shape, dtype=torch.bfloat16, device=q.device)
+        dyq = zeros() if dyq is None else dyq.to(torch.bfloat16)
+        dyk = zeros() if dyk is None else dyk.to(torch.bfloat16)
+        dq, dk, dwq, dwk = _ext.ops().qk_norm_rope_bwd(dyq, dyk, q, k, wqf, wkf, rstd, cos=cos, sin=sin,
+                                                       head_dim=head_dim, total_dim=total_dim,
+                                                       **(exchange() if exchange else {}))
+        return dq, dk, dwq.to(wdtype), dwk.to(wdtype), None, None, None, None, None, None
+
+
+def qk_norm_rope_supported(q, k):
+    return (q.is_cuda and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and q.dim() == 2
+            and q.shape == k.shape and q.shape[1] % 8 == 0 and q.shape[1] <= 2048
+            and all(t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0 for t in (q, k))
+            and _ext.has("qk_norm_rope_fwd"))
+
+
+def qk_norm_rope(q, k, wq, wk, cos, sin, head_dim, total_dim, eps, exchange=None):
+    """Wan self-attention q / k: ``rope(rms_norm(q) * wq)`` and the same for k in one kernel each way.
+
+    ``q``, ``k`` ``[rows, D]`` bf16 (row-strided views allowed) hold this rank's heads of a
+    ``total_dim``-wide vector; the norm's per-row sums run over the full width, so at TP > 1
+    ``exchange()`` returns the peer-exchange arguments of one call (``SymmetricWorkspace.
+    exchange_kwargs``) and the sums cross NVLink inside the kernel. ``cos`` / ``sin`` fp32 ``[rows,
+    head_dim / 2]`` (the complex-pair RoPE angles) or None for the norm alone. Returns contiguous
+    ``[rows, D]`` outputs. Reference: ``norm_q`` / ``norm_k`` and then ``rotary`` on q and k in
+    ``models/generator_wan21.py:109-113``, three separate operations there."""
+    if cos is not None:
+        cos, sin = cos.float().contiguous(), sin.float().contiguous()
+    return _QKNormRope.apply(q, k, wq, wk, cos, sin, head_dim, total_dim, eps, exchange)

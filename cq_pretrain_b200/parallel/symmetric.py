@@ -22,7 +22,8 @@ Protocol (epochs count calls of each kind; every rank issues the same sequence):
   into the owner's ``recv[e % 2][src]`` and stamped with e in the owner's (tile, src, warp) slot;
   this rank's own tiles come last, wait for the peers' stamps of the same tile, and add the
   peers' bf16 partials to their fp32 accumulator (and the bias) before storing the result.
-* row statistics (epoch e, Wan's full-width Q/K RMSNorm, and the vocabulary-parallel cross-entropy's
+* row statistics (epoch e, Wan's full-width Q/K RMSNorm (q and k in one call, with the RoPE of the
+  self-attention fused), and the vocabulary-parallel cross-entropy's
   (max, sum exp, target logit) triples): one kernel per call; each 64-row block
   stores its partial sums into ``stat[e % 2][rank]`` of every peer, publishes a per-block flag and
   acquires the peers' flags of the same block before normalising its rows.
@@ -189,14 +190,24 @@ class SymmetricWorkspace:
     def supports_rms(self, x):
         return (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
                 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and x.shape[1] % 8 == 0
-                and x.shape[1] <= 1024 and x.shape[0] <= self.stat_rows)
+                and x.shape[1] <= 2048 and x.shape[0] <= self.stat_rows)
 
-    def _stat_kwargs(self):
+    def supports_qk(self, q, k):
+        """Eligibility of the fused q / k norm (+ RoPE): both tensors in one exchange."""
+        return (self.supports_rms(q) and self.supports_rms(k) and q.shape == k.shape
+                and 2 * q.shape[0] <= self.stat_rows and _ext.has("qk_norm_rope_fwd"))
+
+    def exchange_kwargs(self):
+        """Keyword arguments of one row-statistic exchange call (the statistics kind's slabs,
+        flags and device epoch counter); every rank must make the same sequence of such calls."""
         self.epoch_stat += 1
         return dict(peer_recv=self.stat[0], my_recv=self.base + self.off_stat[0], peer_flags=self.stat_flags,
                     my_flags=self.base + self.off_stat_flags, rank=self.rank, tp=self.tp, max_rows=self.stat_rows,
-                    epoch=0, epoch_ctr=self._ctr[2], epoch_done=self._done[2], peer_recv_odd=self.stat[1],
+                    epoch_ctr=self._ctr[2], epoch_done=self._done[2], peer_recv_odd=self.stat[1],
                     my_recv_odd=self.base + self.off_stat[1])
+
+    def _stat_kwargs(self):
+        return dict(self.exchange_kwargs(), epoch=0)
 
     def rms_forward(self, x, weight, total_dim, eps):
         return _ext.ops().tp_rms_fwd(x, weight, total_dim=total_dim, eps=eps, **self._stat_kwargs())

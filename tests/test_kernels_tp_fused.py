@@ -128,6 +128,7 @@ def _worker(rank, world, port, out):
     for a, b in zip(*results):
         errors.append(float((a - b).norm() / b.norm().clamp_min(1e-6)))
     errors += _graph_replays(ws, world)
+    errors += _qk_exchange(ws, world)
     torch.cuda.synchronize()
     status = symmetric.status()
     symmetric.disable()
@@ -178,6 +179,32 @@ def _graph_replays(ws, world):
     return errors
 
 
+def _qk_exchange(ws, world):
+    """Fused q / k norm + RoPE with the in-kernel row-sum exchange vs the NCCL-summed fp32 formula."""
+    from cq_pretrain_b200.ops import norms as N
+    from torch.distributed.nn.functional import all_reduce as ar_autograd
+    dev, rows, width, hd = torch.device("cuda"), 1100, 384, 64
+    gen = torch.Generator(device="cuda").manual_seed(5)   # same angles on every rank
+    ang = torch.rand(rows, hd // 2, device=dev, generator=gen) * 6.28
+    cos, sin = ang.cos(), ang.sin()
+    q = torch.randn(rows, width, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(rows, width, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    wq = (1 + 0.1 * torch.randn(width, device=dev)).requires_grad_()
+    wk = (1 + 0.1 * torch.randn(width, device=dev)).requires_grad_()
+    assert ws.supports_qk(q, k)
+    yq, yk = N.qk_norm_rope(q, k, wq, wk, cos, sin, hd, width * world, 1e-6, ws.exchange_kwargs)
+    gq, gk = torch.randn_like(yq), torch.randn_like(yk)
+    torch.autograd.backward([yq, yk], [gq, gk])
+    leaves = [t.detach().float().requires_grad_() for t in (q, k, wq, wk)]
+    rq, rk = _qk_reference(*leaves, cos, sin, width // hd, hd, width * world, 1e-6, sum_rows=ar_autograd)
+    torch.autograd.backward([rq, rk], [gq.float(), gk.float()])
+    errors = []
+    for got, ref in ((yq, rq), (yk, rk), (q.grad, leaves[0].grad), (k.grad, leaves[1].grad), (wq.grad, leaves[2].grad),
+                     (wk.grad, leaves[3].grad)):
+        errors.append(float((got.float() - ref.detach()).norm() / ref.detach().norm()))
+    return errors
+
+
 def _all_gather(x):
     """Differentiable row all-gather (NCCL) for the reference path."""
     from torch.distributed.nn.functional import all_gather
@@ -200,12 +227,12 @@ def test_device_epochs_advance_in_graph_replays():
     done = torch.zeros(1, dtype=torch.int32, device=dev)
     x = torch.randn(700, 256, device=dev, dtype=torch.bfloat16)
     w = torch.rand(256, device=dev) + 0.5
+    kw = dict(peer_recv=ptr(slabs[0]), my_recv=slabs[0].data_ptr(), peer_flags=ptr(flags), my_flags=flags.data_ptr(),
+              rank=0, tp=1, max_rows=max_rows, epoch=0, epoch_ctr=ctr.data_ptr(), epoch_done=done.data_ptr(),
+              peer_recv_odd=ptr(slabs[1]), my_recv_odd=slabs[1].data_ptr())   # built before any capture
 
     def call():
-        return ops.tp_rms_fwd(x, w, peer_recv=ptr(slabs[0]), my_recv=slabs[0].data_ptr(), peer_flags=ptr(flags),
-                              my_flags=flags.data_ptr(), rank=0, tp=1, max_rows=max_rows, epoch=0, total_dim=256,
-                              eps=1e-6, epoch_ctr=ctr.data_ptr(), epoch_done=done.data_ptr(),
-                              peer_recv_odd=ptr(slabs[1]), my_recv_odd=slabs[1].data_ptr())
+        return ops.tp_rms_fwd(x, w, total_dim=256, eps=1e-6, **kw)
 
     def ref():
         xf = x.float()
@@ -228,6 +255,61 @@ def test_device_epochs_advance_in_graph_replays():
         # this epoch's partial sums went to the slab of its parity, the other one is stale
         assert slabs[(2 + rep) % 2][:700].abs().sum() > 0
     assert int(flags[:8].max()) == 5 and ops.comm_status_read(True) == 0
+    # backward (eager, epoch 6): dx and dw against autograd of the fp32 formula
+    y, rstd = call()
+    dy = torch.randn_like(y)
+    dx, dw = ops.tp_rms_bwd(dy, x, w, rstd, total_dim=256, **kw)
+    xr, wr = x.float().requires_grad_(), w.clone().requires_grad_()
+    (xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + 1e-6) * wr).backward(dy.float())
+    torch.testing.assert_close(dx.float(), xr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(dw, wr.grad, rtol=1e-2, atol=1e-1)
+    torch.cuda.synchronize()
+    assert int(ctr) == 7 and int(done) == 0 and ops.comm_status_read(True) == 0
+
+
+def _qk_reference(q, k, wq, wk, cos, sin, heads, hd, total_dim, eps, sum_rows=None):
+    """fp32 autograd reference: full-width RMSNorm (row sums through ``sum_rows`` at TP > 1) then
+    the complex-pair RoPE, for q and k."""
+    from cq_pretrain_b200.ops import reference as R
+    outs = []
+    for x, w in ((q, wq), (k, wk)):
+        sq = x.square().sum(-1, keepdim=True)
+        if sum_rows is not None:
+            sq = sum_rows(sq)
+        y = x * torch.rsqrt(sq / total_dim + eps) * w
+        outs.append(R.rotary_pairs(y.view(-1, heads, hd), cos, sin).flatten(1))
+    return outs
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("width,hd", [(1536, 128), (768, 128), (256, 64)])
+def test_qk_norm_rope_single_rank(width, hd):
+    """The fused q / k RMSNorm + RoPE kernel (no exchange) against the fp32 formula, forward and
+    backward, with k a row-strided view of a wider projection (the kv output's first half)."""
+    from cq_pretrain_b200.ops import norms as N
+    torch.manual_seed(0)
+    rows, dev = 1000, torch.device("cuda")
+    q = torch.randn(rows, width, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    kv = torch.randn(rows, 2 * width, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    k = kv[:, :width]
+    wq = (1 + 0.1 * torch.randn(width, device=dev)).requires_grad_()
+    wk = (1 + 0.1 * torch.randn(width, device=dev)).requires_grad_()
+    ang = torch.rand(rows, hd // 2, device=dev) * 6.28
+    cos, sin = ang.cos(), ang.sin()
+    assert N.qk_norm_rope_supported(q, k)
+    yq, yk = N.qk_norm_rope(q, k, wq, wk, cos, sin, hd, width, 1e-6)
+    gq, gk = torch.randn_like(yq), torch.randn_like(yk)
+    torch.autograd.backward([yq, yk], [gq, gk])
+    leaves = [t.detach().float().requires_grad_() for t in (q, kv, wq, wk)]
+    rq, rk = _qk_reference(leaves[0], leaves[1][:, :width], leaves[2], leaves[3], cos, sin, width // hd, hd, width,
+                           1e-6)
+    torch.autograd.backward([rq, rk], [gq.float(), gk.float()])
+    for got, ref in ((yq, rq), (yk, rk), (q.grad, leaves[0].grad), (kv.grad, leaves[1].grad)):
+        err = float((got.float() - ref.detach()).norm() / ref.detach().norm())
+        assert err < 1e-2, err
+    for got, ref in ((wq.grad, leaves[2].grad), (wk.grad, leaves[3].grad)):
+        torch.testing.assert_close(got, ref, rtol=1e-2, atol=1e-1)
+    assert float(kv.grad[:, width:].abs().max()) == 0.0
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
