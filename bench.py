@@ -208,6 +208,7 @@ def main():
                          "source": "reference 1.946 s joint 8K step on 16x 910B TP2xDP8, global batch 8"},
         }
         print(json.dumps(line), flush=True)
+    trainer.close()
     if world > 1:
         dist.barrier()
         ps.destroy()

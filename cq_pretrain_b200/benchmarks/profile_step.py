@@ -56,6 +56,7 @@ def main():
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
         trainer.train_step([(host, receipt)], phases=timer)
         torch.cuda.synchronize()
+    trainer.close()
     if st is not None and st.rank != 0:
         ps.destroy()
         return

@@ -74,6 +74,7 @@ def main():
             text_targets=int(host.text_indices.numel()), peak_gib=round(peak, 1),
             checkpoint_dit_layers=args.checkpoint_dit, recompute_backbone=args.recompute,
             steps=args.steps, warmup=args.warmup, data="synthetic (random-init weights)")), flush=True)
+    trainer.close()
     if world > 1:
         ps.destroy()
 

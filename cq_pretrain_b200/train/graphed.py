@@ -105,6 +105,14 @@ class RendererGraphs:
         self.pool = None
         self.replays = 0
 
+    def release(self):
+        """Drop every captured graph and its memory pool. Graphs that captured NCCL calls must be
+        released before the process group is destroyed, or the teardown waits on them."""
+        self.entries.clear()
+        self.pool = None
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+
     def _key(self, leaf, bound):
         tensors = []
         spec = _flatten(bound, tensors)

@@ -71,6 +71,11 @@ class Trainer:
             from ..parallel import symmetric
             symmetric.enable()
 
+    def close(self):
+        """Release the captured renderer graphs (call before ``parallel.state.destroy``)."""
+        if self.renderer_graphs is not None:
+            self.renderer_graphs.release()
+
     def _micro(self, batch, scales, backward_scale, timer=None):
         deferred = batch.generation is not None and (bool(batch.generation.microbatches)
                                                      or self.renderer_graphs is not None)
