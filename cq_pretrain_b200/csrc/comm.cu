@@ -81,7 +81,7 @@ __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, const _
 // is persistent (<= one CTA per SM per tensor) and every rank walks the blocks in the same order.
 //
 // One launch normalises up to two tensors of the same geometry (Wan's q and k: blockIdx.y picks
-// the tensor; tensor t uses rows [t * rows, (t + 1) * rows) of the slabs and flag blocks
+// the tensor; tensor t uses slab rows [t * 64 * blocks, (t + 1) * 64 * blocks) and flag blocks
 // [t * blocks, (t + 1) * blocks)). With `cos` set, the Wan complex-pair RoPE of head size `hd` is
 // applied to the normalised row in the forward, and the backward first rotates dy back (the
 // rotation by -angle) before the norm backward. Without `exchange` the partials are this rank's
@@ -163,7 +163,9 @@ __global__ void __launch_bounds__(256) tp_norm_kernel(TpNormArgs a) {
   const bool odd = (epoch & 1) && a.peer_recv_odd;
   float* const* peer_recv = odd ? a.peer_recv_odd : a.peer_recv;
   const float* my_recv = odd ? a.my_recv_odd : a.my_recv;
-  const size_t slab_row0 = (size_t)t * a.rows;   // this tensor's rows in the slabs
+  // this tensor's rows in the slabs, padded to whole blocks: the last block of tensor 0 stores
+  // partials for all 64 of its rows, which must not land on tensor 1's first rows
+  const size_t slab_row0 = (size_t)t * blocks * STAT_ROWS;
   for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
     // 1) local partials: warp w handles rows 8w..8w+7 of the block; the row loop is innermost and
     // unrolled so a lane has the loads of all eight rows in flight (the pass is latency-bound
@@ -493,7 +495,7 @@ __global__ void __launch_bounds__(256) ce_combine_tp_kernel(const float2* __rest
 
 // part: [rows, tiles] float2 from the LM-head GEMM (epilogue 3); tgt_local [rows]; returns the
 // full-vocabulary (lse, target logit) per row. The exchange uses three floats per row of the
-// statistics slab, so 3 * rows <= max_rows.
+// statistics slab for every row of its whole 64-row blocks, so 3 * rows rounded up to 64 <= max_rows.
 std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at::Tensor peer_recv, int64_t my_recv,
                                       at::Tensor peer_flags, int64_t my_flags, int64_t rank, int64_t tp,
                                       int64_t max_rows, int64_t epoch, int64_t epoch_ctr, int64_t epoch_done,
@@ -504,7 +506,8 @@ std::vector<at::Tensor> ce_combine_tp(at::Tensor part, at::Tensor tgt_local, at:
   const int64_t rows = part.size(0);
   TORCH_CHECK(tgt_local.scalar_type() == at::kFloat && tgt_local.numel() == rows && tgt_local.is_contiguous(),
               "tgt_local: fp32 [rows]");
-  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && 3 * rows <= max_rows, "rows exceed the exchange slab");
+  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && 3 * ((rows + STAT_ROWS - 1) / STAT_ROWS * STAT_ROWS) <= max_rows,
+              "rows exceed the exchange slab (whole 64-row blocks)");
   auto lse = at::empty({rows}, part.options()), tgt = at::empty({rows}, part.options());
   if (!rows) return {lse, tgt};
   TORCH_CHECK(!epoch_ctr || (epoch_done && my_recv_odd && peer_recv_odd && peer_recv_odd->numel() == tp),
@@ -558,7 +561,8 @@ void set_exchange(TpNormArgs& a, int ntens, const c10::optional<at::Tensor>& pee
                   const c10::optional<at::Tensor>& peer_recv_odd, int64_t my_recv_odd) {
   if (!peer_recv) return;
   TORCH_CHECK(peer_flags && my_recv && my_flags, "the row-statistic exchange needs slabs and flags");
-  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && (int64_t)ntens * a.rows <= max_rows, "rows exceed the exchange slab");
+  const int64_t padded = (int64_t)(a.rows + STAT_ROWS - 1) / STAT_ROWS * STAT_ROWS;
+  TORCH_CHECK(tp >= 1 && tp <= STAT_MAX_TP && ntens * padded <= max_rows, "rows exceed the exchange slab");
   TORCH_CHECK(peer_recv->is_cuda() && peer_recv->numel() == tp && peer_flags->numel() == tp,
               "peer arrays: cuda int64 [tp]");
   a.exchange = true;

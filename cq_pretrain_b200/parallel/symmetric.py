@@ -190,12 +190,12 @@ class SymmetricWorkspace:
     def supports_rms(self, x):
         return (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
                 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and x.shape[1] % 8 == 0
-                and x.shape[1] <= 2048 and x.shape[0] <= self.stat_rows)
+                and x.shape[1] <= 2048 and -(-x.shape[0] // 64) * 64 <= self.stat_rows)
 
     def supports_qk(self, q, k):
         """Eligibility of the fused q / k norm (+ RoPE): both tensors in one exchange."""
         return (self.supports_rms(q) and self.supports_rms(k) and q.shape == k.shape
-                and 2 * q.shape[0] <= self.stat_rows and _ext.has("qk_norm_rope_fwd"))
+                and 2 * (-(-q.shape[0] // 64) * 64) <= self.stat_rows and _ext.has("qk_norm_rope_fwd"))
 
     def exchange_kwargs(self):
         """Keyword arguments of one row-statistic exchange call (the statistics kind's slabs,
@@ -216,7 +216,7 @@ class SymmetricWorkspace:
         return _ext.ops().tp_rms_bwd(dy, x, weight, rstd, total_dim=total_dim, **self._stat_kwargs())
 
     def supports_ce(self, rows):
-        return 3 * rows <= self.stat_rows and _ext.has("ce_combine_tp")
+        return 3 * (-(-rows // 64) * 64) <= self.stat_rows and _ext.has("ce_combine_tp")
 
     def ce_combine(self, part, tgt_local):
         """Full-vocabulary (lse, target logit) per row from this rank's LM-head partials: the

@@ -120,6 +120,10 @@ class RendererGraphs:
 
     def run(self, model, leaf, bound, factor):
         from ..parallel import state as ps, symmetric
+        if self.optimizer is not None and hasattr(self.optimizer, "wait_params"):
+            # pending DP parameter all-gathers: the stream waits for them here, outside any capture
+            # (their forward pre-hooks would otherwise wait on uncaptured work inside it)
+            self.optimizer.wait_params()
         if ps.tp_size() > 1 and os.environ.get("CQB_GRAPHS_TP_NCCL") == "1":
             with symmetric.suspended():
                 return self._run(model, leaf, bound, factor)

@@ -312,6 +312,40 @@ def test_qk_norm_rope_single_rank(width, hd):
     assert float(kv.grad[:, width:].abs().max()) == 0.0
 
 
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_qk_exchange_slabs_of_partial_blocks():
+    """q and k exchanged in one call with a row count that is not a multiple of the 64-row block:
+    tensor 0's last (partial) block must not store over tensor 1's first rows in the slab. One
+    rank (tp = 1, this GPU's own slabs as the peer arrays) gives the same bits as no exchange."""
+    from cq_pretrain_b200.ops import _ext
+    ops = _ext.ops()
+    dev = torch.device("cuda")
+    max_rows = 4096
+    flags = torch.zeros(-(-max_rows // 64) * 8, dtype=torch.int64, device=dev)
+    slabs = [torch.zeros(max_rows, dtype=torch.float32, device=dev) for _ in range(2)]
+    ptr = lambda t: torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev)
+    ctr = torch.zeros(1, dtype=torch.int64, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    kw = dict(peer_recv=ptr(slabs[0]), my_recv=slabs[0].data_ptr(), peer_flags=ptr(flags), my_flags=flags.data_ptr(),
+              rank=0, tp=1, max_rows=max_rows, epoch_ctr=ctr.data_ptr(), epoch_done=done.data_ptr(),
+              peer_recv_odd=ptr(slabs[1]), my_recv_odd=slabs[1].data_ptr())
+    torch.manual_seed(3)
+    rows, width = 1100, 512
+    q = torch.randn(rows, width, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(rows, width, device=dev, dtype=torch.bfloat16) * 3
+    wq, wk = torch.rand(width, device=dev) + 0.5, torch.rand(width, device=dev) + 0.5
+    want = ops.qk_norm_rope_fwd(q, k, wq, wk, total_dim=width, eps=1e-6)
+    dyq, dyk = torch.randn_like(q), torch.randn_like(k)
+    want_b = ops.qk_norm_rope_bwd(dyq, dyk, q, k, wq, wk, want[2], total_dim=width)
+    for _ in range(6):
+        got = ops.qk_norm_rope_fwd(q, k, wq, wk, total_dim=width, eps=1e-6, **kw)
+        got_b = ops.qk_norm_rope_bwd(dyq, dyk, q, k, wq, wk, got[2], total_dim=width, **kw)
+        for a, b in zip(got + got_b, want + want_b):
+            assert torch.equal(a, b)
+    torch.cuda.synchronize()
+    assert int(ctr) == 12 and ops.comm_status_read(True) == 0
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.timeout(300)
 def test_fused_tp_collectives_match_nccl():
