@@ -681,8 +681,11 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
   const long long a_block = (long long)BM * args.K * 2;
   args.group_m = (int)std::max(1LL, std::min<long long>(tiles_m, (48LL << 20) / std::max(1LL, a_block)));
   // All-gather: tiles follow the ranks' row ranges (own rows first), so the first tiles need no
-  // peer data and the copy of the other ranks' rows overlaps them.
-  if (GATHER) args.group_m = std::min(args.group_m, std::max(1, args.rows_per_rank / BM));
+  // peer data and the copy of the other ranks' rows overlaps them. One row block per group (all
+  // column tiles of a row block before the next block): a wave of tiles then needs only the next
+  // ~148 / tiles_n row blocks, in the order the copy warps publish them, instead of every block of
+  // a 32-block group; the row block's 12-24 column tiles share it in L2 and B stays resident.
+  if (GATHER) args.group_m = 1;
   // GEMM -> reduce-scatter: groups must not straddle two owners, so that this rank's own row
   // blocks (rotated to the end of the order) form the last groups.
   if (EPI == 5) {
