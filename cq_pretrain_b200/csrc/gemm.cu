@@ -25,9 +25,10 @@
 //    D = A B^T + A2 B2^T runs as one accumulation (e.g. dX = dY1 W1 + dY2 W2 of two projections
 //    of one gathered input); rows of A2 past its own extent read as zero;
 //  * GATHER: two extra warps pull the A row blocks of every TP rank (peer memory, plain loads)
-//    into this GPU's gather buffer and publish a flag per 128-row block; the TMA producer waits
-//    for a block's flag before loading it, and tiles of this rank's own rows go first
-//    (all-gather -> GEMM in one kernel; each remote byte crosses NVLink once).
+//    into this GPU's gather buffer and publish a flag per 16-row sub-chunk; the TMA producer waits
+//    for a block's flags before loading it, and tiles of this rank's own rows go first, read by
+//    TMA straight from the caller's shard while the copy warps publish it to the peers and pull
+//    theirs (all-gather -> GEMM in one kernel; each remote byte crosses NVLink once).
 //
 // Waits are bounded (tcgen05.cuh); on expiry the kernel records an error code, stops issuing,
 // waits for its outstanding TMA transactions (bounded), frees TMEM and exits.
@@ -72,10 +73,11 @@ struct GemmArgs {
   const __nv_bfloat16* const* peer_in;
   __nv_bfloat16* a_local;
   const long long* ready;     // this rank's flag area: ready[s] >= epoch when rank s published
-  // GATHER with in-kernel staging: this rank's rows are read from x_local, written to both the
-  // gather buffer and send_mine (the symmetric send buffer the peers read), and once every own
-  // sub-chunk is staged (own_done counts them) epoch is published into slot src_rank of every
-  // peer's flag area (peer_ready[p]).
+  // GATHER with in-kernel staging: the tensor cores read this rank's rows straight from x_local
+  // (map_a2); the copy warps first write them into send_mine (the symmetric send buffer the peers
+  // read) and, once every own sub-chunk is there (own_done counts them), publish the epoch into
+  // slot src_rank of every peer's flag area (peer_ready[p]); then they pull the peers' rows into
+  // the gather buffer (published per sub-chunk) and last copy the own rows into it (output only).
   const __nv_bfloat16* x_local;
   __nv_bfloat16* send_mine;
   long long* const* peer_ready;
@@ -247,6 +249,8 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       if (args.K2 > 0) {
         tc::prefetch_map(&map_a2);
         tc::prefetch_map(&map_b2);
+      } else if (GATHER && args.x_local) {
+        tc::prefetch_map(&map_a2);
       }
       int stage = 0;
       uint32_t phase = 0;
@@ -260,7 +264,10 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       while (ok && work.next(t, kb0, kb1)) {
         int m0, n0;
         tile_coords(t, tiles_m, tiles_n, args.group_m, rotate, m0, n0);
-        if (GATHER && m0 != ready_m0) {
+        // GATHER with staging: this rank's row blocks come from x_local (map_a2), never waited for
+        const int own_row = m0 - args.src_rank * args.rows_per_rank;
+        const bool own_tile = GATHER && args.x_local != nullptr && own_row >= 0 && own_row < args.rows_per_rank;
+        if (GATHER && !own_tile && m0 != ready_m0) {
           // the row block is ready once all of its 16-row sub-chunks are published
           for (int j = 0; j < BM / GATHER_SUB && ok; ++j)
             ok = wait_flag<false>(args.chunk_flags + m0 / GATHER_SUB + j, epoch, status, abort_flag, 5);
@@ -277,14 +284,15 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           uint8_t* sb = sa + A_BYTES;
           tc::mbar_expect_tx(&full[stage], STAGE_BYTES);
           const bool second = kb >= kb_first;
-          const CUtensorMap* ma = second ? &map_a2 : &map_a;
+          const CUtensorMap* ma = (second || own_tile) ? &map_a2 : &map_a;
           const CUtensorMap* mb = second ? &map_b2 : &map_b;
           const int k0 = (second ? kb - kb_first : kb) * BK;
+          const int am0 = own_tile ? own_row : m0;
           if (A_MN) {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sa + j * (BK * 128), ma, &full[stage], m0 + j * 64, k0);
+            for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(sa + j * (BK * 128), ma, &full[stage], am0 + j * 64, k0);
           } else {
-            tc::tma_load_2d(sa, ma, &full[stage], k0, m0);
+            tc::tma_load_2d(sa, ma, &full[stage], k0, am0);
           }
           if (B_MN) {
 #pragma unroll
@@ -539,25 +547,34 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     if (EPI != 2 && EPI != 3 && lane == 0) tc::bulk_wait_all();
     __syncwarp();
   } else if (GATHER) {
-    // Copy warps 6..7 of every CTA pull 16-row sub-chunks of A into the local gather buffer,
-    // in tile order (this rank's rows first), and publish each sub-chunk with the call's epoch.
-    // Spreading sub-chunks over all CTAs keeps ~16 KB of NVLink loads in flight per SM.
+    // Copy warps 6..7 of every CTA move 16-row sub-chunks, handed out round-robin over the CTAs.
+    // Without x_local: every rank's rows (peer_in[s]; this rank's own send buffer included) into
+    // the gather buffer, in tile order (this rank's rows first), each sub-chunk published with the
+    // call's epoch for the TMA producer. With x_local, three phases: (1) this rank's rows into
+    // send_mine, the last of them publishing the shard to the peers; (2) the peers' rows into the
+    // gather buffer, published per sub-chunk (the tensor cores read this rank's rows from x_local
+    // meanwhile); (3) this rank's rows into the gather buffer, which only the caller reads.
     const int ct = threadIdx.x - 192;  // 0..63
     const int subs = args.M / GATHER_SUB;
     const int rot = rotate * (BM / GATHER_SUB);
-    for (int i = blockIdx.x; i < subs; i += gridDim.x) {
-      const int sub = (i + rot) % subs;
+    const bool staged = args.x_local != nullptr;
+    const int own_subs = args.rows_per_rank / GATHER_SUB;
+    const int items = staged ? subs + own_subs : subs;
+    for (int i = blockIdx.x; i < items; i += gridDim.x) {
+      // phase of item i and its sub-chunk (phase 0: the unstaged single pass)
+      const int phase = !staged ? 0 : (i < own_subs ? 1 : (i < subs ? 2 : 3));
+      const int sub = phase == 1 ? rot + i : (phase == 3 ? rot + (i - subs) : (i + rot) % subs);
       const int row0 = sub * GATHER_SUB;
       const int s = row0 / args.rows_per_rank;
       const int lrow = row0 - s * args.rows_per_rank;
-      const bool stage = s == args.src_rank && args.x_local != nullptr;
       bool ok = true;
       if (ct == 0 && s != args.src_rank) ok = wait_flag<true>(args.ready + s, epoch, status, abort_flag, 6);
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (*abort_flag || !ok) break;
-      const uint4* src = reinterpret_cast<const uint4*>((stage ? args.x_local : peer_in[s]) + (size_t)lrow * args.K);
-      uint4* dst = reinterpret_cast<uint4*>(args.a_local + (size_t)row0 * args.K);
-      uint4* dst2 = stage ? reinterpret_cast<uint4*>(send_mine + (size_t)lrow * args.K) : nullptr;
+      const bool from_local = phase == 1 || phase == 3;
+      const uint4* src = reinterpret_cast<const uint4*>((from_local ? args.x_local : peer_in[s]) + (size_t)lrow * args.K);
+      uint4* dst = phase == 1 ? reinterpret_cast<uint4*>(send_mine + (size_t)lrow * args.K)
+                              : reinterpret_cast<uint4*>(args.a_local + (size_t)row0 * args.K);
       const int vecs = GATHER_SUB * args.K / 8;
       // 16 independent 16-byte loads in flight per thread: NVLink latency is hidden by
       // memory-level parallelism rather than by occupancy.
@@ -569,25 +586,21 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         for (int u = 0; u < UNROLL; ++u) r[u] = __ldcg(src + v + 64 * u);
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) dst[v + 64 * u] = r[u];
-        if (stage) {
-#pragma unroll
-          for (int u = 0; u < UNROLL; ++u) dst2[v + 64 * u] = r[u];
-        }
       }
-      for (; v < vecs; v += 64) {
-        const uint4 r = __ldcg(src + v);
-        dst[v] = r;
-        if (stage) dst2[v] = r;
+      for (; v < vecs; v += 64) dst[v] = __ldcg(src + v);
+      if (phase == 3) continue;   // output rows only: the kernel's completion publishes them
+      if (phase == 1) {
+        __threadfence_system();
+      } else {
+        fence_proxy_async_global();
+        __threadfence();
       }
-      fence_proxy_async_global();
-      if (stage) __threadfence_system(); else __threadfence();
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (ct == 0) {
-        st_release_gpu(args.chunk_flags + sub, epoch);
-        if (stage) {
+        if (phase != 1) st_release_gpu(args.chunk_flags + sub, epoch);
+        if (phase == 1) {
           // the last own sub-chunk staged (over all CTAs) publishes this rank's shard to the peers
-          const unsigned own_subs = (unsigned)(args.rows_per_rank / GATHER_SUB);
-          if (atomicAdd(args.own_done, 1u) + 1u == own_subs) {
+          if (atomicAdd(args.own_done, 1u) + 1u == (unsigned)own_subs) {
             atomicExch(args.own_done, 0u);
             __threadfence_system();
             for (int p = 0; p < args.tp; ++p)
@@ -960,10 +973,12 @@ at::Tensor gather_gemm(at::Tensor a_local, at::Tensor w, c10::optional<at::Tenso
     args.peer_in_odd = reinterpret_cast<const __nv_bfloat16* const*>(peer_in_odd->data_ptr());
     args.send_mine_odd = reinterpret_cast<__nv_bfloat16*>(send_mine_odd);
   }
+  CUtensorMap mx;
+  if (args.x_local) mx = make_map(*x_local, BM);   // this rank's rows, read by the tensor cores directly
   if (mn_major)
-    launch<false, true, 0, true>(ma, mb, make_out_map(y), args);
+    launch<false, true, 0, true>(ma, mb, make_out_map(y), args, args.x_local ? &mx : nullptr);
   else
-    launch<false, false, 0, true>(ma, mb, make_out_map(y), args);
+    launch<false, false, 0, true>(ma, mb, make_out_map(y), args, args.x_local ? &mx : nullptr);
   return y;
 }
 
