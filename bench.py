@@ -172,6 +172,7 @@ def main():
     tokens_per_step = args.length * st.dp
     ms_per_step = compute_ms / args.steps
     pack = _composition(host)
+    trainer.close()   # captured graphs (which may hold NCCL work) go before the process group
     del trainer
     torch.cuda.empty_cache()
     gdn = None
@@ -208,7 +209,6 @@ def main():
                          "source": "reference 1.946 s joint 8K step on 16x 910B TP2xDP8, global batch 8"},
         }
         print(json.dumps(line), flush=True)
-    trainer.close()
     if world > 1:
         dist.barrier()
         ps.destroy()
