@@ -20,7 +20,7 @@ replays:
   ``_ext.launches()`` counts executed kernels.
 
 Graphs are used where the captured work is position independent: CUDA, no activation recompute
-inside the DiT, and the Wan renderer. At TP > 1 (opt-in, ``CQB_GRAPHS_TP=1``) the fused TP kernels
+inside the DiT, and the Wan renderer. At TP > 1 (``CQB_GRAPHS_TP=0`` keeps it eager) the fused TP kernels
 are captured with the rest: they read their call epochs from device counters, so every replay
 takes fresh epochs and parity buffers (``parallel.symmetric``). ``CQB_GRAPHS_TP_NCCL=1`` routes the
 captured TP linears through NCCL and the plain GEMM instead (``parallel.symmetric.suspended``; the
@@ -73,7 +73,7 @@ def _rebuild(spec, tensors):
 def graphs_enabled(cfg, device, tp):
     if os.environ.get("CQB_GRAPHS", "1") == "0":
         return False
-    if tp > 1 and os.environ.get("CQB_GRAPHS_TP", "0") != "1":
+    if tp > 1 and os.environ.get("CQB_GRAPHS_TP", "1") == "0":
         return False
     return (torch.device(device).type == "cuda" and cfg.renderer == "wan"
             and not getattr(cfg, "checkpoint_dit", 0) and not getattr(cfg, "checkpoint_dit_layers", 0))
