@@ -159,20 +159,30 @@ def main():
     out.append(dict(op="pair_input_grad_reducescatter (q/gate + kv)", tp=tp, shape=[M, n1, rows2, n2, H],
                     fused_ms=t_fused, nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
                     speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err5))
-    # Wan QKV projection with the cross-rank Q/K RMSNorm: [32760, 1536] x [1536, 3 x 1536] (rows padded
-    # to 128 x tp), q and kv sharing one in-kernel all-gather, then the full-width RMSNorm of q and k
-    # with the per-row sums exchanged in-kernel; baseline: NCCL all-gather + GEMMs + NCCL all-reduce.
-    from ..models.wan21 import Attention
+    # Wan self-attention QKV projection with the cross-rank Q/K RMSNorm and the 3D RoPE: [32760, 1536]
+    # x [1536, 3 x 1536] (rows padded to 128 x tp), q and kv sharing one in-kernel all-gather, then
+    # q and k normalised over the full width (per-row sums exchanged in-kernel) and rotated in one
+    # kernel, as the model runs it; baseline: NCCL all-gather + GEMMs + NCCL all-reduce of the sums +
+    # the normalisation + the RoPE kernel.
+    from types import SimpleNamespace
+
     from ..config import qwen35_2b_wan
+    from ..models.wan21 import Attention
+    from ..ops import rope as ROPE
     wan_rows = -(-32760 // (128 * tp)) * 128 * tp
     attn = Attention(qwen35_2b_wan()).cuda().to(torch.bfloat16)
     xw = torch.randn(wan_rows // tp, 1536, device="cuda", dtype=torch.bfloat16)
+    gen = torch.Generator(device="cuda").manual_seed(3)   # the same angles on every rank
+    ang = torch.rand(wan_rows, attn.head_dim // 2, device="cuda", generator=gen) * 6.28
+    layout = SimpleNamespace(cos_rows=ang.cos(), sin_rows=ang.sin())
 
     def wan_fused():
         from ..parallel import layers as PL
         q, kv = PL.column_pair(xw, attn.q, attn.kv)
         k, v = kv.chunk(2, -1)
-        return attn.norm_q(q), attn.norm_k(k), v
+        fused_qk = attn._fused_qk(q, k, layout)
+        assert fused_qk is not None, "the fused q / k kernel does not take this shape"
+        return fused_qk[0], fused_qk[1], v.reshape(-1, attn.heads, attn.head_dim)
 
     def wan_nccl():
         xg_ = fused.gather_rows_raw(xw)
@@ -182,8 +192,9 @@ def main():
         for t, norm in ((q, attn.norm_q), (k, attn.norm_k)):
             sq = t.float().square().sum(-1, keepdim=True)
             dist.all_reduce(sq, group=st.tp_group)
-            out_.append((t.float() * torch.rsqrt(sq / 1536 + 1e-6)).to(t.dtype) * norm.weight.to(t.dtype))
-        return out_[0], out_[1], v
+            y = (t.float() * torch.rsqrt(sq / 1536 + 1e-6)).to(t.dtype) * norm.weight.to(t.dtype)
+            out_.append(ROPE.rotary_pairs(y.view(-1, attn.heads, attn.head_dim), layout.cos_rows, layout.sin_rows))
+        return out_[0], out_[1], v.reshape(-1, attn.heads, attn.head_dim)
 
     with torch.no_grad():
         wf, wn = wan_fused(), wan_nccl()
@@ -192,7 +203,7 @@ def main():
     flops = 2.0 * wan_rows * 1536 * (3 * 1536 // tp)
     nv_bytes = (tp - 1) * (wan_rows // tp) * 1536 * 2 + 2 * (tp - 1) * wan_rows * 4
     roof = max(flops / (peak * 1e12), nv_bytes / (PEER_GBS * 1e9)) * 1e3
-    out.append(dict(op="wan_qkv_gemm + cross-rank q/k rmsnorm", tp=tp, shape=[wan_rows, 1536, 3 * 1536 // tp],
+    out.append(dict(op="wan_qkv_gemm + cross-rank q/k rmsnorm + rope", tp=tp, shape=[wan_rows, 1536, 3 * 1536 // tp],
                     fused_ms=t_fused, nccl_cublas_ms=t_nccl, roofline_ms=roof, roofline_fraction=roof / t_fused,
                     speedup_vs_nccl=t_nccl / t_fused, max_rel_err=err6))
     # vocabulary-parallel CE statistics: LM-head partials -> in-kernel exchange vs NCCL MAX + SUM

@@ -60,7 +60,7 @@ def _align(n, a=4096):
 
 
 class SymmetricWorkspace:
-    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192, stat_rows=65536,
+    def __init__(self, send_bytes=192 << 20, recv_bytes=384 << 20, max_subchunks=8192, stat_rows=131072,
                  rs_tiles=8192):
         st = ps.state()
         if st.tp < 2:
