@@ -5,9 +5,8 @@ import copy
 import pytest
 import torch
 
-pytestmark = pytest.mark.gpu
 
-
+@pytest.mark.gpu
 def test_graphed_renderer_matches_eager_over_steps():
     from cq_pretrain_b200.config import tiny_config
     from cq_pretrain_b200.data.synthetic import synthetic_batch
@@ -36,3 +35,44 @@ def test_graphed_renderer_matches_eager_over_steps():
     for (name, p), (_, q) in zip(graphed.model.named_parameters(), eager.model.named_parameters()):
         rel = (p.float() - q.float()).norm() / q.float().norm().clamp_min(1e-12)
         assert rel < 2e-3, (name, rel.item())
+
+
+@pytest.mark.parametrize("env,tp,device,want", [
+    ({}, 1, "cuda", True), ({}, 2, "cuda", True), ({"CQB_GRAPHS_TP": "0"}, 2, "cuda", False),
+    ({"CQB_GRAPHS_TP": "0"}, 1, "cuda", True), ({"CQB_GRAPHS": "0"}, 1, "cuda", False), ({}, 1, "cpu", False)])
+def test_graph_gating(monkeypatch, env, tp, device, want):
+    """Which configurations replay the DiT chunk as a graph (no GPU needed: only the decision)."""
+    from cq_pretrain_b200.config import tiny_config
+    from cq_pretrain_b200.train.graphed import graphs_enabled
+    for key in ("CQB_GRAPHS", "CQB_GRAPHS_TP"):
+        monkeypatch.delenv(key, raising=False)
+    for key, value in env.items():
+        monkeypatch.setenv(key, value)
+    cfg = tiny_config()
+    assert graphs_enabled(cfg, device, tp) is want
+    cfg.checkpoint_dit_layers = 2     # recomputed DiT blocks stay eager
+    assert graphs_enabled(cfg, device, tp) is False
+
+
+class _Optimizer:
+    def __init__(self):
+        self.waits = 0
+
+    def wait_params(self):
+        self.waits += 1
+
+
+def test_graph_runner_waits_for_parameter_gathers_first():
+    """Before any capture or replay the runner makes the stream wait for pending DP parameter
+    all-gathers (their forward hooks must not wait inside a capture)."""
+    from cq_pretrain_b200.train.graphed import RendererGraphs
+    opt = _Optimizer()
+    graphs = RendererGraphs(opt)       # the first sighting of a geometry runs eagerly (no CUDA needed)
+
+    class Model:
+        def renderer(self, leaf, bound):
+            return (leaf * 2).sum()
+
+    leaf = torch.ones(3, requires_grad=True)
+    loss, grad = graphs.run(Model(), leaf, None, 1.0)
+    assert opt.waits == 1 and float(loss) == 6.0 and torch.equal(grad, torch.full((3,), 2.0))
