@@ -1,6 +1,6 @@
 """The fused TP GEMM kernels of rank 0 of a TP = 2 group, emulated on one GPU (for ncu).
 
-``python -m cq_pretrain_b200.benchmarks.tp_fused_1gpu [--only ag|rs] [--iters 20] [--warmup 5]``
+``python -m cq_pretrain_b200.benchmarks.tp_fused_1gpu [--only ag|rs|qk] [--iters 20] [--warmup 5]``
 
 ncu does not run on multi-rank commands, so the one-kernel all-gather -> GEMM (``gather_gemm``)
 and GEMM -> reduce-scatter (``gemm_scatter_reduce``, epilogue 5) are launched here exactly as
@@ -109,9 +109,45 @@ def gemm_reducescatter(iters, warmup, rows=4096, k=3072, n=2048):
                 max_rel_err=max(err, sent), status=ops.gemm_status(True))
 
 
+def qk_norm_rope(iters, warmup, rows=32768, width=768, hd=128):
+    """Wan q / k full-width RMSNorm + RoPE (one kernel each way) at config 4's per-rank TP2 shape,
+    with the row-sum exchange running against this GPU's own slabs (tp = 1: the publish / flag /
+    acquire steps execute, the peer is this rank)."""
+    from ..ops import _ext
+    ops = _ext.ops()
+    dev = torch.device("cuda")
+    max_rows = 2 * rows
+    flags = torch.zeros(-(-max_rows // 64) * 8, dtype=torch.int64, device=dev)
+    slabs = [torch.zeros(max_rows, dtype=torch.float32, device=dev) for _ in range(2)]
+    ctr = torch.zeros(1, dtype=torch.int64, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    kw = dict(peer_recv=_ptrs(slabs[0]), my_recv=slabs[0].data_ptr(), peer_flags=_ptrs(flags),
+              my_flags=flags.data_ptr(), rank=0, tp=1, max_rows=max_rows, epoch_ctr=ctr.data_ptr(),
+              epoch_done=done.data_ptr(), peer_recv_odd=_ptrs(slabs[1]), my_recv_odd=slabs[1].data_ptr())
+    q = torch.randn(rows, width, device=dev, dtype=torch.bfloat16)
+    kv = torch.randn(rows, 2 * width, device=dev, dtype=torch.bfloat16)
+    k = kv[:, :width]                                   # the kv projection's k half, row-strided
+    wq, wk = torch.rand(width, device=dev) + 0.5, torch.rand(width, device=dev) + 0.5
+    ang = torch.rand(rows, hd // 2, device=dev) * 6.28
+    cos, sin = ang.cos(), ang.sin()
+    fwd = lambda: ops.qk_norm_rope_fwd(q, k, wq, wk, cos=cos, sin=sin, head_dim=hd, total_dim=2 * width, eps=1e-6,
+                                       **kw)
+    yq, yk, rstd = fwd()
+    dyq, dyk = torch.randn_like(yq), torch.randn_like(yk)
+    bwd = lambda: ops.qk_norm_rope_bwd(dyq, dyk, q, k, wq, wk, rstd, cos=cos, sin=sin, head_dim=hd,
+                                       total_dim=2 * width, **kw)
+    t_f, t_b = _events(fwd, iters, warmup), _events(bwd, iters, warmup)
+    tensor = rows * width * 2
+    angles = 2 * rows * (hd // 2) * 4
+    f_bytes, b_bytes = 4 * tensor + angles, 6 * tensor + angles   # fwd: q, k in / out; bwd: dy, x in, dx out
+    return dict(op="wan q/k rmsnorm + rope (exchange against own slabs)", shape=[rows, width, hd],
+                fwd_ms=t_f, bwd_ms=t_b, fwd_gbs=f_bytes / t_f / 1e6, bwd_gbs=b_bytes / t_b / 1e6,
+                comm_status=ops.comm_status_read(True))
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--only", choices=("ag", "rs"), default=None)
+    parser.add_argument("--only", choices=("ag", "rs", "qk"), default=None)
     parser.add_argument("--iters", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     args = parser.parse_args()
@@ -120,6 +156,8 @@ def main():
         print(json.dumps(allgather_gemm(args.iters, args.warmup)), flush=True)
     if args.only in (None, "rs"):
         print(json.dumps(gemm_reducescatter(args.iters, args.warmup)), flush=True)
+    if args.only in (None, "qk"):
+        print(json.dumps(qk_norm_rope(args.iters, args.warmup)), flush=True)
 
 
 if __name__ == "__main__":
