@@ -66,7 +66,9 @@ class Trainer:
         self.preparer = DevicePreparer(cfg, self.device, dtype)
         self.step_index = 0
         # the DiT chunk (forward + backward) replays as a CUDA graph once its geometry repeats
-        self.renderer_graphs = RendererGraphs(self.optimizer) if graphs_enabled(cfg, self.device, tp) else None
+        # (at TP > 1 only with the fused TP kernels: captured NCCL collectives measured slower than eager)
+        use_graphs = graphs_enabled(cfg, self.device, tp) and (tp == 1 or fused_tp)
+        self.renderer_graphs = RendererGraphs(self.optimizer) if use_graphs else None
         if tp > 1 and fused_tp and self.device.type == "cuda":
             from ..parallel import symmetric
             symmetric.enable()
