@@ -78,7 +78,8 @@ __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, const _
 // stored into slot `rank` of every peer's receive slab (plain peer stores), a system-scope
 // release flag per (block, rank) publishes them, and after acquiring the peers' flags for the
 // same block (bounded wait) the block reduces the tp partials and finishes its rows. The grid
-// is persistent (<= one CTA per SM per tensor) and every rank walks the blocks in the same order.
+// is persistent (every CTA resident at once, sized by the kernel's occupancy) and every rank
+// walks the blocks in the same order.
 //
 // One launch normalises up to two tensors of the same geometry (Wan's q and k: blockIdx.y picks
 // the tensor; tensor t uses slab rows [t * 64 * blocks, (t + 1) * 64 * blocks) and flag blocks
@@ -598,7 +599,19 @@ void set_rope(TpNormArgs& a, const c10::optional<at::Tensor>& cos_t, const c10::
   a.hd = (int)head_dim;
 }
 
-int tp_norm_grid(int rows) { return std::max(1, std::min((rows + STAT_ROWS - 1) / STAT_ROWS, sm_count())); }
+// Persistent grid of one tensor's CTAs: every CTA of the launch (ntens tensors) must be resident at
+// once, because a block's exchange waits for the peers' CTAs of the same block; the per-SM limit
+// comes from the kernel instance's occupancy (registers differ between the variants).
+template <bool BWD, int NCH>
+int tp_norm_grid(int rows, int ntens) {
+  static const int per_sm = [] {
+    int n = 0;
+    CQB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tp_norm_kernel<BWD, NCH>, 256, 0));
+    return std::max(1, n);
+  }();
+  const int blocks = (rows + STAT_ROWS - 1) / STAT_ROWS;
+  return std::max(1, std::min(blocks, per_sm * sm_count() / ntens));
+}
 
 // Forward of one or two tensors: returns (y per tensor, rstd [ntens, rows]).
 std::vector<at::Tensor> norm_fwd(TpNormArgs& a, int ntens, const at::TensorOptions& opts) {
@@ -610,11 +623,10 @@ std::vector<at::Tensor> norm_fwd(TpNormArgs& a, int ntens, const at::TensorOptio
     a.rstd[t] = rstd.data_ptr<float>() + (size_t)t * a.rows;
   }
   if (a.rows) {
-    const dim3 grid(tp_norm_grid(a.rows), ntens);
     if (a.D <= 1024)
-      tp_norm_kernel<false, 4><<<grid, 256, 0, stream()>>>(a);
+      tp_norm_kernel<false, 4><<<dim3(tp_norm_grid<false, 4>(a.rows, ntens), ntens), 256, 0, stream()>>>(a);
     else
-      tp_norm_kernel<false, 8><<<grid, 256, 0, stream()>>>(a);
+      tp_norm_kernel<false, 8><<<dim3(tp_norm_grid<false, 8>(a.rows, ntens), ntens), 256, 0, stream()>>>(a);
     CQB_LAUNCH_CHECK();
     count_launch();
   }
@@ -628,7 +640,7 @@ std::vector<at::Tensor> norm_bwd(TpNormArgs& a, int ntens, const std::vector<at:
   TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.is_contiguous() && rstd.numel() == (int64_t)ntens * a.rows,
               "rstd: fp32 [ntens, rows]");
   std::vector<at::Tensor> dx, dw, keep;
-  const int grid = tp_norm_grid(a.rows);
+  const int grid = a.D <= 1024 ? tp_norm_grid<true, 4>(a.rows, ntens) : tp_norm_grid<true, 8>(a.rows, ntens);
   for (int t = 0; t < ntens; ++t) {
     auto dyc = dys[t].contiguous();
     TORCH_CHECK(dyc.scalar_type() == at::kBFloat16 && dyc.numel() == (int64_t)a.rows * a.D, "dy like x");
