@@ -2,10 +2,10 @@
 
 ``python bench.py --gpus N --steps K --warmup W`` (N > 1 under ``torch.distributed.run``). Each
 DP rank trains on one synthetic 8192-token pack per step (random-init weights, synthetic
-merger features and latents of the BASELINE config-2 shape). The pack is a joint T2I + I2T pack:
+merger features and latents of the production-model shape). The pack is a joint T2I + I2T pack:
 two T2I documents (caption -> 512x512 image: 1024 merger tokens, 256 visual queries and a
 16x1x64x64 Wan target each), one I2T document (image -> caption) and log-uniform text documents
-filling the rest. TP is 2 from N = 2 up (TP2 x DP N/2; the BASELINE target is TP2 x DP4 on 8
+filling the rest. TP is 2 from N = 2 up (TP2 x DP N/2; the headline target is TP2 x DP4 on 8
 GPUs) and 1 on a single GPU.
 
 Reported: ``value`` = content tokens/s of the whole job, from CUDA-event device time of the
@@ -15,7 +15,7 @@ and the device->host read of the loss. Working set per step (weights, optimizer 
 far larger than the 126 MB L2, so no explicit flush is needed between iterations.
 ``--impl reference`` reports why the reference cannot run here.
 
-Extra keys: ``gdn_fwd_bwd_ms`` (one GDN layer forward+backward at 2048 and
+Extra keys: ``gdn_fwd_bwd_ms`` (the GDN layer microbenchmark: one layer forward+backward at 2048 and
 8192 content tokens with 32 and 16 value heads, median of 12 after 3 warm-ups, heads split over
 TP when N > 1) and, for N > 1, ``fused_tp_check``: the maximum relative error of every in-kernel
 TP collective against NCCL on the live process group, run once before the warm-up.

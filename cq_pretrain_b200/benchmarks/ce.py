@@ -1,4 +1,4 @@
-"""LM-head + cross-entropy benchmark (BASELINE config 5 shape: 8192 tokens x 2048 x 248K vocab).
+"""LM-head + cross-entropy benchmark (8192 tokens x 2048 x 248K vocab).
 
 ``[torchrun --nproc-per-node N] python -m cq_pretrain_b200.benchmarks.ce [--rows 8192] [--chunk 1024]``
 times forward+backward of ``ops.cross_entropy.linear_cross_entropy`` (GEMM epilogues that fold

@@ -1,4 +1,4 @@
-"""Gated-DeltaNet layer forward+backward microbenchmark (BASELINE config 3).
+"""Gated-DeltaNet layer forward+backward microbenchmark.
 
 ``python -m cq_pretrain_b200.benchmarks.gdn [--lengths 2048 8192] [--value-heads 32 16] [--iterations 12]``
 builds one GDN layer of the Qwen3.5-2B shape with 16 q/k heads and 32 (config 3) or 16 (the

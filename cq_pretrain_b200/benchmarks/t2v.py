@@ -1,4 +1,4 @@
-"""joint T2V + V2T training step (Qwen3.5-2B + Wan2.1-1.3B, bf16).
+"""Joint T2V + V2T training step (Qwen3.5-2B + Wan2.1-1.3B, bf16).
 
 ``[torchrun --nproc-per-node N] python -m cq_pretrain_b200.benchmarks.t2v [--tp T] [--steps K]``
 packs one T2V document (81 frames at 480x832: a 16x21x60x104 latent = 32,760 DiT tokens; Qwen
@@ -65,7 +65,7 @@ def main():
     gen = host.generation
     if st.rank == 0:
         print(json.dumps(dict(
-            config="BASELINE config 4: joint T2V + V2T, Qwen3.5-2B + Wan2.1-1.3B", n_gpus=world,
+            config="joint T2V + V2T, Qwen3.5-2B + Wan2.1-1.3B", n_gpus=world,
             parallelism=f"tp{tp}xdp{st.dp}", ms_per_step=round(step_ms, 2), wall_ms_per_step=round(wall_ms, 2),
             content_tokens_per_s=round(args.length * st.dp / (step_ms / 1000), 1),
             dit_tokens_per_step=int(sum(gen.lengths)) * st.dp,

@@ -1,4 +1,4 @@
-"""BASELINE config 5: TP collective-fused ops vs NCCL + cuBLAS at 2/4/8 GPUs (bf16).
+"""TP collective-fused ops vs NCCL + cuBLAS at 2/4/8 GPUs (bf16).
 
 ``torchrun --nproc-per-node N -m cq_pretrain_b200.benchmarks.tp_fused`` times, with CUDA events
 and the max over ranks (median of 20 after 5 warm-ups):

@@ -10,7 +10,7 @@ buffer whose address stands in for the peer pointer, and the peer's publication 
 stamps are set in advance. Nothing waits on another kernel: every flag the kernel polls is already
 set, so each call is one self-contained launch. What differs from the real TP run: the peer rows
 are read from local HBM instead of over NVLink, and no skew between ranks is absorbed. The shapes
-are BASELINE config 5's at TP = 2 (column-parallel [8192/2, 2048] x [2048, 6144/2]; row-parallel
+are the fused-op sweep's at TP = 2 (column-parallel [8192/2, 2048] x [2048, 6144/2]; row-parallel
 [8192, 6144/2] x [6144/2, 2048]); each result is checked against the plain GEMM.
 
 Prints one JSON line per op: fused and plain-GEMM CUDA-event times (median after warm-up) and

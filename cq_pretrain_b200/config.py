@@ -239,7 +239,7 @@ def load_sections(path) -> tuple[RunConfig, dict, dict]:
 
 
 def tiny_config(**overrides) -> RunConfig:
-    """a 4-layer hybrid (3 GDN + 1 attention) joint model that runs on CPU in fp32."""
+    """The tiny joint model: a 4-layer hybrid (3 GDN + 1 attention) that runs on CPU in fp32."""
     values = dict(
         renderer="wan",
         vision_encoder="qwen35",
@@ -277,7 +277,7 @@ def tiny_config(**overrides) -> RunConfig:
 
 
 def qwen35_2b_wan(**overrides) -> RunConfig:
-    """BASELINE config 2: Qwen3.5-2B hybrid backbone + Wan2.1-T2V-1.3B (the reference production model)."""
+    """Qwen3.5-2B hybrid backbone + Wan2.1-T2V-1.3B (the reference production model)."""
     values = dict(ce_chunk=1024, generation_token_budget=65536, visual_uncond_probability=0.1,
                   preserve_documents=False)
     values.update(overrides)

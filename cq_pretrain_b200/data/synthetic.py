@@ -1,4 +1,4 @@
-"""Synthetic document streams for the BASELINE configurations (no corpus, no network).
+"""Synthetic document streams for the benchmark configurations (no corpus, no network).
 
 Documents use the same element format as real corpora: text elements carry token ids, visual
 elements carry a Qwen patch grid, synthetic merger features ``N(0,1)`` of the backbone width
@@ -62,7 +62,7 @@ def joint_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), latent
                          doc_range=(64, 4096), caption=32, understanding=True):
     """Documents that fill one pack of ``length`` tokens: T2I captions (+ I2T) and log-uniform text docs.
 
-    BASELINE config 2 shape: each visual has ``grid`` Qwen patches (merged tokens = t*h*w/4) and a
+    Production-model shape: each visual has ``grid`` Qwen patches (merged tokens = t*h*w/4) and a
     ``latent_shape`` Wan target; remaining space is text documents of log-uniform lengths in
     ``doc_range``; the last document is cut to fill the pack exactly.
     """
@@ -92,7 +92,7 @@ def joint_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), latent
 
 def video_pack_documents(cfg, length, seed=0, grid=(4, 30, 52), latent_shape=(16, 21, 60, 104), text=4096,
                          understanding=True):
-    """one T2V target (81 frames at 480x832 -> 32,760 DiT tokens; Qwen content 8
+    """The T2V + V2T workload: one T2V target (81 frames at 480x832 -> 32,760 DiT tokens; Qwen content 8
     frames -> 1,560 merged tokens and 1,560 queries), with ``understanding`` one V2T document of the
     same geometry (video, then its caption as the text target), plus ``text`` tokens of text
     documents."""
@@ -116,7 +116,7 @@ def video_pack_documents(cfg, length, seed=0, grid=(4, 30, 52), latent_shape=(16
 
 def tiny_pack_documents(cfg, length=512, seed=0, images=2, grid=(1, 16, 16), latent_shape=(16, 1, 8, 8),
                         doc_range=(32, 256)):
-    """512 ids, 2 images of 64 merged tokens, docs of 32-256 tokens."""
+    """The tiny-model workload: 512 ids, 2 images of 64 merged tokens, docs of 32-256 tokens."""
     rng = np.random.default_rng(seed)
     docs = []
     for i in range(images):
@@ -130,7 +130,7 @@ def tiny_pack_documents(cfg, length=512, seed=0, images=2, grid=(1, 16, 16), lat
 
 
 def synthetic_batch(cfg, length=512, seed=0, kind="tiny", pad_multiple=1, **kwargs):
-    """One packed, planned batch (host memory) of a BASELINE configuration shape."""
+    """One packed, planned batch (host memory) of a benchmark configuration shape."""
     maker = dict(tiny=tiny_pack_documents, joint=joint_pack_documents, video=video_pack_documents,
                  gdn=gdn_pack_documents)[kind]
     docs = maker(cfg, length, seed=seed, **kwargs)
@@ -141,7 +141,7 @@ def synthetic_batch(cfg, length=512, seed=0, kind="tiny", pad_multiple=1, **kwar
 
 
 def gdn_pack_documents(cfg, length, images=2, seed=0, grid=(1, 32, 32), doc_length=1024, caption=32):
-    """BASELINE config 3 (GDN layer microbenchmark): T2I captions, then text documents of
+    """The GDN layer microbenchmark workload: T2I captions, then text documents of
     ``doc_length`` tokens (a packed document boundary every 1024 tokens) up to ``length``."""
     rng = np.random.default_rng(seed)
     docs = []

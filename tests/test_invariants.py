@@ -3,7 +3,7 @@
 * the chunked renderer backward gives the unchunked loss and every gradient (reference
   ``tests/test_wan_unified.py:84-109``);
 * DP/GA loss scales make sparse image objectives a global average (``tests/test_i2t_loss_scaling.py``);
-* TP=2 equals TP=1 for the whole tiny joint model (BASELINE config 1, gloo);
+* TP=2 equals TP=1 for the whole tiny joint model (gloo);
 * a DP rank without generation targets issues the same collective sequence as one with them
   (``tests/test_collective_order.py``);
 * the EMA install/restore and the evaluation-snapshot round trip at world 4 (TP2 x DP2,
