@@ -102,7 +102,7 @@ def main():
     parser.add_argument("--tp", type=int, default=None)
     parser.add_argument("--length", type=int, default=8192)
     parser.add_argument("--images", type=int, default=3, help="visual documents per pack (all but one are T2I)")
-    parser.add_argument("--no-gdn", action="store_true", help="skip the config-3 GDN layer timings")
+    parser.add_argument("--no-gdn", action="store_true", help="skip the GDN layer microbenchmark timings")
     parser.add_argument("--clocks-csv", default=None, help="where to keep the nvidia-smi samples (default: a temp file)")
     parser.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid as a bench value)")
     parser.add_argument("--recompute", type=int, default=0, help="recompute backbone layers in backward")

@@ -1,7 +1,7 @@
 """Gated-DeltaNet layer forward+backward microbenchmark.
 
 ``python -m cq_pretrain_b200.benchmarks.gdn [--lengths 2048 8192] [--value-heads 32 16] [--iterations 12]``
-builds one GDN layer of the Qwen3.5-2B shape with 16 q/k heads and 32 (config 3) or 16 (the
+builds one GDN layer of the Qwen3.5-2B shape with 16 q/k heads and 32 (the microbenchmark's) or 16 (the
 reference's published run) v heads of dim 128 (short conv 4,
 gated RMSNorm output), random N(0, 0.02) weights, and the CQ event plan of a synthetic pack
 (2 T2I images, text documents with a boundary every 1024 tokens). Each iteration runs the

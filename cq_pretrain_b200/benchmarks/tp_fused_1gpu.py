@@ -110,7 +110,7 @@ def gemm_reducescatter(iters, warmup, rows=4096, k=3072, n=2048):
 
 
 def qk_norm_rope(iters, warmup, rows=32768, width=768, hd=128):
-    """Wan q / k full-width RMSNorm + RoPE (one kernel each way) at config 4's per-rank TP2 shape,
+    """Wan q / k full-width RMSNorm + RoPE (one kernel each way) at the T2V workload's per-rank TP2 shape,
     with the row-sum exchange running against this GPU's own slabs (tp = 1: the publish / flag /
     acquire steps execute, the peer is this rank)."""
     from ..ops import _ext
