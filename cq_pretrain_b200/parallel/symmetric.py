@@ -14,10 +14,11 @@ handles, and opens every peer's buffer (NVLink P2P). Layout::
 
 Protocol (epochs count calls of each kind; every rank issues the same sequence):
 
-* all-gather -> GEMM (epoch e): one kernel. Its copy warps stage the local shard into the gather
-  buffer and into ``send[e % 2]`` (own rows first), publish flag e to every peer once the whole
-  shard is staged, and pull each peer's shard into local memory block by block (after acquiring
-  that peer's flag) while the tensor cores consume the blocks already present.
+* all-gather -> GEMM (epoch e): one kernel. The tensor cores read this rank's rows straight from
+  the caller's shard; the copy warps stage that shard into ``send[e % 2]``, publish flag e to every
+  peer once the whole shard is staged, pull each peer's shard into the gather buffer sub-chunk by
+  sub-chunk (after acquiring that peer's flag) while the tensor cores consume the blocks already
+  present, and finally copy the own rows into the gather buffer (the gathered output).
 * GEMM -> reduce-scatter (epoch e): one kernel. Tiles of rows owned by another rank are stored
   into the owner's ``recv[e % 2][src]`` and stamped with e in the owner's (tile, src, warp) slot;
   this rank's own tiles come last, wait for the peers' stamps of the same tile, and add the
