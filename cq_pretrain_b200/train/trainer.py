@@ -111,13 +111,16 @@ class Trainer:
         if timing and self.device.type == "cuda":
             events = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
             events[0].record()
-        self.optimizer.zero_grad()
         n_text = sum(int(b.text_indices.numel()) for b, _ in micro_batches)
         n_img = sum(b.generation_image_count for b, _ in micro_batches)
-        counts = torch.tensor([float(n_text), float(n_img)], dtype=torch.float64, device=self.device)
         if self.state.dp > 1:
+            # before the gradient zeroing: the host waits for this small collective only
+            counts = torch.tensor([float(n_text), float(n_img)], dtype=torch.float64, device=self.device)
             dist.all_reduce(counts, group=self.state.dp_group)
-        total_text, total_img = counts.tolist()
+            total_text, total_img = counts.tolist()
+        else:   # nothing to combine: no device round trip (it would wait for the queued work)
+            total_text, total_img = float(n_text), float(n_img)
+        self.optimizer.zero_grad()
         dp = self.state.dp
         accumulated = torch.zeros(3, dtype=torch.float32, device=self.device)
         ga = len(micro_batches)
